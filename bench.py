@@ -1,0 +1,358 @@
+"""Benchmark of the temporal-attention training step (TGAT 2-layer, config 2).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl fast|reference]
+
+One step = one chronological batch of 600 positive edges + 600 negatives per
+GPU (weak scaling: the global batch is 600*N, each rank a contiguous slice):
+2-hop uniform 10x10 temporal sampling, feature gather + time encoding,
+Q/K/V projections, edge softmax + aggregate, w_out/LayerNorm, edge
+predictor, BCE, backward, Adam (reference train.py:307-393).
+
+`value`   positive training edges/s with graph, features and batch lists
+          resident in HBM (device-timed, max over ranks).
+`e2e`     the same through the reference-facing API with host buffers: numpy
+          roots/timestamps handed to ParallelSampler.sample() (H2D inside the
+          timed region) and the loss read back to the host every step.
+`--impl reference` times the reference's CPU path of the same step: the
+          reference sampler built from its own source (oracle/_ref, all host
+          threads) + the fp32 CPU restatement of layers.py/modules.py + Adam.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "TGAT 2-layer training edges/sec"
+UNIT = "edges/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="fast", choices=["fast", "reference"])
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the cpu_baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-steps", type=int, default=5)
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- helpers
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return dict(hbm=float(p["hbm_gbs"]), tf=float(p["bf16_tflops"]), tf_sus=float(p["bf16_tflops_sustained"]),
+                    src="measured")
+    return dict(hbm=6650.0, tf=1590.0, tf_sus=1400.0, src="fallback")
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", "fb_clocks_%d_%d.csv" % (os.getpid(), gpu_index))
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.Q,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_reference_step_fn(cfg, graph, edge_feats_cpu, node_feats_cpu, threads):
+    """Closure running one reference-CPU training step; returns (fn, kind)."""
+    import torch
+    from fast_b200.data import model_params
+    from fast_b200.model import GeneralModel
+    from oracle import ref_math
+    from oracle.sampler import OracleSampler, load_reference
+    torch.set_num_threads(threads)
+    sp, mp, gp, tp = model_params(cfg)
+    ref = load_reference()
+    kind = "reference" if ref is not None else "port"
+    S = ref.ParallelSampler if ref is not None else OracleSampler
+    sampler = S(graph.indptr, graph.indices, graph.eid, graph.ts_csr, threads, 1, sp["layer"], sp["neighbor"],
+                sp["strategy"] == "recent", False, 1, 0.0)
+    torch.manual_seed(0)
+    model = GeneralModel(0 if node_feats_cpu is None else node_feats_cpu.shape[1], edge_feats_cpu.shape[1],
+                         sp, mp, gp, tp)
+    opt = torch.optim.Adam(model.parameters(), lr=tp["lr"])
+    rng = np.random.default_rng(1)
+    B = cfg.batch
+    state = {"b": 0}
+
+    def step():
+        b0 = (state["b"] * B) % (graph.train_end - B)
+        state["b"] += 1
+        src, dst, t = graph.src[b0:b0 + B], graph.dst[b0:b0 + B], graph.ts[b0:b0 + B]
+        roots = np.concatenate([src, dst, rng.integers(0, graph.n_nodes, B).astype(np.int32)])
+        rts = np.concatenate([t, t, t]).astype(np.float32)
+        sampler.sample(roots, rts, [])
+        blocks = sampler.get_ret()
+        opt.zero_grad()
+        pp, pn = ref_math.model_forward(model, blocks, node_feats_cpu, edge_feats_cpu)
+        loss = ref_math.bce_loss(pp, pn)
+        loss.backward()
+        opt.step()
+        return float(loss)
+
+    return step, kind
+
+
+def cpu_workload(cfg):
+    import torch
+    from fast_b200.data import make_graph
+    graph = make_graph(cfg)
+    g = torch.Generator()
+    g.manual_seed(7)
+    ef = torch.randn(cfg.edges, cfg.d_edge, generator=g) if cfg.d_edge else None
+    nf = torch.randn(cfg.nodes, cfg.d_node, generator=g) if cfg.d_node else None
+    return graph, ef, nf
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from fast_b200.data import CONFIGS
+    cfg = CONFIGS[args.config]
+    threads = len(os.sched_getaffinity(0))
+    graph, ef, nf = cpu_workload(cfg)
+    step, kind = cpu_reference_step_fn(cfg, graph, ef, nf, threads)
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    value = args.steps * cfg.batch / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded, %s shapes)" % cfg.name,
+        "config": {"workload": cfg.name, "global_batch": cfg.batch, "fanout": list(cfg.fanout),
+                   "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": "%d chronological batches of %d+%d roots, full graph" %
+                                   (args.steps, cfg.batch, 2 * cfg.batch)},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------- fast arm
+def run_fast(args):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    from fast_b200 import ops
+    from fast_b200.data import CONFIGS, make_features, make_graph, model_params
+    from fast_b200.train import Trainer
+    cfg = CONFIGS[args.config]
+    graph = make_graph(cfg)
+    nf, ef = make_features(cfg, cfg.edges, dev)
+    sp, mp, gp, tp = model_params(cfg)
+    tr = Trainer(graph, nf, ef, sp, mp, gp, tp, dev, rank=rank, world=world)
+    B = cfg.batch
+    gB = B * world
+    n_batches = graph.train_end // gB
+    starts = [(i * gB) for i in range(n_batches)]
+    it = {"i": 0}
+
+    def next_range():
+        b0 = starts[it["i"] % n_batches]
+        it["i"] += 1
+        return b0, b0 + gB
+
+    def dev_step():
+        b0, b1 = next_range()
+        roots, rts = tr.device_roots(b0, b1)
+        return tr.step_device(roots, rts)
+
+    for _ in range(args.warmup):
+        dev_step()
+    torch.cuda.synchronize()
+    clock = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clock.start()
+    l0 = ops.LAUNCHES[0]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        loss = dev_step()
+    ev1.record()
+    torch.cuda.synchronize()
+    clocks = clock.stop()
+    ms = ev0.elapsed_time(ev1)
+    launches = ops.LAUNCHES[0] - l0 + args.steps * tr.sampler_kernels_per_step()
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    value = args.steps * gB / (ms / 1000.0)
+
+    # end-to-end through the reference-facing API with host buffers
+    rng = np.random.default_rng(5)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        b0, b1 = next_range()
+        lo, hi = tr.local_slice(b0, b1)
+        t_np = graph.ts[lo:hi]
+        roots = np.concatenate([graph.src[lo:hi], graph.dst[lo:hi],
+                                rng.integers(0, graph.n_nodes, hi - lo).astype(np.int32)])
+        tr.step_host(roots, np.concatenate([t_np, t_np, t_np]).astype(np.float32))
+    torch.cuda.synchronize()
+    e2e_s = torch.tensor([time.perf_counter() - t0], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+    e2e_value = args.steps * gB / float(e2e_s.item())
+
+    # per-kernel device times for the roofline (separate, instrumented steps)
+    ops.TIMER = ops.KernelTimer()
+    for _ in range(args.profile_steps):
+        dev_step()
+    kern = ops.TIMER.summary()
+    ops.TIMER = None
+
+    if rank != 0:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+    pk = peaks()
+    kernels = {}
+    for name, r in kern.items():
+        per_ms = r["ms"] / r["launches"]
+        gbs = r["bytes"] / (r["ms"] / 1000.0) / 1e9 if r["ms"] > 0 else 0.0
+        tfs = r["flops"] / (r["ms"] / 1000.0) / 1e12 if r["ms"] > 0 else 0.0
+        kernels[name] = {"launches_per_step": r["launches"] / args.profile_steps,
+                         "ms_per_step": r["ms"] / args.profile_steps, "us_per_launch": 1000 * per_ms,
+                         "GB/s": round(gbs, 1), "TFLOP/s": round(tfs, 2),
+                         "hbm_frac": round(gbs / pk["hbm"], 4)}
+    top = max(kern.items(), key=lambda kv: kv[1]["ms"])
+    name, r = top
+    if r["flops"] > 0 and name.startswith("gemm"):
+        ach = r["flops"] / (r["ms"] / 1000.0) / 1e12
+        roof = {"kernel": name, "bound": "tensor", "achieved": round(ach, 3), "peak": pk["tf"], "unit": "TFLOP/s",
+                "frac": round(ach / pk["tf"], 5), "traffic": None,
+                "peak_source": "%s bf16 burst (MEASURED_PEAKS.json)" % pk["src"]}
+    else:
+        ach = r["bytes"] / (r["ms"] / 1000.0) / 1e9
+        roof = {"kernel": name, "bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm"], "unit": "GB/s",
+                "frac": round(ach / pk["hbm"], 4), "traffic": None,
+                "peak_source": "%s copy bandwidth (MEASURED_PEAKS.json)" % pk["src"]}
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, %s shapes)" % cfg.name,
+        "config": {"workload": cfg.name, "global_batch": gB, "local_batch": B, "fanout": list(cfg.fanout),
+                   "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge,
+                   "parallelism": "dp%d" % world,
+                   "l2": "inputs larger than L2 (%.1f GB edge-feature table gathered at random rows)" %
+                         (cfg.edges * cfg.d_edge * 4 / 1e9)},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": world * 3 * B * 8,
+                "d2h_bytes_per_step": world * 4},
+        "gpu_launches": int(launches),
+        "roofline": roof,
+        "kernels": kernels,
+        "clocks": clocks,
+        "last_loss": float(loss),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def cpu_baseline(cfg, budget_s):
+    """Reference CPU path on a bounded sample: as many batches as fit in ~budget_s."""
+    threads = len(os.sched_getaffinity(0))
+    graph, ef, nf = cpu_workload(cfg)
+    step, kind = cpu_reference_step_fn(cfg, graph, ef, nf, threads)
+    step()  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        step()
+        n += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or n >= 200:
+            break
+    return {"value": n * cfg.batch / el, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": "%d chronological batches of %d+%d roots on the full %s graph (%.1f s)" %
+                      (n, cfg.batch, 2 * cfg.batch, cfg.name, el)}
+
+
+def main():
+    args = parse()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_fast(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

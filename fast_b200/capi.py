@@ -1,0 +1,183 @@
+"""ctypes binding of the libfast_b200 C ABI (include/fast_b200.h).
+
+The training path calls the kernels through these wrappers with raw device
+pointers taken from torch tensors, on torch's current stream.  A non-zero
+status raises ``FastB200Error`` with the library's message.  There is no
+fallback: if the library is missing the import fails.
+"""
+import ctypes
+import os
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libfast_b200.so")
+
+
+class FastB200Error(RuntimeError):
+    pass
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            "fast_b200: %s is missing; build it with `python -m fast_b200.build` "
+            "(or __graft_entry__.build())" % LIB_PATH)
+    return ctypes.CDLL(LIB_PATH)
+
+
+lib = _load()
+
+c_i32p = ctypes.c_void_p
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+_F = ctypes.c_float
+_U64 = ctypes.c_uint64
+_SZ = ctypes.c_size_t
+
+_SIGS = {
+    "fb_last_error": (ctypes.c_char_p, []),
+    "fb_version": (ctypes.c_char_p, []),
+    "fb_sampler_create": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I, _P, _I, _I, _I, _F, _U64, _P]),
+    "fb_sampler_destroy": (_I, [_P]),
+    "fb_sampler_reset": (_I, [_P, _P]),
+    "fb_sampler_sample": (_I, [_P, _P, _P, _I64, _I, _P]),
+    "fb_sampler_num_blocks": (_I, [_P]),
+    "fb_sampler_block": (_I, [_P, _I, _P]),
+    "fb_sampler_dims": (_I, [_P, _P, _P]),
+    "fb_sampler_dedup": (_I, [_P, _I, _P]),
+    "fb_sampler_set_call_index": (_I, [_P, _U64]),
+    "fb_attn_fwd": (_I, [_P, _I64, _P, _P, _I64, _P, _I64, _P, _I, _I, _F, _F, _U64, _U64, _P, _P, _I64, _P]),
+    "fb_attn_bwd": (_I, [_P, _I64, _P, _P, _I64, _P, _I64, _P, _I, _I, _F, _F, _U64, _U64, _P, _P, _I64,
+                         _P, _P, _P, _I64, _P]),
+    "fb_attn_logits_fwd": (_I, [_P, _P, _I64, _P, _I64, _P, _I64, _I, _I, _F, _F, _P, _P, _P, _P]),
+    "fb_attn_logits_bwd": (_I, [_P, _P, _I64, _P, _I64, _P, _I64, _I, _I, _F, _F, _P, _P, _P, _P, _P, _P]),
+    "fb_dropout_scale": (_I, [_I64, _I, _F, _U64, _U64, _P, _P]),
+    "fb_count_ids": (_I, [_P, _I64, _P, _I64, _P]),
+    "fb_balanced_mask": (_I, [_P, _I64, _I, _P, _P]),
+    "fb_edge_softmax_fwd": (_I, [_P, _I64, _P, _I, _P, _P]),
+    "fb_edge_softmax_bwd": (_I, [_P, _I64, _P, _P, _I, _P, _P]),
+    "fb_scatter_rows": (_I, [_P, _P, _I64, _P, _I64, _I, _P, _I64, _P]),
+    "fb_segment_rows": (_I, [_P, _I64, _P, _P, _P, _I64, _I, _P, _I64, _P]),
+    "fb_exclusive_sum_ws_bytes": (_SZ, [_I64]),
+    "fb_exclusive_sum": (_I, [_P, _I64, _P, _P, _P]),
+    "fb_gather_time_encode": (_I, [_P, _I64, _P, _I64, _I, _P, _I64, _P, _I, _P, _P, _P, _I, _P, _I64, _I64, _P, _P]),
+    "fb_time_encode_bwd_ws_bytes": (_SZ, [_I64, _I]),
+    "fb_time_encode_bwd": (_I, [_P, _I64, _P, _P, _P, _I, _I64, _P, _P, _P, _P, _P]),
+    "fb_gemm_nt": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _I, _I, _I, _P]),
+    "fb_gemm_tn_ws_bytes": (_SZ, [_I64, _I, _I]),
+    "fb_gemm_tn": (_I, [_P, _I64, _P, _I64, _P, _I64, _I64, _P, _I, _I, _I, _P, _P]),
+    "fb_colsum_ws_bytes": (_SZ, [_I64, _I]),
+    "fb_colsum": (_I, [_P, _I64, _P, _I64, _P, _I, _I, _P, _P]),
+}
+
+for _name, (_res, _args) in _SIGS.items():
+    _fn = getattr(lib, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args
+
+
+class BlockView(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in
+                ("row", "col", "eid", "ts", "dts", "nodes", "rptr", "cntE", "uniE", "invE", "dims")] + \
+               [("max_roots", ctypes.c_int64), ("max_edges", ctypes.c_int64)]
+
+
+def exported_symbols():
+    """Names this binding expects the library to export."""
+    return list(_SIGS)
+
+
+def check(rc):
+    if rc != 0:
+        raise FastB200Error("fast_b200: " + lib.fb_last_error().decode())
+
+
+def call(name, *args):
+    """Calls an fb_* entry point and raises on a non-zero status."""
+    check(getattr(lib, name)(*args))
+
+
+def ptr(t):
+    """Device pointer of a tensor (None -> NULL)."""
+    return None if t is None else t.data_ptr()
+
+
+def stream_ptr(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+class CSampler:
+    """Direct C-ABI handle of the device sampler (fb_sampler_*), for callers
+    that do not go through the pybind `sampler_core` module."""
+
+    def __init__(self, indptr, indices, eid, ts, num_layers, num_neighbors, recent, prop_time=False,
+                 num_history=1, window_duration=0.0, seed=0):
+        import numpy as np
+        self._keep = [np.ascontiguousarray(a) for a in (indptr, indices, eid, ts)]
+        nn = (ctypes.c_int32 * len(num_neighbors))(*num_neighbors)
+        h = ctypes.c_void_p()
+        ip, ix, ei, t = self._keep
+        check(lib.fb_sampler_create(ip.ctypes.data, ix.ctypes.data, ei.ctypes.data, t.ctypes.data, ip.size - 1,
+                                    ix.size, 0, num_layers, nn, int(recent), int(prop_time), num_history,
+                                    float(window_duration), seed, ctypes.byref(h)))
+        self.h = h
+        self.nblocks = lib.fb_sampler_num_blocks(h)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib.fb_sampler_destroy(self.h)
+            self.h = None
+
+    def reset(self):
+        check(lib.fb_sampler_reset(self.h, stream_ptr()))
+
+    def sample(self, roots, root_ts):
+        import numpy as np
+        r = np.ascontiguousarray(roots, dtype=np.int32)
+        t = np.ascontiguousarray(root_ts, dtype=np.float32)
+        check(lib.fb_sampler_sample(self.h, r.ctypes.data, t.ctypes.data, r.size, 0, stream_ptr()))
+
+    def dims(self):
+        import numpy as np
+        d = np.zeros(8 * self.nblocks, np.int32)
+        check(lib.fb_sampler_dims(self.h, d.ctypes.data, stream_ptr()))
+        return d.reshape(self.nblocks, 8)
+
+    def dedup(self, i):
+        check(lib.fb_sampler_dedup(self.h, i, stream_ptr()))
+
+    def block_arrays(self, i, dedup=True):
+        """Host copies of block i (reference TemporalGraphBlock fields)."""
+        import numpy as np
+        import torch
+        if dedup:
+            self.dedup(i)
+        d = self.dims()[i]
+        R, E, S, dim_in, nu = (int(x) for x in d[:5])
+        v = BlockView()
+        check(lib.fb_sampler_block(self.h, i, ctypes.byref(v)))
+
+        def grab(p, n, dt):
+            if n == 0:
+                return np.empty(0, dt)
+            return device_array(p, n, dt).cpu().numpy().copy()
+        return dict(row=grab(v.row, E, np.int32), col=grab(v.col, E, np.int32), eid=grab(v.eid, E, np.int32),
+                    ts=grab(v.ts, dim_in, np.float32), dts=grab(v.dts, dim_in, np.float32),
+                    nodes=grab(v.nodes, dim_in, np.int32), rptr=grab(v.rptr, R + 1, np.int32),
+                    cntE=grab(v.cntE, S + 1 if E else 0, np.int32), uniE=grab(v.uniE, nu if dedup else 0, np.int32),
+                    invE=grab(v.invE, E if dedup else 0, np.int32), dim_in=dim_in, dim_out=R)
+
+
+class _CudaArray:
+    def __init__(self, p, n, typestr):
+        self.__cuda_array_interface__ = {"shape": (int(n),), "typestr": typestr, "data": (int(p), False),
+                                         "version": 3, "strides": None}
+
+
+def device_array(p, n, dtype):
+    """Zero-copy torch view of n elements of numpy dtype at device pointer p."""
+    import numpy as np
+    import torch
+    return torch.as_tensor(_CudaArray(p, n, np.dtype(dtype).str), device="cuda")

@@ -1,0 +1,479 @@
+// Fused temporal attention over destination segments, one warp per
+// destination row, plus the legacy fastAgg segment operators.
+//
+// Reference semantics (NoneBone/FAST):
+//   logits  LeakyReLU_0.2(sum_d Q.K)           layers.py:165-173
+//   softmax per destination (dgl edge_softmax) layers.py:188-192, edge_softmax.cu:255-293
+//   dropout on att, V*att, scatter-sum          layers.py:198-222
+//   backward                                    efficientGOP.py:80-131 (true gradient)
+//
+// Memory plan per destination row j with edges [rptr[j], rptr[j+1]):
+//   forward reads q_j once, each K row once (pass 1) and each V row once
+//   (pass 3), writes att[e, :] and agg_j.  Backward reads q_j, dagg_j, each
+//   V row (pass 1) and K row (pass 2) once, writes dV, dK rows and dq_j.
+// Rows are 16-byte vectors spread over the lanes, so every K/V row is one
+// fully coalesced warp load.  Reductions stay inside the warp: no atomics,
+// results are bit-identical run to run.
+#include <cfloat>
+#include "runtime.cuh"
+
+namespace {
+
+constexpr int kWarpsPerCta = 8;
+constexpr int kMaxHeads = 4;
+constexpr int kStash = 64;  // edges whose per-head values a warp keeps in shared memory
+
+struct RowGeom {
+  int nv4;   // float4 vectors per row
+  int dh;    // features per head
+  int heads;
+};
+
+// Head index of each of the 4 components of the lane's t-th vector.
+template <int NV>
+__device__ __forceinline__ void lane_heads(const RowGeom &g, int lane, int hsel[NV][4]) {
+#pragma unroll
+  for (int t = 0; t < NV; ++t)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      int idx = 4 * (lane + 32 * t) + c;
+      hsel[t][c] = (lane + 32 * t < g.nv4) ? idx / g.dh : kMaxHeads;
+    }
+}
+
+template <int NV>
+__device__ __forceinline__ void load_row(const float *__restrict__ p, const RowGeom &g, int lane, float4 r[NV]) {
+#pragma unroll
+  for (int t = 0; t < NV; ++t) {
+    int v = lane + 32 * t;
+    r[t] = (v < g.nv4) ? __ldg(reinterpret_cast<const float4 *>(p) + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+template <int NV>
+__device__ __forceinline__ void store_row(float *__restrict__ p, const RowGeom &g, int lane, const float4 r[NV]) {
+#pragma unroll
+  for (int t = 0; t < NV; ++t) {
+    int v = lane + 32 * t;
+    if (v < g.nv4) reinterpret_cast<float4 *>(p)[v] = r[t];
+  }
+}
+
+__device__ __forceinline__ float comp(const float4 &v, int c) {
+  return c == 0 ? v.x : (c == 1 ? v.y : (c == 2 ? v.z : v.w));
+}
+
+__device__ __forceinline__ float pick(const float (&a)[kMaxHeads], int h) {
+  return h == 0 ? a[0] : (h == 1 ? a[1] : (h == 2 ? a[2] : (h == 3 ? a[3] : 0.f)));
+}
+
+// Per-head dot products of two rows, reduced over the warp (all lanes get them).
+template <int NV>
+__device__ __forceinline__ void head_dots(const float4 a[NV], const float4 b[NV], const int hsel[NV][4], int heads,
+                                          float (&out)[kMaxHeads]) {
+#pragma unroll
+  for (int h = 0; h < kMaxHeads; ++h) out[h] = 0.f;
+#pragma unroll
+  for (int t = 0; t < NV; ++t)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float p = comp(a[t], c) * comp(b[t], c);
+      int h = hsel[t][c];
+#pragma unroll
+      for (int hh = 0; hh < kMaxHeads; ++hh)
+        if (h == hh) out[hh] += p;
+    }
+#pragma unroll
+  for (int h = 0; h < kMaxHeads; ++h)
+    if (h < heads) out[h] = fb::warp_sum(out[h]);
+}
+
+__device__ __forceinline__ float leaky(float z, float slope) { return z > 0.f ? z : z * slope; }
+
+// Dropout keep-scale of (edge, head): 0 or 1/(1-p).  The keep decision comes
+// from explicit uniforms when given (kept when u > p, as the reference mask
+// test does), else from Philox(seed, offset; edge) so the backward pass can
+// regenerate it without storing a mask.
+__device__ __forceinline__ void drop_scale(int64_t e, int heads, float p, uint64_t seed, uint64_t offset,
+                                           const float *mask_u, float (&s)[kMaxHeads]) {
+  if (p <= 0.f) {
+#pragma unroll
+    for (int h = 0; h < kMaxHeads; ++h) s[h] = 1.f;
+    return;
+  }
+  const float inv = 1.f / (1.f - p);
+  if (mask_u) {
+#pragma unroll
+    for (int h = 0; h < kMaxHeads; ++h) s[h] = (h < heads && mask_u[e * heads + h] > p) ? inv : 0.f;
+    return;
+  }
+  fb::Philox4 r = fb::philox4x32_10((uint32_t)e, (uint32_t)(e >> 32), (uint32_t)offset, (uint32_t)(offset >> 32),
+                                    (uint32_t)seed, (uint32_t)(seed >> 32));
+#pragma unroll
+  for (int h = 0; h < kMaxHeads; ++h) {
+    float u = (float)(r.v[h] >> 8) * (1.0f / 16777216.0f);
+    s[h] = (h < heads && u >= p) ? inv : 0.f;
+  }
+}
+
+struct AttnArgs {
+  const float *q; int64_t ldq;
+  const float *k, *v; int64_t ldkv;
+  const int32_t *rptr; int64_t n_dst; const int32_t *n_dst_dev;
+  int heads, dim;
+  float slope, drop_p; uint64_t seed, offset;
+  const float *att; float *att_out;
+  float *agg; int64_t ldagg;
+  const float *x;          // optional pre-activation logits [E, heads] replacing q.k
+  const float *mask_u;     // optional dropout uniforms [E, heads]
+  const int64_t *seg_row;  // optional: segment s owns output row seg_row[rptr[s]]
+  int64_t n_out;           // rows of agg / dagg when seg_row is given (others are skipped)
+  float *dx;               // optional gradient of the pre-activation logits
+  const float *dagg; int64_t lddagg;
+  float *dq, *dk, *dv; int64_t lddkv;
+};
+
+// Output (or incoming gradient) row of segment j: j itself, or the row named
+// by seg_row at the segment's first edge (legacy cntE segments).
+__device__ __forceinline__ int64_t seg_out_row(const AttnArgs &a, int64_t j, int beg, int end) {
+  if (!a.seg_row) return j;
+  if (end <= beg) return -1;
+  const int64_t r = a.seg_row[beg];
+  return (r >= 0 && r < a.n_out) ? r : -1;
+}
+
+template <int NV>
+__device__ __forceinline__ void edge_logits(const AttnArgs &a, const float4 q[NV], int e, const RowGeom &g, int lane,
+                                            const int hsel[NV][4], float (&z)[kMaxHeads]) {
+  if (a.x) {
+#pragma unroll
+    for (int h = 0; h < kMaxHeads; ++h) z[h] = (h < a.heads) ? __ldg(a.x + (int64_t)e * a.heads + h) : 0.f;
+  } else {
+    float4 kr[NV];
+    load_row<NV>(a.k + (int64_t)e * a.ldkv, g, lane, kr);
+    head_dots<NV>(q, kr, hsel, a.heads, z);
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_fwd(AttnArgs a) {
+  __shared__ float stash[kWarpsPerCta][kStash][kMaxHeads];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t n_dst = a.n_dst_dev ? (int64_t)(*a.n_dst_dev) : a.n_dst;
+  RowGeom g{a.dim / 4, a.dim / a.heads, a.heads};
+  int hsel[NV][4];
+  lane_heads<NV>(g, lane, hsel);
+  for (int64_t j = (int64_t)blockIdx.x * kWarpsPerCta + w; j < n_dst; j += (int64_t)gridDim.x * kWarpsPerCta) {
+    const int beg = a.rptr[j], end = a.rptr[j + 1];
+    const int64_t orow = seg_out_row(a, j, beg, end);
+    float4 acc[NV];
+#pragma unroll
+    for (int t = 0; t < NV; ++t) acc[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (end > beg) {
+      float4 q[NV];
+      if (!a.x) load_row<NV>(a.q + j * a.ldq, g, lane, q);
+      float m[kMaxHeads];
+#pragma unroll
+      for (int h = 0; h < kMaxHeads; ++h) m[h] = -FLT_MAX;
+      // pass 1: activated logits (stashed), running max
+      for (int e = beg; e < end; ++e) {
+        float z[kMaxHeads];
+        edge_logits<NV>(a, q, e, g, lane, hsel, z);
+#pragma unroll
+        for (int h = 0; h < kMaxHeads; ++h) {
+          z[h] = leaky(z[h], a.slope);
+          m[h] = fmaxf(m[h], z[h]);
+        }
+        const int i = e - beg;
+        if (lane < a.heads) {
+          if (i < kStash) stash[w][i][lane] = pick(z, lane);
+          else a.att_out[(int64_t)e * a.heads + lane] = pick(z, lane);
+        }
+      }
+      __syncwarp();
+      // pass 2: softmax denominators
+      float ssum[kMaxHeads];
+#pragma unroll
+      for (int h = 0; h < kMaxHeads; ++h) ssum[h] = 0.f;
+      for (int e = beg + lane; e < end; e += 32) {
+        const int i = e - beg;
+#pragma unroll
+        for (int h = 0; h < kMaxHeads; ++h)
+          if (h < a.heads) {
+            float l = (i < kStash) ? stash[w][i][h] : a.att_out[(int64_t)e * a.heads + h];
+            ssum[h] += expf(l - m[h]);
+          }
+      }
+      float inv[kMaxHeads];
+#pragma unroll
+      for (int h = 0; h < kMaxHeads; ++h) inv[h] = (h < a.heads) ? 1.f / fb::warp_sum(ssum[h]) : 0.f;
+      __syncwarp();
+      // pass 3: probabilities, dropout, weighted sum of V
+      for (int e = beg; e < end; ++e) {
+        const int i = e - beg;
+        float y[kMaxHeads], ds[kMaxHeads];
+#pragma unroll
+        for (int h = 0; h < kMaxHeads; ++h) {
+          float l = (h < a.heads) ? ((i < kStash) ? stash[w][i][h] : a.att_out[(int64_t)e * a.heads + h]) : 0.f;
+          y[h] = (h < a.heads) ? expf(l - m[h]) * inv[h] : 0.f;
+        }
+        __syncwarp();
+        if (lane < a.heads) a.att_out[(int64_t)e * a.heads + lane] = pick(y, lane);
+        drop_scale(e, a.heads, a.drop_p, a.seed, a.offset, a.mask_u, ds);
+#pragma unroll
+        for (int h = 0; h < kMaxHeads; ++h) y[h] *= ds[h];
+        float4 vr[NV];
+        load_row<NV>(a.v + (int64_t)e * a.ldkv, g, lane, vr);
+#pragma unroll
+        for (int t = 0; t < NV; ++t) {
+          acc[t].x = fmaf(pick(y, hsel[t][0]), vr[t].x, acc[t].x);
+          acc[t].y = fmaf(pick(y, hsel[t][1]), vr[t].y, acc[t].y);
+          acc[t].z = fmaf(pick(y, hsel[t][2]), vr[t].z, acc[t].z);
+          acc[t].w = fmaf(pick(y, hsel[t][3]), vr[t].w, acc[t].w);
+        }
+      }
+    }
+    if (orow >= 0) store_row<NV>(a.agg + orow * a.ldagg, g, lane, acc);
+    __syncwarp();
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_bwd(AttnArgs a) {
+  __shared__ float stash[kWarpsPerCta][kStash][kMaxHeads];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t n_dst = a.n_dst_dev ? (int64_t)(*a.n_dst_dev) : a.n_dst;
+  RowGeom g{a.dim / 4, a.dim / a.heads, a.heads};
+  int hsel[NV][4];
+  lane_heads<NV>(g, lane, hsel);
+  const bool need_dl = (a.dq != nullptr) || (a.dk != nullptr) || (a.dx != nullptr);
+  for (int64_t j = (int64_t)blockIdx.x * kWarpsPerCta + w; j < n_dst; j += (int64_t)gridDim.x * kWarpsPerCta) {
+    const int beg = a.rptr[j], end = a.rptr[j + 1];
+    const int64_t irow = seg_out_row(a, j, beg, end);
+    float4 dqa[NV];
+#pragma unroll
+    for (int t = 0; t < NV; ++t) dqa[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (end > beg && irow >= 0) {
+      float4 da[NV], q[NV];
+      load_row<NV>(a.dagg + irow * a.lddagg, g, lane, da);
+      if (!a.x) load_row<NV>(a.q + j * a.ldq, g, lane, q);
+      float sdot[kMaxHeads];
+#pragma unroll
+      for (int h = 0; h < kMaxHeads; ++h) sdot[h] = 0.f;
+      // pass 1: dL/d(att) through dropout, dV, and sum_e y * dL/dy per head
+      for (int e = beg; e < end; ++e) {
+        float4 vr[NV];
+        load_row<NV>(a.v + (int64_t)e * a.ldkv, g, lane, vr);
+        float datt[kMaxHeads], ds[kMaxHeads], y[kMaxHeads];
+        head_dots<NV>(da, vr, hsel, a.heads, datt);
+        drop_scale(e, a.heads, a.drop_p, a.seed, a.offset, a.mask_u, ds);
+#pragma unroll
+        for (int h = 0; h < kMaxHeads; ++h) {
+          y[h] = (h < a.heads) ? __ldg(a.att + (int64_t)e * a.heads + h) : 0.f;
+          datt[h] *= ds[h];
+          sdot[h] = fmaf(y[h], datt[h], sdot[h]);
+        }
+        const int i = e - beg;
+        if (i < kStash && lane < a.heads) stash[w][i][lane] = pick(datt, lane);
+        if (a.dv) {
+          float4 o[NV];
+#pragma unroll
+          for (int t = 0; t < NV; ++t) {
+            o[t].x = pick(y, hsel[t][0]) * pick(ds, hsel[t][0]) * da[t].x;
+            o[t].y = pick(y, hsel[t][1]) * pick(ds, hsel[t][1]) * da[t].y;
+            o[t].z = pick(y, hsel[t][2]) * pick(ds, hsel[t][2]) * da[t].z;
+            o[t].w = pick(y, hsel[t][3]) * pick(ds, hsel[t][3]) * da[t].w;
+          }
+          store_row<NV>(a.dv + (int64_t)e * a.lddkv, g, lane, o);
+        }
+      }
+      __syncwarp();
+      if (need_dl) {
+        // pass 2: softmax and LeakyReLU backward, dK rows, dq accumulation
+        for (int e = beg; e < end; ++e) {
+          const int i = e - beg;
+          float dy[kMaxHeads];
+          if (i < kStash) {
+#pragma unroll
+            for (int h = 0; h < kMaxHeads; ++h) dy[h] = (h < a.heads) ? stash[w][i][h] : 0.f;
+          } else {
+            float4 vr[NV];
+            float ds[kMaxHeads];
+            load_row<NV>(a.v + (int64_t)e * a.ldkv, g, lane, vr);
+            head_dots<NV>(da, vr, hsel, a.heads, dy);
+            drop_scale(e, a.heads, a.drop_p, a.seed, a.offset, a.mask_u, ds);
+#pragma unroll
+            for (int h = 0; h < kMaxHeads; ++h) dy[h] *= ds[h];
+          }
+          float z[kMaxHeads], dz[kMaxHeads];
+          float4 kr[NV];
+          if (a.x) {
+#pragma unroll
+            for (int h = 0; h < kMaxHeads; ++h) z[h] = (h < a.heads) ? __ldg(a.x + (int64_t)e * a.heads + h) : 0.f;
+          } else {
+            load_row<NV>(a.k + (int64_t)e * a.ldkv, g, lane, kr);
+            head_dots<NV>(q, kr, hsel, a.heads, z);
+          }
+#pragma unroll
+          for (int h = 0; h < kMaxHeads; ++h) {
+            const float y = (h < a.heads) ? __ldg(a.att + (int64_t)e * a.heads + h) : 0.f;
+            const float dl = y * (dy[h] - sdot[h]);
+            dz[h] = z[h] > 0.f ? dl : dl * a.slope;
+          }
+          if (a.dx && lane < a.heads) a.dx[(int64_t)e * a.heads + lane] = pick(dz, lane);
+          if (!a.x) {
+            if (a.dk) {
+              float4 o[NV];
+#pragma unroll
+              for (int t = 0; t < NV; ++t) {
+                o[t].x = pick(dz, hsel[t][0]) * q[t].x;
+                o[t].y = pick(dz, hsel[t][1]) * q[t].y;
+                o[t].z = pick(dz, hsel[t][2]) * q[t].z;
+                o[t].w = pick(dz, hsel[t][3]) * q[t].w;
+              }
+              store_row<NV>(a.dk + (int64_t)e * a.lddkv, g, lane, o);
+            }
+#pragma unroll
+            for (int t = 0; t < NV; ++t) {
+              dqa[t].x = fmaf(pick(dz, hsel[t][0]), kr[t].x, dqa[t].x);
+              dqa[t].y = fmaf(pick(dz, hsel[t][1]), kr[t].y, dqa[t].y);
+              dqa[t].z = fmaf(pick(dz, hsel[t][2]), kr[t].z, dqa[t].z);
+              dqa[t].w = fmaf(pick(dz, hsel[t][3]), kr[t].w, dqa[t].w);
+            }
+          }
+        }
+      }
+    }
+    if (a.dq) store_row<NV>(a.dq + j * (int64_t)a.dim, g, lane, dqa);
+    __syncwarp();
+  }
+}
+
+int attn_grid(int64_t n_dst) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int64_t need = (n_dst + kWarpsPerCta - 1) / kWarpsPerCta;
+  int64_t cap = (int64_t)sms * 8;  // 8 resident CTAs of 8 warps per SM
+  return (int)std::max<int64_t>(1, std::min(need, cap));
+}
+
+bool aligned16(const void *p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_attn(const AttnArgs &a, bool bwd) {
+  if (a.dim <= 0 || a.dim % 4 || a.dim > 512 || a.heads < 1 || a.heads > kMaxHeads || a.dim % a.heads)
+    return fb::set_error(FB_ERR_UNSUPPORTED,
+                         "attention: need dim % 4 == 0, dim <= 512, 1 <= heads <= 4, dim % heads == 0");
+  if ((!a.x && (!a.q || !a.k)) || !a.v || !a.rptr || a.n_dst < 0 || a.ldkv % 4 || a.ldq % 4 || a.ldkv < 0 ||
+      a.ldq < 0)
+    return fb::set_error(FB_ERR_ARG, "attention: bad pointer or leading dimension (multiples of 4 floats)");
+  if (!aligned16(a.q) || !aligned16(a.k) || !aligned16(a.v))
+    return fb::set_error(FB_ERR_ARG, "attention: q/k/v must be 16-byte aligned");
+  if (!(a.drop_p >= 0.f && a.drop_p < 1.f)) return fb::set_error(FB_ERR_ARG, "attention: dropout p must be in [0, 1)");
+  if (!bwd) {
+    if (!a.att_out || !a.agg || a.ldagg % 4 || !aligned16(a.agg))
+      return fb::set_error(FB_ERR_ARG, "attn_fwd: bad att/agg output");
+  } else {
+    if (!a.att || !a.dagg || a.lddagg % 4 || !aligned16(a.dagg) || a.lddkv % 4 || !aligned16(a.dk) ||
+        !aligned16(a.dv) || !aligned16(a.dq))
+      return fb::set_error(FB_ERR_ARG, "attn_bwd: bad gradient buffers");
+  }
+  return FB_OK;
+}
+
+int launch_fwd(const AttnArgs &a, cudaStream_t stream) {
+  int rc = check_attn(a, false);
+  if (rc) return rc;
+  if (a.n_dst == 0) return FB_OK;
+  const int grid = attn_grid(a.n_dst), nv = (a.dim / 4 + 31) / 32;
+  switch (nv) {
+    case 1: k_attn_fwd<1><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a); break;
+    case 2: k_attn_fwd<2><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a); break;
+    case 3: k_attn_fwd<3><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a); break;
+    default: k_attn_fwd<4><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a); break;
+  }
+  FB_LAUNCHED("k_attn_fwd");
+  return FB_OK;
+}
+
+int launch_bwd(const AttnArgs &a, cudaStream_t stream) {
+  int rc = check_attn(a, true);
+  if (rc) return rc;
+  if (a.n_dst == 0) return FB_OK;
+  const int grid = attn_grid(a.n_dst), nv = (a.dim / 4 + 31) / 32;
+  switch (nv) {
+    case 1: k_attn_bwd<1><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a); break;
+    case 2: k_attn_bwd<2><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a); break;
+    case 3: k_attn_bwd<3><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a); break;
+    default: k_attn_bwd<4><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a); break;
+  }
+  FB_LAUNCHED("k_attn_bwd");
+  return FB_OK;
+}
+
+__global__ void k_dropout_scale(int64_t E, int heads, float p, uint64_t seed, uint64_t offset, float *out) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= E) return;
+  float s[kMaxHeads];
+  drop_scale(e, heads, p, seed, offset, nullptr, s);
+  for (int h = 0; h < heads; ++h) out[e * heads + h] = s[h];
+}
+
+}  // namespace
+
+extern "C" int fb_dropout_scale(int64_t n_edges, int heads, float drop_p, uint64_t seed, uint64_t offset, float *out,
+                                cudaStream_t stream) {
+  if (n_edges < 0 || heads < 1 || heads > kMaxHeads || !(drop_p >= 0.f && drop_p < 1.f) || (n_edges && !out))
+    return fb::set_error(FB_ERR_ARG, "dropout_scale: bad argument");
+  if (n_edges == 0) return FB_OK;
+  k_dropout_scale<<<(unsigned)((n_edges + 255) / 256), 256, 0, stream>>>(n_edges, heads, drop_p, seed, offset, out);
+  FB_LAUNCHED("k_dropout_scale");
+  return FB_OK;
+}
+
+extern "C" int fb_attn_fwd(const float *q, int64_t ldq, const float *k, const float *v, int64_t ldkv,
+                           const int32_t *rptr, int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim,
+                           float slope, float drop_p, uint64_t seed, uint64_t offset, float *att, float *agg,
+                           int64_t ldagg, cudaStream_t stream) {
+  AttnArgs a{};
+  a.q = q; a.ldq = ldq; a.k = k; a.v = v; a.ldkv = ldkv; a.rptr = rptr; a.n_dst = n_dst; a.n_dst_dev = n_dst_dev;
+  a.heads = heads; a.dim = dim; a.slope = slope; a.drop_p = drop_p; a.seed = seed; a.offset = offset;
+  a.att_out = att; a.agg = agg; a.ldagg = ldagg;
+  return launch_fwd(a, stream);
+}
+
+extern "C" int fb_attn_bwd(const float *q, int64_t ldq, const float *k, const float *v, int64_t ldkv,
+                           const int32_t *rptr, int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim,
+                           float slope, float drop_p, uint64_t seed, uint64_t offset, const float *att,
+                           const float *dagg, int64_t lddagg, float *dq, float *dk, float *dv, int64_t lddkv,
+                           cudaStream_t stream) {
+  AttnArgs a{};
+  a.q = q; a.ldq = ldq; a.k = k; a.v = v; a.ldkv = ldkv; a.rptr = rptr; a.n_dst = n_dst; a.n_dst_dev = n_dst_dev;
+  a.heads = heads; a.dim = dim; a.slope = slope; a.drop_p = drop_p; a.seed = seed; a.offset = offset;
+  a.att = att; a.dagg = dagg; a.lddagg = lddagg; a.dq = dq; a.dk = dk; a.dv = dv; a.lddkv = lddkv;
+  return launch_bwd(a, stream);
+}
+
+extern "C" int fb_attn_logits_fwd(const float *x, const float *v, int64_t ldv, const int32_t *indptr, int64_t n_seg,
+                                  const int64_t *seg_row, int64_t n_out, int heads, int dim, float slope,
+                                  float drop_p, const float *mask_u, float *att, float *agg, cudaStream_t stream) {
+  AttnArgs a{};
+  a.n_out = n_out;
+  a.x = x; a.v = v; a.ldkv = ldv; a.rptr = indptr; a.n_dst = n_seg; a.seg_row = seg_row; a.heads = heads;
+  a.dim = dim; a.slope = slope; a.drop_p = drop_p; a.mask_u = mask_u; a.att_out = att; a.agg = agg; a.ldagg = dim;
+  if (!x) return fb::set_error(FB_ERR_ARG, "attn_logits_fwd: x is required");
+  return launch_fwd(a, stream);
+}
+
+extern "C" int fb_attn_logits_bwd(const float *x, const float *v, int64_t ldv, const int32_t *indptr, int64_t n_seg,
+                                  const int64_t *seg_row, int64_t n_out, int heads, int dim, float slope,
+                                  float drop_p, const float *mask_u, const float *att, const float *dagg, float *dx,
+                                  float *dv, cudaStream_t stream) {
+  AttnArgs a{};
+  a.n_out = n_out;
+  a.x = x; a.v = v; a.ldkv = ldv; a.rptr = indptr; a.n_dst = n_seg; a.seg_row = seg_row; a.heads = heads;
+  a.dim = dim; a.slope = slope; a.drop_p = drop_p; a.mask_u = mask_u; a.att = att; a.dagg = dagg; a.lddagg = dim;
+  a.dx = dx; a.dv = dv; a.lddkv = ldv;
+  if (!x) return fb::set_error(FB_ERR_ARG, "attn_logits_bwd: x is required");
+  return launch_bwd(a, stream);
+}

@@ -1,0 +1,141 @@
+// Feature gather fused with the cos time encoding, and its backward.
+//
+// Reference: prepare_input gathers node_feats[ID] / edge_feats[eID] on the
+// host and copies them over PCIe (utils.py:126-196); TimeEncode computes
+// cos(Linear(1, d)(dt)) (layers.py:8-29); the attention layer concatenates
+// [h_src | f | time] as the K/V projection input (layers.py:157-164).
+// Here one kernel reads the device-resident tables and writes the
+// concatenated projection rows directly.
+//
+// Rounding: torch's CPU Linear(1, d) produces w*dt + b with one rounding
+// (a fused multiply-add); with dt up to ~1e8 the argument of cos is large and
+// a second rounding changes the feature by O(1), so the kernel uses fmaf.
+#include "runtime.cuh"
+
+namespace {
+
+constexpr int kRowsPerCta = 8;
+
+template <bool VEC>
+__device__ __forceinline__ void copy_seg(const float *__restrict__ src, float *__restrict__ dst, int n, int lane) {
+  if (VEC) {
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+    float4 *d4 = reinterpret_cast<float4 *>(dst);
+    for (int c = lane; c < (n >> 2); c += 32) d4[c] = __ldg(s4 + c);
+  } else {
+    for (int c = lane; c < n; c += 32) dst[c] = __ldg(src + c);
+  }
+}
+
+struct GatherArgs {
+  const float *h; int64_t ldh; const int32_t *h_idx; int64_t h_off; int dn;
+  const float *f; int64_t ldf; const int32_t *f_idx; int de;
+  const float *dt, *w, *b; int dtime;
+  float *A; int64_t lda; int64_t n_rows; const int32_t *n_rows_dev;
+};
+
+template <bool VEC>
+__global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode(GatherArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n = a.n_rows_dev ? (int64_t)(*a.n_rows_dev) : a.n_rows;
+  for (int64_t r = (int64_t)blockIdx.x * kRowsPerCta + (threadIdx.x >> 5); r < n;
+       r += (int64_t)gridDim.x * kRowsPerCta) {
+    float *out = a.A + r * a.lda;
+    if (a.dn > 0) {
+      const int64_t hr = a.h_idx ? (int64_t)a.h_idx[r] : r + a.h_off;
+      copy_seg<VEC>(a.h + hr * a.ldh, out, a.dn, lane);
+    }
+    if (a.de > 0) {
+      const int64_t fr = a.f_idx ? (int64_t)a.f_idx[r] : r;
+      copy_seg<VEC>(a.f + fr * a.ldf, out + a.dn, a.de, lane);
+    }
+    if (a.dtime > 0) {
+      const float t = a.dt ? a.dt[r] : 0.f;
+      float *o = out + a.dn + a.de;
+      for (int c = lane; c < a.dtime; c += 32) o[c] = cosf(fmaf(t, __ldg(a.w + c), __ldg(a.b + c)));
+    }
+  }
+}
+
+// Time-encoding backward, stage 1: per-CTA partial sums over a row chunk.
+__global__ void __launch_bounds__(256) k_te_bwd_part(const float *__restrict__ g, int64_t ldg,
+                                                     const float *__restrict__ dt, const float *__restrict__ w,
+                                                     const float *__restrict__ b, int dtime, int64_t n_rows,
+                                                     const int32_t *n_rows_dev, int64_t rows_per_cta,
+                                                     float *__restrict__ part) {
+  const int64_t n = n_rows_dev ? (int64_t)(*n_rows_dev) : n_rows;
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
+  const int64_t r1 = min(n, r0 + rows_per_cta);
+  for (int c = threadIdx.x; c < dtime; c += blockDim.x) {
+    const float wc = w[c], bc = b[c];
+    float sw = 0.f, sb = 0.f;
+    for (int64_t r = r0; r < r1; ++r) {
+      const float t = dt[r];
+      const float gs = -sinf(fmaf(t, wc, bc)) * g[r * ldg + c];
+      sw = fmaf(gs, t, sw);
+      sb += gs;
+    }
+    part[((int64_t)blockIdx.x * 2 + 0) * dtime + c] = sw;
+    part[((int64_t)blockIdx.x * 2 + 1) * dtime + c] = sb;
+  }
+}
+
+// Stage 2: fixed-order sum of the partials (deterministic).
+__global__ void k_te_bwd_reduce(const float *__restrict__ part, int nparts, int dtime, float *dw, float *db) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= dtime) return;
+  float sw = 0.f, sb = 0.f;
+  for (int p = 0; p < nparts; ++p) {
+    sw += part[((int64_t)p * 2 + 0) * dtime + c];
+    sb += part[((int64_t)p * 2 + 1) * dtime + c];
+  }
+  dw[c] += sw;
+  db[c] += sb;
+}
+
+constexpr int64_t kTeRowsPerCta = 512;
+constexpr int kTeMaxParts = 4096;
+
+inline bool a16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" int fb_gather_time_encode(const float *h, int64_t ldh, const int32_t *h_idx, int64_t h_off, int dn,
+                                     const float *f, int64_t ldf, const int32_t *f_idx, int de, const float *dt,
+                                     const float *w, const float *b, int dtime, float *A, int64_t lda,
+                                     int64_t n_rows, const int32_t *n_rows_dev, cudaStream_t stream) {
+  if (!A || n_rows < 0 || dn < 0 || de < 0 || dtime < 0 || lda < dn + de + dtime || (dn > 0 && !h) ||
+      (de > 0 && !f) || (dtime > 0 && (!w || !b)))
+    return fb::set_error(FB_ERR_ARG, "gather_time_encode: bad argument");
+  if (n_rows == 0) return FB_OK;
+  GatherArgs a{h, ldh, h_idx, h_off, dn, f, ldf, f_idx, de, dt, w, b, dtime, A, lda, n_rows, n_rows_dev};
+  const bool vec = (dn % 4 == 0) && (de % 4 == 0) && (lda % 4 == 0) && (ldh % 4 == 0 || dn == 0) &&
+                   (ldf % 4 == 0 || de == 0) && a16(A) && (dn == 0 || a16(h)) && (de == 0 || a16(f));
+  int64_t need = (n_rows + kRowsPerCta - 1) / kRowsPerCta;
+  int grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, 148 * 16));
+  if (vec) k_gather_time_encode<true><<<grid, 32 * kRowsPerCta, 0, stream>>>(a);
+  else k_gather_time_encode<false><<<grid, 32 * kRowsPerCta, 0, stream>>>(a);
+  FB_LAUNCHED("k_gather_time_encode");
+  return FB_OK;
+}
+
+extern "C" size_t fb_time_encode_bwd_ws_bytes(int64_t n_rows, int dtime) {
+  int64_t rows = std::max<int64_t>(kTeRowsPerCta, (n_rows + kTeMaxParts - 1) / kTeMaxParts);
+  int64_t parts = std::max<int64_t>(1, (n_rows + rows - 1) / rows);
+  return (size_t)(parts * 2 * std::max(dtime, 1)) * sizeof(float);
+}
+
+extern "C" int fb_time_encode_bwd(const float *g, int64_t ldg, const float *dt, const float *w, const float *b,
+                                  int dtime, int64_t n_rows, const int32_t *n_rows_dev, float *dw, float *db,
+                                  void *ws, cudaStream_t stream) {
+  if (!g || !dt || !w || !b || !dw || !db || !ws || dtime < 1 || n_rows < 0)
+    return fb::set_error(FB_ERR_ARG, "time_encode_bwd: bad argument");
+  int64_t rows = std::max<int64_t>(kTeRowsPerCta, (n_rows + kTeMaxParts - 1) / kTeMaxParts);
+  int parts = (int)std::max<int64_t>(1, (n_rows + rows - 1) / rows);
+  float *part = static_cast<float *>(ws);
+  k_te_bwd_part<<<parts, 256, 0, stream>>>(g, ldg, dt, w, b, dtime, n_rows, n_rows_dev, rows, part);
+  FB_LAUNCHED("k_te_bwd_part");
+  k_te_bwd_reduce<<<(dtime + 127) / 128, 128, 0, stream>>>(part, parts, dtime, dw, db);
+  FB_LAUNCHED("k_te_bwd_reduce");
+  return FB_OK;
+}

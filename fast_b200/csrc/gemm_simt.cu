@@ -1,0 +1,255 @@
+// fp32 projection GEMMs on the CUDA cores (FFMA), exact fp32 arithmetic.
+//   NT: C[m,n] = sum_k A[m,k] B[n,k] + bias[n]      (nn.Linear forward / dX)
+//   TN: C[n,k] = sum_m G[m,n] X[m,k]                 (nn.Linear weight grad)
+// 128x64 CTA tiles, 16-deep k slices staged through shared memory with a
+// register prefetch of the next slice, 8x4 outputs per thread.  The TN form
+// splits the long m reduction over CTAs and sums the partials in a fixed
+// order, so every result is deterministic.
+#include <algorithm>
+#include "runtime.cuh"
+
+namespace {
+
+constexpr int BM = 128, BN = 64, BK = 16, PAD = 4, NT = 256;
+
+__device__ __forceinline__ void tile_fma(float (&acc)[8][4], const float (*As)[BM + PAD], const float (*Bs)[BN + PAD],
+                                         int ty, int tx) {
+#pragma unroll
+  for (int kk = 0; kk < BK; ++kk) {
+    float4 a0 = *reinterpret_cast<const float4 *>(&As[kk][ty * 8]);
+    float4 a1 = *reinterpret_cast<const float4 *>(&As[kk][ty * 8 + 4]);
+    float4 b = *reinterpret_cast<const float4 *>(&Bs[kk][tx * 4]);
+    float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    float bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+  }
+}
+
+__device__ __forceinline__ float4 ld4_guard(const float *p, int64_t row, int64_t nrows, int col, int ncols, int64_t ld,
+                                            bool vec) {
+  if (row >= nrows) return make_float4(0.f, 0.f, 0.f, 0.f);
+  const float *q = p + row * ld + col;
+  if (vec && col + 3 < ncols) return __ldg(reinterpret_cast<const float4 *>(q));
+  float4 r;
+  r.x = (col + 0 < ncols) ? __ldg(q + 0) : 0.f;
+  r.y = (col + 1 < ncols) ? __ldg(q + 1) : 0.f;
+  r.z = (col + 2 < ncols) ? __ldg(q + 2) : 0.f;
+  r.w = (col + 3 < ncols) ? __ldg(q + 3) : 0.f;
+  return r;
+}
+
+// C[M,N] = A[M,K] * B[N,K]^T
+__global__ void __launch_bounds__(NT) k_gemm_nt(const float *__restrict__ A, int64_t lda, const float *__restrict__ B,
+                                                int64_t ldb, const float *__restrict__ bias, float *__restrict__ C,
+                                                int64_t ldc, int64_t M_host, const int32_t *M_dev, int N, int K,
+                                                int accumulate, bool vecA, bool vecB) {
+  __shared__ __align__(16) float As[2][BK][BM + PAD];
+  __shared__ __align__(16) float Bs[2][BK][BN + PAD];
+  const int64_t M = M_dev ? (int64_t)(*M_dev) : M_host;
+  const int64_t m0 = (int64_t)blockIdx.y * BM;
+  const int n0 = blockIdx.x * BN;
+  if (m0 >= M) return;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  float acc[8][4] = {};
+  // loader coordinates: A 128x16 = 512 float4 (2 per thread), B 64x16 = 256 float4
+  const int ar0 = tid >> 2, ac = (tid & 3) * 4;  // rows ar0 and ar0 + 64
+  const int br = tid >> 2, bc = (tid & 3) * 4;
+  float4 ra0, ra1, rb;
+  auto load = [&](int k0) {
+    ra0 = ld4_guard(A, m0 + ar0, M, k0 + ac, K, lda, vecA);
+    ra1 = ld4_guard(A, m0 + ar0 + 64, M, k0 + ac, K, lda, vecA);
+    rb = ld4_guard(B, n0 + br, N, k0 + bc, K, ldb, vecB);
+  };
+  auto stash = [&](int buf) {
+    As[buf][ac + 0][ar0] = ra0.x; As[buf][ac + 1][ar0] = ra0.y;
+    As[buf][ac + 2][ar0] = ra0.z; As[buf][ac + 3][ar0] = ra0.w;
+    As[buf][ac + 0][ar0 + 64] = ra1.x; As[buf][ac + 1][ar0 + 64] = ra1.y;
+    As[buf][ac + 2][ar0 + 64] = ra1.z; As[buf][ac + 3][ar0 + 64] = ra1.w;
+    Bs[buf][bc + 0][br] = rb.x; Bs[buf][bc + 1][br] = rb.y;
+    Bs[buf][bc + 2][br] = rb.z; Bs[buf][bc + 3][br] = rb.w;
+  };
+  const int nk = (K + BK - 1) / BK;
+  load(0);
+  stash(0);
+  __syncthreads();
+  for (int t = 0; t < nk; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < nk) load((t + 1) * BK);
+    tile_fma(acc, As[buf], Bs[buf], ty, tx);
+    if (t + 1 < nk) stash(buf ^ 1);
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t m = m0 + ty * 8 + i;
+    if (m >= M) break;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx * 4 + j;
+      if (n < N) {
+        float v = acc[i][j];
+        if (bias) v += bias[n];
+        float *c = C + m * ldc + n;
+        *c = accumulate ? (*c + v) : v;
+      }
+    }
+  }
+}
+
+// P[split][N][K] = sum_{m in split} G[m,n] X[m,k]
+__global__ void __launch_bounds__(NT) k_gemm_tn(const float *__restrict__ G, int64_t ldg, const float *__restrict__ X,
+                                                int64_t ldx, float *__restrict__ P, int64_t ldp, int64_t M_host,
+                                                const int32_t *M_dev, int N, int K, int64_t rows_per_split,
+                                                bool vecG, bool vecX) {
+  __shared__ __align__(16) float Gs[2][BK][BM + PAD];
+  __shared__ __align__(16) float Xs[2][BK][BN + PAD];
+  const int64_t M = M_dev ? (int64_t)(*M_dev) : M_host;
+  const int n0 = blockIdx.y * BM, k0 = blockIdx.x * BN;
+  const int64_t s0 = (int64_t)blockIdx.z * rows_per_split;
+  const int64_t s1 = min(M, s0 + rows_per_split);
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  float acc[8][4] = {};
+  // loader: G slice 16 x 128 (2 float4 per thread), X slice 16 x 64 (1 float4)
+  const int gr = tid >> 5, gc = (tid & 31) * 4;  // rows gr and gr + 8
+  const int xr = tid >> 4, xc = (tid & 15) * 4;
+  float4 rg0, rg1, rx;
+  auto load = [&](int64_t m) {
+    rg0 = ld4_guard(G, m + gr, s1, n0 + gc, N, ldg, vecG);
+    rg1 = ld4_guard(G, m + gr + 8, s1, n0 + gc, N, ldg, vecG);
+    rx = ld4_guard(X, m + xr, s1, k0 + xc, K, ldx, vecX);
+  };
+  auto stash = [&](int buf) {
+    *reinterpret_cast<float4 *>(&Gs[buf][gr][gc]) = rg0;
+    *reinterpret_cast<float4 *>(&Gs[buf][gr + 8][gc]) = rg1;
+    *reinterpret_cast<float4 *>(&Xs[buf][xr][xc]) = rx;
+  };
+  if (s0 < s1) {
+    const int64_t nt = (s1 - s0 + BK - 1) / BK;
+    load(s0);
+    stash(0);
+    __syncthreads();
+    for (int64_t t = 0; t < nt; ++t) {
+      const int buf = (int)(t & 1);
+      if (t + 1 < nt) load(s0 + (t + 1) * BK);
+      tile_fma(acc, Gs[buf], Xs[buf], ty, tx);
+      if (t + 1 < nt) stash(buf ^ 1);
+      __syncthreads();
+    }
+  }
+  float *out = P + (int64_t)blockIdx.z * N * ldp;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int n = n0 + ty * 8 + i;
+    if (n >= N) break;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k = k0 + tx * 4 + j;
+      if (k < K) out[(int64_t)n * ldp + k] = acc[i][j];
+    }
+  }
+}
+
+__global__ void k_split_reduce(const float *__restrict__ P, int nsplit, int N, int K, float *__restrict__ C,
+                               int64_t ldc, int accumulate) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)N * K) return;
+  const int n = (int)(i / K), k = (int)(i % K);
+  float s = 0.f;
+  for (int p = 0; p < nsplit; ++p) s += P[(int64_t)p * N * K + i];
+  float *c = C + (int64_t)n * ldc + k;
+  *c = accumulate ? (*c + s) : s;
+}
+
+__global__ void __launch_bounds__(256) k_colsum_part(const float *__restrict__ G, int64_t ldg, int64_t M_host,
+                                                     const int32_t *M_dev, int N, int64_t rows_per_part,
+                                                     float *__restrict__ part) {
+  const int64_t M = M_dev ? (int64_t)(*M_dev) : M_host;
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per_part, r1 = min(M, r0 + rows_per_part);
+  for (int c = threadIdx.x; c < N; c += blockDim.x) {
+    float s = 0.f;
+    for (int64_t r = r0; r < r1; ++r) s += G[r * ldg + c];
+    part[(int64_t)blockIdx.x * N + c] = s;
+  }
+}
+
+__global__ void k_colsum_reduce(const float *__restrict__ part, int nparts, int N, float *db, int accumulate) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= N) return;
+  float s = 0.f;
+  for (int p = 0; p < nparts; ++p) s += part[(int64_t)p * N + c];
+  db[c] = accumulate ? db[c] + s : s;
+}
+
+inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Rows of the m reduction per split of the TN GEMM: enough splits to fill
+// the machine, never fewer than 256 rows each.
+inline int64_t tn_rows_per_split(int64_t M, int N, int K) {
+  const int64_t tiles = (int64_t)((N + BM - 1) / BM) * ((K + BN - 1) / BN);
+  const int64_t want = std::max<int64_t>(1, (148 * 4) / std::max<int64_t>(tiles, 1));
+  int64_t rows = (M + want - 1) / want;
+  rows = std::max<int64_t>(256, (rows + BK - 1) / BK * BK);
+  return rows;
+}
+
+constexpr int64_t kColsumRows = 1024;
+
+}  // namespace
+
+extern "C" int fb_gemm_nt(const float *A, int64_t lda, const float *B, int64_t ldb, const float *bias, float *C,
+                          int64_t ldc, int64_t M, const int32_t *M_dev, int N, int K, int accumulate,
+                          cudaStream_t stream) {
+  if (!A || !B || !C || M < 0 || N < 1 || K < 1 || lda < K || ldb < K || ldc < N)
+    return fb::set_error(FB_ERR_ARG, "gemm_nt: bad argument");
+  if (M == 0) return FB_OK;
+  const bool vecA = (lda % 4 == 0) && al16(A), vecB = (ldb % 4 == 0) && al16(B);
+  dim3 grid((N + BN - 1) / BN, (unsigned)((M + BM - 1) / BM));
+  if (grid.y > 65535u) return fb::set_error(FB_ERR_UNSUPPORTED, "gemm_nt: M too large for one launch");
+  k_gemm_nt<<<grid, NT, 0, stream>>>(A, lda, B, ldb, bias, C, ldc, M, M_dev, N, K, accumulate, vecA, vecB);
+  FB_LAUNCHED("k_gemm_nt");
+  return FB_OK;
+}
+
+extern "C" size_t fb_gemm_tn_ws_bytes(int64_t M, int N, int K) {
+  const int64_t rows = tn_rows_per_split(std::max<int64_t>(M, 1), N, K);
+  const int64_t ns = std::max<int64_t>(1, (M + rows - 1) / rows);
+  return (size_t)(ns * (int64_t)N * K) * sizeof(float);
+}
+
+extern "C" int fb_gemm_tn(const float *G, int64_t ldg, const float *X, int64_t ldx, float *C, int64_t ldc, int64_t M,
+                          const int32_t *M_dev, int N, int K, int accumulate, void *ws, cudaStream_t stream) {
+  if (!G || !X || !C || !ws || M < 0 || N < 1 || K < 1 || ldg < N || ldx < K || ldc < K)
+    return fb::set_error(FB_ERR_ARG, "gemm_tn: bad argument");
+  const int64_t rows = tn_rows_per_split(std::max<int64_t>(M, 1), N, K);
+  const int ns = (int)std::max<int64_t>(1, (M + rows - 1) / rows);
+  if (ns > 65535) return fb::set_error(FB_ERR_UNSUPPORTED, "gemm_tn: M too large");
+  const bool vecG = (ldg % 4 == 0) && al16(G), vecX = (ldx % 4 == 0) && al16(X);
+  float *P = static_cast<float *>(ws);
+  dim3 grid((K + BN - 1) / BN, (N + BM - 1) / BM, ns);
+  k_gemm_tn<<<grid, NT, 0, stream>>>(G, ldg, X, ldx, P, K, M, M_dev, N, K, rows, vecG, vecX);
+  FB_LAUNCHED("k_gemm_tn");
+  const int64_t tot = (int64_t)N * K;
+  k_split_reduce<<<(unsigned)((tot + 255) / 256), 256, 0, stream>>>(P, ns, N, K, C, ldc, accumulate);
+  FB_LAUNCHED("k_split_reduce");
+  return FB_OK;
+}
+
+extern "C" size_t fb_colsum_ws_bytes(int64_t M, int N) {
+  const int64_t parts = std::max<int64_t>(1, (M + kColsumRows - 1) / kColsumRows);
+  return (size_t)(parts * std::max(N, 1)) * sizeof(float);
+}
+
+extern "C" int fb_colsum(const float *G, int64_t ldg, float *db, int64_t M, const int32_t *M_dev, int N,
+                         int accumulate, void *ws, cudaStream_t stream) {
+  if (!G || !db || !ws || M < 0 || N < 1 || ldg < N) return fb::set_error(FB_ERR_ARG, "colsum: bad argument");
+  const int parts = (int)std::max<int64_t>(1, (M + kColsumRows - 1) / kColsumRows);
+  float *part = static_cast<float *>(ws);
+  k_colsum_part<<<parts, 256, 0, stream>>>(G, ldg, M, M_dev, N, kColsumRows, part);
+  FB_LAUNCHED("k_colsum_part");
+  k_colsum_reduce<<<(N + 127) / 128, 128, 0, stream>>>(part, parts, N, db, accumulate);
+  FB_LAUNCHED("k_colsum_reduce");
+  return FB_OK;
+}

@@ -1,0 +1,630 @@
+// Temporal neighbour sampler on the device: the stateful time pointers,
+// most-recent-k and uniform-k sampling, COO/CSR block construction and eid
+// dedup, all on one CUDA stream without host round trips.
+//
+// Reference: NoneBone/FAST getSamplerCore/sampler_core.cpp
+//   update_ts_ptr   :133-157   pointer scan          -> k_update_ptr (binary search + atomicMax)
+//   sample_layer    :458-595   per-root window/pick  -> k_sample_count + k_sample_write
+//   combine_coo     :185-456   concat / cntE / dedup -> scan offsets, rptr/cntE, k_dedup_*
+//   sample          :597-712   layer/history driver  -> fb_sampler_sample
+//
+// Layout per block (all device, int32 unless noted): row/col/eid[E], then
+// ts/dts(float)/nodes[R+E] with the R roots first, rptr[R+1] over every root,
+// cntE[S+1] over non-empty roots, dims[8] = {R, E, S, R+E, n_uni}.
+#include <algorithm>
+#include <climits>
+#include <vector>
+#include "runtime.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kErrRootRange = 1;
+
+struct BlockBuf {
+  int32_t *row = nullptr, *col = nullptr, *eid = nullptr, *nodes = nullptr;
+  int32_t *rptr = nullptr, *cntE = nullptr, *uniE = nullptr, *invE = nullptr;
+  float *ts = nullptr, *dts = nullptr;
+  int64_t cap_roots = 0, cap_edges = 0;
+};
+
+// First index in [lo, hi) with ts[i] > v (std::upper_bound on a sorted run).
+__device__ __forceinline__ int upper_bound_dev(const float *__restrict__ ts, int lo, int hi, float v) {
+  while (lo < hi) {
+    int mid = lo + ((hi - lo) >> 1);
+    if (v < __ldg(ts + mid)) hi = mid; else lo = mid + 1;
+  }
+  return lo;
+}
+
+struct SampleArgs {
+  const int32_t *indptr, *indices, *eid;
+  const float *ts;
+  int64_t n_nodes;
+  const int32_t *ptr_s, *ptr_e;  // pointer slots (nh-1-i) and (nh-i)
+  const int32_t *roots;
+  const float *rts;
+  int64_t R_host;
+  const int32_t *R_dev;
+  int use_ptr, num_history, neighs, recent, prop_time;
+  float wd, offset;
+  uint32_t key0, key1, call_lo, slot;
+  int32_t *err;
+};
+
+__device__ __forceinline__ int64_t num_roots(const SampleArgs &a) {
+  return a.R_dev ? (int64_t)(*a.R_dev) : a.R_host;
+}
+
+// The window [s, e] of one root (sampler_core.cpp:522-552).
+__device__ __forceinline__ void root_window(const SampleArgs &a, int n, float nts, int &s, int &e) {
+  if (a.use_ptr) {
+    s = a.ptr_s[n];
+    e = a.ptr_e[n];
+  } else if (a.num_history == 1) {
+    s = a.indptr[n];
+    int ub = upper_bound_dev(a.ts, a.indptr[n], a.indptr[n + 1], nts);
+    e = max(ub - 1, s);
+  } else {
+    int lo = a.indptr[n], hi = a.indptr[n + 1];
+    int ub = upper_bound_dev(a.ts, lo, hi, __fsub_rn(__fadd_rn(nts, a.offset), a.wd));
+    s = max(ub - 1, lo);
+    int ub2 = upper_bound_dev(a.ts, lo, hi, __fadd_rn(nts, a.offset));
+    e = max(ub2 - 1, s);
+  }
+}
+
+// Uniform pick number i of root j: s + floor(u * (e - s + 1)), u from Philox.
+__device__ __forceinline__ int uniform_pick(const SampleArgs &a, int64_t j, int i, int s, int e) {
+  fb::Philox4 r = fb::philox4x32_10((uint32_t)j, (uint32_t)(i >> 2), a.call_lo, a.slot, a.key0, a.key1);
+  uint32_t u = r.v[i & 3];
+  uint32_t span = (uint32_t)(e - s + 1);
+  return s + (int)(((uint64_t)u * (uint64_t)span) >> 32);
+}
+
+// Visits the kept neighbours of root j in the reference order; f(k) per edge.
+template <typename F>
+__device__ __forceinline__ void for_each_pick(const SampleArgs &a, int64_t j, int n, float nts, F f) {
+  int s, e;
+  root_window(a, n, nts, s, e);
+  const float keep_thr = __fsub_rn(__fadd_rn(nts, a.offset), 1e-7f);
+  if (a.recent || (e - s < a.neighs)) {
+    const int lo = max(s, e - a.neighs);
+    for (int k = e; k > lo; --k)
+      if (__ldg(a.ts + k) < keep_thr) f(k);
+  } else {
+    for (int i = 0; i < a.neighs; ++i) {
+      int k = uniform_pick(a, j, i, s, e);
+      if (__ldg(a.ts + k) < keep_thr) f(k);
+    }
+  }
+}
+
+__global__ void k_reset(const int32_t *__restrict__ indptr, int32_t *__restrict__ ptr, int64_t n_nodes,
+                        int nslots) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_nodes) return;
+  int32_t v = indptr[i];
+  for (int s = 0; s < nslots; ++s) ptr[s * n_nodes + i] = v;
+}
+
+// update_ts_ptr (sampler_core.cpp:133-157).  With per-node time-sorted
+// edges the reference scan leaves ptr = max(ptr, ub - 1), ub = first edge with
+// ts > root_ts + offset - 1e-7f; a max is order independent, so every root
+// applies its candidate with one atomicMax instead of a per-node lock.
+__global__ void k_update_ptr(const int32_t *__restrict__ indptr, const float *__restrict__ ts,
+                             int64_t n_nodes, int32_t *__restrict__ ptr, const int32_t *__restrict__ roots,
+                             const float *__restrict__ rts, int64_t R_host, const int32_t *R_dev,
+                             float offset, int32_t *err) {
+  int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t R = R_dev ? (int64_t)(*R_dev) : R_host;
+  if (j >= R) return;
+  int n = roots[j];
+  if (n < 0 || n >= n_nodes) { atomicOr(err, kErrRootRange); return; }
+  int beg = indptr[n], end = indptr[n + 1];
+  if (end <= beg) return;
+  float thr = __fsub_rn(__fadd_rn(rts[j], offset), 1e-7f);
+  int ub = upper_bound_dev(ts, beg, end, thr);
+  if (ub > beg) atomicMax(ptr + n, ub - 1);
+}
+
+// Pass 1: kept-edge count per root plus per-CTA partial sums (edges, non-empty rows).
+__global__ void __launch_bounds__(kThreads) k_sample_count(SampleArgs a, int32_t *__restrict__ cnt,
+                                                           int2 *__restrict__ part) {
+  __shared__ int sm[64];
+  int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t R = num_roots(a);
+  int c = 0;
+  if (j < R) {
+    int n = a.roots[j];
+    if (n >= 0 && n < a.n_nodes) {
+      for_each_pick(a, j, n, a.rts[j], [&](int) { ++c; });
+    } else {
+      atomicOr(a.err, kErrRootRange);
+    }
+    cnt[j] = c;
+  }
+  int ea, eb;
+  int2 tot = fb::block_excl_scan2(c, c > 0 ? 1 : 0, ea, eb, sm);
+  if (threadIdx.x == 0) part[blockIdx.x] = tot;
+}
+
+// Pass 2: one CTA turns the partial sums into exclusive CTA offsets and
+// publishes the block dims; it also writes the closing entries of rptr/cntE.
+__global__ void __launch_bounds__(1024) k_scan_parts(int2 *__restrict__ part, int nparts, int64_t R_host,
+                                                     const int32_t *R_dev, int32_t *__restrict__ dims,
+                                                     int32_t *__restrict__ rptr, int32_t *__restrict__ cntE) {
+  __shared__ int sm[64];
+  int runA = 0, runB = 0;
+  for (int base = 0; base < nparts; base += blockDim.x) {
+    int i = base + threadIdx.x;
+    int2 v = i < nparts ? part[i] : make_int2(0, 0);
+    int ea, eb;
+    int2 tot = fb::block_excl_scan2(v.x, v.y, ea, eb, sm);
+    if (i < nparts) part[i] = make_int2(runA + ea, runB + eb);
+    runA += tot.x;
+    runB += tot.y;
+  }
+  if (threadIdx.x == 0) {
+    int R = R_dev ? *R_dev : (int)R_host;
+    dims[0] = R;
+    dims[1] = runA;
+    dims[2] = runB;
+    dims[3] = R + runA;
+    dims[4] = 0;
+    rptr[R] = runA;
+    if (runA > 0) cntE[runB] = runA;
+  }
+}
+
+// Pass 3: offsets from the CTA scan, then the COO/CSR writes.
+__global__ void __launch_bounds__(kThreads) k_sample_write(SampleArgs a, const int32_t *__restrict__ cnt,
+                                                           const int2 *__restrict__ part,
+                                                           int32_t *__restrict__ row, int32_t *__restrict__ col,
+                                                           int32_t *__restrict__ eid_out, float *__restrict__ ts_out,
+                                                           float *__restrict__ dts_out, int32_t *__restrict__ nodes_out,
+                                                           int32_t *__restrict__ rptr, int32_t *__restrict__ cntE) {
+  __shared__ int sm[64];
+  int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t R = num_roots(a);
+  int c = (j < R) ? cnt[j] : 0;
+  int ea, eb;
+  fb::block_excl_scan2(c, c > 0 ? 1 : 0, ea, eb, sm);
+  if (j >= R) return;
+  const int2 base = part[blockIdx.x];
+  const int off = base.x + ea;
+  const int seg = base.y + eb;
+  const int n = a.roots[j];
+  const float nts = a.rts[j];
+  ts_out[j] = nts;
+  dts_out[j] = 0.f;
+  nodes_out[j] = n;
+  rptr[j] = off;
+  if (c > 0) cntE[seg] = off;
+  if (n < 0 || n >= a.n_nodes) return;
+  int t = off;
+  for_each_pick(a, j, n, nts, [&](int k) {
+    float tk = __ldg(a.ts + k);
+    row[t] = (int32_t)j;
+    col[t] = (int32_t)(R + t);
+    eid_out[t] = __ldg(a.eid + k);
+    ts_out[R + t] = a.prop_time ? nts : tk;
+    dts_out[R + t] = __fsub_rn(nts, tk);
+    nodes_out[R + t] = __ldg(a.indices + k);
+    ++t;
+  });
+}
+
+// ---- eid dedup (combine_coo :414-451), first-appearance order -------------
+__global__ void k_dedup_init(int32_t *keys, int32_t *minpos, int64_t cap) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < cap) { keys[i] = -1; minpos[i] = INT_MAX; }
+}
+
+__device__ __forceinline__ uint32_t hash_eid(int32_t k) { return (uint32_t)k * 2654435761u; }
+
+__global__ void k_dedup_insert(const int32_t *__restrict__ eid, const int32_t *dims, int32_t *keys,
+                               int32_t *minpos, int32_t *slot, uint32_t mask) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= dims[1]) return;
+  int32_t k = eid[i];
+  uint32_t h = hash_eid(k) & mask;
+  // Linear probing; the table holds at least 2x the edges, so a free or
+  // matching slot is always found within `mask + 1` probes.
+  for (uint32_t probe = 0; probe <= mask; ++probe) {
+    int32_t prev = atomicCAS(keys + h, -1, k);
+    if (prev == -1 || prev == k) {
+      atomicMin(minpos + h, (int32_t)i);
+      slot[i] = (int32_t)h;
+      return;
+    }
+    h = (h + 1) & mask;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_dedup_count(const int32_t *dims, const int32_t *minpos,
+                                                          const int32_t *slot, int2 *part) {
+  __shared__ int sm[64];
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int first = (i < dims[1]) ? (minpos[slot[i]] == (int32_t)i) : 0;
+  int ea, eb;
+  int2 tot = fb::block_excl_scan2(first, 0, ea, eb, sm);
+  if (threadIdx.x == 0) part[blockIdx.x] = tot;
+}
+
+__global__ void __launch_bounds__(1024) k_dedup_scan(int2 *part, int nparts, int32_t *dims) {
+  __shared__ int sm[64];
+  int run = 0;
+  for (int base = 0; base < nparts; base += blockDim.x) {
+    int i = base + threadIdx.x;
+    int v = i < nparts ? part[i].x : 0;
+    int ea, eb;
+    int2 tot = fb::block_excl_scan2(v, 0, ea, eb, sm);
+    if (i < nparts) part[i].x = run + ea;
+    run += tot.x;
+  }
+  if (threadIdx.x == 0) dims[4] = run;
+}
+
+__global__ void __launch_bounds__(kThreads) k_dedup_emit(const int32_t *__restrict__ eid, const int32_t *dims,
+                                                         const int32_t *minpos, const int32_t *slot,
+                                                         const int2 *part, int32_t *uidx, int32_t *uniE) {
+  __shared__ int sm[64];
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int E = dims[1];
+  int first = (i < E) ? (minpos[slot[i]] == (int32_t)i) : 0;
+  int ea, eb;
+  fb::block_excl_scan2(first, 0, ea, eb, sm);
+  if (i < E && first) {
+    int u = part[blockIdx.x].x + ea;
+    uidx[i] = u;
+    uniE[u] = eid[i];
+  }
+}
+
+__global__ void k_dedup_inv(const int32_t *dims, const int32_t *minpos, const int32_t *slot,
+                            const int32_t *uidx, int32_t *invE) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= dims[1]) return;
+  invE[i] = uidx[minpos[slot[i]]];
+}
+
+inline int nblk(int64_t n, int t = kThreads) { return (int)std::max<int64_t>(1, (n + t - 1) / t); }
+
+}  // namespace
+
+struct fb_sampler {
+  int device = 0;
+  int64_t n_nodes = 0, n_edges = 0;
+  int32_t *indptr = nullptr, *indices = nullptr, *eid = nullptr;
+  float *ts = nullptr;
+  bool owns_graph = false;
+  int num_layers = 0, num_history = 1;
+  std::vector<int> neigh;
+  bool recent = true, prop_time = false;
+  float wd = 0.f;
+  uint64_t seed = 0, call_index = 0;
+  int32_t *ts_ptr = nullptr;   // (num_history + 1) slots x n_nodes
+  std::vector<BlockBuf> blocks;
+  int32_t *dims = nullptr;     // 8 per block
+  int32_t *err = nullptr;
+  int32_t *roots_in = nullptr;
+  float *rts_in = nullptr;
+  int64_t cap_r0 = 0;
+  int32_t *ws_cnt = nullptr;
+  int2 *ws_part = nullptr;
+  int64_t ws_cap_roots = 0;
+  int32_t *dd_keys = nullptr, *dd_minpos = nullptr, *dd_slot = nullptr, *dd_uidx = nullptr;
+  int2 *dd_part = nullptr;
+  int64_t dd_cap_edges = 0, dd_table = 0;
+  bool sampled = false;
+};
+
+namespace {
+
+void free_block(BlockBuf &b) {
+  int32_t *ip[] = {b.row, b.col, b.eid, b.nodes, b.rptr, b.cntE, b.uniE, b.invE};
+  for (auto p : ip) if (p) cudaFree(p);
+  if (b.ts) cudaFree(b.ts);
+  if (b.dts) cudaFree(b.dts);
+  b = BlockBuf();
+}
+
+int alloc_block(BlockBuf &b, int64_t cr, int64_t ce) {
+  free_block(b);
+  const int64_t ce1 = std::max<int64_t>(ce, 1), cn = cr + ce1;
+  FB_TRY_CUDA(cudaMalloc(&b.row, ce1 * 4));
+  FB_TRY_CUDA(cudaMalloc(&b.col, ce1 * 4));
+  FB_TRY_CUDA(cudaMalloc(&b.eid, ce1 * 4));
+  FB_TRY_CUDA(cudaMalloc(&b.uniE, ce1 * 4));
+  FB_TRY_CUDA(cudaMalloc(&b.invE, ce1 * 4));
+  FB_TRY_CUDA(cudaMalloc(&b.nodes, cn * 4));
+  FB_TRY_CUDA(cudaMalloc(&b.ts, cn * 4));
+  FB_TRY_CUDA(cudaMalloc(&b.dts, cn * 4));
+  FB_TRY_CUDA(cudaMalloc(&b.rptr, (cr + 1) * 4));
+  FB_TRY_CUDA(cudaMalloc(&b.cntE, (cr + 1) * 4));
+  b.cap_roots = cr;
+  b.cap_edges = ce;
+  return FB_OK;
+}
+
+// Capacity of every block for r0 layer-0 roots.
+void block_caps(const fb_sampler *s, int64_t r0, std::vector<int64_t> &cr, std::vector<int64_t> &ce) {
+  const int nh = s->num_history;
+  cr.assign(s->num_layers * nh, 0);
+  ce.assign(s->num_layers * nh, 0);
+  int64_t roots = r0;
+  for (int l = 0; l < s->num_layers; ++l) {
+    int64_t edges = roots * (int64_t)std::max(0, s->neigh[l]);
+    for (int h = 0; h < nh; ++h) { cr[l * nh + h] = roots; ce[l * nh + h] = edges; }
+    roots += edges;
+  }
+}
+
+int ensure_capacity(fb_sampler *s, int64_t r0) {
+  if (r0 <= s->cap_r0 && !s->blocks.empty()) return FB_OK;
+  FB_TRY_CUDA(cudaDeviceSynchronize());
+  std::vector<int64_t> cr, ce;
+  block_caps(s, r0, cr, ce);
+  int64_t max_roots = 0, total = 0;
+  for (size_t i = 0; i < cr.size(); ++i) {
+    max_roots = std::max(max_roots, cr[i]);
+    total += cr[i] + ce[i];
+  }
+  if (total > INT32_MAX) return fb::set_error(FB_ERR_UNSUPPORTED, "sampler: block sizes exceed int32 indexing");
+  s->blocks.resize(cr.size());
+  for (size_t i = 0; i < cr.size(); ++i) {
+    int rc = alloc_block(s->blocks[i], cr[i], ce[i]);
+    if (rc) return rc;
+  }
+  if (s->roots_in) cudaFree(s->roots_in);
+  if (s->rts_in) cudaFree(s->rts_in);
+  FB_TRY_CUDA(cudaMalloc(&s->roots_in, std::max<int64_t>(r0, 1) * 4));
+  FB_TRY_CUDA(cudaMalloc(&s->rts_in, std::max<int64_t>(r0, 1) * 4));
+  if (s->ws_cnt) cudaFree(s->ws_cnt);
+  if (s->ws_part) cudaFree(s->ws_part);
+  FB_TRY_CUDA(cudaMalloc(&s->ws_cnt, std::max<int64_t>(max_roots, 1) * 4));
+  FB_TRY_CUDA(cudaMalloc(&s->ws_part, nblk(max_roots) * sizeof(int2)));
+  s->ws_cap_roots = max_roots;
+  s->cap_r0 = r0;
+  return FB_OK;
+}
+
+int run_layer_slot(fb_sampler *s, int bidx, const int32_t *roots, const float *rts, int64_t R_host,
+                   const int32_t *R_dev, int64_t R_cap, int use_ptr, int hist_i, int neighs, float offset,
+                   cudaStream_t st) {
+  const int nh = s->num_history;
+  BlockBuf &b = s->blocks[bidx];
+  SampleArgs a;
+  a.indptr = s->indptr; a.indices = s->indices; a.eid = s->eid; a.ts = s->ts;
+  a.n_nodes = s->n_nodes;
+  a.ptr_s = s->ts_ptr + (int64_t)(nh - 1 - hist_i) * s->n_nodes;
+  a.ptr_e = s->ts_ptr + (int64_t)(nh - hist_i) * s->n_nodes;
+  a.roots = roots; a.rts = rts; a.R_host = R_host; a.R_dev = R_dev;
+  a.use_ptr = use_ptr; a.num_history = nh; a.neighs = neighs;
+  a.recent = s->recent; a.prop_time = s->prop_time;
+  a.wd = s->wd; a.offset = offset;
+  a.key0 = (uint32_t)s->seed; a.key1 = (uint32_t)(s->seed >> 32);
+  a.call_lo = (uint32_t)s->call_index; a.slot = (uint32_t)bidx;
+  a.err = s->err;
+  int32_t *dims = s->dims + 8 * bidx;
+  const int nb = nblk(R_cap);
+  k_sample_count<<<nb, kThreads, 0, st>>>(a, s->ws_cnt, s->ws_part);
+  FB_LAUNCHED("k_sample_count");
+  k_scan_parts<<<1, 1024, 0, st>>>(s->ws_part, nb, R_host, R_dev, dims, b.rptr, b.cntE);
+  FB_LAUNCHED("k_scan_parts");
+  k_sample_write<<<nb, kThreads, 0, st>>>(a, s->ws_cnt, s->ws_part, b.row, b.col, b.eid, b.ts, b.dts,
+                                          b.nodes, b.rptr, b.cntE);
+  FB_LAUNCHED("k_sample_write");
+  return FB_OK;
+}
+
+}  // namespace
+
+extern "C" int fb_sampler_create(const int32_t *indptr, const int32_t *indices, const int32_t *eid,
+                                 const float *ts, int64_t n_nodes, int64_t n_edges, int graph_on_device,
+                                 int num_layers, const int32_t *num_neighbors, int recent, int prop_time,
+                                 int num_history, float window_duration, uint64_t seed, fb_sampler **out) {
+  if (!out || !indptr || (n_edges > 0 && (!indices || !eid || !ts)) || n_nodes < 0 || n_edges < 0 ||
+      num_layers < 1 || num_history < 1 || !num_neighbors)
+    return fb::set_error(FB_ERR_ARG, "fb_sampler_create: bad argument");
+  if (n_edges >= INT32_MAX || n_nodes >= INT32_MAX)
+    return fb::set_error(FB_ERR_UNSUPPORTED, "fb_sampler_create: graph exceeds int32 ids");
+  auto *s = new fb_sampler();
+  FB_TRY_CUDA(cudaGetDevice(&s->device));
+  s->n_nodes = n_nodes; s->n_edges = n_edges;
+  s->num_layers = num_layers; s->num_history = num_history;
+  s->neigh.assign(num_neighbors, num_neighbors + num_layers);
+  s->recent = recent != 0; s->prop_time = prop_time != 0;
+  s->wd = window_duration; s->seed = seed;
+  if (graph_on_device) {
+    s->indptr = const_cast<int32_t *>(indptr);
+    s->indices = const_cast<int32_t *>(indices);
+    s->eid = const_cast<int32_t *>(eid);
+    s->ts = const_cast<float *>(ts);
+    s->owns_graph = false;
+  } else {
+    const int64_t e1 = std::max<int64_t>(n_edges, 1);
+    FB_TRY_CUDA(cudaMalloc(&s->indptr, (n_nodes + 1) * 4));
+    FB_TRY_CUDA(cudaMalloc(&s->indices, e1 * 4));
+    FB_TRY_CUDA(cudaMalloc(&s->eid, e1 * 4));
+    FB_TRY_CUDA(cudaMalloc(&s->ts, e1 * 4));
+    FB_TRY_CUDA(cudaMemcpy(s->indptr, indptr, (n_nodes + 1) * 4, cudaMemcpyHostToDevice));
+    if (n_edges > 0) {
+      FB_TRY_CUDA(cudaMemcpy(s->indices, indices, n_edges * 4, cudaMemcpyHostToDevice));
+      FB_TRY_CUDA(cudaMemcpy(s->eid, eid, n_edges * 4, cudaMemcpyHostToDevice));
+      FB_TRY_CUDA(cudaMemcpy(s->ts, ts, n_edges * 4, cudaMemcpyHostToDevice));
+    }
+    s->owns_graph = true;
+  }
+  FB_TRY_CUDA(cudaMalloc(&s->ts_ptr, std::max<int64_t>(n_nodes, 1) * 4 * (num_history + 1)));
+  FB_TRY_CUDA(cudaMalloc(&s->dims, 8 * 4 * num_layers * num_history));
+  FB_TRY_CUDA(cudaMemset(s->dims, 0, 8 * 4 * num_layers * num_history));
+  FB_TRY_CUDA(cudaMalloc(&s->err, 4));
+  FB_TRY_CUDA(cudaMemset(s->err, 0, 4));
+  *out = s;
+  return fb_sampler_reset(s, 0) == FB_OK ? (cudaDeviceSynchronize() == cudaSuccess ? FB_OK : FB_ERR_CUDA)
+                                         : FB_ERR_CUDA;
+}
+
+extern "C" int fb_sampler_destroy(fb_sampler *s) {
+  if (!s) return FB_OK;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  cudaSetDevice(s->device);
+  cudaDeviceSynchronize();
+  for (auto &b : s->blocks) free_block(b);
+  if (s->owns_graph) {
+    cudaFree(s->indptr); cudaFree(s->indices); cudaFree(s->eid); cudaFree(s->ts);
+  }
+  void *ps[] = {s->ts_ptr, s->dims, s->err, s->roots_in, s->rts_in, s->ws_cnt, s->ws_part,
+                s->dd_keys, s->dd_minpos, s->dd_slot, s->dd_uidx, s->dd_part};
+  for (auto p : ps) if (p) cudaFree(p);
+  cudaSetDevice(cur);
+  delete s;
+  return FB_OK;
+}
+
+extern "C" int fb_sampler_reset(fb_sampler *s, cudaStream_t st) {
+  if (!s) return fb::set_error(FB_ERR_ARG, "fb_sampler_reset: null sampler");
+  if (s->n_nodes == 0) return FB_OK;
+  k_reset<<<nblk(s->n_nodes), kThreads, 0, st>>>(s->indptr, s->ts_ptr, s->n_nodes, s->num_history + 1);
+  FB_LAUNCHED("k_reset");
+  return FB_OK;
+}
+
+extern "C" int fb_sampler_sample(fb_sampler *s, const int32_t *roots, const float *root_ts, int64_t n_roots,
+                                 int roots_on_device, cudaStream_t st) {
+  if (!s || n_roots < 0 || (n_roots > 0 && (!roots || !root_ts)))
+    return fb::set_error(FB_ERR_ARG, "fb_sampler_sample: bad argument");
+  int rc = ensure_capacity(s, n_roots);
+  if (rc) return rc;
+  const int32_t *r0 = roots;
+  const float *t0 = root_ts;
+  if (!roots_on_device && n_roots > 0) {
+    FB_TRY_CUDA(cudaMemcpyAsync(s->roots_in, roots, n_roots * 4, cudaMemcpyHostToDevice, st));
+    FB_TRY_CUDA(cudaMemcpyAsync(s->rts_in, root_ts, n_roots * 4, cudaMemcpyHostToDevice, st));
+    r0 = s->roots_in;
+    t0 = s->rts_in;
+  }
+  const int nh = s->num_history;
+  std::vector<int64_t> cr, ce;
+  block_caps(s, n_roots, cr, ce);
+  bool first = true;
+  for (int l = 0; l < s->num_layers; ++l) {
+    int use_ptr = 0;
+    if (first || (s->prop_time && nh == 1) || s->recent) { first = false; use_ptr = 1; }
+    const int neighs = s->neigh[l];
+    // Roots of the pointer update before the history loop (sampler_core.cpp:464-476).
+    const int32_t *ur = r0;
+    const float *ut = t0;
+    const int32_t *uR = nullptr;
+    if (l > 0) {
+      const int pb = (l - 1) * nh + nh - 1;
+      ur = s->blocks[pb].nodes; ut = s->blocks[pb].ts; uR = s->dims + 8 * pb + 3;
+    }
+    const int64_t rcap = cr[l * nh];
+    if (use_ptr && rcap > 0) {
+      k_update_ptr<<<nblk(rcap), kThreads, 0, st>>>(s->indptr, s->ts, s->n_nodes, s->ts_ptr + (int64_t)nh * s->n_nodes,
+                                                    ur, ut, n_roots, uR, 0.f, s->err);
+      FB_LAUNCHED("k_update_ptr");
+    }
+    for (int i = 0; i < nh; ++i) {
+      const int32_t *hr = r0;
+      const float *ht = t0;
+      const int32_t *hR = nullptr;
+      if (l > 0) {
+        const int pb = (l - 1) * nh + nh - 1 - i;
+        hr = s->blocks[pb].nodes; ht = s->blocks[pb].ts; hR = s->dims + 8 * pb + 3;
+      }
+      const float offset = (float)(-i) * s->wd;
+      if (use_ptr && fabsf(s->wd) > 1e-7f && rcap > 0) {
+        k_update_ptr<<<nblk(rcap), kThreads, 0, st>>>(s->indptr, s->ts, s->n_nodes,
+                                                      s->ts_ptr + (int64_t)(nh - 1 - i) * s->n_nodes, hr, ht,
+                                                      n_roots, hR, offset - s->wd, s->err);
+        FB_LAUNCHED("k_update_ptr");
+      }
+      rc = run_layer_slot(s, l * nh + nh - 1 - i, hr, ht, n_roots, hR, rcap, use_ptr, i, neighs, offset, st);
+      if (rc) return rc;
+    }
+  }
+  s->call_index++;
+  s->sampled = true;
+  return FB_OK;
+}
+
+extern "C" int fb_sampler_num_blocks(const fb_sampler *s) {
+  return s ? s->num_layers * s->num_history : 0;
+}
+
+extern "C" int fb_sampler_block(const fb_sampler *s, int i, fb_block_view *out) {
+  if (!s || !out || i < 0 || i >= (int)s->blocks.size())
+    return fb::set_error(FB_ERR_ARG, "fb_sampler_block: bad block index (sample() first)");
+  const BlockBuf &b = s->blocks[i];
+  out->row = b.row; out->col = b.col; out->eid = b.eid;
+  out->ts = b.ts; out->dts = b.dts; out->nodes = b.nodes;
+  out->rptr = b.rptr; out->cntE = b.cntE; out->uniE = b.uniE; out->invE = b.invE;
+  out->dims = s->dims + 8 * i;
+  out->max_roots = b.cap_roots;
+  out->max_edges = b.cap_edges;
+  return FB_OK;
+}
+
+extern "C" int fb_sampler_dims(fb_sampler *s, int32_t *host_dims, cudaStream_t st) {
+  if (!s || !host_dims) return fb::set_error(FB_ERR_ARG, "fb_sampler_dims: bad argument");
+  const int nb = s->num_layers * s->num_history;
+  int32_t err = 0;
+  FB_TRY_CUDA(cudaMemcpyAsync(host_dims, s->dims, 8 * 4 * nb, cudaMemcpyDeviceToHost, st));
+  FB_TRY_CUDA(cudaMemcpyAsync(&err, s->err, 4, cudaMemcpyDeviceToHost, st));
+  FB_TRY_CUDA(cudaStreamSynchronize(st));
+  if (err & kErrRootRange) {
+    cudaMemsetAsync(s->err, 0, 4, st);
+    return fb::set_error(FB_ERR_ARG, "sampler: a root node id is outside [0, num_nodes)");
+  }
+  return FB_OK;
+}
+
+extern "C" int fb_sampler_set_call_index(fb_sampler *s, uint64_t call_index) {
+  if (!s) return fb::set_error(FB_ERR_ARG, "fb_sampler_set_call_index: null sampler");
+  s->call_index = call_index;
+  return FB_OK;
+}
+
+extern "C" int fb_sampler_dedup(fb_sampler *s, int i, cudaStream_t st) {
+  if (!s || i < 0 || i >= (int)s->blocks.size())
+    return fb::set_error(FB_ERR_ARG, "fb_sampler_dedup: bad block index");
+  BlockBuf &b = s->blocks[i];
+  const int64_t ce = std::max<int64_t>(b.cap_edges, 1);
+  if (ce > s->dd_cap_edges) {
+    FB_TRY_CUDA(cudaStreamSynchronize(st));
+    void *ps[] = {s->dd_keys, s->dd_minpos, s->dd_slot, s->dd_uidx, s->dd_part};
+    for (auto p : ps) if (p) cudaFree(p);
+    int64_t table = 1;
+    while (table < 2 * ce) table <<= 1;
+    FB_TRY_CUDA(cudaMalloc(&s->dd_keys, table * 4));
+    FB_TRY_CUDA(cudaMalloc(&s->dd_minpos, table * 4));
+    FB_TRY_CUDA(cudaMalloc(&s->dd_slot, ce * 4));
+    FB_TRY_CUDA(cudaMalloc(&s->dd_uidx, ce * 4));
+    FB_TRY_CUDA(cudaMalloc(&s->dd_part, nblk(ce) * sizeof(int2)));
+    s->dd_cap_edges = ce;
+    s->dd_table = table;
+  }
+  // The table must be at least twice the edge count of this block.
+  int64_t table = 1;
+  while (table < 2 * ce) table <<= 1;
+  int32_t *dims = s->dims + 8 * i;
+  const int nb = nblk(ce);
+  k_dedup_init<<<nblk(table), kThreads, 0, st>>>(s->dd_keys, s->dd_minpos, table);
+  FB_LAUNCHED("k_dedup_init");
+  k_dedup_insert<<<nb, kThreads, 0, st>>>(b.eid, dims, s->dd_keys, s->dd_minpos, s->dd_slot, (uint32_t)(table - 1));
+  FB_LAUNCHED("k_dedup_insert");
+  k_dedup_count<<<nb, kThreads, 0, st>>>(dims, s->dd_minpos, s->dd_slot, s->dd_part);
+  FB_LAUNCHED("k_dedup_count");
+  k_dedup_scan<<<1, 1024, 0, st>>>(s->dd_part, nb, dims);
+  FB_LAUNCHED("k_dedup_scan");
+  k_dedup_emit<<<nb, kThreads, 0, st>>>(b.eid, dims, s->dd_minpos, s->dd_slot, s->dd_part, s->dd_uidx, b.uniE);
+  FB_LAUNCHED("k_dedup_emit");
+  k_dedup_inv<<<nb, kThreads, 0, st>>>(dims, s->dd_minpos, s->dd_slot, s->dd_uidx, b.invE);
+  FB_LAUNCHED("k_dedup_inv");
+  return FB_OK;
+}

@@ -1,0 +1,134 @@
+"""Device-resident training loop for the temporal-attention hot path.
+
+One training step follows train.py:307-393 of the reference: roots =
+[src | dst | negatives] of a chronological batch, temporal sampling, feature
+gather + time encoding, forward, BCE loss, backward, Adam.  Everything stays
+in HBM; the only host round trip per step is reading the sampled block
+sizes (and, in the end-to-end mode, the batch upload and the loss readback).
+
+Data parallelism: each rank takes a contiguous slice of every chronological
+batch, gradients are averaged with one NCCL all-reduce over a single flat
+bucket.  Equal slices make the averaged gradient the gradient of the global
+batch loss (mean_pos + mean_neg, train.py:373-374).
+"""
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import ops
+from .model import DeviceBlock, GeneralModel
+from .ext import sampler_core
+
+
+class Trainer:
+    def __init__(self, graph, node_feats, edge_feats, sample_param, memory_param, gnn_param, train_param,
+                 device, rank=0, world=1, seed=42, sampler_seed=1234):
+        self.device = torch.device(device)
+        self.rank, self.world = rank, world
+        self.graph = graph
+        self.sample_param = sample_param
+        self.node_feats, self.edge_feats = node_feats, edge_feats
+        torch.manual_seed(seed)
+        self.model = GeneralModel(0 if node_feats is None else node_feats.shape[1],
+                                  0 if edge_feats is None else edge_feats.shape[1],
+                                  sample_param, memory_param, gnn_param, train_param).to(self.device)
+        if world > 1:
+            for p in self.model.parameters():   # identical start on every rank
+                dist.broadcast(p.data, 0)
+        self.opt = torch.optim.Adam(self.model.parameters(), lr=train_param["lr"])
+        self.crit = torch.nn.BCEWithLogitsLoss()
+        dv = self.device
+        self.indptr = torch.from_numpy(graph.indptr).to(dv)
+        self.indices = torch.from_numpy(graph.indices).to(dv)
+        self.eid = torch.from_numpy(graph.eid).to(dv)
+        self.ts_csr = torch.from_numpy(graph.ts_csr).to(dv)
+        self.src = torch.from_numpy(graph.src).to(dv)
+        self.dst = torch.from_numpy(graph.dst).to(dv)
+        self.ts = torch.from_numpy(graph.ts).to(dv)
+        self.sampler = sampler_core.ParallelSampler(
+            self.indptr, self.indices, self.eid, self.ts_csr, 1, 1, sample_param["layer"],
+            list(sample_param["neighbor"]), sample_param["strategy"] == "recent", sample_param["prop_time"],
+            sample_param["history"], float(sample_param["duration"]), sampler_seed)
+        self.neg_gen = torch.Generator(device=dv)
+        self.neg_gen.manual_seed(seed + 17)
+        self._views = None
+        self._flat = None
+
+    def sampler_kernels_per_step(self):
+        """Kernels one sample() call launches: a pointer update per layer that
+        uses the stateful pointers, then count / scan / write per block."""
+        sp = self.sample_param
+        n, first = 0, True
+        for _ in range(sp["layer"]):
+            use_ptr = first or sp["strategy"] == "recent" or (sp["prop_time"] and sp["history"] == 1)
+            first = False
+            n += (1 if use_ptr else 0) + 3 * sp["history"]
+        return n
+
+    def reset_epoch(self):
+        self.sampler.reset()
+
+    # -- inputs ---------------------------------------------------------------
+    def local_slice(self, b0, b1):
+        """Contiguous slice of the global batch [b0, b1) owned by this rank."""
+        n = b1 - b0
+        per = n // self.world
+        lo = b0 + self.rank * per
+        return lo, lo + per
+
+    def device_roots(self, b0, b1):
+        lo, hi = self.local_slice(b0, b1)
+        n = hi - lo
+        neg = torch.randint(0, self.graph.n_nodes, (n,), device=self.device, generator=self.neg_gen,
+                            dtype=torch.int32)
+        roots = torch.cat([self.src[lo:hi], self.dst[lo:hi], neg])
+        t = self.ts[lo:hi]
+        return roots, torch.cat([t, t, t])
+
+    # -- step -----------------------------------------------------------------
+    def blocks(self):
+        dims = self.sampler.dims()
+        views = self.sampler.block_views()
+        return [DeviceBlock(v, d) for v, d in zip(views, dims)]
+
+    def _allreduce_grads(self):
+        grads = [p.grad for p in self.model.parameters() if p.grad is not None]
+        if self._flat is None or self._flat.numel() != sum(g.numel() for g in grads):
+            self._flat = torch.empty(sum(g.numel() for g in grads), device=self.device)
+        torch.cat([g.reshape(-1) for g in grads], out=self._flat)
+        dist.all_reduce(self._flat)
+        self._flat.div_(self.world)
+        off = 0
+        for g in grads:
+            g.copy_(self._flat[off:off + g.numel()].view_as(g))
+            off += g.numel()
+
+    def step_device(self, roots, root_ts):
+        """One training step on device-resident roots; returns the loss tensor."""
+        self.sampler.sample_device(roots, root_ts)
+        blocks = self.blocks()
+        self.opt.zero_grad(set_to_none=False)
+        pred_pos, pred_neg = self.model(blocks, self.node_feats, self.edge_feats)
+        loss = self.crit(pred_pos, torch.ones_like(pred_pos)) + self.crit(pred_neg, torch.zeros_like(pred_neg))
+        loss.backward()
+        if self.world > 1:
+            self._allreduce_grads()
+        self.opt.step()
+        return loss.detach()
+
+    def step_host(self, roots_np, ts_np):
+        """End-to-end step through the reference-facing API: host roots in, host loss out."""
+        self.sampler.sample(roots_np, ts_np, [])
+        blocks = self.blocks()
+        self.opt.zero_grad(set_to_none=False)
+        pred_pos, pred_neg = self.model(blocks, self.node_feats, self.edge_feats)
+        loss = self.crit(pred_pos, torch.ones_like(pred_pos)) + self.crit(pred_neg, torch.zeros_like(pred_neg))
+        loss.backward()
+        if self.world > 1:
+            self._allreduce_grads()
+        self.opt.step()
+        return float(loss)
+
+
+def batch_ranges(train_end, batch):
+    return [(b, min(b + batch, train_end)) for b in range(0, train_end, batch) if min(b + batch, train_end) - b == batch]

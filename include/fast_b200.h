@@ -1,0 +1,219 @@
+/*
+ * fast_b200 -- C ABI of the B200-native temporal-attention hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t,
+ * launches sm_100a kernels on that stream, never synchronises unless it says
+ * so, and returns an fb_status (0 == FB_OK).  Sizes that are only known on
+ * the device (edge counts produced by the sampler) can be passed as a device
+ * pointer (`*_dev`, may be NULL) together with a host upper bound, so a whole
+ * training step can be enqueued without a host round trip.
+ *
+ * Reference interfaces replaced (paths inside NoneBone/FAST):
+ *   ParallelSampler / TemporalGraphBlock   getSamplerCore/sampler_core.cpp:31-712, :1115-1149
+ *   fastAgg operators                      getFastAgg/cuda_operators/operators.cpp:606-624
+ *   prepare_input + TimeEncode             utils.py:126-196, layers.py:8-29
+ *   Q/K/V torch.nn.Linear                  layers.py:91-95, :149-164
+ */
+#ifndef FAST_B200_H
+#define FAST_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  FB_OK = 0,
+  FB_ERR_ARG = 1,          /* bad pointer / size / layout argument                */
+  FB_ERR_CUDA = 2,         /* a CUDA runtime call or kernel launch failed         */
+  FB_ERR_UNSUPPORTED = 3,  /* shape outside what the kernels are built for        */
+  FB_ERR_NOMEM = 4,        /* device allocation inside a runtime object failed    */
+  FB_ERR_STATE = 5         /* object used in the wrong order                      */
+} fb_status;
+
+/* Human-readable text of the last error raised on the calling thread. */
+const char *fb_last_error(void);
+/* Library version string. */
+const char *fb_version(void);
+
+/* ------------------------------------------------------------------------- */
+/* Temporal neighbour sampler (runtime object).                               */
+/* Replaces ParallelSampler (sampler_core.cpp:67-712, bound at :1139-1149).   */
+/* ------------------------------------------------------------------------- */
+typedef struct fb_sampler fb_sampler;
+
+/* Device view of one sampled block (TemporalGraphBlock, sampler_core.cpp:31-65).
+ * Arrays are sized for the block's capacity; `dims` (device, 8 x int32) holds
+ * {dim_out (= roots), E, S (non-empty rows), dim_in (= roots + E), n_uni, 0,0,0}.
+ *   row[E], col[E], eid[E]            COO in root order (sampler_core.cpp:273-277)
+ *   ts[dim_in], dts[dim_in], nodes[dim_in]  roots first, then one entry per edge
+ *   rptr[dim_out + 1]                 CSR offsets over ALL roots (empty rows allowed)
+ *   cntE[S + 1]                       offsets over non-empty rows only (:384-410)
+ *   uniE[n_uni], invE[E]              eid dedup, first-appearance order (:414-451),
+ *                                     valid after fb_sampler_dedup()          */
+typedef struct {
+  int32_t *row, *col, *eid;
+  float *ts, *dts;
+  int32_t *nodes, *rptr, *cntE, *uniE, *invE;
+  int32_t *dims;
+  int64_t max_roots, max_edges;
+} fb_block_view;
+
+/* Copies (graph_on_device == 0) or borrows (== 1) the time-sorted CSR
+ * indptr[n_nodes+1], indices/eid/ts[n_edges] on the current device.
+ * Mirrors the ParallelSampler constructor (sampler_core.cpp:89-114);
+ * thread counts of the reference have no meaning here.  `seed` keys the
+ * Philox stream used by uniform sampling. */
+int fb_sampler_create(const int32_t *indptr, const int32_t *indices, const int32_t *eid,
+                      const float *ts, int64_t n_nodes, int64_t n_edges, int graph_on_device,
+                      int num_layers, const int32_t *num_neighbors, int recent, int prop_time,
+                      int num_history, float window_duration, uint64_t seed, fb_sampler **out);
+int fb_sampler_destroy(fb_sampler *s);
+/* Rewinds the stateful time pointers (ParallelSampler::reset, :122-131). */
+int fb_sampler_reset(fb_sampler *s, cudaStream_t stream);
+/* Samples all layers/history slots for n_roots roots (ParallelSampler::sample,
+ * :597-712).  roots/root_ts are host arrays when roots_on_device == 0 (copied
+ * on `stream`), device arrays otherwise.  May grow the block buffers (which
+ * synchronises the device) when n_roots exceeds every earlier call. */
+int fb_sampler_sample(fb_sampler *s, const int32_t *roots, const float *root_ts, int64_t n_roots,
+                      int roots_on_device, cudaStream_t stream);
+/* Number of blocks from the last sample() (= num_layers * num_history), in
+ * the reference's get_ret() order. */
+int fb_sampler_num_blocks(const fb_sampler *s);
+int fb_sampler_block(const fb_sampler *s, int i, fb_block_view *out);
+/* Copies every block's dims to host_dims[8 * num_blocks]; synchronises `stream`. */
+int fb_sampler_dims(fb_sampler *s, int32_t *host_dims, cudaStream_t stream);
+/* Builds uniE/invE of block i on the device (dims[4] receives n_uni). */
+int fb_sampler_dedup(fb_sampler *s, int i, cudaStream_t stream);
+/* Sampler step counter that keys uniform draws; set it to replay a batch. */
+int fb_sampler_set_call_index(fb_sampler *s, uint64_t call_index);
+
+/* ------------------------------------------------------------------------- */
+/* Fused temporal attention: LeakyReLU(q.k) -> per-destination edge softmax  */
+/* -> dropout -> weighted aggregate.  Replaces, in one launch, layers.py:165-223
+ * = ESM_Function_TGAT (efficientGOP.py:66-78, kernel edge_softmax.cu:255-293)
+ * + MA_Function_TGAT (efficientGOP.py:97-113, aggregate_*_kernel.cu).       */
+/* ------------------------------------------------------------------------- */
+/* q[n_dst, dim] (ldq elements per row; ldq == 0 broadcasts one row),
+ * k/v rows of edge e at k + e*ldkv, v + e*ldkv, rptr[n_dst+1] CSR over
+ * destinations.  Writes att[E, heads] (softmax before dropout) and
+ * agg[n_dst, dim] (zero rows for destinations without edges).  dim % 4 == 0,
+ * dim <= 512, heads <= 4, dim % heads == 0.  drop_p == 0 disables dropout;
+ * otherwise the keep mask is Philox(seed, offset, edge, head). */
+int fb_attn_fwd(const float *q, int64_t ldq, const float *k, const float *v, int64_t ldkv,
+                const int32_t *rptr, int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim,
+                float slope, float drop_p, uint64_t seed, uint64_t offset, float *att, float *agg,
+                int64_t ldagg, cudaStream_t stream);
+/* Backward of fb_attn_fwd (efficientGOP.py:80-95,115-131, but with the true
+ * gradient).  Writes dq[n_dst, dim] (ld = dim; the segment sum of the
+ * per-edge gradient), dk, dv (rows at e*lddkv).  Any of dq/dk/dv may be NULL. */
+int fb_attn_bwd(const float *q, int64_t ldq, const float *k, const float *v, int64_t ldkv,
+                const int32_t *rptr, int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim,
+                float slope, float drop_p, uint64_t seed, uint64_t offset, const float *att,
+                const float *dagg, int64_t lddagg, float *dq, float *dk, float *dv, int64_t lddkv,
+                cudaStream_t stream);
+
+/* The dropout multipliers (0 or 1/(1-p)) fb_attn_fwd/bwd apply to edge e,
+ * head h for (seed, offset): out[e*heads + h].  For checking and replay. */
+int fb_dropout_scale(int64_t n_edges, int heads, float drop_p, uint64_t seed, uint64_t offset, float *out,
+                     cudaStream_t stream);
+/* Same attention with precomputed pre-activation logits x[E, heads] in place
+ * of q.k, V rows at v + e*ldv, segments [indptr[s], indptr[s+1]) over n_seg
+ * segments.  seg_row (int64, may be NULL) names the output row of a segment
+ * at its first edge, seg_row[indptr[s]] (rows of agg not named are left as
+ * they are; ids outside [0, n_out) are skipped); NULL means segment s writes
+ * row s.  mask_u (may be NULL) holds
+ * dropout uniforms [E, heads], kept when u > drop_p.  agg rows have `dim`
+ * floats.  Replaces forward_fused_attn (fused_attention.cu:68-127,203-328). */
+int fb_attn_logits_fwd(const float *x, const float *v, int64_t ldv, const int32_t *indptr, int64_t n_seg,
+                       const int64_t *seg_row, int64_t n_out, int heads, int dim, float slope, float drop_p,
+                       const float *mask_u, float *att, float *agg, cudaStream_t stream);
+/* Backward of fb_attn_logits_fwd: dx[E, heads] (gradient of the
+ * pre-activation logits, LeakyReLU included) and dv rows at e*ldv.
+ * Replaces backward_fused_attn (fused_attention.cu:129-200,330-446). */
+int fb_attn_logits_bwd(const float *x, const float *v, int64_t ldv, const int32_t *indptr, int64_t n_seg,
+                       const int64_t *seg_row, int64_t n_out, int heads, int dim, float slope, float drop_p,
+                       const float *mask_u, const float *att, const float *dagg, float *dx, float *dv,
+                       cudaStream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* fastAgg legacy operators (operators.cpp:606-624), correct semantics.        */
+/* ------------------------------------------------------------------------- */
+/* cal_deg (utils.cu:42-79): deg[edges[e]] += 1 for e < n_edges; deg zeroed by caller. */
+int fb_count_ids(const int32_t *ids, int64_t n, int32_t *deg, int64_t n_ids, cudaStream_t stream);
+/* getBalancedPtr (utils.cu:81-141): for segment i (< n_ptr - 1) with the
+ * inclusive prefix P_i of degrees taken within its aligned group of 256
+ * segments, mask[i] = (P_i / threshold > (P_i - deg_i) / threshold). */
+int fb_balanced_mask(const int32_t *ptr, int64_t n_ptr, int threshold, int32_t *mask, cudaStream_t stream);
+/* forward_edge_softmax / forward_csr_edge_softmax (edge_softmax.cu:55-78,178-206):
+ * y[e,h] = softmax of x over each segment [indptr[s], indptr[s+1]). */
+int fb_edge_softmax_fwd(const int32_t *indptr, int64_t n_seg, const float *x, int heads,
+                        float *y, cudaStream_t stream);
+/* backward_edge_softmax / backward_csr_edge_softmax (edge_softmax.cu:79-106,207-235):
+ * dx = y * (dy - sum_seg(y * dy)). */
+int fb_edge_softmax_bwd(const int32_t *indptr, int64_t n_seg, const float *dy, const float *y,
+                        int heads, float *dx, cudaStream_t stream);
+/* forward_tgat (aggregate_acc_kernel.cu:36-69), over ALL n_edges edges:
+ * out[dst_idx[e], :] += v[src_idx[e], :].  `out` must be zeroed by the caller. */
+int fb_scatter_rows(const int64_t *dst_idx, const int64_t *src_idx, int64_t n_edges,
+                    const float *v, int64_t n_v, int dim, float *out, int64_t n_out,
+                    cudaStream_t stream);
+/* forward_tgat_shd (aggregate_shd_kernel.cu:37-94): segment sums
+ * out[row[indptr[s]], :] = sum_{e in s} v[col[e], :] (deterministic order). */
+int fb_segment_rows(const int32_t *indptr, int64_t n_seg, const int64_t *row, const int64_t *col,
+                    const float *v, int64_t n_v, int dim, float *out, int64_t n_out,
+                    cudaStream_t stream);
+/* exclusive_sum (utils.cu:16-40): out[0] = 0, out[i+1] = sum(in[0..i]).
+ * `ws` must hold fb_exclusive_sum_ws_bytes(n) bytes. */
+size_t fb_exclusive_sum_ws_bytes(int64_t n);
+int fb_exclusive_sum(const int32_t *in, int64_t n, int32_t *out, void *ws, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Feature gather fused with the cos time encoding (utils.py:126-196,         */
+/* layers.py:17-29,103-110,157-164).                                           */
+/* ------------------------------------------------------------------------- */
+/* For every row r < n_rows (n_rows_dev overrides when not NULL):
+ *   A[r, 0:dn)          = h[(h_idx ? h_idx[r] : r + h_off), :]
+ *   A[r, dn:dn+de)      = f[(f_idx ? f_idx[r] : r), :]
+ *   A[r, dn+de:+dtime)  = cos(w * dt[r] + b)          (dt == NULL -> dt = 0)
+ * Any block with dn/de/dtime == 0 is skipped. */
+int fb_gather_time_encode(const float *h, int64_t ldh, const int32_t *h_idx, int64_t h_off, int dn,
+                          const float *f, int64_t ldf, const int32_t *f_idx, int de,
+                          const float *dt, const float *w, const float *b, int dtime,
+                          float *A, int64_t lda, int64_t n_rows, const int32_t *n_rows_dev,
+                          cudaStream_t stream);
+/* Gradient of the time encoding: with g = dL/dcos(w*dt+b) (rows at g + r*ldg),
+ * dw[j] += sum_r -sin(w_j dt_r + b_j) dt_r g[r,j],  db[j] += sum_r -sin(..) g[r,j].
+ * `ws` must hold fb_time_encode_bwd_ws_bytes(n_rows, dtime) bytes. */
+size_t fb_time_encode_bwd_ws_bytes(int64_t n_rows, int dtime);
+int fb_time_encode_bwd(const float *g, int64_t ldg, const float *dt, const float *w, const float *b,
+                       int dtime, int64_t n_rows, const int32_t *n_rows_dev, float *dw, float *db,
+                       void *ws, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* fp32 projection GEMMs (torch.nn.Linear, layers.py:91-95).                  */
+/* ------------------------------------------------------------------------- */
+/* C[m, n] = sum_k A[m,k] B[n,k] (+ bias[n]) (+ C when accumulate)   "NT"
+ * m < M (M_dev overrides), n < N, k < K.  Row-major with leading dims. */
+int fb_gemm_nt(const float *A, int64_t lda, const float *B, int64_t ldb, const float *bias,
+               float *C, int64_t ldc, int64_t M, const int32_t *M_dev, int N, int K,
+               int accumulate, cudaStream_t stream);
+/* C[n, k] = sum_m G[m, n] X[m, k]  (+ C when accumulate)              "TN"
+ * the weight gradient of a Linear layer; deterministic split over M.
+ * `ws` must hold fb_gemm_tn_ws_bytes(M, N, K) bytes. */
+size_t fb_gemm_tn_ws_bytes(int64_t M, int N, int K);
+int fb_gemm_tn(const float *G, int64_t ldg, const float *X, int64_t ldx, float *C, int64_t ldc,
+               int64_t M, const int32_t *M_dev, int N, int K, int accumulate, void *ws,
+               cudaStream_t stream);
+/* db[n] (+)= sum_m G[m, n]; deterministic.  ws: fb_colsum_ws_bytes(M, N). */
+size_t fb_colsum_ws_bytes(int64_t M, int N);
+int fb_colsum(const float *G, int64_t ldg, float *db, int64_t M, const int32_t *M_dev, int N,
+              int accumulate, void *ws, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FAST_B200_H */

@@ -1,0 +1,173 @@
+"""GPU: fused LeakyReLU(q.k) -> segment softmax -> dropout -> aggregate, forward
+and backward, against a plain PyTorch fp32 reference of the same op
+(oracle/ref_math.py restates DGL's edge_softmax and copy_u/sum).
+
+Tolerance: the north-star bound for fp32 outputs and gradients,
+rtol 1e-5 / atol 1e-6.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle.ref_math import edge_softmax
+
+pytestmark = pytest.mark.gpu
+RTOL, ATOL = 1e-5, 1e-6
+
+
+def _segments(rng, n_dst, max_deg, big=()):
+    deg = rng.integers(0, max_deg + 1, n_dst)
+    for j, d in big:
+        deg[j] = d
+    rptr = np.concatenate([[0], np.cumsum(deg)]).astype(np.int32)
+    row = np.repeat(np.arange(n_dst), deg).astype(np.int64)
+    return rptr, row
+
+
+def _reference(q, k, v, row, n_dst, heads, slope, scale=None, per_edge_q=False):
+    E, D = k.shape
+    qe = q if per_edge_q else (q.expand(n_dst, -1) if q.shape[0] == 1 else q)[row]
+    z = (qe.view(E, heads, -1) * k.view(E, heads, -1)).sum(-1)
+    att = edge_softmax(torch.nn.functional.leaky_relu(z, slope), torch.from_numpy(row), n_dst)
+    a = att if scale is None else att * scale
+    vv = (v.view(E, heads, -1) * a[:, :, None]).reshape(E, D)
+    agg = torch.zeros(n_dst, D, dtype=v.dtype).index_add_(0, torch.from_numpy(row), vv)
+    return agg, att
+
+
+@pytest.mark.parametrize("heads,dim", [(2, 100), (2, 128), (4, 200), (1, 64)])
+@pytest.mark.parametrize("drop_p", [0.0, 0.1])
+def test_attention_fwd_bwd(cuda, heads, dim, drop_p):
+    from fast_b200 import ops
+    from fast_b200.capi import call, ptr, stream_ptr
+    rng = np.random.default_rng(heads * 1000 + dim)
+    n_dst = 700
+    rptr, row = _segments(rng, n_dst, 12, big=((3, 70), (10, 150), (11, 1)))
+    E = int(rptr[-1])
+    torch.manual_seed(0)
+    q = torch.randn(n_dst, dim) * 0.5
+    kv = torch.randn(E, 2 * dim) * 0.5
+    dagg = torch.randn(n_dst, dim)
+    k, v = kv[:, :dim], kv[:, dim:]
+    scale = None
+    if drop_p > 0:
+        sc = torch.empty(E, heads, device=cuda)
+        call("fb_dropout_scale", E, heads, drop_p, 123, 7, ptr(sc), stream_ptr())
+        scale = sc.cpu()
+        kept = (scale > 0).float().mean().item()
+        assert abs(kept - (1 - drop_p)) < 0.02
+    # reference (CPU fp32, autograd)
+    qr, kr, vr = (t.clone().requires_grad_(True) for t in (q, k, v))
+    agg_r, att_r = _reference(qr, kr, vr, row, n_dst, heads, 0.2, scale)
+    agg_r.backward(dagg)
+    # device
+    qd, kvd, rp = q.to(cuda), kv.to(cuda), torch.from_numpy(rptr).to(cuda)
+    agg, att = ops.attn_fwd(qd, kvd[:, :dim], kvd[:, dim:], rp, heads, 0.2, drop_p, 123, 7)
+    dq, dkv = ops.attn_bwd(qd, kvd[:, :dim], kvd[:, dim:], rp, att, dagg.to(cuda), heads, 0.2, drop_p, 123, 7)
+    torch.testing.assert_close(att.cpu(), att_r.detach(), rtol=RTOL, atol=ATOL)
+    torch.testing.assert_close(agg.cpu(), agg_r.detach(), rtol=RTOL, atol=ATOL)
+    torch.testing.assert_close(dq.cpu(), qr.grad, rtol=RTOL, atol=ATOL)
+    torch.testing.assert_close(dkv[:, :dim].cpu(), kr.grad, rtol=RTOL, atol=ATOL)
+    torch.testing.assert_close(dkv[:, dim:].cpu(), vr.grad, rtol=RTOL, atol=ATOL)
+    # rows without edges are exact zeros; results are bit-identical on rerun
+    empty = np.where(np.diff(rptr) == 0)[0]
+    assert torch.count_nonzero(agg[torch.from_numpy(empty).to(cuda)]) == 0
+    agg2, _ = ops.attn_fwd(qd, kvd[:, :dim], kvd[:, dim:], rp, heads, 0.2, drop_p, 123, 7)
+    assert torch.equal(agg, agg2)
+
+
+def test_attention_broadcast_q(cuda):
+    """ldq == 0: one query row for every destination (layers.py:149-152, d_node == 0)."""
+    from fast_b200 import ops
+    rng = np.random.default_rng(5)
+    n_dst, dim, heads = 300, 100, 2
+    rptr, row = _segments(rng, n_dst, 10)
+    E = int(rptr[-1])
+    q = torch.randn(1, dim)
+    kv = torch.randn(E, 2 * dim)
+    dagg = torch.randn(n_dst, dim)
+    qr = q.clone().requires_grad_(True)
+    kr, vr = kv[:, :dim].clone().requires_grad_(True), kv[:, dim:].clone().requires_grad_(True)
+    agg_r, _ = _reference(qr, kr, vr, row, n_dst, heads, 0.2)
+    agg_r.backward(dagg)
+    kvd = kv.to(cuda)
+    rp = torch.from_numpy(rptr).to(cuda)
+    agg, att = ops.attn_fwd(q.to(cuda), kvd[:, :dim], kvd[:, dim:], rp, heads, 0.2)
+    dq, dkv = ops.attn_bwd(q.to(cuda), kvd[:, :dim], kvd[:, dim:], rp, att, dagg.to(cuda), heads, 0.2)
+    torch.testing.assert_close(agg.cpu(), agg_r.detach(), rtol=RTOL, atol=ATOL)
+    torch.testing.assert_close(dq.sum(0, keepdim=True).cpu(), qr.grad, rtol=RTOL, atol=1e-5)
+    torch.testing.assert_close(dkv[:, :dim].cpu(), kr.grad, rtol=RTOL, atol=ATOL)
+
+
+def test_fastagg_fused_attn_logits(cuda):
+    """forward_fused_attn / backward_fused_attn of the drop-in module (precomputed logits)."""
+    from fast_b200.ext import fastAgg
+    rng = np.random.default_rng(8)
+    n_dst, heads, dh = 200, 2, 50
+    rptr_all, row = _segments(rng, n_dst, 9)
+    nonempty = np.where(np.diff(rptr_all) > 0)[0]
+    cnt = np.concatenate([[0], np.cumsum(np.diff(rptr_all)[nonempty])]).astype(np.int32)
+    E = int(cnt[-1])
+    x = torch.randn(E, heads)
+    V = torch.randn(E, heads, dh)
+    xr = x.clone().requires_grad_(True)
+    Vr = V.clone().requires_grad_(True)
+    att_r = edge_softmax(torch.nn.functional.leaky_relu(xr, 0.2), torch.from_numpy(row), n_dst)
+    agg_r = torch.zeros(n_dst, heads * dh).index_add_(0, torch.from_numpy(row),
+                                                      (Vr * att_r[:, :, None]).reshape(E, -1))
+    dy = torch.randn(n_dst, heads * dh)
+    agg_r.backward(dy)
+    dev = [t.to(cuda) for t in (x, V, torch.from_numpy(cnt), torch.from_numpy(row))]
+    out_agg, att, mask = fastAgg.forward_fused_attn(dev[0], dev[1], dev[2], dev[2], dev[3], dev[3] + n_dst,
+                                                    n_dst, heads, 0.2, 0.0)
+    torch.testing.assert_close(out_agg.cpu(), agg_r.detach(), rtol=RTOL, atol=ATOL)
+    torch.testing.assert_close(att.cpu(), att_r.detach(), rtol=RTOL, atol=ATOL)
+    dx, dV = fastAgg.backward_fused_attn(dy.to(cuda), dev[1], att, mask, dev[2], dev[2], dev[3], dev[3] + n_dst,
+                                         n_dst, heads, 0.2, 0.0, input_feat=dev[0])
+    torch.testing.assert_close(dx.cpu(), xr.grad, rtol=RTOL, atol=ATOL)
+    torch.testing.assert_close(dV.cpu(), Vr.grad, rtol=RTOL, atol=ATOL)
+
+
+def test_fastagg_legacy_ops(cuda):
+    """edge softmax, forward/backward_tgat(_shd), exclusive_sum, cal_deg with the reference names."""
+    from fast_b200.ext import fastAgg
+    rng = np.random.default_rng(3)
+    n_dst, heads, D = 150, 2, 100
+    rptr_all, row = _segments(rng, n_dst, 11)
+    deg = np.diff(rptr_all)
+    nonempty = np.where(deg > 0)[0]
+    cnt = np.concatenate([[0], np.cumsum(deg[nonempty])]).astype(np.int32)
+    E = int(cnt[-1])
+    x = torch.randn(E, heads)
+    y_r = edge_softmax(x, torch.from_numpy(row), n_dst)
+    c = torch.from_numpy(cnt).to(cuda)
+    for fwd in (lambda: fastAgg.forward_edge_softmax(c, c, x.to(cuda), 512, heads)[0],
+                lambda: fastAgg.forward_csr_edge_softmax(c, c, x.to(cuda), 32, 16)[0]):
+        torch.testing.assert_close(fwd().cpu(), y_r, rtol=RTOL, atol=ATOL)
+    dy = torch.randn(E, heads)
+    dx_r = y_r * (dy - torch.zeros(n_dst, heads).index_add_(0, torch.from_numpy(row), y_r * dy)[row])
+    dx = fastAgg.backward_edge_softmax(c, c, dy.to(cuda), y_r.to(cuda), 512, heads)[0]
+    torch.testing.assert_close(dx.cpu(), dx_r, rtol=RTOL, atol=ATOL)
+    # aggregation over the block's src table [Nd zeros | V]
+    V = torch.randn(n_dst + E, D)
+    rowt = torch.from_numpy(row)
+    colt = torch.arange(n_dst, n_dst + E, dtype=torch.int64)
+    agg_r = torch.zeros(n_dst, D).index_add_(0, rowt, V[colt])
+    for out in (fastAgg.forward_tgat(rowt.to(cuda), colt.to(cuda), V.to(cuda), n_dst, 8, 128)[0],
+                fastAgg.forward_tgat_shd(c, c, rowt.to(cuda), colt.to(cuda), V.to(cuda), n_dst, 8, 32)[0]):
+        torch.testing.assert_close(out.cpu(), agg_r, rtol=RTOL, atol=ATOL)
+    dyn = torch.randn(n_dst, D)
+    dv_r = torch.zeros(n_dst + E, D)
+    dv_r[colt] = dyn[rowt]
+    for out in (fastAgg.backward_tgat(rowt.to(cuda), colt.to(cuda), dyn.to(cuda), n_dst + E, 8, 128)[0],
+                fastAgg.backward_tgat_shd(c, c, rowt.to(cuda), colt.to(cuda), dyn.to(cuda), n_dst + E, 8, 32)[0]):
+        torch.testing.assert_close(out.cpu(), dv_r, rtol=RTOL, atol=ATOL)
+    degs = torch.from_numpy(deg.astype(np.int32)).to(cuda)
+    np.testing.assert_array_equal(fastAgg.exclusive_sum(degs).cpu().numpy(),
+                                  np.concatenate([[0], np.cumsum(deg)]).astype(np.int32))
+    ids = torch.from_numpy(rng.integers(0, 50, 999).astype(np.int32)).to(cuda)
+    np.testing.assert_array_equal(fastAgg.cal_deg(ids, 50).cpu().numpy(),
+                                  np.bincount(ids.cpu().numpy(), minlength=50))
+    big = torch.from_numpy(rng.integers(0, 5, 300_000).astype(np.int32)).to(cuda)
+    np.testing.assert_array_equal(fastAgg.exclusive_sum(big).cpu().numpy()[1:],
+                                  np.cumsum(big.cpu().numpy()))
