@@ -43,6 +43,7 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=5)
+    ap.add_argument("--eager", action="store_true", help="launch kernels step by step instead of a CUDA graph")
     return ap.parse_args()
 
 
@@ -201,12 +202,15 @@ def run_fast(args):
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     from fast_b200 import ops
     from fast_b200.data import CONFIGS, make_features, make_graph, model_params
-    from fast_b200.train import Trainer
+    from fast_b200.train import GraphTrainer, Trainer
     cfg = CONFIGS[args.config]
     graph = make_graph(cfg)
     nf, ef = make_features(cfg, cfg.edges, dev)
     sp, mp, gp, tp = model_params(cfg)
-    tr = Trainer(graph, nf, ef, sp, mp, gp, tp, dev, rank=rank, world=world)
+    if args.eager:
+        tr = Trainer(graph, nf, ef, sp, mp, gp, tp, dev, rank=rank, world=world)
+    else:
+        tr = GraphTrainer(graph, nf, ef, sp, mp, gp, tp, dev, batch=cfg.batch, rank=rank, world=world)
     B = cfg.batch
     gB = B * world
     n_batches = graph.train_end // gB
@@ -220,8 +224,11 @@ def run_fast(args):
 
     def dev_step():
         b0, b1 = next_range()
-        roots, rts = tr.device_roots(b0, b1)
-        return tr.step_device(roots, rts)
+        if args.eager:
+            roots, rts = tr.device_roots(b0, b1)
+            return tr.step_device(roots, rts)
+        tr.load_device_roots(b0, b1)
+        return tr.step_device()
 
     for _ in range(args.warmup):
         dev_step()
@@ -232,6 +239,14 @@ def run_fast(args):
     torch.cuda.synchronize()
     clock.start()
     l0 = ops.LAUNCHES[0]
+    if not args.eager:
+        # kernels per replayed step = kernels of one eager launch of the same body
+        b0, b1 = next_range()
+        tr.load_device_roots(b0, b1)
+        tr._eager_step()
+        torch.cuda.synchronize()
+        per_step = ops.LAUNCHES[0] - l0 + tr.sampler_kernels_per_step()
+        l0 = ops.LAUNCHES[0]
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for _ in range(args.steps):
@@ -240,7 +255,10 @@ def run_fast(args):
     torch.cuda.synchronize()
     clocks = clock.stop()
     ms = ev0.elapsed_time(ev1)
-    launches = ops.LAUNCHES[0] - l0 + args.steps * tr.sampler_kernels_per_step()
+    if args.eager:
+        launches = ops.LAUNCHES[0] - l0 + args.steps * tr.sampler_kernels_per_step()
+    else:
+        launches = per_step * args.steps
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.barrier()
@@ -267,10 +285,16 @@ def run_fast(args):
         dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
     e2e_value = args.steps * gB / float(e2e_s.item())
 
-    # per-kernel device times for the roofline (separate, instrumented steps)
+    # per-kernel device times for the roofline: the same kernels launched one
+    # by one (outside the graph) with CUDA events around each
     ops.TIMER = ops.KernelTimer()
     for _ in range(args.profile_steps):
-        dev_step()
+        if args.eager:
+            dev_step()
+        else:
+            b0, b1 = next_range()
+            tr.load_device_roots(b0, b1)
+            tr._eager_step()
     kern = ops.TIMER.summary()
     ops.TIMER = None
 
@@ -307,7 +331,7 @@ def run_fast(args):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, %s shapes)" % cfg.name,
         "config": {"workload": cfg.name, "global_batch": gB, "local_batch": B, "fanout": list(cfg.fanout),
                    "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge,
-                   "parallelism": "dp%d" % world,
+                   "parallelism": "dp%d" % world, "launch": "eager" if args.eager else "cuda_graph",
                    "l2": "inputs larger than L2 (%.1f GB edge-feature table gathered at random rows)" %
                          (cfg.edges * cfg.d_edge * 4 / 1e9)},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": world * 3 * B * 8,

@@ -46,8 +46,8 @@ _SIGS = {
     "fb_sampler_dims": (_I, [_P, _P, _P]),
     "fb_sampler_dedup": (_I, [_P, _I, _P]),
     "fb_sampler_set_call_index": (_I, [_P, _U64]),
-    "fb_attn_fwd": (_I, [_P, _I64, _P, _P, _I64, _P, _I64, _P, _I, _I, _F, _F, _U64, _U64, _P, _P, _I64, _P]),
-    "fb_attn_bwd": (_I, [_P, _I64, _P, _P, _I64, _P, _I64, _P, _I, _I, _F, _F, _U64, _U64, _P, _P, _I64,
+    "fb_attn_fwd": (_I, [_P, _I64, _P, _P, _I64, _P, _I64, _P, _I, _I, _F, _F, _U64, _U64, _P, _P, _P, _I64, _P]),
+    "fb_attn_bwd": (_I, [_P, _I64, _P, _P, _I64, _P, _I64, _P, _I, _I, _F, _F, _U64, _U64, _P, _P, _P, _I64,
                          _P, _P, _P, _I64, _P]),
     "fb_attn_logits_fwd": (_I, [_P, _P, _I64, _P, _I64, _P, _I64, _I, _I, _F, _F, _P, _P, _P, _P]),
     "fb_attn_logits_bwd": (_I, [_P, _P, _I64, _P, _I64, _P, _I64, _I, _I, _F, _F, _P, _P, _P, _P, _P, _P]),
@@ -60,7 +60,8 @@ _SIGS = {
     "fb_segment_rows": (_I, [_P, _I64, _P, _P, _P, _I64, _I, _P, _I64, _P]),
     "fb_exclusive_sum_ws_bytes": (_SZ, [_I64]),
     "fb_exclusive_sum": (_I, [_P, _I64, _P, _P, _P]),
-    "fb_gather_time_encode": (_I, [_P, _I64, _P, _I64, _I, _P, _I64, _P, _I, _P, _P, _P, _I, _P, _I64, _I64, _P, _P]),
+    "fb_gather_time_encode": (_I, [_P, _I64, _P, _I64, _P, _I, _P, _I64, _P, _I, _P, _P, _P, _I, _P, _I64, _I64, _P,
+                                   _P]),
     "fb_time_encode_bwd_ws_bytes": (_SZ, [_I64, _I]),
     "fb_time_encode_bwd": (_I, [_P, _I64, _P, _P, _P, _I, _I64, _P, _P, _P, _P, _P]),
     "fb_gemm_nt": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _I, _I, _I, _P]),
@@ -79,7 +80,8 @@ for _name, (_res, _args) in _SIGS.items():
 class BlockView(ctypes.Structure):
     _fields_ = [(n, ctypes.c_void_p) for n in
                 ("row", "col", "eid", "ts", "dts", "nodes", "rptr", "cntE", "uniE", "invE", "dims")] + \
-               [("max_roots", ctypes.c_int64), ("max_edges", ctypes.c_int64)]
+               [("max_roots", ctypes.c_int64), ("max_edges", ctypes.c_int64), ("dte", ctypes.c_void_p),
+                ("nbr", ctypes.c_void_p)]
 
 
 def exported_symbols():

@@ -122,6 +122,7 @@ struct AttnArgs {
   const int32_t *rptr; int64_t n_dst; const int32_t *n_dst_dev;
   int heads, dim;
   float slope, drop_p; uint64_t seed, offset;
+  const uint64_t *offset_dev;  // optional: dropout stream offset read on the device (graph replays)
   const float *att; float *att_out;
   float *agg; int64_t ldagg;
   const float *x;          // optional pre-activation logits [E, heads] replacing q.k
@@ -159,10 +160,18 @@ template <int NV>
 __global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_fwd(AttnArgs a) {
   __shared__ float stash[kWarpsPerCta][kStash][kMaxHeads];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int64_t n_dst = a.n_dst_dev ? (int64_t)(*a.n_dst_dev) : a.n_dst;
+  const int64_t n_dst = a.n_dst_dev ? min((int64_t)(*a.n_dst_dev), a.n_dst) : a.n_dst;
   RowGeom g{a.dim / 4, a.dim / a.heads, a.heads};
   int hsel[NV][4];
   lane_heads<NV>(g, lane, hsel);
+  const uint64_t doff = a.offset_dev ? *a.offset_dev : a.offset;
+  if (a.n_dst_dev && !a.seg_row) {
+    // rows past the device-side count: zeros, so fixed-size consumers stay finite
+    const float4 z[NV] = {};
+    for (int64_t j = n_dst + (int64_t)blockIdx.x * kWarpsPerCta + w; j < a.n_dst;
+         j += (int64_t)gridDim.x * kWarpsPerCta)
+      store_row<NV>(a.agg + j * a.ldagg, g, lane, z);
+  }
   for (int64_t j = (int64_t)blockIdx.x * kWarpsPerCta + w; j < n_dst; j += (int64_t)gridDim.x * kWarpsPerCta) {
     const int beg = a.rptr[j], end = a.rptr[j + 1];
     const int64_t orow = seg_out_row(a, j, beg, end);
@@ -219,7 +228,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_fwd(AttnArgs a) {
         }
         __syncwarp();
         if (lane < a.heads) a.att_out[(int64_t)e * a.heads + lane] = pick(y, lane);
-        drop_scale(e, a.heads, a.drop_p, a.seed, a.offset, a.mask_u, ds);
+        drop_scale(e, a.heads, a.drop_p, a.seed, doff, a.mask_u, ds);
 #pragma unroll
         for (int h = 0; h < kMaxHeads; ++h) y[h] *= ds[h];
         float4 vr[NV];
@@ -242,10 +251,11 @@ template <int NV>
 __global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_bwd(AttnArgs a) {
   __shared__ float stash[kWarpsPerCta][kStash][kMaxHeads];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int64_t n_dst = a.n_dst_dev ? (int64_t)(*a.n_dst_dev) : a.n_dst;
+  const int64_t n_dst = a.n_dst_dev ? min((int64_t)(*a.n_dst_dev), a.n_dst) : a.n_dst;
   RowGeom g{a.dim / 4, a.dim / a.heads, a.heads};
   int hsel[NV][4];
   lane_heads<NV>(g, lane, hsel);
+  const uint64_t doff = a.offset_dev ? *a.offset_dev : a.offset;
   const bool need_dl = (a.dq != nullptr) || (a.dk != nullptr) || (a.dx != nullptr);
   for (int64_t j = (int64_t)blockIdx.x * kWarpsPerCta + w; j < n_dst; j += (int64_t)gridDim.x * kWarpsPerCta) {
     const int beg = a.rptr[j], end = a.rptr[j + 1];
@@ -266,7 +276,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_bwd(AttnArgs a) {
         load_row<NV>(a.v + (int64_t)e * a.ldkv, g, lane, vr);
         float datt[kMaxHeads], ds[kMaxHeads], y[kMaxHeads];
         head_dots<NV>(da, vr, hsel, a.heads, datt);
-        drop_scale(e, a.heads, a.drop_p, a.seed, a.offset, a.mask_u, ds);
+        drop_scale(e, a.heads, a.drop_p, a.seed, doff, a.mask_u, ds);
 #pragma unroll
         for (int h = 0; h < kMaxHeads; ++h) {
           y[h] = (h < a.heads) ? __ldg(a.att + (int64_t)e * a.heads + h) : 0.f;
@@ -301,7 +311,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_bwd(AttnArgs a) {
             float ds[kMaxHeads];
             load_row<NV>(a.v + (int64_t)e * a.ldkv, g, lane, vr);
             head_dots<NV>(da, vr, hsel, a.heads, dy);
-            drop_scale(e, a.heads, a.drop_p, a.seed, a.offset, a.mask_u, ds);
+            drop_scale(e, a.heads, a.drop_p, a.seed, doff, a.mask_u, ds);
 #pragma unroll
             for (int h = 0; h < kMaxHeads; ++h) dy[h] *= ds[h];
           }
@@ -433,9 +443,10 @@ extern "C" int fb_dropout_scale(int64_t n_edges, int heads, float drop_p, uint64
 
 extern "C" int fb_attn_fwd(const float *q, int64_t ldq, const float *k, const float *v, int64_t ldkv,
                            const int32_t *rptr, int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim,
-                           float slope, float drop_p, uint64_t seed, uint64_t offset, float *att, float *agg,
-                           int64_t ldagg, cudaStream_t stream) {
+                           float slope, float drop_p, uint64_t seed, uint64_t offset, const uint64_t *offset_dev,
+                           float *att, float *agg, int64_t ldagg, cudaStream_t stream) {
   AttnArgs a{};
+  a.offset_dev = offset_dev;
   a.q = q; a.ldq = ldq; a.k = k; a.v = v; a.ldkv = ldkv; a.rptr = rptr; a.n_dst = n_dst; a.n_dst_dev = n_dst_dev;
   a.heads = heads; a.dim = dim; a.slope = slope; a.drop_p = drop_p; a.seed = seed; a.offset = offset;
   a.att_out = att; a.agg = agg; a.ldagg = ldagg;
@@ -444,10 +455,11 @@ extern "C" int fb_attn_fwd(const float *q, int64_t ldq, const float *k, const fl
 
 extern "C" int fb_attn_bwd(const float *q, int64_t ldq, const float *k, const float *v, int64_t ldkv,
                            const int32_t *rptr, int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim,
-                           float slope, float drop_p, uint64_t seed, uint64_t offset, const float *att,
-                           const float *dagg, int64_t lddagg, float *dq, float *dk, float *dv, int64_t lddkv,
-                           cudaStream_t stream) {
+                           float slope, float drop_p, uint64_t seed, uint64_t offset, const uint64_t *offset_dev,
+                           const float *att, const float *dagg, int64_t lddagg, float *dq, float *dk, float *dv,
+                           int64_t lddkv, cudaStream_t stream) {
   AttnArgs a{};
+  a.offset_dev = offset_dev;
   a.q = q; a.ldq = ldq; a.k = k; a.v = v; a.ldkv = ldkv; a.rptr = rptr; a.n_dst = n_dst; a.n_dst_dev = n_dst_dev;
   a.heads = heads; a.dim = dim; a.slope = slope; a.drop_p = drop_p; a.seed = seed; a.offset = offset;
   a.att = att; a.dagg = dagg; a.lddagg = lddagg; a.dq = dq; a.dk = dk; a.dv = dv; a.lddkv = lddkv;

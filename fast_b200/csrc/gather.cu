@@ -28,7 +28,7 @@ __device__ __forceinline__ void copy_seg(const float *__restrict__ src, float *_
 }
 
 struct GatherArgs {
-  const float *h; int64_t ldh; const int32_t *h_idx; int64_t h_off; int dn;
+  const float *h; int64_t ldh; const int32_t *h_idx; int64_t h_off; const int32_t *h_off_dev; int dn;
   const float *f; int64_t ldf; const int32_t *f_idx; int de;
   const float *dt, *w, *b; int dtime;
   float *A; int64_t lda; int64_t n_rows; const int32_t *n_rows_dev;
@@ -38,11 +38,12 @@ template <bool VEC>
 __global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode(GatherArgs a) {
   const int lane = threadIdx.x & 31;
   const int64_t n = a.n_rows_dev ? (int64_t)(*a.n_rows_dev) : a.n_rows;
+  const int64_t h_off = a.h_off + (a.h_off_dev ? (int64_t)(*a.h_off_dev) : 0);
   for (int64_t r = (int64_t)blockIdx.x * kRowsPerCta + (threadIdx.x >> 5); r < n;
        r += (int64_t)gridDim.x * kRowsPerCta) {
     float *out = a.A + r * a.lda;
     if (a.dn > 0) {
-      const int64_t hr = a.h_idx ? (int64_t)a.h_idx[r] : r + a.h_off;
+      const int64_t hr = a.h_idx ? (int64_t)a.h_idx[r] : r + h_off;
       copy_seg<VEC>(a.h + hr * a.ldh, out, a.dn, lane);
     }
     if (a.de > 0) {
@@ -57,26 +58,39 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode(GatherA
   }
 }
 
-// Time-encoding backward, stage 1: per-CTA partial sums over a row chunk.
+// Time-encoding backward, stage 1: CTA (x = 32-column tile, y = row chunk)
+// with 8 warps striding over the chunk's rows, lanes over columns; the warps'
+// sums are combined in shared memory in a fixed order.
 __global__ void __launch_bounds__(256) k_te_bwd_part(const float *__restrict__ g, int64_t ldg,
                                                      const float *__restrict__ dt, const float *__restrict__ w,
                                                      const float *__restrict__ b, int dtime, int64_t n_rows,
                                                      const int32_t *n_rows_dev, int64_t rows_per_cta,
                                                      float *__restrict__ part) {
+  __shared__ float sw_s[8][32], sb_s[8][32];
   const int64_t n = n_rows_dev ? (int64_t)(*n_rows_dev) : n_rows;
-  const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_cta;
   const int64_t r1 = min(n, r0 + rows_per_cta);
-  for (int c = threadIdx.x; c < dtime; c += blockDim.x) {
-    const float wc = w[c], bc = b[c];
-    float sw = 0.f, sb = 0.f;
-    for (int64_t r = r0; r < r1; ++r) {
-      const float t = dt[r];
+  float sw = 0.f, sb = 0.f;
+  if (c < dtime) {
+    const float wc = __ldg(w + c), bc = __ldg(b + c);
+    for (int64_t r = r0 + wp; r < r1; r += 8) {
+      const float t = __ldg(dt + r);
       const float gs = -sinf(fmaf(t, wc, bc)) * g[r * ldg + c];
       sw = fmaf(gs, t, sw);
       sb += gs;
     }
-    part[((int64_t)blockIdx.x * 2 + 0) * dtime + c] = sw;
-    part[((int64_t)blockIdx.x * 2 + 1) * dtime + c] = sb;
+  }
+  sw_s[wp][lane] = sw;
+  sb_s[wp][lane] = sb;
+  __syncthreads();
+  if (wp == 0 && c < dtime) {
+    float aw = 0.f, ab = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { aw += sw_s[i][lane]; ab += sb_s[i][lane]; }
+    part[((int64_t)blockIdx.y * 2 + 0) * dtime + c] = aw;
+    part[((int64_t)blockIdx.y * 2 + 1) * dtime + c] = ab;
   }
 }
 
@@ -93,14 +107,15 @@ __global__ void k_te_bwd_reduce(const float *__restrict__ part, int nparts, int 
   db[c] += sb;
 }
 
-constexpr int64_t kTeRowsPerCta = 512;
-constexpr int kTeMaxParts = 4096;
+constexpr int64_t kTeRowsPerCta = 128;
+constexpr int kTeMaxParts = 2048;
 
 inline bool a16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
 
-extern "C" int fb_gather_time_encode(const float *h, int64_t ldh, const int32_t *h_idx, int64_t h_off, int dn,
+extern "C" int fb_gather_time_encode(const float *h, int64_t ldh, const int32_t *h_idx, int64_t h_off,
+                                     const int32_t *h_off_dev, int dn,
                                      const float *f, int64_t ldf, const int32_t *f_idx, int de, const float *dt,
                                      const float *w, const float *b, int dtime, float *A, int64_t lda,
                                      int64_t n_rows, const int32_t *n_rows_dev, cudaStream_t stream) {
@@ -108,7 +123,7 @@ extern "C" int fb_gather_time_encode(const float *h, int64_t ldh, const int32_t 
       (de > 0 && !f) || (dtime > 0 && (!w || !b)))
     return fb::set_error(FB_ERR_ARG, "gather_time_encode: bad argument");
   if (n_rows == 0) return FB_OK;
-  GatherArgs a{h, ldh, h_idx, h_off, dn, f, ldf, f_idx, de, dt, w, b, dtime, A, lda, n_rows, n_rows_dev};
+  GatherArgs a{h, ldh, h_idx, h_off, h_off_dev, dn, f, ldf, f_idx, de, dt, w, b, dtime, A, lda, n_rows, n_rows_dev};
   const bool vec = (dn % 4 == 0) && (de % 4 == 0) && (lda % 4 == 0) && (ldh % 4 == 0 || dn == 0) &&
                    (ldf % 4 == 0 || de == 0) && a16(A) && (dn == 0 || a16(h)) && (de == 0 || a16(f));
   int64_t need = (n_rows + kRowsPerCta - 1) / kRowsPerCta;
@@ -133,7 +148,8 @@ extern "C" int fb_time_encode_bwd(const float *g, int64_t ldg, const float *dt, 
   int64_t rows = std::max<int64_t>(kTeRowsPerCta, (n_rows + kTeMaxParts - 1) / kTeMaxParts);
   int parts = (int)std::max<int64_t>(1, (n_rows + rows - 1) / rows);
   float *part = static_cast<float *>(ws);
-  k_te_bwd_part<<<parts, 256, 0, stream>>>(g, ldg, dt, w, b, dtime, n_rows, n_rows_dev, rows, part);
+  dim3 grid((dtime + 31) / 32, parts);
+  k_te_bwd_part<<<grid, 256, 0, stream>>>(g, ldg, dt, w, b, dtime, n_rows, n_rows_dev, rows, part);
   FB_LAUNCHED("k_te_bwd_part");
   k_te_bwd_reduce<<<(dtime + 127) / 128, 128, 0, stream>>>(part, parts, dtime, dw, db);
   FB_LAUNCHED("k_te_bwd_reduce");

@@ -163,15 +163,26 @@ __global__ void k_split_reduce(const float *__restrict__ P, int nsplit, int N, i
   *c = accumulate ? (*c + s) : s;
 }
 
+// Column sums, stage 1: CTA (x = 32-column tile, y = row chunk), 8 warps
+// striding over rows, lanes over columns, warp sums combined in fixed order.
 __global__ void __launch_bounds__(256) k_colsum_part(const float *__restrict__ G, int64_t ldg, int64_t M_host,
                                                      const int32_t *M_dev, int N, int64_t rows_per_part,
                                                      float *__restrict__ part) {
+  __shared__ float s_acc[8][32];
   const int64_t M = M_dev ? (int64_t)(*M_dev) : M_host;
-  const int64_t r0 = (int64_t)blockIdx.x * rows_per_part, r1 = min(M, r0 + rows_per_part);
-  for (int c = threadIdx.x; c < N; c += blockDim.x) {
-    float s = 0.f;
-    for (int64_t r = r0; r < r1; ++r) s += G[r * ldg + c];
-    part[(int64_t)blockIdx.x * N + c] = s;
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
+  const int64_t r0 = (int64_t)blockIdx.y * rows_per_part, r1 = min(M, r0 + rows_per_part);
+  float s = 0.f;
+  if (c < N)
+    for (int64_t r = r0 + wp; r < r1; r += 8) s += G[r * ldg + c];
+  s_acc[wp][lane] = s;
+  __syncthreads();
+  if (wp == 0 && c < N) {
+    float a = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a += s_acc[i][lane];
+    part[(int64_t)blockIdx.y * N + c] = a;
   }
 }
 
@@ -195,7 +206,7 @@ inline int64_t tn_rows_per_split(int64_t M, int N, int K) {
   return rows;
 }
 
-constexpr int64_t kColsumRows = 1024;
+constexpr int64_t kColsumRows = 256;
 
 }  // namespace
 
@@ -247,7 +258,8 @@ extern "C" int fb_colsum(const float *G, int64_t ldg, float *db, int64_t M, cons
   if (!G || !db || !ws || M < 0 || N < 1 || ldg < N) return fb::set_error(FB_ERR_ARG, "colsum: bad argument");
   const int parts = (int)std::max<int64_t>(1, (M + kColsumRows - 1) / kColsumRows);
   float *part = static_cast<float *>(ws);
-  k_colsum_part<<<parts, 256, 0, stream>>>(G, ldg, M, M_dev, N, kColsumRows, part);
+  dim3 grid((N + 31) / 32, parts);
+  k_colsum_part<<<grid, 256, 0, stream>>>(G, ldg, M, M_dev, N, kColsumRows, part);
   FB_LAUNCHED("k_colsum_part");
   k_colsum_reduce<<<(N + 127) / 128, 128, 0, stream>>>(part, parts, N, db, accumulate);
   FB_LAUNCHED("k_colsum_reduce");

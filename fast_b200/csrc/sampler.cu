@@ -23,8 +23,8 @@ constexpr int kErrRootRange = 1;
 
 struct BlockBuf {
   int32_t *row = nullptr, *col = nullptr, *eid = nullptr, *nodes = nullptr;
-  int32_t *rptr = nullptr, *cntE = nullptr, *uniE = nullptr, *invE = nullptr;
-  float *ts = nullptr, *dts = nullptr;
+  int32_t *rptr = nullptr, *cntE = nullptr, *uniE = nullptr, *invE = nullptr, *nbr = nullptr;
+  float *ts = nullptr, *dts = nullptr, *dte = nullptr;
   int64_t cap_roots = 0, cap_edges = 0;
 };
 
@@ -48,7 +48,8 @@ struct SampleArgs {
   const int32_t *R_dev;
   int use_ptr, num_history, neighs, recent, prop_time;
   float wd, offset;
-  uint32_t key0, key1, call_lo, slot;
+  uint32_t key0, key1, slot;
+  const uint32_t *call_dev;  // sampler step counter (device)
   int32_t *err;
 };
 
@@ -76,7 +77,7 @@ __device__ __forceinline__ void root_window(const SampleArgs &a, int n, float nt
 
 // Uniform pick number i of root j: s + floor(u * (e - s + 1)), u from Philox.
 __device__ __forceinline__ int uniform_pick(const SampleArgs &a, int64_t j, int i, int s, int e) {
-  fb::Philox4 r = fb::philox4x32_10((uint32_t)j, (uint32_t)(i >> 2), a.call_lo, a.slot, a.key0, a.key1);
+  fb::Philox4 r = fb::philox4x32_10((uint32_t)j, (uint32_t)(i >> 2), *a.call_dev, a.slot, a.key0, a.key1);
   uint32_t u = r.v[i & 3];
   uint32_t span = (uint32_t)(e - s + 1);
   return s + (int)(((uint64_t)u * (uint64_t)span) >> 32);
@@ -99,6 +100,10 @@ __device__ __forceinline__ void for_each_pick(const SampleArgs &a, int64_t j, in
     }
   }
 }
+
+__global__ void k_bump_call(uint32_t *call) { *call += 1; }
+
+__global__ void k_set_call(uint32_t *call, uint32_t v) { *call = v; }
 
 __global__ void k_reset(const int32_t *__restrict__ indptr, int32_t *__restrict__ ptr, int64_t n_nodes,
                         int nslots) {
@@ -183,7 +188,8 @@ __global__ void __launch_bounds__(kThreads) k_sample_write(SampleArgs a, const i
                                                            int32_t *__restrict__ row, int32_t *__restrict__ col,
                                                            int32_t *__restrict__ eid_out, float *__restrict__ ts_out,
                                                            float *__restrict__ dts_out, int32_t *__restrict__ nodes_out,
-                                                           int32_t *__restrict__ rptr, int32_t *__restrict__ cntE) {
+                                                           int32_t *__restrict__ rptr, int32_t *__restrict__ cntE,
+                                                           float *__restrict__ dte, int32_t *__restrict__ nbr) {
   __shared__ int sm[64];
   int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   int64_t R = num_roots(a);
@@ -204,13 +210,17 @@ __global__ void __launch_bounds__(kThreads) k_sample_write(SampleArgs a, const i
   if (n < 0 || n >= a.n_nodes) return;
   int t = off;
   for_each_pick(a, j, n, nts, [&](int k) {
-    float tk = __ldg(a.ts + k);
+    const float tk = __ldg(a.ts + k);
+    const float d = __fsub_rn(nts, tk);
+    const int32_t nb = __ldg(a.indices + k);
     row[t] = (int32_t)j;
     col[t] = (int32_t)(R + t);
     eid_out[t] = __ldg(a.eid + k);
     ts_out[R + t] = a.prop_time ? nts : tk;
-    dts_out[R + t] = __fsub_rn(nts, tk);
-    nodes_out[R + t] = __ldg(a.indices + k);
+    dts_out[R + t] = d;
+    nodes_out[R + t] = nb;
+    dte[t] = d;
+    nbr[t] = nb;
     ++t;
   });
 }
@@ -308,6 +318,7 @@ struct fb_sampler {
   std::vector<BlockBuf> blocks;
   int32_t *dims = nullptr;     // 8 per block
   int32_t *err = nullptr;
+  uint32_t *call_dev = nullptr;
   int32_t *roots_in = nullptr;
   float *rts_in = nullptr;
   int64_t cap_r0 = 0;
@@ -323,10 +334,11 @@ struct fb_sampler {
 namespace {
 
 void free_block(BlockBuf &b) {
-  int32_t *ip[] = {b.row, b.col, b.eid, b.nodes, b.rptr, b.cntE, b.uniE, b.invE};
+  int32_t *ip[] = {b.row, b.col, b.eid, b.nodes, b.rptr, b.cntE, b.uniE, b.invE, b.nbr};
   for (auto p : ip) if (p) cudaFree(p);
   if (b.ts) cudaFree(b.ts);
   if (b.dts) cudaFree(b.dts);
+  if (b.dte) cudaFree(b.dte);
   b = BlockBuf();
 }
 
@@ -338,6 +350,8 @@ int alloc_block(BlockBuf &b, int64_t cr, int64_t ce) {
   FB_TRY_CUDA(cudaMalloc(&b.eid, ce1 * 4));
   FB_TRY_CUDA(cudaMalloc(&b.uniE, ce1 * 4));
   FB_TRY_CUDA(cudaMalloc(&b.invE, ce1 * 4));
+  FB_TRY_CUDA(cudaMalloc(&b.nbr, ce1 * 4));
+  FB_TRY_CUDA(cudaMalloc(&b.dte, ce1 * 4));
   FB_TRY_CUDA(cudaMalloc(&b.nodes, cn * 4));
   FB_TRY_CUDA(cudaMalloc(&b.ts, cn * 4));
   FB_TRY_CUDA(cudaMalloc(&b.dts, cn * 4));
@@ -405,7 +419,7 @@ int run_layer_slot(fb_sampler *s, int bidx, const int32_t *roots, const float *r
   a.recent = s->recent; a.prop_time = s->prop_time;
   a.wd = s->wd; a.offset = offset;
   a.key0 = (uint32_t)s->seed; a.key1 = (uint32_t)(s->seed >> 32);
-  a.call_lo = (uint32_t)s->call_index; a.slot = (uint32_t)bidx;
+  a.call_dev = s->call_dev; a.slot = (uint32_t)bidx;
   a.err = s->err;
   int32_t *dims = s->dims + 8 * bidx;
   const int nb = nblk(R_cap);
@@ -414,7 +428,7 @@ int run_layer_slot(fb_sampler *s, int bidx, const int32_t *roots, const float *r
   k_scan_parts<<<1, 1024, 0, st>>>(s->ws_part, nb, R_host, R_dev, dims, b.rptr, b.cntE);
   FB_LAUNCHED("k_scan_parts");
   k_sample_write<<<nb, kThreads, 0, st>>>(a, s->ws_cnt, s->ws_part, b.row, b.col, b.eid, b.ts, b.dts,
-                                          b.nodes, b.rptr, b.cntE);
+                                          b.nodes, b.rptr, b.cntE, b.dte, b.nbr);
   FB_LAUNCHED("k_sample_write");
   return FB_OK;
 }
@@ -462,6 +476,8 @@ extern "C" int fb_sampler_create(const int32_t *indptr, const int32_t *indices, 
   FB_TRY_CUDA(cudaMemset(s->dims, 0, 8 * 4 * num_layers * num_history));
   FB_TRY_CUDA(cudaMalloc(&s->err, 4));
   FB_TRY_CUDA(cudaMemset(s->err, 0, 4));
+  FB_TRY_CUDA(cudaMalloc(&s->call_dev, 4));
+  FB_TRY_CUDA(cudaMemset(s->call_dev, 0, 4));
   *out = s;
   return fb_sampler_reset(s, 0) == FB_OK ? (cudaDeviceSynchronize() == cudaSuccess ? FB_OK : FB_ERR_CUDA)
                                          : FB_ERR_CUDA;
@@ -477,7 +493,7 @@ extern "C" int fb_sampler_destroy(fb_sampler *s) {
   if (s->owns_graph) {
     cudaFree(s->indptr); cudaFree(s->indices); cudaFree(s->eid); cudaFree(s->ts);
   }
-  void *ps[] = {s->ts_ptr, s->dims, s->err, s->roots_in, s->rts_in, s->ws_cnt, s->ws_part,
+  void *ps[] = {s->ts_ptr, s->dims, s->err, s->call_dev, s->roots_in, s->rts_in, s->ws_cnt, s->ws_part,
                 s->dd_keys, s->dd_minpos, s->dd_slot, s->dd_uidx, s->dd_part};
   for (auto p : ps) if (p) cudaFree(p);
   cudaSetDevice(cur);
@@ -548,6 +564,8 @@ extern "C" int fb_sampler_sample(fb_sampler *s, const int32_t *roots, const floa
       if (rc) return rc;
     }
   }
+  k_bump_call<<<1, 1, 0, st>>>(s->call_dev);
+  FB_LAUNCHED("k_bump_call");
   s->call_index++;
   s->sampled = true;
   return FB_OK;
@@ -564,6 +582,7 @@ extern "C" int fb_sampler_block(const fb_sampler *s, int i, fb_block_view *out) 
   out->row = b.row; out->col = b.col; out->eid = b.eid;
   out->ts = b.ts; out->dts = b.dts; out->nodes = b.nodes;
   out->rptr = b.rptr; out->cntE = b.cntE; out->uniE = b.uniE; out->invE = b.invE;
+  out->dte = b.dte; out->nbr = b.nbr;
   out->dims = s->dims + 8 * i;
   out->max_roots = b.cap_roots;
   out->max_edges = b.cap_edges;
@@ -587,6 +606,9 @@ extern "C" int fb_sampler_dims(fb_sampler *s, int32_t *host_dims, cudaStream_t s
 extern "C" int fb_sampler_set_call_index(fb_sampler *s, uint64_t call_index) {
   if (!s) return fb::set_error(FB_ERR_ARG, "fb_sampler_set_call_index: null sampler");
   s->call_index = call_index;
+  k_set_call<<<1, 1>>>(s->call_dev, (uint32_t)call_index);
+  FB_LAUNCHED("k_set_call");
+  FB_TRY_CUDA(cudaDeviceSynchronize());
   return FB_OK;
 }
 

@@ -9,13 +9,20 @@ LayerNorm, edge predictor) stays in PyTorch.
 import numpy as np
 import torch
 
+from . import ops
 from .ops import AttentionCore
 
 
 class DeviceBlock:
     """One sampled block resident on the GPU (replaces the DGL block built by
-    utils.py:67-87).  Destinations are the block's roots; sources are
-    [roots | one node per edge]; edges are grouped by destination."""
+    utils.py:67-87), sized from host-read dims.  Destinations are the block's
+    roots; sources are [roots | one node per edge]; edges are grouped by
+    destination."""
+
+    static = False
+    n_dst_static = True
+    n_dst_dev = None
+    n_edges_dev = None
 
     def __init__(self, view, dims):
         R, E, S, dim_in = (int(x) for x in dims[:4])
@@ -24,8 +31,9 @@ class DeviceBlock:
         self.eid = view["eid"][:E]
         self.nodes = view["nodes"][:dim_in]
         self.ts = view["ts"][:dim_in]
-        self.dts = view["dts"][:dim_in]
-        self.dt_edges = view["dts"][R:R + E]
+        self.dst_nodes = view["nodes"][:R]
+        self.src_nodes = view["nbr"][:E]
+        self.dt_edges = view["dte"][:E]
         self.rptr = view["rptr"][:R + 1]
         self.cntE = view["cntE"][:S + 1] if E > 0 else view["cntE"][:0]
 
@@ -34,6 +42,36 @@ class DeviceBlock:
 
     def num_src_nodes(self):
         return self.n_src
+
+    def num_edges(self):
+        return self.n_edges
+
+
+class StaticBlock:
+    """Capacity-sized views of a sampled block with its sizes left on the
+    device (dims[0] = roots, dims[1] = edges): every kernel launched on it has
+    a fixed shape, so a training step over static blocks can be captured in a
+    CUDA graph and replayed.  `n_roots` fixes the root count when the host
+    knows it (the batch roots of block 0)."""
+
+    static = True
+
+    def __init__(self, view, n_roots=None):
+        cap_r, cap_e = int(view["max_roots"]), max(int(view["max_edges"]), 1)
+        self.n_dst_static = n_roots is not None
+        self.n_dst = int(n_roots) if n_roots is not None else cap_r
+        self.n_edges = cap_e
+        self.n_src = self.n_dst + cap_e
+        self.n_dst_dev = view["dims"][0:1]
+        self.n_edges_dev = view["dims"][1:2]
+        self.eid = view["eid"][:cap_e]
+        self.dst_nodes = view["nodes"][:self.n_dst]
+        self.src_nodes = view["nbr"][:cap_e]
+        self.dt_edges = view["dte"][:cap_e]
+        self.rptr = view["rptr"][:self.n_dst + 1]
+
+    def num_dst_nodes(self):
+        return self.n_dst
 
     def num_edges(self):
         return self.n_edges
@@ -102,11 +140,12 @@ class TransfomerAttentionLayer(torch.nn.Module):
         self.layer_norm = torch.nn.LayerNorm(dim_out)
         self.step_seed = 0
 
-    def forward(self, blk, h_all=None, node_table=None, edge_table=None, seed=0, offset=0):
-        """blk: DeviceBlock; h_all: [n_src, dim_node_feat] previous-layer output,
-        or node_table + blk.nodes for the input layer."""
+    def forward(self, blk, h_all=None, node_table=None, edge_table=None, seed=0, offset_dev=None):
+        """blk: DeviceBlock or StaticBlock; h_all: [n_src, dim_node_feat]
+        previous-layer output, or node_table + blk node ids for the input layer.
+        offset_dev: int64 device counter keying the attention dropout."""
         dev = self.w_k.weight.device
-        if blk.n_edges == 0:
+        if not blk.static and blk.n_edges == 0:
             return torch.zeros((blk.n_dst, self.dim_out), device=dev)
         if self.dim_node_feat + self.dim_time == 0:
             raise NotImplementedError("Q = ones branch (layers.py:137-140) is not on the device path")
@@ -118,9 +157,16 @@ class TransfomerAttentionLayer(torch.nn.Module):
         agg = AttentionCore.apply(h_all, te_w, te_b, self.w_q.weight, self.w_q.bias, W_kv, b_kv, blk,
                                   node_table if h_all is None else None,
                                   edge_table if self.dim_edge_feat > 0 else None,
-                                  self.num_head, self.negative_slope, p, seed, offset)
+                                  self.num_head, self.negative_slope, p, seed, offset_dev)
         if self.dim_node_feat != 0:
-            h_dst = h_all[:blk.n_dst] if h_all is not None else node_table[blk.nodes[:blk.n_dst].long()]
+            if h_all is not None:
+                h_dst = h_all[:blk.n_dst]
+            elif blk.static:
+                h_dst = ops.gather_time_encode(blk.n_dst, h=node_table, h_idx=blk.dst_nodes,
+                                               out=torch.zeros(blk.n_dst, self.dim_node_feat, device=dev),
+                                               n_rows_dev=blk.n_dst_dev)
+            else:
+                h_dst = node_table[blk.dst_nodes.long()]
             rst = torch.cat([agg, h_dst], dim=1)
         else:
             rst = agg
@@ -158,18 +204,22 @@ class GeneralModel(torch.nn.Module):
                                                                 train_param["dropout"],
                                                                 train_param["att_dropout"], gnn_param["dim_out"])
         self.edge_predictor = EdgePredictor(gnn_param["dim_out"])
-        self.step = 0
+        self._drop_step = None      # device counter keying attention dropout (not part of the state_dict)
 
     def embed(self, blocks, node_table=None, edge_table=None):
-        """blocks: DeviceBlocks in sampler order (hop 1 first); returns the
-        root embeddings [n_roots, dim_out]."""
+        """blocks: Device/StaticBlocks in sampler order (hop 1 first); returns
+        the root embeddings [n_roots, dim_out]."""
         mfgs = list(reversed(blocks))      # layer order, as to_dgl_blocks(...).reverse()
-        self.step += 1
+        dev = self.edge_predictor.out_fc.weight.device
+        if self._drop_step is None or self._drop_step.device != dev:
+            self._drop_step = torch.zeros(1, dtype=torch.int64, device=dev)
+        if self.training:
+            self._drop_step += 1
         h = None
         for l in range(self.gnn_param["layer"]):
             layer = self.layers["l%dh0" % l]
             h = layer(mfgs[l], h_all=h, node_table=node_table if l == 0 else None, edge_table=edge_table,
-                      seed=0x5EED + l, offset=self.step)
+                      seed=0x5EED + l, offset_dev=self._drop_step)
         return h
 
     def forward(self, blocks, node_table=None, edge_table=None, neg_samples=1):

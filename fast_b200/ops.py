@@ -55,8 +55,13 @@ def _f32_rows(t, name):
         raise ValueError("%s must be a CUDA fp32 matrix with unit column stride" % name)
 
 
-def gemm_nt(A, B, bias=None, out=None, accumulate=False):
-    """out[m, n] (+)= sum_k A[m, k] B[n, k] + bias[n]."""
+def _p(t):
+    """Device pointer of an optional device-count tensor."""
+    return None if t is None else t.data_ptr()
+
+
+def gemm_nt(A, B, bias=None, out=None, accumulate=False, M_dev=None):
+    """out[m, n] (+)= sum_k A[m, k] B[n, k] + bias[n]; rows m < *M_dev when given."""
     _f32_rows(A, "A")
     _f32_rows(B, "B")
     M, K = A.shape
@@ -66,13 +71,13 @@ def gemm_nt(A, B, bias=None, out=None, accumulate=False):
     if out is None:
         out = torch.empty(M, N, device=A.device, dtype=torch.float32)
     with _timed("gemm_nt", 4 * (M * K + N * K + M * N), 2 * M * N * K):
-        call("fb_gemm_nt", ptr(A), A.stride(0), ptr(B), B.stride(0), ptr(bias), ptr(out), out.stride(0), M, None,
-             N, K, int(accumulate), stream_ptr())
+        call("fb_gemm_nt", ptr(A), A.stride(0), ptr(B), B.stride(0), ptr(bias), ptr(out), out.stride(0), M,
+             _p(M_dev), N, K, int(accumulate), stream_ptr())
     return out
 
 
-def gemm_tn(G, X, out=None, accumulate=False):
-    """out[n, k] (+)= sum_m G[m, n] X[m, k]  (weight gradient)."""
+def gemm_tn(G, X, out=None, accumulate=False, M_dev=None):
+    """out[n, k] (+)= sum_m G[m, n] X[m, k]  (weight gradient); rows m < *M_dev when given."""
     _f32_rows(G, "G")
     _f32_rows(X, "X")
     M, N = G.shape
@@ -81,25 +86,26 @@ def gemm_tn(G, X, out=None, accumulate=False):
         out = torch.empty(N, K, device=G.device, dtype=torch.float32)
     ws = torch.empty(int(lib.fb_gemm_tn_ws_bytes(M, N, K)), device=G.device, dtype=torch.uint8)
     with _timed("gemm_tn", 4 * (M * N + M * K + N * K), 2 * M * N * K, kernels=2):
-        call("fb_gemm_tn", ptr(G), G.stride(0), ptr(X), X.stride(0), ptr(out), out.stride(0), M, None, N, K,
+        call("fb_gemm_tn", ptr(G), G.stride(0), ptr(X), X.stride(0), ptr(out), out.stride(0), M, _p(M_dev), N, K,
              int(accumulate), ptr(ws), stream_ptr())
     return out
 
 
-def colsum(G, out=None, accumulate=False):
+def colsum(G, out=None, accumulate=False, M_dev=None):
     _f32_rows(G, "G")
     M, N = G.shape
     if out is None:
         out = torch.empty(N, device=G.device, dtype=torch.float32)
     ws = torch.empty(int(lib.fb_colsum_ws_bytes(M, N)), device=G.device, dtype=torch.uint8)
     with _timed("colsum", 4 * (M * N + N), M * N, kernels=2):
-        call("fb_colsum", ptr(G), G.stride(0), ptr(out), M, None, N, int(accumulate), ptr(ws), stream_ptr())
+        call("fb_colsum", ptr(G), G.stride(0), ptr(out), M, _p(M_dev), N, int(accumulate), ptr(ws), stream_ptr())
     return out
 
 
 def gather_time_encode(n_rows, h=None, h_idx=None, h_off=0, f=None, f_idx=None, dt=None, w=None, b=None,
-                       out=None, device=None):
-    """Rows [h[h_idx or r + h_off] | f[f_idx or r] | cos(w*dt + b)]."""
+                       out=None, device=None, n_rows_dev=None, h_off_dev=None):
+    """Rows [h[h_idx or r + h_off (+ *h_off_dev)] | f[f_idx or r] | cos(w*dt + b)] for r < n_rows
+    (r < *n_rows_dev when given; the rest of `out` is left untouched)."""
     dn = 0 if h is None else h.shape[1]
     de = 0 if f is None else f.shape[1]
     dtime = 0 if w is None else w.numel()
@@ -109,22 +115,22 @@ def gather_time_encode(n_rows, h=None, h_idx=None, h_off=0, f=None, f_idx=None, 
     nbytes = 4 * n_rows * (2 * (dn + de) + dtime + (1 if dt is not None else 0)
                            + (1 if h_idx is not None else 0) + (1 if f_idx is not None else 0))
     with _timed("gather_time_encode", nbytes):
-        call("fb_gather_time_encode", ptr(h), 0 if h is None else h.stride(0), ptr(h_idx), int(h_off), dn,
-             ptr(f), 0 if f is None else f.stride(0), ptr(f_idx), de, ptr(dt), ptr(w), ptr(b), dtime,
-             ptr(out), out.stride(0), n_rows, None, stream_ptr())
+        call("fb_gather_time_encode", ptr(h), 0 if h is None else h.stride(0), ptr(h_idx), int(h_off),
+             _p(h_off_dev), dn, ptr(f), 0 if f is None else f.stride(0), ptr(f_idx), de, ptr(dt), ptr(w), ptr(b),
+             dtime, ptr(out), out.stride(0), n_rows, _p(n_rows_dev), stream_ptr())
     return out
 
 
-def time_encode_bwd(g, dt, w, b, dw, db):
+def time_encode_bwd(g, dt, w, b, dw, db, n_dev=None):
     """dw/db += gradient of cos(w*dt + b) given g = dL/dcos (rows at g.stride(0))."""
     n, dtime = g.shape
     ws = torch.empty(int(lib.fb_time_encode_bwd_ws_bytes(n, dtime)), device=g.device, dtype=torch.uint8)
     with _timed("time_encode_bwd", 4 * n * (dtime + 1), kernels=2):
-        call("fb_time_encode_bwd", ptr(g), g.stride(0), ptr(dt), ptr(w), ptr(b), dtime, n, None, ptr(dw),
+        call("fb_time_encode_bwd", ptr(g), g.stride(0), ptr(dt), ptr(w), ptr(b), dtime, n, _p(n_dev), ptr(dw),
              ptr(db), ptr(ws), stream_ptr())
 
 
-def attn_fwd(q, k, v, rptr, heads, slope, drop_p=0.0, seed=0, offset=0):
+def attn_fwd(q, k, v, rptr, heads, slope, drop_p=0.0, seed=0, offset=0, n_dst_dev=None, offset_dev=None):
     """agg, att = fused LeakyReLU(q.k) -> segment softmax -> dropout -> sum(att * v).
     q: [Nd, D] or [1, D] (broadcast); k, v: [E, D] views sharing a row stride."""
     nd = rptr.numel() - 1
@@ -135,12 +141,13 @@ def attn_fwd(q, k, v, rptr, heads, slope, drop_p=0.0, seed=0, offset=0):
     qrows = nd if ldq else 1
     nbytes = 4 * (qrows * D + 2 * E * D + (nd + 1) + nd * D + E * heads)
     with _timed("attn_fwd", nbytes):
-        call("fb_attn_fwd", ptr(q), ldq, ptr(k), ptr(v), k.stride(0), ptr(rptr), nd, None, heads, D, slope,
-             drop_p, seed, offset, ptr(att), ptr(agg), agg.stride(0), stream_ptr())
+        call("fb_attn_fwd", ptr(q), ldq, ptr(k), ptr(v), k.stride(0), ptr(rptr), nd, _p(n_dst_dev), heads, D, slope,
+             drop_p, seed, offset, _p(offset_dev), ptr(att), ptr(agg), agg.stride(0), stream_ptr())
     return agg, att
 
 
-def attn_bwd(q, k, v, rptr, att, dagg, heads, slope, drop_p=0.0, seed=0, offset=0, dkv=None):
+def attn_bwd(q, k, v, rptr, att, dagg, heads, slope, drop_p=0.0, seed=0, offset=0, dkv=None, n_dst_dev=None,
+             offset_dev=None):
     """dq [Nd, D] per destination, dk/dv [E, D] written interleaved into dkv [E, 2D]."""
     nd = rptr.numel() - 1
     E, D = k.shape
@@ -151,9 +158,9 @@ def attn_bwd(q, k, v, rptr, att, dagg, heads, slope, drop_p=0.0, seed=0, offset=
     qrows = nd if ldq else 1
     nbytes = 4 * (qrows * D + nd * D + 2 * E * D + E * heads + (nd + 1) + 2 * E * D + nd * D)
     with _timed("attn_bwd", nbytes):
-        call("fb_attn_bwd", ptr(q), ldq, ptr(k), ptr(v), k.stride(0), ptr(rptr), nd, None, heads, D, slope,
-             drop_p, seed, offset, ptr(att), ptr(dagg), dagg.stride(0), ptr(dq), ptr(dkv), dkv.data_ptr() + 4 * D,
-             dkv.stride(0), stream_ptr())
+        call("fb_attn_bwd", ptr(q), ldq, ptr(k), ptr(v), k.stride(0), ptr(rptr), nd, _p(n_dst_dev), heads, D,
+             slope, drop_p, seed, offset, _p(offset_dev), ptr(att), ptr(dagg), dagg.stride(0), ptr(dq), ptr(dkv),
+             dkv.data_ptr() + 4 * D, dkv.stride(0), stream_ptr())
     return dq, dkv
 
 
@@ -167,73 +174,88 @@ class AttentionCore(torch.autograd.Function):
 
     Node inputs come either from the previous layer's output h_all
     ([Nd + E, dn], differentiable; dst rows first, then one row per edge) or
-    from a node-feature table gathered by node id.  Returns agg [Nd, D]."""
+    from a node-feature table gathered by node id.  Returns agg [Nd, D].
+
+    With a static block (capacity-sized views and device-resident counts,
+    blk.static) every launch has a fixed shape and reads the true sizes on
+    the device, so the whole step can be captured in a CUDA graph."""
 
     @staticmethod
     def forward(ctx, h_all, w_t, b_t, W_q, b_q, W_kv, b_kv, blk, node_table, edge_table, heads, slope, drop_p,
-                seed, offset):
+                seed, offset_dev):
         nd, E = blk.n_dst, blk.n_edges
+        nd_dev, E_dev = blk.n_dst_dev, blk.n_edges_dev
+        if blk.static and h_all is not None and not blk.n_dst_static:
+            raise NotImplementedError("graph mode feeds h_all only to blocks with a host-known root count")
         dn = h_all.shape[1] if h_all is not None else (node_table.shape[1] if node_table is not None else 0)
         de = edge_table.shape[1] if edge_table is not None else 0
         dtime = 0 if w_t is None else w_t.numel()
         D = W_kv.shape[0] // 2
         wv = w_t.reshape(-1) if w_t is not None else None
-        # node rows: from h_all (dst 0..nd-1, src nd + e) or the feature table via node ids
+        dv = W_kv.device
         if h_all is not None:
             hsrc = dict(h=h_all, h_off=nd)
             hdst = dict(h=h_all, h_off=0)
         elif node_table is not None:
-            hsrc = dict(h=node_table, h_idx=blk.nodes[nd:nd + E])
-            hdst = dict(h=node_table, h_idx=blk.nodes[:nd])
+            hsrc = dict(h=node_table, h_idx=blk.src_nodes)
+            hdst = dict(h=node_table, h_idx=blk.dst_nodes)
         else:
             hsrc = hdst = {}
-        A = gather_time_encode(E, f=edge_table, f_idx=blk.eid, dt=blk.dt_edges, w=wv, b=b_t, device=W_kv.device,
-                               **hsrc)
-        KV = gemm_nt(A, W_kv, b_kv)
+        A = gather_time_encode(E, f=edge_table, f_idx=blk.eid, dt=blk.dt_edges, w=wv, b=b_t, device=dv,
+                               n_rows_dev=E_dev, **hsrc)
+        KV = gemm_nt(A, W_kv, b_kv, M_dev=E_dev)
         if dn > 0:
-            Qin = gather_time_encode(nd, w=wv, b=b_t, device=W_kv.device, **hdst)
+            Qin = torch.zeros(nd, dn + dtime, device=dv) if blk.static else None
+            Qin = gather_time_encode(nd, w=wv, b=b_t, device=dv, out=Qin, n_rows_dev=nd_dev, **hdst)
+            Q = gemm_nt(Qin, W_q, b_q, M_dev=nd_dev)
         else:
-            Qin = gather_time_encode(1, w=wv, b=b_t, device=W_kv.device)
-        Q = gemm_nt(Qin, W_q, b_q)
-        agg, att = attn_fwd(Q, KV[:, :D], KV[:, D:], blk.rptr, heads, slope, drop_p, seed, offset)
-        ctx.save_for_backward(A, KV, Qin, Q, att, W_q, W_kv, wv, b_t)
+            Qin = gather_time_encode(1, w=wv, b=b_t, device=dv)
+            Q = gemm_nt(Qin, W_q, b_q)
+        agg, att = attn_fwd(Q, KV[:, :D], KV[:, D:], blk.rptr, heads, slope, drop_p, seed, 0, n_dst_dev=nd_dev,
+                            offset_dev=offset_dev)
+        ctx.save_for_backward(A, KV, Qin, Q, att, W_q, W_kv, wv, b_t, offset_dev)
         ctx.blk = blk
-        ctx.cfg = (dn, de, dtime, D, heads, slope, drop_p, seed, offset, h_all is not None)
+        ctx.cfg = (dn, de, dtime, D, heads, slope, drop_p, seed, h_all is not None)
         return agg
 
     @staticmethod
     def backward(ctx, dagg):
-        A, KV, Qin, Q, att, W_q, W_kv, wv, b_t = ctx.saved_tensors
-        dn, de, dtime, D, heads, slope, drop_p, seed, offset, has_h = ctx.cfg
+        A, KV, Qin, Q, att, W_q, W_kv, wv, b_t, offset_dev = ctx.saved_tensors
+        dn, de, dtime, D, heads, slope, drop_p, seed, has_h = ctx.cfg
         blk = ctx.blk
         nd, E = blk.n_dst, blk.n_edges
+        nd_dev, E_dev = blk.n_dst_dev, blk.n_edges_dev
         dagg = dagg.contiguous()
-        dQ, dKV = attn_bwd(Q, KV[:, :D], KV[:, D:], blk.rptr, att, dagg, heads, slope, drop_p, seed, offset)
-        dW_kv = gemm_tn(dKV, A)
-        db_kv = colsum(dKV)
+        dQ, dKV = attn_bwd(Q, KV[:, :D], KV[:, D:], blk.rptr, att, dagg, heads, slope, drop_p, seed, 0,
+                           n_dst_dev=nd_dev, offset_dev=offset_dev)
+        dW_kv = gemm_tn(dKV, A, M_dev=E_dev)
+        db_kv = colsum(dKV, M_dev=E_dev)
         g_h = g_w = g_b = None
         if has_h and ctx.needs_input_grad[0]:
-            g_h = torch.empty(nd + E, dn, device=dagg.device, dtype=torch.float32)
-            gemm_nt(dKV, W_kv[:, :dn].t().contiguous(), out=g_h[nd:])
+            g_h = torch.zeros(nd + E, dn, device=dagg.device, dtype=torch.float32)
+            gemm_nt(dKV, W_kv[:, :dn].t().contiguous(), out=g_h[nd:], M_dev=E_dev)
         if dtime > 0:
             g_w = torch.zeros(dtime, device=dagg.device, dtype=torch.float32)
             g_b = torch.zeros(dtime, device=dagg.device, dtype=torch.float32)
-            dA_t = gemm_nt(dKV, W_kv[:, dn + de:].t().contiguous())
-            time_encode_bwd(dA_t, blk.dt_edges, wv, b_t, g_w, g_b)
+            dA_t = gemm_nt(dKV, W_kv[:, dn + de:].t().contiguous(), M_dev=E_dev)
+            time_encode_bwd(dA_t, blk.dt_edges, wv, b_t, g_w, g_b, n_dev=E_dev)
         # Q side
         if Qin.shape[0] == 1 and nd != 1:
-            dq_vec = colsum(dQ)
+            dq_vec = colsum(dQ, M_dev=nd_dev)
             dW_q = torch.outer(dq_vec, Qin[0])
             db_q = dq_vec
             dQin = (dq_vec @ W_q).unsqueeze(0)
         else:
-            dW_q = gemm_tn(dQ, Qin)
-            db_q = colsum(dQ)
-            dQin = gemm_nt(dQ, W_q.t().contiguous())
+            dW_q = gemm_tn(dQ, Qin, M_dev=nd_dev)
+            db_q = colsum(dQ, M_dev=nd_dev)
+            dQin = gemm_nt(dQ, W_q.t().contiguous(), M_dev=nd_dev)
         if g_h is not None and dn > 0:
             g_h[:nd].copy_(dQin[:, :dn])
         if dtime > 0:
-            # every Q row's time block is cos(b_t) (TimeEncode of dt = 0)
-            g_b -= torch.sin(b_t) * dQin[:, dn:].sum(0)
+            # every Q row's time block is cos(b_t) (TimeEncode of dt = 0); rows
+            # past the device-side count carry no gradient
+            rows = dQin[:, dn:] if nd_dev is None or Qin.shape[0] == 1 else \
+                torch.where((torch.arange(nd, device=dagg.device) < nd_dev).unsqueeze(1), dQin[:, dn:], 0.0)
+            g_b -= torch.sin(b_t) * rows.sum(0)
         return (g_h, None if g_w is None else g_w.view(-1, 1), g_b, dW_q, db_q, dW_kv, db_kv,
                 None, None, None, None, None, None, None, None)

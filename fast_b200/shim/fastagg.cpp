@@ -224,7 +224,8 @@ TL forward_fused_softmax_agg(torch::Tensor q, torch::Tensor k, torch::Tensor v, 
   auto agg = torch::empty({nd, (int64_t)dim}, f32(q));
   check(fb_attn_fwd(q.data_ptr<float>(), ldq, k.data_ptr<float>(), v.data_ptr<float>(), k.stride(0),
                     rptr.data_ptr<int32_t>(), nd, nullptr, num_heads, dim, (float)negative_slope, (float)attn_drop,
-                    (uint64_t)seed, (uint64_t)offset, att.data_ptr<float>(), agg.data_ptr<float>(), dim, cur_stream()));
+                    (uint64_t)seed, (uint64_t)offset, nullptr, att.data_ptr<float>(), agg.data_ptr<float>(), dim,
+                    cur_stream()));
   return {agg, att};
 }
 
@@ -243,7 +244,8 @@ TL backward_fused_softmax_agg(torch::Tensor q, torch::Tensor k, torch::Tensor v,
   auto dv = torch::empty({E, (int64_t)dim}, f32(q));
   check(fb_attn_bwd(q.data_ptr<float>(), ldq, k.data_ptr<float>(), v.data_ptr<float>(), k.stride(0),
                     rptr.data_ptr<int32_t>(), nd, nullptr, num_heads, dim, (float)negative_slope, (float)attn_drop,
-                    (uint64_t)seed, (uint64_t)offset, att.data_ptr<float>(), dagg.data_ptr<float>(), dagg.stride(0),
+                    (uint64_t)seed, (uint64_t)offset, nullptr, att.data_ptr<float>(), dagg.data_ptr<float>(),
+                    dagg.stride(0),
                     dq.data_ptr<float>(), dk.data_ptr<float>(), dv.data_ptr<float>(), dim, cur_stream()));
   return {dq, dk, dv};
 }

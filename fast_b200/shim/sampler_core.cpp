@@ -188,6 +188,8 @@ class Sampler {
       d["uniE"] = view_of(h, v.uniE, ce, torch::kInt32);
       d["invE"] = view_of(h, v.invE, ce, torch::kInt32);
       d["dims"] = view_of(h, v.dims, 8, torch::kInt32);
+      d["dte"] = view_of(h, v.dte, ce, torch::kFloat32);
+      d["nbr"] = view_of(h, v.nbr, ce, torch::kInt32);
       d["max_roots"] = cr;
       d["max_edges"] = v.max_edges;
       out.append(d);

@@ -16,7 +16,7 @@ import torch
 import torch.distributed as dist
 
 from . import ops
-from .model import DeviceBlock, GeneralModel
+from .model import DeviceBlock, GeneralModel, StaticBlock
 from .ext import sampler_core
 
 
@@ -63,7 +63,7 @@ class Trainer:
             use_ptr = first or sp["strategy"] == "recent" or (sp["prop_time"] and sp["history"] == 1)
             first = False
             n += (1 if use_ptr else 0) + 3 * sp["history"]
-        return n
+        return n + 1   # the device call-counter bump
 
     def reset_epoch(self):
         self.sampler.reset()
@@ -132,3 +132,128 @@ class Trainer:
 
 def batch_ranges(train_end, batch):
     return [(b, min(b + batch, train_end)) for b in range(0, train_end, batch) if min(b + batch, train_end) - b == batch]
+
+
+class GraphTrainer(Trainer):
+    """Trainer whose whole step -- sampling, gather + time encoding,
+    projections, attention, layer tails, loss, backward and Adam -- is
+    captured once in a CUDA graph and replayed.  Blocks are StaticBlocks
+    (capacity-sized, sizes on the device), so no step reads anything back to
+    the host.  With several ranks the step is two graphs around one NCCL
+    all-reduce of the flat gradient bucket."""
+
+    def __init__(self, graph, node_feats, edge_feats, sample_param, memory_param, gnn_param, train_param,
+                 device, batch, rank=0, world=1, seed=42, sampler_seed=1234):
+        super().__init__(graph, node_feats, edge_feats, sample_param, memory_param, gnn_param, train_param,
+                         device, rank=rank, world=world, seed=seed, sampler_seed=sampler_seed)
+        self.B = batch
+        self.R0 = 3 * batch
+        dv = self.device
+        self.opt = torch.optim.Adam(self.model.parameters(), lr=train_param["lr"], capturable=True)
+        self.roots_buf = torch.zeros(self.R0, dtype=torch.int32, device=dv)
+        self.ts_buf = torch.zeros(self.R0, dtype=torch.float32, device=dv)
+        self.loss_buf = torch.zeros((), device=dv)
+        self.h_roots = torch.zeros(self.R0, dtype=torch.int32).pin_memory()
+        self.h_ts = torch.zeros(self.R0, dtype=torch.float32).pin_memory()
+        self.g_main = self.g_opt = None
+        self._params = [p for p in self.model.parameters()]
+
+    # the body of one step on the static input buffers
+    def _fwd_bwd(self):
+        self.sampler.sample_device(self.roots_buf, self.ts_buf)
+        views = self.sampler.block_views()
+        blocks = [StaticBlock(views[0], n_roots=self.R0)] + [StaticBlock(v) for v in views[1:]]
+        for p in self._params:
+            if p.grad is not None:
+                p.grad.zero_()
+        pred_pos, pred_neg = self.model(blocks, self.node_feats, self.edge_feats)
+        loss = self.crit(pred_pos, torch.ones_like(pred_pos)) + self.crit(pred_neg, torch.zeros_like(pred_neg))
+        loss.backward()
+        self.loss_buf.copy_(loss.detach())
+        if self.world > 1:
+            torch.cat([p.grad.reshape(-1) for p in self._params], out=self._flat)
+
+    def _apply(self):
+        if self.world > 1:
+            self._flat.div_(self.world)
+            off = 0
+            for p in self._params:
+                n = p.numel()
+                p.grad.copy_(self._flat[off:off + n].view_as(p))
+                off += n
+        self.opt.step()
+
+    def _eager_step(self):
+        self._fwd_bwd()
+        if self.world > 1:
+            dist.all_reduce(self._flat)
+        self._apply()
+
+    def capture(self, warmup=3):
+        """Warm up on a side stream (allocator, lazy kernel loads, Adam state),
+        then capture.  The warm-up steps are real training steps on whatever
+        is in the input buffers."""
+        for p in self._params:
+            p.grad = torch.zeros_like(p)
+        if self.world > 1:
+            self._flat = torch.zeros(sum(p.numel() for p in self._params), device=self.device)
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self._eager_step()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        self.g_main = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.g_main):
+            self._fwd_bwd()
+            if self.world == 1:
+                self._apply()
+        if self.world > 1:
+            self.g_opt = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.g_opt, pool=self.g_main.pool()):
+                self._apply()
+        torch.cuda.synchronize(self.device)
+
+    def _replay(self):
+        self.g_main.replay()
+        if self.world > 1:
+            dist.all_reduce(self._flat)
+            self.g_opt.replay()
+
+    def load_device_roots(self, b0, b1):
+        """Fills the input buffers with this rank's slice of the global batch [b0, b1)."""
+        lo, hi = self.local_slice(b0, b1)
+        B = hi - lo
+        assert B == self.B, "graph was captured for a local batch of %d" % self.B
+        self.roots_buf[:B].copy_(self.src[lo:hi])
+        self.roots_buf[B:2 * B].copy_(self.dst[lo:hi])
+        torch.randint(0, self.graph.n_nodes, (B,), device=self.device, generator=self.neg_gen,
+                      out=self.roots_buf[2 * B:])
+        t = self.ts[lo:hi]
+        self.ts_buf[:B].copy_(t)
+        self.ts_buf[B:2 * B].copy_(t)
+        self.ts_buf[2 * B:].copy_(t)
+
+    def step_device(self, roots=None, root_ts=None):
+        """One replayed step on the device-resident input buffers (or the given
+        device tensors); returns the loss tensor (no host round trip)."""
+        if roots is not None:
+            self.roots_buf.copy_(roots)
+            self.ts_buf.copy_(root_ts)
+        if self.g_main is None:
+            self.capture()
+        self._replay()
+        return self.loss_buf
+
+    def step_host(self, roots_np, ts_np):
+        """End-to-end step: host roots -> pinned staging -> device buffers ->
+        replay -> loss read back to the host."""
+        self.h_roots.numpy()[:] = roots_np
+        self.h_ts.numpy()[:] = ts_np
+        self.roots_buf.copy_(self.h_roots, non_blocking=True)
+        self.ts_buf.copy_(self.h_ts, non_blocking=True)
+        if self.g_main is None:
+            self.capture()
+        self._replay()
+        return float(self.loss_buf)

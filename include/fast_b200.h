@@ -53,13 +53,18 @@ typedef struct fb_sampler fb_sampler;
  *   rptr[dim_out + 1]                 CSR offsets over ALL roots (empty rows allowed)
  *   cntE[S + 1]                       offsets over non-empty rows only (:384-410)
  *   uniE[n_uni], invE[E]              eid dedup, first-appearance order (:414-451),
- *                                     valid after fb_sampler_dedup()          */
+ *                                     valid after fb_sampler_dedup()
+ *   dte[E], nbr[E]                    copies of dts[R + e] and nodes[R + e] at a
+ *                                     fixed base, for launches that must not
+ *                                     depend on the device-only root count   */
 typedef struct {
   int32_t *row, *col, *eid;
   float *ts, *dts;
   int32_t *nodes, *rptr, *cntE, *uniE, *invE;
   int32_t *dims;
   int64_t max_roots, max_edges;
+  float *dte;
+  int32_t *nbr;
 } fb_block_view;
 
 /* Copies (graph_on_device == 0) or borrows (== 1) the time-sorted CSR
@@ -88,7 +93,9 @@ int fb_sampler_block(const fb_sampler *s, int i, fb_block_view *out);
 int fb_sampler_dims(fb_sampler *s, int32_t *host_dims, cudaStream_t stream);
 /* Builds uniE/invE of block i on the device (dims[4] receives n_uni). */
 int fb_sampler_dedup(fb_sampler *s, int i, cudaStream_t stream);
-/* Sampler step counter that keys uniform draws; set it to replay a batch. */
+/* Sampler step counter that keys uniform draws; set it to replay a batch.
+ * The counter lives in device memory and every sample() call advances it on
+ * the stream, so a captured CUDA graph draws fresh samples on each replay. */
 int fb_sampler_set_call_index(fb_sampler *s, uint64_t call_index);
 
 /* ------------------------------------------------------------------------- */
@@ -100,21 +107,23 @@ int fb_sampler_set_call_index(fb_sampler *s, uint64_t call_index);
 /* q[n_dst, dim] (ldq elements per row; ldq == 0 broadcasts one row),
  * k/v rows of edge e at k + e*ldkv, v + e*ldkv, rptr[n_dst+1] CSR over
  * destinations.  Writes att[E, heads] (softmax before dropout) and
- * agg[n_dst, dim] (zero rows for destinations without edges).  dim % 4 == 0,
+ * agg[n_dst, dim] (zero rows for destinations without edges).  With
+ * n_dst_dev, the rows [*n_dst_dev, n_dst) of agg are written as zeros.  dim % 4 == 0,
  * dim <= 512, heads <= 4, dim % heads == 0.  drop_p == 0 disables dropout;
- * otherwise the keep mask is Philox(seed, offset, edge, head). */
+ * otherwise the keep mask is Philox(seed, offset, edge, head), with the
+ * offset read from offset_dev when that is not NULL (for graph replays). */
 int fb_attn_fwd(const float *q, int64_t ldq, const float *k, const float *v, int64_t ldkv,
                 const int32_t *rptr, int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim,
-                float slope, float drop_p, uint64_t seed, uint64_t offset, float *att, float *agg,
-                int64_t ldagg, cudaStream_t stream);
+                float slope, float drop_p, uint64_t seed, uint64_t offset, const uint64_t *offset_dev,
+                float *att, float *agg, int64_t ldagg, cudaStream_t stream);
 /* Backward of fb_attn_fwd (efficientGOP.py:80-95,115-131, but with the true
  * gradient).  Writes dq[n_dst, dim] (ld = dim; the segment sum of the
  * per-edge gradient), dk, dv (rows at e*lddkv).  Any of dq/dk/dv may be NULL. */
 int fb_attn_bwd(const float *q, int64_t ldq, const float *k, const float *v, int64_t ldkv,
                 const int32_t *rptr, int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim,
-                float slope, float drop_p, uint64_t seed, uint64_t offset, const float *att,
-                const float *dagg, int64_t lddagg, float *dq, float *dk, float *dv, int64_t lddkv,
-                cudaStream_t stream);
+                float slope, float drop_p, uint64_t seed, uint64_t offset, const uint64_t *offset_dev,
+                const float *att, const float *dagg, int64_t lddagg, float *dq, float *dk, float *dv,
+                int64_t lddkv, cudaStream_t stream);
 
 /* The dropout multipliers (0 or 1/(1-p)) fb_attn_fwd/bwd apply to edge e,
  * head h for (seed, offset): out[e*heads + h].  For checking and replay. */
@@ -179,8 +188,10 @@ int fb_exclusive_sum(const int32_t *in, int64_t n, int32_t *out, void *ws, cudaS
  *   A[r, 0:dn)          = h[(h_idx ? h_idx[r] : r + h_off), :]
  *   A[r, dn:dn+de)      = f[(f_idx ? f_idx[r] : r), :]
  *   A[r, dn+de:+dtime)  = cos(w * dt[r] + b)          (dt == NULL -> dt = 0)
- * Any block with dn/de/dtime == 0 is skipped. */
-int fb_gather_time_encode(const float *h, int64_t ldh, const int32_t *h_idx, int64_t h_off, int dn,
+ * Any block with dn/de/dtime == 0 is skipped.  h_off_dev (may be NULL) adds a
+ * device-resident row offset to h_off. */
+int fb_gather_time_encode(const float *h, int64_t ldh, const int32_t *h_idx, int64_t h_off,
+                          const int32_t *h_off_dev, int dn,
                           const float *f, int64_t ldf, const int32_t *f_idx, int de,
                           const float *dt, const float *w, const float *b, int dtime,
                           float *A, int64_t lda, int64_t n_rows, const int32_t *n_rows_dev,

@@ -24,9 +24,23 @@ def edge_softmax(x, row, n_dst):
     H = x.shape[1]
     idx = row.long().unsqueeze(1).expand(-1, H)
     mx = torch.full((n_dst, H), -float("inf"), dtype=x.dtype).scatter_reduce(0, idx, x, "amax", include_self=True)
-    ex = torch.exp(x - mx[row.long()])
+    ex = torch.exp(x - mx[row.long()].detach())
     s = torch.zeros((n_dst, H), dtype=x.dtype).index_add_(0, row.long(), ex)
     return ex / s[row.long()]
+
+
+def time_encode(te, dt):
+    """TimeEncode.forward (layers.py:17-29): cos(Linear(1, d)(dt)).  The
+    argument is the fp32 value w*dt + b rounded once, which is what torch's
+    fp32 Linear(1, d) produces on the CPU; in a wider dtype the argument keeps
+    that fp32 value (gradients flow in the wide dtype), so an fp64 run computes
+    the same function as the fp32 one."""
+    w, b = te.w.weight, te.w.bias
+    if w.dtype == torch.float32:
+        return torch.cos(te.w(dt.reshape(-1, 1).float()))
+    y = dt.reshape(-1, 1).to(w.dtype) * w.reshape(1, -1) + b
+    y32 = torch.nn.functional.linear(dt.reshape(-1, 1).float(), w.detach().float(), b.detach().float())
+    return torch.cos(y + (y32.to(w.dtype) - y).detach())
 
 
 def copy_u_sum(v_src, col, row, n_dst):
@@ -35,20 +49,25 @@ def copy_u_sum(v_src, col, row, n_dst):
     return out.index_add_(0, row.long(), v_src[col.long()])
 
 
+def _dtype(layer):
+    return layer.w_k.weight.dtype
+
+
 def layer_forward(layer, row, col, dt, n_dst, h=None, f=None, att_mask=None):
     """One TransfomerAttentionLayer (layers.py:98-240, DGL path).
     h: srcdata['h'] [n_src, dn] or None; f: edata['f'] [E, de] or None;
     dt: edata['dt'] [E]; att_mask: optional dropout multipliers [E, H]."""
     E = row.shape[0]
+    dty = _dtype(layer)
     if E == 0:
-        return torch.zeros((n_dst, layer.dim_out))
+        return torch.zeros((n_dst, layer.dim_out), dtype=dty)
     if layer.dim_time > 0:
-        time_feat = layer.time_enc(dt)
-        zero_time_feat = layer.time_enc(torch.zeros(n_dst, dtype=torch.float32))
+        time_feat = time_encode(layer.time_enc, dt)
+        zero_time_feat = time_encode(layer.time_enc, torch.zeros(n_dst, dtype=torch.float32))
     dn, de, dtm = layer.dim_node_feat, layer.dim_edge_feat, layer.dim_time
     rl = row.long()
     if dtm == 0 and dn == 0:
-        Q = torch.ones((E, layer.dim_out))
+        Q = torch.ones((E, layer.dim_out), dtype=dty)
         K = layer.w_k(f)
         V = layer.w_v(f)
     elif dtm == 0 and de == 0:
@@ -80,7 +99,7 @@ def layer_forward(layer, row, col, dt, n_dst, h=None, f=None, att_mask=None):
     if att_mask is not None:
         att = att * att_mask
     V = torch.reshape(V * att[:, :, None], (E, -1))
-    v_src = torch.cat([torch.zeros((n_dst, V.shape[1])), V], dim=0)
+    v_src = torch.cat([torch.zeros((n_dst, V.shape[1]), dtype=dty), V], dim=0)
     agg = copy_u_sum(v_src, col, row, n_dst)
     if dn != 0:
         rst = torch.cat([agg, h[:n_dst]], dim=1)
@@ -106,9 +125,9 @@ def model_forward(model, blocks, node_feats=None, edge_feats=None, neg_samples=1
         dt = torch.from_numpy(b.dts())[n_dst:]
         f = None
         if edge_feats is not None and layer.dim_edge_feat > 0:
-            f = edge_feats[torch.from_numpy(b.eid()).long()]
+            f = edge_feats[torch.from_numpy(b.eid()).long()].to(_dtype(layer))
         if l == 0:
-            hin = node_feats[torch.from_numpy(b.nodes()).long()] if node_feats is not None else None
+            hin = node_feats[torch.from_numpy(b.nodes()).long()].to(_dtype(layer)) if node_feats is not None else None
         else:
             hin = h
         h = layer_forward(layer, row, col, dt, n_dst, h=hin, f=f)

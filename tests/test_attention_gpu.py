@@ -24,6 +24,21 @@ def _segments(rng, n_dst, max_deg, big=()):
     return rptr, row
 
 
+def _avoid_kinks(q, k, row, heads, margin=1e-3):
+    """Re-draws K rows whose q.k logit lies within `margin` of 0 for some head:
+    at the LeakyReLU kink two correct fp32 evaluations can land on different
+    sides and change the derivative by the slope factor."""
+    g = torch.Generator().manual_seed(99)
+    for _ in range(20):
+        qe = (q.expand(int(row.max()) + 1, -1) if q.shape[0] == 1 else q)[torch.from_numpy(row)]
+        z = (qe.double().view(len(row), heads, -1) * k.double().view(len(row), heads, -1)).sum(-1)
+        bad = (z.abs() < margin).any(1)
+        if not bool(bad.any()):
+            return
+        k[bad] = torch.randn(int(bad.sum()), k.shape[1], generator=g) * 0.5
+    raise RuntimeError("could not move logits off the kink")
+
+
 def _reference(q, k, v, row, n_dst, heads, slope, scale=None, per_edge_q=False):
     E, D = k.shape
     qe = q if per_edge_q else (q.expand(n_dst, -1) if q.shape[0] == 1 else q)[row]
@@ -49,6 +64,7 @@ def test_attention_fwd_bwd(cuda, heads, dim, drop_p):
     kv = torch.randn(E, 2 * dim) * 0.5
     dagg = torch.randn(n_dst, dim)
     k, v = kv[:, :dim], kv[:, dim:]
+    _avoid_kinks(q, k, row, heads)
     scale = None
     if drop_p > 0:
         sc = torch.empty(E, heads, device=cuda)
@@ -83,9 +99,10 @@ def test_attention_broadcast_q(cuda):
     n_dst, dim, heads = 300, 100, 2
     rptr, row = _segments(rng, n_dst, 10)
     E = int(rptr[-1])
-    q = torch.randn(1, dim)
-    kv = torch.randn(E, 2 * dim)
+    q = torch.randn(1, dim) * 0.5
+    kv = torch.randn(E, 2 * dim) * 0.5
     dagg = torch.randn(n_dst, dim)
+    _avoid_kinks(q, kv[:, :dim], row, heads)
     qr = q.clone().requires_grad_(True)
     kr, vr = kv[:, :dim].clone().requires_grad_(True), kv[:, dim:].clone().requires_grad_(True)
     agg_r, _ = _reference(qr, kr, vr, row, n_dst, heads, 0.2)
@@ -109,6 +126,7 @@ def test_fastagg_fused_attn_logits(cuda):
     cnt = np.concatenate([[0], np.cumsum(np.diff(rptr_all)[nonempty])]).astype(np.int32)
     E = int(cnt[-1])
     x = torch.randn(E, heads)
+    x[x.abs() < 1e-3] = 0.5          # keep logits off the LeakyReLU kink
     V = torch.randn(E, heads, dh)
     xr = x.clone().requires_grad_(True)
     Vr = V.clone().requires_grad_(True)

@@ -1,12 +1,18 @@
 """GPU: a whole training step (sample -> gather/time-encode -> Q/K/V ->
 softmax/aggregate -> w_out/LayerNorm -> edge predictor -> BCE -> backward)
 on the device path against the CPU oracle (reference sampler restatement +
-fp32 restatement of layers.py/modules.py) with identical parameters.
-Dropout is off so the two paths compute the same function.
+restatement of layers.py/modules.py) with identical parameters.  Dropout is
+off so both paths compute the same function.
 
-Tolerance: rtol 1e-5 / atol 1e-6 on predictions, loss and every parameter
-gradient, except the time-encoding frequency gradient, a sum of E terms
-each scaled by dt, which is held to the fp32 summation bound of that sum.
+Criterion, per output tensor T (predictions, loss, every parameter gradient),
+with T64 the fp64 run of the oracle and T32 its fp32 run (the reference's own
+arithmetic):
+  * elementwise |T_dev - T64| <= 1e-6 + 1e-5 |T64|, or
+  * ||T_dev - T64||_2 <= 2 ||T32 - T64||_2 + 1e-6 sqrt(n)
+The second form covers gradients that are long sums with cancellation (the
+time-encoding frequencies sum E terms scaled by dt): there fp32 itself, the
+reference's included, is only as good as eps * sum|terms|, and the device
+result must be as accurate as the reference's fp32 result.
 """
 import copy
 
@@ -30,7 +36,19 @@ CASES = {
 
 
 def _grads(model):
-    return {n: (p.grad.detach().cpu().clone() if p.grad is not None else None) for n, p in model.named_parameters()}
+    return {n: (p.grad.detach().cpu().double().clone() if p.grad is not None else None)
+            for n, p in model.named_parameters()}
+
+
+def _check(name, dev, r64, r32, report):
+    dev, r64, r32 = dev.double(), r64.double(), r32.double()
+    err = (dev - r64).abs()
+    elem_ok = bool((err <= ATOL + RTOL * r64.abs()).all())
+    e_dev = float(err.norm())
+    e_ref = float((r32 - r64).norm())
+    norm_ok = e_dev <= 2 * e_ref + ATOL * err.numel() ** 0.5
+    report[name] = (round(e_dev, 9), round(e_ref, 9), "elem" if elem_ok else ("norm" if norm_ok else "FAIL"))
+    return elem_ok or norm_ok
 
 
 @pytest.mark.parametrize("case", sorted(CASES))
@@ -46,8 +64,9 @@ def test_train_step_matches_oracle(cuda, case):
     sp = dict(layer=layers, neighbor=fanout, strategy="recent", prop_time=False, history=1, duration=0)
     gnn = dict(arch="transformer_attention", layer=layers, att_head=2, dim_time=100, dim_out=100)
     tr = dict(lr=1e-4, dropout=0.0, att_dropout=0.0)
-    m_cpu = GeneralModel(dn, de, sp, dict(type="none", dim_out=0), gnn, tr)
-    m_gpu = copy.deepcopy(m_cpu).to(cuda)
+    m32 = GeneralModel(dn, de, sp, dict(type="none", dim_out=0), gnn, tr)
+    m64 = copy.deepcopy(m32).double()
+    m_gpu = copy.deepcopy(m32).to(cuda)
     crit = torch.nn.BCEWithLogitsLoss()
     dev = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
     smp = sampler_core.ParallelSampler(dev(g["indptr"]), dev(g["indices"]), dev(g["eid"]), dev(g["ts"]), 1, 1,
@@ -57,7 +76,7 @@ def test_train_step_matches_oracle(cuda, case):
     ef_d = ef.to(cuda) if ef is not None else None
     rng = np.random.default_rng(0)
     B = 200
-    worst = {}
+    failures = []
     for bt, b0 in enumerate(range(5000, 5000 + 3 * B, B)):
         src, dst, t = g["src"][b0:b0 + B], g["dst"][b0:b0 + B], g["t"][b0:b0 + B]
         roots = np.concatenate([src, dst, rng.integers(0, n_nodes, B).astype(np.int32)])
@@ -69,31 +88,32 @@ def test_train_step_matches_oracle(cuda, case):
         pp, pn = m_gpu(blocks, nf_d, ef_d)
         loss_g = crit(pp, torch.ones_like(pp)) + crit(pn, torch.zeros_like(pn))
         loss_g.backward()
-        m_cpu.zero_grad()
-        rp, rn = ref_math.model_forward(m_cpu, ora.get_ret(), nf, ef)
-        loss_c = ref_math.bce_loss(rp, rn)
-        loss_c.backward()
-        torch.testing.assert_close(pp.detach().cpu(), rp.detach(), rtol=RTOL, atol=ATOL)
-        torch.testing.assert_close(pn.detach().cpu(), rn.detach(), rtol=RTOL, atol=ATOL)
-        torch.testing.assert_close(loss_g.detach().cpu(), loss_c.detach(), rtol=RTOL, atol=ATOL)
-        gg, gc = _grads(m_gpu), _grads(m_cpu)
-        for name in gc:
-            a, b = gg[name], gc[name]
-            if b is None:
-                assert a is None or torch.count_nonzero(a) == 0, name
+        outs = {}
+        for tag, m in (("32", m32), ("64", m64)):
+            m.zero_grad()
+            rp, rn = ref_math.model_forward(m, ora.get_ret(), nf, ef)
+            loss = ref_math.bce_loss(rp, rn)
+            loss.backward()
+            outs[tag] = (rp.detach(), rn.detach(), loss.detach(), _grads(m))
+        report = {}
+        ok = _check("pred_pos", pp.detach().cpu(), outs["64"][0], outs["32"][0], report)
+        ok &= _check("pred_neg", pn.detach().cpu(), outs["64"][1], outs["32"][1], report)
+        ok &= _check("loss", loss_g.detach().cpu(), outs["64"][2], outs["32"][2], report)
+        # predictions and loss must meet the elementwise bound outright
+        ok &= all(report[k][2] == "elem" for k in ("pred_pos", "pred_neg", "loss"))
+        gg = _grads(m_gpu)
+        for name, b64 in outs["64"][3].items():
+            if b64 is None:
                 continue
-            err = (a - b).abs()
-            worst[name] = max(worst.get(name, 0.0), float((err / (ATOL + RTOL * b.abs())).max()))
-            if name.endswith("time_enc.w.weight"):
-                # sum over edges of -sin(w dt + b) * dt * g: fp32 summation bound
-                bound = b.abs() * 0 + float(b.abs().max()) * 1e-4 + ATOL
-                assert bool((err <= bound + RTOL * b.abs()).all()), (name, float(err.max()))
-            else:
-                torch.testing.assert_close(a, b, rtol=RTOL, atol=ATOL, msg=lambda m: "%s: %s" % (name, m))
+            ok &= _check(name, gg[name], b64, outs["32"][3][name], report)
+        if not ok:
+            failures.append((bt, {k: v for k, v in report.items() if v[2] != "elem"}))
         with torch.no_grad():
-            for p in m_cpu.parameters():
+            for p in m32.parameters():
                 p.add_(torch.randn_like(p) * 1e-3)
-            for pc, pg in zip(m_cpu.parameters(), m_gpu.parameters()):
-                pg.copy_(pc)
-    print("worst err/tol ratio per parameter (%s):" % case,
-          {k: round(v, 3) for k, v in sorted(worst.items(), key=lambda kv: -kv[1])[:6]})
+            for p32, p64, pg in zip(m32.parameters(), m64.parameters(), m_gpu.parameters()):
+                p64.copy_(p32)
+                pg.copy_(p32)
+        print("batch", bt, "tensors passing only the norm form:",
+              {k: v[:2] for k, v in report.items() if v[2] == "norm"})
+    assert not failures, failures
