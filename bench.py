@@ -285,16 +285,15 @@ def run_fast(args):
         dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
     e2e_value = args.steps * gB / float(e2e_s.item())
 
-    # per-kernel device times for the roofline: the same kernels launched one
-    # by one (outside the graph) with CUDA events around each
+    # per-kernel device times for the roofline: the kernels launched one by one
+    # (outside the graph) with CUDA events around each,
+    # at the blocks' true sizes (host-read dims), so bytes and flops are the
+    # algorithmic ones of each launch
     ops.TIMER = ops.KernelTimer()
     for _ in range(args.profile_steps):
-        if args.eager:
-            dev_step()
-        else:
-            b0, b1 = next_range()
-            tr.load_device_roots(b0, b1)
-            tr._eager_step()
+        b0, b1 = next_range()
+        roots, rts = tr.device_roots(b0, b1)
+        Trainer.step_device(tr, roots, rts)
     kern = ops.TIMER.summary()
     ops.TIMER = None
 

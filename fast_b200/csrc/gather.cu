@@ -64,14 +64,15 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode(GatherA
 __global__ void __launch_bounds__(256) k_te_bwd_part(const float *__restrict__ g, int64_t ldg,
                                                      const float *__restrict__ dt, const float *__restrict__ w,
                                                      const float *__restrict__ b, int dtime, int64_t n_rows,
-                                                     const int32_t *n_rows_dev, int64_t rows_per_cta,
+                                                     const int32_t *n_rows_dev, int64_t unused_rows,
                                                      float *__restrict__ part) {
   __shared__ float sw_s[8][32], sb_s[8][32];
-  const int64_t n = n_rows_dev ? (int64_t)(*n_rows_dev) : n_rows;
+  const int64_t n = n_rows_dev ? min((int64_t)(*n_rows_dev), n_rows) : n_rows;
   const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + lane;
-  const int64_t r0 = (int64_t)blockIdx.y * rows_per_cta;
-  const int64_t r1 = min(n, r0 + rows_per_cta);
+  const int64_t per = (n + gridDim.y - 1) / gridDim.y;   // true rows spread over every chunk
+  const int64_t r0 = (int64_t)blockIdx.y * per;
+  const int64_t r1 = min(n, r0 + per);
   float sw = 0.f, sb = 0.f;
   if (c < dtime) {
     const float wc = __ldg(w + c), bc = __ldg(b + c);
@@ -108,7 +109,11 @@ __global__ void k_te_bwd_reduce(const float *__restrict__ part, int nparts, int 
 }
 
 constexpr int64_t kTeRowsPerCta = 128;
-constexpr int kTeMaxParts = 2048;
+constexpr int64_t kTeMaxParts = 1024;
+
+inline int te_parts(int64_t n) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>((n + kTeRowsPerCta - 1) / kTeRowsPerCta, kTeMaxParts));
+}
 
 inline bool a16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -135,8 +140,7 @@ extern "C" int fb_gather_time_encode(const float *h, int64_t ldh, const int32_t 
 }
 
 extern "C" size_t fb_time_encode_bwd_ws_bytes(int64_t n_rows, int dtime) {
-  int64_t rows = std::max<int64_t>(kTeRowsPerCta, (n_rows + kTeMaxParts - 1) / kTeMaxParts);
-  int64_t parts = std::max<int64_t>(1, (n_rows + rows - 1) / rows);
+  const int64_t parts = te_parts(n_rows);
   return (size_t)(parts * 2 * std::max(dtime, 1)) * sizeof(float);
 }
 
@@ -145,8 +149,8 @@ extern "C" int fb_time_encode_bwd(const float *g, int64_t ldg, const float *dt, 
                                   void *ws, cudaStream_t stream) {
   if (!g || !dt || !w || !b || !dw || !db || !ws || dtime < 1 || n_rows < 0)
     return fb::set_error(FB_ERR_ARG, "time_encode_bwd: bad argument");
-  int64_t rows = std::max<int64_t>(kTeRowsPerCta, (n_rows + kTeMaxParts - 1) / kTeMaxParts);
-  int parts = (int)std::max<int64_t>(1, (n_rows + rows - 1) / rows);
+  const int parts = te_parts(n_rows);
+  const int64_t rows = 0;   // chunk sizes are derived on the device from the true row count
   float *part = static_cast<float *>(ws);
   dim3 grid((dtime + 31) / 32, parts);
   k_te_bwd_part<<<grid, 256, 0, stream>>>(g, ldg, dt, w, b, dtime, n_rows, n_rows_dev, rows, part);

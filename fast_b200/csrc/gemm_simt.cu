@@ -48,11 +48,10 @@ __global__ void __launch_bounds__(NT) k_gemm_nt(const float *__restrict__ A, int
                                                 int accumulate, bool vecA, bool vecB) {
   __shared__ __align__(16) float As[2][BK][BM + PAD];
   __shared__ __align__(16) float Bs[2][BK][BN + PAD];
-  const int64_t M = M_dev ? (int64_t)(*M_dev) : M_host;
-  const int64_t m0 = (int64_t)blockIdx.y * BM;
+  const int64_t M = M_dev ? min((int64_t)(*M_dev), M_host) : M_host;
   const int n0 = blockIdx.x * BN;
-  if (m0 >= M) return;
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  for (int64_t m0 = (int64_t)blockIdx.y * BM; m0 < M; m0 += (int64_t)gridDim.y * BM) {
   float acc[8][4] = {};
   // loader coordinates: A 128x16 = 512 float4 (2 per thread), B 64x16 = 256 float4
   const int ar0 = tid >> 2, ac = (tid & 3) * 4;  // rows ar0 and ar0 + 64
@@ -97,6 +96,8 @@ __global__ void __launch_bounds__(NT) k_gemm_nt(const float *__restrict__ A, int
       }
     }
   }
+  __syncthreads();
+  }
 }
 
 // P[split][N][K] = sum_{m in split} G[m,n] X[m,k]
@@ -106,10 +107,12 @@ __global__ void __launch_bounds__(NT) k_gemm_tn(const float *__restrict__ G, int
                                                 bool vecG, bool vecX) {
   __shared__ __align__(16) float Gs[2][BK][BM + PAD];
   __shared__ __align__(16) float Xs[2][BK][BN + PAD];
-  const int64_t M = M_dev ? (int64_t)(*M_dev) : M_host;
+  const int64_t M = M_dev ? min((int64_t)(*M_dev), M_host) : M_host;
   const int n0 = blockIdx.y * BM, k0 = blockIdx.x * BN;
-  const int64_t s0 = (int64_t)blockIdx.z * rows_per_split;
-  const int64_t s1 = min(M, s0 + rows_per_split);
+  // the true row count is spread over all gridDim.z splits
+  const int64_t per = ((M + gridDim.z - 1) / gridDim.z + BK - 1) / BK * BK;
+  const int64_t s0 = (int64_t)blockIdx.z * per;
+  const int64_t s1 = min(M, s0 + per);
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   float acc[8][4] = {};
   // loader: G slice 16 x 128 (2 float4 per thread), X slice 16 x 64 (1 float4)
@@ -169,10 +172,11 @@ __global__ void __launch_bounds__(256) k_colsum_part(const float *__restrict__ G
                                                      const int32_t *M_dev, int N, int64_t rows_per_part,
                                                      float *__restrict__ part) {
   __shared__ float s_acc[8][32];
-  const int64_t M = M_dev ? (int64_t)(*M_dev) : M_host;
+  const int64_t M = M_dev ? min((int64_t)(*M_dev), M_host) : M_host;
   const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + lane;
-  const int64_t r0 = (int64_t)blockIdx.y * rows_per_part, r1 = min(M, r0 + rows_per_part);
+  const int64_t per = (M + gridDim.y - 1) / gridDim.y;
+  const int64_t r0 = (int64_t)blockIdx.y * per, r1 = min(M, r0 + per);
   float s = 0.f;
   if (c < N)
     for (int64_t r = r0 + wp; r < r1; r += 8) s += G[r * ldg + c];
@@ -207,6 +211,11 @@ inline int64_t tn_rows_per_split(int64_t M, int N, int K) {
 }
 
 constexpr int64_t kColsumRows = 256;
+constexpr int64_t kColsumMaxParts = 1024;
+
+inline int colsum_parts(int64_t M) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>((M + kColsumRows - 1) / kColsumRows, kColsumMaxParts));
+}
 
 }  // namespace
 
@@ -217,8 +226,8 @@ extern "C" int fb_gemm_nt(const float *A, int64_t lda, const float *B, int64_t l
     return fb::set_error(FB_ERR_ARG, "gemm_nt: bad argument");
   if (M == 0) return FB_OK;
   const bool vecA = (lda % 4 == 0) && al16(A), vecB = (ldb % 4 == 0) && al16(B);
-  dim3 grid((N + BN - 1) / BN, (unsigned)((M + BM - 1) / BM));
-  if (grid.y > 65535u) return fb::set_error(FB_ERR_UNSUPPORTED, "gemm_nt: M too large for one launch");
+  const int64_t mt = (M + BM - 1) / BM;
+  dim3 grid((N + BN - 1) / BN, (unsigned)std::min<int64_t>(mt, 148 * 4));
   k_gemm_nt<<<grid, NT, 0, stream>>>(A, lda, B, ldb, bias, C, ldc, M, M_dev, N, K, accumulate, vecA, vecB);
   FB_LAUNCHED("k_gemm_nt");
   return FB_OK;
@@ -249,14 +258,14 @@ extern "C" int fb_gemm_tn(const float *G, int64_t ldg, const float *X, int64_t l
 }
 
 extern "C" size_t fb_colsum_ws_bytes(int64_t M, int N) {
-  const int64_t parts = std::max<int64_t>(1, (M + kColsumRows - 1) / kColsumRows);
+  const int64_t parts = colsum_parts(M);
   return (size_t)(parts * std::max(N, 1)) * sizeof(float);
 }
 
 extern "C" int fb_colsum(const float *G, int64_t ldg, float *db, int64_t M, const int32_t *M_dev, int N,
                          int accumulate, void *ws, cudaStream_t stream) {
   if (!G || !db || !ws || M < 0 || N < 1 || ldg < N) return fb::set_error(FB_ERR_ARG, "colsum: bad argument");
-  const int parts = (int)std::max<int64_t>(1, (M + kColsumRows - 1) / kColsumRows);
+  const int parts = colsum_parts(M);
   float *part = static_cast<float *>(ws);
   dim3 grid((N + 31) / 32, parts);
   k_colsum_part<<<grid, 256, 0, stream>>>(G, ldg, M, M_dev, N, kColsumRows, part);

@@ -40,6 +40,7 @@ class KernelTimer:
 
 
 TIMER = None            # set to a KernelTimer to time every kernel wrapper
+USE_TC = False          # route eligible gemm_nt calls to the tcgen05 kernel
 LAUNCHES = [0]          # kernels launched through these wrappers
 
 
@@ -70,10 +71,33 @@ def gemm_nt(A, B, bias=None, out=None, accumulate=False, M_dev=None):
         raise ValueError("gemm_nt: inner dimensions differ")
     if out is None:
         out = torch.empty(M, N, device=A.device, dtype=torch.float32)
+    if USE_TC and M >= 256 and lib.fb_gemm_nt_tc_supported(ptr(A), A.stride(0), ptr(B), B.stride(0), N, K):
+        return gemm_nt_tc(A, B, bias, out, accumulate, M_dev)
     with _timed("gemm_nt", 4 * (M * K + N * K + M * N), 2 * M * N * K):
         call("fb_gemm_nt", ptr(A), A.stride(0), ptr(B), B.stride(0), ptr(bias), ptr(out), out.stride(0), M,
              _p(M_dev), N, K, int(accumulate), stream_ptr())
     return out
+
+
+def gemm_nt_tc(A, B, bias=None, out=None, accumulate=False, M_dev=None):
+    """gemm_nt on the tcgen05 tensor cores (3xTF32 split, fp32 accuracy)."""
+    _f32_rows(A, "A")
+    _f32_rows(B, "B")
+    M, K = A.shape
+    N = B.shape[0]
+    if out is None:
+        out = torch.empty(M, N, device=A.device, dtype=torch.float32)
+    with _timed("gemm_nt_tc", 4 * (M * K + N * K + M * N), 2 * M * N * K):
+        call("fb_gemm_nt_tc", ptr(A), A.stride(0), ptr(B), B.stride(0), ptr(bias), ptr(out), out.stride(0), M,
+             _p(M_dev), N, K, int(accumulate), stream_ptr())
+    return out
+
+
+def tc_error(clear=True):
+    import ctypes
+    f = ctypes.c_int(0)
+    call("fb_gemm_tc_error", ctypes.byref(f), int(clear))
+    return f.value
 
 
 def gemm_tn(G, X, out=None, accumulate=False, M_dev=None):

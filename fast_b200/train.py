@@ -143,13 +143,16 @@ class GraphTrainer(Trainer):
     all-reduce of the flat gradient bucket."""
 
     def __init__(self, graph, node_feats, edge_feats, sample_param, memory_param, gnn_param, train_param,
-                 device, batch, rank=0, world=1, seed=42, sampler_seed=1234):
+                 device, batch, rank=0, world=1, seed=42, sampler_seed=1234, optimizer="adam"):
         super().__init__(graph, node_feats, edge_feats, sample_param, memory_param, gnn_param, train_param,
                          device, rank=rank, world=world, seed=seed, sampler_seed=sampler_seed)
         self.B = batch
         self.R0 = 3 * batch
         dv = self.device
-        self.opt = torch.optim.Adam(self.model.parameters(), lr=train_param["lr"], capturable=True)
+        if optimizer == "adam":
+            self.opt = torch.optim.Adam(self.model.parameters(), lr=train_param["lr"], capturable=True)
+        else:
+            self.opt = torch.optim.SGD(self.model.parameters(), lr=train_param["lr"])
         self.roots_buf = torch.zeros(self.R0, dtype=torch.int32, device=dv)
         self.ts_buf = torch.zeros(self.R0, dtype=torch.float32, device=dv)
         self.loss_buf = torch.zeros((), device=dv)

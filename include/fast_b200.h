@@ -212,6 +212,18 @@ int fb_time_encode_bwd(const float *g, int64_t ldg, const float *dt, const float
 int fb_gemm_nt(const float *A, int64_t lda, const float *B, int64_t ldb, const float *bias,
                float *C, int64_t ldc, int64_t M, const int32_t *M_dev, int N, int K,
                int accumulate, cudaStream_t stream);
+/* Same contract as fb_gemm_nt on the tcgen05 tensor cores: TMA-fed 128 x N
+ * tiles, fp32 accuracy from three TF32 products per term (Ootomo & Yokota's
+ * hi/lo split, computed in shared memory), accumulation in tensor memory.
+ * Needs N <= 256, K, lda, ldb multiples of 4, A and B 16-byte aligned
+ * (fb_gemm_nt_tc_supported). */
+int fb_gemm_nt_tc_supported(const float *A, int64_t lda, const float *B, int64_t ldb, int N, int K);
+int fb_gemm_nt_tc(const float *A, int64_t lda, const float *B, int64_t ldb, const float *bias, float *C,
+                  int64_t ldc, int64_t M, const int32_t *M_dev, int N, int K, int accumulate,
+                  cudaStream_t stream);
+/* Sticky error bits of the tensor-core kernels on the current device (2 = a
+ * bounded wait timed out and the CTA gave up); synchronises; clear resets. */
+int fb_gemm_tc_error(int *flags, int clear);
 /* C[n, k] = sum_m G[m, n] X[m, k]  (+ C when accumulate)              "TN"
  * the weight gradient of a Linear layer; deterministic split over M.
  * `ws` must hold fb_gemm_tn_ws_bytes(M, N, K) bytes. */

@@ -42,3 +42,26 @@ def small_graph(n_nodes=60, n_edges=4000, seed=0, t_max=1000, int_ts=True, empty
     indptr = np.cumsum(indptr).astype(np.int32)
     return dict(indptr=indptr, indices=dst[order].astype(np.int32), eid=order.astype(np.int32), ts=t[order],
                 src=src, dst=dst, t=t)
+
+
+RTOL, ATOL = 1e-5, 1e-6
+
+
+def parity(dev, ref64, ref32, name="", rtol=RTOL, atol=ATOL):
+    """Device result vs the fp64 restatement T64 and the fp32 one T32 (the
+    reference's own arithmetic).  Passes when, elementwise,
+    |dev - T64| <= atol + rtol |T64|, or when the device result is as
+    accurate as the fp32 reference: ||dev - T64|| <= 2 ||T32 - T64|| + atol sqrt(n).
+    Returns the form that passed ("elem" / "norm"); raises otherwise."""
+    import torch
+    dev, ref64, ref32 = (t.detach().cpu().double() for t in (dev, ref64, ref32))
+    err = (dev - ref64).abs()
+    if bool((err <= atol + rtol * ref64.abs()).all()):
+        return "elem"
+    e_dev, e_ref = float(err.norm()), float((ref32 - ref64).norm())
+    if e_dev <= 2 * e_ref + atol * err.numel() ** 0.5:
+        return "norm"
+    worst = int(torch.argmax(err / (atol + rtol * ref64.abs())))
+    raise AssertionError("%s: device error %.3e (norm) vs fp32 reference %.3e; worst element %d: dev %.9g ref %.9g"
+                         % (name, e_dev, e_ref, worst, float(dev.reshape(-1)[worst]),
+                            float(ref64.reshape(-1)[worst])))
