@@ -44,6 +44,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=5)
     ap.add_argument("--eager", action="store_true", help="launch kernels step by step instead of a CUDA graph")
+    ap.add_argument("--gemm", default="simt", choices=["simt", "tc"],
+                    help="projection GEMMs on the CUDA cores (simt) or the tcgen05 tensor cores (tc)")
     return ap.parse_args()
 
 
@@ -202,6 +204,7 @@ def run_fast(args):
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     from fast_b200 import ops
     from fast_b200.data import CONFIGS, make_features, make_graph, model_params
+    ops.USE_TC = args.gemm == "tc"
     from fast_b200.train import GraphTrainer, Trainer
     cfg = CONFIGS[args.config]
     graph = make_graph(cfg)
@@ -331,6 +334,7 @@ def run_fast(args):
         "config": {"workload": cfg.name, "global_batch": gB, "local_batch": B, "fanout": list(cfg.fanout),
                    "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge,
                    "parallelism": "dp%d" % world, "launch": "eager" if args.eager else "cuda_graph",
+                   "gemm": args.gemm,
                    "l2": "inputs larger than L2 (%.1f GB edge-feature table gathered at random rows)" %
                          (cfg.edges * cfg.d_edge * 4 / 1e9)},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": world * 3 * B * 8,
