@@ -292,7 +292,7 @@ def run_fast(args):
     # (outside the graph) with CUDA events around each,
     # at the blocks' true sizes (host-read dims), so bytes and flops are the
     # algorithmic ones of each launch
-    ops.TIMER = ops.KernelTimer()
+    ops.TIMER = ops.KernelTimer(reps=10)
     for _ in range(args.profile_steps):
         b0, b1 = next_range()
         roots, rts = tr.device_roots(b0, b1)

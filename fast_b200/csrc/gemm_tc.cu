@@ -5,8 +5,8 @@
 // fp32 accuracy from TF32 tensor-core products with the split of Ootomo &
 // Yokota ("Recovering single precision accuracy from Tensor Cores while
 // surpassing the FP32 theoretical peak performance", IJHPCA 2022): every
-// operand x is written as hi + lo with hi = x truncated to TF32 (low 13
-// mantissa bits cleared, exact) and lo = x - hi (exact in fp32), and
+// operand x is written as hi + lo with hi = x rounded to TF32 and lo = the
+// residual x - hi (exact in fp32) rounded to TF32, and
 //   A B ~= A_hi B_hi + A_hi B_lo + A_lo B_hi,
 // three kind::tf32 MMAs accumulating in fp32 in tensor memory.
 //
@@ -153,10 +153,18 @@ struct Cfg {
   static constexpr int kSmem = 1024 + kStages * kStage + 64 * 8 + 64;
 };
 
-__device__ __forceinline__ float4 tf32_hi(float4 v) {
-  const uint32_t m = 0xFFFFE000u;
-  return make_float4(__uint_as_float(__float_as_uint(v.x) & m), __uint_as_float(__float_as_uint(v.y) & m),
-                     __uint_as_float(__float_as_uint(v.z) & m), __uint_as_float(__float_as_uint(v.w) & m));
+// Round-to-nearest TF32 (low 13 mantissa bits cleared), as a float.
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// x = hi + lo with hi = rna_tf32(x) and lo = rna_tf32(x - hi): |x - hi - lo| <= 2^-24 |x|
+// up to rounding of the residual, so the two TF32 cross products recover fp32.
+__device__ __forceinline__ void split_tf32(const float4 v, float4 &h, float4 &l) {
+  h = make_float4(to_tf32(v.x), to_tf32(v.y), to_tf32(v.z), to_tf32(v.w));
+  l = make_float4(to_tf32(v.x - h.x), to_tf32(v.y - h.y), to_tf32(v.z - h.z), to_tf32(v.w - h.w));
 }
 
 template <int BN>
@@ -256,18 +264,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < BM * BK / 4 / 128; ++i) {
         const int idx = ct + 128 * i;
-        const float4 v = a4[idx], h = tf32_hi(v);
+        float4 h, l;
+        split_tf32(a4[idx], h, l);
         a4[idx] = h;
-        al4[idx] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+        al4[idx] = l;
       }
       float4 *b4 = reinterpret_cast<float4 *>(sB(s));
       float4 *bl4 = reinterpret_cast<float4 *>(sBlo(s));
 #pragma unroll
       for (int i = 0; i < BN * BK / 4 / 128; ++i) {
         const int idx = ct + 128 * i;
-        const float4 v = b4[idx], h = tf32_hi(v);
+        float4 h, l;
+        split_tf32(b4[idx], h, l);
         b4[idx] = h;
-        bl4[idx] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+        bl4[idx] = l;
       }
       fence_async_smem();
       mbar_arrive(conv + s);

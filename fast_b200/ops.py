@@ -13,27 +13,32 @@ from .capi import call, ptr, stream_ptr, lib
 
 
 class KernelTimer:
-    """Records CUDA events around every kernel wrapper on the current stream,
-    with the algorithmic bytes and flops of each launch (for the roofline)."""
+    """Times every kernel wrapper with CUDA events on the current stream.
+    Each wrapped launch is issued `reps` times back to back between one event
+    pair, so the host runs ahead of the device and the events bracket device
+    time, not launch gaps.  Records carry the algorithmic bytes and flops of
+    one launch (for the roofline).  Repeated launches of accumulating kernels
+    change their outputs: time only steps whose results are thrown away."""
 
-    def __init__(self):
+    def __init__(self, reps=10):
+        self.reps = reps
         self.records = []
 
-    @contextlib.contextmanager
-    def __call__(self, name, nbytes=0, flops=0):
+    def run(self, name, nbytes, flops, fn):
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        yield
+        for _ in range(self.reps):
+            fn()
         e.record()
-        self.records.append((name, s, e, nbytes, flops))
+        self.records.append((name, s, e, nbytes, flops, self.reps))
 
     def summary(self):
         torch.cuda.synchronize()
         out = {}
-        for name, s, e, nb, fl in self.records:
+        for name, s, e, nb, fl, reps in self.records:
             r = out.setdefault(name, dict(launches=0, ms=0.0, bytes=0, flops=0))
             r["launches"] += 1
-            r["ms"] += s.elapsed_time(e)
+            r["ms"] += s.elapsed_time(e) / reps
             r["bytes"] += nb
             r["flops"] += fl
         return out
@@ -44,11 +49,12 @@ USE_TC = False          # route eligible gemm_nt calls to the tcgen05 kernel
 LAUNCHES = [0]          # kernels launched through these wrappers
 
 
-def _timed(name, nbytes=0, flops=0, kernels=1):
+def _launch(name, nbytes, flops, kernels, fn):
     LAUNCHES[0] += kernels
     if TIMER is None:
-        return contextlib.nullcontext()
-    return TIMER(name, nbytes, flops)
+        fn()
+    else:
+        TIMER.run(name, nbytes, flops, fn)
 
 
 def _f32_rows(t, name):
@@ -73,9 +79,9 @@ def gemm_nt(A, B, bias=None, out=None, accumulate=False, M_dev=None):
         out = torch.empty(M, N, device=A.device, dtype=torch.float32)
     if USE_TC and M >= 256 and lib.fb_gemm_nt_tc_supported(ptr(A), A.stride(0), ptr(B), B.stride(0), N, K):
         return gemm_nt_tc(A, B, bias, out, accumulate, M_dev)
-    with _timed("gemm_nt", 4 * (M * K + N * K + M * N), 2 * M * N * K):
-        call("fb_gemm_nt", ptr(A), A.stride(0), ptr(B), B.stride(0), ptr(bias), ptr(out), out.stride(0), M,
-             _p(M_dev), N, K, int(accumulate), stream_ptr())
+    _launch("gemm_nt", 4 * (M * K + N * K + M * N), 2 * M * N * K, 1,
+            lambda: call("fb_gemm_nt", ptr(A), A.stride(0), ptr(B), B.stride(0), ptr(bias), ptr(out),
+                         out.stride(0), M, _p(M_dev), N, K, int(accumulate), stream_ptr()))
     return out
 
 
@@ -87,9 +93,9 @@ def gemm_nt_tc(A, B, bias=None, out=None, accumulate=False, M_dev=None):
     N = B.shape[0]
     if out is None:
         out = torch.empty(M, N, device=A.device, dtype=torch.float32)
-    with _timed("gemm_nt_tc", 4 * (M * K + N * K + M * N), 2 * M * N * K):
-        call("fb_gemm_nt_tc", ptr(A), A.stride(0), ptr(B), B.stride(0), ptr(bias), ptr(out), out.stride(0), M,
-             _p(M_dev), N, K, int(accumulate), stream_ptr())
+    _launch("gemm_nt_tc", 4 * (M * K + N * K + M * N), 2 * M * N * K, 1,
+            lambda: call("fb_gemm_nt_tc", ptr(A), A.stride(0), ptr(B), B.stride(0), ptr(bias), ptr(out),
+                         out.stride(0), M, _p(M_dev), N, K, int(accumulate), stream_ptr()))
     return out
 
 
@@ -109,9 +115,9 @@ def gemm_tn(G, X, out=None, accumulate=False, M_dev=None):
     if out is None:
         out = torch.empty(N, K, device=G.device, dtype=torch.float32)
     ws = torch.empty(int(lib.fb_gemm_tn_ws_bytes(M, N, K)), device=G.device, dtype=torch.uint8)
-    with _timed("gemm_tn", 4 * (M * N + M * K + N * K), 2 * M * N * K, kernels=2):
-        call("fb_gemm_tn", ptr(G), G.stride(0), ptr(X), X.stride(0), ptr(out), out.stride(0), M, _p(M_dev), N, K,
-             int(accumulate), ptr(ws), stream_ptr())
+    _launch("gemm_tn", 4 * (M * N + M * K + N * K), 2 * M * N * K, 2,
+            lambda: call("fb_gemm_tn", ptr(G), G.stride(0), ptr(X), X.stride(0), ptr(out), out.stride(0), M,
+                         _p(M_dev), N, K, int(accumulate), ptr(ws), stream_ptr()))
     return out
 
 
@@ -121,8 +127,9 @@ def colsum(G, out=None, accumulate=False, M_dev=None):
     if out is None:
         out = torch.empty(N, device=G.device, dtype=torch.float32)
     ws = torch.empty(int(lib.fb_colsum_ws_bytes(M, N)), device=G.device, dtype=torch.uint8)
-    with _timed("colsum", 4 * (M * N + N), M * N, kernels=2):
-        call("fb_colsum", ptr(G), G.stride(0), ptr(out), M, _p(M_dev), N, int(accumulate), ptr(ws), stream_ptr())
+    _launch("colsum", 4 * (M * N + N), M * N, 2,
+            lambda: call("fb_colsum", ptr(G), G.stride(0), ptr(out), M, _p(M_dev), N, int(accumulate), ptr(ws),
+                         stream_ptr()))
     return out
 
 
@@ -138,10 +145,11 @@ def gather_time_encode(n_rows, h=None, h_idx=None, h_off=0, f=None, f_idx=None, 
         out = torch.empty(n_rows, dn + de + dtime, device=dev, dtype=torch.float32)
     nbytes = 4 * n_rows * (2 * (dn + de) + dtime + (1 if dt is not None else 0)
                            + (1 if h_idx is not None else 0) + (1 if f_idx is not None else 0))
-    with _timed("gather_time_encode", nbytes):
-        call("fb_gather_time_encode", ptr(h), 0 if h is None else h.stride(0), ptr(h_idx), int(h_off),
-             _p(h_off_dev), dn, ptr(f), 0 if f is None else f.stride(0), ptr(f_idx), de, ptr(dt), ptr(w), ptr(b),
-             dtime, ptr(out), out.stride(0), n_rows, _p(n_rows_dev), stream_ptr())
+    _launch("gather_time_encode", nbytes, 0, 1,
+            lambda: call("fb_gather_time_encode", ptr(h), 0 if h is None else h.stride(0), ptr(h_idx),
+                         int(h_off), _p(h_off_dev), dn, ptr(f), 0 if f is None else f.stride(0), ptr(f_idx), de,
+                         ptr(dt), ptr(w), ptr(b), dtime, ptr(out), out.stride(0), n_rows, _p(n_rows_dev),
+                         stream_ptr()))
     return out
 
 
@@ -149,9 +157,9 @@ def time_encode_bwd(g, dt, w, b, dw, db, n_dev=None):
     """dw/db += gradient of cos(w*dt + b) given g = dL/dcos (rows at g.stride(0))."""
     n, dtime = g.shape
     ws = torch.empty(int(lib.fb_time_encode_bwd_ws_bytes(n, dtime)), device=g.device, dtype=torch.uint8)
-    with _timed("time_encode_bwd", 4 * n * (dtime + 1), kernels=2):
-        call("fb_time_encode_bwd", ptr(g), g.stride(0), ptr(dt), ptr(w), ptr(b), dtime, n, _p(n_dev), ptr(dw),
-             ptr(db), ptr(ws), stream_ptr())
+    _launch("time_encode_bwd", 4 * n * (dtime + 1), 0, 2,
+            lambda: call("fb_time_encode_bwd", ptr(g), g.stride(0), ptr(dt), ptr(w), ptr(b), dtime, n, _p(n_dev),
+                         ptr(dw), ptr(db), ptr(ws), stream_ptr()))
 
 
 def attn_fwd(q, k, v, rptr, heads, slope, drop_p=0.0, seed=0, offset=0, n_dst_dev=None, offset_dev=None):
@@ -164,9 +172,10 @@ def attn_fwd(q, k, v, rptr, heads, slope, drop_p=0.0, seed=0, offset=0, n_dst_de
     agg = torch.empty(nd, D, device=k.device, dtype=torch.float32)
     qrows = nd if ldq else 1
     nbytes = 4 * (qrows * D + 2 * E * D + (nd + 1) + nd * D + E * heads)
-    with _timed("attn_fwd", nbytes):
-        call("fb_attn_fwd", ptr(q), ldq, ptr(k), ptr(v), k.stride(0), ptr(rptr), nd, _p(n_dst_dev), heads, D, slope,
-             drop_p, seed, offset, _p(offset_dev), ptr(att), ptr(agg), agg.stride(0), stream_ptr())
+    _launch("attn_fwd", nbytes, 0, 1,
+            lambda: call("fb_attn_fwd", ptr(q), ldq, ptr(k), ptr(v), k.stride(0), ptr(rptr), nd, _p(n_dst_dev),
+                         heads, D, slope, drop_p, seed, offset, _p(offset_dev), ptr(att), ptr(agg),
+                         agg.stride(0), stream_ptr()))
     return agg, att
 
 
@@ -181,10 +190,10 @@ def attn_bwd(q, k, v, rptr, att, dagg, heads, slope, drop_p=0.0, seed=0, offset=
         dkv = torch.empty(E, 2 * D, device=k.device, dtype=torch.float32)
     qrows = nd if ldq else 1
     nbytes = 4 * (qrows * D + nd * D + 2 * E * D + E * heads + (nd + 1) + 2 * E * D + nd * D)
-    with _timed("attn_bwd", nbytes):
-        call("fb_attn_bwd", ptr(q), ldq, ptr(k), ptr(v), k.stride(0), ptr(rptr), nd, _p(n_dst_dev), heads, D,
-             slope, drop_p, seed, offset, _p(offset_dev), ptr(att), ptr(dagg), dagg.stride(0), ptr(dq), ptr(dkv),
-             dkv.data_ptr() + 4 * D, dkv.stride(0), stream_ptr())
+    _launch("attn_bwd", nbytes, 0, 1,
+            lambda: call("fb_attn_bwd", ptr(q), ldq, ptr(k), ptr(v), k.stride(0), ptr(rptr), nd, _p(n_dst_dev),
+                         heads, D, slope, drop_p, seed, offset, _p(offset_dev), ptr(att), ptr(dagg),
+                         dagg.stride(0), ptr(dq), ptr(dkv), dkv.data_ptr() + 4 * D, dkv.stride(0), stream_ptr()))
     return dq, dkv
 
 
