@@ -60,6 +60,7 @@ _SIGS = {
     "fb_segment_rows": (_I, [_P, _I64, _P, _P, _P, _I64, _I, _P, _I64, _P]),
     "fb_exclusive_sum_ws_bytes": (_SZ, [_I64]),
     "fb_exclusive_sum": (_I, [_P, _I64, _P, _P, _P]),
+    "fb_exclusive_sum_noalloc": (_I, [_P, _I64, _P, _P]),
     "fb_gather_time_encode": (_I, [_P, _I64, _P, _I64, _P, _I, _P, _I64, _P, _I, _P, _P, _P, _I, _P, _I64, _I64, _P,
                                    _P]),
     "fb_time_encode_bwd_ws_bytes": (_SZ, [_I64, _I]),

@@ -232,3 +232,48 @@ extern "C" int fb_balanced_mask(const int32_t *ptr, int64_t n_ptr, int threshold
   FB_LAUNCHED("k_balanced_mask");
   return FB_OK;
 }
+
+// ---- exclusive sum without any allocation ------------------------------------
+// Callers that cannot allocate device memory (code running while a CUDA graph
+// is being captured, hosts that hand the library a fixed memory budget, or
+// latency-critical loops where an allocator call would synchronise the device)
+// still need the scan's per-chunk partial sums somewhere.  They live in this
+// file-scope array: one int2 per 256-element chunk, 4096 chunks (32 KiB), so at
+// most 4096 * 256 = 1,048,576 elements per call.  Every GPU that loads the
+// library holds the array until the process exits.  All calls share it and it
+// keeps the last call's contents: the first kernel overwrites every chunk entry
+// a call uses before anything reads it, so nothing needs clearing, but two
+// calls whose kernels overlap on the GPU (different streams, no ordering)
+// corrupt each other's results.
+namespace {
+constexpr int64_t kStaticScanChunks = 4096;
+int2 *g_static_scan_scratch[64] = {nullptr};   // device address per device, from cudaGetSymbolAddress
+}  // namespace
+
+static __device__ __align__(256) int2 g_scan_scratch[kStaticScanChunks];
+
+extern "C" int fb_exclusive_sum_noalloc(const int32_t *in, int64_t n, int32_t *out, cudaStream_t stream) {
+  if (n < 0 || !out || (n && !in)) return fb::set_error(FB_ERR_ARG, "exclusive_sum_noalloc: bad argument");
+  if (n > kStaticScanChunks * 256)
+    return fb::set_error(FB_ERR_UNSUPPORTED,
+                         "exclusive_sum_noalloc: at most 1048576 elements (4096 chunks of 256) per call");
+  int dev = 0;
+  FB_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fb::set_error(FB_ERR_UNSUPPORTED, "exclusive_sum_noalloc: device index >= 64");
+  if (!g_static_scan_scratch[dev]) {
+    // one-time set-up on this device: the host-side symbol is not a device
+    // address, so ask the runtime for the array's address on the current device
+    void *p = nullptr;
+    FB_TRY_CUDA(cudaGetSymbolAddress(&p, g_scan_scratch));
+    g_static_scan_scratch[dev] = static_cast<int2 *>(p);
+  }
+  int2 *part = g_static_scan_scratch[dev];
+  const int nb = (int)std::max<int64_t>(1, (n + 255) / 256);
+  k_xsum_part<<<nb, 256, 0, stream>>>(in, n, part);
+  FB_LAUNCHED("k_xsum_part");
+  k_xsum_scan<<<1, 1024, 0, stream>>>(part, nb, out, n);
+  FB_LAUNCHED("k_xsum_scan");
+  k_xsum_write<<<nb, 256, 0, stream>>>(in, n, part, out);
+  FB_LAUNCHED("k_xsum_write");
+  return FB_OK;
+}

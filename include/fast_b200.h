@@ -179,6 +179,17 @@ int fb_segment_rows(const int32_t *indptr, int64_t n_seg, const int64_t *row, co
  * `ws` must hold fb_exclusive_sum_ws_bytes(n) bytes. */
 size_t fb_exclusive_sum_ws_bytes(int64_t n);
 int fb_exclusive_sum(const int32_t *in, int64_t n, int32_t *out, void *ws, cudaStream_t stream);
+/* No counterpart in the reference.  fb_exclusive_sum for callers that cannot
+ * allocate device memory -- code running while a CUDA graph is captured, hosts
+ * that give the library a fixed memory budget, loops where an allocator call
+ * would stall the device -- and so cannot provide `ws`.  The scratch is a
+ * library-owned static device array (32 KiB, held by every GPU that loads the
+ * library until exit); n is limited to 1,048,576 and larger n returns
+ * FB_ERR_UNSUPPORTED.  It allocates nothing.  Its first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress), so make that first
+ * call outside any stream capture.  All calls share the one array: calls whose
+ * kernels can overlap on the GPU (different streams without ordering) race. */
+int fb_exclusive_sum_noalloc(const int32_t *in, int64_t n, int32_t *out, cudaStream_t stream);
 
 /* ------------------------------------------------------------------------- */
 /* Feature gather fused with the cos time encoding (utils.py:126-196,         */
