@@ -143,18 +143,12 @@ __device__ __forceinline__ int64_t seg_out_row(const AttnArgs &a, int64_t j, int
   return (r >= 0 && r < a.n_out) ? r : -1;
 }
 
+// Edges handled per chunk: all of a chunk's K (or V) rows are loaded before
+// any of them is reduced, so the row loads overlap instead of serialising.
 template <int NV>
-__device__ __forceinline__ void edge_logits(const AttnArgs &a, const float4 q[NV], int e, const RowGeom &g, int lane,
-                                            const int hsel[NV][4], float (&z)[kMaxHeads]) {
-  if (a.x) {
-#pragma unroll
-    for (int h = 0; h < kMaxHeads; ++h) z[h] = (h < a.heads) ? __ldg(a.x + (int64_t)e * a.heads + h) : 0.f;
-  } else {
-    float4 kr[NV];
-    load_row<NV>(a.k + (int64_t)e * a.ldkv, g, lane, kr);
-    head_dots<NV>(q, kr, hsel, a.heads, z);
-  }
-}
+struct Chunk {
+  static constexpr int value = NV <= 1 ? 8 : (NV == 2 ? 4 : 2);
+};
 
 template <int NV>
 __global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_fwd(AttnArgs a) {
@@ -185,18 +179,35 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_fwd(AttnArgs a) {
 #pragma unroll
       for (int h = 0; h < kMaxHeads; ++h) m[h] = -FLT_MAX;
       // pass 1: activated logits (stashed), running max
-      for (int e = beg; e < end; ++e) {
-        float z[kMaxHeads];
-        edge_logits<NV>(a, q, e, g, lane, hsel, z);
+      constexpr int CH = Chunk<NV>::value;
+      for (int e0 = beg; e0 < end; e0 += CH) {
+        float4 kr[CH][NV];
+        if (!a.x) {
 #pragma unroll
-        for (int h = 0; h < kMaxHeads; ++h) {
-          z[h] = leaky(z[h], a.slope);
-          m[h] = fmaxf(m[h], z[h]);
+          for (int c = 0; c < CH; ++c)
+            if (e0 + c < end) load_row<NV>(a.k + (int64_t)(e0 + c) * a.ldkv, g, lane, kr[c]);
         }
-        const int i = e - beg;
-        if (lane < a.heads) {
-          if (i < kStash) stash[w][i][lane] = pick(z, lane);
-          else a.att_out[(int64_t)e * a.heads + lane] = pick(z, lane);
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+          const int e = e0 + c;
+          if (e >= end) break;
+          float z[kMaxHeads];
+          if (a.x) {
+#pragma unroll
+            for (int h = 0; h < kMaxHeads; ++h) z[h] = (h < a.heads) ? __ldg(a.x + (int64_t)e * a.heads + h) : 0.f;
+          } else {
+            head_dots<NV>(q, kr[c], hsel, a.heads, z);
+          }
+#pragma unroll
+          for (int h = 0; h < kMaxHeads; ++h) {
+            z[h] = leaky(z[h], a.slope);
+            m[h] = fmaxf(m[h], z[h]);
+          }
+          const int i = e - beg;
+          if (lane < a.heads) {
+            if (i < kStash) stash[w][i][lane] = pick(z, lane);
+            else a.att_out[(int64_t)e * a.heads + lane] = pick(z, lane);
+          }
         }
       }
       __syncwarp();
@@ -218,27 +229,34 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_fwd(AttnArgs a) {
       for (int h = 0; h < kMaxHeads; ++h) inv[h] = (h < a.heads) ? 1.f / fb::warp_sum(ssum[h]) : 0.f;
       __syncwarp();
       // pass 3: probabilities, dropout, weighted sum of V
-      for (int e = beg; e < end; ++e) {
-        const int i = e - beg;
-        float y[kMaxHeads], ds[kMaxHeads];
+      for (int e0 = beg; e0 < end; e0 += CH) {
+        float4 vr[CH][NV];
 #pragma unroll
-        for (int h = 0; h < kMaxHeads; ++h) {
-          float l = (h < a.heads) ? ((i < kStash) ? stash[w][i][h] : a.att_out[(int64_t)e * a.heads + h]) : 0.f;
-          y[h] = (h < a.heads) ? expf(l - m[h]) * inv[h] : 0.f;
-        }
-        __syncwarp();
-        if (lane < a.heads) a.att_out[(int64_t)e * a.heads + lane] = pick(y, lane);
-        drop_scale(e, a.heads, a.drop_p, a.seed, doff, a.mask_u, ds);
+        for (int c = 0; c < CH; ++c)
+          if (e0 + c < end) load_row<NV>(a.v + (int64_t)(e0 + c) * a.ldkv, g, lane, vr[c]);
 #pragma unroll
-        for (int h = 0; h < kMaxHeads; ++h) y[h] *= ds[h];
-        float4 vr[NV];
-        load_row<NV>(a.v + (int64_t)e * a.ldkv, g, lane, vr);
+        for (int c = 0; c < CH; ++c) {
+          const int e = e0 + c;
+          if (e >= end) break;
+          const int i = e - beg;
+          float y[kMaxHeads], ds[kMaxHeads];
 #pragma unroll
-        for (int t = 0; t < NV; ++t) {
-          acc[t].x = fmaf(pick(y, hsel[t][0]), vr[t].x, acc[t].x);
-          acc[t].y = fmaf(pick(y, hsel[t][1]), vr[t].y, acc[t].y);
-          acc[t].z = fmaf(pick(y, hsel[t][2]), vr[t].z, acc[t].z);
-          acc[t].w = fmaf(pick(y, hsel[t][3]), vr[t].w, acc[t].w);
+          for (int h = 0; h < kMaxHeads; ++h) {
+            float l = (h < a.heads) ? ((i < kStash) ? stash[w][i][h] : a.att_out[(int64_t)e * a.heads + h]) : 0.f;
+            y[h] = (h < a.heads) ? expf(l - m[h]) * inv[h] : 0.f;
+          }
+          __syncwarp();
+          if (lane < a.heads) a.att_out[(int64_t)e * a.heads + lane] = pick(y, lane);
+          drop_scale(e, a.heads, a.drop_p, a.seed, doff, a.mask_u, ds);
+#pragma unroll
+          for (int h = 0; h < kMaxHeads; ++h) y[h] *= ds[h];
+#pragma unroll
+          for (int t = 0; t < NV; ++t) {
+            acc[t].x = fmaf(pick(y, hsel[t][0]), vr[c][t].x, acc[t].x);
+            acc[t].y = fmaf(pick(y, hsel[t][1]), vr[c][t].y, acc[t].y);
+            acc[t].z = fmaf(pick(y, hsel[t][2]), vr[c][t].z, acc[t].z);
+            acc[t].w = fmaf(pick(y, hsel[t][3]), vr[c][t].w, acc[t].w);
+          }
         }
       }
     }
@@ -271,36 +289,54 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_bwd(AttnArgs a) {
 #pragma unroll
       for (int h = 0; h < kMaxHeads; ++h) sdot[h] = 0.f;
       // pass 1: dL/d(att) through dropout, dV, and sum_e y * dL/dy per head
-      for (int e = beg; e < end; ++e) {
-        float4 vr[NV];
-        load_row<NV>(a.v + (int64_t)e * a.ldkv, g, lane, vr);
-        float datt[kMaxHeads], ds[kMaxHeads], y[kMaxHeads];
-        head_dots<NV>(da, vr, hsel, a.heads, datt);
-        drop_scale(e, a.heads, a.drop_p, a.seed, doff, a.mask_u, ds);
+      constexpr int CH = Chunk<NV>::value;
+      for (int e0 = beg; e0 < end; e0 += CH) {
+        float4 vr[CH][NV];
 #pragma unroll
-        for (int h = 0; h < kMaxHeads; ++h) {
-          y[h] = (h < a.heads) ? __ldg(a.att + (int64_t)e * a.heads + h) : 0.f;
-          datt[h] *= ds[h];
-          sdot[h] = fmaf(y[h], datt[h], sdot[h]);
-        }
-        const int i = e - beg;
-        if (i < kStash && lane < a.heads) stash[w][i][lane] = pick(datt, lane);
-        if (a.dv) {
-          float4 o[NV];
+        for (int c = 0; c < CH; ++c)
+          if (e0 + c < end) load_row<NV>(a.v + (int64_t)(e0 + c) * a.ldkv, g, lane, vr[c]);
 #pragma unroll
-          for (int t = 0; t < NV; ++t) {
-            o[t].x = pick(y, hsel[t][0]) * pick(ds, hsel[t][0]) * da[t].x;
-            o[t].y = pick(y, hsel[t][1]) * pick(ds, hsel[t][1]) * da[t].y;
-            o[t].z = pick(y, hsel[t][2]) * pick(ds, hsel[t][2]) * da[t].z;
-            o[t].w = pick(y, hsel[t][3]) * pick(ds, hsel[t][3]) * da[t].w;
+        for (int c = 0; c < CH; ++c) {
+          const int e = e0 + c;
+          if (e >= end) break;
+          float datt[kMaxHeads], ds[kMaxHeads], y[kMaxHeads];
+          head_dots<NV>(da, vr[c], hsel, a.heads, datt);
+          drop_scale(e, a.heads, a.drop_p, a.seed, doff, a.mask_u, ds);
+#pragma unroll
+          for (int h = 0; h < kMaxHeads; ++h) {
+            y[h] = (h < a.heads) ? __ldg(a.att + (int64_t)e * a.heads + h) : 0.f;
+            datt[h] *= ds[h];
+            sdot[h] = fmaf(y[h], datt[h], sdot[h]);
           }
-          store_row<NV>(a.dv + (int64_t)e * a.lddkv, g, lane, o);
+          const int i = e - beg;
+          if (i < kStash && lane < a.heads) stash[w][i][lane] = pick(datt, lane);
+          if (a.dv) {
+            float4 o[NV];
+#pragma unroll
+            for (int t = 0; t < NV; ++t) {
+              o[t].x = pick(y, hsel[t][0]) * pick(ds, hsel[t][0]) * da[t].x;
+              o[t].y = pick(y, hsel[t][1]) * pick(ds, hsel[t][1]) * da[t].y;
+              o[t].z = pick(y, hsel[t][2]) * pick(ds, hsel[t][2]) * da[t].z;
+              o[t].w = pick(y, hsel[t][3]) * pick(ds, hsel[t][3]) * da[t].w;
+            }
+            store_row<NV>(a.dv + (int64_t)e * a.lddkv, g, lane, o);
+          }
         }
       }
       __syncwarp();
       if (need_dl) {
         // pass 2: softmax and LeakyReLU backward, dK rows, dq accumulation
-        for (int e = beg; e < end; ++e) {
+        for (int e0 = beg; e0 < end; e0 += CH) {
+        float4 krc[CH][NV];
+        if (!a.x) {
+#pragma unroll
+          for (int c = 0; c < CH; ++c)
+            if (e0 + c < end) load_row<NV>(a.k + (int64_t)(e0 + c) * a.ldkv, g, lane, krc[c]);
+        }
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+          const int e = e0 + c;
+          if (e >= end) break;
           const int i = e - beg;
           float dy[kMaxHeads];
           if (i < kStash) {
@@ -316,13 +352,12 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_bwd(AttnArgs a) {
             for (int h = 0; h < kMaxHeads; ++h) dy[h] *= ds[h];
           }
           float z[kMaxHeads], dz[kMaxHeads];
-          float4 kr[NV];
+          const float4 *kr = krc[c];
           if (a.x) {
 #pragma unroll
             for (int h = 0; h < kMaxHeads; ++h) z[h] = (h < a.heads) ? __ldg(a.x + (int64_t)e * a.heads + h) : 0.f;
           } else {
-            load_row<NV>(a.k + (int64_t)e * a.ldkv, g, lane, kr);
-            head_dots<NV>(q, kr, hsel, a.heads, z);
+            head_dots<NV>(q, krc[c], hsel, a.heads, z);
           }
 #pragma unroll
           for (int h = 0; h < kMaxHeads; ++h) {
@@ -351,6 +386,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_bwd(AttnArgs a) {
               dqa[t].w = fmaf(pick(dz, hsel[t][3]), kr[t].w, dqa[t].w);
             }
           }
+        }
         }
       }
     }

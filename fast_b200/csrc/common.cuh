@@ -98,4 +98,15 @@ __device__ __forceinline__ int2 block_excl_scan2(int a, int b, int &ea, int &eb,
   return tot;
 }
 
+// Number of partial sums a split reduction over n rows uses: one per
+// rows_min rows, between 1 and max_parts.  Kernels launched for a capacity
+// recompute it from the true row count on the device, so the partition and
+// the summation order, and with them the rounded result, depend on n only.
+__host__ __device__ __forceinline__ int split_parts(int64_t n, int64_t rows_min, int64_t max_parts) {
+  int64_t p = (n + rows_min - 1) / rows_min;
+  if (p > max_parts) p = max_parts;
+  if (p < 1) p = 1;
+  return (int)p;
+}
+
 }  // namespace fb

@@ -58,19 +58,23 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode(GatherA
   }
 }
 
+constexpr int64_t kTeRowsPerCta = 128;
+constexpr int64_t kTeMaxParts = 296;   // two waves of 148 SMs at most
+
 // Time-encoding backward, stage 1: CTA (x = 32-column tile, y = row chunk)
 // with 8 warps striding over the chunk's rows, lanes over columns; the warps'
 // sums are combined in shared memory in a fixed order.
 __global__ void __launch_bounds__(256) k_te_bwd_part(const float *__restrict__ g, int64_t ldg,
                                                      const float *__restrict__ dt, const float *__restrict__ w,
                                                      const float *__restrict__ b, int dtime, int64_t n_rows,
-                                                     const int32_t *n_rows_dev, int64_t unused_rows,
-                                                     float *__restrict__ part) {
+                                                     const int32_t *n_rows_dev, float *__restrict__ part) {
   __shared__ float sw_s[8][32], sb_s[8][32];
   const int64_t n = n_rows_dev ? min((int64_t)(*n_rows_dev), n_rows) : n_rows;
   const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + lane;
-  const int64_t per = (n + gridDim.y - 1) / gridDim.y;   // true rows spread over every chunk
+  const int parts = fb::split_parts(n, kTeRowsPerCta, kTeMaxParts);
+  if ((int)blockIdx.y >= parts) return;
+  const int64_t per = (n + parts - 1) / parts;
   const int64_t r0 = (int64_t)blockIdx.y * per;
   const int64_t r1 = min(n, r0 + per);
   float sw = 0.f, sb = 0.f;
@@ -95,25 +99,28 @@ __global__ void __launch_bounds__(256) k_te_bwd_part(const float *__restrict__ g
   }
 }
 
-// Stage 2: fixed-order sum of the partials (deterministic).
-__global__ void k_te_bwd_reduce(const float *__restrict__ part, int nparts, int dtime, float *dw, float *db) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+// Stage 2: one warp per column sums the partials, lanes striding over them,
+// then a fixed shuffle tree (deterministic).
+__global__ void k_te_bwd_reduce(const float *__restrict__ part, int64_t n_rows, const int32_t *n_rows_dev, int dtime,
+                                float *dw, float *db) {
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (c >= dtime) return;
+  const int64_t n = n_rows_dev ? min((int64_t)(*n_rows_dev), n_rows) : n_rows;
+  const int nparts = fb::split_parts(n, kTeRowsPerCta, kTeMaxParts);
   float sw = 0.f, sb = 0.f;
-  for (int p = 0; p < nparts; ++p) {
+  for (int p = lane; p < nparts; p += 32) {
     sw += part[((int64_t)p * 2 + 0) * dtime + c];
     sb += part[((int64_t)p * 2 + 1) * dtime + c];
   }
-  dw[c] += sw;
-  db[c] += sb;
+  sw = fb::warp_sum(sw);
+  sb = fb::warp_sum(sb);
+  if (lane == 0) {
+    dw[c] += sw;
+    db[c] += sb;
+  }
 }
 
-constexpr int64_t kTeRowsPerCta = 128;
-constexpr int64_t kTeMaxParts = 1024;
-
-inline int te_parts(int64_t n) {
-  return (int)std::max<int64_t>(1, std::min<int64_t>((n + kTeRowsPerCta - 1) / kTeRowsPerCta, kTeMaxParts));
-}
+inline int te_parts(int64_t n) { return fb::split_parts(n, kTeRowsPerCta, kTeMaxParts); }
 
 inline bool a16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -149,13 +156,14 @@ extern "C" int fb_time_encode_bwd(const float *g, int64_t ldg, const float *dt, 
                                   void *ws, cudaStream_t stream) {
   if (!g || !dt || !w || !b || !dw || !db || !ws || dtime < 1 || n_rows < 0)
     return fb::set_error(FB_ERR_ARG, "time_encode_bwd: bad argument");
+  // launched for n_rows (a capacity when n_rows_dev is given); the kernels
+  // take the partition from the true count
   const int parts = te_parts(n_rows);
-  const int64_t rows = 0;   // chunk sizes are derived on the device from the true row count
   float *part = static_cast<float *>(ws);
   dim3 grid((dtime + 31) / 32, parts);
-  k_te_bwd_part<<<grid, 256, 0, stream>>>(g, ldg, dt, w, b, dtime, n_rows, n_rows_dev, rows, part);
+  k_te_bwd_part<<<grid, 256, 0, stream>>>(g, ldg, dt, w, b, dtime, n_rows, n_rows_dev, part);
   FB_LAUNCHED("k_te_bwd_part");
-  k_te_bwd_reduce<<<(dtime + 127) / 128, 128, 0, stream>>>(part, parts, dtime, dw, db);
+  k_te_bwd_reduce<<<(dtime * 32 + 255) / 256, 256, 0, stream>>>(part, n_rows, n_rows_dev, dtime, dw, db);
   FB_LAUNCHED("k_te_bwd_reduce");
   return FB_OK;
 }

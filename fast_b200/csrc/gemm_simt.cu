@@ -100,17 +100,23 @@ __global__ void __launch_bounds__(NT) k_gemm_nt(const float *__restrict__ A, int
   }
 }
 
+constexpr int64_t kTnRowsMin = 256;      // rows per TN split, at least
+constexpr int64_t kColsumRows = 256;
+constexpr int64_t kColsumMaxParts = 148;
+
 // P[split][N][K] = sum_{m in split} G[m,n] X[m,k]
 __global__ void __launch_bounds__(NT) k_gemm_tn(const float *__restrict__ G, int64_t ldg, const float *__restrict__ X,
                                                 int64_t ldx, float *__restrict__ P, int64_t ldp, int64_t M_host,
-                                                const int32_t *M_dev, int N, int K, int64_t rows_per_split,
+                                                const int32_t *M_dev, int N, int K, int max_splits,
                                                 bool vecG, bool vecX) {
   __shared__ __align__(16) float Gs[2][BK][BM + PAD];
   __shared__ __align__(16) float Xs[2][BK][BN + PAD];
   const int64_t M = M_dev ? min((int64_t)(*M_dev), M_host) : M_host;
   const int n0 = blockIdx.y * BM, k0 = blockIdx.x * BN;
-  // the true row count is spread over all gridDim.z splits
-  const int64_t per = ((M + gridDim.z - 1) / gridDim.z + BK - 1) / BK * BK;
+  // the partition comes from the true row count, not from the launch
+  const int ns = fb::split_parts(M, kTnRowsMin, max_splits);
+  if ((int)blockIdx.z >= ns) return;
+  const int64_t per = ((M + ns - 1) / ns + BK - 1) / BK * BK;
   const int64_t s0 = (int64_t)blockIdx.z * per;
   const int64_t s1 = min(M, s0 + per);
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -155,10 +161,12 @@ __global__ void __launch_bounds__(NT) k_gemm_tn(const float *__restrict__ G, int
   }
 }
 
-__global__ void k_split_reduce(const float *__restrict__ P, int nsplit, int N, int K, float *__restrict__ C,
-                               int64_t ldc, int accumulate) {
+__global__ void k_split_reduce(const float *__restrict__ P, int64_t M_host, const int32_t *M_dev, int max_splits,
+                               int N, int K, float *__restrict__ C, int64_t ldc, int accumulate) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)N * K) return;
+  const int64_t M = M_dev ? min((int64_t)(*M_dev), M_host) : M_host;
+  const int nsplit = fb::split_parts(M, kTnRowsMin, max_splits);
   const int n = (int)(i / K), k = (int)(i % K);
   float s = 0.f;
   for (int p = 0; p < nsplit; ++p) s += P[(int64_t)p * N * K + i];
@@ -169,13 +177,14 @@ __global__ void k_split_reduce(const float *__restrict__ P, int nsplit, int N, i
 // Column sums, stage 1: CTA (x = 32-column tile, y = row chunk), 8 warps
 // striding over rows, lanes over columns, warp sums combined in fixed order.
 __global__ void __launch_bounds__(256) k_colsum_part(const float *__restrict__ G, int64_t ldg, int64_t M_host,
-                                                     const int32_t *M_dev, int N, int64_t rows_per_part,
-                                                     float *__restrict__ part) {
+                                                     const int32_t *M_dev, int N, float *__restrict__ part) {
   __shared__ float s_acc[8][32];
   const int64_t M = M_dev ? min((int64_t)(*M_dev), M_host) : M_host;
   const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + lane;
-  const int64_t per = (M + gridDim.y - 1) / gridDim.y;
+  const int parts = fb::split_parts(M, kColsumRows, kColsumMaxParts);
+  if ((int)blockIdx.y >= parts) return;
+  const int64_t per = (M + parts - 1) / parts;
   const int64_t r0 = (int64_t)blockIdx.y * per, r1 = min(M, r0 + per);
   float s = 0.f;
   if (c < N)
@@ -190,32 +199,29 @@ __global__ void __launch_bounds__(256) k_colsum_part(const float *__restrict__ G
   }
 }
 
-__global__ void k_colsum_reduce(const float *__restrict__ part, int nparts, int N, float *db, int accumulate) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+// One warp per column over the partials, fixed shuffle tree (deterministic).
+__global__ void k_colsum_reduce(const float *__restrict__ part, int64_t M_host, const int32_t *M_dev, int N,
+                                float *db, int accumulate) {
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (c >= N) return;
+  const int64_t M = M_dev ? min((int64_t)(*M_dev), M_host) : M_host;
+  const int nparts = fb::split_parts(M, kColsumRows, kColsumMaxParts);
   float s = 0.f;
-  for (int p = 0; p < nparts; ++p) s += part[(int64_t)p * N + c];
-  db[c] = accumulate ? db[c] + s : s;
+  for (int p = lane; p < nparts; p += 32) s += part[(int64_t)p * N + c];
+  s = fb::warp_sum(s);
+  if (lane == 0) db[c] = accumulate ? db[c] + s : s;
 }
 
 inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Rows of the m reduction per split of the TN GEMM: enough splits to fill
-// the machine, never fewer than 256 rows each.
-inline int64_t tn_rows_per_split(int64_t M, int N, int K) {
+// Most splits of the TN GEMM's m reduction: enough to fill the machine with
+// output tiles.  Each split covers at least kTnRowsMin rows.
+inline int tn_max_splits(int N, int K) {
   const int64_t tiles = (int64_t)((N + BM - 1) / BM) * ((K + BN - 1) / BN);
-  const int64_t want = std::max<int64_t>(1, (148 * 4) / std::max<int64_t>(tiles, 1));
-  int64_t rows = (M + want - 1) / want;
-  rows = std::max<int64_t>(256, (rows + BK - 1) / BK * BK);
-  return rows;
+  return (int)std::max<int64_t>(1, (148 * 4) / std::max<int64_t>(tiles, 1));
 }
 
-constexpr int64_t kColsumRows = 256;
-constexpr int64_t kColsumMaxParts = 1024;
-
-inline int colsum_parts(int64_t M) {
-  return (int)std::max<int64_t>(1, std::min<int64_t>((M + kColsumRows - 1) / kColsumRows, kColsumMaxParts));
-}
+inline int colsum_parts(int64_t M) { return fb::split_parts(M, kColsumRows, kColsumMaxParts); }
 
 }  // namespace
 
@@ -227,15 +233,15 @@ extern "C" int fb_gemm_nt(const float *A, int64_t lda, const float *B, int64_t l
   if (M == 0) return FB_OK;
   const bool vecA = (lda % 4 == 0) && al16(A), vecB = (ldb % 4 == 0) && al16(B);
   const int64_t mt = (M + BM - 1) / BM;
-  dim3 grid((N + BN - 1) / BN, (unsigned)std::min<int64_t>(mt, 148 * 4));
+  const int nt = (N + BN - 1) / BN;
+  dim3 grid(nt, (unsigned)std::min<int64_t>(mt, std::max<int64_t>(1, 148 * 4 / nt)));
   k_gemm_nt<<<grid, NT, 0, stream>>>(A, lda, B, ldb, bias, C, ldc, M, M_dev, N, K, accumulate, vecA, vecB);
   FB_LAUNCHED("k_gemm_nt");
   return FB_OK;
 }
 
 extern "C" size_t fb_gemm_tn_ws_bytes(int64_t M, int N, int K) {
-  const int64_t rows = tn_rows_per_split(std::max<int64_t>(M, 1), N, K);
-  const int64_t ns = std::max<int64_t>(1, (M + rows - 1) / rows);
+  const int64_t ns = fb::split_parts(M, kTnRowsMin, tn_max_splits(N, K));
   return (size_t)(ns * (int64_t)N * K) * sizeof(float);
 }
 
@@ -243,16 +249,18 @@ extern "C" int fb_gemm_tn(const float *G, int64_t ldg, const float *X, int64_t l
                           const int32_t *M_dev, int N, int K, int accumulate, void *ws, cudaStream_t stream) {
   if (!G || !X || !C || !ws || M < 0 || N < 1 || K < 1 || ldg < N || ldx < K || ldc < K)
     return fb::set_error(FB_ERR_ARG, "gemm_tn: bad argument");
-  const int64_t rows = tn_rows_per_split(std::max<int64_t>(M, 1), N, K);
-  const int ns = (int)std::max<int64_t>(1, (M + rows - 1) / rows);
-  if (ns > 65535) return fb::set_error(FB_ERR_UNSUPPORTED, "gemm_tn: M too large");
+  // launched for M (a capacity when M_dev is given); the kernels take the
+  // partition from the true row count
+  const int max_splits = tn_max_splits(N, K);
+  const int ns = fb::split_parts(M, kTnRowsMin, max_splits);
   const bool vecG = (ldg % 4 == 0) && al16(G), vecX = (ldx % 4 == 0) && al16(X);
   float *P = static_cast<float *>(ws);
   dim3 grid((K + BN - 1) / BN, (N + BM - 1) / BM, ns);
-  k_gemm_tn<<<grid, NT, 0, stream>>>(G, ldg, X, ldx, P, K, M, M_dev, N, K, rows, vecG, vecX);
+  k_gemm_tn<<<grid, NT, 0, stream>>>(G, ldg, X, ldx, P, K, M, M_dev, N, K, max_splits, vecG, vecX);
   FB_LAUNCHED("k_gemm_tn");
   const int64_t tot = (int64_t)N * K;
-  k_split_reduce<<<(unsigned)((tot + 255) / 256), 256, 0, stream>>>(P, ns, N, K, C, ldc, accumulate);
+  k_split_reduce<<<(unsigned)((tot + 255) / 256), 256, 0, stream>>>(P, M, M_dev, max_splits, N, K, C, ldc,
+                                                                      accumulate);
   FB_LAUNCHED("k_split_reduce");
   return FB_OK;
 }
@@ -268,9 +276,9 @@ extern "C" int fb_colsum(const float *G, int64_t ldg, float *db, int64_t M, cons
   const int parts = colsum_parts(M);
   float *part = static_cast<float *>(ws);
   dim3 grid((N + 31) / 32, parts);
-  k_colsum_part<<<grid, 256, 0, stream>>>(G, ldg, M, M_dev, N, kColsumRows, part);
+  k_colsum_part<<<grid, 256, 0, stream>>>(G, ldg, M, M_dev, N, part);
   FB_LAUNCHED("k_colsum_part");
-  k_colsum_reduce<<<(N + 127) / 128, 128, 0, stream>>>(part, parts, N, db, accumulate);
+  k_colsum_reduce<<<(N * 32 + 255) / 256, 256, 0, stream>>>(part, M, M_dev, N, db, accumulate);
   FB_LAUNCHED("k_colsum_reduce");
   return FB_OK;
 }

@@ -10,16 +10,19 @@
 //   A B ~= A_hi B_hi + A_hi B_lo + A_lo B_hi,
 // three kind::tf32 MMAs accumulating in fp32 in tensor memory.
 //
-// CTA = 6 warps, one 128 x BN output tile, K in 32-float (128-byte) slices:
+// CTA = 10 warps, one 128 x BN output tile (BN <= 128), K in 32-float
+// (128-byte) slices:
 //   warp 0      TMA producer: raw A/B slices -> SWIZZLE_128B shared memory
 //   warp 1      TMEM allocator and the single MMA-issuing thread
-//   warps 2..5  split each slice into hi (in place) + lo, then the epilogue
-//               (tcgen05.ld of their 32 accumulator lanes, bias, store)
+//   warps 2..5  split each slice into hi (in place) + lo
+//   warps 6..9  per slice, add the slice's TMEM accumulator into fp32
+//               registers (one output row per thread); finally bias + store
 // Stages are handed over with mbarriers: full (TMA bytes landed) -> conv
 // (split written, made visible to the async proxy) -> empty (tcgen05.commit
-// once the MMAs reading the stage are done).  Every wait is bounded: past the
-// limit the CTA records an error, stops issuing work, drains what it already
-// issued (again bounded), frees its tensor memory and exits.
+// once the MMAs reading the stage are done); the two slice accumulators with
+// accf (committed) / acce (promoted).  Every wait is bounded: past the limit
+// the CTA records an error, stops issuing work, drains what it already issued
+// (again bounded), frees its tensor memory and exits.
 //
 // TMA loads here never use cluster multicast.
 #include <cuda.h>
@@ -30,7 +33,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 32;                       // fp32 per 128-byte swizzle row
-constexpr int kThreads = 192;
+
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 constexpr int kErrTimeout = 2;
 
@@ -145,11 +148,12 @@ __host__ __device__ constexpr uint32_t idesc_tf32() {
 
 template <int BN>
 struct Cfg {
-  static constexpr int kStages = BN <= 128 ? 3 : 2;
+  static constexpr int kStages = 3;
   static constexpr int kTileA = BM * BK * 4;   // bytes of one A slice
   static constexpr int kTileB = BN * BK * 4;
   static constexpr int kStage = 2 * kTileA + 2 * kTileB;   // raw/hi + lo of A and B
-  static constexpr int kTmemCols = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
+  static constexpr int kAccStride = 128;       // TMEM columns between the two slice accumulators
+  static constexpr int kTmemCols = 256;
   static constexpr int kSmem = 1024 + kStages * kStage + 64 * 8 + 64;
 };
 
@@ -160,15 +164,23 @@ __device__ __forceinline__ float to_tf32(float x) {
   return __uint_as_float(r);
 }
 
-// x = hi + lo with hi = rna_tf32(x) and lo = rna_tf32(x - hi): |x - hi - lo| <= 2^-24 |x|
-// up to rounding of the residual, so the two TF32 cross products recover fp32.
+// x = hi + lo with hi = rna_tf32(x) and lo = rna_tf32(x - hi).
 __device__ __forceinline__ void split_tf32(const float4 v, float4 &h, float4 &l) {
   h = make_float4(to_tf32(v.x), to_tf32(v.y), to_tf32(v.z), to_tf32(v.w));
   l = make_float4(to_tf32(v.x - h.x), to_tf32(v.y - h.y), to_tf32(v.z - h.z), to_tf32(v.w - h.w));
 }
 
+// Warp roles of the 10-warp CTA.
+constexpr int kWarpProducer = 0, kWarpMma = 1, kWarpConv0 = 2, kWarpEpi0 = 6;
+constexpr int kThreadsTc = 320;
+
+// The tensor-core accumulator adds with truncation; summing a whole K range in
+// it loses ~10x more than fp32.  So each 32-wide K slice is accumulated alone
+// (small correction products first, hi*hi last) in one of two TMEM buffers,
+// and the promotion warps add the finished slice into fp32 registers with
+// round-to-nearest while the tensor cores fill the other buffer.
 template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsTc, 1)
     k_gemm_nt_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const float *__restrict__ bias, float *__restrict__ C, int64_t ldc, int64_t M_host,
                  const int32_t *M_dev, int N, int K, int accumulate, int32_t *err) {
@@ -176,6 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int S = CF::kStages;
   const int64_t M = M_dev ? min((int64_t)(*M_dev), M_host) : M_host;
   const int64_t m0 = (int64_t)blockIdx.x * BM;
+  const int n0 = blockIdx.y * BN;
   if (m0 >= M) return;
 
   extern __shared__ uint8_t smem_raw[];
@@ -185,8 +198,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto sB = [&](int s) { return smem + s * CF::kStage + 2 * CF::kTileA; };
   auto sBlo = [&](int s) { return smem + s * CF::kStage + 2 * CF::kTileA + CF::kTileB; };
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * CF::kStage);
-  uint64_t *full = bars, *conv = bars + S, *empty = bars + 2 * S, *tmem_full = bars + 3 * S;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * S + 1);
+  uint64_t *full = bars, *conv = bars + S, *empty = bars + 2 * S;
+  uint64_t *accf = bars + 3 * S, *acce = bars + 3 * S + 2, *drain = bars + 3 * S + 4;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * S + 5);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -196,17 +210,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(conv + s, 128);
       mbar_init(empty + s, 1);
     }
-    mbar_init(tmem_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf + b, 1);
+      mbar_init(acce + b, 128);
+    }
+    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_holder, CF::kTmemCols);
+  if (warp == kWarpMma) tmem_alloc(tmem_holder, CF::kTmemCols);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   const int nk = (K + BK - 1) / BK;
 
-  if (warp == 0) {
+  if (warp == kWarpProducer) {
     if (lane == 0) {
       int issued = 0;
       for (int kt = 0; kt < nk; ++kt) {
@@ -214,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (kt >= S && !mbar_wait(empty + s, (u - 1) & 1, abort_flag, err)) break;
         mbar_expect_tx(full + s, CF::kTileA + CF::kTileB);
         tma_load_2d(sA(s), &tmA, full + s, kt * BK, (int)m0);
-        tma_load_2d(sB(s), &tmB, full + s, kt * BK, 0);
+        tma_load_2d(sB(s), &tmB, full + s, kt * BK, n0);
         ++issued;
       }
       if (*abort_flag) {
@@ -226,36 +244,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kWarpMma) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_tf32<BN>();
-      bool issued_any = false;
       for (int kt = 0; kt < nk; ++kt) {
-        const int s = kt % S, u = kt / S;
-        if (!mbar_wait(conv + s, u & 1, abort_flag, err)) break;
+        const int s = kt % S, b = kt & 1;
+        if (kt >= 2 && !mbar_wait(acce + b, ((kt >> 1) - 1) & 1, abort_flag, err)) break;
+        if (!mbar_wait(conv + s, (kt / S) & 1, abort_flag, err)) break;
         tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * CF::kAccStride);
         const uint64_t ah = sdesc_k_sw128(smem_u32(sA(s))), al = sdesc_k_sw128(smem_u32(sAlo(s)));
         const uint64_t bh = sdesc_k_sw128(smem_u32(sB(s))), bl = sdesc_k_sw128(smem_u32(sBlo(s)));
 #pragma unroll
+        for (int kk = 0; kk < BK / 8; ++kk) {   // 8 tf32 = 32 bytes along K per MMA
+          const uint64_t adv = (uint64_t)(kk * 32 >> 4);
+          umma_tf32(d, al + adv, bh + adv, idesc, kk != 0);
+        }
+#pragma unroll
         for (int kk = 0; kk < BK / 8; ++kk) {
-          const uint64_t adv = (uint64_t)(kk * 32 >> 4);   // 8 tf32 = 32 bytes along K
-          umma_tf32(tmem, ah + adv, bh + adv, idesc, (kt | kk) != 0);
-          umma_tf32(tmem, ah + adv, bl + adv, idesc, 1);
-          umma_tf32(tmem, al + adv, bh + adv, idesc, 1);
+          const uint64_t adv = (uint64_t)(kk * 32 >> 4);
+          umma_tf32(d, ah + adv, bl + adv, idesc, 1);
+        }
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; ++kk) {
+          const uint64_t adv = (uint64_t)(kk * 32 >> 4);
+          umma_tf32(d, ah + adv, bh + adv, idesc, 1);
         }
         umma_commit(empty + s);
-        issued_any = true;
+        umma_commit(accf + b);
       }
-      umma_commit(tmem_full);
-      if (issued_any) {
-        // the accumulator must be complete before anybody frees it
-        const long long t0 = clock64();
-        while (!mbar_try_wait(tmem_full, 0) && clock64() - t0 < kWaitCycles) {
-        }
+      // every MMA this thread issued must be complete before TMEM is freed
+      umma_commit(drain);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitCycles) {
       }
     }
-  } else {
-    const int ct = threadIdx.x - 64;   // 0..127
+  } else if (warp < kWarpEpi0) {
+    const int ct = threadIdx.x - kWarpConv0 * 32;   // 0..127
     for (int kt = 0; kt < nk; ++kt) {
       const int s = kt % S, u = kt / S;
       if (!mbar_wait(full + s, u & 1, abort_flag, err)) break;
@@ -282,47 +307,58 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_async_smem();
       mbar_arrive(conv + s);
     }
-    // epilogue: warp w reads TMEM lanes 32*(w % 4) .. +31, one output row per thread;
-    // tcgen05.ld is warp-collective, so the go/no-go decision is made warp-wide
-    const bool ready = __all_sync(0xffffffffu, mbar_wait(tmem_full, 0, abort_flag, err) ? 1 : 0);
-    if (ready) {
+  } else {
+    // promotion + epilogue: warp w owns TMEM lanes 32*(w % 4) .. +31 = one output row per thread
+    const int q = warp & 3;
+    const uint32_t tlane = (uint32_t)(q * 32) << 16;
+    float acc[BN];
+#pragma unroll
+    for (int c = 0; c < BN; ++c) acc[c] = 0.f;
+    bool ok = true;
+    for (int kt = 0; kt < nk; ++kt) {
+      const int b = kt & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(accf + b, (kt >> 1) & 1, abort_flag, err) ? 1 : 0);
+      if (!ok) break;
       tc_fence_after();
-      const int q = warp & 3;
-      const int64_t row = m0 + q * 32 + lane;
-      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
-      const bool vec = (ldc % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
-#pragma unroll 1
+      const uint32_t t = tmem + tlane + (uint32_t)(b * CF::kAccStride);
+#pragma unroll
       for (int c0 = 0; c0 < BN; c0 += 16) {
         uint32_t r[16];
-        tmem_ld16(tbase + c0, r);
-        if (row < M) {
-          float *crow = C + row * ldc;
+        tmem_ld16(t + c0, r);
 #pragma unroll
-          for (int j = 0; j < 16; j += 4) {
-            const int col = c0 + j;
-            float v[4];
+        for (int j = 0; j < 16; ++j) acc[c0 + j] += __uint_as_float(r[j]);
+      }
+      tc_fence_before();
+      mbar_arrive(acce + b);
+    }
+    const int64_t row = m0 + q * 32 + lane;
+    if (ok && row < M) {
+      float *crow = C + row * ldc + n0;
+      const bool vec = (ldc % 4 == 0) && (n0 % 4 == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
 #pragma unroll
-            for (int t = 0; t < 4; ++t) v[t] = __uint_as_float(r[j + t]) + ((bias && col + t < N) ? bias[col + t] : 0.f);
-            if (vec && col + 3 < N) {
-              float4 *p = reinterpret_cast<float4 *>(crow + col);
-              if (accumulate) {
-                const float4 o = *p;
-                v[0] += o.x; v[1] += o.y; v[2] += o.z; v[3] += o.w;
-              }
-              *p = make_float4(v[0], v[1], v[2], v[3]);
-            } else {
+      for (int c = 0; c < BN; c += 4) {
+        const int col = n0 + c;
+        float v[4];
 #pragma unroll
-              for (int t = 0; t < 4; ++t)
-                if (col + t < N) crow[col + t] = accumulate ? crow[col + t] + v[t] : v[t];
-            }
+        for (int t = 0; t < 4; ++t) v[t] = acc[c + t] + ((bias && col + t < N) ? bias[col + t] : 0.f);
+        if (vec && col + 3 < N) {
+          float4 *p = reinterpret_cast<float4 *>(crow + c);
+          if (accumulate) {
+            const float4 o = *p;
+            v[0] += o.x; v[1] += o.y; v[2] += o.z; v[3] += o.w;
           }
+          *p = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            if (col + t < N) crow[c + t] = accumulate ? crow[c + t] + v[t] : v[t];
         }
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, CF::kTmemCols);
+  if (warp == kWarpMma) tmem_dealloc(tmem, CF::kTmemCols);
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -378,9 +414,9 @@ int launch_tc(const CUtensorMap &ma, const CUtensorMap &mb, const float *bias, f
     FB_TRY_CUDA(cudaFuncSetAttribute(k_gemm_nt_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::kSmem));
     attr_set[dev] = true;
   }
-  const unsigned grid = (unsigned)((M + BM - 1) / BM);
-  k_gemm_nt_tc<BN><<<grid, kThreads, CF::kSmem, stream>>>(ma, mb, bias, C, ldc, M, M_dev, N, K, accumulate,
-                                                           tc_err_word());
+  dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((N + BN - 1) / BN));
+  k_gemm_nt_tc<BN><<<grid, kThreadsTc, CF::kSmem, stream>>>(ma, mb, bias, C, ldc, M, M_dev, N, K, accumulate,
+                                                             tc_err_word());
   FB_LAUNCHED("k_gemm_nt_tc");
   return FB_OK;
 }
@@ -401,7 +437,9 @@ extern "C" int fb_gemm_nt_tc(const float *A, int64_t lda, const float *B, int64_
     return fb::set_error(FB_ERR_UNSUPPORTED,
                          "gemm_nt_tc: needs N <= 256, K, lda, ldb multiples of 4 and 16-byte aligned A, B");
   if (M == 0) return FB_OK;
-  const int BNr = N <= 64 ? 64 : (N <= 112 ? 112 : (N <= 128 ? 128 : (N <= 208 ? 208 : 256)));
+  // N tiles of at most 128 columns (two slice accumulators fit TMEM, and the
+  // fp32 promotion sums fit the registers of one thread per row)
+  const int BNr = N <= 64 ? 64 : (N <= 112 ? 112 : (N <= 128 ? 128 : (N <= 224 ? 112 : 128)));
   CUtensorMap ma, mb;
   int rc = make_map(&ma, A, M, K, lda, BM);
   if (rc) return rc;
@@ -410,9 +448,7 @@ extern "C" int fb_gemm_nt_tc(const float *A, int64_t lda, const float *B, int64_
   switch (BNr) {
     case 64: return launch_tc<64>(ma, mb, bias, C, ldc, M, M_dev, N, K, accumulate, stream);
     case 112: return launch_tc<112>(ma, mb, bias, C, ldc, M, M_dev, N, K, accumulate, stream);
-    case 128: return launch_tc<128>(ma, mb, bias, C, ldc, M, M_dev, N, K, accumulate, stream);
-    case 208: return launch_tc<208>(ma, mb, bias, C, ldc, M, M_dev, N, K, accumulate, stream);
-    default: return launch_tc<256>(ma, mb, bias, C, ldc, M, M_dev, N, K, accumulate, stream);
+    default: return launch_tc<128>(ma, mb, bias, C, ldc, M, M_dev, N, K, accumulate, stream);
   }
 }
 

@@ -20,6 +20,31 @@ from .model import DeviceBlock, GeneralModel, StaticBlock
 from .ext import sampler_core
 
 
+def slice_for_rank(b0, b1, rank, world):
+    """Contiguous slice of the global chronological batch [b0, b1) owned by `rank`."""
+    per = (b1 - b0) // world
+    lo = b0 + rank * per
+    return lo, lo + per
+
+
+def average_gradients(params, world, flat=None):
+    """Averages the gradients of `params` over the process group with ONE
+    all-reduce of a flat bucket (the model is ~0.2 M parameters, so one bucket
+    is latency-optimal).  Returns the bucket for reuse."""
+    grads = [p.grad for p in params if p.grad is not None]
+    n = sum(g.numel() for g in grads)
+    if flat is None or flat.numel() != n or flat.device != grads[0].device:
+        flat = torch.empty(n, device=grads[0].device, dtype=grads[0].dtype)
+    torch.cat([g.reshape(-1) for g in grads], out=flat)
+    dist.all_reduce(flat)
+    flat.div_(world)
+    off = 0
+    for g in grads:
+        g.copy_(flat[off:off + g.numel()].view_as(g))
+        off += g.numel()
+    return flat
+
+
 class Trainer:
     def __init__(self, graph, node_feats, edge_feats, sample_param, memory_param, gnn_param, train_param,
                  device, rank=0, world=1, seed=42, sampler_seed=1234):
@@ -71,10 +96,7 @@ class Trainer:
     # -- inputs ---------------------------------------------------------------
     def local_slice(self, b0, b1):
         """Contiguous slice of the global batch [b0, b1) owned by this rank."""
-        n = b1 - b0
-        per = n // self.world
-        lo = b0 + self.rank * per
-        return lo, lo + per
+        return slice_for_rank(b0, b1, self.rank, self.world)
 
     def device_roots(self, b0, b1):
         lo, hi = self.local_slice(b0, b1)
@@ -92,16 +114,7 @@ class Trainer:
         return [DeviceBlock(v, d) for v, d in zip(views, dims)]
 
     def _allreduce_grads(self):
-        grads = [p.grad for p in self.model.parameters() if p.grad is not None]
-        if self._flat is None or self._flat.numel() != sum(g.numel() for g in grads):
-            self._flat = torch.empty(sum(g.numel() for g in grads), device=self.device)
-        torch.cat([g.reshape(-1) for g in grads], out=self._flat)
-        dist.all_reduce(self._flat)
-        self._flat.div_(self.world)
-        off = 0
-        for g in grads:
-            g.copy_(self._flat[off:off + g.numel()].view_as(g))
-            off += g.numel()
+        self._flat = average_gradients(list(self.model.parameters()), self.world, self._flat)
 
     def step_device(self, roots, root_ts):
         """One training step on device-resident roots; returns the loss tensor."""
@@ -149,41 +162,39 @@ class GraphTrainer(Trainer):
         self.B = batch
         self.R0 = 3 * batch
         dv = self.device
+        # every gradient is a view of one flat buffer: one memset clears them,
+        # and the data-parallel all-reduce runs on the buffer itself
+        self._params = [p for p in self.model.parameters()]
+        self._flat = torch.zeros(sum(p.numel() for p in self._params), device=dv)
+        off = 0
+        for p in self._params:
+            p.grad = self._flat[off:off + p.numel()].view_as(p)
+            off += p.numel()
         if optimizer == "adam":
-            self.opt = torch.optim.Adam(self.model.parameters(), lr=train_param["lr"], capturable=True)
+            self.opt = torch.optim.Adam(self._params, lr=train_param["lr"], capturable=True, fused=True)
         else:
-            self.opt = torch.optim.SGD(self.model.parameters(), lr=train_param["lr"])
+            self.opt = torch.optim.SGD(self._params, lr=train_param["lr"])
         self.roots_buf = torch.zeros(self.R0, dtype=torch.int32, device=dv)
         self.ts_buf = torch.zeros(self.R0, dtype=torch.float32, device=dv)
         self.loss_buf = torch.zeros((), device=dv)
         self.h_roots = torch.zeros(self.R0, dtype=torch.int32).pin_memory()
         self.h_ts = torch.zeros(self.R0, dtype=torch.float32).pin_memory()
         self.g_main = self.g_opt = None
-        self._params = [p for p in self.model.parameters()]
 
     # the body of one step on the static input buffers
     def _fwd_bwd(self):
         self.sampler.sample_device(self.roots_buf, self.ts_buf)
         views = self.sampler.block_views()
         blocks = [StaticBlock(views[0], n_roots=self.R0)] + [StaticBlock(v) for v in views[1:]]
-        for p in self._params:
-            if p.grad is not None:
-                p.grad.zero_()
+        self._flat.zero_()
         pred_pos, pred_neg = self.model(blocks, self.node_feats, self.edge_feats)
         loss = self.crit(pred_pos, torch.ones_like(pred_pos)) + self.crit(pred_neg, torch.zeros_like(pred_neg))
         loss.backward()
         self.loss_buf.copy_(loss.detach())
-        if self.world > 1:
-            torch.cat([p.grad.reshape(-1) for p in self._params], out=self._flat)
 
     def _apply(self):
         if self.world > 1:
             self._flat.div_(self.world)
-            off = 0
-            for p in self._params:
-                n = p.numel()
-                p.grad.copy_(self._flat[off:off + n].view_as(p))
-                off += n
         self.opt.step()
 
     def _eager_step(self):
@@ -196,10 +207,6 @@ class GraphTrainer(Trainer):
         """Warm up on a side stream (allocator, lazy kernel loads, Adam state),
         then capture.  The warm-up steps are real training steps on whatever
         is in the input buffers."""
-        for p in self._params:
-            p.grad = torch.zeros_like(p)
-        if self.world > 1:
-            self._flat = torch.zeros(sum(p.numel() for p in self._params), device=self.device)
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):

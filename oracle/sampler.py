@@ -164,17 +164,18 @@ class OracleSampler:
 
 def reference_path():
     """Path of the reference sampler built from its own source, or None."""
-    hits = glob.glob(os.path.join(_HERE, "_ref", "sampler_core*.so"))
+    hits = glob.glob(os.path.join(_HERE, "_ref", "sampler_core_ref*.so"))
     return hits[0] if hits else None
 
 
 def load_reference():
-    """Import the compiled reference ``sampler_core`` without registering it in
-    sys.modules (so it can sit beside the product module of the same name)."""
+    """Import the compiled reference sampler (module ``sampler_core_ref``: the
+    reference source built with its module renamed, so it can sit beside the
+    product module ``sampler_core`` in one process)."""
     path = reference_path()
     if path is None:
         return None
-    spec = importlib.util.spec_from_file_location("sampler_core", path)
+    spec = importlib.util.spec_from_file_location("sampler_core_ref", path)
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     return mod

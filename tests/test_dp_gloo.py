@@ -1,0 +1,107 @@
+"""CPU, two gloo ranks: the data-parallel logic of fast_b200.train.
+
+* Each rank takes a contiguous slice of the chronological batch, samples it,
+  runs the model and calls average_gradients (one all-reduce of a flat
+  bucket); the result must equal the mean over slices of the per-slice
+  gradients computed in one process.
+* Failure detection without a GPU: a rank that raises before the collective
+  makes its peer's all-reduce end with an error under a short process-group
+  timeout, instead of hanging.
+"""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _setup():
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from conftest import small_graph
+    from fast_b200.model import GeneralModel
+    g = small_graph(n_nodes=120, n_edges=6000, seed=4, int_ts=False, t_max=1e4, zipf=1.0)
+    torch.manual_seed(0)
+    ef = torch.randn(6000, 24)
+    sp = dict(layer=2, neighbor=[6, 4], strategy="recent", prop_time=False, history=1, duration=0)
+    gp = dict(arch="transformer_attention", layer=2, att_head=2, dim_time=100, dim_out=100)
+    tp = dict(lr=1e-3, dropout=0.0, att_dropout=0.0)
+    model = GeneralModel(0, 24, sp, dict(type="none", dim_out=0), gp, tp)
+    return g, ef, model
+
+
+def _slice_grads(g, ef, model, lo, hi, neg_seed):
+    from oracle import ref_math
+    from oracle.sampler import OracleSampler
+    s = OracleSampler(g["indptr"], g["indices"], g["eid"], g["ts"], 1, 1, 2, [6, 4], True, False, 1, 0.0)
+    neg = np.random.default_rng(neg_seed).integers(0, 120, hi - lo).astype(np.int32)
+    roots = np.concatenate([g["src"][lo:hi], g["dst"][lo:hi], neg])
+    rts = np.concatenate([g["t"][lo:hi]] * 3).astype(np.float32)
+    s.sample(roots, rts)
+    model.zero_grad()
+    pp, pn = ref_math.model_forward(model, s.get_ret(), None, ef)
+    ref_math.bce_loss(pp, pn).backward()
+
+
+def _worker(rank, world, port, outdir, fail_rank):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=8))
+    try:
+        from fast_b200.train import average_gradients, slice_for_rank
+        g, ef, model = _setup()
+        lo, hi = slice_for_rank(3000, 3000 + 80, rank, world)
+        _slice_grads(g, ef, model, lo, hi, neg_seed=100 + rank)
+        if rank == fail_rank:
+            raise RuntimeError("injected failure on rank %d" % rank)
+        average_gradients(list(model.parameters()), world)
+        torch.save({n: p.grad for n, p in model.named_parameters()}, os.path.join(outdir, "grads%d.pt" % rank))
+        status = "ok"
+    except RuntimeError as e:
+        status = "error: " + str(e)[:200]
+    with open(os.path.join(outdir, "status%d.txt" % rank), "w") as f:
+        f.write(status)
+    try:
+        dist.destroy_process_group()
+    except Exception:
+        pass
+
+
+def test_dp_average_equals_mean_of_slices(tmp_path):
+    mp.spawn(_worker, args=(2, _port(), str(tmp_path), -1), nprocs=2, join=True)
+    sys.path.insert(0, ROOT)
+    from fast_b200.train import slice_for_rank
+    for r in range(2):
+        assert (tmp_path / ("status%d.txt" % r)).read_text() == "ok"
+    g, ef, model = _setup()
+    ref = None
+    for r in range(2):
+        lo, hi = slice_for_rank(3000, 3080, r, 2)
+        _slice_grads(g, ef, model, lo, hi, neg_seed=100 + r)
+        gr = {n: p.grad.clone() / 2 for n, p in model.named_parameters()}
+        ref = gr if ref is None else {n: ref[n] + gr[n] for n in ref}
+    for r in range(2):
+        got = torch.load(str(tmp_path / ("grads%d.pt" % r)))
+        for n in ref:
+            torch.testing.assert_close(got[n], ref[n], rtol=1e-5, atol=1e-7)
+
+
+def test_dp_failed_rank_is_detected(tmp_path):
+    mp.spawn(_worker, args=(2, _port(), str(tmp_path), 1), nprocs=2, join=True)
+    assert (tmp_path / "status1.txt").read_text().startswith("error: injected failure")
+    s0 = (tmp_path / "status0.txt").read_text()
+    assert s0.startswith("error"), s0      # the peer's all-reduce ended with an error, it did not hang
