@@ -36,7 +36,7 @@ UNIT = "edges/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="fast", choices=["fast", "reference"])
     ap.add_argument("--config", type=int, default=2)
@@ -44,6 +44,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=5)
     ap.add_argument("--eager", action="store_true", help="launch kernels step by step instead of a CUDA graph")
+    ap.add_argument("--cuda-profiler-range", action="store_true",
+                    help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--gemm", default="simt", choices=["simt", "tc"],
                     help="projection GEMMs on the CUDA cores (simt) or the tcgen05 tensor cores (tc)")
     return ap.parse_args()
@@ -106,8 +108,9 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def cpu_reference_step_fn(cfg, graph, edge_feats_cpu, node_feats_cpu, threads):
-    """Closure running one reference-CPU training step; returns (fn, kind)."""
+def cpu_reference_step_fn(cfg, graph, edge_feats_cpu, node_feats_cpu, threads, B):
+    """Closures running one reference-CPU training step on a batch index and
+    resetting the sampler (epoch start); returns (step, reset, kind)."""
     import torch
     from fast_b200.data import model_params
     from fast_b200.model import GeneralModel
@@ -125,12 +128,10 @@ def cpu_reference_step_fn(cfg, graph, edge_feats_cpu, node_feats_cpu, threads):
                          sp, mp, gp, tp)
     opt = torch.optim.Adam(model.parameters(), lr=tp["lr"])
     rng = np.random.default_rng(1)
-    B = cfg.batch
-    state = {"b": 0}
 
-    def step():
-        b0 = (state["b"] * B) % (graph.train_end - B)
-        state["b"] += 1
+    def step(i):
+        """Training step on chronological batch i (positive edges [i*B, (i+1)*B))."""
+        b0 = i * B
         src, dst, t = graph.src[b0:b0 + B], graph.dst[b0:b0 + B], graph.ts[b0:b0 + B]
         roots = np.concatenate([src, dst, rng.integers(0, graph.n_nodes, B).astype(np.int32)])
         rts = np.concatenate([t, t, t]).astype(np.float32)
@@ -143,7 +144,24 @@ def cpu_reference_step_fn(cfg, graph, edge_feats_cpu, node_feats_cpu, threads):
         opt.step()
         return float(loss)
 
-    return step, kind
+    return step, sampler.reset, kind
+
+
+SCHEDULE_NOTE = ("warm-up = the epoch's first W batches; timed = K batches spread evenly over the rest of the "
+                 "epoch, chronological; sampler reset before each pass")
+
+
+def epoch_schedule(n_batches, warmup, steps):
+    """Batch indices of a run: the first `warmup` batches of the epoch, then
+    `steps` batches spread evenly over the rest of it, in chronological order.
+    Sampled neighbourhoods grow as the epoch advances (the first batches have
+    almost no history), so the timed steps cover the whole epoch instead of
+    its first few batches."""
+    warm = list(range(min(warmup, n_batches)))
+    lo = len(warm)
+    span = max(n_batches - lo, 1)
+    timed = [min(lo + int((j + 0.5) * span / steps), n_batches - 1) for j in range(steps)]
+    return warm, timed
 
 
 def cpu_workload(cfg):
@@ -166,24 +184,28 @@ def run_reference(args):
     cfg = CONFIGS[args.config]
     threads = len(os.sched_getaffinity(0))
     graph, ef, nf = cpu_workload(cfg)
-    step, kind = cpu_reference_step_fn(cfg, graph, ef, nf, threads)
-    for _ in range(args.warmup):
-        step()
+    gB = cfg.batch * args.gpus          # the fast arm's global batch
+    step, reset, kind = cpu_reference_step_fn(cfg, graph, ef, nf, threads, gB)
+    warm, timed = epoch_schedule(graph.train_end // gB, args.warmup, args.steps)
+    reset()
+    for i in warm:
+        step(i)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
+    for i in timed:
+        step(i)
     dt = time.perf_counter() - t0
-    value = args.steps * cfg.batch / dt
+    value = args.steps * gB / dt
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded, %s shapes)" % cfg.name,
-        "config": {"workload": cfg.name, "global_batch": cfg.batch, "fanout": list(cfg.fanout),
-                   "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge},
+        "config": {"workload": cfg.name, "global_batch": gB, "fanout": list(cfg.fanout),
+                   "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge,
+                   "batches": SCHEDULE_NOTE},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
-                         "sample": "%d chronological batches of %d+%d roots, full graph" %
-                                   (args.steps, cfg.batch, 2 * cfg.batch)},
+                         "sample": "%d batches of %d+%d roots spread over one epoch of the full graph "
+                                   "(after %d warm-up batches)" % (args.steps, gB, 2 * gB, len(warm))},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -217,24 +239,19 @@ def run_fast(args):
     B = cfg.batch
     gB = B * world
     n_batches = graph.train_end // gB
-    starts = [(i * gB) for i in range(n_batches)]
-    it = {"i": 0}
+    warm, timed = epoch_schedule(n_batches, args.warmup, args.steps)
 
-    def next_range():
-        b0 = starts[it["i"] % n_batches]
-        it["i"] += 1
-        return b0, b0 + gB
-
-    def dev_step():
-        b0, b1 = next_range()
+    def dev_step(i):
+        b0, b1 = i * gB, (i + 1) * gB
         if args.eager:
             roots, rts = tr.device_roots(b0, b1)
             return tr.step_device(roots, rts)
         tr.load_device_roots(b0, b1)
         return tr.step_device()
 
-    for _ in range(args.warmup):
-        dev_step()
+    tr.reset_epoch()
+    for i in warm:
+        dev_step(i)
     torch.cuda.synchronize()
     clock = ClockSampler(local)
     if world > 1:
@@ -244,18 +261,21 @@ def run_fast(args):
     l0 = ops.LAUNCHES[0]
     if not args.eager:
         # kernels per replayed step = kernels of one eager launch of the same body
-        b0, b1 = next_range()
-        tr.load_device_roots(b0, b1)
+        tr.load_device_roots(timed[0] * gB, (timed[0] + 1) * gB)
         tr._eager_step()
         torch.cuda.synchronize()
         per_step = ops.LAUNCHES[0] - l0 + tr.sampler_kernels_per_step()
         l0 = ops.LAUNCHES[0]
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.cuda_profiler_range:
+        torch.cuda.cudart().cudaProfilerStart()
     ev0.record()
-    for _ in range(args.steps):
-        loss = dev_step()
+    for i in timed:
+        loss = dev_step(i)
     ev1.record()
     torch.cuda.synchronize()
+    if args.cuda_profiler_range:
+        torch.cuda.cudart().cudaProfilerStop()
     clocks = clock.stop()
     ms = ev0.elapsed_time(ev1)
     if args.eager:
@@ -269,14 +289,16 @@ def run_fast(args):
     ms = float(t.item())
     value = args.steps * gB / (ms / 1000.0)
 
-    # end-to-end through the reference-facing API with host buffers
+    # end-to-end through the reference-facing API with host buffers, over the
+    # same batches from a fresh epoch
     rng = np.random.default_rng(5)
+    tr.reset_epoch()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        b0, b1 = next_range()
+    for i in timed:
+        b0, b1 = i * gB, (i + 1) * gB
         lo, hi = tr.local_slice(b0, b1)
         t_np = graph.ts[lo:hi]
         roots = np.concatenate([graph.src[lo:hi], graph.dst[lo:hi],
@@ -293,9 +315,11 @@ def run_fast(args):
     # at the blocks' true sizes (host-read dims), so bytes and flops are the
     # algorithmic ones of each launch
     ops.TIMER = ops.KernelTimer(reps=10)
-    for _ in range(args.profile_steps):
-        b0, b1 = next_range()
-        roots, rts = tr.device_roots(b0, b1)
+    tr.reset_epoch()
+    args.profile_steps = max(1, min(args.profile_steps, len(timed)))
+    prof = [timed[(2 * j + 1) * len(timed) // (2 * args.profile_steps)] for j in range(args.profile_steps)]
+    for i in prof:
+        roots, rts = tr.device_roots(i * gB, (i + 1) * gB)
         Trainer.step_device(tr, roots, rts)
     kern = ops.TIMER.summary()
     ops.TIMER = None
@@ -334,6 +358,7 @@ def run_fast(args):
         "config": {"workload": cfg.name, "global_batch": gB, "local_batch": B, "fanout": list(cfg.fanout),
                    "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge,
                    "parallelism": "dp%d" % world, "launch": "eager" if args.eager else "cuda_graph",
+                   "batches": SCHEDULE_NOTE,
                    "gemm": args.gemm,
                    "l2": "inputs larger than L2 (%.1f GB edge-feature table gathered at random rows)" %
                          (cfg.edges * cfg.d_edge * 4 / 1e9)},
@@ -346,7 +371,7 @@ def run_fast(args):
         "last_loss": float(loss),
     }
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
+        line["cpu_baseline"] = cpu_baseline(cfg, warm, timed, args.cpu_seconds)
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -354,22 +379,27 @@ def run_fast(args):
     return 0
 
 
-def cpu_baseline(cfg, budget_s):
-    """Reference CPU path on a bounded sample: as many batches as fit in ~budget_s."""
+def cpu_baseline(cfg, warm, timed, budget_s):
+    """Reference CPU path on the GPU run's batch schedule (1 GPU), stopped
+    after ~budget_s; a stop before the end keeps the earlier, smaller batches,
+    which favours the CPU."""
     threads = len(os.sched_getaffinity(0))
     graph, ef, nf = cpu_workload(cfg)
-    step, kind = cpu_reference_step_fn(cfg, graph, ef, nf, threads)
-    step()  # warm-up
+    step, reset, kind = cpu_reference_step_fn(cfg, graph, ef, nf, threads, cfg.batch)
+    reset()
+    for i in warm:
+        step(i)
     n, t0 = 0, time.perf_counter()
-    while True:
-        step()
+    for i in timed:
+        step(i)
         n += 1
         el = time.perf_counter() - t0
-        if el > budget_s or n >= 200:
+        if el > budget_s:
             break
+    el = time.perf_counter() - t0
     return {"value": n * cfg.batch / el, "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": "%d chronological batches of %d+%d roots on the full %s graph (%.1f s)" %
-                      (n, cfg.batch, 2 * cfg.batch, cfg.name, el)}
+            "sample": "%d of the %d timed batches (%d+%d roots each, spread over one epoch of the full %s graph), "
+                      "%.1f s" % (n, len(timed), cfg.batch, 2 * cfg.batch, cfg.name, el)}
 
 
 def main():
