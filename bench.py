@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--eager", action="store_true", help="launch kernels step by step instead of a CUDA graph")
     ap.add_argument("--cuda-profiler-range", action="store_true",
                     help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
+    ap.add_argument("--path", default="fused", choices=["fused", "autograd"],
+                    help="training step as FusedStep kernels (fused) or the GeneralModel module under autograd")
     ap.add_argument("--gemm", default="simt", choices=["simt", "tc"],
                     help="projection GEMMs on the CUDA cores (simt) or the tcgen05 tensor cores (tc)")
     return ap.parse_args()
@@ -232,10 +234,12 @@ def run_fast(args):
     graph = make_graph(cfg)
     nf, ef = make_features(cfg, cfg.edges, dev)
     sp, mp, gp, tp = model_params(cfg)
+    fused = args.path == "fused"
     if args.eager:
-        tr = Trainer(graph, nf, ef, sp, mp, gp, tp, dev, rank=rank, world=world)
+        tr = Trainer(graph, nf, ef, sp, mp, gp, tp, dev, rank=rank, world=world, fused=fused)
     else:
-        tr = GraphTrainer(graph, nf, ef, sp, mp, gp, tp, dev, batch=cfg.batch, rank=rank, world=world)
+        tr = GraphTrainer(graph, nf, ef, sp, mp, gp, tp, dev, batch=cfg.batch, rank=rank, world=world,
+                          fused=fused)
     B = cfg.batch
     gB = B * world
     n_batches = graph.train_end // gB
@@ -359,7 +363,7 @@ def run_fast(args):
                    "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge,
                    "parallelism": "dp%d" % world, "launch": "eager" if args.eager else "cuda_graph",
                    "batches": SCHEDULE_NOTE,
-                   "gemm": args.gemm,
+                   "gemm": args.gemm, "step": args.path,
                    "l2": "inputs larger than L2 (%.1f GB edge-feature table gathered at random rows)" %
                          (cfg.edges * cfg.d_edge * 4 / 1e9)},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": world * 3 * B * 8,

@@ -73,6 +73,16 @@ _SIGS = {
     "fb_gemm_tn": (_I, [_P, _I64, _P, _I64, _P, _I64, _I64, _P, _I, _I, _I, _P, _P]),
     "fb_colsum_ws_bytes": (_SZ, [_I64, _I]),
     "fb_colsum": (_I, [_P, _I64, _P, _I64, _P, _I, _I, _P, _P]),
+    "fb_gemm_nn": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _I, _I, _I, _P]),
+    "fb_gemm_tn_bias": (_I, [_P, _I64, _P, _I64, _P, _I64, _I64, _P, _I, _I, _I, _P, _I, _P, _P]),
+    "fb_layer_tail_fwd": (_I, [_P, _I64, _P, _P, _F, _F, _U64, _U64, _P, _P, _P, _I64, _P, _I64, _I64, _P, _P,
+                               _I, _P]),
+    "fb_layer_tail_bwd_ws_bytes": (_SZ, [_I64, _I]),
+    "fb_layer_tail_bwd": (_I, [_P, _I64, _P, _I64, _P, _F, _F, _P, _I64, _P, _P, _I64, _P, _P, _I, _P, _P]),
+    "fb_edge_predictor_loss_ws_bytes": (_SZ, [_I64, _I]),
+    "fb_edge_predictor_loss": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _I, _P, _P, _I64, _P, _I64, _P, _P, _P,
+                                    _P, _P]),
+    "fb_q_time_bwd": (_I, [_P, _I, _P, _I64, _I, _I, _P, _P, _P, _I64, _P, _P, _P]),
 }
 
 for _name, (_res, _args) in _SIGS.items():

@@ -20,6 +20,13 @@
 namespace {
 
 constexpr int kWarpsPerCta = 8;
+// Segments are short (fan-out ~10), so a warp's work is a chain of a few
+// dependent loads; resident warps hide that latency.  Rows of <= 128 floats
+// fit 3 CTAs (24 warps) per SM; wider rows need the registers of 2.
+template <int NV>
+struct MinCtas {
+  static constexpr int value = NV <= 1 ? 3 : 2;
+};
 constexpr int kMaxHeads = 4;
 constexpr int kStash = 64;  // edges whose per-head values a warp keeps in shared memory
 
@@ -147,11 +154,11 @@ __device__ __forceinline__ int64_t seg_out_row(const AttnArgs &a, int64_t j, int
 // any of them is reduced, so the row loads overlap instead of serialising.
 template <int NV>
 struct Chunk {
-  static constexpr int value = NV <= 1 ? 8 : (NV == 2 ? 4 : 2);
+  static constexpr int value = NV <= 1 ? 4 : (NV == 2 ? 2 : 1);
 };
 
 template <int NV>
-__global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_fwd(AttnArgs a) {
+__global__ void __launch_bounds__(32 * kWarpsPerCta, MinCtas<NV>::value) k_attn_fwd(AttnArgs a) {
   __shared__ float stash[kWarpsPerCta][kStash][kMaxHeads];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int64_t n_dst = a.n_dst_dev ? min((int64_t)(*a.n_dst_dev), a.n_dst) : a.n_dst;
@@ -266,7 +273,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_fwd(AttnArgs a) {
 }
 
 template <int NV>
-__global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_bwd(AttnArgs a) {
+__global__ void __launch_bounds__(32 * kWarpsPerCta, MinCtas<NV>::value) k_attn_bwd(AttnArgs a) {
   __shared__ float stash[kWarpsPerCta][kStash][kMaxHeads];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int64_t n_dst = a.n_dst_dev ? min((int64_t)(*a.n_dst_dev), a.n_dst) : a.n_dst;
@@ -396,11 +403,13 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta) k_attn_bwd(AttnArgs a) {
 }
 
 int attn_grid(int64_t n_dst) {
-  int dev = 0, sms = 148;
+  static int sms_of[64] = {0};
+  int dev = 0;
   cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int &sms = sms_of[dev & 63];
+  if (sms == 0 && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
   int64_t need = (n_dst + kWarpsPerCta - 1) / kWarpsPerCta;
-  int64_t cap = (int64_t)sms * 8;  // 8 resident CTAs of 8 warps per SM
+  int64_t cap = (int64_t)sms * 8;  // grid-stride beyond a few waves of resident CTAs
   return (int)std::max<int64_t>(1, std::min(need, cap));
 }
 

@@ -41,7 +41,9 @@ __device__ __forceinline__ float4 ld4_guard(const float *p, int64_t row, int64_t
   return r;
 }
 
-// C[M,N] = A[M,K] * B[N,K]^T
+// C[M,N] = A[M,K] * B[N,K]^T       (BKN = false: B stored [N, K])
+// C[M,N] = A[M,K] * B[K,N]         (BKN = true:  B stored [K, N])
+template <bool BKN>
 __global__ void __launch_bounds__(NT) k_gemm_nt(const float *__restrict__ A, int64_t lda, const float *__restrict__ B,
                                                 int64_t ldb, const float *__restrict__ bias, float *__restrict__ C,
                                                 int64_t ldc, int64_t M_host, const int32_t *M_dev, int N, int K,
@@ -55,20 +57,27 @@ __global__ void __launch_bounds__(NT) k_gemm_nt(const float *__restrict__ A, int
   float acc[8][4] = {};
   // loader coordinates: A 128x16 = 512 float4 (2 per thread), B 64x16 = 256 float4
   const int ar0 = tid >> 2, ac = (tid & 3) * 4;  // rows ar0 and ar0 + 64
-  const int br = tid >> 2, bc = (tid & 3) * 4;
+  // B [N,K]: 64 rows x 16 k, one float4 along k per thread;
+  // B [K,N]: 16 k-rows x 64 n, one float4 along n per thread
+  const int br = BKN ? (tid >> 4) : (tid >> 2), bc = BKN ? (tid & 15) * 4 : (tid & 3) * 4;
   float4 ra0, ra1, rb;
   auto load = [&](int k0) {
     ra0 = ld4_guard(A, m0 + ar0, M, k0 + ac, K, lda, vecA);
     ra1 = ld4_guard(A, m0 + ar0 + 64, M, k0 + ac, K, lda, vecA);
-    rb = ld4_guard(B, n0 + br, N, k0 + bc, K, ldb, vecB);
+    if (BKN) rb = ld4_guard(B, k0 + br, K, n0 + bc, N, ldb, vecB);
+    else rb = ld4_guard(B, n0 + br, N, k0 + bc, K, ldb, vecB);
   };
   auto stash = [&](int buf) {
     As[buf][ac + 0][ar0] = ra0.x; As[buf][ac + 1][ar0] = ra0.y;
     As[buf][ac + 2][ar0] = ra0.z; As[buf][ac + 3][ar0] = ra0.w;
     As[buf][ac + 0][ar0 + 64] = ra1.x; As[buf][ac + 1][ar0 + 64] = ra1.y;
     As[buf][ac + 2][ar0 + 64] = ra1.z; As[buf][ac + 3][ar0 + 64] = ra1.w;
-    Bs[buf][bc + 0][br] = rb.x; Bs[buf][bc + 1][br] = rb.y;
-    Bs[buf][bc + 2][br] = rb.z; Bs[buf][bc + 3][br] = rb.w;
+    if (BKN) {
+      *reinterpret_cast<float4 *>(&Bs[buf][br][bc]) = rb;
+    } else {
+      Bs[buf][bc + 0][br] = rb.x; Bs[buf][bc + 1][br] = rb.y;
+      Bs[buf][bc + 2][br] = rb.z; Bs[buf][bc + 3][br] = rb.w;
+    }
   };
   const int nk = (K + BK - 1) / BK;
   load(0);
@@ -105,10 +114,12 @@ constexpr int64_t kColsumRows = 256;
 constexpr int64_t kColsumMaxParts = 148;
 
 // P[split][N][K] = sum_{m in split} G[m,n] X[m,k]
+// With ones = true, X carries a virtual column of ones at k = K, so output
+// column K of P holds sum_m G[m,n] (the bias gradient).
 __global__ void __launch_bounds__(NT) k_gemm_tn(const float *__restrict__ G, int64_t ldg, const float *__restrict__ X,
                                                 int64_t ldx, float *__restrict__ P, int64_t ldp, int64_t M_host,
                                                 const int32_t *M_dev, int N, int K, int max_splits,
-                                                bool vecG, bool vecX) {
+                                                bool vecG, bool vecX, bool ones) {
   __shared__ __align__(16) float Gs[2][BK][BM + PAD];
   __shared__ __align__(16) float Xs[2][BK][BN + PAD];
   const int64_t M = M_dev ? min((int64_t)(*M_dev), M_host) : M_host;
@@ -129,6 +140,13 @@ __global__ void __launch_bounds__(NT) k_gemm_tn(const float *__restrict__ G, int
     rg0 = ld4_guard(G, m + gr, s1, n0 + gc, N, ldg, vecG);
     rg1 = ld4_guard(G, m + gr + 8, s1, n0 + gc, N, ldg, vecG);
     rx = ld4_guard(X, m + xr, s1, k0 + xc, K, ldx, vecX);
+    if (ones && m + xr < s1) {
+      const int j = K - (k0 + xc);
+      if (j == 0) rx.x = 1.f;
+      else if (j == 1) rx.y = 1.f;
+      else if (j == 2) rx.z = 1.f;
+      else if (j == 3) rx.w = 1.f;
+    }
   };
   auto stash = [&](int buf) {
     *reinterpret_cast<float4 *>(&Gs[buf][gr][gc]) = rg0;
@@ -149,6 +167,7 @@ __global__ void __launch_bounds__(NT) k_gemm_tn(const float *__restrict__ G, int
     }
   }
   float *out = P + (int64_t)blockIdx.z * N * ldp;
+  const int Kout = K + (ones ? 1 : 0);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int n = n0 + ty * 8 + i;
@@ -156,22 +175,26 @@ __global__ void __launch_bounds__(NT) k_gemm_tn(const float *__restrict__ G, int
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int k = k0 + tx * 4 + j;
-      if (k < K) out[(int64_t)n * ldp + k] = acc[i][j];
+      if (k < Kout) out[(int64_t)n * ldp + k] = acc[i][j];
     }
   }
 }
 
+// Sums the splits in order.  P rows hold Kp = K (+1 with a bias column)
+// values; column K goes to db.
 __global__ void k_split_reduce(const float *__restrict__ P, int64_t M_host, const int32_t *M_dev, int max_splits,
-                               int N, int K, float *__restrict__ C, int64_t ldc, int accumulate) {
+                               int N, int K, int Kp, float *__restrict__ C, int64_t ldc, int accumulate,
+                               float *__restrict__ db, int db_accumulate) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (int64_t)N * K) return;
+  if (i >= (int64_t)N * Kp) return;
   const int64_t M = M_dev ? min((int64_t)(*M_dev), M_host) : M_host;
   const int nsplit = fb::split_parts(M, kTnRowsMin, max_splits);
-  const int n = (int)(i / K), k = (int)(i % K);
+  const int n = (int)(i / Kp), k = (int)(i % Kp);
   float s = 0.f;
-  for (int p = 0; p < nsplit; ++p) s += P[(int64_t)p * N * K + i];
-  float *c = C + (int64_t)n * ldc + k;
-  *c = accumulate ? (*c + s) : s;
+  for (int p = 0; p < nsplit; ++p) s += P[(int64_t)p * N * Kp + i];
+  float *c = (k < K) ? C + (int64_t)n * ldc + k : db + n;
+  const int acc = (k < K) ? accumulate : db_accumulate;
+  *c = acc ? (*c + s) : s;
 }
 
 // Column sums, stage 1: CTA (x = 32-column tile, y = row chunk), 8 warps
@@ -214,6 +237,20 @@ __global__ void k_colsum_reduce(const float *__restrict__ part, int64_t M_host, 
 
 inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+}  // namespace
+
+namespace fb {
+bool pgemm_ok(const float *A, int64_t lda, const float *B, int64_t ldb, int N, int K, bool b_kn);
+int pgemm_launch(const float *A, int64_t lda, const float *B, int64_t ldb, const float *bias, float *C, int64_t ldc,
+                 int64_t M, const int32_t *M_dev, int N, int K, int accumulate, bool b_kn, cudaStream_t stream);
+bool ptn_ok(const float *G, int64_t ldg, const float *X, int64_t ldx, int N, int K);
+int ptn_max_splits(int N, int Kp);
+int ptn_launch(const float *G, int64_t ldg, const float *X, int64_t ldx, float *P, int64_t M, const int32_t *M_dev,
+               int N, int K, bool ones, int max_splits, int64_t rows_min, cudaStream_t stream);
+}  // namespace fb
+
+namespace {
+
 // Most splits of the TN GEMM's m reduction: enough to fill the machine with
 // output tiles.  Each split covers at least kTnRowsMin rows.
 inline int tn_max_splits(int N, int K) {
@@ -231,38 +268,77 @@ extern "C" int fb_gemm_nt(const float *A, int64_t lda, const float *B, int64_t l
   if (!A || !B || !C || M < 0 || N < 1 || K < 1 || lda < K || ldb < K || ldc < N)
     return fb::set_error(FB_ERR_ARG, "gemm_nt: bad argument");
   if (M == 0) return FB_OK;
+  if (fb::pgemm_ok(A, lda, B, ldb, N, K, false))
+    return fb::pgemm_launch(A, lda, B, ldb, bias, C, ldc, M, M_dev, N, K, accumulate, false, stream);
   const bool vecA = (lda % 4 == 0) && al16(A), vecB = (ldb % 4 == 0) && al16(B);
   const int64_t mt = (M + BM - 1) / BM;
   const int nt = (N + BN - 1) / BN;
   dim3 grid(nt, (unsigned)std::min<int64_t>(mt, std::max<int64_t>(1, 148 * 4 / nt)));
-  k_gemm_nt<<<grid, NT, 0, stream>>>(A, lda, B, ldb, bias, C, ldc, M, M_dev, N, K, accumulate, vecA, vecB);
+  k_gemm_nt<false><<<grid, NT, 0, stream>>>(A, lda, B, ldb, bias, C, ldc, M, M_dev, N, K, accumulate, vecA, vecB);
   FB_LAUNCHED("k_gemm_nt");
   return FB_OK;
 }
 
+extern "C" int fb_gemm_nn(const float *A, int64_t lda, const float *B, int64_t ldb, const float *bias, float *C,
+                          int64_t ldc, int64_t M, const int32_t *M_dev, int N, int K, int accumulate,
+                          cudaStream_t stream) {
+  if (!A || !B || !C || M < 0 || N < 1 || K < 1 || lda < K || ldb < N || ldc < N)
+    return fb::set_error(FB_ERR_ARG, "gemm_nn: bad argument");
+  if (M == 0) return FB_OK;
+  if (fb::pgemm_ok(A, lda, B, ldb, N, K, true))
+    return fb::pgemm_launch(A, lda, B, ldb, bias, C, ldc, M, M_dev, N, K, accumulate, true, stream);
+  const bool vecA = (lda % 4 == 0) && al16(A), vecB = (ldb % 4 == 0) && al16(B);
+  const int64_t mt = (M + BM - 1) / BM;
+  const int nt = (N + BN - 1) / BN;
+  dim3 grid(nt, (unsigned)std::min<int64_t>(mt, std::max<int64_t>(1, 148 * 4 / nt)));
+  k_gemm_nt<true><<<grid, NT, 0, stream>>>(A, lda, B, ldb, bias, C, ldc, M, M_dev, N, K, accumulate, vecA, vecB);
+  FB_LAUNCHED("k_gemm_nn");
+  return FB_OK;
+}
+
 extern "C" size_t fb_gemm_tn_ws_bytes(int64_t M, int N, int K) {
-  const int64_t ns = fb::split_parts(M, kTnRowsMin, tn_max_splits(N, K));
-  return (size_t)(ns * (int64_t)N * K) * sizeof(float);
+  // room for either kernel family, with or without the bias column
+  int64_t most = 0;
+  for (int Kp = K; Kp <= K + 1; ++Kp) {
+    const int64_t a = fb::split_parts(M, kTnRowsMin, tn_max_splits(N, Kp));
+    const int64_t b = fb::split_parts(M, kTnRowsMin, fb::ptn_max_splits(N, Kp));
+    most = std::max(most, std::max(a, b) * (int64_t)N * Kp);
+  }
+  return (size_t)most * sizeof(float);
+}
+
+extern "C" int fb_gemm_tn_bias(const float *G, int64_t ldg, const float *X, int64_t ldx, float *C, int64_t ldc,
+                               int64_t M, const int32_t *M_dev, int N, int K, int accumulate, float *db,
+                               int db_accumulate, void *ws, cudaStream_t stream) {
+  if (!G || !X || !C || !ws || M < 0 || N < 1 || K < 1 || ldg < N || ldx < K || ldc < K)
+    return fb::set_error(FB_ERR_ARG, "gemm_tn: bad argument");
+  const bool ones = db != nullptr;
+  const int Kp = K + (ones ? 1 : 0);
+  float *P = static_cast<float *>(ws);
+  // launched for M (a capacity when M_dev is given); the kernels take the
+  // partition from the true row count
+  const bool pipe = fb::ptn_ok(G, ldg, X, ldx, N, K);
+  const int max_splits = pipe ? fb::ptn_max_splits(N, Kp) : tn_max_splits(N, Kp);
+  if (pipe) {
+    const int rc = fb::ptn_launch(G, ldg, X, ldx, P, M, M_dev, N, K, ones, max_splits, kTnRowsMin, stream);
+    if (rc != FB_OK) return rc;
+  } else {
+    const int ns = fb::split_parts(M, kTnRowsMin, max_splits);
+    const bool vecG = (ldg % 4 == 0) && al16(G), vecX = (ldx % 4 == 0) && al16(X);
+    dim3 grid((Kp + BN - 1) / BN, (N + BM - 1) / BM, ns);
+    k_gemm_tn<<<grid, NT, 0, stream>>>(G, ldg, X, ldx, P, Kp, M, M_dev, N, K, max_splits, vecG, vecX, ones);
+    FB_LAUNCHED("k_gemm_tn");
+  }
+  const int64_t tot = (int64_t)N * Kp;
+  k_split_reduce<<<(unsigned)((tot + 255) / 256), 256, 0, stream>>>(P, M, M_dev, max_splits, N, K, Kp, C, ldc,
+                                                                      accumulate, db, db_accumulate);
+  FB_LAUNCHED("k_split_reduce");
+  return FB_OK;
 }
 
 extern "C" int fb_gemm_tn(const float *G, int64_t ldg, const float *X, int64_t ldx, float *C, int64_t ldc, int64_t M,
                           const int32_t *M_dev, int N, int K, int accumulate, void *ws, cudaStream_t stream) {
-  if (!G || !X || !C || !ws || M < 0 || N < 1 || K < 1 || ldg < N || ldx < K || ldc < K)
-    return fb::set_error(FB_ERR_ARG, "gemm_tn: bad argument");
-  // launched for M (a capacity when M_dev is given); the kernels take the
-  // partition from the true row count
-  const int max_splits = tn_max_splits(N, K);
-  const int ns = fb::split_parts(M, kTnRowsMin, max_splits);
-  const bool vecG = (ldg % 4 == 0) && al16(G), vecX = (ldx % 4 == 0) && al16(X);
-  float *P = static_cast<float *>(ws);
-  dim3 grid((K + BN - 1) / BN, (N + BM - 1) / BM, ns);
-  k_gemm_tn<<<grid, NT, 0, stream>>>(G, ldg, X, ldx, P, K, M, M_dev, N, K, max_splits, vecG, vecX);
-  FB_LAUNCHED("k_gemm_tn");
-  const int64_t tot = (int64_t)N * K;
-  k_split_reduce<<<(unsigned)((tot + 255) / 256), 256, 0, stream>>>(P, M, M_dev, max_splits, N, K, C, ldc,
-                                                                      accumulate);
-  FB_LAUNCHED("k_split_reduce");
-  return FB_OK;
+  return fb_gemm_tn_bias(G, ldg, X, ldx, C, ldc, M, M_dev, N, K, accumulate, nullptr, 0, ws, stream);
 }
 
 extern "C" size_t fb_colsum_ws_bytes(int64_t M, int N) {

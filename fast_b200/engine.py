@@ -1,0 +1,236 @@
+"""Autograd-free training step of the TGAT GeneralModel on the fast_b200 kernels.
+
+The reference trains GeneralModel (modules.py:8-70) with PyTorch autograd:
+per layer the attention core, then w_out / ReLU / dropout / LayerNorm
+(layers.py:213-223), the EdgePredictor (layers.py:31-50) and
+BCEWithLogitsLoss (train.py:205-206).  `FusedStep` runs that same forward
+and its hand-derived backward as an explicit sequence of kernel launches:
+
+  per layer, forward     gather + time encode -> K|V GEMM -> Q GEMM ->
+                         attention -> w_out GEMM(s) -> tail (dropout, ReLU, LayerNorm)
+  predictor + loss       src_fc / dst_fc GEMMs -> fused scores + loss + dS, dP
+  per layer, backward    tail backward -> w_out grads (bias in the same pass) ->
+                         d agg -> attention backward -> K|V grads -> time-encode
+                         grads -> Q grads -> input gradient of the layer below
+
+Parameter gradients go straight into `.grad` tensors that are views of one
+flat buffer (`flat`), so there is no autograd graph, no gradient
+accumulation pass and one memset per step; the flat buffer is also what
+data-parallel training all-reduces.  w_k / w_v are re-seated as adjacent rows
+of one [2D, K] tensor (and their biases of one [2D] tensor), so K and V come
+from one GEMM; their state_dict names and shapes are unchanged.
+
+Every launch honours device-side row counts (StaticBlock), so the step can
+be captured in a CUDA graph.
+"""
+import torch
+
+from . import ops
+
+_ALIGN = 64            # flat-buffer segments start on 256-byte boundaries
+
+
+def _seat_pair(a, b):
+    """Re-seat two Linear layers' weights (and biases) as adjacent rows of one
+    tensor; returns (W [2D, K], bias [2D])."""
+    D = a.weight.shape[0]
+    W = torch.cat([a.weight.data, b.weight.data], 0).contiguous()
+    bias = torch.cat([a.bias.data, b.bias.data], 0).contiguous()
+    a.weight = torch.nn.Parameter(W[:D])
+    b.weight = torch.nn.Parameter(W[D:])
+    a.bias = torch.nn.Parameter(bias[:D])
+    b.bias = torch.nn.Parameter(bias[D:])
+    return W, bias
+
+
+class _LayerParams:
+    def __init__(self, layer):
+        self.L = layer
+        self.D = layer.dim_out
+        self.dn, self.de, self.dtime = layer.dim_node_feat, layer.dim_edge_feat, layer.dim_time
+        self.W_kv, self.b_kv = _seat_pair(layer.w_k, layer.w_v)
+        self.gW_kv = self.gb_kv = None
+
+
+class FusedStep:
+    """Forward + backward + loss of a memoryless transformer_attention
+    GeneralModel.  Call `step(blocks, node_table, edge_table, loss_out)`; then
+    run the optimizer on the model's parameters."""
+
+    def __init__(self, model):
+        if model.memory_param.get("type", "none") != "none":
+            raise NotImplementedError("FusedStep covers memoryless models")
+        self.model = model
+        self.layers = [_LayerParams(model.layers["l%dh0" % l]) for l in range(model.gnn_param["layer"])]
+        for lp in self.layers:
+            if lp.dn + lp.dtime == 0:
+                raise NotImplementedError("Q = ones branch (layers.py:137-140) is not on the device path")
+            if lp.L.layer_norm.weight.shape[0] % 4 or lp.D % 4:
+                raise NotImplementedError("dim_out must be a multiple of 4")
+        self.flat = self._build_flat()
+
+    # -- gradient storage -----------------------------------------------------
+    def _build_flat(self):
+        groups = []                      # (owner, shape, [(param, slice-or-None)])
+        seated = set()
+        for lp in self.layers:
+            D = lp.D
+            groups.append(((lp, "gW_kv"), tuple(lp.W_kv.shape),
+                           [(lp.L.w_k.weight, slice(0, D)), (lp.L.w_v.weight, slice(D, 2 * D))]))
+            groups.append(((lp, "gb_kv"), tuple(lp.b_kv.shape),
+                           [(lp.L.w_k.bias, slice(0, D)), (lp.L.w_v.bias, slice(D, 2 * D))]))
+            seated.update(id(p) for p in (lp.L.w_k.weight, lp.L.w_v.weight, lp.L.w_k.bias, lp.L.w_v.bias))
+        for p in self.model.parameters():
+            if id(p) not in seated:
+                groups.append((None, tuple(p.shape), [(p, None)]))
+        numel = lambda shape: int(torch.Size(shape).numel())
+        total = sum((numel(shape) + _ALIGN - 1) // _ALIGN * _ALIGN for _, shape, _ in groups)
+        dev = next(self.model.parameters()).device
+        flat = torch.zeros(total, device=dev, dtype=torch.float32)
+        off = 0
+        for owner, shape, members in groups:
+            n = numel(shape)
+            view = flat[off:off + n].view(shape)
+            for p, sl in members:
+                p.grad = view if sl is None else view[sl]
+            if owner is not None:
+                setattr(owner[0], owner[1], view)
+            off += (n + _ALIGN - 1) // _ALIGN * _ALIGN
+        return flat
+
+    def parameters(self):
+        return list(self.model.parameters())
+
+    # -- one layer ------------------------------------------------------------
+    def _layer_fwd(self, l, blk, h, node_table, edge_table, offset_dev, training):
+        lp = self.layers[l]
+        L, D, dn, de, dtime = lp.L, lp.D, lp.dn, lp.de, lp.dtime
+        nd, E = blk.n_dst, blk.n_edges
+        nd_dev, E_dev = blk.n_dst_dev, blk.n_edges_dev
+        dev = lp.W_kv.device
+        if not blk.static and E == 0:
+            # layers.py:101-102: a block without edges outputs zeros
+            return None, torch.zeros(nd, D, device=dev)
+        wv = L.time_enc.w.weight.view(-1) if dtime > 0 else None
+        bt = L.time_enc.w.bias if dtime > 0 else None
+        if h is not None:
+            if blk.static and not blk.n_dst_static:
+                raise NotImplementedError("graph mode feeds a previous layer's output only to the top block")
+            hsrc, hdst = dict(h=h, h_off=nd), dict(h=h, h_off=0)
+        elif node_table is not None and dn > 0:
+            hsrc, hdst = dict(h=node_table, h_idx=blk.src_nodes), dict(h=node_table, h_idx=blk.dst_nodes)
+        else:
+            hsrc = hdst = {}
+        A = ops.gather_time_encode(E, f=edge_table if de > 0 else None, f_idx=blk.eid, dt=blk.dt_edges, w=wv, b=bt,
+                                   device=dev, n_rows_dev=E_dev, **hsrc)
+        KV = ops.gemm_nt(A, lp.W_kv, lp.b_kv, M_dev=E_dev)
+        if dn > 0:
+            Qin = ops.gather_time_encode(nd, w=wv, b=bt, device=dev, n_rows_dev=nd_dev, **hdst)
+            Q = ops.gemm_nt(Qin, L.w_q.weight, L.w_q.bias, M_dev=nd_dev)
+        else:
+            Qin = ops.gather_time_encode(1, w=wv, b=bt, device=dev)
+            Q = ops.gemm_nt(Qin, L.w_q.weight, L.w_q.bias)
+        p_att = L.att_dropout_p if training else 0.0
+        agg, att = ops.attn_fwd(Q, KV[:, :D], KV[:, D:], blk.rptr, L.num_head, L.negative_slope, p_att,
+                                0x5EED + l, 0, n_dst_dev=nd_dev, offset_dev=offset_dev)
+        Wo = L.w_out.weight
+        Z = ops.gemm_nt(agg, Wo[:, :D], L.w_out.bias, M_dev=nd_dev)
+        if dn > 0:
+            ops.gemm_nt(Qin[:, :dn], Wo[:, D:], out=Z, accumulate=True, M_dev=nd_dev)
+        p_drop = L.dropout.p if training else 0.0
+        y, out = ops.layer_tail_fwd(Z, L.layer_norm.weight, L.layer_norm.bias, eps=L.layer_norm.eps, drop_p=p_drop,
+                                    seed=0x7A11 + l, offset_dev=offset_dev, y=Z, n_dev=nd_dev,
+                                    gate_dev=E_dev if blk.static else None)
+        st = dict(blk=blk, A=A, KV=KV, Qin=Qin, Q=Q, agg=agg, att=att, y=y, p_att=p_att, p_drop=p_drop,
+                  offset_dev=offset_dev)
+        return st, out
+
+    def _layer_bwd(self, l, st, dout, dh_rows):
+        """Adds layer l's parameter gradients; returns the gradient of its
+        input h (rows dh_rows) when l > 0, else None."""
+        lp = self.layers[l]
+        L, D, dn, de, dtime = lp.L, lp.D, lp.dn, lp.de, lp.dtime
+        if st is None:                     # empty block (eager): zero output, no gradient
+            return None if l == 0 else torch.zeros(dh_rows, dn, device=dout.device)
+        blk = st["blk"]
+        nd, E = blk.n_dst, blk.n_edges
+        nd_dev, E_dev = blk.n_dst_dev, blk.n_edges_dev
+        g = lambda p: p.grad
+        dZ = ops.layer_tail_bwd(dout, st["y"], L.layer_norm.weight, g(L.layer_norm.weight), g(L.layer_norm.bias),
+                                eps=L.layer_norm.eps, drop_p=st["p_drop"], n_dev=nd_dev,
+                                gate_dev=E_dev if blk.static else None)
+        Wo, gWo = L.w_out.weight, g(L.w_out.weight)
+        agg, Qin = st["agg"], st["Qin"]
+        ops.gemm_tn(dZ, agg, out=gWo[:, :D], accumulate=True, M_dev=nd_dev, db=g(L.w_out.bias))
+        if dn > 0:
+            ops.gemm_tn(dZ, Qin[:, :dn], out=gWo[:, D:], accumulate=True, M_dev=nd_dev)
+        dagg = ops.gemm_nn(dZ, Wo[:, :D], M_dev=nd_dev)
+        dh = None
+        if l > 0:
+            assert dh_rows >= nd + E
+            dh = torch.empty(dh_rows, dn, device=dout.device)
+            ops.gemm_nn(dZ, Wo[:, D:], out=dh[:nd], M_dev=nd_dev)
+        KV = st["KV"]
+        dQ, dKV = ops.attn_bwd(st["Q"], KV[:, :D], KV[:, D:], blk.rptr, st["att"], dagg, L.num_head,
+                               L.negative_slope, st["p_att"], 0x5EED + l, 0, n_dst_dev=nd_dev,
+                               offset_dev=st["offset_dev"])
+        ops.gemm_tn(dKV, st["A"], out=lp.gW_kv, accumulate=True, M_dev=E_dev, db=lp.gb_kv)
+        if dh is not None:
+            ops.gemm_nn(dKV, lp.W_kv[:, :dn], out=dh[nd:nd + E], M_dev=E_dev)
+        if dtime > 0:
+            dA_t = ops.gemm_nn(dKV, lp.W_kv[:, dn + de:], M_dev=E_dev)
+            ops.time_encode_bwd(dA_t, blk.dt_edges, L.time_enc.w.weight.view(-1), L.time_enc.w.bias,
+                                g(L.time_enc.w.weight).view(-1), g(L.time_enc.w.bias), n_dev=E_dev)
+        bt = L.time_enc.w.bias if dtime > 0 else None
+        gbt = g(L.time_enc.w.bias) if dtime > 0 else None
+        if dn == 0:
+            # one shared Q input row cos(b_t): every Q-side gradient needs only sum_rows dQ
+            v = ops.colsum(dQ, M_dev=nd_dev)
+            ops.q_time_bwd(v, L.w_q.weight, dn, dtime, bt, g(L.w_q.bias), gbt, qin0=Qin[0], dW_q=g(L.w_q.weight))
+        else:
+            v = torch.empty(D, device=dout.device)
+            ops.gemm_tn(dQ, Qin, out=g(L.w_q.weight), accumulate=True, M_dev=nd_dev, db=v, db_accumulate=False)
+            ops.q_time_bwd(v, L.w_q.weight, dn, dtime, bt, g(L.w_q.bias), gbt)
+            if dh is not None:
+                ops.gemm_nn(dQ, L.w_q.weight[:, :dn], out=dh[:nd], accumulate=True, M_dev=nd_dev)
+        return dh
+
+    # -- whole step -----------------------------------------------------------
+    def step(self, blocks, node_table, edge_table, loss_out, zero_grad=True, scores=None):
+        """blocks in sampler order (hop 1 first), Device- or StaticBlocks.
+        Writes the loss into loss_out (a 0-d device tensor) and the gradients
+        into the parameters' .grad (zeroed first unless zero_grad=False);
+        with `scores` ([2B] device tensor) also the positive then negative
+        edge scores."""
+        m = self.model
+        training = m.training
+        mfgs = list(reversed(blocks))
+        dev = self.flat.device
+        if m._drop_step is None or m._drop_step.device != dev:
+            m._drop_step = torch.zeros(1, dtype=torch.int64, device=dev)
+        if training:
+            m._drop_step += 1
+        if zero_grad:
+            self.flat.zero_()
+        saved, h = [], None
+        for l, blk in enumerate(mfgs):
+            st, h = self._layer_fwd(l, blk, h, node_table if l == 0 else None, edge_table, m._drop_step, training)
+            saved.append(st)
+        ep = m.edge_predictor
+        B = h.shape[0] // 3
+        D = h.shape[1]
+        S = ops.gemm_nt(h[:B], ep.src_fc.weight, ep.src_fc.bias)
+        P = ops.gemm_nt(h[B:3 * B], ep.dst_fc.weight, ep.dst_fc.bias)
+        dS = torch.empty(B, D, device=dev)
+        dP = torch.empty(2 * B, D, device=dev)
+        ops.edge_predictor_loss(S, P, ep.out_fc.weight.view(-1), ep.out_fc.bias, loss_out, dS, dP,
+                                ep.out_fc.weight.grad.view(-1), ep.out_fc.bias.grad, scores=scores)
+        dh = torch.empty(3 * B, D, device=dev)
+        ops.gemm_tn(dS, h[:B], out=ep.src_fc.weight.grad, accumulate=True, db=ep.src_fc.bias.grad)
+        ops.gemm_tn(dP, h[B:3 * B], out=ep.dst_fc.weight.grad, accumulate=True, db=ep.dst_fc.bias.grad)
+        ops.gemm_nn(dS, ep.src_fc.weight, out=dh[:B])
+        ops.gemm_nn(dP, ep.dst_fc.weight, out=dh[B:3 * B])
+        for l in range(len(mfgs) - 1, -1, -1):
+            rows = mfgs[l - 1].n_dst if l > 0 else 0
+            dh = self._layer_bwd(l, saved[l], dh, rows)
+        return loss_out

@@ -172,7 +172,11 @@ class TransfomerAttentionLayer(torch.nn.Module):
             rst = agg
         rst = self.w_out(rst)
         rst = torch.nn.functional.relu(self.dropout(rst))
-        return self.layer_norm(rst)
+        out = self.layer_norm(rst)
+        if blk.static:
+            # layers.py:101-102: a block without edges outputs zeros
+            out = torch.where(blk.n_edges_dev > 0, out, 0.0)
+        return out
 
 
 class GeneralModel(torch.nn.Module):

@@ -106,19 +106,84 @@ def tc_error(clear=True):
     return f.value
 
 
-def gemm_tn(G, X, out=None, accumulate=False, M_dev=None):
-    """out[n, k] (+)= sum_m G[m, n] X[m, k]  (weight gradient); rows m < *M_dev when given."""
+def gemm_nn(A, B, bias=None, out=None, accumulate=False, M_dev=None):
+    """out[m, n] (+)= sum_k A[m, k] B[k, n] + bias[n]  (B stored [K, N]); rows m < *M_dev when given."""
+    _f32_rows(A, "A")
+    _f32_rows(B, "B")
+    M, K = A.shape
+    N = B.shape[1]
+    if B.shape[0] != K:
+        raise ValueError("gemm_nn: inner dimensions differ")
+    if out is None:
+        out = torch.empty(M, N, device=A.device, dtype=torch.float32)
+    _launch("gemm_nn", 4 * (M * K + N * K + M * N), 2 * M * N * K, 1,
+            lambda: call("fb_gemm_nn", ptr(A), A.stride(0), ptr(B), B.stride(0), ptr(bias), ptr(out),
+                         out.stride(0), M, _p(M_dev), N, K, int(accumulate), stream_ptr()))
+    return out
+
+
+def gemm_tn(G, X, out=None, accumulate=False, M_dev=None, db=None, db_accumulate=None):
+    """out[n, k] (+)= sum_m G[m, n] X[m, k]  (weight gradient); rows m < *M_dev when given.
+    With db, also db[n] (+)= sum_m G[m, n] in the same pass (db_accumulate
+    defaults to accumulate)."""
     _f32_rows(G, "G")
     _f32_rows(X, "X")
     M, N = G.shape
     K = X.shape[1]
     if out is None:
         out = torch.empty(N, K, device=G.device, dtype=torch.float32)
+    dba = accumulate if db_accumulate is None else db_accumulate
     ws = torch.empty(int(lib.fb_gemm_tn_ws_bytes(M, N, K)), device=G.device, dtype=torch.uint8)
     _launch("gemm_tn", 4 * (M * N + M * K + N * K), 2 * M * N * K, 2,
-            lambda: call("fb_gemm_tn", ptr(G), G.stride(0), ptr(X), X.stride(0), ptr(out), out.stride(0), M,
-                         _p(M_dev), N, K, int(accumulate), ptr(ws), stream_ptr()))
+            lambda: call("fb_gemm_tn_bias", ptr(G), G.stride(0), ptr(X), X.stride(0), ptr(out), out.stride(0), M,
+                         _p(M_dev), N, K, int(accumulate), ptr(db), int(dba), ptr(ws), stream_ptr()))
     return out
+
+
+def layer_tail_fwd(z, gamma, beta, eps=1e-5, drop_p=0.0, seed=0, offset=0, offset_dev=None, mask_u=None,
+                   y=None, out=None, n_dev=None, gate_dev=None):
+    """y = relu(dropout(z)), out = LayerNorm(y) per row (rows >= *n_dev: out = 0;
+    all rows when *gate_dev == 0)."""
+    n, d = z.shape
+    y = torch.empty_like(z) if y is None else y
+    out = torch.empty_like(z) if out is None else out
+    _launch("layer_tail_fwd", 4 * (3 * n * d + 2 * d), 0, 1,
+            lambda: call("fb_layer_tail_fwd", ptr(z), z.stride(0), ptr(gamma), ptr(beta), float(eps),
+                         float(drop_p), int(seed), int(offset), _p(offset_dev), ptr(mask_u), ptr(y), y.stride(0),
+                         ptr(out), out.stride(0), n, _p(n_dev), _p(gate_dev), d, stream_ptr()))
+    return y, out
+
+
+def layer_tail_bwd(dout, y, gamma, dgamma, dbeta, eps=1e-5, drop_p=0.0, dz=None, n_dev=None, gate_dev=None):
+    """dz from dout and the saved y; dgamma / dbeta accumulate."""
+    n, d = y.shape
+    dz = torch.empty_like(y) if dz is None else dz
+    ws = torch.empty(int(lib.fb_layer_tail_bwd_ws_bytes(n, d)), device=y.device, dtype=torch.uint8)
+    _launch("layer_tail_bwd", 4 * (3 * n * d + 3 * d), 0, 2,
+            lambda: call("fb_layer_tail_bwd", ptr(dout), dout.stride(0), ptr(y), y.stride(0), ptr(gamma),
+                         float(eps), float(drop_p), ptr(dz), dz.stride(0), ptr(dgamma), ptr(dbeta), n, _p(n_dev),
+                         _p(gate_dev), d, ptr(ws), stream_ptr()))
+    return dz
+
+
+def edge_predictor_loss(S, P, w_o, b_o, loss, dS, dP, dw_o, db_o, scores=None):
+    """Scores relu(S_i + P_.) . w_o + b_o of the B positive and B negative
+    pairs, the BCE-with-logits loss (written to `loss`), dS / dP, and the
+    out_fc gradients (accumulated)."""
+    B, d = S.shape
+    ws = torch.empty(int(lib.fb_edge_predictor_loss_ws_bytes(B, d)), device=S.device, dtype=torch.uint8)
+    _launch("edge_predictor_loss", 4 * (2 * 3 * B * d + 2 * d), 0, 2,
+            lambda: call("fb_edge_predictor_loss", ptr(S), S.stride(0), ptr(P), P.stride(0), ptr(w_o), ptr(b_o), B,
+                         d, ptr(loss), ptr(dS), dS.stride(0), ptr(dP), dP.stride(0), ptr(dw_o), ptr(db_o),
+                         ptr(scores), ptr(ws), stream_ptr()))
+
+
+def q_time_bwd(v, W_q, dn, dtime, b_t, db_q, db_t, qin0=None, dW_q=None):
+    """db_q += v; db_t -= sin(b_t) * (v @ W_q[:, dn:]); with qin0, dW_q += outer(v, qin0)."""
+    D = v.numel()
+    _launch("q_time_bwd", 4 * (D * (dn + dtime) + 2 * D + 2 * dtime), 0, 1,
+            lambda: call("fb_q_time_bwd", ptr(v), D, ptr(W_q), W_q.stride(0), dn, dtime, ptr(b_t), ptr(qin0),
+                         ptr(dW_q), 0 if dW_q is None else dW_q.stride(0), ptr(db_q), ptr(db_t), stream_ptr()))
 
 
 def colsum(G, out=None, accumulate=False, M_dev=None):

@@ -16,6 +16,7 @@ import torch
 import torch.distributed as dist
 
 from . import ops
+from .engine import FusedStep
 from .model import DeviceBlock, GeneralModel, StaticBlock
 from .ext import sampler_core
 
@@ -46,8 +47,12 @@ def average_gradients(params, world, flat=None):
 
 
 class Trainer:
+    """Eager trainer: host-sized blocks (the sampled sizes are read back each
+    step).  fused=True runs forward + backward through FusedStep (no
+    autograd); fused=False through the GeneralModel module under autograd."""
+
     def __init__(self, graph, node_feats, edge_feats, sample_param, memory_param, gnn_param, train_param,
-                 device, rank=0, world=1, seed=42, sampler_seed=1234):
+                 device, rank=0, world=1, seed=42, sampler_seed=1234, fused=False):
         self.device = torch.device(device)
         self.rank, self.world = rank, world
         self.graph = graph
@@ -60,6 +65,9 @@ class Trainer:
         if world > 1:
             for p in self.model.parameters():   # identical start on every rank
                 dist.broadcast(p.data, 0)
+        # FusedStep re-seats w_k / w_v: build it before the optimizer sees the parameters
+        self.engine = FusedStep(self.model) if fused else None
+        self.loss_buf = torch.zeros((), device=self.device)
         self.opt = torch.optim.Adam(self.model.parameters(), lr=train_param["lr"])
         self.crit = torch.nn.BCEWithLogitsLoss()
         dv = self.device
@@ -114,33 +122,35 @@ class Trainer:
         return [DeviceBlock(v, d) for v, d in zip(views, dims)]
 
     def _allreduce_grads(self):
-        self._flat = average_gradients(list(self.model.parameters()), self.world, self._flat)
+        if self.engine is not None:          # the gradients already live in one flat buffer
+            dist.all_reduce(self.engine.flat)
+            self.engine.flat.div_(self.world)
+        else:
+            self._flat = average_gradients(list(self.model.parameters()), self.world, self._flat)
 
-    def step_device(self, roots, root_ts):
-        """One training step on device-resident roots; returns the loss tensor."""
-        self.sampler.sample_device(roots, root_ts)
-        blocks = self.blocks()
-        self.opt.zero_grad(set_to_none=False)
-        pred_pos, pred_neg = self.model(blocks, self.node_feats, self.edge_feats)
-        loss = self.crit(pred_pos, torch.ones_like(pred_pos)) + self.crit(pred_neg, torch.zeros_like(pred_neg))
-        loss.backward()
+    def _train_on(self, blocks):
+        if self.engine is not None:
+            self.engine.step(blocks, self.node_feats, self.edge_feats, self.loss_buf)
+            loss = self.loss_buf
+        else:
+            self.opt.zero_grad(set_to_none=False)
+            pred_pos, pred_neg = self.model(blocks, self.node_feats, self.edge_feats)
+            loss = self.crit(pred_pos, torch.ones_like(pred_pos)) + self.crit(pred_neg, torch.zeros_like(pred_neg))
+            loss.backward()
         if self.world > 1:
             self._allreduce_grads()
         self.opt.step()
         return loss.detach()
 
+    def step_device(self, roots, root_ts):
+        """One training step on device-resident roots; returns the loss tensor."""
+        self.sampler.sample_device(roots, root_ts)
+        return self._train_on(self.blocks())
+
     def step_host(self, roots_np, ts_np):
         """End-to-end step through the reference-facing API: host roots in, host loss out."""
         self.sampler.sample(roots_np, ts_np, [])
-        blocks = self.blocks()
-        self.opt.zero_grad(set_to_none=False)
-        pred_pos, pred_neg = self.model(blocks, self.node_feats, self.edge_feats)
-        loss = self.crit(pred_pos, torch.ones_like(pred_pos)) + self.crit(pred_neg, torch.zeros_like(pred_neg))
-        loss.backward()
-        if self.world > 1:
-            self._allreduce_grads()
-        self.opt.step()
-        return float(loss)
+        return float(self._train_on(self.blocks()))
 
 
 def batch_ranges(train_end, batch):
@@ -156,27 +166,29 @@ class GraphTrainer(Trainer):
     all-reduce of the flat gradient bucket."""
 
     def __init__(self, graph, node_feats, edge_feats, sample_param, memory_param, gnn_param, train_param,
-                 device, batch, rank=0, world=1, seed=42, sampler_seed=1234, optimizer="adam"):
+                 device, batch, rank=0, world=1, seed=42, sampler_seed=1234, optimizer="adam", fused=True):
         super().__init__(graph, node_feats, edge_feats, sample_param, memory_param, gnn_param, train_param,
-                         device, rank=rank, world=world, seed=seed, sampler_seed=sampler_seed)
+                         device, rank=rank, world=world, seed=seed, sampler_seed=sampler_seed, fused=fused)
         self.B = batch
         self.R0 = 3 * batch
         dv = self.device
         # every gradient is a view of one flat buffer: one memset clears them,
         # and the data-parallel all-reduce runs on the buffer itself
         self._params = [p for p in self.model.parameters()]
-        self._flat = torch.zeros(sum(p.numel() for p in self._params), device=dv)
-        off = 0
-        for p in self._params:
-            p.grad = self._flat[off:off + p.numel()].view_as(p)
-            off += p.numel()
+        if self.engine is not None:
+            self._flat = self.engine.flat
+        else:
+            self._flat = torch.zeros(sum(p.numel() for p in self._params), device=dv)
+            off = 0
+            for p in self._params:
+                p.grad = self._flat[off:off + p.numel()].view_as(p)
+                off += p.numel()
         if optimizer == "adam":
             self.opt = torch.optim.Adam(self._params, lr=train_param["lr"], capturable=True, fused=True)
         else:
             self.opt = torch.optim.SGD(self._params, lr=train_param["lr"])
         self.roots_buf = torch.zeros(self.R0, dtype=torch.int32, device=dv)
         self.ts_buf = torch.zeros(self.R0, dtype=torch.float32, device=dv)
-        self.loss_buf = torch.zeros((), device=dv)
         self.h_roots = torch.zeros(self.R0, dtype=torch.int32).pin_memory()
         self.h_ts = torch.zeros(self.R0, dtype=torch.float32).pin_memory()
         self.g_main = self.g_opt = None
@@ -186,6 +198,9 @@ class GraphTrainer(Trainer):
         self.sampler.sample_device(self.roots_buf, self.ts_buf)
         views = self.sampler.block_views()
         blocks = [StaticBlock(views[0], n_roots=self.R0)] + [StaticBlock(v) for v in views[1:]]
+        if self.engine is not None:
+            self.engine.step(blocks, self.node_feats, self.edge_feats, self.loss_buf)
+            return
         self._flat.zero_()
         pred_pos, pred_neg = self.model(blocks, self.node_feats, self.edge_feats)
         loss = self.crit(pred_pos, torch.ones_like(pred_pos)) + self.crit(pred_neg, torch.zeros_like(pred_neg))

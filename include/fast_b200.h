@@ -223,6 +223,12 @@ int fb_time_encode_bwd(const float *g, int64_t ldg, const float *dt, const float
 int fb_gemm_nt(const float *A, int64_t lda, const float *B, int64_t ldb, const float *bias,
                float *C, int64_t ldc, int64_t M, const int32_t *M_dev, int N, int K,
                int accumulate, cudaStream_t stream);
+/* C[m, n] = sum_k A[m,k] B[k,n] (+ bias[n]) (+ C when accumulate)   "NN"
+ * B stored [K, N] (ldb >= N): the input gradient dX = dY W of a Linear layer
+ * without transposing W. */
+int fb_gemm_nn(const float *A, int64_t lda, const float *B, int64_t ldb, const float *bias,
+               float *C, int64_t ldc, int64_t M, const int32_t *M_dev, int N, int K,
+               int accumulate, cudaStream_t stream);
 /* Same contract as fb_gemm_nt on the tcgen05 tensor cores: TMA-fed 128 x N
  * tiles, fp32 accuracy from three TF32 products per term (Ootomo & Yokota's
  * hi/lo split, computed in shared memory), accumulation in tensor memory.
@@ -242,10 +248,54 @@ size_t fb_gemm_tn_ws_bytes(int64_t M, int N, int K);
 int fb_gemm_tn(const float *G, int64_t ldg, const float *X, int64_t ldx, float *C, int64_t ldc,
                int64_t M, const int32_t *M_dev, int N, int K, int accumulate, void *ws,
                cudaStream_t stream);
+/* fb_gemm_tn plus the bias gradient in the same pass: db[n] (+)= sum_m G[m, n]
+ * (X gets a virtual column of ones).  db_accumulate applies to db alone. */
+int fb_gemm_tn_bias(const float *G, int64_t ldg, const float *X, int64_t ldx, float *C, int64_t ldc,
+                    int64_t M, const int32_t *M_dev, int N, int K, int accumulate, float *db,
+                    int db_accumulate, void *ws, cudaStream_t stream);
 /* db[n] (+)= sum_m G[m, n]; deterministic.  ws: fb_colsum_ws_bytes(M, N). */
 size_t fb_colsum_ws_bytes(int64_t M, int N);
 int fb_colsum(const float *G, int64_t ldg, float *db, int64_t M, const int32_t *M_dev, int N,
               int accumulate, void *ws, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Layer tail and edge predictor (layers.py:213-223, layers.py:31-50,        */
+/* train.py:205-206).                                                         */
+/* ------------------------------------------------------------------------- */
+/* y = relu(dropout(z)), out = LayerNorm(y; gamma, beta, eps) per row.  Rows at
+ * or past the count (n_rows_dev overrides n_rows) get out = 0, and so do all
+ * rows when gate_dev is given and *gate_dev == 0 (a block without edges
+ * outputs zeros, layers.py:101-102; the backward then gives dz = 0).  Dropout keeps a
+ * value when u >= drop_p, u from Philox keyed by (seed, offset or *offset_dev),
+ * or from mask_u [n_rows, dim] when given; kept values scale by 1/(1-p).
+ * dim % 4 == 0, dim <= 512, 16-byte aligned rows. */
+int fb_layer_tail_fwd(const float *z, int64_t ldz, const float *gamma, const float *beta, float eps,
+                      float drop_p, uint64_t seed, uint64_t offset, const int64_t *offset_dev,
+                      const float *mask_u, float *y, int64_t ldy, float *out, int64_t ldo, int64_t n_rows,
+                      const int32_t *n_rows_dev, const int32_t *gate_dev, int dim, cudaStream_t stream);
+/* Backward from dout and the saved y: dz, and dgamma += sum dout*xhat,
+ * dbeta += sum dout (deterministic).  ws: fb_layer_tail_bwd_ws_bytes. */
+size_t fb_layer_tail_bwd_ws_bytes(int64_t n_rows, int dim);
+int fb_layer_tail_bwd(const float *dout, int64_t lddo, const float *y, int64_t ldy, const float *gamma,
+                      float eps, float drop_p, float *dz, int64_t lddz, float *dgamma, float *dbeta,
+                      int64_t n_rows, const int32_t *n_rows_dev, const int32_t *gate_dev, int dim, void *ws,
+                      cudaStream_t stream);
+/* EdgePredictor scores and BCE-with-logits loss, forward and backward:
+ * S = src_fc(h_src) [B, dim], P = dst_fc([h_pos; h_neg]) [2B, dim];
+ * x = relu(S_i + P_.) . w_o + b_o;  *loss = mean bce(x_pos, 1) + mean bce(x_neg, 0);
+ * writes dS, dP; dw_o += ..., *db_o += ...; scores [2B] optional.  Deterministic;
+ * ws: fb_edge_predictor_loss_ws_bytes(B, dim) bytes. */
+size_t fb_edge_predictor_loss_ws_bytes(int64_t B, int dim);
+int fb_edge_predictor_loss(const float *S, int64_t lds, const float *P, int64_t ldp, const float *w_o,
+                           const float *b_o, int64_t B, int dim, float *loss, float *dS, int64_t ldds,
+                           float *dP, int64_t lddp, float *dw_o, float *db_o, float *scores, void *ws,
+                           cudaStream_t stream);
+/* Q-side gradients that depend on v = sum over rows of dQ only:
+ * db_q += v; db_t[c] -= sin(b_t[c]) sum_j v[j] W_q[j, dn + c]; and with qin0
+ * (the single shared Q input row) dW_q[j, c] += v[j] qin0[c]. */
+int fb_q_time_bwd(const float *v, int D, const float *W_q, int64_t ldwq, int dn, int dtime,
+                  const float *b_t, const float *qin0, float *dW_q, int64_t lddwq, float *db_q,
+                  float *db_t, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -30,11 +30,14 @@ def _setup(cuda, t_max, strategy="uniform", att_dropout=0.2):
     return cfg, g, ef, sp, mp, gp, tp
 
 
-def test_graph_replay_is_the_static_eager_step(cuda):
+@pytest.mark.parametrize("fused", [True, False])
+def test_graph_replay_is_the_static_eager_step(cuda, fused):
     from fast_b200.train import GraphTrainer
     cfg, g, ef, sp, mp, gp, tp = _setup(cuda, 1e5)
+    if fused:
+        tp["dropout"] = 0.1            # keyed by the model's device counter, replay-safe
     mk = lambda: GraphTrainer(g, None, ef, dict(sp), mp, dict(gp), tp, cuda, batch=cfg.batch, seed=5,
-                              sampler_seed=77, optimizer="sgd")
+                              sampler_seed=77, optimizer="sgd", fused=fused)
     graph, static = mk(), mk()
     B = cfg.batch
     starts = [10000 + i * B for i in range(7)]
@@ -56,14 +59,17 @@ def test_graph_replay_is_the_static_eager_step(cuda):
         assert torch.equal(pg, ps), n
 
 
+@pytest.mark.parametrize("fused", [True, False])
 @pytest.mark.parametrize("strategy", ["recent", "uniform"])
-def test_graph_trainer_matches_eager_trainer(cuda, strategy):
+def test_graph_trainer_matches_eager_trainer(cuda, strategy, fused):
     from fast_b200.train import GraphTrainer, Trainer
     cfg, g, ef, sp, mp, gp, tp = _setup(cuda, 2e3, strategy)
-    eager = Trainer(g, None, ef, dict(sp), mp, dict(gp), tp, cuda, seed=5, sampler_seed=77)
+    if fused:
+        tp["dropout"] = 0.1            # same Philox-keyed tail dropout on both paths
+    eager = Trainer(g, None, ef, dict(sp), mp, dict(gp), tp, cuda, seed=5, sampler_seed=77, fused=fused)
     eager.opt = torch.optim.SGD(eager.model.parameters(), lr=tp["lr"])
     graph = GraphTrainer(g, None, ef, dict(sp), mp, dict(gp), tp, cuda, batch=cfg.batch, seed=5, sampler_seed=77,
-                         optimizer="sgd")
+                         optimizer="sgd", fused=fused)
     B = cfg.batch
     starts = [10000 + i * B for i in range(7)]
     graph.load_device_roots(starts[0], starts[0] + B)

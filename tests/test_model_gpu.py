@@ -51,8 +51,13 @@ def _check(name, dev, r64, r32, report):
     return elem_ok or norm_ok
 
 
+@pytest.mark.parametrize("path", ["autograd", "fused"])
 @pytest.mark.parametrize("case", sorted(CASES))
-def test_train_step_matches_oracle(cuda, case):
+def test_train_step_matches_oracle(cuda, case, path):
+    """path: the GeneralModel module under torch autograd (attention core on
+    the device kernels), or FusedStep (the whole step on the device kernels
+    with a hand-derived backward)."""
+    from fast_b200.engine import FusedStep
     from fast_b200.ext import sampler_core
     from fast_b200.model import DeviceBlock, GeneralModel
     layers, fanout, dn, de = CASES[case]
@@ -67,6 +72,7 @@ def test_train_step_matches_oracle(cuda, case):
     m32 = GeneralModel(dn, de, sp, dict(type="none", dim_out=0), gnn, tr)
     m64 = copy.deepcopy(m32).double()
     m_gpu = copy.deepcopy(m32).to(cuda)
+    eng = FusedStep(m_gpu) if path == "fused" else None
     crit = torch.nn.BCEWithLogitsLoss()
     dev = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
     smp = sampler_core.ParallelSampler(dev(g["indptr"]), dev(g["indices"]), dev(g["eid"]), dev(g["ts"]), 1, 1,
@@ -84,10 +90,16 @@ def test_train_step_matches_oracle(cuda, case):
         smp.sample_device(dev(roots), dev(rts))
         blocks = [DeviceBlock(v, d) for v, d in zip(smp.block_views(), smp.dims())]
         ora.sample(roots, rts)
-        m_gpu.zero_grad()
-        pp, pn = m_gpu(blocks, nf_d, ef_d)
-        loss_g = crit(pp, torch.ones_like(pp)) + crit(pn, torch.zeros_like(pn))
-        loss_g.backward()
+        if eng is None:
+            m_gpu.zero_grad()
+            pp, pn = m_gpu(blocks, nf_d, ef_d)
+            loss_g = crit(pp, torch.ones_like(pp)) + crit(pn, torch.zeros_like(pn))
+            loss_g.backward()
+        else:
+            loss_g = torch.zeros((), device=cuda)
+            scores = torch.empty(2 * B, device=cuda)
+            eng.step(blocks, nf_d, ef_d, loss_g, scores=scores)
+            pp, pn = scores[:B].view(-1, 1), scores[B:].view(-1, 1)
         outs = {}
         for tag, m in (("32", m32), ("64", m64)):
             m.zero_grad()
