@@ -248,8 +248,9 @@ def run_fast(args):
     def dev_step(i):
         b0, b1 = i * gB, (i + 1) * gB
         if args.eager:
-            roots, rts = tr.device_roots(b0, b1)
-            return tr.step_device(roots, rts)
+            groots, gts = tr.batch_roots(b0, b1)
+            roots, rts = tr.local_of(groots, gts)
+            return tr.step_device(roots, rts, groots, gts)
         tr.load_device_roots(b0, b1)
         return tr.step_device()
 
@@ -303,11 +304,14 @@ def run_fast(args):
     t0 = time.perf_counter()
     for i in timed:
         b0, b1 = i * gB, (i + 1) * gB
-        lo, hi = tr.local_slice(b0, b1)
-        t_np = graph.ts[lo:hi]
-        roots = np.concatenate([graph.src[lo:hi], graph.dst[lo:hi],
-                                rng.integers(0, graph.n_nodes, hi - lo).astype(np.int32)])
-        tr.step_host(roots, np.concatenate([t_np, t_np, t_np]).astype(np.float32))
+        # the global batch [src | dst | neg] (same rng seed on every rank), then this rank's slice
+        t_np = graph.ts[b0:b1]
+        groots = np.concatenate([graph.src[b0:b1], graph.dst[b0:b1],
+                                 rng.integers(0, graph.n_nodes, gB).astype(np.int32)])
+        gts = np.concatenate([t_np, t_np, t_np]).astype(np.float32)
+        lo = tr.rank * B
+        sel = np.concatenate([np.arange(lo, lo + B), gB + np.arange(lo, lo + B), 2 * gB + np.arange(lo, lo + B)])
+        tr.step_host(groots[sel], gts[sel], groots, gts)
     torch.cuda.synchronize()
     e2e_s = torch.tensor([time.perf_counter() - t0], device=dev)
     if world > 1:
@@ -323,8 +327,9 @@ def run_fast(args):
     args.profile_steps = max(1, min(args.profile_steps, len(timed)))
     prof = [timed[(2 * j + 1) * len(timed) // (2 * args.profile_steps)] for j in range(args.profile_steps)]
     for i in prof:
-        roots, rts = tr.device_roots(i * gB, (i + 1) * gB)
-        Trainer.step_device(tr, roots, rts)
+        groots, gts = tr.batch_roots(i * gB, (i + 1) * gB)
+        roots, rts = tr.local_of(groots, gts)
+        Trainer.step_device(tr, roots, rts, groots, gts)
     kern = ops.TIMER.summary()
     ops.TIMER = None
 
@@ -366,7 +371,8 @@ def run_fast(args):
                    "gemm": args.gemm, "step": args.path,
                    "l2": "inputs larger than L2 (%.1f GB edge-feature table gathered at random rows)" %
                          (cfg.edges * cfg.d_edge * 4 / 1e9)},
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": world * 3 * B * 8,
+        "e2e": {"value": e2e_value, "unit": UNIT,
+                "h2d_bytes_per_step": world * 3 * B * 8 + (world * world * 3 * B * 8 if world > 1 else 0),
                 "d2h_bytes_per_step": world * 4},
         "gpu_launches": int(launches),
         "roofline": roof,

@@ -41,6 +41,7 @@ _SIGS = {
     "fb_sampler_destroy": (_I, [_P]),
     "fb_sampler_reset": (_I, [_P, _P]),
     "fb_sampler_sample": (_I, [_P, _P, _P, _I64, _I, _P]),
+    "fb_sampler_update_pointers": (_I, [_P, _P, _P, _I64, _P]),
     "fb_sampler_num_blocks": (_I, [_P]),
     "fb_sampler_block": (_I, [_P, _I, _P]),
     "fb_sampler_dims": (_I, [_P, _P, _P]),

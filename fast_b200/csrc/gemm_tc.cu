@@ -24,7 +24,7 @@
 // the CTA records an error, stops issuing work, drains what it already issued
 // (again bounded), frees its tensor memory and exits.
 //
-// TMA loads here never use cluster multicast.
+// Every TMA load here is issued by one CTA for its own shared memory.
 #include <cuda.h>
 #include <algorithm>
 #include "runtime.cuh"

@@ -571,6 +571,28 @@ extern "C" int fb_sampler_sample(fb_sampler *s, const int32_t *roots, const floa
   return FB_OK;
 }
 
+extern "C" int fb_sampler_update_pointers(fb_sampler *s, const int32_t *roots, const float *root_ts, int64_t n_roots,
+                                          cudaStream_t st) {
+  if (!s || n_roots < 0 || (n_roots > 0 && (!roots || !root_ts)))
+    return fb::set_error(FB_ERR_ARG, "fb_sampler_update_pointers: bad argument");
+  if (n_roots == 0) return FB_OK;
+  // the first layer's pointer updates of sample(), for these roots only
+  const int nh = s->num_history;
+  k_update_ptr<<<nblk(n_roots), kThreads, 0, st>>>(s->indptr, s->ts, s->n_nodes, s->ts_ptr + (int64_t)nh * s->n_nodes,
+                                                    roots, root_ts, n_roots, nullptr, 0.f, s->err);
+  FB_LAUNCHED("k_update_ptr");
+  for (int i = 0; i < nh; ++i) {
+    const float offset = (float)(-i) * s->wd;
+    if (fabsf(s->wd) > 1e-7f) {
+      k_update_ptr<<<nblk(n_roots), kThreads, 0, st>>>(s->indptr, s->ts, s->n_nodes,
+                                                        s->ts_ptr + (int64_t)(nh - 1 - i) * s->n_nodes, roots,
+                                                        root_ts, n_roots, nullptr, offset - s->wd, s->err);
+      FB_LAUNCHED("k_update_ptr");
+    }
+  }
+  return FB_OK;
+}
+
 extern "C" int fb_sampler_num_blocks(const fb_sampler *s) {
   return s ? s->num_layers * s->num_history : 0;
 }

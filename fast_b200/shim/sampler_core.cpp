@@ -159,6 +159,18 @@ class Sampler {
                             cur_stream()));
   }
 
+  // Pointer updates of the first layer for (global) device roots, no sampling.
+  void update_pointers(torch::Tensor roots, torch::Tensor root_ts) {
+    TORCH_CHECK(roots.is_cuda() && root_ts.is_cuda() && roots.is_contiguous() && root_ts.is_contiguous(),
+                "update_pointers wants contiguous CUDA tensors");
+    TORCH_CHECK(roots.scalar_type() == torch::kInt32 && root_ts.scalar_type() == torch::kFloat32,
+                "roots int32, ts float32");
+    TORCH_CHECK(roots.numel() == root_ts.numel(), "roots and ts differ in length");
+    const c10::cuda::CUDAGuard g(h->device);
+    check(fb_sampler_update_pointers(h->s, roots.data_ptr<int32_t>(), root_ts.data_ptr<float>(), roots.numel(),
+                                     cur_stream()));
+  }
+
   std::vector<std::vector<int32_t>> dims() {
     const c10::cuda::CUDAGuard g(h->device);
     const int nb = fb_sampler_num_blocks(h->s);
@@ -283,6 +295,7 @@ PYBIND11_MODULE(sampler_core, m) {
       .def("sample", &Sampler::sample, py::arg("root_nodes"), py::arg("root_ts"),
            py::arg("csrFlag") = std::vector<int>())
       .def("sample_device", &Sampler::sample_device)
+      .def("update_pointers", &Sampler::update_pointers)
       .def("reset", &Sampler::reset)
       .def("get_ret", &Sampler::get_ret)
       .def("dims", &Sampler::dims)

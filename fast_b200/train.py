@@ -96,7 +96,7 @@ class Trainer:
             use_ptr = first or sp["strategy"] == "recent" or (sp["prop_time"] and sp["history"] == 1)
             first = False
             n += (1 if use_ptr else 0) + 3 * sp["history"]
-        return n + 1   # the device call-counter bump
+        return n + 1 + (1 if self.world > 1 else 0)   # the call-counter bump (+ the global pointer update)
 
     def reset_epoch(self):
         self.sampler.reset()
@@ -106,14 +106,28 @@ class Trainer:
         """Contiguous slice of the global batch [b0, b1) owned by this rank."""
         return slice_for_rank(b0, b1, self.rank, self.world)
 
-    def device_roots(self, b0, b1):
-        lo, hi = self.local_slice(b0, b1)
-        n = hi - lo
-        neg = torch.randint(0, self.graph.n_nodes, (n,), device=self.device, generator=self.neg_gen,
+    def batch_roots(self, b0, b1):
+        """Roots [src | dst | neg] and times of the global batch [b0, b1)
+        (train.py:182-183).  The negatives come from a generator seeded
+        identically on every rank, so all ranks hold the same global list."""
+        neg = torch.randint(0, self.graph.n_nodes, (b1 - b0,), device=self.device, generator=self.neg_gen,
                             dtype=torch.int32)
-        roots = torch.cat([self.src[lo:hi], self.dst[lo:hi], neg])
-        t = self.ts[lo:hi]
-        return roots, torch.cat([t, t, t])
+        t = self.ts[b0:b1]
+        return torch.cat([self.src[b0:b1], self.dst[b0:b1], neg]), torch.cat([t, t, t])
+
+    def local_of(self, roots, ts):
+        """This rank's roots [src_r | dst_r | neg_r] of a global [src | dst | neg] list."""
+        if self.world == 1:
+            return roots, ts
+        g = roots.shape[0] // 3
+        per = g // self.world
+        lo = self.rank * per
+        pick = lambda a: torch.cat([a[lo:lo + per], a[g + lo:g + lo + per], a[2 * g + lo:2 * g + lo + per]])
+        return pick(roots), pick(ts)
+
+    def device_roots(self, b0, b1):
+        """This rank's roots and times of the global batch [b0, b1)."""
+        return self.local_of(*self.batch_roots(b0, b1))
 
     # -- step -----------------------------------------------------------------
     def blocks(self):
@@ -142,13 +156,20 @@ class Trainer:
         self.opt.step()
         return loss.detach()
 
-    def step_device(self, roots, root_ts):
-        """One training step on device-resident roots; returns the loss tensor."""
+    def step_device(self, roots, root_ts, global_roots=None, global_ts=None):
+        """One training step on device-resident roots; returns the loss tensor.
+        With several ranks, the global batch's roots first advance the time
+        pointers, as one process training on the whole batch would."""
+        if self.world > 1 and global_roots is not None:
+            self.sampler.update_pointers(global_roots, global_ts)
         self.sampler.sample_device(roots, root_ts)
         return self._train_on(self.blocks())
 
-    def step_host(self, roots_np, ts_np):
+    def step_host(self, roots_np, ts_np, global_roots_np=None, global_ts_np=None):
         """End-to-end step through the reference-facing API: host roots in, host loss out."""
+        if self.world > 1 and global_roots_np is not None:
+            self.sampler.update_pointers(torch.from_numpy(global_roots_np).to(self.device),
+                                         torch.from_numpy(global_ts_np).to(self.device))
         self.sampler.sample(roots_np, ts_np, [])
         return float(self._train_on(self.blocks()))
 
@@ -189,12 +210,19 @@ class GraphTrainer(Trainer):
             self.opt = torch.optim.SGD(self._params, lr=train_param["lr"])
         self.roots_buf = torch.zeros(self.R0, dtype=torch.int32, device=dv)
         self.ts_buf = torch.zeros(self.R0, dtype=torch.float32, device=dv)
+        # the global batch's roots (every rank's), for the time-pointer update
+        self.groots_buf = torch.zeros(self.R0 * world, dtype=torch.int32, device=dv) if world > 1 else None
+        self.gts_buf = torch.zeros(self.R0 * world, dtype=torch.float32, device=dv) if world > 1 else None
+        self.h_groots = torch.zeros(self.R0 * world, dtype=torch.int32).pin_memory() if world > 1 else None
+        self.h_gts = torch.zeros(self.R0 * world, dtype=torch.float32).pin_memory() if world > 1 else None
         self.h_roots = torch.zeros(self.R0, dtype=torch.int32).pin_memory()
         self.h_ts = torch.zeros(self.R0, dtype=torch.float32).pin_memory()
         self.g_main = self.g_opt = None
 
     # the body of one step on the static input buffers
     def _fwd_bwd(self):
+        if self.world > 1:
+            self.sampler.update_pointers(self.groots_buf, self.gts_buf)
         self.sampler.sample_device(self.roots_buf, self.ts_buf)
         views = self.sampler.block_views()
         blocks = [StaticBlock(views[0], n_roots=self.R0)] + [StaticBlock(v) for v in views[1:]]
@@ -247,37 +275,44 @@ class GraphTrainer(Trainer):
             self.g_opt.replay()
 
     def load_device_roots(self, b0, b1):
-        """Fills the input buffers with this rank's slice of the global batch [b0, b1)."""
-        lo, hi = self.local_slice(b0, b1)
-        B = hi - lo
-        assert B == self.B, "graph was captured for a local batch of %d" % self.B
-        self.roots_buf[:B].copy_(self.src[lo:hi])
-        self.roots_buf[B:2 * B].copy_(self.dst[lo:hi])
-        torch.randint(0, self.graph.n_nodes, (B,), device=self.device, generator=self.neg_gen,
-                      out=self.roots_buf[2 * B:])
-        t = self.ts[lo:hi]
-        self.ts_buf[:B].copy_(t)
-        self.ts_buf[B:2 * B].copy_(t)
-        self.ts_buf[2 * B:].copy_(t)
+        """Fills the input buffers with this rank's slice of the global batch
+        [b0, b1) (and, with several ranks, the global roots)."""
+        assert (b1 - b0) // self.world == self.B, "graph was captured for a local batch of %d" % self.B
+        groots, gts = self.batch_roots(b0, b1)
+        roots, ts = self.local_of(groots, gts)
+        self.roots_buf.copy_(roots)
+        self.ts_buf.copy_(ts)
+        if self.world > 1:
+            self.groots_buf.copy_(groots)
+            self.gts_buf.copy_(gts)
 
-    def step_device(self, roots=None, root_ts=None):
+    def step_device(self, roots=None, root_ts=None, global_roots=None, global_ts=None):
         """One replayed step on the device-resident input buffers (or the given
         device tensors); returns the loss tensor (no host round trip)."""
         if roots is not None:
             self.roots_buf.copy_(roots)
             self.ts_buf.copy_(root_ts)
+        if global_roots is not None and self.world > 1:
+            self.groots_buf.copy_(global_roots)
+            self.gts_buf.copy_(global_ts)
         if self.g_main is None:
             self.capture()
         self._replay()
         return self.loss_buf
 
-    def step_host(self, roots_np, ts_np):
+    def step_host(self, roots_np, ts_np, global_roots_np=None, global_ts_np=None):
         """End-to-end step: host roots -> pinned staging -> device buffers ->
         replay -> loss read back to the host."""
         self.h_roots.numpy()[:] = roots_np
         self.h_ts.numpy()[:] = ts_np
         self.roots_buf.copy_(self.h_roots, non_blocking=True)
         self.ts_buf.copy_(self.h_ts, non_blocking=True)
+        if self.world > 1:
+            assert global_roots_np is not None, "several ranks: pass the global batch's roots too"
+            self.h_groots.numpy()[:] = global_roots_np
+            self.h_gts.numpy()[:] = global_ts_np
+            self.groots_buf.copy_(self.h_groots, non_blocking=True)
+            self.gts_buf.copy_(self.h_gts, non_blocking=True)
         if self.g_main is None:
             self.capture()
         self._replay()

@@ -85,6 +85,12 @@ int fb_sampler_reset(fb_sampler *s, cudaStream_t stream);
  * synchronises the device) when n_roots exceeds every earlier call. */
 int fb_sampler_sample(fb_sampler *s, const int32_t *roots, const float *root_ts, int64_t n_roots,
                       int roots_on_device, cudaStream_t stream);
+/* Applies the first layer's pointer updates of sample() (update_ts_ptr,
+ * :133-157) for device roots without sampling.  Data-parallel ranks call it
+ * with the global batch's roots before sampling their own slice, so every
+ * rank's time pointers equal the single-process ones (a max is idempotent). */
+int fb_sampler_update_pointers(fb_sampler *s, const int32_t *roots, const float *root_ts, int64_t n_roots,
+                               cudaStream_t stream);
 /* Number of blocks from the last sample() (= num_layers * num_history), in
  * the reference's get_ret() order. */
 int fb_sampler_num_blocks(const fb_sampler *s);

@@ -1,0 +1,99 @@
+"""GPU, two NCCL ranks (skipped with fewer than two GPUs): data-parallel
+training with the CUDA-graph trainer equals single-process training on the
+global batch.
+
+Each rank replays its captured step on a contiguous slice of every global
+batch, after advancing its time pointers with the global batch's roots
+(fb_sampler_update_pointers) and with the global negative list drawn from a
+generator seeded alike on every rank; gradients are averaged with one NCCL
+all-reduce of the flat gradient buffer.  With recent sampling and one layer
+the sampled blocks are then exactly the single process's, so losses and
+parameters agree to fp32 rounding.  (With two or more recent layers the
+deeper layers' pointer updates see only the rank's own hop-1 nodes.)
+"""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _setup(dev):
+    sys.path.insert(0, ROOT)
+    from fast_b200.data import WorkloadConfig, make_graph
+    cfg = WorkloadConfig("small", 400, 40000, ("zipf", 1.1), ("uniform",), 2e3, False, 0, 48, "normal", "TGAT",
+                         "recent", (8,), 64)
+    g = make_graph(cfg, seed=3)
+    ef = torch.randn(cfg.edges, cfg.d_edge, generator=torch.Generator().manual_seed(1)).to(dev)
+    sp = dict(layer=1, neighbor=[8], strategy="recent", prop_time=False, history=1, duration=0)
+    mp_ = dict(type="none", dim_out=0)
+    gp = dict(arch="transformer_attention", layer=1, att_head=2, dim_time=100, dim_out=100)
+    tp = dict(lr=1e-3, dropout=0.0, att_dropout=0.0)
+    return cfg, g, ef, sp, mp_, gp, tp
+
+
+STEPS = [10000 + 128 * i for i in range(5)]
+
+
+def _run(tr, gB):
+    losses = []
+    for b0 in STEPS:
+        tr.load_device_roots(b0, b0 + gB)
+        losses.append(float(tr.step_device()))
+    return losses
+
+
+def _worker(rank, world, port, outdir):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from fast_b200.train import GraphTrainer
+        cfg, g, ef, sp, mp_, gp, tp = _setup(dev)
+        gB = 128
+        tr = GraphTrainer(g, None, ef, sp, mp_, dict(gp), tp, dev, batch=gB // world, rank=rank, world=world,
+                          seed=5, sampler_seed=77, optimizer="sgd")
+        losses = _run(tr, gB)
+        t = torch.tensor(losses, device=dev)
+        dist.all_reduce(t)
+        params = torch.cat([p.detach().reshape(-1) for p in tr.model.parameters()]).cpu()
+        tr.g_main = tr.g_opt = None          # release graphs before tearing down NCCL
+        torch.cuda.synchronize()
+        if rank == 0:
+            np.save(os.path.join(outdir, "dp_loss.npy"), (t / world).cpu().numpy())
+            np.save(os.path.join(outdir, "dp_params.npy"), params.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_dp_two_ranks_equal_single_process(tmp_path):
+    import torch.multiprocessing as mp
+    mp.spawn(_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
+    from fast_b200.train import GraphTrainer
+    dev = torch.device("cuda", 0)
+    cfg, g, ef, sp, mp_, gp, tp = _setup(dev)
+    tr = GraphTrainer(g, None, ef, sp, mp_, dict(gp), tp, dev, batch=128, seed=5, sampler_seed=77, optimizer="sgd")
+    single = np.array(_run(tr, 128))
+    params = torch.cat([p.detach().reshape(-1) for p in tr.model.parameters()]).cpu().numpy()
+    dp = np.load(tmp_path / "dp_loss.npy")
+    dp_params = np.load(tmp_path / "dp_params.npy")
+    np.testing.assert_allclose(dp, single, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(dp_params, params, rtol=1e-4, atol=1e-6)
