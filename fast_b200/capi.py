@@ -86,6 +86,23 @@ _SIGS = {
     "fb_q_time_bwd": (_I, [_P, _I, _P, _I64, _I, _I, _P, _P, _P, _I64, _P, _P, _P]),
 }
 
+class GemmProblem(ctypes.Structure):
+    """fb_gemm_problem (include/fast_b200.h)."""
+    _fields_ = [("kind", ctypes.c_int),
+                ("A", ctypes.c_void_p), ("lda", ctypes.c_int64),
+                ("A2", ctypes.c_void_p), ("lda2", ctypes.c_int64), ("k1", ctypes.c_int),
+                ("B", ctypes.c_void_p), ("ldb", ctypes.c_int64),
+                ("bias", ctypes.c_void_p),
+                ("C", ctypes.c_void_p), ("ldc", ctypes.c_int64),
+                ("M", ctypes.c_int64), ("M_dev", ctypes.c_void_p),
+                ("N", ctypes.c_int), ("K", ctypes.c_int),
+                ("accumulate", ctypes.c_int),
+                ("db", ctypes.c_void_p), ("db_accumulate", ctypes.c_int)]
+
+
+_SIGS["fb_gemm_group_ws_bytes"] = (_SZ, [ctypes.POINTER(GemmProblem), _I])
+_SIGS["fb_gemm_group"] = (_I, [ctypes.POINTER(GemmProblem), _I, _P, _SZ, _P])
+
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(lib, _name)
     _fn.restype = _res

@@ -15,6 +15,7 @@
 // fully coalesced warp load.  Reductions stay inside the warp: no atomics,
 // results are bit-identical run to run.
 #include <cfloat>
+#include <cstdlib>
 #include "runtime.cuh"
 
 namespace {
@@ -402,6 +403,340 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta, MinCtas<NV>::value) k_attn_
   }
 }
 
+// ---------------------------------------------------------------------------
+// Short-segment kernels (rows of <= 128 floats, logits from q.k).  A
+// destination's edges go in groups of G = min(16, 32 / H) (H = heads rounded
+// up to a power of two), so G x H <= 32 (edge, head) pairs: after one
+// transposed warp reduction every lane owns the total of one pair.  Per
+// group the K rows are loaded in one round trip (and then the V rows), the
+// G x H dot products cost G x H - 1 + 5 - log2(G x H) shuffles together, and
+// softmax statistics are reduced over the lanes owning one head.  Fan-outs up
+// to 16 are a single group.
+
+template <int HP, int GG = (HP == 1 ? 16 : 32 / HP)>
+struct SGeom {
+  static constexpr int G = GG;                                     // edges per group
+  static constexpr int V = G * HP;                                 // (edge, head) pairs per group (<= 32)
+  static constexpr int K = V == 8 ? 3 : (V == 16 ? 4 : 5);         // log2 V
+  static constexpr int S = 5 - K;                                  // lanes per pair = 2^S
+  static constexpr int LH = HP == 1 ? 0 : (HP == 2 ? 1 : 2);       // log2 HP
+};
+
+// In: per-lane partial sums v[0..V).  Returns the warp total of pair
+// lane >> (5 - log2 V).  Each butterfly step keeps half of the values and
+// trades the other half with the partner lane.
+template <int V>
+__device__ __forceinline__ float xreduce_own(float (&v)[V], int lane) {
+  constexpr int k = V == 8 ? 3 : (V == 16 ? 4 : 5);
+#pragma unroll
+  for (int st = 0; st < k; ++st) {
+    const int off = 16 >> st, half = V >> (st + 1);
+    const bool up = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      const float send = up ? v[i] : v[i + half];
+      const float keep = up ? v[i + half] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  float t = v[0];
+#pragma unroll
+  for (int off = 16 >> k; off >= 1; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+  return t;
+}
+
+// Sum / max over the lanes that own the same head (over the edge bits).
+template <class SG>
+__device__ __forceinline__ float head_sum(float x) {
+#pragma unroll
+  for (int off = 1 << (SG::S + SG::LH); off < 32; off <<= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+  return x;
+}
+template <class SG>
+__device__ __forceinline__ float head_max(float x) {
+#pragma unroll
+  for (int off = 1 << (SG::S + SG::LH); off < 32; off <<= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
+  return x;
+}
+// Value of pair (c, h) from its owner lanes.
+template <class SG, int HP>
+__device__ __forceinline__ float pair_val(float x, int c, int h) {
+  return __shfl_sync(0xffffffffu, x, (c * HP + h) << SG::S);
+}
+// The four per-component values of a row given per-head values (lane's heads hs).
+template <int HP>
+__device__ __forceinline__ float4 by_head(const float (&vh)[HP], const int (&hs)[4]) {
+  float r[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    r[c] = 0.f;
+#pragma unroll
+    for (int h = 0; h < HP; ++h)
+      if (hs[c] == h) r[c] = vh[h];
+  }
+  return make_float4(r[0], r[1], r[2], r[3]);
+}
+
+// Per-head partial dot products of the lane's 4 components.
+template <int HP>
+__device__ __forceinline__ void head_partials(const float4 &a, const float4 &b, const int (&hs)[4],
+                                              float (&out)[HP]) {
+#pragma unroll
+  for (int h = 0; h < HP; ++h) out[h] = 0.f;
+  const float p[4] = {a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w};
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int h = 0; h < HP; ++h)
+      if (hs[c] == h) out[h] += p[c];
+}
+
+// Dropout scale (0 or 1/(1-p)) of (edge e, head h): the decisions of drop_scale().
+__device__ __forceinline__ float keep_scale(const AttnArgs &a, uint64_t doff, int64_t e, int h, float inv_keep) {
+  if (a.drop_p <= 0.f) return 1.f;
+  if (a.mask_u) return a.mask_u[e * a.heads + h] > a.drop_p ? inv_keep : 0.f;
+  fb::Philox4 r = fb::philox4x32_10((uint32_t)e, (uint32_t)(e >> 32), (uint32_t)doff, (uint32_t)(doff >> 32),
+                                    (uint32_t)a.seed, (uint32_t)(a.seed >> 32));
+  const uint32_t bits = h == 0 ? r.v[0] : (h == 1 ? r.v[1] : (h == 2 ? r.v[2] : r.v[3]));
+  return (float)(bits >> 8) * (1.0f / 16777216.0f) >= a.drop_p ? inv_keep : 0.f;
+}
+
+template <int G>
+__device__ __forceinline__ void load_rows(const float *base, int64_t ld, int g0, int n, int lane, bool live,
+                                          float4 (&r)[G]) {
+#pragma unroll
+  for (int c = 0; c < G; ++c)
+    r[c] = (c < n && live) ? __ldg(reinterpret_cast<const float4 *>(base + (int64_t)(g0 + c) * ld) + lane)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+template <int HP>
+__global__ void __launch_bounds__(32 * kWarpsPerCta, 2) k_attn_fwd_s(AttnArgs a) {
+  using SG = SGeom<HP, 8>;      // K and V rows of 8 edges in flight together
+  constexpr int G = SG::G, V = SG::V;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t n_dst = a.n_dst_dev ? min((int64_t)(*a.n_dst_dev), a.n_dst) : a.n_dst;
+  RowGeom geo{a.dim / 4, a.dim / a.heads, a.heads};
+  int hsel1[1][4];
+  lane_heads<1>(geo, lane, hsel1);
+  const int hs[4] = {hsel1[0][0], hsel1[0][1], hsel1[0][2], hsel1[0][3]};
+  const uint64_t doff = a.offset_dev ? *a.offset_dev : a.offset;
+  const float inv_keep = a.drop_p > 0.f ? 1.f / (1.f - a.drop_p) : 1.f;
+  const bool live = lane < geo.nv4;
+  const int own = lane >> SG::S, oc = own >> SG::LH, oh = own & (HP - 1);
+  const bool writer = (lane & ((1 << SG::S) - 1)) == 0;
+  const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (a.n_dst_dev) {
+    for (int64_t j = n_dst + (int64_t)blockIdx.x * kWarpsPerCta + w; j < a.n_dst;
+         j += (int64_t)gridDim.x * kWarpsPerCta)
+      if (live) reinterpret_cast<float4 *>(a.agg + j * a.ldagg)[lane] = zero4;
+  }
+  for (int64_t j = (int64_t)blockIdx.x * kWarpsPerCta + w; j < n_dst; j += (int64_t)gridDim.x * kWarpsPerCta) {
+    const int beg = a.rptr[j], end = a.rptr[j + 1];
+    float4 acc = zero4;
+    if (end > beg) {
+      const float4 q = live ? __ldg(reinterpret_cast<const float4 *>(a.q + j * a.ldq) + lane) : zero4;
+      const bool one = end - beg <= G;
+      float m = -FLT_MAX, ssum = 0.f, ex = 0.f;       // running max / sum of the lane's own head
+      for (int g0 = beg; g0 < end; g0 += G) {
+        const int n = min(G, end - g0);
+        const bool valid = oc < n && oh < a.heads;
+        float4 kr[G], vr[G];
+        load_rows<G>(a.k, a.ldkv, g0, n, lane, live, kr);
+        load_rows<G>(a.v, a.ldkv, g0, n, lane, live, vr);
+        float v[V];
+#pragma unroll
+        for (int c = 0; c < G; ++c) {
+          float ph[HP];
+          head_partials<HP>(q, kr[c], hs, ph);
+#pragma unroll
+          for (int h = 0; h < HP; ++h) v[c * HP + h] = ph[h];
+        }
+        // every lane takes part in the reduction's shuffles; only then select
+        const float zr = xreduce_own<V>(v, lane);
+        const float z = valid ? leaky(zr, a.slope) : -FLT_MAX;
+        if (!one && writer && valid) a.att_out[(int64_t)(g0 + oc) * a.heads + oh] = z;   // raw, normalised below
+        const float mn = fmaxf(m, head_max<SG>(z));
+        const float sc = (m == -FLT_MAX) ? 0.f : expf(m - mn);
+        m = mn;
+        ex = valid ? expf(z - m) : 0.f;
+        ssum = ssum * sc + head_sum<SG>(ex);
+        const float wt = valid ? ex * keep_scale(a, doff, g0 + oc, oh, inv_keep) : 0.f;
+        float sch[HP];
+#pragma unroll
+        for (int h = 0; h < HP; ++h) sch[h] = pair_val<SG, HP>(sc, 0, h);
+        const float4 s4 = by_head<HP>(sch, hs);
+        acc.x *= s4.x; acc.y *= s4.y; acc.z *= s4.z; acc.w *= s4.w;
+#pragma unroll
+        for (int c = 0; c < G; ++c) {
+          if (c >= n) break;
+          float wh[HP];
+#pragma unroll
+          for (int h = 0; h < HP; ++h) wh[h] = pair_val<SG, HP>(wt, c, h);
+          const float4 w4 = by_head<HP>(wh, hs);
+          acc.x = fmaf(w4.x, vr[c].x, acc.x);
+          acc.y = fmaf(w4.y, vr[c].y, acc.y);
+          acc.z = fmaf(w4.z, vr[c].z, acc.z);
+          acc.w = fmaf(w4.w, vr[c].w, acc.w);
+        }
+      }
+      const float inv = oh < a.heads ? 1.f / ssum : 0.f;      // for the lane's own head
+      float ih[HP];
+#pragma unroll
+      for (int h = 0; h < HP; ++h) ih[h] = pair_val<SG, HP>(inv, 0, h);
+      const float4 i4 = by_head<HP>(ih, hs);
+      acc.x *= i4.x; acc.y *= i4.y; acc.z *= i4.z; acc.w *= i4.w;
+      if (one) {
+        if (writer && oc < end - beg && oh < a.heads) a.att_out[(int64_t)(beg + oc) * a.heads + oh] = ex * inv;
+      } else {
+        float mh[HP];
+#pragma unroll
+        for (int h = 0; h < HP; ++h) mh[h] = pair_val<SG, HP>(m, 0, h);
+        __syncwarp();
+        for (int t = lane; t < (end - beg) * a.heads; t += 32) {
+          const int h = t % a.heads;
+          float mm = 0.f, ii = 0.f;
+#pragma unroll
+          for (int hh = 0; hh < HP; ++hh)
+            if (h == hh) { mm = mh[hh]; ii = ih[hh]; }
+          float *pz = a.att_out + (int64_t)beg * a.heads + t;
+          *pz = expf(*pz - mm) * ii;
+        }
+      }
+    }
+    if (live) reinterpret_cast<float4 *>(a.agg + j * a.ldagg)[lane] = acc;
+    __syncwarp();
+  }
+}
+
+constexpr int kStashGroups = 4;     // groups whose dL/dy the backward keeps in shared memory
+
+template <int HP>
+__global__ void __launch_bounds__(32 * kWarpsPerCta, 2) k_attn_bwd_s(AttnArgs a) {
+  using SG = SGeom<HP>;
+  constexpr int G = SG::G, V = SG::V;
+  __shared__ float stash[kWarpsPerCta][kStashGroups][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t n_dst = a.n_dst_dev ? min((int64_t)(*a.n_dst_dev), a.n_dst) : a.n_dst;
+  RowGeom geo{a.dim / 4, a.dim / a.heads, a.heads};
+  int hsel1[1][4];
+  lane_heads<1>(geo, lane, hsel1);
+  const int hs[4] = {hsel1[0][0], hsel1[0][1], hsel1[0][2], hsel1[0][3]};
+  const uint64_t doff = a.offset_dev ? *a.offset_dev : a.offset;
+  const float inv_keep = a.drop_p > 0.f ? 1.f / (1.f - a.drop_p) : 1.f;
+  const bool live = lane < geo.nv4;
+  const int own = lane >> SG::S, oc = own >> SG::LH, oh = own & (HP - 1);
+  const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t j = (int64_t)blockIdx.x * kWarpsPerCta + w; j < n_dst; j += (int64_t)gridDim.x * kWarpsPerCta) {
+    const int beg = a.rptr[j], end = a.rptr[j + 1];
+    float4 dq = zero4;
+    if (end > beg) {
+      const float4 da = live ? __ldg(reinterpret_cast<const float4 *>(a.dagg + j * a.lddagg) + lane) : zero4;
+      const float4 q = live ? __ldg(reinterpret_cast<const float4 *>(a.q + j * a.ldq) + lane) : zero4;
+      // pass 1: dL/dy (through dropout) of each pair, sum_e y dL/dy per head, dV rows
+      float sd = 0.f, dl_one = 0.f, y_one = 0.f;
+      int gi = 0;
+      for (int g0 = beg; g0 < end; g0 += G, ++gi) {
+        const int n = min(G, end - g0);
+        const bool valid = oc < n && oh < a.heads;
+        float v[V];
+        {
+          float4 vr[G];
+          load_rows<G>(a.v, a.ldkv, g0, n, lane, live, vr);
+#pragma unroll
+          for (int c = 0; c < G; ++c) {
+            float ph[HP];
+            head_partials<HP>(da, vr[c], hs, ph);
+#pragma unroll
+            for (int h = 0; h < HP; ++h) v[c * HP + h] = ph[h];
+          }
+        }
+        const float kp = valid ? keep_scale(a, doff, g0 + oc, oh, inv_keep) : 0.f;
+        const float dl = xreduce_own<V>(v, lane) * kp;
+        const float y = valid ? __ldg(a.att + (int64_t)(g0 + oc) * a.heads + oh) : 0.f;
+        sd += head_sum<SG>(y * dl);
+        if (gi < kStashGroups) stash[w][gi][lane] = dl;
+        dl_one = dl;
+        y_one = y;
+        if (a.dv) {
+          const float yk = y * kp;
+#pragma unroll
+          for (int c = 0; c < G; ++c) {
+            if (c >= n) break;
+            float yh[HP];
+#pragma unroll
+            for (int h = 0; h < HP; ++h) yh[h] = pair_val<SG, HP>(yk, c, h);
+            const float4 y4 = by_head<HP>(yh, hs);
+            if (live)
+              reinterpret_cast<float4 *>(a.dv + (int64_t)(g0 + c) * a.lddkv)[lane] =
+                  make_float4(y4.x * da.x, y4.y * da.y, y4.z * da.z, y4.w * da.w);
+          }
+        }
+      }
+      __syncwarp();
+      // pass 2: logits again, LeakyReLU and softmax backward, dK rows, dq
+      gi = 0;
+      for (int g0 = beg; g0 < end; g0 += G, ++gi) {
+        const int n = min(G, end - g0);
+        const bool valid = oc < n && oh < a.heads;
+        float dl, y;
+        if (end - beg <= G) {
+          dl = dl_one;
+          y = y_one;
+        } else {
+          y = valid ? __ldg(a.att + (int64_t)(g0 + oc) * a.heads + oh) : 0.f;
+          if (gi < kStashGroups) {
+            dl = stash[w][gi][lane];
+          } else {            // long segment: dL/dy again from the V rows
+            float u[V];
+            float4 vr[G];
+            load_rows<G>(a.v, a.ldkv, g0, n, lane, live, vr);
+#pragma unroll
+            for (int c = 0; c < G; ++c) {
+              float ph[HP];
+              head_partials<HP>(da, vr[c], hs, ph);
+#pragma unroll
+              for (int h = 0; h < HP; ++h) u[c * HP + h] = ph[h];
+            }
+            const float kp = valid ? keep_scale(a, doff, g0 + oc, oh, inv_keep) : 0.f;
+            dl = xreduce_own<V>(u, lane) * kp;
+          }
+        }
+        float4 kr[G];
+        load_rows<G>(a.k, a.ldkv, g0, n, lane, live, kr);
+        float v[V];
+#pragma unroll
+        for (int c = 0; c < G; ++c) {
+          float ph[HP];
+          head_partials<HP>(q, kr[c], hs, ph);
+#pragma unroll
+          for (int h = 0; h < HP; ++h) v[c * HP + h] = ph[h];
+        }
+        const float zt = xreduce_own<V>(v, lane);
+        const float g = y * (dl - sd);
+        const float dz = valid ? (zt > 0.f ? g : g * a.slope) : 0.f;
+#pragma unroll
+        for (int c = 0; c < G; ++c) {
+          if (c >= n) break;
+          float zh[HP];
+#pragma unroll
+          for (int h = 0; h < HP; ++h) zh[h] = pair_val<SG, HP>(dz, c, h);
+          const float4 d4 = by_head<HP>(zh, hs);
+          if (a.dk && live)
+            reinterpret_cast<float4 *>(a.dk + (int64_t)(g0 + c) * a.lddkv)[lane] =
+                make_float4(d4.x * q.x, d4.y * q.y, d4.z * q.z, d4.w * q.w);
+          dq.x = fmaf(d4.x, kr[c].x, dq.x);
+          dq.y = fmaf(d4.y, kr[c].y, dq.y);
+          dq.z = fmaf(d4.z, kr[c].z, dq.z);
+          dq.w = fmaf(d4.w, kr[c].w, dq.w);
+        }
+      }
+    }
+    if (a.dq && live) reinterpret_cast<float4 *>(a.dq + j * (int64_t)a.dim)[lane] = dq;
+    __syncwarp();
+  }
+}
+
 int attn_grid(int64_t n_dst) {
   static int sms_of[64] = {0};
   int dev = 0;
@@ -436,11 +771,26 @@ int check_attn(const AttnArgs &a, bool bwd) {
   return FB_OK;
 }
 
+// The grouped kernels take rows of <= 128 floats with logits from q.k, one
+// output row per segment, and (backward) no pre-activation gradient output.
+// FB_GENERIC_ATTN in the environment forces the general kernels.
+bool short_path(const AttnArgs &a) {
+  static const bool generic = getenv("FB_GENERIC_ATTN") != nullptr;
+  return !generic && a.dim <= 128 && !a.x && !a.seg_row && !a.dx && a.heads != 3;
+}
+
 int launch_fwd(const AttnArgs &a, cudaStream_t stream) {
   int rc = check_attn(a, false);
   if (rc) return rc;
   if (a.n_dst == 0) return FB_OK;
   const int grid = attn_grid(a.n_dst), nv = (a.dim / 4 + 31) / 32;
+  if (short_path(a)) {
+    if (a.heads == 1) k_attn_fwd_s<1><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a);
+    else if (a.heads == 2) k_attn_fwd_s<2><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a);
+    else k_attn_fwd_s<4><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a);
+    FB_LAUNCHED("k_attn_fwd_s");
+    return FB_OK;
+  }
   switch (nv) {
     case 1: k_attn_fwd<1><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a); break;
     case 2: k_attn_fwd<2><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a); break;
@@ -456,6 +806,13 @@ int launch_bwd(const AttnArgs &a, cudaStream_t stream) {
   if (rc) return rc;
   if (a.n_dst == 0) return FB_OK;
   const int grid = attn_grid(a.n_dst), nv = (a.dim / 4 + 31) / 32;
+  if (short_path(a)) {
+    if (a.heads == 1) k_attn_bwd_s<1><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a);
+    else if (a.heads == 2) k_attn_bwd_s<2><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a);
+    else k_attn_bwd_s<4><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a);
+    FB_LAUNCHED("k_attn_bwd_s");
+    return FB_OK;
+  }
   switch (nv) {
     case 1: k_attn_bwd<1><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a); break;
     case 2: k_attn_bwd<2><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a); break;

@@ -123,20 +123,22 @@ class FusedStep:
             hsrc = hdst = {}
         A = ops.gather_time_encode(E, f=edge_table if de > 0 else None, f_idx=blk.eid, dt=blk.dt_edges, w=wv, b=bt,
                                    device=dev, n_rows_dev=E_dev, **hsrc)
-        KV = ops.gemm_nt(A, lp.W_kv, lp.b_kv, M_dev=E_dev)
         if dn > 0:
             Qin = ops.gather_time_encode(nd, w=wv, b=bt, device=dev, n_rows_dev=nd_dev, **hdst)
-            Q = ops.gemm_nt(Qin, L.w_q.weight, L.w_q.bias, M_dev=nd_dev)
         else:
             Qin = ops.gather_time_encode(1, w=wv, b=bt, device=dev)
-            Q = ops.gemm_nt(Qin, L.w_q.weight, L.w_q.bias)
+        KV = torch.empty(E, 2 * D, device=dev)
+        Q = torch.empty(Qin.shape[0], D, device=dev)
+        ops.gemm_group([dict(kind=ops.NT, A=A, B=lp.W_kv, bias=lp.b_kv, out=KV, M_dev=E_dev),
+                        dict(kind=ops.NT, A=Qin, B=L.w_q.weight, bias=L.w_q.bias, out=Q,
+                             M_dev=nd_dev if dn > 0 else None)])
         p_att = L.att_dropout_p if training else 0.0
         agg, att = ops.attn_fwd(Q, KV[:, :D], KV[:, D:], blk.rptr, L.num_head, L.negative_slope, p_att,
                                 0x5EED + l, 0, n_dst_dev=nd_dev, offset_dev=offset_dev)
-        Wo = L.w_out.weight
-        Z = ops.gemm_nt(agg, Wo[:, :D], L.w_out.bias, M_dev=nd_dev)
-        if dn > 0:
-            ops.gemm_nt(Qin[:, :dn], Wo[:, D:], out=Z, accumulate=True, M_dev=nd_dev)
+        # w_out([agg | h_dst]) as one GEMM over the concatenation along K (h_dst = Qin[:, :dn])
+        Z = torch.empty(nd, D, device=dev)
+        ops.gemm_group([dict(kind=ops.NT, A=agg, A2=Qin[:, :dn] if dn > 0 else None, B=L.w_out.weight,
+                             bias=L.w_out.bias, out=Z, M_dev=nd_dev)])
         p_drop = L.dropout.p if training else 0.0
         y, out = ops.layer_tail_fwd(Z, L.layer_norm.weight, L.layer_norm.bias, eps=L.layer_norm.eps, drop_p=p_drop,
                                     seed=0x7A11 + l, offset_dev=offset_dev, y=Z, n_dev=nd_dev,
@@ -161,38 +163,51 @@ class FusedStep:
                                 gate_dev=E_dev if blk.static else None)
         Wo, gWo = L.w_out.weight, g(L.w_out.weight)
         agg, Qin = st["agg"], st["Qin"]
-        ops.gemm_tn(dZ, agg, out=gWo[:, :D], accumulate=True, M_dev=nd_dev, db=g(L.w_out.bias))
-        if dn > 0:
-            ops.gemm_tn(dZ, Qin[:, :dn], out=gWo[:, D:], accumulate=True, M_dev=nd_dev)
-        dagg = ops.gemm_nn(dZ, Wo[:, :D], M_dev=nd_dev)
+        dev = dout.device
+        dagg = torch.empty(nd, D, device=dev)
         dh = None
+        # every product that reads dZ, in one launch
+        probs = [dict(kind=ops.TN, A=dZ, B=agg, out=gWo[:, :D], accumulate=True, M_dev=nd_dev, db=g(L.w_out.bias)),
+                 dict(kind=ops.NN, A=dZ, B=Wo[:, :D], out=dagg, M_dev=nd_dev)]
+        if dn > 0:
+            probs.append(dict(kind=ops.TN, A=dZ, B=Qin[:, :dn], out=gWo[:, D:], accumulate=True, M_dev=nd_dev))
         if l > 0:
             assert dh_rows >= nd + E
-            dh = torch.empty(dh_rows, dn, device=dout.device)
-            ops.gemm_nn(dZ, Wo[:, D:], out=dh[:nd], M_dev=nd_dev)
+            dh = torch.empty(dh_rows, dn, device=dev)
+            probs.append(dict(kind=ops.NN, A=dZ, B=Wo[:, D:], out=dh[:nd], M_dev=nd_dev))
+        ops.gemm_group(probs)
         KV = st["KV"]
         dQ, dKV = ops.attn_bwd(st["Q"], KV[:, :D], KV[:, D:], blk.rptr, st["att"], dagg, L.num_head,
                                L.negative_slope, st["p_att"], 0x5EED + l, 0, n_dst_dev=nd_dev,
                                offset_dev=st["offset_dev"])
-        ops.gemm_tn(dKV, st["A"], out=lp.gW_kv, accumulate=True, M_dev=E_dev, db=lp.gb_kv)
+        # every product that reads dKV or dQ, in one launch
+        v = torch.empty(D, device=dev)            # sum over rows of dQ
+        probs = [dict(kind=ops.TN, A=dKV, B=st["A"], out=lp.gW_kv, accumulate=True, M_dev=E_dev, db=lp.gb_kv)]
         if dh is not None:
-            ops.gemm_nn(dKV, lp.W_kv[:, :dn], out=dh[nd:nd + E], M_dev=E_dev)
+            probs.append(dict(kind=ops.NN, A=dKV, B=lp.W_kv[:, :dn], out=dh[nd:nd + E], M_dev=E_dev))
+        dA_t = None
         if dtime > 0:
-            dA_t = ops.gemm_nn(dKV, lp.W_kv[:, dn + de:], M_dev=E_dev)
+            dA_t = torch.empty(E, dtime, device=dev)
+            probs.append(dict(kind=ops.NN, A=dKV, B=lp.W_kv[:, dn + de:], out=dA_t, M_dev=E_dev))
+        if dn == 0:
+            probs.append(dict(kind=ops.TN, A=dQ, B=None, out=None, M_dev=nd_dev, db=v, db_accumulate=False))
+        else:
+            probs.append(dict(kind=ops.TN, A=dQ, B=Qin, out=g(L.w_q.weight), accumulate=True, M_dev=nd_dev,
+                              db=v, db_accumulate=False))
+            if dh is not None:
+                probs.append(dict(kind=ops.NN, A=dQ, B=L.w_q.weight[:, :dn], out=dh[:nd], accumulate=True,
+                                  M_dev=nd_dev))
+        ops.gemm_group(probs)
+        if dtime > 0:
             ops.time_encode_bwd(dA_t, blk.dt_edges, L.time_enc.w.weight.view(-1), L.time_enc.w.bias,
                                 g(L.time_enc.w.weight).view(-1), g(L.time_enc.w.bias), n_dev=E_dev)
         bt = L.time_enc.w.bias if dtime > 0 else None
         gbt = g(L.time_enc.w.bias) if dtime > 0 else None
         if dn == 0:
             # one shared Q input row cos(b_t): every Q-side gradient needs only sum_rows dQ
-            v = ops.colsum(dQ, M_dev=nd_dev)
             ops.q_time_bwd(v, L.w_q.weight, dn, dtime, bt, g(L.w_q.bias), gbt, qin0=Qin[0], dW_q=g(L.w_q.weight))
         else:
-            v = torch.empty(D, device=dout.device)
-            ops.gemm_tn(dQ, Qin, out=g(L.w_q.weight), accumulate=True, M_dev=nd_dev, db=v, db_accumulate=False)
             ops.q_time_bwd(v, L.w_q.weight, dn, dtime, bt, g(L.w_q.bias), gbt)
-            if dh is not None:
-                ops.gemm_nn(dQ, L.w_q.weight[:, :dn], out=dh[:nd], accumulate=True, M_dev=nd_dev)
         return dh
 
     # -- whole step -----------------------------------------------------------
@@ -219,17 +234,21 @@ class FusedStep:
         ep = m.edge_predictor
         B = h.shape[0] // 3
         D = h.shape[1]
-        S = ops.gemm_nt(h[:B], ep.src_fc.weight, ep.src_fc.bias)
-        P = ops.gemm_nt(h[B:3 * B], ep.dst_fc.weight, ep.dst_fc.bias)
+        S = torch.empty(B, D, device=dev)
+        P = torch.empty(2 * B, D, device=dev)
+        ops.gemm_group([dict(kind=ops.NT, A=h[:B], B=ep.src_fc.weight, bias=ep.src_fc.bias, out=S),
+                        dict(kind=ops.NT, A=h[B:3 * B], B=ep.dst_fc.weight, bias=ep.dst_fc.bias, out=P)])
         dS = torch.empty(B, D, device=dev)
         dP = torch.empty(2 * B, D, device=dev)
         ops.edge_predictor_loss(S, P, ep.out_fc.weight.view(-1), ep.out_fc.bias, loss_out, dS, dP,
                                 ep.out_fc.weight.grad.view(-1), ep.out_fc.bias.grad, scores=scores)
         dh = torch.empty(3 * B, D, device=dev)
-        ops.gemm_tn(dS, h[:B], out=ep.src_fc.weight.grad, accumulate=True, db=ep.src_fc.bias.grad)
-        ops.gemm_tn(dP, h[B:3 * B], out=ep.dst_fc.weight.grad, accumulate=True, db=ep.dst_fc.bias.grad)
-        ops.gemm_nn(dS, ep.src_fc.weight, out=dh[:B])
-        ops.gemm_nn(dP, ep.dst_fc.weight, out=dh[B:3 * B])
+        ops.gemm_group([
+            dict(kind=ops.TN, A=dS, B=h[:B], out=ep.src_fc.weight.grad, accumulate=True, db=ep.src_fc.bias.grad),
+            dict(kind=ops.TN, A=dP, B=h[B:3 * B], out=ep.dst_fc.weight.grad, accumulate=True,
+                 db=ep.dst_fc.bias.grad),
+            dict(kind=ops.NN, A=dS, B=ep.src_fc.weight, out=dh[:B]),
+            dict(kind=ops.NN, A=dP, B=ep.dst_fc.weight, out=dh[B:3 * B])])
         for l in range(len(mfgs) - 1, -1, -1):
             rows = mfgs[l - 1].n_dst if l > 0 else 0
             dh = self._layer_bwd(l, saved[l], dh, rows)

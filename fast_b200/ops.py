@@ -140,6 +140,57 @@ def gemm_tn(G, X, out=None, accumulate=False, M_dev=None, db=None, db_accumulate
     return out
 
 
+NT, NN, TN = 0, 1, 2
+
+
+def gemm_group(problems):
+    """Runs independent GEMMs in one launch (+ one split-reduce for the TN
+    ones).  Each problem is a dict: kind (NT / NN / TN), A, B (TN: X; may be
+    None for a TN with K == 0), out, and optionally A2 / k1 (NT / NN: A's
+    columns >= k1 come from A2), bias, M_dev, accumulate, db, db_accumulate.
+    Shapes: NT A [M, K], B [N, K]; NN A [M, K], B [K, N]; TN A = G [M, N],
+    B = X [M, K], out [N, K]."""
+    from .capi import GemmProblem
+    import ctypes
+    arr = (GemmProblem * len(problems))()
+    nbytes, flops = 0, 0
+    keep = []
+    for i, p in enumerate(problems):
+        A, B, out = p["A"], p.get("B"), p.get("out")
+        A2 = p.get("A2")
+        kind = p["kind"]
+        for t in (A, B, A2, out):
+            if t is not None:
+                _f32_rows(t, "gemm_group operand")
+        M = A.shape[0]
+        if kind == TN:
+            N, K = A.shape[1], (0 if B is None else B.shape[1])
+        elif kind == NT:
+            N, K = B.shape[0], A.shape[1] + (0 if A2 is None else A2.shape[1])
+        else:
+            N, K = B.shape[1], A.shape[1] + (0 if A2 is None else A2.shape[1])
+        k1 = A.shape[1] if A2 is not None else K
+        db = p.get("db")
+        acc = int(bool(p.get("accumulate", False)))
+        dba = p.get("db_accumulate")
+        if out is None:                      # TN column sums only (K == 0): nothing lands in C
+            assert kind == TN and K == 0 and db is not None
+            c_ptr, ldc = ptr(db), 0
+        else:
+            c_ptr, ldc = ptr(out), out.stride(0)
+        arr[i] = GemmProblem(kind, ptr(A), A.stride(0), ptr(A2), 0 if A2 is None else A2.stride(0), k1,
+                             ptr(B), 0 if B is None else B.stride(0), ptr(p.get("bias")), c_ptr, ldc,
+                             M, _p(p.get("M_dev")), N, K, acc, ptr(db), int(acc if dba is None else bool(dba)))
+        keep.append((A, B, A2, out, db))
+        nbytes += 4 * (M * K + N * K + M * N)
+        flops += 2 * M * N * K
+    n = len(problems)
+    dev = problems[0]["A"].device
+    ws = torch.empty(int(lib.fb_gemm_group_ws_bytes(arr, n)), device=dev, dtype=torch.uint8)
+    _launch("gemm_group", nbytes, flops, 2,
+            lambda: call("fb_gemm_group", arr, n, ptr(ws), ws.numel(), stream_ptr()))
+
+
 def layer_tail_fwd(z, gamma, beta, eps=1e-5, drop_p=0.0, seed=0, offset=0, offset_dev=None, mask_u=None,
                    y=None, out=None, n_dev=None, gate_dev=None):
     """y = relu(dropout(z)), out = LayerNorm(y) per row (rows >= *n_dev: out = 0;

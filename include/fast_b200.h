@@ -259,6 +259,29 @@ int fb_gemm_tn(const float *G, int64_t ldg, const float *X, int64_t ldx, float *
 int fb_gemm_tn_bias(const float *G, int64_t ldg, const float *X, int64_t ldx, float *C, int64_t ldc,
                     int64_t M, const int32_t *M_dev, int N, int K, int accumulate, float *db,
                     int db_accumulate, void *ws, cudaStream_t stream);
+/* Grouped launch of independent projection GEMMs (one grid, one split-reduce
+ * pass): the GEMMs of one dependency level of a layer (e.g. every product
+ * that reads dKV) run concurrently.  Outputs must not overlap.  Problems whose
+ * rows are not 16-byte aligned run as single launches.  NT / NN may take A
+ * as the concatenation along K of A (columns < k1) and A2 (columns >= k1):
+ * torch.cat([agg, h_dst], 1) @ W^T without the copy (layers.py:213-217).
+ * TN with K == 0 and db set computes column sums only.  ws:
+ * fb_gemm_group_ws_bytes(probs, n) bytes. */
+enum { FB_GEMM_NT = 0, FB_GEMM_NN = 1, FB_GEMM_TN = 2 };
+typedef struct fb_gemm_problem {
+  int kind;
+  const float *A; int64_t lda;             /* NT / NN: A [M, K]; TN: G [M, N] */
+  const float *A2; int64_t lda2; int k1;   /* NT / NN: columns >= k1 from A2 (NULL: none) */
+  const float *B; int64_t ldb;             /* NT: [N, K]; NN: [K, N]; TN: X [M, K] */
+  const float *bias;                       /* NT / NN, or NULL */
+  float *C; int64_t ldc;                   /* NT / NN: [M, N]; TN: [N, K] */
+  int64_t M; const int32_t *M_dev;         /* rows (capacity) and optional device count */
+  int N, K;
+  int accumulate;
+  float *db; int db_accumulate;            /* TN: db[n] (+)= sum_m G[m, n], or NULL */
+} fb_gemm_problem;
+size_t fb_gemm_group_ws_bytes(const fb_gemm_problem *probs, int n);
+int fb_gemm_group(const fb_gemm_problem *probs, int n, void *ws, size_t ws_bytes, cudaStream_t stream);
 /* db[n] (+)= sum_m G[m, n]; deterministic.  ws: fb_colsum_ws_bytes(M, N). */
 size_t fb_colsum_ws_bytes(int64_t M, int N);
 int fb_colsum(const float *G, int64_t ldg, float *db, int64_t M, const int32_t *M_dev, int N,

@@ -157,3 +157,40 @@ def test_q_time_bwd(cuda, dn, with_row):
                    qin0=qin0.to(cuda) if with_row else None, dW_q=g_dWq if with_row else None)
     for name, dev, a, c in zip(["db_q", "db_t", "dW_q"], [g_dbq, g_dbt, g_dWq], e64, e32):
         _close(dev, a, c, name)
+
+
+def test_gemm_group_mixed(cuda):
+    """One grouped launch: NT with A concatenated along K, NN, TN with the bias
+    column, TN column sums only (K == 0), and a device-side row count."""
+    from fast_b200 import ops
+    torch.manual_seed(5)
+    M, D, dn, E = 900, 100, 100, 2500
+    agg, hd = torch.randn(M, D), torch.randn(M, dn + 100)[:, :dn]
+    Wo, bo = torch.randn(D, D + dn), torch.randn(D)
+    dKV, A, Wkv = torch.randn(E, 2 * D), torch.randn(E, 272), torch.randn(2 * D, 272)
+    dQ = torch.randn(M, D)
+    e_true = E - 11
+    cnt = torch.tensor([e_true], dtype=torch.int32, device=cuda)
+    c = lambda t: t.to(cuda)                  # noqa: E731
+    hd_d = c(torch.cat([hd, torch.zeros(M, 100)], 1))[:, :dn]
+    Z = torch.empty(M, D, device=cuda)
+    dA = torch.full((E, 72), 3.0, device=cuda)
+    gW = torch.ones(2 * D, 272, device=cuda)
+    gb = torch.ones(2 * D, device=cuda)
+    v = torch.full((D,), 9.0, device=cuda)
+    ops.gemm_group([
+        dict(kind=ops.NT, A=c(agg), A2=hd_d, B=c(Wo), bias=c(bo), out=Z),
+        dict(kind=ops.NN, A=c(dKV), B=c(Wkv)[:, 200:], out=dA, M_dev=cnt),
+        dict(kind=ops.TN, A=c(dKV), B=c(A), out=gW, accumulate=True, M_dev=cnt, db=gb),
+        dict(kind=ops.TN, A=c(dQ), B=None, out=None, db=v, db_accumulate=False)])
+    r = lambda t: t.double()                  # noqa: E731
+    exp = {
+        "Z": (torch.cat([agg, hd], 1).double() @ r(Wo).t() + r(bo), torch.cat([agg, hd], 1) @ Wo.t() + bo, Z),
+        "dA": (r(dKV[:e_true]) @ r(Wkv[:, 200:]), dKV[:e_true] @ Wkv[:, 200:], dA[:e_true]),
+        "gW": (r(dKV[:e_true]).t() @ r(A[:e_true]), dKV[:e_true].t() @ A[:e_true], gW - 1.0),
+        "gb": (r(dKV[:e_true]).sum(0), dKV[:e_true].sum(0), gb - 1.0),
+        "v": (r(dQ).sum(0), dQ.sum(0), v),
+    }
+    for name, (e64, e32, got) in exp.items():
+        _close(got, e64, e32, name)
+    assert bool((dA[e_true:] == 3.0).all())           # rows past the count untouched
