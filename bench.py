@@ -44,6 +44,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=5)
     ap.add_argument("--eager", action="store_true", help="launch kernels step by step instead of a CUDA graph")
+    ap.add_argument("--suite", default=None, choices=["kernels"],
+                    help="kernels: time each hot kernel alone at config-5 block sizes against the HBM roofline "
+                         "(one JSON line per kernel instead of the training-step line)")
+    ap.add_argument("--suite-scale", type=float, default=1.0,
+                    help="--suite kernels: fraction of the config-5 block sizes (small cases for ncu captures)")
     ap.add_argument("--cuda-profiler-range", action="store_true",
                     help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--path", default="fused", choices=["fused", "autograd"],
@@ -412,10 +417,107 @@ def cpu_baseline(cfg, warm, timed, budget_s):
                       "%.1f s" % (n, len(timed), cfg.batch, 2 * cfg.batch, cfg.name, el)}
 
 
+# ----------------------------------------------------------------------------- kernel roofline suite
+def run_kernel_suite(args):
+    """Each HBM-bound kernel of the step, alone, at the block sizes of config 5
+    (hop 2: 132 k destinations x fan-out 10 = 1.32 M edges; D = 100, 2 heads,
+    172-d edge features, 100-d time encoding).  Algorithmic bytes per launch
+    count every tensor the kernel must read or write once; time is the mean
+    of 10 back-to-back launches between CUDA events, inputs larger than L2."""
+    import torch
+    from fast_b200 import ops
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    pk = peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    Nd, fan, D, H, de, dt_ = int(132_000 * args.suite_scale), 10, 100, 2, 172, 100
+    E = Nd * fan
+    rows_tab = int(4_000_000 * args.suite_scale)
+    table = torch.randn(rows_tab, de, device=dev, generator=g)
+    eid = torch.randint(0, rows_tab, (E,), device=dev, generator=g, dtype=torch.int32)
+    dts = torch.rand(E, device=dev, generator=g) * 1e5
+    w = (1.0 / 10 ** torch.linspace(0, 9, dt_, device=dev)).contiguous()
+    b = torch.zeros(dt_, device=dev)
+    rptr = torch.arange(0, E + 1, fan, device=dev, dtype=torch.int32)
+    q = torch.randn(Nd, D, device=dev, generator=g) * 0.5
+    kv = torch.randn(E, 2 * D, device=dev, generator=g) * 0.5
+    dagg = torch.randn(Nd, D, device=dev, generator=g)
+    z = torch.randn(E, D, device=dev, generator=g)
+    gamma, beta = torch.ones(D, device=dev), torch.zeros(D, device=dev)
+    dA = torch.randn(E, dt_, device=dev, generator=g)
+    out = []
+
+    def timed(name, nbytes, flops, fn, shape):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(10):
+            fn()
+        s1.record()
+        torch.cuda.synchronize()
+        us = s0.elapsed_time(s1) * 100.0          # per launch, microseconds
+        line = {"suite": "kernels", "kernel": name, "shape": shape, "us_per_launch": round(us, 2),
+                "bytes_per_launch": int(nbytes)}
+        if flops:
+            line.update({"bound": "FFMA (fp32 CUDA cores)", "TFLOP_s": round(flops / us / 1e6, 2)})
+        else:
+            gbs = nbytes / us / 1e3
+            line.update({"bound": "hbm", "achieved_GB_s": round(gbs, 1), "peak_GB_s": pk["hbm"],
+                         "frac": round(gbs / pk["hbm"], 3), "peak_source": "%s copy bandwidth" % pk["src"]})
+        out.append(line)
+        print(json.dumps(line), flush=True)
+
+    A = torch.empty(E, de + dt_, device=dev)
+    timed("k_gather_time_encode", E * (de * 4 + 4 + 4 + (de + dt_) * 4), 0,
+          lambda: ops.gather_time_encode(E, f=table, f_idx=eid, dt=dts, w=w, b=b, out=A),
+          "E=%d rows of [f(%d) | cos(%d)]" % (E, de, dt_))
+    att_b = 4 * (Nd * D + 2 * E * D + (Nd + 1) + Nd * D + E * H)
+    timed("k_attn_fwd_s", att_b, 0,
+          lambda: ops.attn_fwd(q, kv[:, :D], kv[:, D:], rptr, H, 0.2, 0.1, 1, 2),
+          "Nd=%d, E=%d, D=%d, H=%d, dropout 0.1" % (Nd, E, D, H))
+    agg, att = ops.attn_fwd(q, kv[:, :D], kv[:, D:], rptr, H, 0.2, 0.1, 1, 2)
+    dkv = torch.empty(E, 2 * D, device=dev)
+    bwd_b = 4 * (2 * Nd * D + 2 * E * D + E * H + (Nd + 1) + 2 * E * D + Nd * D)
+    timed("k_attn_bwd_s", bwd_b, 0,
+          lambda: ops.attn_bwd(q, kv[:, :D], kv[:, D:], rptr, att, dagg, H, 0.2, 0.1, 1, 2, dkv=dkv),
+          "Nd=%d, E=%d, D=%d, H=%d, dropout 0.1" % (Nd, E, D, H))
+    y = torch.empty_like(z)
+    o = torch.empty_like(z)
+    timed("k_tail_fwd", E * D * 4 * 3 + 8 * D, 0,
+          lambda: ops.layer_tail_fwd(z, gamma, beta, drop_p=0.1, seed=5, y=y, out=o),
+          "rows=%d, D=%d, dropout 0.1" % (E, D))
+    dg, dbb = torch.zeros(D, device=dev), torch.zeros(D, device=dev)
+    dz = torch.empty_like(z)
+    timed("k_tail_bwd", E * D * 4 * 3 + 12 * D, 0,
+          lambda: ops.layer_tail_bwd(z, y, gamma, dg, dbb, drop_p=0.1, dz=dz),
+          "rows=%d, D=%d" % (E, D))
+    dw_, db_ = torch.zeros(dt_, device=dev), torch.zeros(dt_, device=dev)
+    timed("k_te_bwd", E * (dt_ + 1) * 4, 0,
+          lambda: ops.time_encode_bwd(dA, dts, w, b, dw_, db_),
+          "rows=%d, dtime=%d" % (E, dt_))
+    W_kv = torch.randn(2 * D, de + dt_, device=dev, generator=g) * 0.05
+    b_kv = torch.zeros(2 * D, device=dev)
+    KV = torch.empty(E, 2 * D, device=dev)
+    timed("k_gemm_group (K|V projection, NT)", 0, 2 * E * 2 * D * (de + dt_),
+          lambda: ops.gemm_group([dict(kind=ops.NT, A=A, B=W_kv, bias=b_kv, out=KV)]),
+          "M=%d, N=%d, K=%d" % (E, 2 * D, de + dt_))
+    gW = torch.zeros(2 * D, de + dt_, device=dev)
+    gb = torch.zeros(2 * D, device=dev)
+    timed("k_gemm_group (K|V weight + bias gradient, TN)", 0, 2 * E * 2 * D * (de + dt_ + 1),
+          lambda: ops.gemm_group([dict(kind=ops.TN, A=dkv, B=A, out=gW, accumulate=True, db=gb)]),
+          "M=%d, N=%d, K=%d+1" % (E, 2 * D, de + dt_))
+    return 0
+
+
 def main():
     args = parse()
     if args.warmup < 3:
         args.warmup = 3
+    if args.suite == "kernels":
+        return run_kernel_suite(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_fast(args)

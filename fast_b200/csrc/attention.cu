@@ -404,127 +404,94 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta, MinCtas<NV>::value) k_attn_
 }
 
 // ---------------------------------------------------------------------------
-// Short-segment kernels (rows of <= 128 floats, logits from q.k).  A
-// destination's edges go in groups of G = min(16, 32 / H) (H = heads rounded
-// up to a power of two), so G x H <= 32 (edge, head) pairs: after one
-// transposed warp reduction every lane owns the total of one pair.  Per
-// group the K rows are loaded in one round trip (and then the V rows), the
-// G x H dot products cost G x H - 1 + 5 - log2(G x H) shuffles together, and
-// softmax statistics are reduced over the lanes owning one head.  Fan-outs up
-// to 16 are a single group.
+// Edge-parallel kernels (rows of <= 128 floats, logits from q.k, even
+// per-head width).  Per destination a warp works in groups of up to 32 edges:
+//   * dot products are lane-per-edge: lane c reads edge c's K (or V) row in
+//     16-byte chunks and multiplies it with q (or dagg) staged in shared
+//     memory once per head, masked to that head's features, so one warp
+//     instruction advances up to 32 edges and no shuffle reduction is needed;
+//   * softmax statistics are warp reductions over the group's lanes;
+//   * row outputs (agg, dK, dV, dq) are lane-per-feature: lane t owns the
+//     16-byte chunk t of the row, and each edge's per-head weights are
+//     broadcast from the edge's lane.
+// With an even per-head width, features 4t, 4t+1 share one head (hA) and
+// 4t+2, 4t+3 another (hB).
 
-template <int HP, int GG = (HP == 1 ? 16 : 32 / HP)>
-struct SGeom {
-  static constexpr int G = GG;                                     // edges per group
-  static constexpr int V = G * HP;                                 // (edge, head) pairs per group (<= 32)
-  static constexpr int K = V == 8 ? 3 : (V == 16 ? 4 : 5);         // log2 V
-  static constexpr int S = 5 - K;                                  // lanes per pair = 2^S
-  static constexpr int LH = HP == 1 ? 0 : (HP == 2 ? 1 : 2);       // log2 HP
-};
+constexpr int kEdgeGroup = 32;
 
-// In: per-lane partial sums v[0..V).  Returns the warp total of pair
-// lane >> (5 - log2 V).  Each butterfly step keeps half of the values and
-// trades the other half with the partner lane.
-template <int V>
-__device__ __forceinline__ float xreduce_own(float (&v)[V], int lane) {
-  constexpr int k = V == 8 ? 3 : (V == 16 ? 4 : 5);
-#pragma unroll
-  for (int st = 0; st < k; ++st) {
-    const int off = 16 >> st, half = V >> (st + 1);
-    const bool up = (lane & off) != 0;
-#pragma unroll
-    for (int i = 0; i < half; ++i) {
-      const float send = up ? v[i] : v[i + half];
-      const float keep = up ? v[i + half] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-    }
-  }
-  float t = v[0];
-#pragma unroll
-  for (int off = 16 >> k; off >= 1; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
-  return t;
-}
-
-// Sum / max over the lanes that own the same head (over the edge bits).
-template <class SG>
-__device__ __forceinline__ float head_sum(float x) {
-#pragma unroll
-  for (int off = 1 << (SG::S + SG::LH); off < 32; off <<= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
-  return x;
-}
-template <class SG>
-__device__ __forceinline__ float head_max(float x) {
-#pragma unroll
-  for (int off = 1 << (SG::S + SG::LH); off < 32; off <<= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
-  return x;
-}
-// Value of pair (c, h) from its owner lanes.
-template <class SG, int HP>
-__device__ __forceinline__ float pair_val(float x, int c, int h) {
-  return __shfl_sync(0xffffffffu, x, (c * HP + h) << SG::S);
-}
-// The four per-component values of a row given per-head values (lane's heads hs).
 template <int HP>
-__device__ __forceinline__ float4 by_head(const float (&vh)[HP], const int (&hs)[4]) {
-  float r[4];
+__device__ __forceinline__ float hv(const float (&a)[HP], int h) {
+  float r = a[0];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    r[c] = 0.f;
-#pragma unroll
-    for (int h = 0; h < HP; ++h)
-      if (hs[c] == h) r[c] = vh[h];
-  }
-  return make_float4(r[0], r[1], r[2], r[3]);
+  for (int i = 1; i < HP; ++i)
+    if (h == i) r = a[i];
+  return r;
 }
 
-// Per-head partial dot products of the lane's 4 components.
+// Philox keep scales of edge e for every head (the decisions of drop_scale()).
 template <int HP>
-__device__ __forceinline__ void head_partials(const float4 &a, const float4 &b, const int (&hs)[4],
-                                              float (&out)[HP]) {
+__device__ __forceinline__ void keep_heads(const AttnArgs &a, uint64_t doff, int64_t e, bool valid, float inv_keep,
+                                           float (&k)[HP]) {
+  if (!valid) {
 #pragma unroll
-  for (int h = 0; h < HP; ++h) out[h] = 0.f;
-  const float p[4] = {a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w};
+    for (int h = 0; h < HP; ++h) k[h] = 0.f;
+    return;
+  }
+  if (a.drop_p <= 0.f) {
 #pragma unroll
-  for (int c = 0; c < 4; ++c)
+    for (int h = 0; h < HP; ++h) k[h] = 1.f;
+    return;
+  }
+  if (a.mask_u) {
 #pragma unroll
-    for (int h = 0; h < HP; ++h)
-      if (hs[c] == h) out[h] += p[c];
-}
-
-// Dropout scale (0 or 1/(1-p)) of (edge e, head h): the decisions of drop_scale().
-__device__ __forceinline__ float keep_scale(const AttnArgs &a, uint64_t doff, int64_t e, int h, float inv_keep) {
-  if (a.drop_p <= 0.f) return 1.f;
-  if (a.mask_u) return a.mask_u[e * a.heads + h] > a.drop_p ? inv_keep : 0.f;
+    for (int h = 0; h < HP; ++h) k[h] = (h < a.heads && a.mask_u[e * a.heads + h] > a.drop_p) ? inv_keep : 0.f;
+    return;
+  }
   fb::Philox4 r = fb::philox4x32_10((uint32_t)e, (uint32_t)(e >> 32), (uint32_t)doff, (uint32_t)(doff >> 32),
                                     (uint32_t)a.seed, (uint32_t)(a.seed >> 32));
-  const uint32_t bits = h == 0 ? r.v[0] : (h == 1 ? r.v[1] : (h == 2 ? r.v[2] : r.v[3]));
-  return (float)(bits >> 8) * (1.0f / 16777216.0f) >= a.drop_p ? inv_keep : 0.f;
+#pragma unroll
+  for (int h = 0; h < HP; ++h) k[h] = ((float)(r.v[h] >> 8) * (1.0f / 16777216.0f) >= a.drop_p) ? inv_keep : 0.f;
 }
 
-template <int G>
-__device__ __forceinline__ void load_rows(const float *base, int64_t ld, int g0, int n, int lane, bool live,
-                                          float4 (&r)[G]) {
+// Stages x (one row, nq chunks) into sm[h][t], masked to head h's features.
+template <int HP>
+__device__ __forceinline__ void stage_masked(float4 (*sm)[32], const float *x, int nq, int dh, int lane) {
+  if (lane < nq) {
+    const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + lane);
+    const int hA = (4 * lane) / dh, hB = (4 * lane + 2) / dh;
 #pragma unroll
-  for (int c = 0; c < G; ++c)
-    r[c] = (c < n && live) ? __ldg(reinterpret_cast<const float4 *>(base + (int64_t)(g0 + c) * ld) + lane)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int h = 0; h < HP; ++h)
+      sm[h][lane] = make_float4(hA == h ? v.x : 0.f, hA == h ? v.y : 0.f, hB == h ? v.z : 0.f, hB == h ? v.w : 0.f);
+  }
+}
+
+// Lane-per-edge: out[h] = sum_t sm[h][t] . row[t] over the row's nq chunks.
+template <int HP>
+__device__ __forceinline__ void row_dots(const float *row, const float4 (*sm)[32], int nq, float (&out)[HP]) {
+#pragma unroll
+  for (int h = 0; h < HP; ++h) out[h] = 0.f;
+  const float4 *r4 = reinterpret_cast<const float4 *>(row);
+#pragma unroll 5
+  for (int t = 0; t < nq; ++t) {
+    const float4 k = __ldg(r4 + t);
+#pragma unroll
+    for (int h = 0; h < HP; ++h) {
+      const float4 m = sm[h][t];
+      out[h] = fmaf(m.x, k.x, fmaf(m.y, k.y, fmaf(m.z, k.z, fmaf(m.w, k.w, out[h]))));
+    }
+  }
 }
 
 template <int HP>
-__global__ void __launch_bounds__(32 * kWarpsPerCta, 2) k_attn_fwd_s(AttnArgs a) {
-  using SG = SGeom<HP, 8>;      // K and V rows of 8 edges in flight together
-  constexpr int G = SG::G, V = SG::V;
+__global__ void __launch_bounds__(32 * kWarpsPerCta, 4) k_attn_fwd_s(AttnArgs a) {
+  __shared__ float4 qm[kWarpsPerCta][HP][32];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int64_t n_dst = a.n_dst_dev ? min((int64_t)(*a.n_dst_dev), a.n_dst) : a.n_dst;
-  RowGeom geo{a.dim / 4, a.dim / a.heads, a.heads};
-  int hsel1[1][4];
-  lane_heads<1>(geo, lane, hsel1);
-  const int hs[4] = {hsel1[0][0], hsel1[0][1], hsel1[0][2], hsel1[0][3]};
+  const int nq = a.dim / 4, dh = a.dim / a.heads;
+  const bool live = lane < nq;
+  const int hA = live ? (4 * lane) / dh : 0, hB = live ? (4 * lane + 2) / dh : 0;
   const uint64_t doff = a.offset_dev ? *a.offset_dev : a.offset;
   const float inv_keep = a.drop_p > 0.f ? 1.f / (1.f - a.drop_p) : 1.f;
-  const bool live = lane < geo.nv4;
-  const int own = lane >> SG::S, oc = own >> SG::LH, oh = own & (HP - 1);
-  const bool writer = (lane & ((1 << SG::S) - 1)) == 0;
   const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
   if (a.n_dst_dev) {
     for (int64_t j = n_dst + (int64_t)blockIdx.x * kWarpsPerCta + w; j < a.n_dst;
@@ -535,205 +502,179 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta, 2) k_attn_fwd_s(AttnArgs a)
     const int beg = a.rptr[j], end = a.rptr[j + 1];
     float4 acc = zero4;
     if (end > beg) {
-      const float4 q = live ? __ldg(reinterpret_cast<const float4 *>(a.q + j * a.ldq) + lane) : zero4;
-      const bool one = end - beg <= G;
-      float m = -FLT_MAX, ssum = 0.f, ex = 0.f;       // running max / sum of the lane's own head
-      for (int g0 = beg; g0 < end; g0 += G) {
-        const int n = min(G, end - g0);
-        const bool valid = oc < n && oh < a.heads;
-        float4 kr[G], vr[G];
-        load_rows<G>(a.k, a.ldkv, g0, n, lane, live, kr);
-        load_rows<G>(a.v, a.ldkv, g0, n, lane, live, vr);
-        float v[V];
+      __syncwarp();
+      stage_masked<HP>(qm[w], a.q + j * a.ldq, nq, dh, lane);
+      __syncwarp();
+      const bool one = end - beg <= kEdgeGroup;
+      float m[HP], ssum[HP], ex[HP];
 #pragma unroll
-        for (int c = 0; c < G; ++c) {
-          float ph[HP];
-          head_partials<HP>(q, kr[c], hs, ph);
+      for (int h = 0; h < HP; ++h) { m[h] = -FLT_MAX; ssum[h] = 0.f; ex[h] = 0.f; }
+      for (int g0 = beg; g0 < end; g0 += kEdgeGroup) {
+        const int n = min(kEdgeGroup, end - g0);
+        const bool valid = lane < n;
+        const int64_t e = g0 + lane;
+        float z[HP];
+        if (valid) row_dots<HP>(a.k + e * a.ldkv, qm[w], nq, z);
+        float kp[HP];
+        keep_heads<HP>(a, doff, e, valid, inv_keep, kp);
+        float wt[HP], sc[HP];
 #pragma unroll
-          for (int h = 0; h < HP; ++h) v[c * HP + h] = ph[h];
+        for (int h = 0; h < HP; ++h) {
+          const bool ok = valid && h < a.heads;
+          const float zz = ok ? leaky(z[h], a.slope) : -FLT_MAX;
+          if (!one && ok) a.att_out[e * a.heads + h] = zz;          // raw; normalised below
+          const float mn = fmaxf(m[h], fb::warp_max(zz));
+          sc[h] = (m[h] == -FLT_MAX) ? 0.f : expf(m[h] - mn);
+          m[h] = mn;
+          ex[h] = ok ? expf(zz - mn) : 0.f;
+          ssum[h] = ssum[h] * sc[h] + fb::warp_sum(ex[h]);
+          wt[h] = ex[h] * kp[h];
         }
-        // every lane takes part in the reduction's shuffles; only then select
-        const float zr = xreduce_own<V>(v, lane);
-        const float z = valid ? leaky(zr, a.slope) : -FLT_MAX;
-        if (!one && writer && valid) a.att_out[(int64_t)(g0 + oc) * a.heads + oh] = z;   // raw, normalised below
-        const float mn = fmaxf(m, head_max<SG>(z));
-        const float sc = (m == -FLT_MAX) ? 0.f : expf(m - mn);
-        m = mn;
-        ex = valid ? expf(z - m) : 0.f;
-        ssum = ssum * sc + head_sum<SG>(ex);
-        const float wt = valid ? ex * keep_scale(a, doff, g0 + oc, oh, inv_keep) : 0.f;
-        float sch[HP];
+        const float sa = hv<HP>(sc, hA), sb = hv<HP>(sc, hB);
+        acc.x *= sa; acc.y *= sa; acc.z *= sb; acc.w *= sb;
+        // lane-per-feature weighted sum of the group's V rows
+#pragma unroll 4
+        for (int c = 0; c < n; ++c) {
+          float wc[HP];
 #pragma unroll
-        for (int h = 0; h < HP; ++h) sch[h] = pair_val<SG, HP>(sc, 0, h);
-        const float4 s4 = by_head<HP>(sch, hs);
-        acc.x *= s4.x; acc.y *= s4.y; acc.z *= s4.z; acc.w *= s4.w;
-#pragma unroll
-        for (int c = 0; c < G; ++c) {
-          if (c >= n) break;
-          float wh[HP];
-#pragma unroll
-          for (int h = 0; h < HP; ++h) wh[h] = pair_val<SG, HP>(wt, c, h);
-          const float4 w4 = by_head<HP>(wh, hs);
-          acc.x = fmaf(w4.x, vr[c].x, acc.x);
-          acc.y = fmaf(w4.y, vr[c].y, acc.y);
-          acc.z = fmaf(w4.z, vr[c].z, acc.z);
-          acc.w = fmaf(w4.w, vr[c].w, acc.w);
+          for (int h = 0; h < HP; ++h) wc[h] = __shfl_sync(0xffffffffu, wt[h], c);
+          const float wa = hv<HP>(wc, hA), wb = hv<HP>(wc, hB);
+          const float4 v = live ? __ldg(reinterpret_cast<const float4 *>(a.v + (int64_t)(g0 + c) * a.ldkv) + lane)
+                                : zero4;
+          acc.x = fmaf(wa, v.x, acc.x);
+          acc.y = fmaf(wa, v.y, acc.y);
+          acc.z = fmaf(wb, v.z, acc.z);
+          acc.w = fmaf(wb, v.w, acc.w);
         }
       }
-      const float inv = oh < a.heads ? 1.f / ssum : 0.f;      // for the lane's own head
-      float ih[HP];
+      float inv[HP];
 #pragma unroll
-      for (int h = 0; h < HP; ++h) ih[h] = pair_val<SG, HP>(inv, 0, h);
-      const float4 i4 = by_head<HP>(ih, hs);
-      acc.x *= i4.x; acc.y *= i4.y; acc.z *= i4.z; acc.w *= i4.w;
+      for (int h = 0; h < HP; ++h) inv[h] = h < a.heads ? 1.f / ssum[h] : 0.f;
+      const float ia = hv<HP>(inv, hA), ib = hv<HP>(inv, hB);
+      acc.x *= ia; acc.y *= ia; acc.z *= ib; acc.w *= ib;
       if (one) {
-        if (writer && oc < end - beg && oh < a.heads) a.att_out[(int64_t)(beg + oc) * a.heads + oh] = ex * inv;
-      } else {
-        float mh[HP];
+        if (lane < end - beg)
 #pragma unroll
-        for (int h = 0; h < HP; ++h) mh[h] = pair_val<SG, HP>(m, 0, h);
+          for (int h = 0; h < HP; ++h)
+            if (h < a.heads) a.att_out[(int64_t)(beg + lane) * a.heads + h] = ex[h] * inv[h];
+      } else {
         __syncwarp();
         for (int t = lane; t < (end - beg) * a.heads; t += 32) {
           const int h = t % a.heads;
-          float mm = 0.f, ii = 0.f;
-#pragma unroll
-          for (int hh = 0; hh < HP; ++hh)
-            if (h == hh) { mm = mh[hh]; ii = ih[hh]; }
           float *pz = a.att_out + (int64_t)beg * a.heads + t;
-          *pz = expf(*pz - mm) * ii;
+          *pz = expf(*pz - hv<HP>(m, h)) * hv<HP>(inv, h);
         }
       }
     }
     if (live) reinterpret_cast<float4 *>(a.agg + j * a.ldagg)[lane] = acc;
-    __syncwarp();
   }
 }
 
-constexpr int kStashGroups = 4;     // groups whose dL/dy the backward keeps in shared memory
-
 template <int HP>
-__global__ void __launch_bounds__(32 * kWarpsPerCta, 2) k_attn_bwd_s(AttnArgs a) {
-  using SG = SGeom<HP>;
-  constexpr int G = SG::G, V = SG::V;
-  __shared__ float stash[kWarpsPerCta][kStashGroups][32];
+__global__ void __launch_bounds__(32 * kWarpsPerCta, 4) k_attn_bwd_s(AttnArgs a) {
+  __shared__ float4 qm[kWarpsPerCta][HP][32];
+  __shared__ float4 dm[kWarpsPerCta][HP][32];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int64_t n_dst = a.n_dst_dev ? min((int64_t)(*a.n_dst_dev), a.n_dst) : a.n_dst;
-  RowGeom geo{a.dim / 4, a.dim / a.heads, a.heads};
-  int hsel1[1][4];
-  lane_heads<1>(geo, lane, hsel1);
-  const int hs[4] = {hsel1[0][0], hsel1[0][1], hsel1[0][2], hsel1[0][3]};
+  const int nq = a.dim / 4, dh = a.dim / a.heads;
+  const bool live = lane < nq;
+  const int hA = live ? (4 * lane) / dh : 0, hB = live ? (4 * lane + 2) / dh : 0;
   const uint64_t doff = a.offset_dev ? *a.offset_dev : a.offset;
   const float inv_keep = a.drop_p > 0.f ? 1.f / (1.f - a.drop_p) : 1.f;
-  const bool live = lane < geo.nv4;
-  const int own = lane >> SG::S, oc = own >> SG::LH, oh = own & (HP - 1);
   const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int64_t j = (int64_t)blockIdx.x * kWarpsPerCta + w; j < n_dst; j += (int64_t)gridDim.x * kWarpsPerCta) {
     const int beg = a.rptr[j], end = a.rptr[j + 1];
     float4 dq = zero4;
     if (end > beg) {
-      const float4 da = live ? __ldg(reinterpret_cast<const float4 *>(a.dagg + j * a.lddagg) + lane) : zero4;
-      const float4 q = live ? __ldg(reinterpret_cast<const float4 *>(a.q + j * a.ldq) + lane) : zero4;
-      // pass 1: dL/dy (through dropout) of each pair, sum_e y dL/dy per head, dV rows
-      float sd = 0.f, dl_one = 0.f, y_one = 0.f;
-      int gi = 0;
-      for (int g0 = beg; g0 < end; g0 += G, ++gi) {
-        const int n = min(G, end - g0);
-        const bool valid = oc < n && oh < a.heads;
-        float v[V];
-        {
-          float4 vr[G];
-          load_rows<G>(a.v, a.ldkv, g0, n, lane, live, vr);
+      __syncwarp();
+      stage_masked<HP>(qm[w], a.q + j * a.ldq, nq, dh, lane);
+      stage_masked<HP>(dm[w], a.dagg + j * a.lddagg, nq, dh, lane);
+      __syncwarp();
+      const float4 q4 = live ? __ldg(reinterpret_cast<const float4 *>(a.q + j * a.ldq) + lane) : zero4;
+      const float4 da4 = live ? __ldg(reinterpret_cast<const float4 *>(a.dagg + j * a.lddagg) + lane) : zero4;
+      const bool one = end - beg <= kEdgeGroup;
+      // pass 1: dL/dy through dropout (lane per edge), sum_e y dL/dy per head, dV rows
+      float sd[HP], dl1[HP], y1[HP];
 #pragma unroll
-          for (int c = 0; c < G; ++c) {
-            float ph[HP];
-            head_partials<HP>(da, vr[c], hs, ph);
+      for (int h = 0; h < HP; ++h) { sd[h] = 0.f; dl1[h] = 0.f; y1[h] = 0.f; }
+      for (int g0 = beg; g0 < end; g0 += kEdgeGroup) {
+        const int n = min(kEdgeGroup, end - g0);
+        const bool valid = lane < n;
+        const int64_t e = g0 + lane;
+        float d[HP], kp[HP], yk[HP];
+        if (valid) row_dots<HP>(a.v + e * a.ldkv, dm[w], nq, d);
+        keep_heads<HP>(a, doff, e, valid, inv_keep, kp);
 #pragma unroll
-            for (int h = 0; h < HP; ++h) v[c * HP + h] = ph[h];
-          }
+        for (int h = 0; h < HP; ++h) {
+          const bool ok = valid && h < a.heads;
+          const float y = ok ? __ldg(a.att + e * a.heads + h) : 0.f;
+          const float dl = ok ? d[h] * kp[h] : 0.f;
+          sd[h] += fb::warp_sum(y * dl);
+          dl1[h] = dl;
+          y1[h] = y;
+          yk[h] = y * kp[h];
         }
-        const float kp = valid ? keep_scale(a, doff, g0 + oc, oh, inv_keep) : 0.f;
-        const float dl = xreduce_own<V>(v, lane) * kp;
-        const float y = valid ? __ldg(a.att + (int64_t)(g0 + oc) * a.heads + oh) : 0.f;
-        sd += head_sum<SG>(y * dl);
-        if (gi < kStashGroups) stash[w][gi][lane] = dl;
-        dl_one = dl;
-        y_one = y;
         if (a.dv) {
-          const float yk = y * kp;
+#pragma unroll 4
+          for (int c = 0; c < n; ++c) {
+            float yc[HP];
 #pragma unroll
-          for (int c = 0; c < G; ++c) {
-            if (c >= n) break;
-            float yh[HP];
-#pragma unroll
-            for (int h = 0; h < HP; ++h) yh[h] = pair_val<SG, HP>(yk, c, h);
-            const float4 y4 = by_head<HP>(yh, hs);
+            for (int h = 0; h < HP; ++h) yc[h] = __shfl_sync(0xffffffffu, yk[h], c);
+            const float ya = hv<HP>(yc, hA), yb = hv<HP>(yc, hB);
             if (live)
               reinterpret_cast<float4 *>(a.dv + (int64_t)(g0 + c) * a.lddkv)[lane] =
-                  make_float4(y4.x * da.x, y4.y * da.y, y4.z * da.z, y4.w * da.w);
+                  make_float4(ya * da4.x, ya * da4.y, yb * da4.z, yb * da4.w);
           }
         }
       }
-      __syncwarp();
-      // pass 2: logits again, LeakyReLU and softmax backward, dK rows, dq
-      gi = 0;
-      for (int g0 = beg; g0 < end; g0 += G, ++gi) {
-        const int n = min(G, end - g0);
-        const bool valid = oc < n && oh < a.heads;
-        float dl, y;
-        if (end - beg <= G) {
-          dl = dl_one;
-          y = y_one;
+      // pass 2: logits again (lane per edge), LeakyReLU and softmax backward,
+      // dK rows and dq (lane per feature)
+      for (int g0 = beg; g0 < end; g0 += kEdgeGroup) {
+        const int n = min(kEdgeGroup, end - g0);
+        const bool valid = lane < n;
+        const int64_t e = g0 + lane;
+        float z[HP], dl[HP], y[HP], dz[HP];
+        if (valid) row_dots<HP>(a.k + e * a.ldkv, qm[w], nq, z);
+        if (one) {
+#pragma unroll
+          for (int h = 0; h < HP; ++h) { dl[h] = dl1[h]; y[h] = y1[h]; }
         } else {
-          y = valid ? __ldg(a.att + (int64_t)(g0 + oc) * a.heads + oh) : 0.f;
-          if (gi < kStashGroups) {
-            dl = stash[w][gi][lane];
-          } else {            // long segment: dL/dy again from the V rows
-            float u[V];
-            float4 vr[G];
-            load_rows<G>(a.v, a.ldkv, g0, n, lane, live, vr);
+          float d[HP], kp[HP];
+          if (valid) row_dots<HP>(a.v + e * a.ldkv, dm[w], nq, d);
+          keep_heads<HP>(a, doff, e, valid, inv_keep, kp);
 #pragma unroll
-            for (int c = 0; c < G; ++c) {
-              float ph[HP];
-              head_partials<HP>(da, vr[c], hs, ph);
-#pragma unroll
-              for (int h = 0; h < HP; ++h) u[c * HP + h] = ph[h];
-            }
-            const float kp = valid ? keep_scale(a, doff, g0 + oc, oh, inv_keep) : 0.f;
-            dl = xreduce_own<V>(u, lane) * kp;
+          for (int h = 0; h < HP; ++h) {
+            const bool ok = valid && h < a.heads;
+            y[h] = ok ? __ldg(a.att + e * a.heads + h) : 0.f;
+            dl[h] = ok ? d[h] * kp[h] : 0.f;
           }
         }
-        float4 kr[G];
-        load_rows<G>(a.k, a.ldkv, g0, n, lane, live, kr);
-        float v[V];
 #pragma unroll
-        for (int c = 0; c < G; ++c) {
-          float ph[HP];
-          head_partials<HP>(q, kr[c], hs, ph);
-#pragma unroll
-          for (int h = 0; h < HP; ++h) v[c * HP + h] = ph[h];
+        for (int h = 0; h < HP; ++h) {
+          const bool ok = valid && h < a.heads;
+          const float g = y[h] * (dl[h] - sd[h]);
+          dz[h] = ok ? (z[h] > 0.f ? g : g * a.slope) : 0.f;
         }
-        const float zt = xreduce_own<V>(v, lane);
-        const float g = y * (dl - sd);
-        const float dz = valid ? (zt > 0.f ? g : g * a.slope) : 0.f;
+#pragma unroll 4
+        for (int c = 0; c < n; ++c) {
+          float zc[HP];
 #pragma unroll
-        for (int c = 0; c < G; ++c) {
-          if (c >= n) break;
-          float zh[HP];
-#pragma unroll
-          for (int h = 0; h < HP; ++h) zh[h] = pair_val<SG, HP>(dz, c, h);
-          const float4 d4 = by_head<HP>(zh, hs);
-          if (a.dk && live)
-            reinterpret_cast<float4 *>(a.dk + (int64_t)(g0 + c) * a.lddkv)[lane] =
-                make_float4(d4.x * q.x, d4.y * q.y, d4.z * q.z, d4.w * q.w);
-          dq.x = fmaf(d4.x, kr[c].x, dq.x);
-          dq.y = fmaf(d4.y, kr[c].y, dq.y);
-          dq.z = fmaf(d4.z, kr[c].z, dq.z);
-          dq.w = fmaf(d4.w, kr[c].w, dq.w);
+          for (int h = 0; h < HP; ++h) zc[h] = __shfl_sync(0xffffffffu, dz[h], c);
+          const float za = hv<HP>(zc, hA), zb = hv<HP>(zc, hB);
+          if (live) {
+            const float4 k = __ldg(reinterpret_cast<const float4 *>(a.k + (int64_t)(g0 + c) * a.ldkv) + lane);
+            if (a.dk)
+              reinterpret_cast<float4 *>(a.dk + (int64_t)(g0 + c) * a.lddkv)[lane] =
+                  make_float4(za * q4.x, za * q4.y, zb * q4.z, zb * q4.w);
+            dq.x = fmaf(za, k.x, dq.x);
+            dq.y = fmaf(za, k.y, dq.y);
+            dq.z = fmaf(zb, k.z, dq.z);
+            dq.w = fmaf(zb, k.w, dq.w);
+          }
         }
       }
     }
     if (a.dq && live) reinterpret_cast<float4 *>(a.dq + j * (int64_t)a.dim)[lane] = dq;
-    __syncwarp();
   }
 }
 
@@ -771,12 +712,13 @@ int check_attn(const AttnArgs &a, bool bwd) {
   return FB_OK;
 }
 
-// The grouped kernels take rows of <= 128 floats with logits from q.k, one
-// output row per segment, and (backward) no pre-activation gradient output.
+// The edge-parallel kernels take rows of <= 128 floats with logits from q.k,
+// an even per-head width, one output row per segment, and (backward) no
+// pre-activation gradient output.
 // FB_GENERIC_ATTN in the environment forces the general kernels.
 bool short_path(const AttnArgs &a) {
   static const bool generic = getenv("FB_GENERIC_ATTN") != nullptr;
-  return !generic && a.dim <= 128 && !a.x && !a.seg_row && !a.dx && a.heads != 3;
+  return !generic && a.dim <= 128 && !a.x && !a.seg_row && !a.dx && a.heads != 3 && (a.dim / a.heads) % 2 == 0;
 }
 
 int launch_fwd(const AttnArgs &a, cudaStream_t stream) {

@@ -10,6 +10,11 @@
 // Rounding: torch's CPU Linear(1, d) produces w*dt + b with one rounding
 // (a fused multiply-add); with dt up to ~1e8 the argument of cos is large and
 // a second rounding changes the feature by O(1), so the kernel uses fmaf.
+// The backward evaluates sin of the fp32 argument in double precision: with
+// arguments of 1e5..1e8 radians the single-precision function takes its slow
+// argument-reduction path, which costs more than the double evaluation in the
+// long per-thread row loops of the reduction (measured on B200); the forward
+// keeps cosf, which measured faster in its wide gather.
 #include "runtime.cuh"
 
 namespace {
@@ -82,7 +87,7 @@ __global__ void __launch_bounds__(256) k_te_bwd_part(const float *__restrict__ g
     const float wc = __ldg(w + c), bc = __ldg(b + c);
     for (int64_t r = r0 + wp; r < r1; r += 8) {
       const float t = __ldg(dt + r);
-      const float gs = -sinf(fmaf(t, wc, bc)) * g[r * ldg + c];
+      const float gs = -(float)sin((double)fmaf(t, wc, bc)) * g[r * ldg + c];
       sw = fmaf(gs, t, sw);
       sb += gs;
     }
