@@ -131,14 +131,14 @@ class FusedStep:
         Q = torch.empty(Qin.shape[0], D, device=dev)
         ops.gemm_group([dict(kind=ops.NT, A=A, B=lp.W_kv, bias=lp.b_kv, out=KV, M_dev=E_dev),
                         dict(kind=ops.NT, A=Qin, B=L.w_q.weight, bias=L.w_q.bias, out=Q,
-                             M_dev=nd_dev if dn > 0 else None)])
+                             M_dev=nd_dev if dn > 0 else None)], name="gemm_group:kv_q")
         p_att = L.att_dropout_p if training else 0.0
         agg, att = ops.attn_fwd(Q, KV[:, :D], KV[:, D:], blk.rptr, L.num_head, L.negative_slope, p_att,
                                 0x5EED + l, 0, n_dst_dev=nd_dev, offset_dev=offset_dev)
         # w_out([agg | h_dst]) as one GEMM over the concatenation along K (h_dst = Qin[:, :dn])
         Z = torch.empty(nd, D, device=dev)
         ops.gemm_group([dict(kind=ops.NT, A=agg, A2=Qin[:, :dn] if dn > 0 else None, B=L.w_out.weight,
-                             bias=L.w_out.bias, out=Z, M_dev=nd_dev)])
+                             bias=L.w_out.bias, out=Z, M_dev=nd_dev)], name="gemm_group:w_out")
         p_drop = L.dropout.p if training else 0.0
         y, out = ops.layer_tail_fwd(Z, L.layer_norm.weight, L.layer_norm.bias, eps=L.layer_norm.eps, drop_p=p_drop,
                                     seed=0x7A11 + l, offset_dev=offset_dev, y=Z, n_dev=nd_dev,
@@ -175,7 +175,7 @@ class FusedStep:
             assert dh_rows >= nd + E
             dh = torch.empty(dh_rows, dn, device=dev)
             probs.append(dict(kind=ops.NN, A=dZ, B=Wo[:, D:], out=dh[:nd], M_dev=nd_dev))
-        ops.gemm_group(probs)
+        ops.gemm_group(probs, name="gemm_group:bwd_dz")
         KV = st["KV"]
         dQ, dKV = ops.attn_bwd(st["Q"], KV[:, :D], KV[:, D:], blk.rptr, st["att"], dagg, L.num_head,
                                L.negative_slope, st["p_att"], 0x5EED + l, 0, n_dst_dev=nd_dev,
@@ -197,7 +197,7 @@ class FusedStep:
             if dh is not None:
                 probs.append(dict(kind=ops.NN, A=dQ, B=L.w_q.weight[:, :dn], out=dh[:nd], accumulate=True,
                                   M_dev=nd_dev))
-        ops.gemm_group(probs)
+        ops.gemm_group(probs, name="gemm_group:bwd_dkv_dq")
         if dtime > 0:
             ops.time_encode_bwd(dA_t, blk.dt_edges, L.time_enc.w.weight.view(-1), L.time_enc.w.bias,
                                 g(L.time_enc.w.weight).view(-1), g(L.time_enc.w.bias), n_dev=E_dev)
@@ -237,7 +237,8 @@ class FusedStep:
         S = torch.empty(B, D, device=dev)
         P = torch.empty(2 * B, D, device=dev)
         ops.gemm_group([dict(kind=ops.NT, A=h[:B], B=ep.src_fc.weight, bias=ep.src_fc.bias, out=S),
-                        dict(kind=ops.NT, A=h[B:3 * B], B=ep.dst_fc.weight, bias=ep.dst_fc.bias, out=P)])
+                        dict(kind=ops.NT, A=h[B:3 * B], B=ep.dst_fc.weight, bias=ep.dst_fc.bias, out=P)],
+                       name="gemm_group:pred")
         dS = torch.empty(B, D, device=dev)
         dP = torch.empty(2 * B, D, device=dev)
         ops.edge_predictor_loss(S, P, ep.out_fc.weight.view(-1), ep.out_fc.bias, loss_out, dS, dP,
@@ -248,7 +249,7 @@ class FusedStep:
             dict(kind=ops.TN, A=dP, B=h[B:3 * B], out=ep.dst_fc.weight.grad, accumulate=True,
                  db=ep.dst_fc.bias.grad),
             dict(kind=ops.NN, A=dS, B=ep.src_fc.weight, out=dh[:B]),
-            dict(kind=ops.NN, A=dP, B=ep.dst_fc.weight, out=dh[B:3 * B])])
+            dict(kind=ops.NN, A=dP, B=ep.dst_fc.weight, out=dh[B:3 * B])], name="gemm_group:pred_bwd")
         for l in range(len(mfgs) - 1, -1, -1):
             rows = mfgs[l - 1].n_dst if l > 0 else 0
             dh = self._layer_bwd(l, saved[l], dh, rows)

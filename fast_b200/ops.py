@@ -57,6 +57,15 @@ def _launch(name, nbytes, flops, kernels, fn):
         TIMER.run(name, nbytes, flops, fn)
 
 
+def timed(name, fn):
+    """Runs fn (device work launched elsewhere, e.g. the sampler) under TIMER
+    when one is set; adds nothing to LAUNCHES."""
+    if TIMER is None:
+        fn()
+    else:
+        TIMER.run(name, 0, 0, fn)
+
+
 def _f32_rows(t, name):
     if t.dtype != torch.float32 or t.dim() != 2 or t.stride(1) != 1 or not t.is_cuda:
         raise ValueError("%s must be a CUDA fp32 matrix with unit column stride" % name)
@@ -143,7 +152,7 @@ def gemm_tn(G, X, out=None, accumulate=False, M_dev=None, db=None, db_accumulate
 NT, NN, TN = 0, 1, 2
 
 
-def gemm_group(problems):
+def gemm_group(problems, name="gemm_group"):
     """Runs independent GEMMs in one launch (+ one split-reduce for the TN
     ones).  Each problem is a dict: kind (NT / NN / TN), A, B (TN: X; may be
     None for a TN with K == 0), out, and optionally A2 / k1 (NT / NN: A's
@@ -151,7 +160,19 @@ def gemm_group(problems):
     Shapes: NT A [M, K], B [N, K]; NN A [M, K], B [K, N]; TN A = G [M, N],
     B = X [M, K], out [N, K]."""
     from .capi import GemmProblem
-    import ctypes
+    if USE_TC:
+        # NT problems the tcgen05 kernel takes run there, one launch each
+        rest = []
+        for p in problems:
+            A, B = p["A"], p.get("B")
+            if (p["kind"] == NT and p.get("A2") is None and A.shape[0] >= 256 and
+                    lib.fb_gemm_nt_tc_supported(ptr(A), A.stride(0), ptr(B), B.stride(0), B.shape[0], A.shape[1])):
+                gemm_nt_tc(A, B, p.get("bias"), p["out"], bool(p.get("accumulate", False)), p.get("M_dev"))
+            else:
+                rest.append(p)
+        problems = rest
+        if not problems:
+            return
     arr = (GemmProblem * len(problems))()
     nbytes, flops = 0, 0
     keep = []
@@ -187,7 +208,7 @@ def gemm_group(problems):
     n = len(problems)
     dev = problems[0]["A"].device
     ws = torch.empty(int(lib.fb_gemm_group_ws_bytes(arr, n)), device=dev, dtype=torch.uint8)
-    _launch("gemm_group", nbytes, flops, 2,
+    _launch(name, nbytes, flops, 2,
             lambda: call("fb_gemm_group", arr, n, ptr(ws), ws.numel(), stream_ptr()))
 
 

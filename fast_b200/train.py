@@ -162,7 +162,7 @@ class Trainer:
         pointers, as one process training on the whole batch would."""
         if self.world > 1 and global_roots is not None:
             self.sampler.update_pointers(global_roots, global_ts)
-        self.sampler.sample_device(roots, root_ts)
+        ops.timed("sampler", lambda: self.sampler.sample_device(roots, root_ts))
         return self._train_on(self.blocks())
 
     def step_host(self, roots_np, ts_np, global_roots_np=None, global_ts_np=None):
