@@ -84,6 +84,7 @@ _SIGS = {
     "fb_edge_predictor_loss": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _I, _P, _P, _I64, _P, _I64, _P, _P, _P,
                                     _P, _P]),
     "fb_q_time_bwd": (_I, [_P, _I, _P, _I64, _I, _I, _P, _P, _P, _I64, _P, _P, _P]),
+    "fb_adam_step": (_I, [_P, _P, _P, _P, _I64, _F, _F, _F, _F, _P, _P, _P]),
 }
 
 class GemmProblem(ctypes.Structure):

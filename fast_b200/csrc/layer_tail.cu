@@ -363,25 +363,30 @@ inline int pred_parts(int64_t B) {
 }
 
 // ---------------------------------------------------------------------------
-// Q-side parameter gradients that only need v = sum_rows dQ (one CTA):
+// Q-side parameter gradients that only need v = sum_rows dQ:
 //   db_q += v;  db_t[c] -= sin(b_t[c]) * sum_j v[j] W_q[j, dn + c]
 // (every Q row's time block is cos(b_t), TimeEncode of dt = 0) and, when the
 // Q input is that single row (no node features), dW_q[j, c] += v[j] qin0[c].
+// Blocks [0, nbc): one warp per time column c, lanes striding over j; the
+// remaining blocks: one thread per element of db_q and of dW_q.
 __global__ void k_q_time_bwd(const float *__restrict__ v, int D, const float *__restrict__ Wq, int64_t ldwq, int dn,
                              int dtime, const float *__restrict__ b_t, const float *__restrict__ qin0, float *dWq,
-                             int64_t lddwq, float *dbq, float *dbt) {
-  // one thread per output element: [dbq (D) | dbt (dtime) | dWq (D x K) when qin0]
+                             int64_t lddwq, float *dbq, float *dbt, int nbc) {
   const int K = dn + dtime;
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if ((int)blockIdx.x < nbc) {
+    const int c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (c >= dtime) return;
+    float s = 0.f;
+    for (int j = lane; j < D; j += 32) s = fmaf(v[j], Wq[(int64_t)j * ldwq + dn + c], s);
+    s = fb::warp_sum(s);
+    if (lane == 0) dbt[c] -= sinf(b_t[c]) * s;
+    return;
+  }
+  const int64_t i = (int64_t)(blockIdx.x - nbc) * blockDim.x + threadIdx.x;
   if (i < D) {
     dbq[i] += v[i];
-  } else if (i < D + dtime) {
-    const int c = (int)(i - D);
-    float s = 0.f;
-    for (int j = 0; j < D; ++j) s = fmaf(v[j], Wq[(int64_t)j * ldwq + dn + c], s);
-    dbt[c] -= sinf(b_t[c]) * s;
-  } else if (qin0 && i < D + dtime + (int64_t)D * K) {
-    const int64_t e = i - D - dtime;
+  } else if (qin0 && i < D + (int64_t)D * K) {
+    const int64_t e = i - D;
     const int j = (int)(e / K), c = (int)(e % K);
     dWq[(int64_t)j * lddwq + c] += v[j] * qin0[c];
   }
@@ -493,9 +498,10 @@ extern "C" int fb_q_time_bwd(const float *v, int D, const float *W_q, int64_t ld
   if (!v || !W_q || !db_q || D < 1 || dn < 0 || dtime < 0 || (dtime > 0 && (!b_t || !db_t)) ||
       (qin0 && !dW_q) || ldwq < dn + dtime)
     return fb::set_error(FB_ERR_ARG, "q_time_bwd: bad argument");
-  const int64_t n = D + dtime + (qin0 ? (int64_t)D * (dn + dtime) : 0);
-  k_q_time_bwd<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(v, D, W_q, ldwq, dn, dtime, b_t, qin0, dW_q, lddwq,
-                                                               db_q, db_t);
+  const int nbc = (dtime * 32 + 255) / 256;
+  const int64_t n = D + (qin0 ? (int64_t)D * (dn + dtime) : 0);
+  k_q_time_bwd<<<(unsigned)(nbc + (n + 255) / 256), 256, 0, stream>>>(v, D, W_q, ldwq, dn, dtime, b_t, qin0, dW_q,
+                                                                     lddwq, db_q, db_t, nbc);
   FB_LAUNCHED("k_q_time_bwd");
   return FB_OK;
 }

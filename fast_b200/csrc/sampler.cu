@@ -51,6 +51,7 @@ struct SampleArgs {
   uint32_t key0, key1, slot;
   const uint32_t *call_dev;  // sampler step counter (device)
   int32_t *err;
+  int32_t *pick;             // staging: the kept edge indices of root j at pick[j * neighs + i]
 };
 
 __device__ __forceinline__ int64_t num_roots(const SampleArgs &a) {
@@ -75,11 +76,10 @@ __device__ __forceinline__ void root_window(const SampleArgs &a, int n, float nt
   }
 }
 
-// Uniform pick number i of root j: s + floor(u * (e - s + 1)), u from Philox.
-__device__ __forceinline__ int uniform_pick(const SampleArgs &a, int64_t j, int i, int s, int e) {
-  fb::Philox4 r = fb::philox4x32_10((uint32_t)j, (uint32_t)(i >> 2), *a.call_dev, a.slot, a.key0, a.key1);
-  uint32_t u = r.v[i & 3];
-  uint32_t span = (uint32_t)(e - s + 1);
+// Uniform pick number i of root j: s + floor(u * (e - s + 1)), u the
+// (i % 4)-th word of Philox(j, i / 4; step, slot).
+__device__ __forceinline__ int uniform_pick_u(uint32_t u, int s, int e) {
+  const uint32_t span = (uint32_t)(e - s + 1);
   return s + (int)(((uint64_t)u * (uint64_t)span) >> 32);
 }
 
@@ -94,8 +94,13 @@ __device__ __forceinline__ void for_each_pick(const SampleArgs &a, int64_t j, in
     for (int k = e; k > lo; --k)
       if (__ldg(a.ts + k) < keep_thr) f(k);
   } else {
+    const uint32_t step = *a.call_dev;
+    fb::Philox4 r{};
     for (int i = 0; i < a.neighs; ++i) {
-      int k = uniform_pick(a, j, i, s, e);
+      if ((i & 3) == 0) r = fb::philox4x32_10((uint32_t)j, (uint32_t)(i >> 2), step, a.slot, a.key0, a.key1);
+      const int w = i & 3;
+      const uint32_t u = w == 0 ? r.v[0] : (w == 1 ? r.v[1] : (w == 2 ? r.v[2] : r.v[3]));
+      const int k = uniform_pick_u(u, s, e);
       if (__ldg(a.ts + k) < keep_thr) f(k);
     }
   }
@@ -133,7 +138,8 @@ __global__ void k_update_ptr(const int32_t *__restrict__ indptr, const float *__
   if (ub > beg) atomicMax(ptr + n, ub - 1);
 }
 
-// Pass 1: kept-edge count per root plus per-CTA partial sums (edges, non-empty rows).
+// Pass 1: kept-edge count per root, its picks staged for pass 3, plus per-CTA
+// partial sums (edges, non-empty rows).
 __global__ void __launch_bounds__(kThreads) k_sample_count(SampleArgs a, int32_t *__restrict__ cnt,
                                                            int2 *__restrict__ part) {
   __shared__ int sm[64];
@@ -143,7 +149,8 @@ __global__ void __launch_bounds__(kThreads) k_sample_count(SampleArgs a, int32_t
   if (j < R) {
     int n = a.roots[j];
     if (n >= 0 && n < a.n_nodes) {
-      for_each_pick(a, j, n, a.rts[j], [&](int) { ++c; });
+      int32_t *pk = a.pick + j * a.neighs;
+      for_each_pick(a, j, n, a.rts[j], [&](int k) { pk[c++] = k; });
     } else {
       atomicOr(a.err, kErrRootRange);
     }
@@ -182,7 +189,7 @@ __global__ void __launch_bounds__(1024) k_scan_parts(int2 *__restrict__ part, in
   }
 }
 
-// Pass 3: offsets from the CTA scan, then the COO/CSR writes.
+// Pass 3: offsets from the CTA scan, then the COO/CSR writes of the staged picks.
 __global__ void __launch_bounds__(kThreads) k_sample_write(SampleArgs a, const int32_t *__restrict__ cnt,
                                                            const int2 *__restrict__ part,
                                                            int32_t *__restrict__ row, int32_t *__restrict__ col,
@@ -209,7 +216,9 @@ __global__ void __launch_bounds__(kThreads) k_sample_write(SampleArgs a, const i
   if (c > 0) cntE[seg] = off;
   if (n < 0 || n >= a.n_nodes) return;
   int t = off;
-  for_each_pick(a, j, n, nts, [&](int k) {
+  const int32_t *pk = a.pick + j * a.neighs;   // the count pass's picks, in the reference order
+  for (int i = 0; i < c; ++i) {
+    const int k = pk[i];
     const float tk = __ldg(a.ts + k);
     const float d = __fsub_rn(nts, tk);
     const int32_t nb = __ldg(a.indices + k);
@@ -222,7 +231,7 @@ __global__ void __launch_bounds__(kThreads) k_sample_write(SampleArgs a, const i
     dte[t] = d;
     nbr[t] = nb;
     ++t;
-  });
+  }
 }
 
 // ---- eid dedup (combine_coo :414-451), first-appearance order -------------
@@ -324,6 +333,7 @@ struct fb_sampler {
   int64_t cap_r0 = 0;
   int32_t *ws_cnt = nullptr;
   int2 *ws_part = nullptr;
+  int32_t *ws_pick = nullptr;  // staged picks of the block being sampled
   int64_t ws_cap_roots = 0;
   int32_t *dd_keys = nullptr, *dd_minpos = nullptr, *dd_slot = nullptr, *dd_uidx = nullptr;
   int2 *dd_part = nullptr;
@@ -397,8 +407,13 @@ int ensure_capacity(fb_sampler *s, int64_t r0) {
   FB_TRY_CUDA(cudaMalloc(&s->rts_in, std::max<int64_t>(r0, 1) * 4));
   if (s->ws_cnt) cudaFree(s->ws_cnt);
   if (s->ws_part) cudaFree(s->ws_part);
+  if (s->ws_pick) cudaFree(s->ws_pick);
+  int64_t max_pick = 1;
+  for (size_t i = 0; i < cr.size(); ++i)
+    max_pick = std::max<int64_t>(max_pick, cr[i] * std::max(0, s->neigh[i / s->num_history]));
   FB_TRY_CUDA(cudaMalloc(&s->ws_cnt, std::max<int64_t>(max_roots, 1) * 4));
   FB_TRY_CUDA(cudaMalloc(&s->ws_part, nblk(max_roots) * sizeof(int2)));
+  FB_TRY_CUDA(cudaMalloc(&s->ws_pick, max_pick * 4));
   s->ws_cap_roots = max_roots;
   s->cap_r0 = r0;
   return FB_OK;
@@ -421,6 +436,7 @@ int run_layer_slot(fb_sampler *s, int bidx, const int32_t *roots, const float *r
   a.key0 = (uint32_t)s->seed; a.key1 = (uint32_t)(s->seed >> 32);
   a.call_dev = s->call_dev; a.slot = (uint32_t)bidx;
   a.err = s->err;
+  a.pick = s->ws_pick;
   int32_t *dims = s->dims + 8 * bidx;
   const int nb = nblk(R_cap);
   k_sample_count<<<nb, kThreads, 0, st>>>(a, s->ws_cnt, s->ws_part);
@@ -493,7 +509,7 @@ extern "C" int fb_sampler_destroy(fb_sampler *s) {
   if (s->owns_graph) {
     cudaFree(s->indptr); cudaFree(s->indices); cudaFree(s->eid); cudaFree(s->ts);
   }
-  void *ps[] = {s->ts_ptr, s->dims, s->err, s->call_dev, s->roots_in, s->rts_in, s->ws_cnt, s->ws_part,
+  void *ps[] = {s->ts_ptr, s->dims, s->err, s->call_dev, s->roots_in, s->rts_in, s->ws_cnt, s->ws_part, s->ws_pick,
                 s->dd_keys, s->dd_minpos, s->dd_slot, s->dd_uidx, s->dd_part};
   for (auto p : ps) if (p) cudaFree(p);
   cudaSetDevice(cur);

@@ -13,12 +13,13 @@ and its hand-derived backward as an explicit sequence of kernel launches:
                          d agg -> attention backward -> K|V grads -> time-encode
                          grads -> Q grads -> input gradient of the layer below
 
-Parameter gradients go straight into `.grad` tensors that are views of one
-flat buffer (`flat`), so there is no autograd graph, no gradient
-accumulation pass and one memset per step; the flat buffer is also what
-data-parallel training all-reduces.  w_k / w_v are re-seated as adjacent rows
-of one [2D, K] tensor (and their biases of one [2D] tensor), so K and V come
-from one GEMM; their state_dict names and shapes are unchanged.
+Parameters and their gradients are views of two flat buffers
+(`flat_params`, `flat`): gradients go straight into `.grad`, so there is no
+autograd graph, no gradient accumulation pass and one memset per step; the
+gradient buffer is what data-parallel training all-reduces and `FlatAdam`
+updates all parameters in one launch.  w_k / w_v are adjacent rows of one
+[2D, K] group (and their biases of one [2D] group), so K and V come from one
+GEMM; state_dict names and shapes are unchanged.
 
 Every launch honours device-side row counts (StaticBlock), so the step can
 be captured in a CUDA graph.
@@ -30,25 +31,12 @@ from . import ops
 _ALIGN = 64            # flat-buffer segments start on 256-byte boundaries
 
 
-def _seat_pair(a, b):
-    """Re-seat two Linear layers' weights (and biases) as adjacent rows of one
-    tensor; returns (W [2D, K], bias [2D])."""
-    D = a.weight.shape[0]
-    W = torch.cat([a.weight.data, b.weight.data], 0).contiguous()
-    bias = torch.cat([a.bias.data, b.bias.data], 0).contiguous()
-    a.weight = torch.nn.Parameter(W[:D])
-    b.weight = torch.nn.Parameter(W[D:])
-    a.bias = torch.nn.Parameter(bias[:D])
-    b.bias = torch.nn.Parameter(bias[D:])
-    return W, bias
-
-
 class _LayerParams:
     def __init__(self, layer):
         self.L = layer
         self.D = layer.dim_out
         self.dn, self.de, self.dtime = layer.dim_node_feat, layer.dim_edge_feat, layer.dim_time
-        self.W_kv, self.b_kv = _seat_pair(layer.w_k, layer.w_v)
+        self.W_kv = self.b_kv = None
         self.gW_kv = self.gb_kv = None
 
 
@@ -69,34 +57,55 @@ class FusedStep:
                 raise NotImplementedError("dim_out must be a multiple of 4")
         self.flat = self._build_flat()
 
-    # -- gradient storage -----------------------------------------------------
+    # -- parameter and gradient storage ---------------------------------------
     def _build_flat(self):
-        groups = []                      # (owner, shape, [(param, slice-or-None)])
+        """Re-seats every parameter as a view of one flat buffer (`flat_params`)
+        and gives it a .grad view at the same offset of the gradient buffer
+        (returned).  w_k / w_v (weights, and biases) become adjacent rows of
+        one group, so K and V come from one GEMM."""
+        m = self.model
+        names = {id(p): n for n, p in m.named_parameters()}
+        groups = []                      # (layer or None, kind, shape, [parameter names])
         seated = set()
         for lp in self.layers:
-            D = lp.D
-            groups.append(((lp, "gW_kv"), tuple(lp.W_kv.shape),
-                           [(lp.L.w_k.weight, slice(0, D)), (lp.L.w_v.weight, slice(D, 2 * D))]))
-            groups.append(((lp, "gb_kv"), tuple(lp.b_kv.shape),
-                           [(lp.L.w_k.bias, slice(0, D)), (lp.L.w_v.bias, slice(D, 2 * D))]))
-            seated.update(id(p) for p in (lp.L.w_k.weight, lp.L.w_v.weight, lp.L.w_k.bias, lp.L.w_v.bias))
-        for p in self.model.parameters():
+            L = lp.L
+            groups.append((lp, "W", (2 * lp.D, L.w_k.weight.shape[1]), [names[id(L.w_k.weight)],
+                                                                         names[id(L.w_v.weight)]]))
+            groups.append((lp, "b", (2 * lp.D,), [names[id(L.w_k.bias)], names[id(L.w_v.bias)]]))
+            seated.update(id(p) for p in (L.w_k.weight, L.w_v.weight, L.w_k.bias, L.w_v.bias))
+        for n_, p in m.named_parameters():
             if id(p) not in seated:
-                groups.append((None, tuple(p.shape), [(p, None)]))
+                groups.append((None, None, tuple(p.shape), [n_]))
         numel = lambda shape: int(torch.Size(shape).numel())
-        total = sum((numel(shape) + _ALIGN - 1) // _ALIGN * _ALIGN for _, shape, _ in groups)
-        dev = next(self.model.parameters()).device
-        flat = torch.zeros(total, device=dev, dtype=torch.float32)
+        total = sum((numel(shape) + _ALIGN - 1) // _ALIGN * _ALIGN for _, _, shape, _ in groups)
+        dev = next(m.parameters()).device
+        flat_p = torch.zeros(total, device=dev, dtype=torch.float32)
+        flat_g = torch.zeros(total, device=dev, dtype=torch.float32)
+        params = dict(m.named_parameters())
         off = 0
-        for owner, shape, members in groups:
+        for lp, kind, shape, members in groups:
             n = numel(shape)
-            view = flat[off:off + n].view(shape)
-            for p, sl in members:
-                p.grad = view if sl is None else view[sl]
-            if owner is not None:
-                setattr(owner[0], owner[1], view)
+            pv = flat_p[off:off + n].view(shape)
+            gv = flat_g[off:off + n].view(shape)
+            rows = 0
+            for name in members:
+                old = params[name]
+                r = old.shape[0]
+                sl = slice(rows, rows + r) if len(members) > 1 else slice(None)
+                pv[sl].copy_(old.data)
+                mod_name, attr = name.rsplit(".", 1)
+                new = torch.nn.Parameter(pv[sl])
+                setattr(m.get_submodule(mod_name), attr, new)
+                new.grad = gv[sl]
+                rows += r
+            if lp is not None:
+                if kind == "W":
+                    lp.W_kv, lp.gW_kv = pv, gv
+                else:
+                    lp.b_kv, lp.gb_kv = pv, gv
             off += (n + _ALIGN - 1) // _ALIGN * _ALIGN
-        return flat
+        self.flat_params = flat_p
+        return flat_g
 
     def parameters(self):
         return list(self.model.parameters())
@@ -254,3 +263,28 @@ class FusedStep:
             rows = mfgs[l - 1].n_dst if l > 0 else 0
             dh = self._layer_bwd(l, saved[l], dh, rows)
         return loss_out
+
+
+class FlatAdam:
+    """torch.optim.Adam (betas, eps; no weight decay, as the reference's
+    train.py:128 uses it) over FusedStep's flat parameter and gradient
+    buffers: one kernel per step, the step count on the device (CUDA-graph
+    safe)."""
+
+    def __init__(self, engine, lr, betas=(0.9, 0.999), eps=1e-8):
+        self.p, self.g = engine.flat_params, engine.flat
+        self.m = torch.zeros_like(self.p)
+        self.v = torch.zeros_like(self.p)
+        self.t = torch.zeros(1, dtype=torch.int64, device=self.p.device)
+        self.done = torch.zeros(1, dtype=torch.int32, device=self.p.device)
+        self.lr, self.betas, self.eps = float(lr), betas, float(eps)
+
+    def step(self):
+        from .capi import call, ptr, stream_ptr
+        ops._launch("adam", 4 * 7 * self.p.numel(), 0, 1,
+                    lambda: call("fb_adam_step", ptr(self.p), ptr(self.g), ptr(self.m), ptr(self.v), self.p.numel(),
+                                 self.lr, float(self.betas[0]), float(self.betas[1]), self.eps, ptr(self.t),
+                                 ptr(self.done), stream_ptr()))
+
+    def zero_grad(self, set_to_none=False):
+        self.g.zero_()

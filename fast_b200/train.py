@@ -16,7 +16,7 @@ import torch
 import torch.distributed as dist
 
 from . import ops
-from .engine import FusedStep
+from .engine import FlatAdam, FusedStep
 from .model import DeviceBlock, GeneralModel, StaticBlock
 from .ext import sampler_core
 
@@ -65,10 +65,11 @@ class Trainer:
         if world > 1:
             for p in self.model.parameters():   # identical start on every rank
                 dist.broadcast(p.data, 0)
-        # FusedStep re-seats w_k / w_v: build it before the optimizer sees the parameters
+        # FusedStep re-seats the parameters in flat buffers: build it before an optimizer sees them
         self.engine = FusedStep(self.model) if fused else None
         self.loss_buf = torch.zeros((), device=self.device)
-        self.opt = torch.optim.Adam(self.model.parameters(), lr=train_param["lr"])
+        self.opt = FlatAdam(self.engine, train_param["lr"]) if fused else \
+            torch.optim.Adam(self.model.parameters(), lr=train_param["lr"])
         self.crit = torch.nn.BCEWithLogitsLoss()
         dv = self.device
         self.indptr = torch.from_numpy(graph.indptr).to(dv)
@@ -205,7 +206,8 @@ class GraphTrainer(Trainer):
                 p.grad = self._flat[off:off + p.numel()].view_as(p)
                 off += p.numel()
         if optimizer == "adam":
-            self.opt = torch.optim.Adam(self._params, lr=train_param["lr"], capturable=True, fused=True)
+            self.opt = FlatAdam(self.engine, train_param["lr"]) if self.engine is not None else \
+                torch.optim.Adam(self._params, lr=train_param["lr"], capturable=True, fused=True)
         else:
             self.opt = torch.optim.SGD(self._params, lr=train_param["lr"])
         self.roots_buf = torch.zeros(self.R0, dtype=torch.int32, device=dv)

@@ -326,6 +326,15 @@ int fb_q_time_bwd(const float *v, int D, const float *W_q, int64_t ldwq, int dn,
                   const float *b_t, const float *qin0, float *dW_q, int64_t lddwq, float *db_q,
                   float *db_t, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------- */
+/* Optimizer (torch.optim.Adam, train.py:128) over one flat fp32 buffer.      */
+/* ------------------------------------------------------------------------- */
+/* p, g, m, v: n floats each, 16-byte aligned.  *step (device) is the number of
+ * steps taken so far and advances by one per call; *done (device, zero before
+ * the first call) is the call's CTA counter and is left at zero. */
+int fb_adam_step(float *p, const float *g, float *m, float *v, int64_t n, float lr, float beta1,
+                 float beta2, float eps, int64_t *step, uint32_t *done, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
