@@ -69,6 +69,55 @@ def peaks():
     return dict(hbm=6650.0, tf=1590.0, tf_sus=1400.0, src="fallback")
 
 
+class NvmlClockSampler:
+    """SM clock and clock-event reasons read through NVML every 2 ms on a
+    background thread while the timed region runs (it lasts well under a
+    second, too short for nvidia-smi's sampling period).  Reads only."""
+
+    BITS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
+
+    def __init__(self, gpu_index):
+        import pynvml
+        self.nv = pynvml
+        pynvml.nvmlInit()
+        self.h = pynvml.nvmlDeviceGetHandleByIndex(gpu_index)
+        self.samples, self.stop_flag, self.thread = [], False, None
+        get = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        self.reasons_of = lambda: get(self.h)
+
+    def _loop(self):
+        nv = self.nv
+        while not self.stop_flag:
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM), self.reasons_of()))
+            except Exception:   # noqa: BLE001 - a failed read skips one sample
+                pass
+            time.sleep(0.002)
+
+    def start(self):
+        import threading
+        self.thread = threading.Thread(target=self._loop, daemon=True)
+        self.thread.start()
+
+    def stop(self):
+        self.stop_flag = True
+        self.thread.join(timeout=5)
+        if not self.samples:
+            return None
+        mx = self.nv.nvmlDeviceGetMaxClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+        reasons = sorted({k for _, r in self.samples for k, b in self.BITS.items() if r & b})
+        return {"sm_mhz": float(np.median([c for c, _ in self.samples])), "sm_max_mhz": float(mx),
+                "reasons": reasons, "samples": len(self.samples), "source": "nvml, 2 ms"}
+
+
+def clock_sampler(gpu_index):
+    try:
+        return NvmlClockSampler(gpu_index)
+    except Exception:           # noqa: BLE001 - no NVML: fall back to nvidia-smi
+        return ClockSampler(gpu_index)
+
+
 class ClockSampler:
     """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
 
@@ -263,7 +312,7 @@ def run_fast(args):
     for i in warm:
         dev_step(i)
     torch.cuda.synchronize()
-    clock = ClockSampler(local)
+    clock = clock_sampler(local)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
