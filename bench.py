@@ -527,13 +527,13 @@ def run_kernel_suite(args):
           lambda: ops.gather_time_encode(E, f=table, f_idx=eid, dt=dts, w=w, b=b, out=A),
           "E=%d rows of [f(%d) | cos(%d)]" % (E, de, dt_))
     att_b = 4 * (Nd * D + 2 * E * D + (Nd + 1) + Nd * D + E * H)
-    timed("k_attn_fwd_s", att_b, 0,
+    timed("k_attn_fwd (bulk-copy path)", att_b, 0,
           lambda: ops.attn_fwd(q, kv[:, :D], kv[:, D:], rptr, H, 0.2, 0.1, 1, 2),
           "Nd=%d, E=%d, D=%d, H=%d, dropout 0.1" % (Nd, E, D, H))
     agg, att = ops.attn_fwd(q, kv[:, :D], kv[:, D:], rptr, H, 0.2, 0.1, 1, 2)
     dkv = torch.empty(E, 2 * D, device=dev)
     bwd_b = 4 * (2 * Nd * D + 2 * E * D + E * H + (Nd + 1) + 2 * E * D + Nd * D)
-    timed("k_attn_bwd_s", bwd_b, 0,
+    timed("k_attn_bwd (bulk-copy path)", bwd_b, 0,
           lambda: ops.attn_bwd(q, kv[:, :D], kv[:, D:], rptr, att, dagg, H, 0.2, 0.1, 1, 2, dkv=dkv),
           "Nd=%d, E=%d, D=%d, H=%d, dropout 0.1" % (Nd, E, D, H))
     y = torch.empty_like(z)

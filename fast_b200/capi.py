@@ -85,6 +85,7 @@ _SIGS = {
                                     _P, _P]),
     "fb_q_time_bwd": (_I, [_P, _I, _P, _I64, _I, _I, _P, _P, _P, _I64, _P, _P, _P]),
     "fb_adam_step": (_I, [_P, _P, _P, _P, _I64, _F, _F, _F, _F, _P, _P, _P]),
+    "fb_attn_error": (_I, [_P, _I]),
 }
 
 class GemmProblem(ctypes.Structure):

@@ -678,6 +678,315 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta, 4) k_attn_bwd_s(AttnArgs a)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Bulk-copy variants of the edge-parallel kernels, for the interleaved K|V
+// layout (V = K + dim, row stride 2 dim): a destination's edges are
+// consecutive rows, so a group's K and V rows are one contiguous block that a
+// single TMA bulk copy (cp.async.bulk, completion on an mbarrier, no
+// multicast) moves into the warp's shared-memory slot.  The whole group's
+// bytes are then in flight at once, where the register-fed kernels kept a few
+// 16-byte loads per lane in flight; K is read from DRAM once in the backward.
+// Every mbarrier wait is bounded: past the bound the warp records bit 2 in
+// g_attn_err (fb_attn_error), waits once more (bounded) for its copy, and
+// stops.
+
+constexpr int kBulkGroup = 12;                         // edges per copy
+constexpr int kBulkWarps = 4;                          // warps (destination slots) per CTA
+constexpr long long kBulkWaitCycles = 4000000000LL;    // ~2 s at 1.9 GHz
+__device__ int g_attn_err;
+
+__device__ __forceinline__ uint32_t sm_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void bar_init(uint64_t *bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(sm_addr(bar)) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ bool bar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(sm_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Lane 0: announce `bytes` and start the copy of [src, src + bytes) into dst.
+__device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sm_addr(bar)), "r"(bytes) : "memory");
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   sm_addr(dst)),
+               "l"(src), "r"(bytes), "r"(sm_addr(bar))
+               : "memory");
+}
+// Whole warp: true once the copy of this phase landed, warp-uniformly; false
+// (error recorded, one more bounded wait done) when it did not in time.
+__device__ __forceinline__ bool bulk_wait(uint64_t *bar, uint32_t parity) {
+  long long t0 = clock64();
+  bool ok = true;
+  while (!bar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kBulkWaitCycles) { ok = false; break; }
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok) {
+    if ((threadIdx.x & 31) == 0) atomicOr(&g_attn_err, 2);
+    t0 = clock64();
+    while (!bar_try_wait(bar, parity) && clock64() - t0 < kBulkWaitCycles) {
+    }
+  }
+  return ok;
+}
+// Orders the warp's earlier generic reads of its slot before the next copy.
+__device__ __forceinline__ void slot_release() {
+  __syncwarp();
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Lane-per-edge dot products against the masked rows in shared memory.
+template <int HP>
+__device__ __forceinline__ void row_dots_sm(const float *row, const float4 (*sm)[32], int nq, float (&out)[HP]) {
+#pragma unroll
+  for (int h = 0; h < HP; ++h) out[h] = 0.f;
+  const float4 *r4 = reinterpret_cast<const float4 *>(row);
+#pragma unroll 5
+  for (int t = 0; t < nq; ++t) {
+    const float4 k = r4[t];
+#pragma unroll
+    for (int h = 0; h < HP; ++h) {
+      const float4 m = sm[h][t];
+      out[h] = fmaf(m.x, k.x, fmaf(m.y, k.y, fmaf(m.z, k.z, fmaf(m.w, k.w, out[h]))));
+    }
+  }
+}
+
+template <int HP>
+__global__ void __launch_bounds__(32 * kBulkWarps) k_attn_fwd_b(AttnArgs a) {
+  extern __shared__ __align__(128) unsigned char smraw[];
+  __shared__ uint64_t bar[kBulkWarps];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int rowf = (int)a.ldkv;
+  float *slot = reinterpret_cast<float *>(smraw) + (size_t)w * kBulkGroup * rowf;
+  float4 (*qm)[32] =
+      reinterpret_cast<float4 (*)[32]>(smraw + (size_t)kBulkWarps * kBulkGroup * rowf * 4) + (size_t)w * HP;
+  const int64_t n_dst = a.n_dst_dev ? min((int64_t)(*a.n_dst_dev), a.n_dst) : a.n_dst;
+  const int nq = a.dim / 4, dh = a.dim / a.heads;
+  const bool live = lane < nq;
+  const int hA = live ? (4 * lane) / dh : 0, hB = live ? (4 * lane + 2) / dh : 0;
+  const uint64_t doff = a.offset_dev ? *a.offset_dev : a.offset;
+  const float inv_keep = a.drop_p > 0.f ? 1.f / (1.f - a.drop_p) : 1.f;
+  const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (lane == 0) bar_init(&bar[w]);
+  __syncwarp();
+  uint32_t phase = 0;
+  if (a.n_dst_dev) {
+    for (int64_t j = n_dst + (int64_t)blockIdx.x * kBulkWarps + w; j < a.n_dst;
+         j += (int64_t)gridDim.x * kBulkWarps)
+      if (live) reinterpret_cast<float4 *>(a.agg + j * a.ldagg)[lane] = zero4;
+  }
+  for (int64_t j = (int64_t)blockIdx.x * kBulkWarps + w; j < n_dst; j += (int64_t)gridDim.x * kBulkWarps) {
+    const int beg = a.rptr[j], end = a.rptr[j + 1];
+    float4 acc = zero4;
+    if (end > beg) {
+      slot_release();
+      stage_masked<HP>(qm, a.q + j * a.ldq, nq, dh, lane);
+      const bool one = end - beg <= kBulkGroup;
+      float m[HP], ssum[HP], ex[HP];
+#pragma unroll
+      for (int h = 0; h < HP; ++h) { m[h] = -FLT_MAX; ssum[h] = 0.f; ex[h] = 0.f; }
+      for (int g0 = beg; g0 < end; g0 += kBulkGroup) {
+        const int n = min(kBulkGroup, end - g0);
+        slot_release();
+        if (lane == 0) bulk_copy(slot, a.k + (int64_t)g0 * a.ldkv, (uint32_t)(n * rowf * 4), &bar[w]);
+        const bool ok = bulk_wait(&bar[w], phase);
+        phase ^= 1u;
+        if (!ok) return;
+        const bool valid = lane < n;
+        const int64_t e = g0 + lane;
+        float z[HP];
+        if (valid) row_dots_sm<HP>(slot + lane * rowf, qm, nq, z);
+        float kp[HP];
+        keep_heads<HP>(a, doff, e, valid, inv_keep, kp);
+        float wt[HP], sc[HP];
+#pragma unroll
+        for (int h = 0; h < HP; ++h) {
+          const bool okh = valid && h < a.heads;
+          const float zz = okh ? leaky(z[h], a.slope) : -FLT_MAX;
+          if (!one && okh) a.att_out[e * a.heads + h] = zz;          // raw; normalised below
+          const float mn = fmaxf(m[h], fb::warp_max(zz));
+          sc[h] = (m[h] == -FLT_MAX) ? 0.f : expf(m[h] - mn);
+          m[h] = mn;
+          ex[h] = okh ? expf(zz - mn) : 0.f;
+          ssum[h] = ssum[h] * sc[h] + fb::warp_sum(ex[h]);
+          wt[h] = ex[h] * kp[h];
+        }
+        const float sa = hv<HP>(sc, hA), sb = hv<HP>(sc, hB);
+        acc.x *= sa; acc.y *= sa; acc.z *= sb; acc.w *= sb;
+#pragma unroll 4
+        for (int c = 0; c < n; ++c) {
+          float wc[HP];
+#pragma unroll
+          for (int h = 0; h < HP; ++h) wc[h] = __shfl_sync(0xffffffffu, wt[h], c);
+          const float wa = hv<HP>(wc, hA), wb = hv<HP>(wc, hB);
+          const float4 v = live ? reinterpret_cast<const float4 *>(slot + c * rowf + a.dim)[lane] : zero4;
+          acc.x = fmaf(wa, v.x, acc.x);
+          acc.y = fmaf(wa, v.y, acc.y);
+          acc.z = fmaf(wb, v.z, acc.z);
+          acc.w = fmaf(wb, v.w, acc.w);
+        }
+      }
+      float inv[HP];
+#pragma unroll
+      for (int h = 0; h < HP; ++h) inv[h] = h < a.heads ? 1.f / ssum[h] : 0.f;
+      const float ia = hv<HP>(inv, hA), ib = hv<HP>(inv, hB);
+      acc.x *= ia; acc.y *= ia; acc.z *= ib; acc.w *= ib;
+      if (one) {
+        if (lane < end - beg)
+#pragma unroll
+          for (int h = 0; h < HP; ++h)
+            if (h < a.heads) a.att_out[(int64_t)(beg + lane) * a.heads + h] = ex[h] * inv[h];
+      } else {
+        __syncwarp();
+        for (int t = lane; t < (end - beg) * a.heads; t += 32) {
+          const int h = t % a.heads;
+          float *pz = a.att_out + (int64_t)beg * a.heads + t;
+          *pz = expf(*pz - hv<HP>(m, h)) * hv<HP>(inv, h);
+        }
+      }
+    }
+    if (live) reinterpret_cast<float4 *>(a.agg + j * a.ldagg)[lane] = acc;
+  }
+}
+
+template <int HP>
+__global__ void __launch_bounds__(32 * kBulkWarps) k_attn_bwd_b(AttnArgs a) {
+  extern __shared__ __align__(128) unsigned char smraw[];
+  __shared__ uint64_t bar[kBulkWarps];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int rowf = (int)a.ldkv;
+  float *slot = reinterpret_cast<float *>(smraw) + (size_t)w * kBulkGroup * rowf;
+  float4 (*qm)[32] =
+      reinterpret_cast<float4 (*)[32]>(smraw + (size_t)kBulkWarps * kBulkGroup * rowf * 4) + (size_t)w * 2 * HP;
+  float4 (*dm)[32] = qm + HP;
+  const int64_t n_dst = a.n_dst_dev ? min((int64_t)(*a.n_dst_dev), a.n_dst) : a.n_dst;
+  const int nq = a.dim / 4, dh = a.dim / a.heads;
+  const bool live = lane < nq;
+  const int hA = live ? (4 * lane) / dh : 0, hB = live ? (4 * lane + 2) / dh : 0;
+  const uint64_t doff = a.offset_dev ? *a.offset_dev : a.offset;
+  const float inv_keep = a.drop_p > 0.f ? 1.f / (1.f - a.drop_p) : 1.f;
+  const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (lane == 0) bar_init(&bar[w]);
+  __syncwarp();
+  uint32_t phase = 0;
+  for (int64_t j = (int64_t)blockIdx.x * kBulkWarps + w; j < n_dst; j += (int64_t)gridDim.x * kBulkWarps) {
+    const int beg = a.rptr[j], end = a.rptr[j + 1];
+    float4 dq = zero4;
+    if (end > beg) {
+      slot_release();
+      stage_masked<HP>(qm, a.q + j * a.ldq, nq, dh, lane);
+      stage_masked<HP>(dm, a.dagg + j * a.lddagg, nq, dh, lane);
+      const float4 q4 = live ? __ldg(reinterpret_cast<const float4 *>(a.q + j * a.ldq) + lane) : zero4;
+      const float4 da4 = live ? __ldg(reinterpret_cast<const float4 *>(a.dagg + j * a.lddagg) + lane) : zero4;
+      const bool one = end - beg <= kBulkGroup;
+      // pass 1: dL/dy through dropout (lane per edge, V rows), sum_e y dL/dy per head, dV rows
+      float sd[HP], dl1[HP], y1[HP];
+#pragma unroll
+      for (int h = 0; h < HP; ++h) { sd[h] = 0.f; dl1[h] = 0.f; y1[h] = 0.f; }
+      for (int g0 = beg; g0 < end; g0 += kBulkGroup) {
+        const int n = min(kBulkGroup, end - g0);
+        slot_release();
+        if (lane == 0) bulk_copy(slot, a.k + (int64_t)g0 * a.ldkv, (uint32_t)(n * rowf * 4), &bar[w]);
+        const bool ok = bulk_wait(&bar[w], phase);
+        phase ^= 1u;
+        if (!ok) return;
+        const bool valid = lane < n;
+        const int64_t e = g0 + lane;
+        float d[HP], kp[HP], yk[HP];
+        if (valid) row_dots_sm<HP>(slot + lane * rowf + a.dim, dm, nq, d);
+        keep_heads<HP>(a, doff, e, valid, inv_keep, kp);
+#pragma unroll
+        for (int h = 0; h < HP; ++h) {
+          const bool okh = valid && h < a.heads;
+          const float y = okh ? __ldg(a.att + e * a.heads + h) : 0.f;
+          const float dl = okh ? d[h] * kp[h] : 0.f;
+          sd[h] += fb::warp_sum(y * dl);
+          dl1[h] = dl;
+          y1[h] = y;
+          yk[h] = y * kp[h];
+        }
+        if (a.dv) {
+#pragma unroll 4
+          for (int c = 0; c < n; ++c) {
+            float yc[HP];
+#pragma unroll
+            for (int h = 0; h < HP; ++h) yc[h] = __shfl_sync(0xffffffffu, yk[h], c);
+            const float ya = hv<HP>(yc, hA), yb = hv<HP>(yc, hB);
+            if (live)
+              reinterpret_cast<float4 *>(a.dv + (int64_t)(g0 + c) * a.lddkv)[lane] =
+                  make_float4(ya * da4.x, ya * da4.y, yb * da4.z, yb * da4.w);
+          }
+        }
+      }
+      // pass 2: logits again (lane per edge, K rows), LeakyReLU and softmax
+      // backward, dK rows and dq (lane per feature); a single group is still
+      // in the slot
+      for (int g0 = beg; g0 < end; g0 += kBulkGroup) {
+        const int n = min(kBulkGroup, end - g0);
+        if (!one) {
+          slot_release();
+          if (lane == 0) bulk_copy(slot, a.k + (int64_t)g0 * a.ldkv, (uint32_t)(n * rowf * 4), &bar[w]);
+          const bool ok = bulk_wait(&bar[w], phase);
+          phase ^= 1u;
+          if (!ok) return;
+        }
+        const bool valid = lane < n;
+        const int64_t e = g0 + lane;
+        float z[HP], dl[HP], y[HP], dz[HP];
+        if (valid) row_dots_sm<HP>(slot + lane * rowf, qm, nq, z);
+        if (one) {
+#pragma unroll
+          for (int h = 0; h < HP; ++h) { dl[h] = dl1[h]; y[h] = y1[h]; }
+        } else {
+          float d[HP], kp[HP];
+          if (valid) row_dots_sm<HP>(slot + lane * rowf + a.dim, dm, nq, d);
+          keep_heads<HP>(a, doff, e, valid, inv_keep, kp);
+#pragma unroll
+          for (int h = 0; h < HP; ++h) {
+            const bool okh = valid && h < a.heads;
+            y[h] = okh ? __ldg(a.att + e * a.heads + h) : 0.f;
+            dl[h] = okh ? d[h] * kp[h] : 0.f;
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < HP; ++h) {
+          const bool okh = valid && h < a.heads;
+          const float g = y[h] * (dl[h] - sd[h]);
+          dz[h] = okh ? (z[h] > 0.f ? g : g * a.slope) : 0.f;
+        }
+#pragma unroll 4
+        for (int c = 0; c < n; ++c) {
+          float zc[HP];
+#pragma unroll
+          for (int h = 0; h < HP; ++h) zc[h] = __shfl_sync(0xffffffffu, dz[h], c);
+          const float za = hv<HP>(zc, hA), zb = hv<HP>(zc, hB);
+          if (live) {
+            const float4 k = reinterpret_cast<const float4 *>(slot + c * rowf)[lane];
+            if (a.dk)
+              reinterpret_cast<float4 *>(a.dk + (int64_t)(g0 + c) * a.lddkv)[lane] =
+                  make_float4(za * q4.x, za * q4.y, zb * q4.z, zb * q4.w);
+            dq.x = fmaf(za, k.x, dq.x);
+            dq.y = fmaf(za, k.y, dq.y);
+            dq.z = fmaf(zb, k.z, dq.z);
+            dq.w = fmaf(zb, k.w, dq.w);
+          }
+        }
+      }
+    }
+    if (a.dq && live) reinterpret_cast<float4 *>(a.dq + j * (int64_t)a.dim)[lane] = dq;
+  }
+}
+
 int attn_grid(int64_t n_dst) {
   static int sms_of[64] = {0};
   int dev = 0;
@@ -721,11 +1030,62 @@ bool short_path(const AttnArgs &a) {
   return !generic && a.dim <= 128 && !a.x && !a.seg_row && !a.dx && a.heads != 3 && (a.dim / a.heads) % 2 == 0;
 }
 
+// Bulk-copy kernels: the edge-parallel shapes with the interleaved K|V rows.
+bool bulk_path(const AttnArgs &a) {
+  static const bool off = getenv("FB_NO_BULK_ATTN") != nullptr;
+  return !off && short_path(a) && a.v == a.k + a.dim && a.ldkv == 2 * a.dim;
+}
+
+size_t bulk_smem(const AttnArgs &a, int hp, bool bwd) {
+  return (size_t)kBulkWarps * ((size_t)kBulkGroup * a.ldkv * 4 + (bwd ? 2 : 1) * (size_t)hp * 32 * 16);
+}
+
+int bulk_grid(int64_t n_dst) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>((n_dst + kBulkWarps - 1) / kBulkWarps, (int64_t)148 * 16));
+}
+
+// Opts a kernel into `bytes` of dynamic shared memory once per device.
+template <typename K>
+int allow_smem(K kernel, size_t bytes, int slot) {
+  static size_t done[8][64] = {};
+  int dev = 0;
+  FB_TRY_CUDA(cudaGetDevice(&dev));
+  size_t &d = done[slot & 7][dev & 63];
+  if (d < bytes) {
+    FB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    d = bytes;
+  }
+  return FB_OK;
+}
+
+template <int HP>
+int launch_bulk(const AttnArgs &a, bool bwd, cudaStream_t stream) {
+  const size_t sm = bulk_smem(a, HP, bwd);
+  const int grid = bulk_grid(a.n_dst);
+  const int slot = (HP == 1 ? 0 : (HP == 2 ? 1 : 2)) + (bwd ? 3 : 0);
+  int rc;
+  if (bwd) {
+    if ((rc = allow_smem(k_attn_bwd_b<HP>, sm, slot))) return rc;
+    k_attn_bwd_b<HP><<<grid, 32 * kBulkWarps, sm, stream>>>(a);
+    FB_LAUNCHED("k_attn_bwd_b");
+  } else {
+    if ((rc = allow_smem(k_attn_fwd_b<HP>, sm, slot))) return rc;
+    k_attn_fwd_b<HP><<<grid, 32 * kBulkWarps, sm, stream>>>(a);
+    FB_LAUNCHED("k_attn_fwd_b");
+  }
+  return FB_OK;
+}
+
 int launch_fwd(const AttnArgs &a, cudaStream_t stream) {
   int rc = check_attn(a, false);
   if (rc) return rc;
   if (a.n_dst == 0) return FB_OK;
   const int grid = attn_grid(a.n_dst), nv = (a.dim / 4 + 31) / 32;
+  if (bulk_path(a)) {
+    if (a.heads == 1) return launch_bulk<1>(a, false, stream);
+    if (a.heads == 2) return launch_bulk<2>(a, false, stream);
+    return launch_bulk<4>(a, false, stream);
+  }
   if (short_path(a)) {
     if (a.heads == 1) k_attn_fwd_s<1><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a);
     else if (a.heads == 2) k_attn_fwd_s<2><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a);
@@ -748,6 +1108,11 @@ int launch_bwd(const AttnArgs &a, cudaStream_t stream) {
   if (rc) return rc;
   if (a.n_dst == 0) return FB_OK;
   const int grid = attn_grid(a.n_dst), nv = (a.dim / 4 + 31) / 32;
+  if (bulk_path(a)) {
+    if (a.heads == 1) return launch_bulk<1>(a, true, stream);
+    if (a.heads == 2) return launch_bulk<2>(a, true, stream);
+    return launch_bulk<4>(a, true, stream);
+  }
   if (short_path(a)) {
     if (a.heads == 1) k_attn_bwd_s<1><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a);
     else if (a.heads == 2) k_attn_bwd_s<2><<<grid, 32 * kWarpsPerCta, 0, stream>>>(a);
@@ -774,6 +1139,16 @@ __global__ void k_dropout_scale(int64_t E, int heads, float p, uint64_t seed, ui
 }
 
 }  // namespace
+
+extern "C" int fb_attn_error(int *flags, int clear) {
+  if (!flags) return fb::set_error(FB_ERR_ARG, "attn_error: null flags");
+  FB_TRY_CUDA(cudaMemcpyFromSymbol(flags, g_attn_err, sizeof(int)));
+  if (clear) {
+    const int zero = 0;
+    FB_TRY_CUDA(cudaMemcpyToSymbol(g_attn_err, &zero, sizeof(int)));
+  }
+  return FB_OK;
+}
 
 extern "C" int fb_dropout_scale(int64_t n_edges, int heads, float drop_p, uint64_t seed, uint64_t offset, float *out,
                                 cudaStream_t stream) {

@@ -130,6 +130,10 @@ int fb_attn_bwd(const float *q, int64_t ldq, const float *k, const float *v, int
                 float slope, float drop_p, uint64_t seed, uint64_t offset, const uint64_t *offset_dev,
                 const float *att, const float *dagg, int64_t lddagg, float *dq, float *dk, float *dv,
                 int64_t lddkv, cudaStream_t stream);
+/* Sticky error bits of the attention kernels on the current device (2 = a
+ * bounded wait for a shared-memory bulk copy timed out and the warp gave up);
+ * synchronises; clear resets. */
+int fb_attn_error(int *flags, int clear);
 
 /* The dropout multipliers (0 or 1/(1-p)) fb_attn_fwd/bwd apply to edge e,
  * head h for (seed, offset): out[e*heads + h].  For checking and replay. */

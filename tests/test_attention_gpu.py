@@ -53,9 +53,13 @@ def _reference(q, k, v, row, n_dst, heads, slope, scale=None, per_edge_q=False):
     return agg, att
 
 
+@pytest.mark.parametrize("layout", ["kv_rows", "separate"])
 @pytest.mark.parametrize("heads,dim", [(2, 100), (2, 128), (4, 200), (1, 64)])
 @pytest.mark.parametrize("drop_p", [0.0, 0.1])
-def test_attention_fwd_bwd(cuda, heads, dim, drop_p):
+def test_attention_fwd_bwd(cuda, heads, dim, drop_p, layout):
+    """layout kv_rows: K and V interleaved in [E, 2D] rows (a destination's
+    rows move to shared memory by bulk copy); separate: K and V in their own
+    [E, D] tensors (register-fed kernels)."""
     from fast_b200 import ops
     from fast_b200.capi import call, ptr, stream_ptr
     rng = np.random.default_rng(heads * 1000 + dim)
@@ -84,16 +88,25 @@ def test_attention_fwd_bwd(cuda, heads, dim, drop_p):
         refs[dt] = dict(att=att_r.detach(), agg=agg_r.detach(), dq=qr.grad, dk=kr.grad, dv=vr.grad)
     # device
     qd, kvd, rp = q.to(cuda), kv.to(cuda), torch.from_numpy(rptr).to(cuda)
-    agg, att = ops.attn_fwd(qd, kvd[:, :dim], kvd[:, dim:], rp, heads, 0.2, drop_p, 123, 7)
-    dq, dkv = ops.attn_bwd(qd, kvd[:, :dim], kvd[:, dim:], rp, att, dagg.to(cuda), heads, 0.2, drop_p, 123, 7)
+    if layout == "kv_rows":
+        kd, vd = kvd[:, :dim], kvd[:, dim:]
+    else:
+        kd, vd = kvd[:, :dim].contiguous(), kvd[:, dim:].contiguous()
+    agg, att = ops.attn_fwd(qd, kd, vd, rp, heads, 0.2, drop_p, 123, 7)
+    dq, dkv = ops.attn_bwd(qd, kd, vd, rp, att, dagg.to(cuda), heads, 0.2, drop_p, 123, 7)
     got = dict(att=att, agg=agg, dq=dq, dk=dkv[:, :dim], dv=dkv[:, dim:])
     for name in got:
         parity(got[name], refs[torch.float64][name], refs[torch.float32][name], name)
     # rows without edges are exact zeros; results are bit-identical on rerun
     empty = np.where(np.diff(rptr) == 0)[0]
     assert torch.count_nonzero(agg[torch.from_numpy(empty).to(cuda)]) == 0
-    agg2, _ = ops.attn_fwd(qd, kvd[:, :dim], kvd[:, dim:], rp, heads, 0.2, drop_p, 123, 7)
+    agg2, _ = ops.attn_fwd(qd, kd, vd, rp, heads, 0.2, drop_p, 123, 7)
     assert torch.equal(agg, agg2)
+    from fast_b200.capi import call as c_call
+    import ctypes
+    flags = ctypes.c_int(0)
+    c_call("fb_attn_error", ctypes.byref(flags), 1)
+    assert flags.value == 0
 
 
 def test_attention_broadcast_q(cuda):
