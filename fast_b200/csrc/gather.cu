@@ -10,11 +10,12 @@
 // Rounding: torch's CPU Linear(1, d) produces w*dt + b with one rounding
 // (a fused multiply-add); with dt up to ~1e8 the argument of cos is large and
 // a second rounding changes the feature by O(1), so the kernel uses fmaf.
-// The backward evaluates sin of the fp32 argument in double precision: with
-// arguments of 1e5..1e8 radians the single-precision function takes its slow
-// argument-reduction path, which costs more than the double evaluation in the
-// long per-thread row loops of the reduction (measured on B200); the forward
-// keeps cosf, which measured faster in its wide gather.
+// The backward evaluates sin of the fp32 argument in double precision: for the
+// 1e5..1e8 radians of real timestamps the single-precision function takes its
+// slow argument-reduction path, which cost more than the double evaluation in
+// the long per-thread row loops of the reduction (measured on B200; choosing
+// per argument size measured slower still, the lanes of a warp diverge).  The
+// forward keeps cosf, which measured faster in its wide gather.
 #include "runtime.cuh"
 
 namespace {
@@ -39,10 +40,75 @@ struct GatherArgs {
   float *A; int64_t lda; int64_t n_rows; const int32_t *n_rows_dev;
 };
 
+// Batched form for 16-byte rows: a warp takes kBatch rows at a time, loads
+// their ids (one lane each), then issues every 16-byte load of the batch's
+// source rows before any store, so kBatch rows are in flight per warp instead
+// of one.  Rows up to 512 floats per source table.
+constexpr int kBatch = 4;
+constexpr int kMaxChunks = 4;                 // 16-byte chunks per lane per source row
+
+__device__ __forceinline__ void gather_rows(const float *__restrict__ src, int64_t ld, const int64_t (&row)[kBatch],
+                                            int nb, int nq, float *__restrict__ out0, int64_t lda, int lane) {
+  float4 v[kBatch][kMaxChunks];
+#pragma unroll
+  for (int i = 0; i < kBatch; ++i)
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int q = lane + 32 * c;
+      v[i][c] = (i < nb && q < nq) ? __ldg(reinterpret_cast<const float4 *>(src + row[i] * ld) + q)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+  for (int i = 0; i < kBatch; ++i)
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int q = lane + 32 * c;
+      if (i < nb && q < nq) reinterpret_cast<float4 *>(out0 + i * lda)[q] = v[i][c];
+    }
+}
+
+__global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode_batched(GatherArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n = a.n_rows_dev ? min((int64_t)(*a.n_rows_dev), a.n_rows) : a.n_rows;
+  const int64_t h_off = a.h_off + (a.h_off_dev ? (int64_t)(*a.h_off_dev) : 0);
+  const int64_t step = (int64_t)gridDim.x * kRowsPerCta * kBatch;
+  for (int64_t r0 = ((int64_t)blockIdx.x * kRowsPerCta + (threadIdx.x >> 5)) * kBatch; r0 < n; r0 += step) {
+    const int nb = (int)min((int64_t)kBatch, n - r0);
+    // ids and times of the batch: lane i loads row r0 + i's, then broadcast
+    int64_t hid = 0, fid = 0;
+    float tt = 0.f;
+    if (lane < nb) {
+      const int64_t r = r0 + lane;
+      hid = a.h_idx ? (int64_t)a.h_idx[r] : r + h_off;
+      fid = a.f_idx ? (int64_t)a.f_idx[r] : r;
+      tt = a.dt ? a.dt[r] : 0.f;
+    }
+    int64_t hr[kBatch], fr[kBatch];
+    float t[kBatch];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      hr[i] = __shfl_sync(0xffffffffu, hid, i);
+      fr[i] = __shfl_sync(0xffffffffu, fid, i);
+      t[i] = __shfl_sync(0xffffffffu, tt, i);
+    }
+    float *out0 = a.A + r0 * a.lda;
+    if (a.dn > 0) gather_rows(a.h, a.ldh, hr, nb, a.dn / 4, out0, a.lda, lane);
+    if (a.de > 0) gather_rows(a.f, a.ldf, fr, nb, a.de / 4, out0 + a.dn, a.lda, lane);
+    if (a.dtime > 0) {
+      for (int c = lane; c < a.dtime; c += 32) {
+        const float wc = __ldg(a.w + c), bc = __ldg(a.b + c);
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i)
+          if (i < nb) out0[i * a.lda + a.dn + a.de + c] = cosf(fmaf(t[i], wc, bc));
+      }
+    }
+  }
+}
+
 template <bool VEC>
 __global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode(GatherArgs a) {
   const int lane = threadIdx.x & 31;
-  const int64_t n = a.n_rows_dev ? (int64_t)(*a.n_rows_dev) : a.n_rows;
+  const int64_t n = a.n_rows_dev ? min((int64_t)(*a.n_rows_dev), a.n_rows) : a.n_rows;
   const int64_t h_off = a.h_off + (a.h_off_dev ? (int64_t)(*a.h_off_dev) : 0);
   for (int64_t r = (int64_t)blockIdx.x * kRowsPerCta + (threadIdx.x >> 5); r < n;
        r += (int64_t)gridDim.x * kRowsPerCta) {
@@ -145,8 +211,15 @@ extern "C" int fb_gather_time_encode(const float *h, int64_t ldh, const int32_t 
                    (ldf % 4 == 0 || de == 0) && a16(A) && (dn == 0 || a16(h)) && (de == 0 || a16(f));
   int64_t need = (n_rows + kRowsPerCta - 1) / kRowsPerCta;
   int grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, 148 * 16));
-  if (vec) k_gather_time_encode<true><<<grid, 32 * kRowsPerCta, 0, stream>>>(a);
-  else k_gather_time_encode<false><<<grid, 32 * kRowsPerCta, 0, stream>>>(a);
+  if (vec && dn <= 4 * 32 * kMaxChunks && de <= 4 * 32 * kMaxChunks) {
+    const int64_t need_b = (n_rows + kRowsPerCta * kBatch - 1) / (kRowsPerCta * kBatch);
+    const int grid_b = (int)std::max<int64_t>(1, std::min<int64_t>(need_b, 148 * 16));
+    k_gather_time_encode_batched<<<grid_b, 32 * kRowsPerCta, 0, stream>>>(a);
+  } else if (vec) {
+    k_gather_time_encode<true><<<grid, 32 * kRowsPerCta, 0, stream>>>(a);
+  } else {
+    k_gather_time_encode<false><<<grid, 32 * kRowsPerCta, 0, stream>>>(a);
+  }
   FB_LAUNCHED("k_gather_time_encode");
   return FB_OK;
 }
