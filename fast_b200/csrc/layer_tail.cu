@@ -17,7 +17,7 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int64_t kTailRowsMin = 64;
-constexpr int64_t kTailMaxParts = 296;
+constexpr int64_t kTailMaxParts = 1184;   // 8 CTAs per SM
 
 struct TailArgs {
   const float *z; int64_t ldz;        // fwd: w_out output (bias included)
@@ -87,8 +87,12 @@ __global__ void __launch_bounds__(32 * kWarps) k_tail_fwd(TailArgs a) {
   float4 g[NV], bt[NV];
   ld_row<NV>(a.gamma, lane, nq, g);
   ld_row<NV>(a.beta, lane, nq, bt);
-  for (int64_t r = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); r < a.n_rows;
-       r += (int64_t)gridDim.x * kWarps) {
+  const int64_t stride = (int64_t)gridDim.x * kWarps;
+  const int64_t rfirst = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  // the next row's z is loaded before this row is normalised
+  float4 vn[NV];
+  if (rfirst < n) ld_row<NV>(a.z + rfirst * a.ldz, lane, nq, vn);
+  for (int64_t r = rfirst; r < a.n_rows; r += stride) {
     float4 v[NV];
     if (r >= n) {
 #pragma unroll
@@ -96,7 +100,9 @@ __global__ void __launch_bounds__(32 * kWarps) k_tail_fwd(TailArgs a) {
       st_row<NV>(a.out + r * a.ldo, lane, nq, v);
       continue;
     }
-    ld_row<NV>(a.z + r * a.ldz, lane, nq, v);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) v[j] = vn[j];
+    if (r + stride < n) ld_row<NV>(a.z + (r + stride) * a.ldz, lane, nq, vn);
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
@@ -152,16 +158,26 @@ __global__ void __launch_bounds__(32 * kWarps) k_tail_bwd(TailArgs a) {
   ld_row<NV>(a.gamma, lane, nq, g);
 #pragma unroll
   for (int j = 0; j < NV; ++j) ag[j] = ab[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int64_t r = r0 + w; r < r1; r += kWarps) {
-    float4 y[NV], d[NV];
-    if (gated) {          // the forward output was a constant zero
+  if (gated) {            // the forward output was a constant zero
+    float4 zr[NV];
 #pragma unroll
-      for (int j = 0; j < NV; ++j) y[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-      st_row<NV>(a.dz + r * a.lddz, lane, nq, y);
-      continue;
+    for (int j = 0; j < NV; ++j) zr[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t r = r0 + w; r < r1; r += kWarps) st_row<NV>(a.dz + r * a.lddz, lane, nq, zr);
+  }
+  // the next row's loads are issued before this row is reduced
+  float4 yn[NV], dnx[NV];
+  if (!gated && r0 + w < r1) {
+    ld_row<NV>(a.y + (r0 + w) * a.ldy, lane, nq, yn);
+    ld_row<NV>(a.dout + (r0 + w) * a.lddo, lane, nq, dnx);
+  }
+  for (int64_t r = r0 + w; !gated && r < r1; r += kWarps) {
+    float4 y[NV], d[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) { y[j] = yn[j]; d[j] = dnx[j]; }
+    if (r + kWarps < r1) {
+      ld_row<NV>(a.y + (r + kWarps) * a.ldy, lane, nq, yn);
+      ld_row<NV>(a.dout + (r + kWarps) * a.lddo, lane, nq, dnx);
     }
-    ld_row<NV>(a.y + r * a.ldy, lane, nq, y);
-    ld_row<NV>(a.dout + r * a.lddo, lane, nq, d);
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) s += sum4(y[j]);
