@@ -763,6 +763,7 @@ __device__ __forceinline__ void row_dots_sm(const float *row, const float4 (*sm)
 
 template <int HP>
 __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_fwd_b(AttnArgs a) {
+  fb::pdl_enter();
   extern __shared__ __align__(128) unsigned char smraw[];
   __shared__ uint64_t bar[kBulkWarps];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -861,6 +862,7 @@ __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_fwd_b(AttnArgs a) {
 
 template <int HP>
 __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_bwd_b(AttnArgs a) {
+  fb::pdl_enter();
   extern __shared__ __align__(128) unsigned char smraw[];
   __shared__ uint64_t bar[kBulkWarps];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -1066,11 +1068,11 @@ int launch_bulk(const AttnArgs &a, bool bwd, cudaStream_t stream) {
   int rc;
   if (bwd) {
     if ((rc = allow_smem(k_attn_bwd_b<HP>, sm, slot))) return rc;
-    k_attn_bwd_b<HP><<<grid, 32 * kBulkWarps, sm, stream>>>(a);
+    FB_TRY_CUDA(fb::launch(k_attn_bwd_b<HP>, grid, 32 * kBulkWarps, sm, stream, a));
     FB_LAUNCHED("k_attn_bwd_b");
   } else {
     if ((rc = allow_smem(k_attn_fwd_b<HP>, sm, slot))) return rc;
-    k_attn_fwd_b<HP><<<grid, 32 * kBulkWarps, sm, stream>>>(a);
+    FB_TRY_CUDA(fb::launch(k_attn_fwd_b<HP>, grid, 32 * kBulkWarps, sm, stream, a));
     FB_LAUNCHED("k_attn_fwd_b");
   }
   return FB_OK;

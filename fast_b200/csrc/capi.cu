@@ -1,4 +1,5 @@
 // Error reporting and version entry points of the C ABI.
+#include <cstdlib>
 #include <string>
 #include "runtime.cuh"
 
@@ -19,3 +20,10 @@ int cuda_error(cudaError_t e, const char *where) {
 extern "C" const char *fb_last_error(void) { return fb::g_last_error.c_str(); }
 
 extern "C" const char *fb_version(void) { return "fast_b200 0.1 (sm_100a)"; }
+
+namespace fb {
+bool pdl_enabled() {
+  static const bool on = getenv("FB_NO_PDL") == nullptr;
+  return on;
+}
+}  // namespace fb

@@ -109,4 +109,13 @@ __host__ __device__ __forceinline__ int split_parts(int64_t n, int64_t rows_min,
   return (int)p;
 }
 
+// First statement of every kernel launched with fb::launch(): wait for the
+// previous grid in the stream (its writes visible), then allow the next one
+// to be scheduled.  Both are no-ops for a kernel launched without the
+// programmatic-dependency attribute.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 }  // namespace fb

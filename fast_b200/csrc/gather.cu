@@ -68,6 +68,7 @@ __device__ __forceinline__ void gather_rows(const float *__restrict__ src, int64
 }
 
 __global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode_batched(GatherArgs a) {
+  fb::pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t n = a.n_rows_dev ? min((int64_t)(*a.n_rows_dev), a.n_rows) : a.n_rows;
   const int64_t h_off = a.h_off + (a.h_off_dev ? (int64_t)(*a.h_off_dev) : 0);
@@ -107,6 +108,7 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode_batched
 
 template <bool VEC>
 __global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode(GatherArgs a) {
+  fb::pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t n = a.n_rows_dev ? min((int64_t)(*a.n_rows_dev), a.n_rows) : a.n_rows;
   const int64_t h_off = a.h_off + (a.h_off_dev ? (int64_t)(*a.h_off_dev) : 0);
@@ -139,6 +141,7 @@ __global__ void __launch_bounds__(256) k_te_bwd_part(const float *__restrict__ g
                                                      const float *__restrict__ dt, const float *__restrict__ w,
                                                      const float *__restrict__ b, int dtime, int64_t n_rows,
                                                      const int32_t *n_rows_dev, float *__restrict__ part) {
+  fb::pdl_enter();
   __shared__ float sw_s[8][32], sb_s[8][32];
   const int64_t n = n_rows_dev ? min((int64_t)(*n_rows_dev), n_rows) : n_rows;
   const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
@@ -174,6 +177,7 @@ __global__ void __launch_bounds__(256) k_te_bwd_part(const float *__restrict__ g
 // then a fixed shuffle tree (deterministic).
 __global__ void k_te_bwd_reduce(const float *__restrict__ part, int64_t n_rows, const int32_t *n_rows_dev, int dtime,
                                 float *dw, float *db) {
+  fb::pdl_enter();
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (c >= dtime) return;
   const int64_t n = n_rows_dev ? min((int64_t)(*n_rows_dev), n_rows) : n_rows;
@@ -214,11 +218,11 @@ extern "C" int fb_gather_time_encode(const float *h, int64_t ldh, const int32_t 
   if (vec && dn <= 4 * 32 * kMaxChunks && de <= 4 * 32 * kMaxChunks) {
     const int64_t need_b = (n_rows + kRowsPerCta * kBatch - 1) / (kRowsPerCta * kBatch);
     const int grid_b = (int)std::max<int64_t>(1, std::min<int64_t>(need_b, 148 * 16));
-    k_gather_time_encode_batched<<<grid_b, 32 * kRowsPerCta, 0, stream>>>(a);
+    FB_TRY_CUDA(fb::launch(k_gather_time_encode_batched, grid_b, 32 * kRowsPerCta, 0, stream, a));
   } else if (vec) {
-    k_gather_time_encode<true><<<grid, 32 * kRowsPerCta, 0, stream>>>(a);
+    FB_TRY_CUDA(fb::launch(k_gather_time_encode<true>, grid, 32 * kRowsPerCta, 0, stream, a));
   } else {
-    k_gather_time_encode<false><<<grid, 32 * kRowsPerCta, 0, stream>>>(a);
+    FB_TRY_CUDA(fb::launch(k_gather_time_encode<false>, grid, 32 * kRowsPerCta, 0, stream, a));
   }
   FB_LAUNCHED("k_gather_time_encode");
   return FB_OK;
@@ -239,9 +243,9 @@ extern "C" int fb_time_encode_bwd(const float *g, int64_t ldg, const float *dt, 
   const int parts = te_parts(n_rows);
   float *part = static_cast<float *>(ws);
   dim3 grid((dtime + 31) / 32, parts);
-  k_te_bwd_part<<<grid, 256, 0, stream>>>(g, ldg, dt, w, b, dtime, n_rows, n_rows_dev, part);
+  FB_TRY_CUDA(fb::launch(k_te_bwd_part, grid, 256, 0, stream, g, ldg, dt, w, b, dtime, n_rows, n_rows_dev, part));
   FB_LAUNCHED("k_te_bwd_part");
-  k_te_bwd_reduce<<<(dtime * 32 + 255) / 256, 256, 0, stream>>>(part, n_rows, n_rows_dev, dtime, dw, db);
+  FB_TRY_CUDA(fb::launch(k_te_bwd_reduce, (dtime * 32 + 255) / 256, 256, 0, stream, part, n_rows, n_rows_dev, dtime, dw, db));
   FB_LAUNCHED("k_te_bwd_reduce");
   return FB_OK;
 }

@@ -289,6 +289,7 @@ struct GroupArgs {
 };
 
 __global__ void __launch_bounds__(PT) k_gemm_group(const __grid_constant__ GroupArgs ga) {
+  fb::pdl_enter();
   __shared__ __align__(16) float As[PS][Tile<true>::SZ];
   __shared__ __align__(16) float Bs[PS][Tile<true>::SZ];
   int p = 0;
@@ -307,6 +308,7 @@ __global__ void __launch_bounds__(PT) k_gemm_group(const __grid_constant__ Group
 
 // Sums the TN partials of every TN problem of the group (fixed order).
 __global__ void k_group_reduce(const __grid_constant__ GroupArgs ga) {
+  fb::pdl_enter();
   int p = -1;
   for (int i = 0; i < ga.n; ++i)
     if (ga.p[i].kind == 2 && (int)blockIdx.x >= ga.red_start[i] && (int)blockIdx.x < ga.red_start[i + 1]) p = i;
@@ -464,10 +466,10 @@ extern "C" int fb_gemm_group(const fb_gemm_problem *probs, int n, void *ws, size
   ga.start[ga.n] = tiles;
   ga.red_start[ga.n] = red;
   if (ga.n > 0) {
-    k_gemm_group<<<tiles, PT, 0, stream>>>(ga);
+    FB_TRY_CUDA(fb::launch(k_gemm_group, tiles, PT, 0, stream, ga));
     FB_LAUNCHED("k_gemm_group");
     if (red > 0) {
-      k_group_reduce<<<red, 256, 0, stream>>>(ga);
+      FB_TRY_CUDA(fb::launch(k_group_reduce, red, 256, 0, stream, ga));
       FB_LAUNCHED("k_group_reduce");
     }
   }

@@ -79,6 +79,7 @@ __device__ __forceinline__ float4 keep4(const TailArgs &a, uint64_t off, int64_t
 // y = relu(dropout(z)); out = (y - mean) * rstd * gamma + beta
 template <int NV>
 __global__ void __launch_bounds__(32 * kWarps) k_tail_fwd(TailArgs a) {
+  fb::pdl_enter();
   const int lane = threadIdx.x & 31;
   const int nq = a.dim / 4;
   const int64_t n = (a.gate_dev && *a.gate_dev == 0) ? 0 : row_count(a.n_rows, a.n_rows_dev);
@@ -143,6 +144,7 @@ __global__ void __launch_bounds__(32 * kWarps) k_tail_fwd(TailArgs a) {
 // dout * xhat (gamma grad) and dout (beta grad) per CTA.
 template <int NV>
 __global__ void __launch_bounds__(32 * kWarps) k_tail_bwd(TailArgs a) {
+  fb::pdl_enter();
   __shared__ __align__(16) float sg[kWarps][128 * NV], sb[kWarps][128 * NV];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int nq = a.dim / 4;
@@ -241,6 +243,7 @@ __global__ void __launch_bounds__(32 * kWarps) k_tail_bwd(TailArgs a) {
 // dgamma/dbeta += sum of the partials (warp per column, fixed order).
 __global__ void k_tail_bwd_reduce(const float *__restrict__ part, int64_t n_rows, const int32_t *n_rows_dev, int dim,
                                   float *dgamma, float *dbeta) {
+  fb::pdl_enter();
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (c >= 2 * dim) return;
   const int parts = fb::split_parts(row_count(n_rows, n_rows_dev), kTailRowsMin, kTailMaxParts);
@@ -280,6 +283,7 @@ __device__ __forceinline__ float bce_logits(float x, float y) {
 // out_fc weight gradient, its bias gradient and the loss.
 template <int NV>
 __global__ void __launch_bounds__(32 * kPredWarps) k_pred_loss(PredArgs a) {
+  fb::pdl_enter();
   __shared__ __align__(16) float sw[kPredWarps][128 * NV];
   __shared__ float sl[kPredWarps], sbias[kPredWarps];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -361,6 +365,7 @@ __global__ void __launch_bounds__(32 * kPredWarps) k_pred_loss(PredArgs a) {
 // accumulate; the loss is written.
 __global__ void k_pred_reduce(const float *__restrict__ part, int parts, int dim, float invB, float *dw_o, float *db_o,
                               float *loss) {
+  fb::pdl_enter();
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (c >= dim + 2) return;
   float s = 0.f;
@@ -388,6 +393,7 @@ inline int pred_parts(int64_t B) {
 __global__ void k_q_time_bwd(const float *__restrict__ v, int D, const float *__restrict__ Wq, int64_t ldwq, int dn,
                              int dtime, const float *__restrict__ b_t, const float *__restrict__ qin0, float *dWq,
                              int64_t lddwq, float *dbq, float *dbt, int nbc) {
+  fb::pdl_enter();
   const int K = dn + dtime;
   if ((int)blockIdx.x < nbc) {
     const int c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -412,7 +418,7 @@ template <int NV>
 inline int launch_tail_fwd(const TailArgs &a, cudaStream_t st) {
   const int64_t need = (a.n_rows + kWarps - 1) / kWarps;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, 148 * 8));
-  k_tail_fwd<NV><<<grid, 32 * kWarps, 0, st>>>(a);
+  FB_TRY_CUDA(fb::launch(k_tail_fwd<NV>, grid, 32 * kWarps, 0, st, a));
   FB_LAUNCHED("k_tail_fwd");
   return FB_OK;
 }
@@ -420,10 +426,10 @@ inline int launch_tail_fwd(const TailArgs &a, cudaStream_t st) {
 template <int NV>
 inline int launch_tail_bwd(const TailArgs &a, cudaStream_t st, float *dgamma, float *dbeta) {
   const int parts = fb::split_parts(a.n_rows, kTailRowsMin, kTailMaxParts);
-  k_tail_bwd<NV><<<parts, 32 * kWarps, 0, st>>>(a);
+  FB_TRY_CUDA(fb::launch(k_tail_bwd<NV>, parts, 32 * kWarps, 0, st, a));
   FB_LAUNCHED("k_tail_bwd");
-  k_tail_bwd_reduce<<<(2 * a.dim * 32 + 255) / 256, 256, 0, st>>>(a.part, a.n_rows, a.n_rows_dev, a.dim, dgamma,
-                                                                   dbeta);
+  FB_TRY_CUDA(fb::launch(k_tail_bwd_reduce, (2 * a.dim * 32 + 255) / 256, 256, 0, st, a.part, a.n_rows, a.n_rows_dev, a.dim, dgamma,
+                                                                   dbeta));
   FB_LAUNCHED("k_tail_bwd_reduce");
   return FB_OK;
 }
@@ -497,13 +503,11 @@ extern "C" int fb_edge_predictor_loss(const float *S, int64_t lds, const float *
   const int parts = pred_parts(B);
   PredArgs a{S, lds, P, ldp, w_o, b_o, B, dim, loss, dS, ldds, dP, lddp, dw_o, db_o, scores, static_cast<float *>(ws)};
   const int nv = (dim / 4 + 31) / 32;
-  if (nv == 1) k_pred_loss<1><<<parts, 32 * kPredWarps, 0, stream>>>(a);
-  else if (nv == 2) k_pred_loss<2><<<parts, 32 * kPredWarps, 0, stream>>>(a);
-  else if (nv == 3) k_pred_loss<3><<<parts, 32 * kPredWarps, 0, stream>>>(a);
-  else k_pred_loss<4><<<parts, 32 * kPredWarps, 0, stream>>>(a);
+  void (*kern)(PredArgs) = nv == 1 ? k_pred_loss<1> : (nv == 2 ? k_pred_loss<2> : (nv == 3 ? k_pred_loss<3> : k_pred_loss<4>));
+  FB_TRY_CUDA(fb::launch(kern, parts, 32 * kPredWarps, 0, stream, a));
   FB_LAUNCHED("k_pred_loss");
-  k_pred_reduce<<<((dim + 2) * 32 + 255) / 256, 256, 0, stream>>>(a.part, parts, dim, 1.f / (float)B, dw_o, db_o,
-                                                                   loss);
+  FB_TRY_CUDA(fb::launch(k_pred_reduce, ((dim + 2) * 32 + 255) / 256, 256, 0, stream, a.part, parts, dim, 1.f / (float)B, dw_o, db_o,
+                                                                   loss));
   FB_LAUNCHED("k_pred_reduce");
   return FB_OK;
 }
@@ -516,8 +520,8 @@ extern "C" int fb_q_time_bwd(const float *v, int D, const float *W_q, int64_t ld
     return fb::set_error(FB_ERR_ARG, "q_time_bwd: bad argument");
   const int nbc = (dtime * 32 + 255) / 256;
   const int64_t n = D + (qin0 ? (int64_t)D * (dn + dtime) : 0);
-  k_q_time_bwd<<<(unsigned)(nbc + (n + 255) / 256), 256, 0, stream>>>(v, D, W_q, ldwq, dn, dtime, b_t, qin0, dW_q,
-                                                                     lddwq, db_q, db_t, nbc);
+  FB_TRY_CUDA(fb::launch(k_q_time_bwd, (unsigned)(nbc + (n + 255) / 256), 256, 0, stream, v, D, W_q, ldwq, dn, dtime, b_t, qin0, dW_q,
+                                                                     lddwq, db_q, db_t, nbc));
   FB_LAUNCHED("k_q_time_bwd");
   return FB_OK;
 }

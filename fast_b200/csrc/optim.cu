@@ -12,6 +12,7 @@ namespace {
 
 __global__ void k_adam(float *__restrict__ p, const float *__restrict__ g, float *__restrict__ m, float *__restrict__ v,
                        int64_t n, float lr, float b1, float b2, float eps, int64_t *step, uint32_t *done) {
+  fb::pdl_enter();
   const int64_t t = *step + 1;
   const float bc1 = 1.f - powf(b1, (float)t), bc2 = 1.f - powf(b2, (float)t);
   const float step_size = lr / bc1, inv_sqrt_bc2 = 1.f / sqrtf(bc2);
@@ -60,7 +61,7 @@ extern "C" int fb_adam_step(float *p, const float *g, float *m, float *v, int64_
     return fb::set_error(FB_ERR_ARG, "adam_step: buffers must be 16-byte aligned");
   const int64_t need = (n / 4 + 255) / 256;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, 148 * 4));
-  k_adam<<<grid, 256, 0, stream>>>(p, g, m, v, n, lr, beta1, beta2, eps, step, done);
+  FB_TRY_CUDA(fb::launch(k_adam, grid, 256, 0, stream, p, g, m, v, n, lr, beta1, beta2, eps, step, done));
   FB_LAUNCHED("k_adam");
   return FB_OK;
 }

@@ -106,7 +106,8 @@ __device__ __forceinline__ void for_each_pick(const SampleArgs &a, int64_t j, in
   }
 }
 
-__global__ void k_bump_call(uint32_t *call) { *call += 1; }
+__global__ void k_bump_call(uint32_t *call) {
+  fb::pdl_enter(); *call += 1; }
 
 __global__ void k_set_call(uint32_t *call, uint32_t v) { *call = v; }
 
@@ -126,6 +127,7 @@ __global__ void k_update_ptr(const int32_t *__restrict__ indptr, const float *__
                              int64_t n_nodes, int32_t *__restrict__ ptr, const int32_t *__restrict__ roots,
                              const float *__restrict__ rts, int64_t R_host, const int32_t *R_dev,
                              float offset, int32_t *err) {
+  fb::pdl_enter();
   int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   int64_t R = R_dev ? (int64_t)(*R_dev) : R_host;
   if (j >= R) return;
@@ -142,6 +144,7 @@ __global__ void k_update_ptr(const int32_t *__restrict__ indptr, const float *__
 // partial sums (edges, non-empty rows).
 __global__ void __launch_bounds__(kThreads) k_sample_count(SampleArgs a, int32_t *__restrict__ cnt,
                                                            int2 *__restrict__ part) {
+  fb::pdl_enter();
   __shared__ int sm[64];
   int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   int64_t R = num_roots(a);
@@ -166,6 +169,7 @@ __global__ void __launch_bounds__(kThreads) k_sample_count(SampleArgs a, int32_t
 __global__ void __launch_bounds__(1024) k_scan_parts(int2 *__restrict__ part, int nparts, int64_t R_host,
                                                      const int32_t *R_dev, int32_t *__restrict__ dims,
                                                      int32_t *__restrict__ rptr, int32_t *__restrict__ cntE) {
+  fb::pdl_enter();
   __shared__ int sm[64];
   int runA = 0, runB = 0;
   for (int base = 0; base < nparts; base += blockDim.x) {
@@ -197,6 +201,7 @@ __global__ void __launch_bounds__(kThreads) k_sample_write(SampleArgs a, const i
                                                            float *__restrict__ dts_out, int32_t *__restrict__ nodes_out,
                                                            int32_t *__restrict__ rptr, int32_t *__restrict__ cntE,
                                                            float *__restrict__ dte, int32_t *__restrict__ nbr) {
+  fb::pdl_enter();
   __shared__ int sm[64];
   int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   int64_t R = num_roots(a);
@@ -439,12 +444,12 @@ int run_layer_slot(fb_sampler *s, int bidx, const int32_t *roots, const float *r
   a.pick = s->ws_pick;
   int32_t *dims = s->dims + 8 * bidx;
   const int nb = nblk(R_cap);
-  k_sample_count<<<nb, kThreads, 0, st>>>(a, s->ws_cnt, s->ws_part);
+  FB_TRY_CUDA(fb::launch(k_sample_count, nb, kThreads, 0, st, a, s->ws_cnt, s->ws_part));
   FB_LAUNCHED("k_sample_count");
-  k_scan_parts<<<1, 1024, 0, st>>>(s->ws_part, nb, R_host, R_dev, dims, b.rptr, b.cntE);
+  FB_TRY_CUDA(fb::launch(k_scan_parts, 1, 1024, 0, st, s->ws_part, nb, R_host, R_dev, dims, b.rptr, b.cntE));
   FB_LAUNCHED("k_scan_parts");
-  k_sample_write<<<nb, kThreads, 0, st>>>(a, s->ws_cnt, s->ws_part, b.row, b.col, b.eid, b.ts, b.dts,
-                                          b.nodes, b.rptr, b.cntE, b.dte, b.nbr);
+  FB_TRY_CUDA(fb::launch(k_sample_write, nb, kThreads, 0, st, a, s->ws_cnt, s->ws_part, b.row, b.col, b.eid, b.ts, b.dts,
+                                          b.nodes, b.rptr, b.cntE, b.dte, b.nbr));
   FB_LAUNCHED("k_sample_write");
   return FB_OK;
 }
@@ -557,8 +562,8 @@ extern "C" int fb_sampler_sample(fb_sampler *s, const int32_t *roots, const floa
     }
     const int64_t rcap = cr[l * nh];
     if (use_ptr && rcap > 0) {
-      k_update_ptr<<<nblk(rcap), kThreads, 0, st>>>(s->indptr, s->ts, s->n_nodes, s->ts_ptr + (int64_t)nh * s->n_nodes,
-                                                    ur, ut, n_roots, uR, 0.f, s->err);
+      FB_TRY_CUDA(fb::launch(k_update_ptr, nblk(rcap), kThreads, 0, st, s->indptr, s->ts, s->n_nodes, s->ts_ptr + (int64_t)nh * s->n_nodes,
+                                                    ur, ut, n_roots, uR, 0.f, s->err));
       FB_LAUNCHED("k_update_ptr");
     }
     for (int i = 0; i < nh; ++i) {
@@ -571,16 +576,16 @@ extern "C" int fb_sampler_sample(fb_sampler *s, const int32_t *roots, const floa
       }
       const float offset = (float)(-i) * s->wd;
       if (use_ptr && fabsf(s->wd) > 1e-7f && rcap > 0) {
-        k_update_ptr<<<nblk(rcap), kThreads, 0, st>>>(s->indptr, s->ts, s->n_nodes,
+        FB_TRY_CUDA(fb::launch(k_update_ptr, nblk(rcap), kThreads, 0, st, s->indptr, s->ts, s->n_nodes,
                                                       s->ts_ptr + (int64_t)(nh - 1 - i) * s->n_nodes, hr, ht,
-                                                      n_roots, hR, offset - s->wd, s->err);
+                                                      n_roots, hR, offset - s->wd, s->err));
         FB_LAUNCHED("k_update_ptr");
       }
       rc = run_layer_slot(s, l * nh + nh - 1 - i, hr, ht, n_roots, hR, rcap, use_ptr, i, neighs, offset, st);
       if (rc) return rc;
     }
   }
-  k_bump_call<<<1, 1, 0, st>>>(s->call_dev);
+  FB_TRY_CUDA(fb::launch(k_bump_call, 1, 1, 0, st, s->call_dev));
   FB_LAUNCHED("k_bump_call");
   s->call_index++;
   s->sampled = true;
@@ -594,15 +599,15 @@ extern "C" int fb_sampler_update_pointers(fb_sampler *s, const int32_t *roots, c
   if (n_roots == 0) return FB_OK;
   // the first layer's pointer updates of sample(), for these roots only
   const int nh = s->num_history;
-  k_update_ptr<<<nblk(n_roots), kThreads, 0, st>>>(s->indptr, s->ts, s->n_nodes, s->ts_ptr + (int64_t)nh * s->n_nodes,
-                                                    roots, root_ts, n_roots, nullptr, 0.f, s->err);
+  FB_TRY_CUDA(fb::launch(k_update_ptr, nblk(n_roots), kThreads, 0, st, s->indptr, s->ts, s->n_nodes, s->ts_ptr + (int64_t)nh * s->n_nodes,
+                                                    roots, root_ts, n_roots, nullptr, 0.f, s->err));
   FB_LAUNCHED("k_update_ptr");
   for (int i = 0; i < nh; ++i) {
     const float offset = (float)(-i) * s->wd;
     if (fabsf(s->wd) > 1e-7f) {
-      k_update_ptr<<<nblk(n_roots), kThreads, 0, st>>>(s->indptr, s->ts, s->n_nodes,
+      FB_TRY_CUDA(fb::launch(k_update_ptr, nblk(n_roots), kThreads, 0, st, s->indptr, s->ts, s->n_nodes,
                                                         s->ts_ptr + (int64_t)(nh - 1 - i) * s->n_nodes, roots,
-                                                        root_ts, n_roots, nullptr, offset - s->wd, s->err);
+                                                        root_ts, n_roots, nullptr, offset - s->wd, s->err));
       FB_LAUNCHED("k_update_ptr");
     }
   }
