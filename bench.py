@@ -53,8 +53,8 @@ def parse():
                     help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--path", default="fused", choices=["fused", "autograd"],
                     help="training step as FusedStep kernels (fused) or the GeneralModel module under autograd")
-    ap.add_argument("--gemm", default="simt", choices=["simt", "tc"],
-                    help="projection GEMMs on the CUDA cores (simt) or the tcgen05 tensor cores (tc)")
+    ap.add_argument("--gemm", default="tc", choices=["tc", "ffma"],
+                    help="projection GEMMs on the tcgen05 tensor cores (tc, 3xTF32) or the CUDA cores (ffma)")
     return ap.parse_args()
 
 
@@ -283,6 +283,8 @@ def run_fast(args):
     from fast_b200 import ops
     from fast_b200.data import CONFIGS, make_features, make_graph, model_params
     ops.USE_TC = args.gemm == "tc"
+    if args.gemm == "ffma":
+        os.environ["FB_GEMM"] = "ffma"          # read by fb_gemm_group at every call
     from fast_b200.train import GraphTrainer, Trainer
     cfg = CONFIGS[args.config]
     graph = make_graph(cfg)
@@ -410,8 +412,9 @@ def run_fast(args):
         roof = {"kernel": name, "bound": "tensor", "achieved": round(ach, 3), "peak": pk["tf"], "unit": "TFLOP/s",
                 "frac": round(ach / pk["tf"], 5), "traffic": None,
                 "peak_source": "%s bf16 burst (MEASURED_PEAKS.json)" % pk["src"],
-                "note": "fp32 products on the CUDA cores (FFMA) unless --gemm tc; the bf16 tensor peak is the "
-                        "only measured compute denominator"}
+                "note": ("fp32-accurate products as three TF32 tcgen05 MMAs each (achieved counts 2MNK, "
+                         "not the 3x tensor work)" if args.gemm == "tc" else "fp32 products on the CUDA cores")
+                        + "; the bf16 tensor peak is the only measured compute denominator"}
     else:
         ach = r["bytes"] / (r["ms"] / 1000.0) / 1e9
         roof = {"kernel": name, "bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm"], "unit": "GB/s",

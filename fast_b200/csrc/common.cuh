@@ -109,6 +109,17 @@ __host__ __device__ __forceinline__ int split_parts(int64_t n, int64_t rows_min,
   return (int)p;
 }
 
+// Splits of a weight-gradient reduction over n rows: split_parts, raised to
+// at least one split per kTnRowsMax rows so that the running sum of a split
+// stays short (its rounding error grows with its length).  A function of n
+// alone, like split_parts.
+constexpr int64_t kTnRowsMax = 8192;
+__host__ __device__ __forceinline__ int tn_parts(int64_t n, int64_t rows_min, int64_t max_parts) {
+  const int p = split_parts(n, rows_min, max_parts);
+  const int64_t q = (n + kTnRowsMax - 1) / kTnRowsMax;
+  return q > p ? (int)q : p;
+}
+
 // First statement of every kernel launched with fb::launch(): wait for the
 // previous grid in the stream (its writes visible), then allow the next one
 // to be scheduled.  Both are no-ops for a kernel launched without the

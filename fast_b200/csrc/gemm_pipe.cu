@@ -12,7 +12,8 @@
 //
 // Each 16-deep slice is summed into a fresh register tile before it is added
 // to the running tile (two-level summation: error grows with the number of
-// slices, not of terms).  Shapes must have 16-byte aligned rows (leading
+// slices, not of terms); the long TN reductions add a third level, every 16
+// slices into a block total.  Shapes must have 16-byte aligned rows (leading
 // dimensions and contiguous extents multiples of 4, aligned bases); the
 // callers fall back to the register-staged kernels otherwise.
 #include <algorithm>
@@ -208,18 +209,19 @@ struct PTn {
 __device__ __forceinline__ void ptn_body(const PTn &a, float (*Gs)[Tile<true>::SZ], float (*Xs)[Tile<true>::SZ],
                                          int64_t k0, int64_t n0, int z) {
   const int64_t M = a.M_dev ? min((int64_t)(*a.M_dev), a.M) : a.M;
-  const int ns = fb::split_parts(M, a.rows_min, a.max_splits);
+  const int ns = fb::tn_parts(M, a.rows_min, a.max_splits);
   if (z >= ns) return;
   const int64_t per = ((M + ns - 1) / ns + PK - 1) / PK * PK;
   const int64_t s0 = (int64_t)z * per, s1 = min(M, s0 + per);
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const bool fix = a.ones && k0 <= a.K && a.K < k0 + PN;     // this tile holds the ones column
   const int nk = s1 > s0 ? (int)((s1 - s0 + PK - 1) / PK) : 0;
-  float acc[8][4];
+  // three-level sum: 16-row slices into acc, acc into tot every 16 slices
+  float acc[8][4], tot[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < 4; ++j) acc[i][j] = tot[i][j] = 0.f;
 #pragma unroll
   for (int s = 0; s < PS - 1; ++s) {
     if (s < nk) {
@@ -242,8 +244,18 @@ __device__ __forceinline__ void ptn_body(const PTn &a, float (*Gs)[Tile<true>::S
     }
     cp_commit();
     slice_fma<false, false>(acc, Gs[t % PS], Xs[t % PS], ty, tx);
+    if ((t & 15) == 15) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tot[i][j] += acc[i][j], acc[i][j] = 0.f;
+    }
   }
   cp_wait<0>();
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] += tot[i][j];
   const int Kout = a.K + (a.ones ? 1 : 0);
   float *out = a.P + (int64_t)z * a.N * a.ldp;
 #pragma unroll
@@ -318,7 +330,7 @@ __global__ void k_group_reduce(const __grid_constant__ GroupArgs ga) {
   const int Kp = q.t.K + (q.t.ones ? 1 : 0);
   if (i >= (int64_t)q.t.N * Kp) return;
   const int64_t M = q.t.M_dev ? min((int64_t)(*q.t.M_dev), q.t.M) : q.t.M;
-  const int nsplit = fb::split_parts(M, q.t.rows_min, q.t.max_splits);
+  const int nsplit = fb::tn_parts(M, q.t.rows_min, q.t.max_splits);
   const int n = (int)(i / Kp), k = (int)(i % Kp);
   float s = 0.f;
   for (int z = 0; z < nsplit; ++z) s += q.t.P[(int64_t)z * q.t.N * Kp + i];
@@ -364,7 +376,7 @@ int ptn_launch(const float *G, int64_t ldg, const float *X, int64_t ldx, float *
                int N, int K, bool ones, int max_splits, int64_t rows_min, cudaStream_t stream) {
   const int Kp = K + (ones ? 1 : 0);
   PTn a{G, ldg, X, ldx, P, Kp, M, M_dev, N, K, max_splits, rows_min, ones};
-  const int ns = fb::split_parts(M, rows_min, max_splits);
+  const int ns = fb::tn_parts(M, rows_min, max_splits);
   dim3 grid((Kp + PN - 1) / PN, (N + PM - 1) / PM, ns);
   k_ptn<<<grid, PT, 0, stream>>>(a);
   FB_LAUNCHED("k_ptn");
@@ -389,7 +401,7 @@ bool problem_pipelined(const fb_gemm_problem &p) {
 
 int64_t tn_ws_floats(const fb_gemm_problem &p) {
   const int Kp = p.K + (p.db ? 1 : 0);
-  const int64_t ns = fb::split_parts(p.M, kGroupRowsMin, fb::ptn_max_splits(p.N, Kp));
+  const int64_t ns = fb::tn_parts(p.M, kGroupRowsMin, fb::ptn_max_splits(p.N, Kp));
   return (ns * (int64_t)p.N * Kp + 63) / 64 * 64;
 }
 
@@ -400,7 +412,7 @@ extern "C" size_t fb_gemm_group_ws_bytes(const fb_gemm_problem *probs, int n) {
   for (int i = 0; i < n; ++i)
     if (probs[i].kind == FB_GEMM_TN && probs[i].M > 0) {
       const size_t own = problem_pipelined(probs[i]) ? 0 : fb_gemm_tn_ws_bytes(probs[i].M, probs[i].N, probs[i].K);
-      f += std::max<int64_t>(tn_ws_floats(probs[i]), (int64_t)((own + 3) / 4 + 63) / 64 * 64);
+      f += std::max({tn_ws_floats(probs[i]), (int64_t)((own + 3) / 4 + 63) / 64 * 64, fb::tc_ws_floats(probs[i])});
     }
   return (size_t)std::max<int64_t>(f, 64) * sizeof(float);
 }
@@ -414,6 +426,9 @@ extern "C" int fb_gemm_group(const fb_gemm_problem *probs, int n, void *ws, size
   int64_t off = 0;
   int tiles = 0, red = 0;
   std::vector<float *> ws_of(n, nullptr);
+  const bool use_tc = fb::tc_enabled();
+  std::vector<const fb_gemm_problem *> tc;   // problems for the tensor cores
+  std::vector<float *> tc_ws;
   for (int i = 0; i < n; ++i) {
     const fb_gemm_problem &p = probs[i];
     if (p.kind < FB_GEMM_NT || p.kind > FB_GEMM_TN || !p.A || !p.C || p.M < 0 || p.N < 1 || p.K < 0 ||
@@ -422,13 +437,18 @@ extern "C" int fb_gemm_group(const fb_gemm_problem *probs, int n, void *ws, size
     if (p.kind == FB_GEMM_TN && p.M > 0) {
       const size_t own = problem_pipelined(p) ? 0 : fb_gemm_tn_ws_bytes(p.M, p.N, p.K);
       ws_of[i] = wsf + off;
-      off += std::max<int64_t>(tn_ws_floats(p), (int64_t)((own + 3) / 4 + 63) / 64 * 64);
+      off += std::max({tn_ws_floats(p), (int64_t)((own + 3) / 4 + 63) / 64 * 64, fb::tc_ws_floats(p)});
     }
     if (p.M == 0) {
       if (p.kind == FB_GEMM_TN && !p.accumulate) {   // an empty sum is zero
         for (int r = 0; r < p.N; ++r) FB_TRY_CUDA(cudaMemsetAsync(p.C + (int64_t)r * p.ldc, 0, p.K * 4, stream));
         if (p.db && !p.db_accumulate) FB_TRY_CUDA(cudaMemsetAsync(p.db, 0, p.N * 4, stream));
       }
+      continue;
+    }
+    if (use_tc && fb::tc_problem_ok(p)) {
+      tc.push_back(&probs[i]);
+      tc_ws.push_back(ws_of[i]);
       continue;
     }
     if (!problem_pipelined(p) || ga.n == kMaxGroup) {
@@ -448,7 +468,7 @@ extern "C" int fb_gemm_group(const fb_gemm_problem *probs, int n, void *ws, size
                 kGroupRowsMin, p.db != nullptr};
       q.kt = (Kp + PN - 1) / PN;
       q.ntn = (p.N + PM - 1) / PM;
-      const int ns = fb::split_parts(p.M, kGroupRowsMin, ms);
+      const int ns = fb::tn_parts(p.M, kGroupRowsMin, ms);
       tiles += q.kt * q.ntn * ns;
       ga.red_start[ga.n] = red;
       red += (int)(((int64_t)p.N * Kp + 255) / 256);
@@ -465,6 +485,10 @@ extern "C" int fb_gemm_group(const fb_gemm_problem *probs, int n, void *ws, size
   }
   ga.start[ga.n] = tiles;
   ga.red_start[ga.n] = red;
+  if (!tc.empty()) {
+    const int rc = fb::tc_group(tc.data(), tc_ws.data(), (int)tc.size(), stream);
+    if (rc != FB_OK) return rc;
+  }
   if (ga.n > 0) {
     FB_TRY_CUDA(fb::launch(k_gemm_group, tiles, PT, 0, stream, ga));
     FB_LAUNCHED("k_gemm_group");

@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(NT) k_gemm_tn(const float *__restrict__ G, int
   const int64_t M = M_dev ? min((int64_t)(*M_dev), M_host) : M_host;
   const int n0 = blockIdx.y * BM, k0 = blockIdx.x * BN;
   // the partition comes from the true row count, not from the launch
-  const int ns = fb::split_parts(M, kTnRowsMin, max_splits);
+  const int ns = fb::tn_parts(M, kTnRowsMin, max_splits);
   if ((int)blockIdx.z >= ns) return;
   const int64_t per = ((M + ns - 1) / ns + BK - 1) / BK * BK;
   const int64_t s0 = (int64_t)blockIdx.z * per;
@@ -188,7 +188,7 @@ __global__ void k_split_reduce(const float *__restrict__ P, int64_t M_host, cons
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)N * Kp) return;
   const int64_t M = M_dev ? min((int64_t)(*M_dev), M_host) : M_host;
-  const int nsplit = fb::split_parts(M, kTnRowsMin, max_splits);
+  const int nsplit = fb::tn_parts(M, kTnRowsMin, max_splits);
   const int n = (int)(i / Kp), k = (int)(i % Kp);
   float s = 0.f;
   for (int p = 0; p < nsplit; ++p) s += P[(int64_t)p * N * Kp + i];
@@ -300,8 +300,8 @@ extern "C" size_t fb_gemm_tn_ws_bytes(int64_t M, int N, int K) {
   // room for either kernel family, with or without the bias column
   int64_t most = 0;
   for (int Kp = K; Kp <= K + 1; ++Kp) {
-    const int64_t a = fb::split_parts(M, kTnRowsMin, tn_max_splits(N, Kp));
-    const int64_t b = fb::split_parts(M, kTnRowsMin, fb::ptn_max_splits(N, Kp));
+    const int64_t a = fb::tn_parts(M, kTnRowsMin, tn_max_splits(N, Kp));
+    const int64_t b = fb::tn_parts(M, kTnRowsMin, fb::ptn_max_splits(N, Kp));
     most = std::max(most, std::max(a, b) * (int64_t)N * Kp);
   }
   return (size_t)most * sizeof(float);
@@ -323,7 +323,7 @@ extern "C" int fb_gemm_tn_bias(const float *G, int64_t ldg, const float *X, int6
     const int rc = fb::ptn_launch(G, ldg, X, ldx, P, M, M_dev, N, K, ones, max_splits, kTnRowsMin, stream);
     if (rc != FB_OK) return rc;
   } else {
-    const int ns = fb::split_parts(M, kTnRowsMin, max_splits);
+    const int ns = fb::tn_parts(M, kTnRowsMin, max_splits);
     const bool vecG = (ldg % 4 == 0) && al16(G), vecX = (ldx % 4 == 0) && al16(X);
     dim3 grid((Kp + BN - 1) / BN, (N + BM - 1) / BM, ns);
     k_gemm_tn<<<grid, NT, 0, stream>>>(G, ldg, X, ldx, P, Kp, M, M_dev, N, K, max_splits, vecG, vecX, ones);

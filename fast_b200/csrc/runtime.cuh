@@ -19,6 +19,14 @@ int cuda_error(cudaError_t e, const char *where);
 // attribute off (plain stream order).
 bool pdl_enabled();
 
+// Projection GEMMs on the tensor cores (gemm_tc.cu).  fb_gemm_group sends every
+// problem tc_problem_ok accepts there unless FB_GEMM=ffma is set in the
+// environment (then the CUDA-core kernels of gemm_pipe.cu run everything).
+bool tc_enabled();
+bool tc_problem_ok(const fb_gemm_problem &p);
+int64_t tc_ws_floats(const fb_gemm_problem &p);   // TN partial sums, floats
+int tc_group(const fb_gemm_problem *const *probs, float *const *ws, int n, cudaStream_t stream);
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                    Args &&...args) {

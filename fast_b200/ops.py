@@ -154,25 +154,13 @@ NT, NN, TN = 0, 1, 2
 
 def gemm_group(problems, name="gemm_group"):
     """Runs independent GEMMs in one launch (+ one split-reduce for the TN
-    ones).  Each problem is a dict: kind (NT / NN / TN), A, B (TN: X; may be
+    ones): on the tcgen05 tensor cores (3xTF32), or on the CUDA cores when
+    FB_GEMM=ffma is set in the environment.  Each problem is a dict: kind (NT / NN / TN), A, B (TN: X; may be
     None for a TN with K == 0), out, and optionally A2 / k1 (NT / NN: A's
     columns >= k1 come from A2), bias, M_dev, accumulate, db, db_accumulate.
     Shapes: NT A [M, K], B [N, K]; NN A [M, K], B [K, N]; TN A = G [M, N],
     B = X [M, K], out [N, K]."""
     from .capi import GemmProblem
-    if USE_TC:
-        # NT problems the tcgen05 kernel takes run there, one launch each
-        rest = []
-        for p in problems:
-            A, B = p["A"], p.get("B")
-            if (p["kind"] == NT and p.get("A2") is None and A.shape[0] >= 256 and
-                    lib.fb_gemm_nt_tc_supported(ptr(A), A.stride(0), ptr(B), B.stride(0), B.shape[0], A.shape[1])):
-                gemm_nt_tc(A, B, p.get("bias"), p["out"], bool(p.get("accumulate", False)), p.get("M_dev"))
-            else:
-                rest.append(p)
-        problems = rest
-        if not problems:
-            return
     arr = (GemmProblem * len(problems))()
     nbytes, flops = 0, 0
     keep = []
