@@ -283,8 +283,6 @@ def run_fast(args):
     from fast_b200 import ops
     from fast_b200.data import CONFIGS, make_features, make_graph, model_params
     ops.USE_TC = args.gemm == "tc"
-    if args.gemm == "ffma":
-        os.environ["FB_GEMM"] = "ffma"          # read by fb_gemm_group at every call
     from fast_b200.train import GraphTrainer, Trainer
     cfg = CONFIGS[args.config]
     graph = make_graph(cfg)
@@ -357,6 +355,9 @@ def run_fast(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    # pipelined when the trainer offers it: step i's loss is read back while
+    # step i + 1 runs (every step still copies its inputs in and its loss out)
+    host_step = getattr(tr, "step_host_pipelined", tr.step_host)
     t0 = time.perf_counter()
     for i in timed:
         b0, b1 = i * gB, (i + 1) * gB
@@ -367,7 +368,9 @@ def run_fast(args):
         gts = np.concatenate([t_np, t_np, t_np]).astype(np.float32)
         lo = tr.rank * B
         sel = np.concatenate([np.arange(lo, lo + B), gB + np.arange(lo, lo + B), 2 * gB + np.arange(lo, lo + B)])
-        tr.step_host(groots[sel], gts[sel], groots, gts)
+        host_step(groots[sel], gts[sel], groots, gts)
+    if hasattr(tr, "finish_pipelined"):
+        tr.finish_pipelined()
     torch.cuda.synchronize()
     e2e_s = torch.tensor([time.perf_counter() - t0], device=dev)
     if world > 1:
@@ -517,7 +520,14 @@ def run_kernel_suite(args):
         line = {"suite": "kernels", "kernel": name, "shape": shape, "us_per_launch": round(us, 2),
                 "bytes_per_launch": int(nbytes)}
         if flops:
-            line.update({"bound": "FFMA (fp32 CUDA cores)", "TFLOP_s": round(flops / us / 1e6, 2)})
+            tfs = flops / us / 1e6
+            if args.gemm == "tc":
+                line.update({"bound": "tensor (tcgen05, three TF32 MMAs per fp32 product)", "TFLOP_s": round(tfs, 2),
+                             "peak_TFLOP_s": pk["tf"], "frac": round(tfs / pk["tf"], 4),
+                             "peak_source": "%s bf16 burst (the only measured tensor peak)" % pk["src"],
+                             "tensor_work_TFLOP_s": round(3 * tfs, 2)})
+            else:
+                line.update({"bound": "FFMA (fp32 CUDA cores)", "TFLOP_s": round(tfs, 2)})
         else:
             gbs = nbytes / us / 1e3
             line.update({"bound": "hbm", "achieved_GB_s": round(gbs, 1), "peak_GB_s": pk["hbm"],
@@ -564,6 +574,10 @@ def run_kernel_suite(args):
     timed("k_gemm_group (K|V weight + bias gradient, TN)", 0, 2 * E * 2 * D * (de + dt_ + 1),
           lambda: ops.gemm_group([dict(kind=ops.TN, A=dkv, B=A, out=gW, accumulate=True, db=gb)]),
           "M=%d, N=%d, K=%d+1" % (E, 2 * D, de + dt_))
+    dAt = torch.empty(E, dt_, device=dev)
+    timed("k_gemm_group (time-encoding input gradient, NN)", 0, 2 * E * dt_ * 2 * D,
+          lambda: ops.gemm_group([dict(kind=ops.NN, A=dkv, B=W_kv[:, de:], out=dAt)]),
+          "M=%d, N=%d, K=%d" % (E, dt_, 2 * D))
     return 0
 
 
@@ -571,6 +585,8 @@ def main():
     args = parse()
     if args.warmup < 3:
         args.warmup = 3
+    if args.gemm == "ffma":
+        os.environ["FB_GEMM"] = "ffma"          # read by fb_gemm_group at every call
     if args.suite == "kernels":
         return run_kernel_suite(args)
     if args.impl == "reference":

@@ -10,12 +10,16 @@
 // Rounding: torch's CPU Linear(1, d) produces w*dt + b with one rounding
 // (a fused multiply-add); with dt up to ~1e8 the argument of cos is large and
 // a second rounding changes the feature by O(1), so the kernel uses fmaf.
-// The backward evaluates sin of the fp32 argument in double precision: for the
-// 1e5..1e8 radians of real timestamps the single-precision function takes its
-// slow argument-reduction path, which cost more than the double evaluation in
-// the long per-thread row loops of the reduction (measured on B200; choosing
-// per argument size measured slower still, the lanes of a warp diverge).  The
-// forward keeps cosf, which measured faster in its wide gather.
+// The backward needs sin of fp32 arguments of 1e5..1e8 radians (real
+// timestamps).  The library's double sin handles them exactly but is bound by
+// the fp64 rate (~100 operations per call).  sin_big() reduces the argument
+// by pi/2 in integer arithmetic instead -- the float's 24-bit mantissa times
+// a 64-bit fixed-point 2/pi gives the quadrant and 32 fraction bits exactly,
+// the idea of Payne & Hanek ("Radian reduction for trigonometric functions",
+// SIGNUM Newsletter 18, 1983) with one word of 2/pi, enough below 2^28 -- and
+// evaluates the Taylor series of sin and cos on |r| <= pi/4 in fp32 (degrees
+// 9 and 10: truncation below 2e-9).  The forward keeps cosf, which measured
+// faster in its wide gather.
 #include "runtime.cuh"
 
 namespace {
@@ -131,6 +135,41 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode(GatherA
   }
 }
 
+// round(2/pi * 2^64)
+constexpr uint64_t kTwoOverPiQ64 = 0xa2f9836e4e44152aull;
+
+// sin(x) for a float x: |x| = (k + f) pi/2 with k an integer and |f| <= 1/2,
+// then +-sin(r) or +-cos(r), r = f pi/2, by the quadrant k mod 4 (the
+// library's double sin from 2^28 on).
+__device__ __forceinline__ float sin_big(float x) {
+  const float ax = fabsf(x);
+  if (ax >= 268435456.f) return (float)sin((double)x);
+  float r;
+  int q = 0;
+  if (ax < 0.78539816f) {
+    r = ax;
+  } else {
+    const uint32_t bits = __float_as_uint(ax);
+    const int e = (int)(bits >> 23) - 127;             // -1 .. 27
+    const uint64_t m = (bits & 0x7FFFFFu) | 0x800000u;  // |x| = m 2^(e-23)
+    const uint64_t lo = m * kTwoOverPiQ64, hi = __umul64hi(m, kTwoOverPiQ64);
+    const int s = 87 - e;                               // |x| 2/pi = (hi:lo) 2^-s, s in 60 .. 88
+    q = (int)((s >= 64 ? hi >> (s - 64) : (lo >> s) | (hi << (64 - s))) & 3u);
+    const int sh = s - 32;                              // 28 .. 56
+    const int32_t fb = (int32_t)(uint32_t)((lo >> sh) | (hi << (64 - sh)));   // fraction, 32 bits
+    if (fb < 0) q = (q + 1) & 3;                        // fraction >= 1/2: the next quadrant
+    r = (float)fb * 0x1.921fb6p-32f;                     // pi/2 * 2^-32
+  }
+  const float r2 = r * r;
+  // Taylor coefficients 1/n!, alternating
+  const float sr = fmaf(r2 * r, fmaf(r2, fmaf(r2, fmaf(r2, 1.f / 362880.f, -1.f / 5040.f), 1.f / 120.f), -1.f / 6.f), r);
+  const float cr = fmaf(r2, fmaf(r2, fmaf(r2, fmaf(r2, fmaf(r2, -1.f / 3628800.f, 1.f / 40320.f), -1.f / 720.f),
+                                                1.f / 24.f), -0.5f), 1.f);
+  const float v = (q & 1) ? cr : sr;
+  const float sv = (q & 2) ? -v : v;
+  return x < 0.f ? -sv : sv;
+}
+
 constexpr int64_t kTeRowsPerCta = 128;
 constexpr int64_t kTeMaxParts = 296;   // two waves of 148 SMs at most
 
@@ -154,9 +193,25 @@ __global__ void __launch_bounds__(256) k_te_bwd_part(const float *__restrict__ g
   float sw = 0.f, sb = 0.f;
   if (c < dtime) {
     const float wc = __ldg(w + c), bc = __ldg(b + c);
-    for (int64_t r = r0 + wp; r < r1; r += 8) {
+    int64_t r = r0 + wp;
+    // eight rows' loads in flight per iteration; rows still summed in order
+    for (; r + 56 < r1; r += 64) {
+      float tv[8], gv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        tv[u] = __ldg(dt + r + 8 * u);
+        gv[u] = __ldg(g + (r + 8 * u) * ldg + c);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float gs = -sin_big(fmaf(tv[u], wc, bc)) * gv[u];
+        sw = fmaf(gs, tv[u], sw);
+        sb += gs;
+      }
+    }
+    for (; r < r1; r += 8) {
       const float t = __ldg(dt + r);
-      const float gs = -(float)sin((double)fmaf(t, wc, bc)) * g[r * ldg + c];
+      const float gs = -sin_big(fmaf(t, wc, bc)) * __ldg(g + r * ldg + c);
       sw = fmaf(gs, t, sw);
       sb += gs;
     }

@@ -285,9 +285,51 @@ constexpr int kThreadsTc = 512;
 // (kept in TMEM, read and written back by the same thread) with
 // round-to-nearest while the tensor cores fill the other buffer.
 __global__ void __launch_bounds__(kThreadsTc, 1) k_tc_group(const __grid_constant__ TcArgs a) {
-  fb::pdl_enter();
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte aligned tile base, derived from the shared array itself so the
+  // compiler keeps every tile access in the shared address space
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  auto sA = [&](int s) { return smem + s * kStage; };
+  auto sAlo = [&](int s) { return smem + s * kStage + kOpBytes; };
+  auto sB = [&](int s) { return smem + s * kStage + 2 * kOpBytes; };
+  auto sBlo = [&](int s) { return smem + s * kStage + 3 * kOpBytes; };
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStage);
+  uint64_t *full = bars, *conv = bars + kStages, *empty = bars + 2 * kStages;
+  uint64_t *accf = bars + 3 * kStages, *acce = bars + 3 * kStages + 2, *drain = bars + 3 * kStages + 4;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * kStages + 5);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+  int32_t *err = a.err;
   __shared__ int s_start[kMaxTc + 1];
   __shared__ long long s_m[kMaxTc], s_per[kMaxTc];
+
+  // Setup that reads nothing the previous kernel writes (barriers, tensor
+  // memory, tensor-map prefetch) runs before the dependency wait, so under
+  // programmatic dependent launch it overlaps the previous kernel's tail.
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(conv + s, kConvThreads);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf + b, 1);
+      mbar_init(acce + b, 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kWarpProducer && lane < a.n) {
+    const TcProb &q = a.p[lane];
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&q.ta)) : "memory");
+    if (q.kind != kTN && q.k1 < q.K)
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&q.ta2)) : "memory");
+    if (!q.b_synth) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&q.tb)) : "memory");
+  }
+  if (warp == kWarpMma) tmem_alloc(tmem_holder, kTmemCols);
+
+  fb::pdl_enter();
   if (threadIdx.x == 0) {
     int acc = 0;
     for (int p = 0; p < a.n; ++p) {
@@ -308,43 +350,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_tc_group(const __grid_constan
     s_start[a.n] = acc;
   }
   __syncthreads();
-  const int total = s_start[a.n];
-  if ((int)blockIdx.x >= total) return;
-
-  extern __shared__ uint8_t smem_raw[];
-  // 1024-byte aligned tile base, derived from the shared array itself so the
-  // compiler keeps every tile access in the shared address space
-  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  auto sA = [&](int s) { return smem + s * kStage; };
-  auto sAlo = [&](int s) { return smem + s * kStage + kOpBytes; };
-  auto sB = [&](int s) { return smem + s * kStage + 2 * kOpBytes; };
-  auto sBlo = [&](int s) { return smem + s * kStage + 3 * kOpBytes; };
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStage);
-  uint64_t *full = bars, *conv = bars + kStages, *empty = bars + 2 * kStages;
-  uint64_t *accf = bars + 3 * kStages, *acce = bars + 3 * kStages + 2, *drain = bars + 3 * kStages + 4;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 3 * kStages + 5);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
-  int32_t *err = a.err;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(full + s, 1);
-      mbar_init(conv + s, kConvThreads);
-      mbar_init(empty + s, 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(accf + b, 1);
-      mbar_init(acce + b, 128);
-    }
-    mbar_init(drain, 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == kWarpMma) tmem_alloc(tmem_holder, kTmemCols);
-  __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  const int total = s_start[a.n];
+  if ((int)blockIdx.x >= total) {         // nothing for this CTA at the device-side sizes
+    if (warp == kWarpMma) tmem_dealloc(tmem, kTmemCols);
+    return;
+  }
 
   if (warp == kWarpProducer) {
     if (lane == 0) {
@@ -609,8 +621,18 @@ __global__ void k_tc_reduce(const __grid_constant__ TcArgs a) {
   M = max(M, (int64_t)0);
   const int ns = fb::tn_parts(M, kTnRowsMin, q.max_splits);
   const int n = (int)(i / q.Kp), k = (int)(i % q.Kp);
+  const int64_t stride = (int64_t)q.N * q.Kp;
+  const float *part = q.P + i;
   float s = 0.f;
-  for (int z = 0; z < ns; ++z) s += q.P[(int64_t)z * q.N * q.Kp + i];
+  int z = 0;
+  for (; z + 8 <= ns; z += 8) {          // eight loads in flight, added in split order
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = part[(int64_t)(z + u) * stride];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) s += v[u];
+  }
+  for (; z < ns; ++z) s += part[(int64_t)z * stride];
   float *c = (k < q.K) ? q.C + (int64_t)n * q.ldc + k : q.db + n;
   const int acc = (k < q.K) ? q.accumulate : q.db_accumulate;
   *c = acc ? (*c + s) : s;

@@ -37,6 +37,51 @@ __device__ __forceinline__ int upper_bound_dev(const float *__restrict__ ts, int
   return lo;
 }
 
+// A group of kGroup lanes works on one root: the time-window search probes
+// kGroup positions per round (a (kGroup+1)-ary search) and each lane takes
+// one candidate pick, so a root costs a few dependent memory latencies
+// instead of one per search step and per pick.
+constexpr int kGroup = 16;
+constexpr int kRootsPerCta = kThreads / kGroup;
+
+struct Lanes {
+  int gl;          // lane within the group
+  unsigned mask;   // the group's lanes in the warp
+  int shift;       // bit offset of the group in a warp ballot
+};
+
+__device__ __forceinline__ Lanes group_lanes() {
+  const int lane = threadIdx.x & 31;
+  Lanes L;
+  L.gl = lane & (kGroup - 1);
+  L.shift = lane & ~(kGroup - 1);
+  L.mask = ((1u << kGroup) - 1) << L.shift;
+  return L;
+}
+
+// The group's ballot of pred, bit i = lane i of the group.
+__device__ __forceinline__ unsigned group_ballot(bool pred, const Lanes &L) {
+  return (__ballot_sync(L.mask, pred) >> L.shift) & ((1u << kGroup) - 1);
+}
+
+// upper_bound_dev by the lanes of a group (same result in every lane).
+__device__ __forceinline__ int upper_bound_group(const float *__restrict__ ts, int lo, int hi, float v,
+                                                 const Lanes &L) {
+  while (hi - lo > kGroup) {
+    const int len = hi - lo;
+    const int q = lo + (int)(((int64_t)(L.gl + 1) * len) / (kGroup + 1));
+    const unsigned b = group_ballot(v < __ldg(ts + q), L);   // probes ascend, so b is 0..0 1..1
+    const int t = b ? __ffs(b) - 1 : kGroup;                  // first probe with ts > v
+    const int q_before = __shfl_sync(L.mask, q, t > 0 ? t - 1 : 0, kGroup);
+    const int q_at = __shfl_sync(L.mask, q, t < kGroup ? t : kGroup - 1, kGroup);
+    if (t > 0) lo = q_before + 1;
+    if (t < kGroup) hi = q_at;
+  }
+  const int i = lo + L.gl;
+  const unsigned b = group_ballot(i < hi && v < __ldg(ts + i), L);
+  return b ? lo + __ffs(b) - 1 : hi;
+}
+
 struct SampleArgs {
   const int32_t *indptr, *indices, *eid;
   const float *ts;
@@ -58,20 +103,20 @@ __device__ __forceinline__ int64_t num_roots(const SampleArgs &a) {
   return a.R_dev ? (int64_t)(*a.R_dev) : a.R_host;
 }
 
-// The window [s, e] of one root (sampler_core.cpp:522-552).
-__device__ __forceinline__ void root_window(const SampleArgs &a, int n, float nts, int &s, int &e) {
+// The window [s, e] of one root (sampler_core.cpp:522-552), by its group.
+__device__ __forceinline__ void root_window(const SampleArgs &a, int n, float nts, int &s, int &e, const Lanes &L) {
   if (a.use_ptr) {
     s = a.ptr_s[n];
     e = a.ptr_e[n];
   } else if (a.num_history == 1) {
     s = a.indptr[n];
-    int ub = upper_bound_dev(a.ts, a.indptr[n], a.indptr[n + 1], nts);
+    int ub = upper_bound_group(a.ts, a.indptr[n], a.indptr[n + 1], nts, L);
     e = max(ub - 1, s);
   } else {
     int lo = a.indptr[n], hi = a.indptr[n + 1];
-    int ub = upper_bound_dev(a.ts, lo, hi, __fsub_rn(__fadd_rn(nts, a.offset), a.wd));
+    int ub = upper_bound_group(a.ts, lo, hi, __fsub_rn(__fadd_rn(nts, a.offset), a.wd), L);
     s = max(ub - 1, lo);
-    int ub2 = upper_bound_dev(a.ts, lo, hi, __fadd_rn(nts, a.offset));
+    int ub2 = upper_bound_group(a.ts, lo, hi, __fadd_rn(nts, a.offset), L);
     e = max(ub2 - 1, s);
   }
 }
@@ -83,27 +128,46 @@ __device__ __forceinline__ int uniform_pick_u(uint32_t u, int s, int e) {
   return s + (int)(((uint64_t)u * (uint64_t)span) >> 32);
 }
 
-// Visits the kept neighbours of root j in the reference order; f(k) per edge.
+// The kept neighbours of root j in the reference order, one candidate per
+// lane: store(rank, k) for each kept edge k; returns the kept count (the same
+// in every lane of the group).
 template <typename F>
-__device__ __forceinline__ void for_each_pick(const SampleArgs &a, int64_t j, int n, float nts, F f) {
+__device__ __forceinline__ int group_picks(const SampleArgs &a, int64_t j, int n, float nts, const Lanes &L,
+                                           F store) {
   int s, e;
-  root_window(a, n, nts, s, e);
+  root_window(a, n, nts, s, e, L);
   const float keep_thr = __fsub_rn(__fadd_rn(nts, a.offset), 1e-7f);
+  const unsigned below = (1u << L.gl) - 1;
+  int c = 0;
   if (a.recent || (e - s < a.neighs)) {
+    // candidates k = e, e - 1, ..., lo + 1
     const int lo = max(s, e - a.neighs);
-    for (int k = e; k > lo; --k)
-      if (__ldg(a.ts + k) < keep_thr) f(k);
+    for (int base = 0; base < e - lo; base += kGroup) {
+      const int k = e - base - L.gl;
+      const bool keep = base + L.gl < e - lo && __ldg(a.ts + k) < keep_thr;
+      const unsigned b = group_ballot(keep, L);
+      if (keep) store(c + __popc(b & below), k);
+      c += __popc(b);
+    }
   } else {
     const uint32_t step = *a.call_dev;
-    fb::Philox4 r{};
-    for (int i = 0; i < a.neighs; ++i) {
-      if ((i & 3) == 0) r = fb::philox4x32_10((uint32_t)j, (uint32_t)(i >> 2), step, a.slot, a.key0, a.key1);
-      const int w = i & 3;
-      const uint32_t u = w == 0 ? r.v[0] : (w == 1 ? r.v[1] : (w == 2 ? r.v[2] : r.v[3]));
-      const int k = uniform_pick_u(u, s, e);
-      if (__ldg(a.ts + k) < keep_thr) f(k);
+    for (int base = 0; base < a.neighs; base += kGroup) {
+      const int i = base + L.gl;
+      bool keep = false;
+      int k = 0;
+      if (i < a.neighs) {
+        const fb::Philox4 r = fb::philox4x32_10((uint32_t)j, (uint32_t)(i >> 2), step, a.slot, a.key0, a.key1);
+        const int w = i & 3;
+        const uint32_t u = w == 0 ? r.v[0] : (w == 1 ? r.v[1] : (w == 2 ? r.v[2] : r.v[3]));
+        k = uniform_pick_u(u, s, e);
+        keep = __ldg(a.ts + k) < keep_thr;
+      }
+      const unsigned b = group_ballot(keep, L);
+      if (keep) store(c + __popc(b & below), k);
+      c += __popc(b);
     }
   }
+  return c;
 }
 
 __global__ void k_bump_call(uint32_t *call) {
@@ -123,21 +187,26 @@ __global__ void k_reset(const int32_t *__restrict__ indptr, int32_t *__restrict_
 // edges the reference scan leaves ptr = max(ptr, ub - 1), ub = first edge with
 // ts > root_ts + offset - 1e-7f; a max is order independent, so every root
 // applies its candidate with one atomicMax instead of a per-node lock.
+// One group of kGroup lanes per root.
 __global__ void k_update_ptr(const int32_t *__restrict__ indptr, const float *__restrict__ ts,
                              int64_t n_nodes, int32_t *__restrict__ ptr, const int32_t *__restrict__ roots,
                              const float *__restrict__ rts, int64_t R_host, const int32_t *R_dev,
                              float offset, int32_t *err) {
   fb::pdl_enter();
-  int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  int64_t R = R_dev ? (int64_t)(*R_dev) : R_host;
-  if (j >= R) return;
-  int n = roots[j];
-  if (n < 0 || n >= n_nodes) { atomicOr(err, kErrRootRange); return; }
-  int beg = indptr[n], end = indptr[n + 1];
+  const Lanes L = group_lanes();
+  const int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / kGroup;
+  const int64_t R = R_dev ? (int64_t)(*R_dev) : R_host;
+  if (j >= R) return;                       // whole groups leave together
+  const int n = roots[j];
+  if (n < 0 || n >= n_nodes) {
+    if (L.gl == 0) atomicOr(err, kErrRootRange);
+    return;
+  }
+  const int beg = indptr[n], end = indptr[n + 1];
   if (end <= beg) return;
-  float thr = __fsub_rn(__fadd_rn(rts[j], offset), 1e-7f);
-  int ub = upper_bound_dev(ts, beg, end, thr);
-  if (ub > beg) atomicMax(ptr + n, ub - 1);
+  const float thr = __fsub_rn(__fadd_rn(rts[j], offset), 1e-7f);
+  const int ub = upper_bound_group(ts, beg, end, thr, L);
+  if (L.gl == 0 && ub > beg) atomicMax(ptr + n, ub - 1);
 }
 
 // Pass 1: kept-edge count per root, its picks staged for pass 3, plus per-CTA
@@ -146,21 +215,23 @@ __global__ void __launch_bounds__(kThreads) k_sample_count(SampleArgs a, int32_t
                                                            int2 *__restrict__ part) {
   fb::pdl_enter();
   __shared__ int sm[64];
-  int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  int64_t R = num_roots(a);
+  const Lanes L = group_lanes();
+  const int64_t j = (int64_t)blockIdx.x * kRootsPerCta + threadIdx.x / kGroup;
+  const int64_t R = num_roots(a);
   int c = 0;
   if (j < R) {
-    int n = a.roots[j];
+    const int n = a.roots[j];
     if (n >= 0 && n < a.n_nodes) {
       int32_t *pk = a.pick + j * a.neighs;
-      for_each_pick(a, j, n, a.rts[j], [&](int k) { pk[c++] = k; });
-    } else {
+      c = group_picks(a, j, n, a.rts[j], L, [&](int rank, int k) { pk[rank] = k; });
+    } else if (L.gl == 0) {
       atomicOr(a.err, kErrRootRange);
     }
-    cnt[j] = c;
+    if (L.gl == 0) cnt[j] = c;
   }
+  const int lead = L.gl == 0 ? c : 0;         // one value per root
   int ea, eb;
-  int2 tot = fb::block_excl_scan2(c, c > 0 ? 1 : 0, ea, eb, sm);
+  int2 tot = fb::block_excl_scan2(lead, lead > 0 ? 1 : 0, ea, eb, sm);
   if (threadIdx.x == 0) part[blockIdx.x] = tot;
 }
 
@@ -203,26 +274,32 @@ __global__ void __launch_bounds__(kThreads) k_sample_write(SampleArgs a, const i
                                                            float *__restrict__ dte, int32_t *__restrict__ nbr) {
   fb::pdl_enter();
   __shared__ int sm[64];
-  int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  int64_t R = num_roots(a);
-  int c = (j < R) ? cnt[j] : 0;
+  const Lanes L = group_lanes();
+  const int64_t j = (int64_t)blockIdx.x * kRootsPerCta + threadIdx.x / kGroup;
+  const int64_t R = num_roots(a);
+  const int c = (j < R) ? cnt[j] : 0;
+  const int lead = L.gl == 0 ? c : 0;
   int ea, eb;
-  fb::block_excl_scan2(c, c > 0 ? 1 : 0, ea, eb, sm);
+  fb::block_excl_scan2(lead, lead > 0 ? 1 : 0, ea, eb, sm);
+  ea = __shfl_sync(0xffffffffu, ea, L.shift);   // the root's offsets, from its group's first lane
+  eb = __shfl_sync(0xffffffffu, eb, L.shift);
   if (j >= R) return;
   const int2 base = part[blockIdx.x];
   const int off = base.x + ea;
   const int seg = base.y + eb;
   const int n = a.roots[j];
   const float nts = a.rts[j];
-  ts_out[j] = nts;
-  dts_out[j] = 0.f;
-  nodes_out[j] = n;
-  rptr[j] = off;
-  if (c > 0) cntE[seg] = off;
+  if (L.gl == 0) {
+    ts_out[j] = nts;
+    dts_out[j] = 0.f;
+    nodes_out[j] = n;
+    rptr[j] = off;
+    if (c > 0) cntE[seg] = off;
+  }
   if (n < 0 || n >= a.n_nodes) return;
-  int t = off;
   const int32_t *pk = a.pick + j * a.neighs;   // the count pass's picks, in the reference order
-  for (int i = 0; i < c; ++i) {
+  for (int i = L.gl; i < c; i += kGroup) {
+    const int t = off + i;
     const int k = pk[i];
     const float tk = __ldg(a.ts + k);
     const float d = __fsub_rn(nts, tk);
@@ -235,7 +312,6 @@ __global__ void __launch_bounds__(kThreads) k_sample_write(SampleArgs a, const i
     nodes_out[R + t] = nb;
     dte[t] = d;
     nbr[t] = nb;
-    ++t;
   }
 }
 
@@ -417,7 +493,7 @@ int ensure_capacity(fb_sampler *s, int64_t r0) {
   for (size_t i = 0; i < cr.size(); ++i)
     max_pick = std::max<int64_t>(max_pick, cr[i] * std::max(0, s->neigh[i / s->num_history]));
   FB_TRY_CUDA(cudaMalloc(&s->ws_cnt, std::max<int64_t>(max_roots, 1) * 4));
-  FB_TRY_CUDA(cudaMalloc(&s->ws_part, nblk(max_roots) * sizeof(int2)));
+  FB_TRY_CUDA(cudaMalloc(&s->ws_part, nblk(max_roots, kRootsPerCta) * sizeof(int2)));
   FB_TRY_CUDA(cudaMalloc(&s->ws_pick, max_pick * 4));
   s->ws_cap_roots = max_roots;
   s->cap_r0 = r0;
@@ -443,7 +519,7 @@ int run_layer_slot(fb_sampler *s, int bidx, const int32_t *roots, const float *r
   a.err = s->err;
   a.pick = s->ws_pick;
   int32_t *dims = s->dims + 8 * bidx;
-  const int nb = nblk(R_cap);
+  const int nb = nblk(R_cap, kRootsPerCta);
   FB_TRY_CUDA(fb::launch(k_sample_count, nb, kThreads, 0, st, a, s->ws_cnt, s->ws_part));
   FB_LAUNCHED("k_sample_count");
   FB_TRY_CUDA(fb::launch(k_scan_parts, 1, 1024, 0, st, s->ws_part, nb, R_host, R_dev, dims, b.rptr, b.cntE));
@@ -562,7 +638,7 @@ extern "C" int fb_sampler_sample(fb_sampler *s, const int32_t *roots, const floa
     }
     const int64_t rcap = cr[l * nh];
     if (use_ptr && rcap > 0) {
-      FB_TRY_CUDA(fb::launch(k_update_ptr, nblk(rcap), kThreads, 0, st, s->indptr, s->ts, s->n_nodes, s->ts_ptr + (int64_t)nh * s->n_nodes,
+      FB_TRY_CUDA(fb::launch(k_update_ptr, nblk(rcap * kGroup), kThreads, 0, st, s->indptr, s->ts, s->n_nodes, s->ts_ptr + (int64_t)nh * s->n_nodes,
                                                     ur, ut, n_roots, uR, 0.f, s->err));
       FB_LAUNCHED("k_update_ptr");
     }
@@ -576,7 +652,7 @@ extern "C" int fb_sampler_sample(fb_sampler *s, const int32_t *roots, const floa
       }
       const float offset = (float)(-i) * s->wd;
       if (use_ptr && fabsf(s->wd) > 1e-7f && rcap > 0) {
-        FB_TRY_CUDA(fb::launch(k_update_ptr, nblk(rcap), kThreads, 0, st, s->indptr, s->ts, s->n_nodes,
+        FB_TRY_CUDA(fb::launch(k_update_ptr, nblk(rcap * kGroup), kThreads, 0, st, s->indptr, s->ts, s->n_nodes,
                                                       s->ts_ptr + (int64_t)(nh - 1 - i) * s->n_nodes, hr, ht,
                                                       n_roots, hR, offset - s->wd, s->err));
         FB_LAUNCHED("k_update_ptr");
@@ -599,13 +675,13 @@ extern "C" int fb_sampler_update_pointers(fb_sampler *s, const int32_t *roots, c
   if (n_roots == 0) return FB_OK;
   // the first layer's pointer updates of sample(), for these roots only
   const int nh = s->num_history;
-  FB_TRY_CUDA(fb::launch(k_update_ptr, nblk(n_roots), kThreads, 0, st, s->indptr, s->ts, s->n_nodes, s->ts_ptr + (int64_t)nh * s->n_nodes,
+  FB_TRY_CUDA(fb::launch(k_update_ptr, nblk(n_roots * kGroup), kThreads, 0, st, s->indptr, s->ts, s->n_nodes, s->ts_ptr + (int64_t)nh * s->n_nodes,
                                                     roots, root_ts, n_roots, nullptr, 0.f, s->err));
   FB_LAUNCHED("k_update_ptr");
   for (int i = 0; i < nh; ++i) {
     const float offset = (float)(-i) * s->wd;
     if (fabsf(s->wd) > 1e-7f) {
-      FB_TRY_CUDA(fb::launch(k_update_ptr, nblk(n_roots), kThreads, 0, st, s->indptr, s->ts, s->n_nodes,
+      FB_TRY_CUDA(fb::launch(k_update_ptr, nblk(n_roots * kGroup), kThreads, 0, st, s->indptr, s->ts, s->n_nodes,
                                                         s->ts_ptr + (int64_t)(nh - 1 - i) * s->n_nodes, roots,
                                                         root_ts, n_roots, nullptr, offset - s->wd, s->err));
       FB_LAUNCHED("k_update_ptr");

@@ -219,6 +219,14 @@ class GraphTrainer(Trainer):
         self.h_gts = torch.zeros(self.R0 * world, dtype=torch.float32).pin_memory() if world > 1 else None
         self.h_roots = torch.zeros(self.R0, dtype=torch.int32).pin_memory()
         self.h_ts = torch.zeros(self.R0, dtype=torch.float32).pin_memory()
+        # two pinned staging slots for step_host_pipelined
+        self._slots = [dict(roots=torch.zeros(self.R0, dtype=torch.int32).pin_memory(),
+                            ts=torch.zeros(self.R0, dtype=torch.float32).pin_memory(),
+                            groots=torch.zeros(self.R0 * world, dtype=torch.int32).pin_memory() if world > 1 else None,
+                            gts=torch.zeros(self.R0 * world, dtype=torch.float32).pin_memory() if world > 1 else None,
+                            loss=None, done=None) for _ in range(2)]
+        self._slot = 0
+        self._pending = None
         self.g_main = self.g_opt = None
 
     # the body of one step on the static input buffers
@@ -301,6 +309,46 @@ class GraphTrainer(Trainer):
             self.capture()
         self._replay()
         return self.loss_buf
+
+    def step_host_pipelined(self, roots_np, ts_np, global_roots_np=None, global_ts_np=None):
+        """step_host without waiting for this step: the inputs go through pinned
+        slot i % 2, the loss comes back into that slot's pinned word, and the
+        call returns the previous step's loss (None on the first call) once that
+        step has completed -- so the host prepares and copies batch i + 1 while
+        the device runs step i.  finish_pipelined() returns the last loss."""
+        sl = self._slots[self._slot]
+        if sl["done"] is not None:
+            sl["done"].synchronize()           # the step that used this slot two calls ago
+        sl["roots"].numpy()[:] = roots_np
+        sl["ts"].numpy()[:] = ts_np
+        self.roots_buf.copy_(sl["roots"], non_blocking=True)
+        self.ts_buf.copy_(sl["ts"], non_blocking=True)
+        if self.world > 1:
+            assert global_roots_np is not None, "several ranks: pass the global batch's roots too"
+            sl["groots"].numpy()[:] = global_roots_np
+            sl["gts"].numpy()[:] = global_ts_np
+            self.groots_buf.copy_(sl["groots"], non_blocking=True)
+            self.gts_buf.copy_(sl["gts"], non_blocking=True)
+        if self.g_main is None:
+            self.capture()
+        self._replay()
+        if sl["loss"] is None:
+            sl["loss"] = torch.zeros_like(self.loss_buf, device="cpu").pin_memory()
+        sl["loss"].copy_(self.loss_buf, non_blocking=True)
+        sl["done"] = torch.cuda.Event()
+        sl["done"].record()
+        prev, self._pending = self._pending, self._slot
+        self._slot ^= 1
+        return None if prev is None else self._read_slot(prev)
+
+    def finish_pipelined(self):
+        """The loss of the last step_host_pipelined call (None if none is pending)."""
+        prev, self._pending = self._pending, None
+        return None if prev is None else self._read_slot(prev)
+
+    def _read_slot(self, i):
+        self._slots[i]["done"].synchronize()
+        return float(self._slots[i]["loss"])
 
     def step_host(self, roots_np, ts_np, global_roots_np=None, global_ts_np=None):
         """End-to-end step: host roots -> pinned staging -> device buffers ->

@@ -80,14 +80,17 @@ def test_gather_time_encode(cuda):
     torch.testing.assert_close(out3.cpu(), torch.cos(lin.bias.data).expand(3, -1), rtol=1e-6, atol=1e-7)
 
 
-def test_time_encode_bwd(cuda):
+@pytest.mark.parametrize("dt_max", [1e4, 2e8, 3e8])
+def test_time_encode_bwd(cuda, dt_max):
     """dw, db of cos(w dt + b) against an fp64 sum over the same single-rounded
     arguments; E-term sums are compared within the fp32 summation bound
-    sum|terms| * E * 2^-24."""
+    sum|terms| * E * 2^-24.  dt up to 2e8 (the timestamps of the synthetic
+    graphs) exercises the kernel's own argument reduction, 3e8 the fallback
+    beyond it."""
     from fast_b200 import ops
     rng = np.random.default_rng(1)
     E, d = 5000, 100
-    dt = torch.from_numpy((rng.random(E) * 1e4).astype(np.float32))
+    dt = torch.from_numpy((rng.random(E) * dt_max).astype(np.float32))
     w = torch.from_numpy(1 / 10 ** np.linspace(0, 9, d, dtype=np.float32))
     b = torch.randn(d) * 0.1
     g = torch.randn(E, d)

@@ -85,3 +85,28 @@ def test_graph_trainer_matches_eager_trainer(cuda, strategy, fused):
         assert abs(lg - le) <= 1e-5 * abs(le) + 1e-6, (lg, le)
     for (n, pe), pg in zip(eager.model.named_parameters(), graph.model.parameters()):
         torch.testing.assert_close(pg, pe, rtol=1e-4, atol=1e-6, msg=lambda m: "%s: %s" % (n, m))
+
+
+def test_pipelined_host_steps_equal_synchronous_ones(cuda):
+    """step_host_pipelined (inputs through two pinned slots, each loss read one
+    call later) trains exactly like step_host, loss for loss."""
+    import numpy as np
+    from fast_b200.train import GraphTrainer
+    cfg, g, ef, sp, mp, gp, tp = _setup(cuda, 2e3)
+    mk = lambda: GraphTrainer(g, None, ef, dict(sp), mp, dict(gp), tp, cuda, batch=cfg.batch, seed=5,  # noqa: E731
+                              sampler_seed=77, optimizer="adam")
+    sync, pipe = mk(), mk()
+    B = cfg.batch
+    rng = np.random.default_rng(3)
+    batches = []
+    for i in range(6):
+        b0 = 10000 + i * B
+        t = g.ts[b0:b0 + B]
+        roots = np.concatenate([g.src[b0:b0 + B], g.dst[b0:b0 + B], rng.integers(0, g.n_nodes, B).astype(np.int32)])
+        batches.append((roots.astype(np.int32), np.concatenate([t, t, t]).astype(np.float32)))
+    want = [sync.step_host(r, t) for r, t in batches]
+    got = [pipe.step_host_pipelined(r, t) for r, t in batches]
+    assert got[0] is None
+    got = got[1:] + [pipe.finish_pipelined()]
+    assert got == want
+    assert pipe.finish_pipelined() is None
