@@ -86,6 +86,11 @@ _SIGS = {
     "fb_q_time_bwd": (_I, [_P, _I, _P, _I64, _I, _I, _P, _P, _P, _I64, _P, _P, _P]),
     "fb_adam_step": (_I, [_P, _P, _P, _P, _I64, _F, _F, _F, _F, _P, _P, _P]),
     "fb_attn_error": (_I, [_P, _I]),
+    "fb_mem_gather": (_I, [_P, _P, _I64, _P, _P, _I, _P, _P, _I, _P, _P, _I, _P, _I64, _P, _P, _P]),
+    "fb_gru_fwd": (_I, [_P, _P, _P, _P, _I64, _P, _I, _P]),
+    "fb_gru_bwd": (_I, [_P, _P, _P, _P, _I64, _I64, _P, _I, _P]),
+    "fb_mailbox_update_self": (_I, [_P, _P, _I64, _P, _I64, _I, _P, _I64, _I, _P, _P, _P, _P, _I, _P, _P, _P, _P]),
+    "fb_memory_update": (_I, [_P, _P, _I64, _P, _I64, _I, _P, _P, _P, _P, _P, _P]),
 }
 
 class GemmProblem(ctypes.Structure):

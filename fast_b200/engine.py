@@ -23,6 +23,14 @@ GEMM; state_dict names and shapes are unchanged.
 
 Every launch honours device-side row counts (StaticBlock), so the step can
 be captured in a CUDA graph.
+
+With node memory (memory.MemoryModel, TGN) the step starts with the memory
+updater on the first layer's source rows (memorys.py:270-304): gather of
+memory / mailbox / memory time encoding -> the GRU's two products as one
+grouped GEMM -> gate kernel; the updated memory is layer 0's node input, and
+the backward runs layer 0's input gradient through the gates into the GRU's
+weights and the memory time encoder.  `last_memory` keeps the updated memory
+for the mailbox writes after the optimizer step (memorys.py:84-142).
 """
 import torch
 
@@ -46,9 +54,11 @@ class FusedStep:
     run the optimizer on the model's parameters."""
 
     def __init__(self, model):
-        if model.memory_param.get("type", "none") != "none":
-            raise NotImplementedError("FusedStep covers memoryless models")
+        self.mem = getattr(model, "memory_updater", None)
+        if model.memory_param.get("type", "none") != "none" and self.mem is None:
+            raise NotImplementedError("node memory needs memory.MemoryModel")
         self.model = model
+        self.last_memory = None
         self.layers = [_LayerParams(model.layers["l%dh0" % l]) for l in range(model.gnn_param["layer"])]
         for lp in self.layers:
             if lp.dn + lp.dtime == 0:
@@ -158,11 +168,12 @@ class FusedStep:
 
     def _layer_bwd(self, l, st, dout, dh_rows):
         """Adds layer l's parameter gradients; returns the gradient of its
-        input h (rows dh_rows) when l > 0, else None."""
+        input h (dh_rows rows: the layer below's destinations, or for layer 0 of
+        a memory model its source rows), or None when dh_rows == 0."""
         lp = self.layers[l]
         L, D, dn, de, dtime = lp.L, lp.D, lp.dn, lp.de, lp.dtime
         if st is None:                     # empty block (eager): zero output, no gradient
-            return None if l == 0 else torch.zeros(dh_rows, dn, device=dout.device)
+            return None if dh_rows == 0 else torch.zeros(dh_rows, dn, device=dout.device)
         blk = st["blk"]
         nd, E = blk.n_dst, blk.n_edges
         nd_dev, E_dev = blk.n_dst_dev, blk.n_edges_dev
@@ -180,7 +191,7 @@ class FusedStep:
                  dict(kind=ops.NN, A=dZ, B=Wo[:, :D], out=dagg, M_dev=nd_dev)]
         if dn > 0:
             probs.append(dict(kind=ops.TN, A=dZ, B=Qin[:, :dn], out=gWo[:, D:], accumulate=True, M_dev=nd_dev))
-        if l > 0:
+        if dh_rows > 0:                    # the layer's input h needs a gradient (layer above, or the memory)
             assert dh_rows >= nd + E
             dh = torch.empty(dh_rows, dn, device=dev)
             probs.append(dict(kind=ops.NN, A=dZ, B=Wo[:, D:], out=dh[:nd], M_dev=nd_dev))
@@ -219,13 +230,60 @@ class FusedStep:
             ops.q_time_bwd(v, L.w_q.weight, dn, dtime, bt, g(L.w_q.bias), gbt)
         return dh
 
+    # -- node memory (GRU updater) ---------------------------------------------
+    def _memory_fwd(self, blk, mailbox):
+        """h' = GRUCell([mail | time encoding], memory) for the source rows of
+        blk (memorys.py:284-304); returns h' [n_src, dim_mem] and the saved
+        state for the backward."""
+        U = self.mem
+        cell = U.updater
+        H = U.dim_hid
+        n, n_dev = blk.n_src, blk.n_src_dev
+        dev = cell.weight_ih.device
+        din = cell.weight_ih.shape[1]
+        x = torch.empty(n, din, device=dev)
+        h0 = torch.empty(n, H, device=dev)
+        dtm = torch.empty(n, device=dev)
+        mailbox.gather(blk.nodes, blk.ts, n, n_dev, U.time_enc if U.dim_time > 0 else None, x, h0, dtm)
+        gi = torch.empty(n, 3 * H, device=dev)
+        gh = torch.empty(n, 3 * H, device=dev)
+        ops.gemm_group([dict(kind=ops.NT, A=x, B=cell.weight_ih, bias=cell.bias_ih, out=gi, M_dev=n_dev),
+                        dict(kind=ops.NT, A=h0, B=cell.weight_hh, bias=cell.bias_hh, out=gh, M_dev=n_dev)],
+                       name="gemm_group:gru")
+        h1 = torch.empty(n, H, device=dev)
+        ops.gru_fwd(gi, gh, h0, h1, n_dev=n_dev)
+        return h1, dict(x=x, h0=h0, dtm=dtm, gi=gi, gh=gh, n=n, n_dev=n_dev)
+
+    def _memory_bwd(self, st, dh1):
+        U = self.mem
+        cell = U.updater
+        g = lambda p: p.grad
+        ops.gru_bwd(st["gi"], st["gh"], st["h0"], dh1, n_dev=st["n_dev"])
+        dgi, dgh, n_dev = st["gi"], st["gh"], st["n_dev"]
+        dmail = cell.weight_ih.shape[1] - U.dim_time
+        probs = [dict(kind=ops.TN, A=dgi, B=st["x"], out=g(cell.weight_ih), accumulate=True, M_dev=n_dev,
+                      db=g(cell.bias_ih)),
+                 dict(kind=ops.TN, A=dgh, B=st["h0"], out=g(cell.weight_hh), accumulate=True, M_dev=n_dev,
+                      db=g(cell.bias_hh))]
+        dxt = None
+        if U.dim_time > 0:
+            dxt = torch.empty(st["n"], U.dim_time, device=dgi.device)
+            probs.append(dict(kind=ops.NN, A=dgi, B=cell.weight_ih[:, dmail:], out=dxt, M_dev=n_dev))
+        ops.gemm_group(probs, name="gemm_group:gru_bwd")
+        if dxt is not None:
+            te = U.time_enc
+            ops.time_encode_bwd(dxt, st["dtm"], te.w.weight.view(-1), te.w.bias, g(te.w.weight).view(-1),
+                                g(te.w.bias), n_dev=n_dev)
+
     # -- whole step -----------------------------------------------------------
-    def step(self, blocks, node_table, edge_table, loss_out, zero_grad=True, scores=None):
+    def step(self, blocks, node_table, edge_table, loss_out, zero_grad=True, scores=None, mailbox=None):
         """blocks in sampler order (hop 1 first), Device- or StaticBlocks.
         Writes the loss into loss_out (a 0-d device tensor) and the gradients
         into the parameters' .grad (zeroed first unless zero_grad=False);
         with `scores` ([2B] device tensor) also the positive then negative
-        edge scores."""
+        edge scores.  Memory models read their inputs from `mailbox` and
+        leave the updated memory of the first layer's source rows in
+        `last_memory`."""
         m = self.model
         training = m.training
         mfgs = list(reversed(blocks))
@@ -237,8 +295,15 @@ class FusedStep:
         if zero_grad:
             self.flat.zero_()
         saved, h = [], None
+        mem_st = None
+        if self.mem is not None:
+            if mailbox is None:
+                raise ValueError("a memory model needs its MailBox")
+            h, mem_st = self._memory_fwd(mfgs[0], mailbox)
+            self.last_memory = h
         for l, blk in enumerate(mfgs):
-            st, h = self._layer_fwd(l, blk, h, node_table if l == 0 else None, edge_table, m._drop_step, training)
+            st, h = self._layer_fwd(l, blk, h, node_table if (l == 0 and mem_st is None) else None, edge_table,
+                                    m._drop_step, training)
             saved.append(st)
         ep = m.edge_predictor
         B = h.shape[0] // 3
@@ -260,8 +325,12 @@ class FusedStep:
             dict(kind=ops.NN, A=dS, B=ep.src_fc.weight, out=dh[:B]),
             dict(kind=ops.NN, A=dP, B=ep.dst_fc.weight, out=dh[B:3 * B])], name="gemm_group:pred_bwd")
         for l in range(len(mfgs) - 1, -1, -1):
-            rows = mfgs[l - 1].n_dst if l > 0 else 0
+            rows = mfgs[l - 1].n_dst if l > 0 else (mfgs[0].n_src if mem_st is not None else 0)
             dh = self._layer_bwd(l, saved[l], dh, rows)
+        if mem_st is not None:
+            if dh is None:                   # an empty block: no gradient reaches the memory updater
+                dh = torch.zeros(mem_st["n"], self.mem.dim_hid, device=dev)
+            self._memory_bwd(mem_st, dh)
         return loss_out
 
 

@@ -23,6 +23,7 @@ class DeviceBlock:
     n_dst_static = True
     n_dst_dev = None
     n_edges_dev = None
+    n_src_dev = None
 
     def __init__(self, view, dims):
         R, E, S, dim_in = (int(x) for x in dims[:4])
@@ -69,6 +70,10 @@ class StaticBlock:
         self.src_nodes = view["nbr"][:cap_e]
         self.dt_edges = view["dte"][:cap_e]
         self.rptr = view["rptr"][:self.n_dst + 1]
+        # all source rows [roots | one per edge] and their times (node memory)
+        self.nodes = view["nodes"][:self.n_src]
+        self.ts = view["ts"][:self.n_src]
+        self.n_src_dev = view["dims"][3:4]
 
     def num_dst_nodes(self):
         return self.n_dst

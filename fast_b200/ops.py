@@ -200,6 +200,26 @@ def gemm_group(problems, name="gemm_group"):
             lambda: call("fb_gemm_group", arr, n, ptr(ws), ws.numel(), stream_ptr()))
 
 
+def gru_fwd(gi, gh, h0, h1, n_dev=None):
+    """GRUCell gates from the products gi = x W_ih^T + b_ih, gh = h0 W_hh^T + b_hh
+    ([n, 3H]); writes h1 and keeps (r, z, n) in gi (memorys.py:272-304)."""
+    n, H = h0.shape
+    for t, w in ((gi, 3 * H), (gh, 3 * H), (h1, H)):
+        if t.shape != (n, w) or not t.is_contiguous():
+            raise ValueError("gru_fwd: expected contiguous [n, 3H] gates and [n, H] states")
+    _launch("gru_fwd", 4 * n * (9 * H), 0, 1,
+            lambda: call("fb_gru_fwd", ptr(gi), ptr(gh), ptr(h0), ptr(h1), n, _p(n_dev), H, stream_ptr()))
+    return h1
+
+
+def gru_bwd(gi, gh, h0, dh1, n_dev=None):
+    """Backward of gru_fwd: gi <- d(gi), gh <- d(gh) for the gradient dh1."""
+    n, H = h0.shape
+    _launch("gru_bwd", 4 * n * (14 * H), 0, 1,
+            lambda: call("fb_gru_bwd", ptr(gi), ptr(gh), ptr(h0), ptr(dh1), dh1.stride(0), n, _p(n_dev), H,
+                         stream_ptr()))
+
+
 def layer_tail_fwd(z, gamma, beta, eps=1e-5, drop_p=0.0, seed=0, offset=0, offset_dev=None, mask_u=None,
                    y=None, out=None, n_dev=None, gate_dev=None):
     """y = relu(dropout(z)), out = LayerNorm(y) per row (rows >= *n_dev: out = 0;

@@ -17,6 +17,7 @@ import torch.distributed as dist
 
 from . import ops
 from .engine import FlatAdam, FusedStep
+from .memory import MailBox, MemoryModel
 from .model import DeviceBlock, GeneralModel, StaticBlock
 from .ext import sampler_core
 
@@ -59,9 +60,18 @@ class Trainer:
         self.sample_param = sample_param
         self.node_feats, self.edge_feats = node_feats, edge_feats
         torch.manual_seed(seed)
-        self.model = GeneralModel(0 if node_feats is None else node_feats.shape[1],
-                                  0 if edge_feats is None else edge_feats.shape[1],
-                                  sample_param, memory_param, gnn_param, train_param).to(self.device)
+        dn = 0 if node_feats is None else node_feats.shape[1]
+        de = 0 if edge_feats is None else edge_feats.shape[1]
+        self.mailbox = None
+        if memory_param.get("type", "none") != "none":
+            if not fused or world > 1:
+                raise NotImplementedError("node memory trains through FusedStep on one GPU")
+            self.model = MemoryModel(dn, de, sample_param, memory_param, gnn_param, train_param).to(self.device)
+            self.mailbox = MailBox(memory_param, graph.n_nodes, de, self.device)
+        else:
+            self.model = GeneralModel(dn, de, sample_param, memory_param, gnn_param, train_param).to(self.device)
+        # id of the batch's first edge (the mailbox reads that batch's edge features)
+        self.e0_buf = torch.zeros(1, dtype=torch.int64, device=self.device)
         if world > 1:
             for p in self.model.parameters():   # identical start on every rank
                 dist.broadcast(p.data, 0)
@@ -101,6 +111,8 @@ class Trainer:
 
     def reset_epoch(self):
         self.sampler.reset()
+        if self.mailbox is not None:
+            self.mailbox.reset()
 
     # -- inputs ---------------------------------------------------------------
     def local_slice(self, b0, b1):
@@ -143,9 +155,18 @@ class Trainer:
         else:
             self._flat = average_gradients(list(self.model.parameters()), self.world, self._flat)
 
+    def _update_memory(self, blocks):
+        """Mailbox then memory writes of the batch (train.py:385-391), from the
+        updated memory the step computed before the optimizer ran."""
+        if self.mailbox is None:
+            return
+        top = blocks[0]
+        R = top.n_dst
+        self.mailbox.update(top.dst_nodes[:R], top.ts[:R], self.engine.last_memory[:R], self.edge_feats, self.e0_buf)
+
     def _train_on(self, blocks):
         if self.engine is not None:
-            self.engine.step(blocks, self.node_feats, self.edge_feats, self.loss_buf)
+            self.engine.step(blocks, self.node_feats, self.edge_feats, self.loss_buf, mailbox=self.mailbox)
             loss = self.loss_buf
         else:
             self.opt.zero_grad(set_to_none=False)
@@ -155,19 +176,29 @@ class Trainer:
         if self.world > 1:
             self._allreduce_grads()
         self.opt.step()
+        self._update_memory(blocks)
         return loss.detach()
 
-    def step_device(self, roots, root_ts, global_roots=None, global_ts=None):
+    def _set_e0(self, e0):
+        if e0 is not None:
+            self.e0_buf.fill_(int(e0))
+        elif self.mailbox is not None:
+            raise ValueError("a memory model's step needs e0, the id of the batch's first edge")
+
+    def step_device(self, roots, root_ts, global_roots=None, global_ts=None, e0=None):
         """One training step on device-resident roots; returns the loss tensor.
         With several ranks, the global batch's roots first advance the time
-        pointers, as one process training on the whole batch would."""
+        pointers, as one process training on the whole batch would.  Memory
+        models also take e0, the id of the batch's first (positive) edge."""
+        self._set_e0(e0)
         if self.world > 1 and global_roots is not None:
             self.sampler.update_pointers(global_roots, global_ts)
         ops.timed("sampler", lambda: self.sampler.sample_device(roots, root_ts))
         return self._train_on(self.blocks())
 
-    def step_host(self, roots_np, ts_np, global_roots_np=None, global_ts_np=None):
+    def step_host(self, roots_np, ts_np, global_roots_np=None, global_ts_np=None, e0=None):
         """End-to-end step through the reference-facing API: host roots in, host loss out."""
+        self._set_e0(e0)
         if self.world > 1 and global_roots_np is not None:
             self.sampler.update_pointers(torch.from_numpy(global_roots_np).to(self.device),
                                          torch.from_numpy(global_ts_np).to(self.device))
@@ -236,8 +267,9 @@ class GraphTrainer(Trainer):
         self.sampler.sample_device(self.roots_buf, self.ts_buf)
         views = self.sampler.block_views()
         blocks = [StaticBlock(views[0], n_roots=self.R0)] + [StaticBlock(v) for v in views[1:]]
+        self._blocks = blocks
         if self.engine is not None:
-            self.engine.step(blocks, self.node_feats, self.edge_feats, self.loss_buf)
+            self.engine.step(blocks, self.node_feats, self.edge_feats, self.loss_buf, mailbox=self.mailbox)
             return
         self._flat.zero_()
         pred_pos, pred_neg = self.model(blocks, self.node_feats, self.edge_feats)
@@ -249,6 +281,7 @@ class GraphTrainer(Trainer):
         if self.world > 1:
             self._flat.div_(self.world)
         self.opt.step()
+        self._update_memory(self._blocks)
 
     def _eager_step(self):
         self._fwd_bwd()
@@ -292,13 +325,16 @@ class GraphTrainer(Trainer):
         roots, ts = self.local_of(groots, gts)
         self.roots_buf.copy_(roots)
         self.ts_buf.copy_(ts)
+        self.e0_buf.fill_(b0)
         if self.world > 1:
             self.groots_buf.copy_(groots)
             self.gts_buf.copy_(gts)
 
-    def step_device(self, roots=None, root_ts=None, global_roots=None, global_ts=None):
+    def step_device(self, roots=None, root_ts=None, global_roots=None, global_ts=None, e0=None):
         """One replayed step on the device-resident input buffers (or the given
         device tensors); returns the loss tensor (no host round trip)."""
+        if e0 is not None:
+            self.e0_buf.fill_(int(e0))
         if roots is not None:
             self.roots_buf.copy_(roots)
             self.ts_buf.copy_(root_ts)
@@ -310,7 +346,7 @@ class GraphTrainer(Trainer):
         self._replay()
         return self.loss_buf
 
-    def step_host_pipelined(self, roots_np, ts_np, global_roots_np=None, global_ts_np=None):
+    def step_host_pipelined(self, roots_np, ts_np, global_roots_np=None, global_ts_np=None, e0=None):
         """step_host without waiting for this step: the inputs go through pinned
         slot i % 2, the loss comes back into that slot's pinned word, and the
         call returns the previous step's loss (None on the first call) once that
@@ -319,6 +355,7 @@ class GraphTrainer(Trainer):
         sl = self._slots[self._slot]
         if sl["done"] is not None:
             sl["done"].synchronize()           # the step that used this slot two calls ago
+        self._set_e0(e0)
         sl["roots"].numpy()[:] = roots_np
         sl["ts"].numpy()[:] = ts_np
         self.roots_buf.copy_(sl["roots"], non_blocking=True)
@@ -350,9 +387,10 @@ class GraphTrainer(Trainer):
         self._slots[i]["done"].synchronize()
         return float(self._slots[i]["loss"])
 
-    def step_host(self, roots_np, ts_np, global_roots_np=None, global_ts_np=None):
+    def step_host(self, roots_np, ts_np, global_roots_np=None, global_ts_np=None, e0=None):
         """End-to-end step: host roots -> pinned staging -> device buffers ->
         replay -> loss read back to the host."""
+        self._set_e0(e0)
         self.h_roots.numpy()[:] = roots_np
         self.h_ts.numpy()[:] = ts_np
         self.roots_buf.copy_(self.h_roots, non_blocking=True)

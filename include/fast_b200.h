@@ -339,6 +339,47 @@ int fb_q_time_bwd(const float *v, int D, const float *W_q, int64_t ldwq, int dn,
 int fb_adam_step(float *p, const float *g, float *m, float *v, int64_t n, float lr, float beta1,
                  float beta2, float eps, int64_t *step, uint32_t *done, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------- */
+/* TGN node memory (memorys.py:6-182, 270-304).  Tables live on the device:  */
+/* memory [N, dmem], mem_ts [N], mailbox [N, mailbox_size, dmail],           */
+/* mailbox_ts [N, mailbox_size], next_pos [N] (int32).                       */
+/* ------------------------------------------------------------------------- */
+/* MailBox.prep_input_mails (memorys.py:51-73) fused with the time encoding of
+ * GRUMemeoryUpdater.forward (memorys.py:286-289): for source rows r < *n_dev
+ * (all n without it), id = nodes[r]:
+ *   h0[r] = memory[id],  dtm[r] = ts[r] - mem_ts[id] (dtm may be NULL),
+ *   x[r]  = [mailbox[id] (dmail = mailbox_size * mail width) | cos(w dtm + b)]. */
+int fb_mem_gather(const int32_t *nodes, const float *ts, int64_t n, const int32_t *n_dev,
+                  const float *memory, int dmem, const float *mem_ts, const float *mailbox, int dmail,
+                  const float *w, const float *b, int dtime, float *x, int64_t ldx, float *h0, float *dtm,
+                  cudaStream_t stream);
+/* torch.nn.GRUCell gates (the updater of memorys.py:272-304) from the products
+ * gi = x W_ih^T + b_ih and gh = h0 W_hh^T + b_hh ([n, 3H], gates r, z, n):
+ * writes h1 = (1 - z) n + z h0 and keeps (r, z, n) in gi for fb_gru_bwd. */
+int fb_gru_fwd(float *gi, const float *gh, const float *h0, float *h1, int64_t n, const int32_t *n_dev, int H,
+               cudaStream_t stream);
+/* Backward of fb_gru_fwd for dh1 (row stride ld_dh): overwrites gi with d(gi)
+ * and gh with d(gh); h0 (the stored memory) gets no gradient. */
+int fb_gru_bwd(float *gi, float *gh, const float *h0, const float *dh1, int64_t ld_dh, int64_t n,
+               const int32_t *n_dev, int H, cudaStream_t stream);
+/* MailBox.update_mailbox, deliver_to 'self', mail_combine 'last'
+ * (memorys.py:101-142): the n positive edges (roots [src | dst | neg], h the
+ * updated memory of those roots, f the edge features of the batch's edges
+ * e0 .. e0+n-1 with e0 = *e0_dev, a device int64, 0 when NULL) deliver
+ * [h_self | h_other | f] to both endpoints; of several
+ * mails to one node the last in the reference's interleaved order wins.
+ * last [N] (uint64, zero-initialised), gen and done (uint32, gen = 1, done = 0
+ * initially) are the write-order bookkeeping, advanced on the device. */
+int fb_mailbox_update_self(const int32_t *roots, const float *root_ts, int64_t n, const float *h, int64_t ldh,
+                           int dmem, const float *f, int64_t ldf, int de, const int64_t *e0_dev, float *mailbox,
+                           float *mailbox_ts, int32_t *next_pos, int mailbox_size, unsigned long long *last,
+                           uint32_t *gen, uint32_t *done, cudaStream_t stream);
+/* MailBox.update_memory (memorys.py:84-99): memory[roots[k]] = h[k],
+ * mem_ts[roots[k]] = root_ts[k] for k < 2n, the last occurrence winning. */
+int fb_memory_update(const int32_t *roots, const float *root_ts, int64_t n, const float *h, int64_t ldh, int dmem,
+                     float *memory, float *mem_ts, unsigned long long *last, uint32_t *gen, uint32_t *done,
+                     cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
