@@ -299,12 +299,15 @@ def run_fast(args):
     n_batches = graph.train_end // gB
     warm, timed = epoch_schedule(n_batches, args.warmup, args.steps)
 
+    # memory models also take the id of the batch's first edge (its mails carry that batch's edge features)
+    e0_kw = (lambda b0: dict(e0=b0)) if getattr(tr, "mailbox", None) is not None else (lambda b0: {})
+
     def dev_step(i):
         b0, b1 = i * gB, (i + 1) * gB
         if args.eager:
             groots, gts = tr.batch_roots(b0, b1)
             roots, rts = tr.local_of(groots, gts)
-            return tr.step_device(roots, rts, groots, gts)
+            return tr.step_device(roots, rts, groots, gts, **e0_kw(b0))
         tr.load_device_roots(b0, b1)
         return tr.step_device()
 
@@ -368,7 +371,7 @@ def run_fast(args):
         gts = np.concatenate([t_np, t_np, t_np]).astype(np.float32)
         lo = tr.rank * B
         sel = np.concatenate([np.arange(lo, lo + B), gB + np.arange(lo, lo + B), 2 * gB + np.arange(lo, lo + B)])
-        host_step(groots[sel], gts[sel], groots, gts)
+        host_step(groots[sel], gts[sel], groots, gts, **e0_kw(b0))
     if hasattr(tr, "finish_pipelined"):
         tr.finish_pipelined()
     torch.cuda.synchronize()
@@ -388,7 +391,7 @@ def run_fast(args):
     for i in prof:
         groots, gts = tr.batch_roots(i * gB, (i + 1) * gB)
         roots, rts = tr.local_of(groots, gts)
-        Trainer.step_device(tr, roots, rts, groots, gts)
+        Trainer.step_device(tr, roots, rts, groots, gts, **e0_kw(i * gB))
     kern = ops.TIMER.summary()
     ops.TIMER = None
 
@@ -443,7 +446,7 @@ def run_fast(args):
         "clocks": clocks,
         "last_loss": float(loss),
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and getattr(tr, "mailbox", None) is None:
         line["cpu_baseline"] = cpu_baseline(cfg, warm, timed, args.cpu_seconds)
     print(json.dumps(line), flush=True)
     if world > 1:
