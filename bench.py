@@ -40,6 +40,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="fast", choices=["fast", "reference"])
     ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--data", default=None,
+                    help="dataset directory in the reference's format (edges.csv + ext_full.npz) instead of the "
+                         "config's synthetic graph; feature widths and the model still come from --config")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=5)
@@ -220,10 +223,14 @@ def epoch_schedule(n_batches, warmup, steps):
     return warm, timed
 
 
-def cpu_workload(cfg):
+def cpu_workload(cfg, data=None):
     import torch
     from fast_b200.data import make_graph
-    graph = make_graph(cfg)
+    if data:
+        from fast_b200.dataio import load_graph
+        graph = load_graph(data)
+    else:
+        graph = make_graph(cfg)
     g = torch.Generator()
     g.manual_seed(7)
     ef = torch.randn(cfg.edges, cfg.d_edge, generator=g) if cfg.d_edge else None
@@ -238,8 +245,10 @@ def run_reference(args):
         return 0
     from fast_b200.data import CONFIGS
     cfg = CONFIGS[args.config]
+    if args.data:
+        _, cfg = workload_graph(args, cfg)
     threads = len(os.sched_getaffinity(0))
-    graph, ef, nf = cpu_workload(cfg)
+    graph, ef, nf = cpu_workload(cfg, args.data)
     gB = cfg.batch * args.gpus          # the fast arm's global batch
     step, reset, kind = cpu_reference_step_fn(cfg, graph, ef, nf, threads, gB)
     warm, timed = epoch_schedule(graph.train_end // gB, args.warmup, args.steps)
@@ -255,7 +264,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded, %s shapes)" % cfg.name,
+        "data": data_label(args, cfg),
         "config": {"workload": cfg.name, "global_batch": gB, "fanout": list(cfg.fanout),
                    "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge,
                    "batches": SCHEDULE_NOTE},
@@ -285,7 +294,7 @@ def run_fast(args):
     ops.USE_TC = args.gemm == "tc"
     from fast_b200.train import GraphTrainer, Trainer
     cfg = CONFIGS[args.config]
-    graph = make_graph(cfg)
+    graph, cfg = workload_graph(args, cfg)
     nf, ef = make_features(cfg, cfg.edges, dev)
     sp, mp, gp, tp = model_params(cfg)
     fused = args.path == "fused"
@@ -429,7 +438,7 @@ def run_fast(args):
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, %s shapes)" % cfg.name,
+        "vs_baseline": None, "dtype": "f32", "data": data_label(args, cfg),
         "config": {"workload": cfg.name, "global_batch": gB, "local_batch": B, "fanout": list(cfg.fanout),
                    "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge,
                    "parallelism": "dp%d" % world, "launch": "eager" if args.eager else "cuda_graph",
@@ -447,7 +456,7 @@ def run_fast(args):
         "last_loss": float(loss),
     }
     if world == 1 and not args.no_cpu_baseline and getattr(tr, "mailbox", None) is None:
-        line["cpu_baseline"] = cpu_baseline(cfg, warm, timed, args.cpu_seconds)
+        line["cpu_baseline"] = cpu_baseline(cfg, warm, timed, args.cpu_seconds, args.data)
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -455,12 +464,12 @@ def run_fast(args):
     return 0
 
 
-def cpu_baseline(cfg, warm, timed, budget_s):
+def cpu_baseline(cfg, warm, timed, budget_s, data=None):
     """Reference CPU path on the GPU run's batch schedule (1 GPU), stopped
     after ~budget_s; a stop before the end keeps the earlier, smaller batches,
     which favours the CPU."""
     threads = len(os.sched_getaffinity(0))
-    graph, ef, nf = cpu_workload(cfg)
+    graph, ef, nf = cpu_workload(cfg, data)
     step, reset, kind = cpu_reference_step_fn(cfg, graph, ef, nf, threads, cfg.batch)
     reset()
     for i in warm:
@@ -582,6 +591,25 @@ def run_kernel_suite(args):
           lambda: ops.gemm_group([dict(kind=ops.NN, A=dkv, B=W_kv[:, de:], out=dAt)]),
           "M=%d, N=%d, K=%d" % (E, dt_, 2 * D))
     return 0
+
+
+def data_label(args, cfg):
+    if args.data:
+        return "dataset %s read from edges.csv + ext_full.npz; seeded random features" % cfg.name
+    return "synthetic (seeded, %s shapes)" % cfg.name
+
+
+def workload_graph(args, cfg):
+    """The config's synthetic graph, or the dataset of --data (the config then
+    takes that graph's node and edge counts)."""
+    import dataclasses
+    from fast_b200.data import make_graph
+    if not args.data:
+        return make_graph(cfg), cfg
+    from fast_b200.dataio import load_graph
+    g = load_graph(args.data)
+    return g, dataclasses.replace(cfg, name=os.path.basename(os.path.normpath(args.data)), nodes=g.n_nodes,
+                                  edges=len(g.src))
 
 
 def main():
