@@ -91,6 +91,12 @@ _SIGS = {
     "fb_gru_bwd": (_I, [_P, _P, _P, _P, _I64, _I64, _P, _I, _P]),
     "fb_mailbox_update_self": (_I, [_P, _P, _I64, _P, _I64, _I, _P, _I64, _I, _P, _P, _P, _P, _I, _P, _P, _P, _P]),
     "fb_memory_update": (_I, [_P, _P, _I64, _P, _I64, _I, _P, _P, _P, _P, _P, _P]),
+    "fb_mail_slots_gather": (_I, [_P, _P, _I64, _P, _P, _I, _P, _P, _I, _I, _P, _P, _I, _P, _I64, _P, _P, _P]),
+    "fb_add_layernorm_fwd": (_I, [_P, _P, _P, _P, _F, _P, _P, _P, _I64, _P, _I, _P]),
+    "fb_add_layernorm_bwd_ws_bytes": (ctypes.c_size_t, [_I64, _I]),
+    "fb_add_layernorm_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64, _P, _I, _P, _P]),
+    "fb_mailbox_update_neighbors": (_I, [_P, _P, _P, _I64, _P, _I64, _P, _I64, _I, _P, _I64, _I, _P, _P, _P, _P, _I,
+                                         _P, _P, _P, _P]),
 }
 
 class GemmProblem(ctypes.Structure):

@@ -59,6 +59,17 @@ class FusedStep:
             raise NotImplementedError("node memory needs memory.MemoryModel")
         self.model = model
         self.last_memory = None
+        # APAN (memorys.py:342-385 + layers.py:242-249): the transformer memory
+        # updater feeds an identity LayerNorm; no attention layers
+        self.apan = model.gnn_param["arch"] == "identity"
+        self.mem_kv = _LayerParams.__new__(_LayerParams) if self.apan else None
+        if self.apan:
+            self.mem_kv.L = self.mem
+            self.mem_kv.D = self.mem.dim_out
+            self.mem_kv.W_kv = self.mem_kv.b_kv = self.mem_kv.gW_kv = self.mem_kv.gb_kv = None
+            self.layers = []
+            self.flat = self._build_flat()
+            return
         self.layers = [_LayerParams(model.layers["l%dh0" % l]) for l in range(model.gnn_param["layer"])]
         for lp in self.layers:
             if lp.dn + lp.dtime == 0:
@@ -77,7 +88,7 @@ class FusedStep:
         names = {id(p): n for n, p in m.named_parameters()}
         groups = []                      # (layer or None, kind, shape, [parameter names])
         seated = set()
-        for lp in self.layers:
+        for lp in self.layers + ([self.mem_kv] if self.apan else []):
             L = lp.L
             groups.append((lp, "W", (2 * lp.D, L.w_k.weight.shape[1]), [names[id(L.w_k.weight)],
                                                                          names[id(L.w_v.weight)]]))
@@ -275,37 +286,67 @@ class FusedStep:
             ops.time_encode_bwd(dxt, st["dtm"], te.w.weight.view(-1), te.w.bias, g(te.w.weight).view(-1),
                                 g(te.w.bias), n_dev=n_dev)
 
-    # -- whole step -----------------------------------------------------------
-    def step(self, blocks, node_table, edge_table, loss_out, zero_grad=True, scores=None, mailbox=None):
-        """blocks in sampler order (hop 1 first), Device- or StaticBlocks.
-        Writes the loss into loss_out (a 0-d device tensor) and the gradients
-        into the parameters' .grad (zeroed first unless zero_grad=False);
-        with `scores` ([2B] device tensor) also the positive then negative
-        edge scores.  Memory models read their inputs from `mailbox` and
-        leave the updated memory of the first layer's source rows in
-        `last_memory`."""
-        m = self.model
-        training = m.training
-        mfgs = list(reversed(blocks))
+    # -- APAN: transformer memory updater + identity LayerNorm -----------------
+    def _apan_step(self, roots, root_ts, mailbox, loss_out, scores, training, offset_dev):
+        """TransformerMemoryUpdater.forward (memorys.py:358-385) on all roots,
+        IdentityNormLayer (layers.py:248-249), edge predictor, loss, and the
+        backward of all of it."""
+        U, m = self.mem, self.model
+        g = lambda p: p.grad
         dev = self.flat.device
-        if m._drop_step is None or m._drop_step.device != dev:
-            m._drop_step = torch.zeros(1, dtype=torch.int64, device=dev)
-        if training:
-            m._drop_step += 1
-        if zero_grad:
-            self.flat.zero_()
-        saved, h = [], None
-        mem_st = None
-        if self.mem is not None:
-            if mailbox is None:
-                raise ValueError("a memory model needs its MailBox")
-            h, mem_st = self._memory_fwd(mfgs[0], mailbox)
-            self.last_memory = h
-        for l, blk in enumerate(mfgs):
-            st, h = self._layer_fwd(l, blk, h, node_table if (l == 0 and mem_st is None) else None, edge_table,
-                                    m._drop_step, training)
-            saved.append(st)
-        ep = m.edge_predictor
+        n = roots.shape[0]
+        S, D, H = mailbox.size, U.dim_out, U.att_h
+        dmail = mailbox.dim_mail
+        kin = dmail + U.dim_time
+        x = torch.empty(n * S, kin, device=dev)
+        h0 = torch.empty(n, D, device=dev)
+        dts = torch.empty(n * S, device=dev)
+        mailbox.gather_slots(roots, root_ts, n, None, U.time_enc if U.dim_time > 0 else None, x, h0, dts)
+        kvp = self.mem_kv
+        KV = torch.empty(n * S, 2 * D, device=dev)
+        Q = torch.empty(n, D, device=dev)
+        ops.gemm_group([dict(kind=ops.NT, A=x, B=kvp.W_kv, bias=kvp.b_kv, out=KV),
+                        dict(kind=ops.NT, A=h0, B=U.w_q.weight, bias=U.w_q.bias, out=Q)], name="gemm_group:kv_q")
+        rptr = torch.arange(0, n * S + 1, S, dtype=torch.int32, device=dev)   # every root: its S slots
+        p_att = U.att_dropout_p if training else 0.0
+        agg, att = ops.attn_fwd(Q, KV[:, :D], KV[:, D:], rptr, H, U.negative_slope, p_att, 0x5EED + 9, 0,
+                                offset_dev=offset_dev)
+        ln1, xhat1, rstd1 = ops.add_layernorm_fwd(agg, h0, U.layer_norm.weight, U.layer_norm.bias,
+                                                  eps=U.layer_norm.eps)
+        Z = torch.empty(n, D, device=dev)
+        ops.gemm_group([dict(kind=ops.NT, A=ln1, B=U.mlp.weight, bias=U.mlp.bias, out=Z)], name="gemm_group:w_out")
+        norm = m.layers["l0h0"].norm
+        p_drop = U.dropout.p if training else 0.0
+        # y = relu(dropout(mlp(.))) is the updated memory; out = the identity layer's LayerNorm of it
+        y, out = ops.layer_tail_fwd(Z, norm.weight, norm.bias, eps=norm.eps, drop_p=p_drop, seed=0x7A11 + 9,
+                                    offset_dev=offset_dev, y=Z)
+        self.last_memory = y
+        dh = self._predictor(out, loss_out, scores)
+        # backward
+        dZ = ops.layer_tail_bwd(dh, y, norm.weight, g(norm.weight), g(norm.bias), eps=norm.eps, drop_p=p_drop)
+        dln1 = torch.empty(n, D, device=dev)
+        ops.gemm_group([dict(kind=ops.TN, A=dZ, B=ln1, out=g(U.mlp.weight), accumulate=True, db=g(U.mlp.bias)),
+                        dict(kind=ops.NN, A=dZ, B=U.mlp.weight, out=dln1)], name="gemm_group:bwd_dz")
+        dagg = ops.add_layernorm_bwd(dln1, xhat1, rstd1, U.layer_norm.weight, g(U.layer_norm.weight),
+                                     g(U.layer_norm.bias))
+        dQ, dKV = ops.attn_bwd(Q, KV[:, :D], KV[:, D:], rptr, att, dagg, H, U.negative_slope, p_att, 0x5EED + 9, 0,
+                               offset_dev=offset_dev)
+        probs = [dict(kind=ops.TN, A=dKV, B=x, out=kvp.gW_kv, accumulate=True, db=kvp.gb_kv),
+                 dict(kind=ops.TN, A=dQ, B=h0, out=g(U.w_q.weight), accumulate=True, db=g(U.w_q.bias))]
+        dxt = None
+        if U.dim_time > 0:
+            dxt = torch.empty(n * S, U.dim_time, device=dev)
+            probs.append(dict(kind=ops.NN, A=dKV, B=kvp.W_kv[:, dmail:], out=dxt))
+        ops.gemm_group(probs, name="gemm_group:bwd_dkv_dq")
+        if dxt is not None:
+            te = U.time_enc
+            ops.time_encode_bwd(dxt, dts, te.w.weight.view(-1), te.w.bias, g(te.w.weight).view(-1), g(te.w.bias))
+        return loss_out
+
+    def _predictor(self, h, loss_out, scores):
+        """EdgePredictor + BCE loss forward and backward; returns dh."""
+        ep = self.model.edge_predictor
+        dev = h.device
         B = h.shape[0] // 3
         D = h.shape[1]
         S = torch.empty(B, D, device=dev)
@@ -324,6 +365,45 @@ class FusedStep:
                  db=ep.dst_fc.bias.grad),
             dict(kind=ops.NN, A=dS, B=ep.src_fc.weight, out=dh[:B]),
             dict(kind=ops.NN, A=dP, B=ep.dst_fc.weight, out=dh[B:3 * B])], name="gemm_group:pred_bwd")
+        return dh
+
+    # -- whole step -----------------------------------------------------------
+    def step(self, blocks, node_table, edge_table, loss_out, zero_grad=True, scores=None, mailbox=None,
+             roots=None, root_ts=None):
+        """blocks in sampler order (hop 1 first), Device- or StaticBlocks.
+        Writes the loss into loss_out (a 0-d device tensor) and the gradients
+        into the parameters' .grad (zeroed first unless zero_grad=False);
+        with `scores` ([2B] device tensor) also the positive then negative
+        edge scores.  Memory models read their inputs from `mailbox` and
+        leave the updated memory of the first layer's source rows in
+        `last_memory`; APAN models take the batch's roots and times (its
+        updater runs on the roots, not on the sampled block)."""
+        m = self.model
+        training = m.training
+        mfgs = list(reversed(blocks))
+        dev = self.flat.device
+        if m._drop_step is None or m._drop_step.device != dev:
+            m._drop_step = torch.zeros(1, dtype=torch.int64, device=dev)
+        if training:
+            m._drop_step += 1
+        if zero_grad:
+            self.flat.zero_()
+        if self.apan:
+            if mailbox is None or roots is None:
+                raise ValueError("an APAN step needs its MailBox and the batch's roots")
+            return self._apan_step(roots, root_ts, mailbox, loss_out, scores, training, m._drop_step)
+        saved, h = [], None
+        mem_st = None
+        if self.mem is not None:
+            if mailbox is None:
+                raise ValueError("a memory model needs its MailBox")
+            h, mem_st = self._memory_fwd(mfgs[0], mailbox)
+            self.last_memory = h
+        for l, blk in enumerate(mfgs):
+            st, h = self._layer_fwd(l, blk, h, node_table if (l == 0 and mem_st is None) else None, edge_table,
+                                    m._drop_step, training)
+            saved.append(st)
+        dh = self._predictor(h, loss_out, scores)
         for l in range(len(mfgs) - 1, -1, -1):
             rows = mfgs[l - 1].n_dst if l > 0 else (mfgs[0].n_src if mem_st is not None else 0)
             dh = self._layer_bwd(l, saved[l], dh, rows)

@@ -10,9 +10,12 @@ trip and can be captured in a CUDA graph.  `GRUMemoryUpdater` and
 (memory_updater.updater.weight_ih, ...), so a state_dict loads across; their
 forward and backward run in `engine.FusedStep`.
 
-Covered: memory 'node', updater 'gru', deliver_to 'self', mail_combine
-'last', combine_node_feature with no node features (TGN-1).  Other variants
-raise NotImplementedError.
+Covered: memory 'node' with
+  * updater 'gru', deliver_to 'self', mail_combine 'last', memory combined
+    into the node input without node features (TGN-1);
+  * updater 'transformer', deliver_to 'neighbors', mail_combine 'last', the
+    'identity' GNN and no_neg sampling (APAN-1).
+Other variants raise NotImplementedError.
 """
 import torch
 
@@ -28,9 +31,10 @@ class MailBox:
     def __init__(self, memory_param, num_nodes, dim_edge_feat, device):
         if memory_param["type"] != "node":
             raise NotImplementedError("memory type %r" % memory_param["type"])
-        if memory_param["deliver_to"] != "self" or memory_param["mail_combine"] != "last":
+        if memory_param["deliver_to"] not in ("self", "neighbors") or memory_param["mail_combine"] != "last":
             raise NotImplementedError("mailbox delivery %r / %r" % (memory_param["deliver_to"],
                                                                     memory_param["mail_combine"]))
+        self.deliver_to = memory_param["deliver_to"]
         dev = torch.device(device)
         self.memory_param = memory_param
         self.dim_mem = memory_param["dim_out"]
@@ -65,17 +69,40 @@ class MailBox:
              ptr(self.node_memory_ts), ptr(self.mailbox), self.size * self.dim_mail, ptr(w), ptr(b), dt, ptr(out_x),
              out_x.stride(0), ptr(out_h0), ptr(out_dt), stream_ptr())
 
-    def update(self, roots, root_ts, h, edge_feats, e0_dev):
-        """update_mailbox then update_memory (memorys.py:101-142, 84-99) after a
+    def gather_slots(self, nodes, ts, n, n_dev, time_enc, out_x, out_h0, out_dt):
+        """APAN's updater input (memorys.py:360-372): one row per (root, mailbox
+        slot) with the time encoding of ts - mail_ts, and the roots' memory."""
+        dt = time_enc.dim if time_enc is not None else 0
+        w = time_enc.w.weight.view(-1) if dt else None
+        b = time_enc.w.bias if dt else None
+        call("fb_mail_slots_gather", ptr(nodes), ptr(ts), n, ptr(n_dev), ptr(self.node_memory), self.dim_mem,
+             ptr(self.mailbox), ptr(self.mailbox_ts), self.size, self.dim_mail, ptr(w), ptr(b), dt, ptr(out_x),
+             out_x.stride(0), ptr(out_h0), ptr(out_dt), stream_ptr())
+
+    def update(self, roots, root_ts, h, edge_feats, e0_dev, block=None):
+        """update_mailbox then update_memory (memorys.py:101-178, 84-99) after a
         step: roots / root_ts the batch's [src | dst | neg] roots, h the updated
         memory of those roots (rows in the same order), edge_feats the edge
-        table and e0_dev (device int64) the id of the batch's first edge."""
+        table and e0_dev (device int64) the id of the batch's first edge.
+        deliver_to 'neighbors' also takes the block sampled for the positive
+        roots (its nodes and each edge's root)."""
         n = roots.shape[0] // 3
         de = self.dim_edge_feat
+        if self.deliver_to == "neighbors":
+            call("fb_mailbox_update_neighbors", ptr(block.nodes), ptr(block.row), ptr(root_ts), n,
+                 ptr(block.n_edges_dev), block.n_edges, ptr(h), h.stride(0), self.dim_mem,
+                 ptr(edge_feats) if de else None, edge_feats.stride(0) if de else 0, de, ptr(e0_dev),
+                 ptr(self.mailbox), ptr(self.mailbox_ts), ptr(self.next_mail_pos), self.size, ptr(self._last_mail),
+                 ptr(self._gen[0:1]), ptr(self._done[0:1]), stream_ptr())
+            self._update_memory(roots, root_ts, h, n)
+            return
         call("fb_mailbox_update_self", ptr(roots), ptr(root_ts), n, ptr(h), h.stride(0), self.dim_mem,
              ptr(edge_feats) if de else None, edge_feats.stride(0) if de else 0, de, ptr(e0_dev), ptr(self.mailbox),
              ptr(self.mailbox_ts), ptr(self.next_mail_pos), self.size, ptr(self._last_mail), ptr(self._gen[0:1]),
              ptr(self._done[0:1]), stream_ptr())
+        self._update_memory(roots, root_ts, h, n)
+
+    def _update_memory(self, roots, root_ts, h, n):
         call("fb_memory_update", ptr(roots), ptr(root_ts), n, ptr(h), h.stride(0), self.dim_mem,
              ptr(self.node_memory), ptr(self.node_memory_ts), ptr(self._last_mem), ptr(self._gen[1:2]),
              ptr(self._done[1:2]), stream_ptr())
@@ -100,16 +127,46 @@ class GRUMemoryUpdater(torch.nn.Module):
             self.time_enc = TimeEncode(dim_time)
 
 
+class TransformerMemoryUpdater(torch.nn.Module):
+    """TransformerMemoryUpdater (memorys.py:342-385): attention of the memory
+    over the mailbox slots, residual, LayerNorm, mlp, dropout, ReLU.
+    Parameters as the reference's."""
+
+    def __init__(self, memory_param, dim_in, dim_out, dim_time, train_param):
+        super().__init__()
+        self.memory_param = memory_param
+        self.dim_time = dim_time
+        self.dim_out = dim_out
+        self.att_h = memory_param["attention_head"]
+        if dim_time > 0:
+            self.time_enc = TimeEncode(dim_time)
+        self.w_q = torch.nn.Linear(dim_out, dim_out)
+        self.w_k = torch.nn.Linear(dim_in + dim_time, dim_out)
+        self.w_v = torch.nn.Linear(dim_in + dim_time, dim_out)
+        self.layer_norm = torch.nn.LayerNorm(dim_out)
+        self.mlp = torch.nn.Linear(dim_out, dim_out)
+        self.dropout = torch.nn.Dropout(train_param["dropout"])
+        self.att_dropout_p = train_param["att_dropout"]
+        self.negative_slope = 0.2
+
+
+class IdentityNormLayer(torch.nn.Module):
+    """IdentityNormLayer (layers.py:242-249): LayerNorm of the node input."""
+
+    def __init__(self, dim_out):
+        super().__init__()
+        self.norm = torch.nn.LayerNorm(dim_out)
+
+
 class MemoryModel(torch.nn.Module):
     """GeneralModel with node memory (modules.py:8-47): memory_updater,
     layers['l0h0'.. ] over the memory as node input, edge_predictor."""
 
     def __init__(self, dim_node, dim_edge, sample_param, memory_param, gnn_param, train_param):
         super().__init__()
-        if memory_param.get("memory_update") != "gru":
-            raise NotImplementedError("memory updater %r" % memory_param.get("memory_update"))
-        if gnn_param["arch"] != "transformer_attention":
-            raise NotImplementedError("only transformer_attention layers are on the device path")
+        upd = memory_param.get("memory_update")
+        if (upd, gnn_param["arch"]) not in (("gru", "transformer_attention"), ("transformer", "identity")):
+            raise NotImplementedError("memory updater %r with %r layers" % (upd, gnn_param["arch"]))
         if sample_param.get("history", 1) != 1:
             raise NotImplementedError("snapshot history > 1 is not on the device path")
         self.dim_node = dim_node
@@ -121,9 +178,18 @@ class MemoryModel(torch.nn.Module):
         self.gnn_param = gnn_param
         self.train_param = train_param
         dmem = memory_param["dim_out"]
+        self.layers = torch.nn.ModuleDict()
+        if upd == "transformer":
+            # modules.py:23-24, 37-43: the transformer updater feeds an identity (LayerNorm) layer
+            self.memory_updater = TransformerMemoryUpdater(memory_param, 2 * dmem + dim_edge, dmem,
+                                                           memory_param["dim_time"], train_param)
+            self.gnn_param["layer"] = 1
+            self.layers["l0h0"] = IdentityNormLayer(dmem)
+            self.edge_predictor = EdgePredictor(self.gnn_param["dim_out"])
+            self._drop_step = None
+            return
         self.memory_updater = GRUMemoryUpdater(memory_param, 2 * dmem + dim_edge, dmem, memory_param["dim_time"],
                                                dim_node)
-        self.layers = torch.nn.ModuleDict()
         self.layers["l0h0"] = TransfomerAttentionLayer(dmem, dim_edge, gnn_param["dim_time"], gnn_param["att_head"],
                                                        train_param["dropout"], train_param["att_dropout"],
                                                        gnn_param["dim_out"])

@@ -70,6 +70,7 @@ class StaticBlock:
         self.src_nodes = view["nbr"][:cap_e]
         self.dt_edges = view["dte"][:cap_e]
         self.rptr = view["rptr"][:self.n_dst + 1]
+        self.row = view["row"][:cap_e]
         # all source rows [roots | one per edge] and their times (node memory)
         self.nodes = view["nodes"][:self.n_src]
         self.ts = view["ts"][:self.n_src]

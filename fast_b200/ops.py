@@ -220,6 +220,31 @@ def gru_bwd(gi, gh, h0, dh1, n_dev=None):
                          stream_ptr()))
 
 
+def add_layernorm_fwd(x, res, gamma, beta, eps=1e-5, n_dev=None):
+    """out = LayerNorm(x + res) per row; returns (out, xhat, rstd) for the backward
+    (the residual step of memorys.py:378-379)."""
+    n, D = x.shape
+    out = torch.empty_like(x)
+    xhat = torch.empty_like(x)
+    rstd = torch.empty(n, device=x.device, dtype=torch.float32)
+    _launch("add_layernorm_fwd", 4 * n * D * 4, 0, 1,
+            lambda: call("fb_add_layernorm_fwd", ptr(x), ptr(res), ptr(gamma), ptr(beta), float(eps), ptr(out),
+                         ptr(xhat), ptr(rstd), n, _p(n_dev), D, stream_ptr()))
+    return out, xhat, rstd
+
+
+def add_layernorm_bwd(dout, xhat, rstd, gamma, dgamma, dbeta, n_dev=None):
+    """Gradient of add_layernorm_fwd's input (x and res alike); accumulates
+    dgamma, dbeta."""
+    n, D = dout.shape
+    dx = torch.empty_like(dout)
+    ws = torch.empty(int(lib.fb_add_layernorm_bwd_ws_bytes(n, D)), device=dout.device, dtype=torch.uint8)
+    _launch("add_layernorm_bwd", 4 * n * D * 3, 0, 2,
+            lambda: call("fb_add_layernorm_bwd", ptr(dout), ptr(xhat), ptr(rstd), ptr(gamma), ptr(dx), ptr(dgamma),
+                         ptr(dbeta), n, _p(n_dev), D, ptr(ws), stream_ptr()))
+    return dx
+
+
 def layer_tail_fwd(z, gamma, beta, eps=1e-5, drop_p=0.0, seed=0, offset=0, offset_dev=None, mask_u=None,
                    y=None, out=None, n_dev=None, gate_dev=None):
     """y = relu(dropout(z)), out = LayerNorm(y) per row (rows >= *n_dev: out = 0;

@@ -155,18 +155,28 @@ class Trainer:
         else:
             self._flat = average_gradients(list(self.model.parameters()), self.world, self._flat)
 
-    def _update_memory(self, blocks):
+    def _update_memory(self, blocks, roots, root_ts):
         """Mailbox then memory writes of the batch (train.py:385-391), from the
-        updated memory the step computed before the optimizer ran."""
+        updated memory the step computed before the optimizer ran (its first
+        rows are the roots'), and for delivery to neighbours the block sampled
+        for the positive roots."""
         if self.mailbox is None:
             return
-        top = blocks[0]
-        R = top.n_dst
-        self.mailbox.update(top.dst_nodes[:R], top.ts[:R], self.engine.last_memory[:R], self.edge_feats, self.e0_buf)
+        R = roots.shape[0]
+        self.mailbox.update(roots, root_ts, self.engine.last_memory[:R], self.edge_feats, self.e0_buf, block=blocks[0])
 
-    def _train_on(self, blocks):
+    def _sample_roots(self, roots, root_ts):
+        """The roots the sampler sees: with no_neg (APAN, train.py:323-325) only
+        the positive [src | dst] ones."""
+        if self.sample_param.get("no_neg"):
+            k = roots.shape[0] // 3 * 2
+            return roots[:k], root_ts[:k]
+        return roots, root_ts
+
+    def _train_on(self, blocks, roots=None, root_ts=None):
         if self.engine is not None:
-            self.engine.step(blocks, self.node_feats, self.edge_feats, self.loss_buf, mailbox=self.mailbox)
+            self.engine.step(blocks, self.node_feats, self.edge_feats, self.loss_buf, mailbox=self.mailbox,
+                             roots=roots, root_ts=root_ts)
             loss = self.loss_buf
         else:
             self.opt.zero_grad(set_to_none=False)
@@ -176,7 +186,8 @@ class Trainer:
         if self.world > 1:
             self._allreduce_grads()
         self.opt.step()
-        self._update_memory(blocks)
+        if self.mailbox is not None:
+            self._update_memory(blocks, roots, root_ts)
         return loss.detach()
 
     def _set_e0(self, e0):
@@ -193,8 +204,9 @@ class Trainer:
         self._set_e0(e0)
         if self.world > 1 and global_roots is not None:
             self.sampler.update_pointers(global_roots, global_ts)
-        ops.timed("sampler", lambda: self.sampler.sample_device(roots, root_ts))
-        return self._train_on(self.blocks())
+        sr, st = self._sample_roots(roots, root_ts)
+        ops.timed("sampler", lambda: self.sampler.sample_device(sr, st))
+        return self._train_on(self.blocks(), roots, root_ts)
 
     def step_host(self, roots_np, ts_np, global_roots_np=None, global_ts_np=None, e0=None):
         """End-to-end step through the reference-facing API: host roots in, host loss out."""
@@ -202,8 +214,12 @@ class Trainer:
         if self.world > 1 and global_roots_np is not None:
             self.sampler.update_pointers(torch.from_numpy(global_roots_np).to(self.device),
                                          torch.from_numpy(global_ts_np).to(self.device))
-        self.sampler.sample(roots_np, ts_np, [])
-        return float(self._train_on(self.blocks()))
+        sr, st = self._sample_roots(roots_np, ts_np)
+        self.sampler.sample(sr, st, [])
+        if self.mailbox is None:
+            return float(self._train_on(self.blocks()))
+        dev = self.device
+        return float(self._train_on(self.blocks(), torch.from_numpy(roots_np).to(dev), torch.from_numpy(ts_np).to(dev)))
 
 
 def batch_ranges(train_end, batch):
@@ -264,12 +280,14 @@ class GraphTrainer(Trainer):
     def _fwd_bwd(self):
         if self.world > 1:
             self.sampler.update_pointers(self.groots_buf, self.gts_buf)
-        self.sampler.sample_device(self.roots_buf, self.ts_buf)
+        sr, st = self._sample_roots(self.roots_buf, self.ts_buf)
+        self.sampler.sample_device(sr, st)
         views = self.sampler.block_views()
-        blocks = [StaticBlock(views[0], n_roots=self.R0)] + [StaticBlock(v) for v in views[1:]]
+        blocks = [StaticBlock(views[0], n_roots=sr.shape[0])] + [StaticBlock(v) for v in views[1:]]
         self._blocks = blocks
         if self.engine is not None:
-            self.engine.step(blocks, self.node_feats, self.edge_feats, self.loss_buf, mailbox=self.mailbox)
+            self.engine.step(blocks, self.node_feats, self.edge_feats, self.loss_buf, mailbox=self.mailbox,
+                             roots=self.roots_buf, root_ts=self.ts_buf)
             return
         self._flat.zero_()
         pred_pos, pred_neg = self.model(blocks, self.node_feats, self.edge_feats)
@@ -281,7 +299,8 @@ class GraphTrainer(Trainer):
         if self.world > 1:
             self._flat.div_(self.world)
         self.opt.step()
-        self._update_memory(self._blocks)
+        if self.mailbox is not None:
+            self._update_memory(self._blocks, self.roots_buf, self.ts_buf)
 
     def _eager_step(self):
         self._fwd_bwd()

@@ -380,6 +380,40 @@ int fb_memory_update(const int32_t *roots, const float *root_ts, int64_t n, cons
                      float *memory, float *mem_ts, unsigned long long *last, uint32_t *gen, uint32_t *done,
                      cudaStream_t stream);
 
+/* APAN's TransformerMemoryUpdater (memorys.py:342-385) input: for roots r <
+ * *n_dev (all n without it), slot s < slots, id = nodes[r]:
+ *   x[r * slots + s] = [mailbox[id, s] (dmail) | cos(w (ts[r] - mailbox_ts[id, s]) + b)],
+ *   dts[r * slots + s] = ts[r] - mailbox_ts[id, s],  h0[r] = memory[id]. */
+int fb_mail_slots_gather(const int32_t *nodes, const float *ts, int64_t n, const int32_t *n_dev,
+                         const float *memory, int dmem, const float *mailbox, const float *mailbox_ts, int slots,
+                         int dmail, const float *w, const float *b, int dtime, float *x, int64_t ldx, float *h0,
+                         float *dts, cudaStream_t stream);
+/* out = LayerNorm(x + res; gamma, beta, eps) per row ([n, D], contiguous), the
+ * residual step of memorys.py:378-379; xhat [n, D] and rstd [n] are kept for
+ * the backward. */
+int fb_add_layernorm_fwd(const float *x, const float *res, const float *gamma, const float *beta, float eps,
+                         float *out, float *xhat, float *rstd, int64_t n, const int32_t *n_dev, int D,
+                         cudaStream_t stream);
+/* dx (the gradient of x and of res), dgamma += , dbeta += ; deterministic.
+ * D <= 1024; ws: fb_add_layernorm_bwd_ws_bytes(n, D) bytes. */
+size_t fb_add_layernorm_bwd_ws_bytes(int64_t n, int D);
+int fb_add_layernorm_bwd(const float *dout, const float *xhat, const float *rstd, const float *gamma, float *dx,
+                         float *dgamma, float *dbeta, int64_t n, const int32_t *n_dev, int D, void *ws,
+                         cudaStream_t stream);
+/* MailBox.update_mailbox, deliver_to 'neighbors', mail_combine 'last'
+ * (memorys.py:143-178, APAN): nodes [2n + E] are the block's nodes (the 2n
+ * positive roots, then the node sampled for each edge), row [E] each edge's
+ * root.  Root j receives its own mail [h[j] | h[j +- n] | f[e0 + j mod n]] with
+ * time root_ts[j]; the node of edge e receives the mail of root row[e].  Of
+ * several mails to one node the last in that list wins; it goes to slot
+ * next_pos[node], which then advances modulo mailbox_size.  E = *E_dev when
+ * given (E_cap rows allocated).  last / gen / done as fb_mailbox_update_self. */
+int fb_mailbox_update_neighbors(const int32_t *nodes, const int32_t *row, const float *root_ts, int64_t n,
+                                const int32_t *E_dev, int64_t E_cap, const float *h, int64_t ldh, int dmem,
+                                const float *f, int64_t ldf, int de, const int64_t *e0_dev, float *mailbox,
+                                float *mailbox_ts, int32_t *next_pos, int mailbox_size, unsigned long long *last,
+                                uint32_t *gen, uint32_t *done, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -9,6 +9,9 @@ the module passed in (fp32 or fp64):
   GeneralModel.forward with memory  modules.py:48-70
   MailBox.update_mailbox 'self'     memorys.py:101-142
   MailBox.update_memory             memorys.py:84-99
+  TransformerMemoryUpdater.forward  memorys.py:358-385 (APAN)
+  IdentityNormLayer                 layers.py:242-249
+  MailBox.update_mailbox 'neighbors' memorys.py:143-178 (APAN)
 Index assignments with repeated node ids keep the last occurrence, which is
 what the reference's CPU tensors do; the loops below write in list order.
 """
@@ -106,3 +109,64 @@ def update_memory(state, roots, root_ts, h):
         node = int(roots[k])
         state.node_memory[node] = h[k].to(state.node_memory.dtype)
         state.node_memory_ts[node] = float(root_ts[k])
+
+
+def transformer_memory_forward(U, state, roots, ts):
+    """TransformerMemoryUpdater.forward (memorys.py:358-385) for the roots
+    (node_to_dgl_blocks: no sampled neighbours); returns the updated memory."""
+    idx = torch.from_numpy(np.asarray(roots)).long()
+    dty = U.w_q.weight.dtype
+    n = idx.shape[0]
+    S = state.size
+    mem = state.node_memory[idx].to(dty)
+    mail = state.mailbox[idx].to(dty)                      # [n, S, dmail]
+    H = U.att_h
+    Q = U.w_q(mem).reshape(n, H, -1)
+    if U.dim_time > 0:
+        dt = torch.from_numpy(np.asarray(ts)).float()[:, None] - state.mailbox_ts[idx]
+        tf = time_encode(U.time_enc, dt.reshape(-1)).reshape(n, S, -1)
+        mail = torch.cat([mail, tf], dim=2)
+    K = U.w_k(mail).reshape(n, S, H, -1)
+    V = U.w_v(mail).reshape(n, S, H, -1)
+    att = torch.nn.functional.leaky_relu((Q[:, None, :, :] * K).sum(dim=3), 0.2)
+    att = torch.softmax(att, dim=1)
+    rst = (att[:, :, :, None] * V).sum(dim=1).reshape(n, -1)
+    rst = rst + mem
+    rst = U.layer_norm(rst)
+    rst = U.mlp(rst)
+    rst = U.dropout(rst)
+    return torch.relu(rst)
+
+
+def apan_forward(model, state, roots, ts, neg_samples=1):
+    """GeneralModel.forward of APAN: memory updater on the roots, the identity
+    layer's LayerNorm, edge predictor.  Returns (pred_pos, pred_neg, updated
+    memory)."""
+    h = transformer_memory_forward(model.memory_updater, state, roots, ts)
+    out = model.layers["l0h0"].norm(h)
+    pos, neg = model.edge_predictor(out, neg_samples=neg_samples)
+    return pos, neg, h
+
+
+def update_mailbox_neighbors(state, roots, root_ts, h, batch_edge_feats, block_nodes, block_row):
+    """update_mailbox, deliver_to 'neighbors', mail_combine 'last': the mail of
+    positive root j is [h_j | h_other | f_i] (src roots j < n, then dst roots),
+    its time root_ts[j]; list entry k < 2n is root k itself, entry 2n + e the
+    node sampled for edge e, which gets the mail of its root row[e].  Each
+    node keeps its last entry, written to its next slot, which then advances."""
+    n = len(roots) // 3
+    h = h.detach()
+    last = {}
+    for k, node in enumerate(np.asarray(block_nodes)):
+        last[int(node)] = k
+    for node, k in last.items():
+        j = k if k < 2 * n else int(block_row[k - 2 * n])
+        other, ei = (j + n, j) if j < n else (j - n, j - n)
+        parts = [h[j], h[other]]
+        if batch_edge_feats is not None:
+            parts.append(batch_edge_feats[ei].to(h.dtype))
+        pos = int(state.next_mail_pos[node])
+        state.mailbox[node, pos] = torch.cat(parts).to(state.mailbox.dtype)
+        state.mailbox_ts[node, pos] = float(root_ts[j])
+        if state.size > 1:
+            state.next_mail_pos[node] = (pos + 1) % state.size

@@ -131,6 +131,90 @@ def run_case(out, name, de, seed):
     out[p + "graph/t"] = g["t"]
 
 
+def run_apan(out, name, de, seed, S=10):
+    """APAN-1 (config/APAN-1.yml): transformer memory updater over a mailbox of
+    S slots, delivery to the sampled neighbours, identity GNN, no_neg sampling
+    (train.py:323-325; the model runs on node_to_dgl_blocks of all roots,
+    utils.py:115-124; the reversed sampled block delivers the mails,
+    train.py:387-389).  modules.py:57 calls every layer as layer(block, l, h)
+    but IdentityNormLayer.forward takes the block alone (layers.py:248), so
+    the reference raises there; the layer is called here with the block."""
+    import layers as ref_layers
+    import memorys as ref_mem
+    import modules as ref_modules
+    from fast_util.efficientGOP import fm
+    ref_layers.torch = _TorchOnCpu()
+    fm.fastESMFlag = fm.fastAggFlag = fm.CSR_OUT = 0
+    fm.fastKQV = fm.fastTIME = fm.fastDrop = 0
+    torch.Tensor.cuda = lambda self, *a, **k: self
+    ref_layers.IdentityNormLayer.forward = lambda self, b, *unused: self.norm(b.srcdata["h"])
+    N = 120
+    g = small_graph(n_nodes=N, n_edges=4000, seed=seed, int_ts=False, t_max=50.0, zipf=1.0)
+    torch.manual_seed(seed)
+    ef = torch.randn(4000, de)
+    sp = dict(layer=1, neighbor=[10], strategy="recent", prop_time=False, history=1, duration=0, no_neg=True)
+    mp = dict(type="node", dim_time=DT, deliver_to="neighbors", mail_combine="last", memory_update="transformer",
+              attention_head=2, mailbox_size=S, combine_node_feature=False, dim_out=DM)
+    gp = dict(arch="identity")
+    tp = dict(lr=LR, dropout=0.0, att_dropout=0.0)
+    model = ref_modules.GeneralModel(0, de, sp, mp, gp, tp)
+    mailbox = ref_mem.MailBox(mp, N, de)
+    opt = torch.optim.SGD(model.parameters(), lr=LR)
+    crit = torch.nn.BCEWithLogitsLoss()
+    p = name + "/"
+    for k, v in model.state_dict().items():
+        out[p + "param0/" + k] = v.numpy().copy()
+    ref = load_reference()
+    s = ref.ParallelSampler(g["indptr"], g["indices"], g["eid"], g["ts"], 1, 1, 1, [10], True, False, 1, 0.0)
+    rng = np.random.default_rng(seed)
+    for step in range(STEPS):
+        b0 = B0 + step * B
+        roots = np.concatenate([g["src"][b0:b0 + B], g["dst"][b0:b0 + B], rng.integers(0, N, B).astype(np.int32)])
+        rts = np.concatenate([g["t"][b0:b0 + B]] * 3).astype(np.float32)
+        s.sample(roots[:2 * B], rts[:2 * B], [])
+        r = s.get_ret()[0]
+        nb = FakeBlock([], [], len(roots), len(roots))            # node_to_dgl_blocks
+        nb.srcdata["ID"] = torch.from_numpy(roots)
+        nb.srcdata["ts"] = torch.from_numpy(rts)
+        mfgs = [[nb]]
+        mailbox.prep_input_mails(mfgs[0])
+        opt.zero_grad()
+        pred_pos, pred_neg = model(mfgs)
+        loss = crit(pred_pos, torch.ones_like(pred_pos)) + crit(pred_neg, torch.zeros_like(pred_neg))
+        loss.backward()
+        q = p + "step%d/" % step
+        out[q + "loss"] = np.array([float(loss.detach())], np.float32)
+        out[q + "updated_memory"] = model.memory_updater.last_updated_memory.numpy().copy()
+        if step in (0, STEPS - 1):
+            for n_, prm in model.named_parameters():
+                if prm.grad is not None:
+                    out[q + "grad/" + n_] = prm.grad.numpy().copy()
+        opt.step()
+        rb = FakeBlock(r.row(), r.col(), r.dim_out(), r.dim_in())  # to_dgl_blocks(..., reverse=True)
+        rb.dstdata["ID"] = torch.from_numpy(r.nodes())
+        rb.dstdata["ts"] = torch.from_numpy(r.ts())
+        rb.edata["ID"] = torch.from_numpy(r.eid())
+        mailbox.update_mailbox(model.memory_updater.last_updated_nid, model.memory_updater.last_updated_memory,
+                               roots, rts, ef[b0:b0 + B], rb)
+        mailbox.update_memory(model.memory_updater.last_updated_nid, model.memory_updater.last_updated_memory,
+                              roots, model.memory_updater.last_updated_ts)
+        out[q + "roots"] = roots
+        out[q + "rts"] = rts
+        out[q + "e0"] = np.array([b0], np.int64)
+        out[q + "node_memory"] = mailbox.node_memory.numpy().copy()
+        out[q + "node_memory_ts"] = mailbox.node_memory_ts.numpy().copy()
+        out[q + "mailbox"] = mailbox.mailbox.numpy().copy()
+        out[q + "mailbox_ts"] = mailbox.mailbox_ts.numpy().copy()
+        out[q + "next_mail_pos"] = mailbox.next_mail_pos.numpy().copy()
+        for k in ("row", "col", "eid", "ts", "dts", "nodes"):
+            out[q + "block/" + k] = getattr(r, k)()
+    out[p + "params"] = np.array([N, de, STEPS, B, B0, DM, DT, S], np.int64)
+    out[p + "edge_feats"] = ef.numpy()
+    out[p + "lr"] = np.array([LR], np.float32)
+    for k in ("indptr", "indices", "eid", "ts", "src", "dst", "t"):
+        out[p + "graph/" + k] = g[k]
+
+
 def main():
     if not os.path.isdir(REF):
         raise SystemExit("reference tree not found")
@@ -139,6 +223,7 @@ def main():
     sys.path.insert(0, REF)
     out = {}
     run_case(out, "tgn1", 24, 21)
+    run_apan(out, "apan1", 24, 22)
     path = os.path.join(HERE, "memory_golden.npz")
     np.savez_compressed(path, **out)
     print("wrote", path, len(out), "arrays")

@@ -10,6 +10,9 @@ Every step: loss, gradients and tables within rtol 2e-4 / atol 2e-5 of the
 reference (two fp32 trajectories separate by rounding after an SGD step);
 memory and mail timestamps are exact.  The CUDA-graph replay of a memory
 step equals the same step run eagerly on the same static blocks, bit for bit.
+The same for APAN-1 (fb_mail_slots_gather, the slot attention on the shared
+attention kernels, fb_add_layernorm_*, fb_mailbox_update_neighbors), whose
+next-slot table is also exact.
 """
 import os
 
@@ -23,9 +26,9 @@ pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "memory_golden.npz")
 
 
-def _golden():
+def _golden(case="tgn1"):
     gold = np.load(GOLDEN)
-    return {k.split("/", 1)[1]: gold[k] for k in gold.files if k.startswith("tgn1/")}
+    return {k.split("/", 1)[1]: gold[k] for k in gold.files if k.startswith(case + "/")}
 
 
 def _graph(g):
@@ -147,3 +150,72 @@ def test_tgn_graph_replay_is_the_static_eager_step(cuda):
             assert torch.equal(getattr(graph.mailbox, name), getattr(static.mailbox, name)), (step, name)
     for (n, pg), ps in zip(graph.model.named_parameters(), static.model.parameters()):
         assert torch.equal(pg, ps), n
+
+
+def _apan_params(g):
+    N, de, steps, B, B0, DM, DT, S = (int(x) for x in g["params"])
+    sp = dict(layer=1, neighbor=[10], strategy="recent", prop_time=False, history=1, duration=0, no_neg=True)
+    mp = dict(type="node", dim_time=DT, deliver_to="neighbors", mail_combine="last", memory_update="transformer",
+              attention_head=2, mailbox_size=S, combine_node_feature=False, dim_out=DM)
+    gp = dict(arch="identity")
+    tp = dict(lr=float(g["lr"][0]), dropout=0.0, att_dropout=0.0)
+    return sp, mp, gp, tp, steps, B
+
+
+def test_apan_training_matches_reference(cuda):
+    from fast_b200.train import Trainer
+    g = _golden("apan1")
+    sp, mp, gp, tp, steps, B = _apan_params(g)
+    ef = torch.from_numpy(g["edge_feats"]).to(cuda)
+    tr = Trainer(_graph(g), None, ef, sp, mp, dict(gp), tp, cuda, fused=True)
+    _load_params(tr.model, g)
+    tr.opt = torch.optim.SGD(tr.model.parameters(), lr=tp["lr"])
+    mb = tr.mailbox
+    for step in range(steps):
+        q = "step%d/" % step
+        roots = torch.from_numpy(g[q + "roots"]).to(cuda)
+        rts = torch.from_numpy(g[q + "rts"]).to(cuda)
+        loss = tr.step_device(roots, rts, e0=int(g[q + "e0"][0]))
+        _close(loss.reshape(1), g[q + "loss"], q + "loss")
+        _close(tr.engine.last_memory, g[q + "updated_memory"], q + "updated_memory")
+        for n_, p in tr.model.named_parameters():
+            key = q + "grad/" + n_
+            if key in g:
+                _close(p.grad, g[key], key)
+        for name in ("node_memory", "mailbox"):
+            _close(getattr(mb, name), g[q + name], q + name)
+        assert torch.equal(mb.node_memory_ts.cpu(), torch.from_numpy(g[q + "node_memory_ts"])), step
+        assert torch.equal(mb.mailbox_ts.cpu(), torch.from_numpy(g[q + "mailbox_ts"])), step
+        assert torch.equal(mb.next_mail_pos.cpu().long(), torch.from_numpy(g[q + "next_mail_pos"]).long()), step
+
+
+def test_apan_graph_replay_is_the_static_eager_step(cuda):
+    from fast_b200.train import GraphTrainer
+    g = _golden("apan1")
+    sp, mp, gp, tp, steps, B = _apan_params(g)
+    ef = torch.from_numpy(g["edge_feats"]).to(cuda)
+    mk = lambda: GraphTrainer(_graph(g), None, ef, dict(sp), mp, dict(gp), tp, cuda, batch=B,  # noqa: E731
+                              optimizer="sgd")
+    graph, static = mk(), mk()
+    _load_params(graph.model, g)
+    _load_params(static.model, g)
+    for tr in (graph, static):
+        tr.roots_buf.copy_(torch.from_numpy(g["step0/roots"]).to(cuda))
+        tr.ts_buf.copy_(torch.from_numpy(g["step0/rts"]).to(cuda))
+        tr.e0_buf.fill_(int(g["step0/e0"][0]))
+    graph.capture()
+    for _ in range(3):
+        static._eager_step()
+    for step in range(1, steps):
+        q = "step%d/" % step
+        roots = torch.from_numpy(g[q + "roots"]).to(cuda)
+        rts = torch.from_numpy(g[q + "rts"]).to(cuda)
+        e0 = int(g[q + "e0"][0])
+        lg = float(graph.step_device(roots, rts, e0=e0))
+        static.roots_buf.copy_(roots)
+        static.ts_buf.copy_(rts)
+        static.e0_buf.fill_(e0)
+        static._eager_step()
+        assert lg == float(static.loss_buf), step
+        for name in ("node_memory", "node_memory_ts", "mailbox", "mailbox_ts", "next_mail_pos"):
+            assert torch.equal(getattr(graph.mailbox, name), getattr(static.mailbox, name)), (step, name)
