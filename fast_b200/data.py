@@ -134,4 +134,12 @@ def model_params(cfg):
         memory = dict(type="node", dim_time=100, deliver_to="self", mail_combine="last", memory_update="gru",
                       mailbox_size=1, combine_node_feature=True, dim_out=100)
         train = dict(lr=0.0001, dropout=0.2, att_dropout=0.2)
+    elif cfg.model.startswith("APAN"):
+        # config/APAN-1.yml: sampling without negatives, transformer memory, identity GNN
+        sample["no_neg"] = True
+        memory = dict(type="node", dim_time=100, deliver_to="neighbors", mail_combine="last",
+                      memory_update="transformer", attention_head=2, mailbox_size=10, combine_node_feature=False,
+                      dim_out=100)
+        gnn = dict(arch="identity")
+        train = dict(lr=0.0001, dropout=0.1, att_dropout=0.1)
     return sample, memory, gnn, train
