@@ -47,7 +47,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=5)
     ap.add_argument("--eager", action="store_true", help="launch kernels step by step instead of a CUDA graph")
-    ap.add_argument("--suite", default=None, choices=["kernels"],
+    ap.add_argument("--edges", type=int, default=None,
+                    help="prefix subsample: the first N edges of the config's synthetic graph")
+    ap.add_argument("--suite", default=None, choices=["kernels", "bf16"],
                     help="kernels: time each hot kernel alone at config-5 block sizes against the HBM roofline "
                          "(one JSON line per kernel instead of the training-step line)")
     ap.add_argument("--suite-scale", type=float, default=1.0,
@@ -290,19 +292,25 @@ def run_fast(args):
         import datetime
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     from fast_b200 import ops
-    from fast_b200.data import CONFIGS, make_features, make_graph, model_params
+    from fast_b200.data import CONFIGS, make_features, make_features_bf16, model_params
     ops.USE_TC = args.gemm == "tc"
     from fast_b200.train import GraphTrainer, Trainer
     cfg = CONFIGS[args.config]
     graph, cfg = workload_graph(args, cfg)
-    nf, ef = make_features(cfg, cfg.edges, dev)
+    bf16 = cfg.dtype == "bf16"
+    if bf16:
+        # bf16 tables, rows padded to 8 columns, generated on the device
+        nf, ef = make_features_bf16(cfg, cfg.edges, dev)
+    else:
+        nf, ef = make_features(cfg, cfg.edges, dev)
     sp, mp, gp, tp = model_params(cfg)
     fused = args.path == "fused"
+    prec = dict(precision="bf16", feat_dims=(cfg.d_node, cfg.d_edge)) if bf16 else {}
     if args.eager:
-        tr = Trainer(graph, nf, ef, sp, mp, gp, tp, dev, rank=rank, world=world, fused=fused)
+        tr = Trainer(graph, nf, ef, sp, mp, gp, tp, dev, rank=rank, world=world, fused=fused, **prec)
     else:
         tr = GraphTrainer(graph, nf, ef, sp, mp, gp, tp, dev, batch=cfg.batch, rank=rank, world=world,
-                          fused=fused)
+                          fused=fused, **prec)
     B = cfg.batch
     gB = B * world
     n_batches = graph.train_end // gB
@@ -438,14 +446,17 @@ def run_fast(args):
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": data_label(args, cfg),
+        "vs_baseline": None, "dtype": "bf16" if bf16 else "f32", "data": data_label(args, cfg),
         "config": {"workload": cfg.name, "global_batch": gB, "local_batch": B, "fanout": list(cfg.fanout),
                    "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge,
                    "parallelism": "dp%d" % world, "launch": "eager" if args.eager else "cuda_graph",
                    "batches": SCHEDULE_NOTE,
                    "gemm": args.gemm, "step": args.path,
                    "l2": "inputs larger than L2 (%.1f GB edge-feature table gathered at random rows)" %
-                         (cfg.edges * cfg.d_edge * 4 / 1e9)},
+                         (cfg.edges * ((cfg.d_edge + 7) // 8 * 16 if bf16 else cfg.d_edge * 4) / 1e9),
+                   "precision": ("bf16 projections (w_q, w_k, w_v, w_out and their gradient products on bf16 "
+                                 "operands, fp32 accumulation); attention, softmax, LayerNorm, loss and Adam "
+                                 "in fp32" if bf16 else "fp32")},
         "e2e": {"value": e2e_value, "unit": UNIT,
                 "h2d_bytes_per_step": world * 3 * B * 8 + (world * world * 3 * B * 8 if world > 1 else 0),
                 "d2h_bytes_per_step": world * 4},
@@ -455,7 +466,7 @@ def run_fast(args):
         "clocks": clocks,
         "last_loss": float(loss),
     }
-    if world == 1 and not args.no_cpu_baseline and getattr(tr, "mailbox", None) is None:
+    if world == 1 and not args.no_cpu_baseline and getattr(tr, "mailbox", None) is None and not bf16:
         line["cpu_baseline"] = cpu_baseline(cfg, warm, timed, args.cpu_seconds, args.data)
     print(json.dumps(line), flush=True)
     if world > 1:
@@ -593,9 +604,97 @@ def run_kernel_suite(args):
     return 0
 
 
+def run_bf16_suite(args):
+    """The bf16 precision mode's kernels alone at config 5's hop-2 sizes (132 k
+    destinations x fan-out 10 = 1.32 M edges; node features 413-d from a
+    16,700-row table, edge features 186-d from a 4 M-row table, both bf16 with
+    rows padded to 8 columns; 100-d time encoding; D = 100).  The K|V
+    projection rows are [h (416) | f (192) | cos (100)] = 708 bf16 columns."""
+    import torch
+    from fast_b200 import ops
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    pk = peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    Nd, fan, D, dn, de, dt_ = int(132_000 * args.suite_scale), 10, 100, 413, 186, 100
+    E = Nd * fan
+    rows_tab = int(4_000_000 * args.suite_scale)
+    ntab = torch.zeros(16_700, ops.pad8(dn), device=dev, dtype=torch.bfloat16)
+    ntab[:, :dn] = torch.randn(16_700, dn, device=dev, generator=g)
+    etab = torch.zeros(rows_tab, ops.pad8(de), device=dev, dtype=torch.bfloat16)
+    etab[:, :de] = torch.randn(rows_tab, de, device=dev, generator=g)
+    nid = torch.randint(0, 16_700, (E,), device=dev, generator=g, dtype=torch.int32)
+    eid = torch.randint(0, rows_tab, (E,), device=dev, generator=g, dtype=torch.int32)
+    dts = torch.rand(E, device=dev, generator=g) * 1e5
+    w = (1.0 / 10 ** torch.linspace(0, 9, dt_, device=dev)).contiguous()
+    b = torch.zeros(dt_, device=dev)
+    (h_at, f_at, t_at), K = ops.bf16_layout(dn, de, dt_)
+    X = torch.empty(E, ops.pad8(K), device=dev, dtype=torch.bfloat16)
+    out = []
+
+    def timed(name, nbytes, flops, fn, shape):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(10):
+            fn()
+        s1.record()
+        torch.cuda.synchronize()
+        us = s0.elapsed_time(s1) * 100.0
+        line = {"suite": "bf16", "kernel": name, "shape": shape, "us_per_launch": round(us, 2),
+                "bytes_per_launch": int(nbytes)}
+        gbs = nbytes / us / 1e3
+        line.update({"achieved_GB_s": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm"], 3)})
+        if flops:
+            tfs = flops / us / 1e6
+            line.update({"TFLOP_s": round(tfs, 2), "peak_TFLOP_s": pk["tf"], "tensor_frac": round(tfs / pk["tf"], 4)})
+        line["peak_source"] = "%s (copy bandwidth, bf16 dense burst)" % pk["src"]
+        out.append(line)
+        print(json.dumps(line), flush=True)
+
+    timed("k_gather_time_encode_bf16", E * (2 * K + 2 * 416 + 2 * 192 + 12), 0,
+          lambda: ops.gather_time_encode_bf16(E, h=ntab, h_idx=nid, f=etab, f_idx=eid, dt=dts, w=w, b=b, out=X,
+                                              dn=dn, de=de),
+          "E=%d rows of [h(%d) | f(%d) | cos(%d)] bf16" % (E, dn, de, dt_))
+    Wb = torch.zeros(2 * D, ops.pad8(K), device=dev, dtype=torch.bfloat16)
+    Wb[:, :K] = torch.randn(2 * D, K, device=dev, generator=g) * 0.05
+    bkv = torch.zeros(2 * D, device=dev)
+    KV = torch.empty(E, 2 * D, device=dev)
+    timed("k_bf_group (K|V projection, NT)", E * (2 * K + 4 * 2 * D), 2 * E * 2 * D * K,
+          lambda: ops.gemm_bf16_group([dict(kind=ops.NT, A=X[:, :K], B=Wb[:, :K], bias=bkv, out=KV)]),
+          "M=%d, N=%d, K=%d" % (E, 2 * D, K))
+    dkv = (torch.randn(E, 2 * D, device=dev, generator=g)).to(torch.bfloat16)
+    gW = torch.zeros(2 * D, dn + de + dt_, device=dev)
+    gb = torch.zeros(2 * D, device=dev)
+    tn = [dict(kind=ops.TN, A=dkv, B=X[:, h_at:h_at + dn], out=gW[:, :dn], accumulate=True),
+          dict(kind=ops.TN, A=dkv, B=X[:, f_at:f_at + de], out=gW[:, dn:dn + de], accumulate=True),
+          dict(kind=ops.TN, A=dkv, B=X[:, t_at:t_at + dt_], out=gW[:, dn + de:], accumulate=True, db=gb)]
+    timed("k_bf_group (K|V weight + bias gradient, TN x3)", E * (2 * K + 2 * 2 * D), 2 * E * 2 * D * (K + 1),
+          lambda: ops.gemm_bf16_group(tn), "M=%d, N=%d, K=%d+%d+%d+1" % (E, 2 * D, dn, de, dt_))
+    dAt = torch.empty(E, dt_, device=dev)
+    timed("k_bf_group (time-encoding input gradient, NN)", E * (2 * 2 * D + 4 * dt_), 2 * E * dt_ * 2 * D,
+          lambda: ops.gemm_bf16_group([dict(kind=ops.NN, A=dkv, B=Wb[:, t_at:t_at + dt_], out=dAt)]),
+          "M=%d, N=%d, K=%d" % (E, dt_, 2 * D))
+    q = torch.randn(Nd, D, device=dev, generator=g) * 0.5
+    kvf = torch.randn(E, 2 * D, device=dev, generator=g) * 0.5
+    rptr = torch.arange(0, E + 1, fan, device=dev, dtype=torch.int32)
+    agg, att = ops.attn_fwd(q, kvf[:, :D], kvf[:, D:], rptr, 2, 0.2, 0.1, 1, 2)
+    dagg = torch.randn(Nd, D, device=dev, generator=g)
+    timed("k_attn_bwd (bulk-copy path, bf16 dK|dV)",
+          4 * (2 * Nd * D + 2 * E * D + E * 2 + (Nd + 1) + Nd * D) + 2 * 2 * E * D, 0,
+          lambda: ops.attn_bwd_bf16kv(q, kvf[:, :D], kvf[:, D:], rptr, att, dagg, 2, 0.2, 0.1, 1, 2),
+          "Nd=%d, E=%d, D=%d, H=2, dropout 0.1" % (Nd, E, D))
+    return 0
+
+
 def data_label(args, cfg):
     if args.data:
         return "dataset %s read from edges.csv + ext_full.npz; seeded random features" % cfg.name
+    if args.edges:
+        return "synthetic (seeded, %s shapes; prefix subsample: first %d edges)" % (cfg.name, cfg.edges)
     return "synthetic (seeded, %s shapes)" % cfg.name
 
 
@@ -603,9 +702,15 @@ def workload_graph(args, cfg):
     """The config's synthetic graph, or the dataset of --data (the config then
     takes that graph's node and edge counts)."""
     import dataclasses
-    from fast_b200.data import make_graph
+    from fast_b200.data import make_graph, make_graph_device
     if not args.data:
-        return make_graph(cfg), cfg
+        n = args.edges or cfg.edges
+        cfg = dataclasses.replace(cfg, edges=n)
+        if cfg.dtype == "bf16":
+            # built on the device (config 5: 191 M edges in seconds, not minutes)
+            import torch
+            return make_graph_device(cfg, torch.device("cuda", torch.cuda.current_device())), cfg
+        return make_graph(cfg, n_edges=n), cfg
     from fast_b200.dataio import load_graph
     g = load_graph(args.data)
     return g, dataclasses.replace(cfg, name=os.path.basename(os.path.normpath(args.data)), nodes=g.n_nodes,
@@ -620,6 +725,8 @@ def main():
         os.environ["FB_GEMM"] = "ffma"          # read by fb_gemm_group at every call
     if args.suite == "kernels":
         return run_kernel_suite(args)
+    if args.suite == "bf16":
+        return run_bf16_suite(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_fast(args)

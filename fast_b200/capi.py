@@ -97,6 +97,10 @@ _SIGS = {
     "fb_add_layernorm_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64, _P, _I, _P, _P]),
     "fb_mailbox_update_neighbors": (_I, [_P, _P, _P, _I64, _P, _I64, _P, _I64, _I, _P, _I64, _I, _P, _P, _P, _P, _I,
                                          _P, _P, _P, _P]),
+    "fb_gather_time_encode_bf16": (_I, [_P, _I, _I64, _P, _I64, _P, _I, _P, _I, _I64, _P, _I, _P, _P, _P, _I, _P,
+                                        _I64, _I64, _P, _P]),
+    "fb_attn_bwd_bf16kv": (_I, [_P, _I64, _P, _P, _I64, _P, _I64, _P, _I, _I, _F, _F, _U64, _U64, _P, _P, _P, _I64,
+                                _P, _P, _P, _I64, _P]),
 }
 
 class GemmProblem(ctypes.Structure):
@@ -115,6 +119,28 @@ class GemmProblem(ctypes.Structure):
 
 _SIGS["fb_gemm_group_ws_bytes"] = (_SZ, [ctypes.POINTER(GemmProblem), _I])
 _SIGS["fb_gemm_group"] = (_I, [ctypes.POINTER(GemmProblem), _I, _P, _SZ, _P])
+
+
+class GemmBf16Problem(ctypes.Structure):
+    """fb_gemm_bf16_problem (include/fast_b200.h): fb_gemm_problem's fields
+    (operand pointers to bf16) plus ka."""
+    _fields_ = GemmProblem._fields_ + [("ka", ctypes.c_int)]
+
+
+_SIGS["fb_gemm_bf16_group_ws_bytes"] = (_SZ, [ctypes.POINTER(GemmBf16Problem), _I])
+_SIGS["fb_gemm_bf16_group"] = (_I, [ctypes.POINTER(GemmBf16Problem), _I, _P, _SZ, _P])
+
+
+class CastJob(ctypes.Structure):
+    """fb_cast_job (include/fast_b200.h)."""
+    _fields_ = [("src", ctypes.c_void_p), ("lds", ctypes.c_int64), ("dst", ctypes.c_void_p), ("ldd", ctypes.c_int64),
+                ("rows", ctypes.c_int64), ("rows_dev", ctypes.c_void_p), ("cols", ctypes.c_int),
+                ("pad_", ctypes.c_int)]
+
+
+CAST_MAX_JOBS = 32
+_SIGS["fb_cast_bf16"] = (_I, [ctypes.POINTER(CastJob), _I, _P])
+_SIGS["fb_fill_normal_bf16"] = (_I, [_P, _I64, _I, _I64, _U64, _P])
 
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(lib, _name)

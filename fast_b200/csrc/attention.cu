@@ -16,6 +16,7 @@
 // results are bit-identical run to run.
 #include <cfloat>
 #include <cstdlib>
+#include <cuda_bf16.h>
 #include "runtime.cuh"
 
 namespace {
@@ -64,6 +65,28 @@ __device__ __forceinline__ void store_row(float *__restrict__ p, const RowGeom &
   for (int t = 0; t < NV; ++t) {
     int v = lane + 32 * t;
     if (v < g.nv4) reinterpret_cast<float4 *>(p)[v] = r[t];
+  }
+}
+
+// Four consecutive gradient values at element offset off of p: fp32, or
+// bf16 when bf (p then holds bf16 bit patterns).
+__device__ __forceinline__ void put4(float *p, int64_t off, float4 v, int bf) {
+  if (bf) {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+    *reinterpret_cast<uint2 *>(reinterpret_cast<uint16_t *>(p) + off) =
+        make_uint2(*reinterpret_cast<const uint32_t *>(&lo), *reinterpret_cast<const uint32_t *>(&hi));
+  } else {
+    *reinterpret_cast<float4 *>(p + off) = v;
+  }
+}
+
+template <int NV>
+__device__ __forceinline__ void store_grad_row(float *__restrict__ p, int64_t row_off, const RowGeom &g, int lane,
+                                               const float4 r[NV], int bf) {
+#pragma unroll
+  for (int t = 0; t < NV; ++t) {
+    int v = lane + 32 * t;
+    if (v < g.nv4) put4(p, row_off + 4 * v, r[t], bf);
   }
 }
 
@@ -140,6 +163,7 @@ struct AttnArgs {
   float *dx;               // optional gradient of the pre-activation logits
   const float *dagg; int64_t lddagg;
   float *dq, *dk, *dv; int64_t lddkv;
+  int kv_bf16;             // dk / dv are bf16 (bit patterns, round to nearest even)
 };
 
 // Output (or incoming gradient) row of segment j: j itself, or the row named
@@ -327,7 +351,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta, MinCtas<NV>::value) k_attn_
               o[t].z = pick(y, hsel[t][2]) * pick(ds, hsel[t][2]) * da[t].z;
               o[t].w = pick(y, hsel[t][3]) * pick(ds, hsel[t][3]) * da[t].w;
             }
-            store_row<NV>(a.dv + (int64_t)e * a.lddkv, g, lane, o);
+            store_grad_row<NV>(a.dv, (int64_t)e * a.lddkv, g, lane, o, a.kv_bf16);
           }
         }
       }
@@ -384,7 +408,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta, MinCtas<NV>::value) k_attn_
                 o[t].z = pick(dz, hsel[t][2]) * q[t].z;
                 o[t].w = pick(dz, hsel[t][3]) * q[t].w;
               }
-              store_row<NV>(a.dk + (int64_t)e * a.lddkv, g, lane, o);
+              store_grad_row<NV>(a.dk, (int64_t)e * a.lddkv, g, lane, o, a.kv_bf16);
             }
 #pragma unroll
             for (int t = 0; t < NV; ++t) {
@@ -622,8 +646,8 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta, 4) k_attn_bwd_s(AttnArgs a)
             for (int h = 0; h < HP; ++h) yc[h] = __shfl_sync(0xffffffffu, yk[h], c);
             const float ya = hv<HP>(yc, hA), yb = hv<HP>(yc, hB);
             if (live)
-              reinterpret_cast<float4 *>(a.dv + (int64_t)(g0 + c) * a.lddkv)[lane] =
-                  make_float4(ya * da4.x, ya * da4.y, yb * da4.z, yb * da4.w);
+              put4(a.dv, (int64_t)(g0 + c) * a.lddkv + 4 * lane,
+                   make_float4(ya * da4.x, ya * da4.y, yb * da4.z, yb * da4.w), a.kv_bf16);
           }
         }
       }
@@ -664,8 +688,8 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta, 4) k_attn_bwd_s(AttnArgs a)
           if (live) {
             const float4 k = __ldg(reinterpret_cast<const float4 *>(a.k + (int64_t)(g0 + c) * a.ldkv) + lane);
             if (a.dk)
-              reinterpret_cast<float4 *>(a.dk + (int64_t)(g0 + c) * a.lddkv)[lane] =
-                  make_float4(za * q4.x, za * q4.y, zb * q4.z, zb * q4.w);
+              put4(a.dk, (int64_t)(g0 + c) * a.lddkv + 4 * lane,
+                   make_float4(za * q4.x, za * q4.y, zb * q4.z, zb * q4.w), a.kv_bf16);
             dq.x = fmaf(za, k.x, dq.x);
             dq.y = fmaf(za, k.y, dq.y);
             dq.z = fmaf(zb, k.z, dq.z);
@@ -925,8 +949,8 @@ __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_bwd_b(AttnArgs a) {
             for (int h = 0; h < HP; ++h) yc[h] = __shfl_sync(0xffffffffu, yk[h], c);
             const float ya = hv<HP>(yc, hA), yb = hv<HP>(yc, hB);
             if (live)
-              reinterpret_cast<float4 *>(a.dv + (int64_t)(g0 + c) * a.lddkv)[lane] =
-                  make_float4(ya * da4.x, ya * da4.y, yb * da4.z, yb * da4.w);
+              put4(a.dv, (int64_t)(g0 + c) * a.lddkv + 4 * lane,
+                   make_float4(ya * da4.x, ya * da4.y, yb * da4.z, yb * da4.w), a.kv_bf16);
           }
         }
       }
@@ -975,8 +999,8 @@ __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_bwd_b(AttnArgs a) {
           if (live) {
             const float4 k = reinterpret_cast<const float4 *>(slot + c * rowf)[lane];
             if (a.dk)
-              reinterpret_cast<float4 *>(a.dk + (int64_t)(g0 + c) * a.lddkv)[lane] =
-                  make_float4(za * q4.x, za * q4.y, zb * q4.z, zb * q4.w);
+              put4(a.dk, (int64_t)(g0 + c) * a.lddkv + 4 * lane,
+                   make_float4(za * q4.x, za * q4.y, zb * q4.z, zb * q4.w), a.kv_bf16);
             dq.x = fmaf(za, k.x, dq.x);
             dq.y = fmaf(za, k.y, dq.y);
             dq.z = fmaf(zb, k.z, dq.z);
@@ -1184,6 +1208,24 @@ extern "C" int fb_attn_bwd(const float *q, int64_t ldq, const float *k, const fl
   a.q = q; a.ldq = ldq; a.k = k; a.v = v; a.ldkv = ldkv; a.rptr = rptr; a.n_dst = n_dst; a.n_dst_dev = n_dst_dev;
   a.heads = heads; a.dim = dim; a.slope = slope; a.drop_p = drop_p; a.seed = seed; a.offset = offset;
   a.att = att; a.dagg = dagg; a.lddagg = lddagg; a.dq = dq; a.dk = dk; a.dv = dv; a.lddkv = lddkv;
+  return launch_bwd(a, stream);
+}
+
+// fb_attn_bwd with dk / dv written as bf16 (round to nearest even): the K|V
+// gradient that feeds the bf16 projection GEMMs.  lddkv % 4 == 0.
+extern "C" int fb_attn_bwd_bf16kv(const float *q, int64_t ldq, const float *k, const float *v, int64_t ldkv,
+                                  const int32_t *rptr, int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim,
+                                  float slope, float drop_p, uint64_t seed, uint64_t offset,
+                                  const uint64_t *offset_dev, const float *att, const float *dagg, int64_t lddagg,
+                                  float *dq, uint16_t *dk, uint16_t *dv, int64_t lddkv, cudaStream_t stream) {
+  AttnArgs a{};
+  a.offset_dev = offset_dev;
+  a.q = q; a.ldq = ldq; a.k = k; a.v = v; a.ldkv = ldkv; a.rptr = rptr; a.n_dst = n_dst; a.n_dst_dev = n_dst_dev;
+  a.heads = heads; a.dim = dim; a.slope = slope; a.drop_p = drop_p; a.seed = seed; a.offset = offset;
+  a.att = att; a.dagg = dagg; a.lddagg = lddagg; a.dq = dq; a.lddkv = lddkv;
+  a.dk = reinterpret_cast<float *>(dk);
+  a.dv = reinterpret_cast<float *>(dv);
+  a.kv_bf16 = 1;
   return launch_bwd(a, stream);
 }
 

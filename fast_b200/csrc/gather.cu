@@ -20,6 +20,7 @@
 // evaluates the Taylor series of sin and cos on |r| <= pi/4 in fp32 (degrees
 // 9 and 10: truncation below 2e-9).  The forward keeps cosf, which measured
 // faster in its wide gather.
+#include <cuda_bf16.h>
 #include "runtime.cuh"
 
 namespace {
@@ -131,6 +132,123 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode(GatherA
       const float t = a.dt ? a.dt[r] : 0.f;
       float *o = out + a.dn + a.de;
       for (int c = lane; c < a.dtime; c += 32) o[c] = cosf(fmaf(t, __ldg(a.w + c), __ldg(a.b + c)));
+    }
+  }
+}
+
+// bf16 projection rows for the bf16 precision mode: [h | f | cos(w dt + b)]
+// with each segment starting at a multiple of 8 columns (16 bytes), so that
+// every segment of the row -- and the matching column block of the bf16
+// weight copy -- is a valid TMA box origin.  bf16 sources (feature tables)
+// are copied as 16-byte words, rows padded with zeros to a multiple of 8
+// columns, so the gap after a segment is copied as zeros; fp32 sources (a
+// layer's output) are rounded to nearest even and the gap is written as
+// zeros.  A warp takes kBatch rows and issues all loads of a segment before
+// its stores, as k_gather_time_encode_batched does.
+struct GatherBfArgs {
+  const void *h; int h_bf; int64_t ldh; const int32_t *h_idx; int64_t h_off; const int32_t *h_off_dev; int dn;
+  const void *f; int f_bf; int64_t ldf; const int32_t *f_idx; int de;
+  const float *dt, *w, *b; int dtime;
+  uint16_t *A; int64_t lda; int f_at, t_at; int64_t n_rows; const int32_t *n_rows_dev;
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float x, float y) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(x, y);
+  return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+// One source segment of kBatch rows into the bf16 row block at out0.
+__device__ __forceinline__ void gather_seg_bf16(const void *src, int is_bf, int64_t ld, const int64_t (&row)[kBatch],
+                                                int nb, int d, uint16_t *__restrict__ out0, int64_t lda, int lane) {
+  if (is_bf) {
+    const int nq = (d + 7) >> 3;             // 16-byte words of the zero-padded row
+    uint4 v[kBatch][kMaxChunks];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i)
+#pragma unroll
+      for (int c = 0; c < kMaxChunks; ++c) {
+        const int q = lane + 32 * c;
+        v[i][c] = (i < nb && q < nq)
+                      ? __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(src) + row[i] * ld) + q)
+                      : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i)
+#pragma unroll
+      for (int c = 0; c < kMaxChunks; ++c) {
+        const int q = lane + 32 * c;
+        if (i < nb && q < nq) reinterpret_cast<uint4 *>(out0 + i * lda)[q] = v[i][c];
+      }
+  } else {
+    const int nq = d >> 2;                   // float4 words (d % 4 == 0)
+    float4 v[kBatch][kMaxChunks];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i)
+#pragma unroll
+      for (int c = 0; c < kMaxChunks; ++c) {
+        const int q = lane + 32 * c;
+        v[i][c] = (i < nb && q < nq)
+                      ? __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(src) + row[i] * ld) + q)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+#pragma unroll
+      for (int c = 0; c < kMaxChunks; ++c) {
+        const int q = lane + 32 * c;
+        if (i < nb && q < nq)
+          reinterpret_cast<uint2 *>(out0 + i * lda)[q] =
+              make_uint2(pack_bf16x2(v[i][c].x, v[i][c].y), pack_bf16x2(v[i][c].z, v[i][c].w));
+      }
+      if (i < nb && lane == 0 && (d & 7)) reinterpret_cast<uint2 *>(out0 + i * lda)[nq] = make_uint2(0u, 0u);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode_bf16(GatherBfArgs a) {
+  fb::pdl_enter();
+  const int lane = threadIdx.x & 31;
+  const int64_t n = a.n_rows_dev ? min((int64_t)(*a.n_rows_dev), a.n_rows) : a.n_rows;
+  const int64_t h_off = a.h_off + (a.h_off_dev ? (int64_t)(*a.h_off_dev) : 0);
+  const int64_t step = (int64_t)gridDim.x * kRowsPerCta * kBatch;
+  for (int64_t r0 = ((int64_t)blockIdx.x * kRowsPerCta + (threadIdx.x >> 5)) * kBatch; r0 < n; r0 += step) {
+    const int nb = (int)min((int64_t)kBatch, n - r0);
+    int64_t hid = 0, fid = 0;
+    float tt = 0.f;
+    if (lane < nb) {
+      const int64_t r = r0 + lane;
+      hid = a.h_idx ? (int64_t)a.h_idx[r] : r + h_off;
+      fid = a.f_idx ? (int64_t)a.f_idx[r] : r;
+      tt = a.dt ? a.dt[r] : 0.f;
+    }
+    int64_t hr[kBatch], fr[kBatch];
+    float t[kBatch];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      hr[i] = __shfl_sync(0xffffffffu, hid, i);
+      fr[i] = __shfl_sync(0xffffffffu, fid, i);
+      t[i] = __shfl_sync(0xffffffffu, tt, i);
+    }
+    uint16_t *out0 = a.A + r0 * a.lda;
+    if (a.dn > 0) gather_seg_bf16(a.h, a.h_bf, a.ldh, hr, nb, a.dn, out0, a.lda, lane);
+    if (a.de > 0) gather_seg_bf16(a.f, a.f_bf, a.ldf, fr, nb, a.de, out0 + a.f_at, a.lda, lane);
+    if (a.dtime > 0) {
+      for (int c = 2 * lane; c < a.dtime; c += 64) {
+        const bool two = c + 1 < a.dtime;
+        const float w0 = __ldg(a.w + c), b0 = __ldg(a.b + c);
+        const float w1 = two ? __ldg(a.w + c + 1) : 0.f, b1 = two ? __ldg(a.b + c + 1) : 0.f;
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+          if (i >= nb) continue;
+          const float x0 = cosf(fmaf(t[i], w0, b0));
+          uint16_t *o = out0 + i * a.lda + a.t_at + c;
+          if (two) {
+            *reinterpret_cast<uint32_t *>(o) = pack_bf16x2(x0, cosf(fmaf(t[i], w1, b1)));
+          } else {
+            *o = (uint16_t)(pack_bf16x2(x0, 0.f) & 0xFFFFu);
+          }
+        }
+      }
     }
   }
 }
@@ -280,6 +398,30 @@ extern "C" int fb_gather_time_encode(const float *h, int64_t ldh, const int32_t 
     FB_TRY_CUDA(fb::launch(k_gather_time_encode<false>, grid, 32 * kRowsPerCta, 0, stream, a));
   }
   FB_LAUNCHED("k_gather_time_encode");
+  return FB_OK;
+}
+
+extern "C" int fb_gather_time_encode_bf16(const void *h, int h_bf16, int64_t ldh, const int32_t *h_idx, int64_t h_off,
+                                          const int32_t *h_off_dev, int dn, const void *f, int f_bf16, int64_t ldf,
+                                          const int32_t *f_idx, int de, const float *dt, const float *w,
+                                          const float *b, int dtime, uint16_t *A, int64_t lda, int64_t n_rows,
+                                          const int32_t *n_rows_dev, cudaStream_t stream) {
+  const int f_at = (dn + 7) / 8 * 8, t_at = f_at + (de + 7) / 8 * 8;
+  const auto src_ok = [](const void *p, int bf, int64_t ld, int d) {
+    return bf ? (a16(p) && ld % 8 == 0 && ld >= (d + 7) / 8 * 8) : (a16(p) && ld % 4 == 0 && d % 4 == 0 && ld >= d);
+  };
+  if (!A || !a16(A) || lda % 8 || n_rows < 0 || dn < 0 || de < 0 || dtime < 0 || lda < t_at + dtime ||
+      (dn > 0 && (!h || !src_ok(h, h_bf16, ldh, dn))) || (de > 0 && (!f || !src_ok(f, f_bf16, ldf, de))) ||
+      (dtime > 0 && (!w || !b)) || dn > 8 * 32 * kMaxChunks || de > 8 * 32 * kMaxChunks ||
+      (!h_bf16 && dn > 4 * 32 * kMaxChunks) || (!f_bf16 && de > 4 * 32 * kMaxChunks))
+    return fb::set_error(FB_ERR_ARG, "gather_time_encode_bf16: bad argument (alignment, widths or pitch)");
+  if (n_rows == 0) return FB_OK;
+  GatherBfArgs a{h, h_bf16, ldh, h_idx, h_off, h_off_dev, dn, f, f_bf16, ldf, f_idx, de, dt, w, b, dtime,
+                 A, lda, f_at, t_at, n_rows, n_rows_dev};
+  const int64_t need = (n_rows + kRowsPerCta * kBatch - 1) / (kRowsPerCta * kBatch);
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, 148 * 16));
+  FB_TRY_CUDA(fb::launch(k_gather_time_encode_bf16, grid, 32 * kRowsPerCta, 0, stream, a));
+  FB_LAUNCHED("k_gather_time_encode_bf16");
   return FB_OK;
 }
 

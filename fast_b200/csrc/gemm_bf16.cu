@@ -1,0 +1,621 @@
+// bf16 projection GEMMs on the tcgen05 tensor cores: kind::f16 MMAs with
+// bf16 operands and fp32 accumulation in tensor memory, grouped like the
+// fp32 ones of gemm_tc.cu (independent NT / NN / TN problems of one
+// dependency level share one persistent launch).
+//
+//   NT: C[m, n] (+)= sum_k A[m, k] B[n, k] + bias[n]     A, B K-major
+//   NN: C[m, n] (+)= sum_k A[m, k] B[k, n] + bias[n]     A K-major, B MN-major
+//   TN: P[s][n, k] = sum_{m in split s} G[m, n] X[m, k]  G, X MN-major; a
+//       ones column of X at k = K gives the bias gradient; k_bf_reduce sums
+//       the splits in a fixed order into C (+ C) and db (+ db)
+//   NT / NN may take A as [A | A2] concatenated along K (k1 % 8 == 0).
+//
+// Operands are bf16 in global memory and reach the tensor cores untouched:
+// TMA moves 64-element (128-byte) rows with the 128-byte swizzle, K-major
+// tiles as [rows][64 k] boxes and MN-major tiles as [64 k][64 mn] boxes side
+// by side, and the MMA reads them through K-major or MN-major descriptors.
+// There is no conversion pass, so a slice costs one TMA write and one MMA
+// read of shared memory.  A tile accumulates its whole reduction range in
+// one of two TMEM accumulators (up to 256 columns each) while the epilogue
+// drains the other.
+//
+// CTA = 12 warps:
+//   warp 0      TMA producer
+//   warp 1      TMEM allocator; the MMA issuer (one elected lane); for TN
+//               slices it clears the rows outside the split (rows past the
+//               device-side count hold stale data) and writes the ones column
+//   warps 4..11 epilogue: two warps per TMEM lane quadrant, alternate
+//               32-column blocks, rows staged through shared memory so each
+//               store instruction writes 32 consecutive columns of one row
+// Every wait is bounded: past the limit the CTA records an error, stops
+// issuing work, drains what it already issued (again bounded), frees its
+// tensor memory and exits.
+#include <cuda.h>
+#include <algorithm>
+#include <cstring>
+#include <vector>
+#include "runtime.cuh"
+#include "tc_common.cuh"
+
+namespace {
+
+using namespace fbtc;
+
+constexpr int BM = 128;                      // MMA M = TMEM lanes
+constexpr int BK = 64;                       // reduction slice: 64 bf16 = one 128-byte swizzle row
+constexpr int kStages = 4;
+constexpr int kMaxBn = 256;
+constexpr int kMaxBf = 7;                    // problems per launch (parameters under 4 KB)
+constexpr int kAOp = BM * BK * 2;            // 16 KB
+constexpr int kBOp = kMaxBn * BK * 2;        // 32 KB
+constexpr int kStage = kAOp + kBOp;
+constexpr int kBox = BK * 128;               // one MN-major box: BK rows of 64 elements
+constexpr int kEpiWarps = 8;
+constexpr int kStagePitch = 33;              // epilogue staging rows (floats; odd: no bank conflicts)
+constexpr int kStageWarp = 32 * kStagePitch * 4;
+constexpr int kBarBytes = 256;
+constexpr int kSmem = 1024 + kStages * kStage + kBarBytes + kEpiWarps * kStageWarp;
+static_assert(kSmem <= 232448, "shared memory of k_bf_group exceeds 227 KB");
+constexpr int kTmemCols = 512;               // two accumulators of up to 256 columns
+constexpr int kAccStride = 256;
+constexpr int64_t kTnRowsMin = 512;          // TN: rows per split, at least
+constexpr int kWarpProducer = 0, kWarpMma = 1, kWarpEpi0 = 4;
+constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;
+
+enum : int { kNT = 0, kNN = 1, kTN = 2 };
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor (128-byte swizzle), tile base 1024-byte
+// aligned.  K-major: rows of 128 B (64 k), 8-row groups 1024 B apart (SBO);
+// a K step of 16 advances the start by 32 B.  MN-major: [64 k][64 mn] boxes
+// side by side along MN (LBO = one box), 8-row k groups 1024 B apart (SBO);
+// a K step of 16 advances the start by 2 KB.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, bool mn) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)(mn ? (kBox >> 4) : 1) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;                    // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                    // SWIZZLE_128B
+  return d;
+}
+
+struct BfProb {
+  CUtensorMap ta, ta2, tb;   // A (TN: G), A2, B (TN: X)
+  int kind, a_mn, b_mn, k1, K, N, Kp, bn, rt, nt, ones, accumulate, db_accumulate, max_splits;
+  uint32_t idesc;
+  int64_t M;
+  const int32_t *M_dev;
+  const float *bias;
+  float *C;
+  int64_t ldc;
+  float *db, *P;
+};
+
+struct BfArgs {
+  BfProb p[kMaxBf];
+  int n;
+  int red_start[kMaxBf + 1];
+  int32_t *err;
+};
+static_assert(sizeof(BfArgs) <= 4096, "kernel parameters of k_bf_group exceed 4 KB");
+
+struct Item {
+  int p, z, nk, nk1, c0;
+  int64_t r0, s0, s1;
+};
+
+__device__ __forceinline__ Item decode(const BfArgs &a, const int *st, const long long *sm, const long long *sper,
+                                       int i) {
+  Item it;
+  int p = 0;
+  while (p + 1 < a.n && i >= st[p + 1]) ++p;
+  const BfProb &q = a.p[p];
+  int l = i - st[p];
+  it.p = p;
+  if (q.kind == kTN) {
+    const int per_z = q.rt * q.nt;
+    it.z = l / per_z;
+    l -= it.z * per_z;
+    it.r0 = (int64_t)(l / q.nt) * BM;
+    it.c0 = (l % q.nt) * q.bn;
+    it.s0 = (int64_t)it.z * sper[p];
+    it.s1 = min((int64_t)sm[p], it.s0 + (int64_t)sper[p]);
+    it.nk1 = 0;
+    it.nk = it.s1 > it.s0 ? (int)((it.s1 - it.s0 + BK - 1) / BK) : 1;   // an empty split writes zeros
+  } else {
+    it.z = 0;
+    it.r0 = (int64_t)(l / q.nt) * BM;
+    it.c0 = (l % q.nt) * q.bn;
+    it.s0 = it.s1 = 0;
+    it.nk1 = (q.k1 + BK - 1) / BK;
+    it.nk = it.nk1 + (q.K - q.k1 + BK - 1) / BK;
+  }
+  return it;
+}
+
+// TN slice fix-up by the MMA warp: rows >= valid of every MN-major box (A's
+// two, B's nbox) are cleared -- they lie past the split or past the
+// device-side row count, where memory may hold anything -- and column
+// `onescol` of B is set to 1 for the rows that count.  In a 128-byte
+// swizzled row, 16-byte chunk c sits at position c ^ (row & 7).
+__device__ __forceinline__ void fix_tn_slice(uint8_t *a, uint8_t *b, int nbox, int valid, int onescol, int lane) {
+  if (valid < BK) {
+    const int per_box = (BK - valid) * 8;    // 16-byte words to clear per box
+    for (int t = lane; t < (2 + nbox) * per_box; t += 32) {
+      const int bx = t / per_box, e = t - bx * per_box;
+      uint8_t *base = bx < 2 ? a + bx * kBox : b + (bx - 2) * kBox;
+      reinterpret_cast<uint4 *>(base + valid * 128)[e] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  if (onescol >= 0) {
+    uint8_t *base = b + (onescol >> 6) * kBox;
+    const int c = onescol & 63;
+    for (int r = lane; r < valid; r += 32)
+      *reinterpret_cast<uint16_t *>(base + r * 128 + (((c >> 3) ^ (r & 7)) << 4) + (c & 7) * 2) = 0x3F80u;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant__ BfArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = align1024(smem_raw);
+  auto sA = [&](int s) { return smem + s * kStage; };
+  auto sB = [&](int s) { return smem + s * kStage + kAOp; };
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStage);
+  uint64_t *full = bars, *empty = bars + kStages;
+  uint64_t *accf = bars + 2 * kStages, *acce = bars + 2 * kStages + 2, *drain = bars + 2 * kStages + 4;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * kStages + 5);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+  int32_t *err = a.err;
+  __shared__ int s_start[kMaxBf + 1];
+  __shared__ long long s_m[kMaxBf], s_per[kMaxBf];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf + b, 1);
+      mbar_init(acce + b, kEpiWarps * 32);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kWarpProducer && lane < a.n) {
+    const BfProb &q = a.p[lane];
+    prefetch_map(&q.ta);
+    if (q.kind != kTN && q.k1 < q.K) prefetch_map(&q.ta2);
+    prefetch_map(&q.tb);
+  }
+  if (warp == kWarpMma) tmem_alloc(tmem_holder, kTmemCols);
+
+  fb::pdl_enter();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int p = 0; p < a.n; ++p) {
+      const BfProb &q = a.p[p];
+      int64_t M = q.M_dev ? min((int64_t)(*q.M_dev), q.M) : q.M;
+      M = max(M, (int64_t)0);
+      s_m[p] = M;
+      s_start[p] = acc;
+      if (q.kind == kTN) {
+        const int ns = fb::tn_parts(M, kTnRowsMin, q.max_splits);
+        s_per[p] = ((M + ns - 1) / ns + BK - 1) / BK * BK;
+        acc += q.rt * q.nt * ns;
+      } else {
+        s_per[p] = 0;
+        acc += (int)((M + BM - 1) / BM) * q.nt;
+      }
+    }
+    s_start[a.n] = acc;
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int total = s_start[a.n];
+  if ((int)blockIdx.x >= total) {
+    if (warp == kWarpMma) tmem_dealloc(tmem, kTmemCols);
+    return;
+  }
+
+  if (warp == kWarpProducer) {
+    if (lane == 0) {
+      uint32_t g = 0;
+      bool stop = false;
+      for (int i = blockIdx.x; i < total && !stop; i += gridDim.x) {
+        const Item it = decode(a, s_start, s_m, s_per, i);
+        const BfProb &q = a.p[it.p];
+        const bool tn = q.kind == kTN, bmn = q.b_mn != 0;
+        const int bn = q.bn, k1 = q.k1, c0 = it.c0;
+        const uint32_t bytes = (uint32_t)(kAOp + bn * BK * 2);
+        const int r0 = (int)it.r0;
+        for (int j = 0; j < it.nk; ++j) {
+          const int s = g % kStages;
+          if (g >= kStages && !mbar_wait(empty + s, ((g / kStages) - 1) & 1, abort_flag, err)) {
+            stop = true;
+            break;
+          }
+          mbar_expect_tx(full + s, bytes);
+          const int kb = j < it.nk1 ? BK * j : k1 + BK * (j - it.nk1);
+          const int my = (int)it.s0 + BK * j;
+          if (tn) {
+            tma_load_2d(sA(s), &q.ta, full + s, r0, my);
+            tma_load_2d(sA(s) + kBox, &q.ta, full + s, r0 + 64, my);
+          } else if (j < it.nk1) {
+            tma_load_2d(sA(s), &q.ta, full + s, BK * j, r0);
+          } else {
+            tma_load_2d(sA(s), &q.ta2, full + s, BK * (j - it.nk1), r0);
+          }
+          if (!bmn) {
+            tma_load_2d(sB(s), &q.tb, full + s, kb, c0);
+          } else {
+            const int y = tn ? my : kb;
+            for (int t = 0; t < bn / 64; ++t) tma_load_2d(sB(s) + t * kBox, &q.tb, full + s, c0 + 64 * t, y);
+          }
+          ++g;
+        }
+      }
+      if (*abort_flag) {
+        // let the copies already issued land before the CTA's memory goes away
+        for (uint32_t h = g > (uint32_t)kStages ? g - kStages : 0; h < g; ++h) mbar_drain(full + h % kStages, (h / kStages) & 1);
+      }
+    }
+  } else if (warp == kWarpMma) {
+    uint32_t g = 0, tc = 0;
+    bool stop = false;
+    for (int i = blockIdx.x; i < total && !stop; i += gridDim.x, ++tc) {
+      const Item it = decode(a, s_start, s_m, s_per, i);
+      const BfProb &q = a.p[it.p];
+      const bool tn = q.kind == kTN, amn = q.a_mn != 0, bmn = q.b_mn != 0;
+      const uint32_t idesc = q.idesc;
+      const int nbox = q.bn / 64;
+      const int onescol = (tn && q.ones && q.K >= it.c0 && q.K < it.c0 + q.bn) ? q.K - it.c0 : -1;
+      const uint64_t adv_a = amn ? (2048 >> 4) : 2, adv_b = bmn ? (2048 >> 4) : 2;   // one K step of 16
+      const int b = tc & 1;
+      if (tc >= 2 && !mbar_wait(acce + b, ((tc >> 1) - 1) & 1, abort_flag, err)) break;
+      const uint32_t d = tmem + (uint32_t)(b * kAccStride);
+      for (int j = 0; j < it.nk; ++j) {
+        const int s = g % kStages;
+        if (!mbar_wait(full + s, (g / kStages) & 1, abort_flag, err)) {
+          stop = true;
+          break;
+        }
+        if (tn) {
+          const int64_t left = it.s1 - (it.s0 + (int64_t)BK * j);
+          const int valid = left <= 0 ? 0 : (left >= BK ? BK : (int)left);
+          if (valid < BK || onescol >= 0) {
+            fix_tn_slice(sA(s), sB(s), nbox, valid, onescol, lane);
+            fence_async_smem();
+          }
+          __syncwarp();
+        }
+        if (lane == 0) {
+          tc_fence_after();
+          const uint64_t ad = sdesc(smem_u32(sA(s)), amn), bd = sdesc(smem_u32(sB(s)), bmn);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_bf16(d, ad + kk * adv_a, bd + kk * adv_b, idesc, (j | kk) != 0 ? 1u : 0u);
+          umma_commit(empty + s);
+          if (j == it.nk - 1) umma_commit(accf + b);
+        }
+        __syncwarp();
+        ++g;
+      }
+    }
+    if (lane == 0) {
+      // every MMA this warp issued must be complete before TMEM is freed
+      umma_commit(drain);
+      mbar_drain(drain, 0);
+    }
+    __syncwarp();
+  } else if (warp >= kWarpEpi0) {
+    const int e = warp - kWarpEpi0;
+    const int qd = warp & 3;                 // TMEM lane quadrant this warp may read
+    const int half = e >> 2;
+    const uint32_t tlane = (uint32_t)(qd * 32) << 16;
+    float *stg = reinterpret_cast<float *>(smem + kStages * kStage + kBarBytes + e * kStageWarp);
+    uint32_t tc = 0;
+    for (int i = blockIdx.x; i < total; i += gridDim.x, ++tc) {
+      const Item it = decode(a, s_start, s_m, s_per, i);
+      const BfProb &q = a.p[it.p];
+      const int b = tc & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(accf + b, (tc >> 1) & 1, abort_flag, err) ? 1 : 0)) break;
+      tc_fence_after();
+      const uint32_t t = tmem + tlane + (uint32_t)(b * kAccStride);
+      // the problem's fields in registers (read through the parameter
+      // pointer they would be reloaded after every store)
+      const int bn = q.bn;
+      const bool tn = q.kind == kTN;
+      const int64_t rows = tn ? (int64_t)q.N : (int64_t)s_m[it.p];
+      const int ncols = tn ? q.Kp : q.N;
+      const int64_t ld = tn ? (int64_t)q.Kp : q.ldc;
+      float *const out = tn ? q.P + (int64_t)it.z * q.N * q.Kp : q.C;
+      const float *const bias = tn ? nullptr : q.bias;
+      const bool accum = !tn && q.accumulate;
+      const int64_t row0 = it.r0 + qd * 32;
+      const int nrows = rows - row0 < 32 ? (int)max(rows - row0, (int64_t)0) : 32;
+#pragma unroll 1
+      for (int c0 = 32 * half; c0 < bn; c0 += 64) {
+        uint32_t r[32];
+        tmem_ld32(t + c0, r);
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 32; ++k) stg[lane * kStagePitch + k] = __uint_as_float(r[k]);
+        __syncwarp();
+        const int col = it.c0 + c0 + lane;
+        if (c0 + lane < bn && col < ncols) {
+          const float bv = bias ? bias[col] : 0.f;
+          float *o = out + row0 * ld + col;
+          const float *sv = stg + lane;
+          if (nrows == 32) {
+            if (accum) {
+#pragma unroll 8
+              for (int rr = 0; rr < 32; ++rr) o[rr * ld] += sv[rr * kStagePitch] + bv;
+            } else {
+#pragma unroll 8
+              for (int rr = 0; rr < 32; ++rr) o[rr * ld] = sv[rr * kStagePitch] + bv;
+            }
+          } else {
+            for (int rr = 0; rr < nrows; ++rr) {
+              const float v = sv[rr * kStagePitch] + bv;
+              o[rr * ld] = accum ? o[rr * ld] + v : v;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acce + b);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kWarpMma) tmem_dealloc(tmem, kTmemCols);
+}
+
+// Sums the TN partials of every TN problem of the launch (fixed split order)
+// into C (+ C) and, for the ones column, db (+ db).
+__global__ void k_bf_reduce(const __grid_constant__ BfArgs a) {
+  fb::pdl_enter();
+  int p = -1;
+  for (int i = 0; i < a.n; ++i)
+    if (a.p[i].kind == kTN && (int)blockIdx.x >= a.red_start[i] && (int)blockIdx.x < a.red_start[i + 1]) p = i;
+  if (p < 0) return;
+  const BfProb &q = a.p[p];
+  const int64_t i = (int64_t)(blockIdx.x - a.red_start[p]) * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)q.N * q.Kp) return;
+  int64_t M = q.M_dev ? min((int64_t)(*q.M_dev), q.M) : q.M;
+  M = max(M, (int64_t)0);
+  const int ns = fb::tn_parts(M, kTnRowsMin, q.max_splits);
+  const int n = (int)(i / q.Kp), k = (int)(i % q.Kp);
+  const int64_t stride = (int64_t)q.N * q.Kp;
+  const float *part = q.P + i;
+  float s = 0.f;
+  int z = 0;
+  for (; z + 8 <= ns; z += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = part[(int64_t)(z + u) * stride];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) s += v[u];
+  }
+  for (; z < ns; ++z) s += part[(int64_t)z * stride];
+  float *c = (k < q.K) ? q.C + (int64_t)n * q.ldc + k : q.db + n;
+  const int acc = (k < q.K) ? q.accumulate : q.db_accumulate;
+  *c = acc ? (*c + s) : s;
+}
+
+// Row-major bf16 [rows, cols] with leading dimension ld (elements), boxes of
+// 64 columns x box_rows rows, 128-byte swizzle; reads past the extents
+// return zeros.
+int make_map(CUtensorMap *m, const uint16_t *base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fb::set_error(FB_ERR_CUDA, "gemm_bf16: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fb::set_error(FB_ERR_ARG, "gemm_bf16: tensor map rejected (alignment or stride)");
+  return FB_OK;
+}
+
+inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Tile width along the MMA N dimension.  K-major B: a multiple of 16 up to
+// 256, as even as the tiles allow.  MN-major B: whole 64-column boxes, the
+// width that wastes the fewest columns counting a per-tile cost.
+int bn_kmajor(int N) {
+  const int t = (N + kMaxBn - 1) / kMaxBn, w = (N + t - 1) / t;
+  return (w + 15) / 16 * 16;
+}
+int bn_mnmajor(int N) {
+  int best = 256, cost = (N + 255) / 256 * (256 + 32);
+  for (int w : {192, 128, 64}) {
+    const int c = (N + w - 1) / w * (w + 32);
+    if (c < cost) cost = c, best = w;
+  }
+  return best;
+}
+
+uint32_t idesc_bf16(int bn, int a_mn, int b_mn) {
+  // D fp32, A and B bf16, dense; N >> 3 at bit 17, M >> 4 at bit 24
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+int tn_splits_max(const fb_gemm_bf16_problem &p) {
+  const int Kp = p.K + (p.db ? 1 : 0);
+  const int tiles = ((p.N + BM - 1) / BM) * ((Kp + bn_mnmajor(Kp) - 1) / bn_mnmajor(Kp));
+  return std::max(1, num_sms() / std::max(tiles, 1));
+}
+
+int64_t slices_per_item(const fb_gemm_bf16_problem &p) {
+  if (p.kind == FB_GEMM_TN) {
+    const int ns = fb::tn_parts(p.M, kTnRowsMin, tn_splits_max(p));
+    return ((p.M + ns - 1) / ns + BK - 1) / BK;
+  }
+  const int k1 = (p.A2 && p.k1 < p.K) ? p.k1 : p.K;
+  return (k1 + BK - 1) / BK + (p.K - k1 + BK - 1) / BK;
+}
+
+bool problem_ok(const fb_gemm_bf16_problem &p) {
+  if (p.kind < FB_GEMM_NT || p.kind > FB_GEMM_TN) return false;
+  if (p.M < 0 || p.M > (int64_t)1 << 30 || p.N < 1 || p.K < 1) return false;
+  if (!p.A || !al16(p.A) || p.lda % 8 || !p.B || !al16(p.B) || p.ldb % 8) return false;
+  if (p.kind == FB_GEMM_TN) return p.lda >= p.N && p.ldb >= p.K && (p.C || p.K == 0) && p.ldc >= p.K;
+  if (!p.C || p.ldc < p.N || p.ldb < (p.kind == FB_GEMM_NT ? p.K : p.N)) return false;
+  if (p.A2 && p.k1 < p.K) {
+    const int ka = p.ka > 0 ? p.ka : p.k1;
+    return p.k1 >= 8 && p.k1 % 8 == 0 && ka <= p.k1 && p.lda >= ka && al16(p.A2) && p.lda2 % 8 == 0 &&
+           p.lda2 >= p.K - p.k1;
+  }
+  return p.lda >= p.K;
+}
+
+int64_t ws_floats(const fb_gemm_bf16_problem &p) {
+  if (p.kind != FB_GEMM_TN || p.M < 1) return 0;
+  const int Kp = p.K + (p.db ? 1 : 0);
+  const int64_t ns = fb::tn_parts(p.M, kTnRowsMin, tn_splits_max(p));
+  return (ns * (int64_t)p.N * Kp + 63) / 64 * 64;
+}
+
+int build_prob(BfProb &q, const fb_gemm_bf16_problem &p, float *ws) {
+  std::memset(&q, 0, sizeof(q));
+  q.kind = p.kind;
+  q.M = p.M;
+  q.M_dev = p.M_dev;
+  q.N = p.N;
+  q.K = p.K;
+  q.accumulate = p.accumulate;
+  q.C = p.C;
+  q.ldc = p.ldc;
+  int rc;
+  if (p.kind == FB_GEMM_TN) {
+    q.a_mn = q.b_mn = 1;
+    q.ones = p.db ? 1 : 0;
+    q.Kp = p.K + q.ones;
+    q.bn = bn_mnmajor(q.Kp);
+    q.rt = (p.N + BM - 1) / BM;
+    q.nt = (q.Kp + q.bn - 1) / q.bn;
+    q.db = p.db;
+    q.db_accumulate = p.db_accumulate;
+    q.P = ws;
+    q.max_splits = tn_splits_max(p);
+    if ((rc = make_map(&q.ta, p.A, p.M, p.N, p.lda, BK))) return rc;
+    if ((rc = make_map(&q.tb, p.B, p.M, p.K, p.ldb, BK))) return rc;
+  } else {
+    const bool two = p.A2 && p.k1 < p.K;
+    q.k1 = two ? p.k1 : p.K;
+    q.bias = p.bias;
+    q.a_mn = 0;
+    q.b_mn = p.kind == FB_GEMM_NN ? 1 : 0;
+    q.bn = q.b_mn ? bn_mnmajor(p.N) : bn_kmajor(p.N);
+    q.nt = (p.N + q.bn - 1) / q.bn;
+    const int ka = two ? (p.ka > 0 ? p.ka : p.k1) : p.K;
+    if ((rc = make_map(&q.ta, p.A, p.M, ka, p.lda, BM))) return rc;
+    if (two && (rc = make_map(&q.ta2, p.A2, p.M, p.K - p.k1, p.lda2, BM))) return rc;
+    if (q.b_mn) rc = make_map(&q.tb, p.B, p.K, p.N, p.ldb, BK);
+    else rc = make_map(&q.tb, p.B, p.N, p.K, p.ldb, q.bn);
+    if (rc) return rc;
+  }
+  q.idesc = idesc_bf16(q.bn, q.a_mn, q.b_mn);
+  return FB_OK;
+}
+
+int launch_group(const std::vector<const fb_gemm_bf16_problem *> &probs, const std::vector<float *> &ws,
+                 cudaStream_t stream) {
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    FB_TRY_CUDA(cudaFuncSetAttribute(k_bf_group, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    attr_set[dev] = true;
+  }
+  BfArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.err = err_word();
+  int64_t items = 0;
+  int red = 0;
+  for (size_t i = 0; i < probs.size(); ++i) {
+    BfProb &q = a.p[a.n];
+    const int rc = build_prob(q, *probs[i], ws[i]);
+    if (rc) return rc;
+    a.red_start[a.n] = red;
+    if (q.kind == kTN) {
+      items += (int64_t)q.rt * q.nt * fb::tn_parts(q.M, kTnRowsMin, q.max_splits);
+      red += (int)(((int64_t)q.N * q.Kp + 255) / 256);
+    } else {
+      items += (q.M + BM - 1) / BM * q.nt;
+    }
+    a.n++;
+  }
+  a.red_start[a.n] = red;
+  if (items == 0) return FB_OK;
+  const int grid = (int)std::min<int64_t>(items, num_sms());
+  FB_TRY_CUDA(fb::launch(k_bf_group, grid, kThreads, kSmem, stream, a));
+  FB_LAUNCHED("k_bf_group");
+  if (red > 0) {
+    FB_TRY_CUDA(fb::launch(k_bf_reduce, red, 256, 0, stream, a));
+    FB_LAUNCHED("k_bf_reduce");
+  }
+  return FB_OK;
+}
+
+}  // namespace
+
+extern "C" size_t fb_gemm_bf16_group_ws_bytes(const fb_gemm_bf16_problem *probs, int n) {
+  size_t total = 0;
+  for (int i = 0; i < n; ++i) total += (size_t)ws_floats(probs[i]) * sizeof(float);
+  return total + 256;
+}
+
+// Runs the problems (at most kMaxBf per launch, longest work items first).
+extern "C" int fb_gemm_bf16_group(const fb_gemm_bf16_problem *probs, int n, void *ws, size_t ws_bytes,
+                                  cudaStream_t stream) {
+  if (n < 0 || (n > 0 && !probs)) return fb::set_error(FB_ERR_ARG, "gemm_bf16_group: bad problem list");
+  if (!encode_fn()) return fb::set_error(FB_ERR_CUDA, "gemm_bf16_group: cuTensorMapEncodeTiled unavailable");
+  std::vector<int> live;
+  std::vector<float *> pws(n, nullptr);
+  size_t need = 0;
+  for (int i = 0; i < n; ++i) {
+    if (!problem_ok(probs[i]))
+      return fb::set_error(FB_ERR_UNSUPPORTED,
+                           "gemm_bf16_group: problem " + std::to_string(i) +
+                               " needs 16-byte aligned operands with leading dimensions (and k1) multiples of 8");
+    if (probs[i].M == 0) continue;
+    const size_t w = (size_t)ws_floats(probs[i]) * sizeof(float);
+    if (w) {
+      pws[i] = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + need);
+      need += w;
+    }
+    live.push_back(i);
+  }
+  if (need > 0 && (!ws || ws_bytes < need)) return fb::set_error(FB_ERR_ARG, "gemm_bf16_group: workspace too small");
+  std::stable_sort(live.begin(), live.end(),
+                   [&](int x, int y) { return slices_per_item(probs[x]) > slices_per_item(probs[y]); });
+  for (size_t s = 0; s < live.size(); s += kMaxBf) {
+    std::vector<const fb_gemm_bf16_problem *> part;
+    std::vector<float *> w;
+    for (size_t i = s; i < std::min(live.size(), s + kMaxBf); ++i) {
+      part.push_back(&probs[live[i]]);
+      w.push_back(pws[live[i]]);
+    }
+    const int rc = launch_group(part, w, stream);
+    if (rc) return rc;
+  }
+  return FB_OK;
+}

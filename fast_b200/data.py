@@ -106,6 +106,83 @@ def make_graph(cfg, seed=42, n_edges=None):
                          train_end=int(E * 0.70), val_end=int(E * 0.85))
 
 
+def _zipf_ids_device(gen, n_nodes, s, count, device, chunk=1 << 25):
+    """_zipf_ids on the device: inverse CDF of P(rank k) ~ k^-s by a search of
+    uniform draws, ranks shuffled onto ids."""
+    w = torch.arange(1, n_nodes + 1, device=device, dtype=torch.float64) ** (-s)
+    cdf = torch.cumsum(w, 0)
+    cdf /= cdf[-1].clone()
+    perm = torch.randperm(n_nodes, device=device, generator=gen).to(torch.int32)
+    out = torch.empty(count, device=device, dtype=torch.int32)
+    for c0 in range(0, count, chunk):
+        c1 = min(count, c0 + chunk)
+        u = torch.rand(c1 - c0, device=device, dtype=torch.float64, generator=gen)
+        ranks = torch.searchsorted(cdf, u, right=True).clamp_(max=n_nodes - 1)
+        out[c0:c1] = perm[ranks]
+    return out
+
+
+def make_graph_device(cfg, device, seed=42, n_edges=None):
+    """make_graph's construction on the device, for graphs too large to build
+    on the host in seconds (config 5: 191 M edges): Zipf endpoints, sorted
+    float32 timestamps, the CSR by a stable sort of the chronological edge
+    list on the source id.  The CSR arrays stay device tensors; src, dst and
+    ts are also returned on the host (the end-to-end path feeds host roots).
+    Draws come from torch's device generator, so the graph differs from
+    make_graph's for the same seed."""
+    E = cfg.edges if n_edges is None else int(n_edges)
+    N = cfg.nodes
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+
+    def ends(spec):
+        if spec[0] == "uniform":
+            return torch.randint(0, N, (E,), device=device, dtype=torch.int32, generator=gen)
+        if spec[0] == "zipf":
+            return _zipf_ids_device(gen, N, spec[1], E, device)
+        if spec[0] == "powerlaw":
+            return _zipf_ids_device(gen, N, 1.0 / (spec[1] - 1.0), E, device)
+        raise ValueError(spec[0])
+
+    src = ends(cfg.src)
+    dst = ends(cfg.dst)
+    ts = torch.rand(E, device=device, generator=gen, dtype=torch.float32) * cfg.t_max
+    if cfg.t_int:
+        ts = ts.floor_()
+    ts = torch.sort(ts).values
+    _, order = torch.sort(src, stable=True)
+    counts = torch.bincount(src, minlength=N)
+    indptr = torch.zeros(N + 1, device=device, dtype=torch.int64)
+    indptr[1:] = torch.cumsum(counts, 0)
+    indices = dst[order]
+    ts_csr = ts[order]
+    eid = order.to(torch.int32)
+    del order
+    return TemporalGraph(src=src.cpu().numpy(), dst=dst.cpu().numpy(), ts=ts.cpu().numpy(),
+                         indptr=indptr.to(torch.int32), indices=indices, eid=eid, ts_csr=ts_csr, n_nodes=N,
+                         train_end=int(E * 0.70), val_end=int(E * 0.85))
+
+
+def make_features_bf16(cfg, n_edges, device, seed=7):
+    """(node_feats, edge_feats) as bf16 device tables with rows padded with
+    zeros to a multiple of 8 columns (the bf16 projection mode's layout),
+    seeded N(0, 1) values from fb_fill_normal_bf16 (None where the width is 0)."""
+    from .capi import call, ptr, stream_ptr
+
+    def mk(rows, cols, salt):
+        if cols == 0:
+            return None
+        ld = (cols + 7) // 8 * 8
+        t = torch.empty(rows, ld, device=device, dtype=torch.bfloat16)
+        if cfg.feat == "zeros":
+            t.zero_()
+        else:
+            call("fb_fill_normal_bf16", ptr(t), rows, cols, ld, seed * 1000003 + salt, stream_ptr())
+        return t
+
+    return mk(cfg.nodes, cfg.d_node, 1), mk(n_edges, cfg.d_edge, 2)
+
+
 def make_features(cfg, n_edges, device, seed=7, dtype=torch.float32):
     """(node_feats, edge_feats) tensors on `device` (None where the width is 0)."""
     g = torch.Generator(device=device)

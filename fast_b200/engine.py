@@ -53,8 +53,13 @@ class FusedStep:
     GeneralModel.  Call `step(blocks, node_table, edge_table, loss_out)`; then
     run the optimizer on the model's parameters."""
 
-    def __init__(self, model):
+    def __init__(self, model, precision="fp32"):
+        if precision not in ("fp32", "bf16"):
+            raise ValueError("precision must be 'fp32' or 'bf16'")
+        self.precision = precision
         self.mem = getattr(model, "memory_updater", None)
+        if precision == "bf16" and self.mem is not None:
+            raise NotImplementedError("the bf16 projection mode covers the memoryless attention layers")
         if model.memory_param.get("type", "none") != "none" and self.mem is None:
             raise NotImplementedError("node memory needs memory.MemoryModel")
         self.model = model
@@ -77,6 +82,8 @@ class FusedStep:
             if lp.L.layer_norm.weight.shape[0] % 4 or lp.D % 4:
                 raise NotImplementedError("dim_out must be a multiple of 4")
         self.flat = self._build_flat()
+        if precision == "bf16":
+            self._build_bf16()
 
     # -- parameter and gradient storage ---------------------------------------
     def _build_flat(self):
@@ -130,6 +137,170 @@ class FusedStep:
 
     def parameters(self):
         return list(self.model.parameters())
+
+    # -- bf16 projection mode -------------------------------------------------
+    def _build_bf16(self):
+        """bf16 copies of the projection weights in the column layout of the
+        bf16 projection rows (segments at multiples of 8, zeros between):
+        W_kv over [h | f | time], W_q over [h | time], W_out over [agg | h].
+        Refreshed from the fp32 master weights by one cast launch per step."""
+        self.cast_jobs = []
+        for lp in self.layers:
+            L, D, dn, de, dt = lp.L, lp.D, lp.dn, lp.de, lp.dtime
+            dev = lp.W_kv.device
+            bf = dict(device=dev, dtype=torch.bfloat16)
+            (h_at, f_at, t_at), kx = ops.bf16_layout(dn, de, dt)
+            lp.kv_segs = [(at, lo, d) for at, lo, d in ((h_at, 0, dn), (f_at, dn, de), (t_at, dn + de, dt)) if d > 0]
+            lp.kx = kx
+            lp.W_kv_bf = torch.zeros(2 * D, ops.pad8(kx), **bf)
+            for at, lo, d in lp.kv_segs:
+                self.cast_jobs.append((lp.W_kv[:, lo:lo + d], lp.W_kv_bf[:, at:at + d]))
+            if dn > 0:
+                (qh, qt), kq = ops.bf16_layout(dn, dt) if dt > 0 else ((0, 0), dn)
+                lp.q_segs = [(qh, 0, dn)] + ([(qt, dn, dt)] if dt > 0 else [])
+                lp.kq = kq
+                lp.W_q_bf = torch.zeros(D, ops.pad8(kq), **bf)
+                for at, lo, d in lp.q_segs:
+                    self.cast_jobs.append((L.w_q.weight[:, lo:lo + d], lp.W_q_bf[:, at:at + d]))
+            lp.ka = ops.pad8(D)
+            lp.W_out_bf = torch.zeros(D, ops.pad8(lp.ka + dn), **bf)
+            self.cast_jobs.append((L.w_out.weight[:, :D], lp.W_out_bf[:, :D]))
+            if dn > 0:
+                self.cast_jobs.append((L.w_out.weight[:, D:], lp.W_out_bf[:, lp.ka:lp.ka + dn]))
+
+    def _layer_fwd_bf16(self, l, blk, h, node_table, edge_table, offset_dev, training):
+        """_layer_fwd with bf16 projections: bf16 projection rows from the
+        gather, K|V, Q and w_out products of bf16 operands accumulated in fp32;
+        attention, tail and everything after in fp32."""
+        lp = self.layers[l]
+        L, D, dn, de, dtime = lp.L, lp.D, lp.dn, lp.de, lp.dtime
+        nd, E = blk.n_dst, blk.n_edges
+        nd_dev, E_dev = blk.n_dst_dev, blk.n_edges_dev
+        dev = lp.W_kv.device
+        if not blk.static and E == 0:
+            return None, torch.zeros(nd, D, device=dev)
+        wv = L.time_enc.w.weight.view(-1) if dtime > 0 else None
+        bt = L.time_enc.w.bias if dtime > 0 else None
+        if h is not None:
+            if blk.static and not blk.n_dst_static:
+                raise NotImplementedError("graph mode feeds a previous layer's output only to the top block")
+            hsrc, hdst = dict(h=h, h_off=nd), dict(h=h, h_off=0)
+        elif node_table is not None and dn > 0:
+            hsrc, hdst = dict(h=node_table, h_idx=blk.src_nodes), dict(h=node_table, h_idx=blk.dst_nodes)
+        else:
+            hsrc = hdst = {}
+        X, kx = ops.gather_time_encode_bf16(E, f=edge_table if de > 0 else None, f_idx=blk.eid, dt=blk.dt_edges,
+                                            w=wv, b=bt, device=dev, n_rows_dev=E_dev, dn=dn, de=de, **hsrc)
+        KV = torch.empty(E, 2 * D, device=dev)
+        probs = [dict(kind=ops.NT, A=X[:, :kx], B=lp.W_kv_bf[:, :kx], bias=lp.b_kv, out=KV, M_dev=E_dev)]
+        if dn > 0:
+            Qin, kq = ops.gather_time_encode_bf16(nd, w=wv, b=bt, device=dev, n_rows_dev=nd_dev, dn=dn, **hdst)
+            Q = torch.empty(nd, D, device=dev)
+            probs.append(dict(kind=ops.NT, A=Qin[:, :kq], B=lp.W_q_bf[:, :kq], bias=L.w_q.bias, out=Q, M_dev=nd_dev))
+            ops.gemm_bf16_group(probs, name="gemm_group:kv_q")
+        else:
+            # one shared Q input row cos(b_t): its product stays fp32
+            Qin = ops.gather_time_encode(1, w=wv, b=bt, device=dev)
+            Q = torch.empty(1, D, device=dev)
+            ops.gemm_bf16_group(probs, name="gemm_group:kv_q")
+            ops.gemm_group([dict(kind=ops.NT, A=Qin, B=L.w_q.weight, bias=L.w_q.bias, out=Q)], name="gemm_group:q1")
+        p_att = L.att_dropout_p if training else 0.0
+        agg, att = ops.attn_fwd(Q, KV[:, :D], KV[:, D:], blk.rptr, L.num_head, L.negative_slope, p_att,
+                                0x5EED + l, 0, n_dst_dev=nd_dev, offset_dev=offset_dev)
+        agg_bf = torch.empty(nd, lp.ka, device=dev, dtype=torch.bfloat16)
+        ops.cast_bf16([(agg, agg_bf[:, :D], nd_dev)])
+        Z = torch.empty(nd, D, device=dev)
+        if dn > 0:
+            p_out = dict(kind=ops.NT, A=agg_bf[:, :D], A2=Qin[:, :dn], k1=lp.ka, B=lp.W_out_bf[:, :lp.ka + dn],
+                         bias=L.w_out.bias, out=Z, M_dev=nd_dev)
+        else:
+            p_out = dict(kind=ops.NT, A=agg_bf[:, :D], B=lp.W_out_bf[:, :D], bias=L.w_out.bias, out=Z, M_dev=nd_dev)
+        ops.gemm_bf16_group([p_out], name="gemm_group:w_out")
+        p_drop = L.dropout.p if training else 0.0
+        y, out = ops.layer_tail_fwd(Z, L.layer_norm.weight, L.layer_norm.bias, eps=L.layer_norm.eps, drop_p=p_drop,
+                                    seed=0x7A11 + l, offset_dev=offset_dev, y=Z, n_dev=nd_dev,
+                                    gate_dev=E_dev if blk.static else None)
+        st = dict(blk=blk, A=X, KV=KV, Qin=Qin, Q=Q, agg=agg, agg_bf=agg_bf, att=att, y=y, p_att=p_att,
+                  p_drop=p_drop, offset_dev=offset_dev)
+        return st, out
+
+    def _layer_bwd_bf16(self, l, st, dout, dh_rows):
+        """_layer_bwd with bf16 operands for every projection-gradient product
+        (the gradient rows rounded to bf16: dZ, dK|dV, dQ)."""
+        lp = self.layers[l]
+        L, D, dn, de, dtime = lp.L, lp.D, lp.dn, lp.de, lp.dtime
+        if st is None:
+            return None if dh_rows == 0 else torch.zeros(dh_rows, dn, device=dout.device)
+        blk = st["blk"]
+        nd, E = blk.n_dst, blk.n_edges
+        nd_dev, E_dev = blk.n_dst_dev, blk.n_edges_dev
+        g = lambda p: p.grad
+        dev = dout.device
+        dZ = ops.layer_tail_bwd(dout, st["y"], L.layer_norm.weight, g(L.layer_norm.weight), g(L.layer_norm.bias),
+                                eps=L.layer_norm.eps, drop_p=st["p_drop"], n_dev=nd_dev,
+                                gate_dev=E_dev if blk.static else None)
+        dZ_bf = torch.empty(nd, lp.ka, device=dev, dtype=torch.bfloat16)
+        ops.cast_bf16([(dZ, dZ_bf[:, :D], nd_dev)])
+        dZb = dZ_bf[:, :D]
+        gWo = g(L.w_out.weight)
+        Qin, agg_bf = st["Qin"], st["agg_bf"]
+        dagg = torch.empty(nd, D, device=dev)
+        dh = None
+        probs = [dict(kind=ops.TN, A=dZb, B=agg_bf[:, :D], out=gWo[:, :D], accumulate=True, M_dev=nd_dev,
+                      db=g(L.w_out.bias)),
+                 dict(kind=ops.NN, A=dZb, B=lp.W_out_bf[:, :D], out=dagg, M_dev=nd_dev)]
+        if dn > 0:
+            probs.append(dict(kind=ops.TN, A=dZb, B=Qin[:, :dn], out=gWo[:, D:], accumulate=True, M_dev=nd_dev))
+        if dh_rows > 0:
+            assert dh_rows >= nd + E
+            dh = torch.empty(dh_rows, dn, device=dev)
+            probs.append(dict(kind=ops.NN, A=dZb, B=lp.W_out_bf[:, lp.ka:lp.ka + dn], out=dh[:nd], M_dev=nd_dev))
+        ops.gemm_bf16_group(probs, name="gemm_group:bwd_dz")
+        KV = st["KV"]
+        dQ, dKV = ops.attn_bwd_bf16kv(st["Q"], KV[:, :D], KV[:, D:], blk.rptr, st["att"], dagg, L.num_head,
+                                      L.negative_slope, st["p_att"], 0x5EED + l, 0, n_dst_dev=nd_dev,
+                                      offset_dev=st["offset_dev"])
+        X = st["A"]
+        v = torch.empty(D, device=dev)            # sum over rows of dQ
+        probs = []
+        last = len(lp.kv_segs) - 1
+        for i, (at, lo, d) in enumerate(lp.kv_segs):
+            probs.append(dict(kind=ops.TN, A=dKV, B=X[:, at:at + d], out=lp.gW_kv[:, lo:lo + d], accumulate=True,
+                              M_dev=E_dev, db=lp.gb_kv if i == last else None))
+        if dh is not None:
+            probs.append(dict(kind=ops.NN, A=dKV, B=lp.W_kv_bf[:, :dn], out=dh[nd:nd + E], M_dev=E_dev))
+        dA_t = None
+        if dtime > 0:
+            t_at = lp.kv_segs[-1][0]
+            dA_t = torch.empty(E, dtime, device=dev)
+            probs.append(dict(kind=ops.NN, A=dKV, B=lp.W_kv_bf[:, t_at:t_at + dtime], out=dA_t, M_dev=E_dev))
+        if dn > 0:
+            dQ_bf = torch.empty(nd, lp.ka, device=dev, dtype=torch.bfloat16)
+            ops.cast_bf16([(dQ, dQ_bf[:, :D], nd_dev)])
+            dQb = dQ_bf[:, :D]
+            last = len(lp.q_segs) - 1
+            for i, (at, lo, d) in enumerate(lp.q_segs):
+                probs.append(dict(kind=ops.TN, A=dQb, B=Qin[:, at:at + d], out=g(L.w_q.weight)[:, lo:lo + d],
+                                  accumulate=True, M_dev=nd_dev, db=v if i == last else None, db_accumulate=False))
+            if dh is not None:
+                probs.append(dict(kind=ops.NN, A=dQb, B=lp.W_q_bf[:, :dn], out=dh[:nd], accumulate=True,
+                                  M_dev=nd_dev))
+            ops.gemm_bf16_group(probs, name="gemm_group:bwd_dkv_dq")
+        else:
+            ops.gemm_bf16_group(probs, name="gemm_group:bwd_dkv_dq")
+            ops.gemm_group([dict(kind=ops.TN, A=dQ, B=None, out=None, M_dev=nd_dev, db=v, db_accumulate=False)],
+                           name="gemm_group:dq_sum")
+        if dtime > 0:
+            ops.time_encode_bwd(dA_t, blk.dt_edges, L.time_enc.w.weight.view(-1), L.time_enc.w.bias,
+                                g(L.time_enc.w.weight).view(-1), g(L.time_enc.w.bias), n_dev=E_dev)
+        bt = L.time_enc.w.bias if dtime > 0 else None
+        gbt = g(L.time_enc.w.bias) if dtime > 0 else None
+        if dn == 0:
+            ops.q_time_bwd(v, L.w_q.weight, dn, dtime, bt, g(L.w_q.bias), gbt, qin0=st["Qin"][0],
+                           dW_q=g(L.w_q.weight))
+        else:
+            ops.q_time_bwd(v, L.w_q.weight, dn, dtime, bt, g(L.w_q.bias), gbt)
+        return dh
 
     # -- one layer ------------------------------------------------------------
     def _layer_fwd(self, l, blk, h, node_table, edge_table, offset_dev, training):
@@ -399,14 +570,19 @@ class FusedStep:
                 raise ValueError("a memory model needs its MailBox")
             h, mem_st = self._memory_fwd(mfgs[0], mailbox)
             self.last_memory = h
+        bf16 = self.precision == "bf16"
+        if bf16:
+            ops.cast_bf16(self.cast_jobs, name="cast_bf16:weights")
+        fwd = self._layer_fwd_bf16 if bf16 else self._layer_fwd
+        bwd = self._layer_bwd_bf16 if bf16 else self._layer_bwd
         for l, blk in enumerate(mfgs):
-            st, h = self._layer_fwd(l, blk, h, node_table if (l == 0 and mem_st is None) else None, edge_table,
-                                    m._drop_step, training)
+            st, h = fwd(l, blk, h, node_table if (l == 0 and mem_st is None) else None, edge_table,
+                        m._drop_step, training)
             saved.append(st)
         dh = self._predictor(h, loss_out, scores)
         for l in range(len(mfgs) - 1, -1, -1):
             rows = mfgs[l - 1].n_dst if l > 0 else (mfgs[0].n_src if mem_st is not None else 0)
-            dh = self._layer_bwd(l, saved[l], dh, rows)
+            dh = bwd(l, saved[l], dh, rows)
         if mem_st is not None:
             if dh is None:                   # an empty block: no gradient reaches the memory updater
                 dh = torch.zeros(mem_st["n"], self.mem.dim_hid, device=dev)

@@ -200,6 +200,139 @@ def gemm_group(problems, name="gemm_group"):
             lambda: call("fb_gemm_group", arr, n, ptr(ws), ws.numel(), stream_ptr()))
 
 
+def pad8(n):
+    """n rounded up to a multiple of 8 (16 bytes of bf16)."""
+    return (n + 7) // 8 * 8
+
+
+def _bf16_rows(t, name):
+    if t.dtype != torch.bfloat16 or t.dim() != 2 or t.stride(1) != 1 or not t.is_cuda:
+        raise ValueError("%s must be a CUDA bf16 matrix with unit column stride" % name)
+
+
+def gemm_bf16_group(problems, name="gemm_bf16_group"):
+    """gemm_group with bf16 operands (torch.bfloat16 matrices; C, bias, db
+    fp32) on the tcgen05 kind::f16 kernel: products of bf16 values
+    accumulated in fp32.  Same problem dicts as gemm_group (B required); with
+    A2, k1 (a multiple of 8, >= A's width) is the column of B where A2's
+    block starts."""
+    from .capi import GemmBf16Problem
+    arr = (GemmBf16Problem * len(problems))()
+    nbytes, flops = 0, 0
+    keep = []
+    for i, p in enumerate(problems):
+        A, B, out, A2 = p["A"], p["B"], p.get("out"), p.get("A2")
+        kind = p["kind"]
+        for t in (A, B, A2):
+            if t is not None:
+                _bf16_rows(t, "gemm_bf16_group operand")
+        _f32_rows(out, "gemm_bf16_group output")
+        M = A.shape[0]
+        if kind == TN:
+            N, K = A.shape[1], B.shape[1]
+        elif kind == NT:
+            N, K = B.shape[0], A.shape[1] + (0 if A2 is None else A2.shape[1])
+        else:
+            N, K = B.shape[1], A.shape[1] + (0 if A2 is None else A2.shape[1])
+        k1 = p.get("k1", A.shape[1]) if A2 is not None else K
+        if A2 is not None:
+            K = k1 + A2.shape[1]
+        db = p.get("db")
+        acc = int(bool(p.get("accumulate", False)))
+        dba = p.get("db_accumulate")
+        arr[i] = GemmBf16Problem(kind, ptr(A), A.stride(0), ptr(A2), 0 if A2 is None else A2.stride(0), k1,
+                                 ptr(B), B.stride(0), ptr(p.get("bias")), ptr(out), out.stride(0),
+                                 M, _p(p.get("M_dev")), N, K, acc, ptr(db), int(acc if dba is None else bool(dba)),
+                                 A.shape[1] if A2 is not None else 0)
+        keep.append((A, B, A2, out, db))
+        nbytes += 2 * (M * K + N * K) + 4 * M * N
+        flops += 2 * M * N * K
+    n = len(problems)
+    dev = problems[0]["A"].device
+    ws = torch.empty(int(lib.fb_gemm_bf16_group_ws_bytes(arr, n)), device=dev, dtype=torch.uint8)
+    _launch(name, nbytes, flops, 2,
+            lambda: call("fb_gemm_bf16_group", arr, n, ptr(ws), ws.numel(), stream_ptr()))
+
+
+def cast_bf16(jobs, name="cast_bf16"):
+    """One launch of fp32 -> bf16 (round to nearest even) block copies: jobs
+    are (src fp32 [rows, cols] view, dst bf16 [rows, cols] view[, rows_dev])."""
+    from .capi import CastJob, CAST_MAX_JOBS
+    if not jobs:
+        return
+    if len(jobs) > CAST_MAX_JOBS:
+        for i in range(0, len(jobs), CAST_MAX_JOBS):
+            cast_bf16(jobs[i:i + CAST_MAX_JOBS], name)
+        return
+    arr = (CastJob * len(jobs))()
+    nbytes = 0
+    for i, j in enumerate(jobs):
+        src, dst = j[0], j[1]
+        rows_dev = j[2] if len(j) > 2 else None
+        _f32_rows(src, "cast_bf16 source")
+        _bf16_rows(dst, "cast_bf16 destination")
+        if tuple(src.shape) != tuple(dst.shape):
+            raise ValueError("cast_bf16: source %s and destination %s differ" % (tuple(src.shape), tuple(dst.shape)))
+        arr[i] = CastJob(ptr(src), src.stride(0), ptr(dst), dst.stride(0), src.shape[0], _p(rows_dev), src.shape[1],
+                         0)
+        nbytes += 6 * src.numel()
+    _launch(name, nbytes, 0, 1, lambda: call("fb_cast_bf16", arr, len(jobs), stream_ptr()))
+
+
+def bf16_layout(*dims):
+    """Column offsets of the segments of a bf16 projection row (each at a
+    multiple of 8) and the row's width (data columns; the last segment unpadded)."""
+    offs, at = [], 0
+    for d in dims:
+        offs.append(at)
+        at += pad8(d)
+    width = offs[-1] + dims[-1] if dims else 0
+    return offs, width
+
+
+def gather_time_encode_bf16(n_rows, h=None, h_idx=None, h_off=0, f=None, f_idx=None, dt=None, w=None, b=None,
+                            out=None, device=None, n_rows_dev=None, h_off_dev=None, dn=None, de=None):
+    """bf16 rows [h | f | cos(w*dt + b)] with segments at multiples of 8 columns
+    (zeros between).  h / f: fp32 matrices, or bf16 tables with rows padded
+    with zeros to a multiple of 8 (then dn / de give the true widths)."""
+    dn = 0 if h is None else (dn if dn is not None else h.shape[1])
+    de = 0 if f is None else (de if de is not None else f.shape[1])
+    dtime = 0 if w is None else w.numel()
+    dev = device or (h.device if h is not None else (f.device if f is not None else w.device))
+    width = pad8(dn) + pad8(de) + dtime
+    if out is None:
+        out = torch.empty(n_rows, pad8(width), device=dev, dtype=torch.bfloat16)
+    hb = int(h is not None and h.dtype == torch.bfloat16)
+    fb_ = int(f is not None and f.dtype == torch.bfloat16)
+    nbytes = n_rows * (2 * width + (2 if hb else 4) * dn + (2 if fb_ else 4) * de + 4 * (dt is not None)
+                       + 4 * (h_idx is not None) + 4 * (f_idx is not None))
+    _launch("gather_time_encode", nbytes, 0, 1,
+            lambda: call("fb_gather_time_encode_bf16", ptr(h), hb, 0 if h is None else h.stride(0), ptr(h_idx),
+                         int(h_off), _p(h_off_dev), dn, ptr(f), fb_, 0 if f is None else f.stride(0), ptr(f_idx), de,
+                         ptr(dt), ptr(w), ptr(b), dtime, ptr(out), out.stride(0), n_rows, _p(n_rows_dev),
+                         stream_ptr()))
+    return out, width
+
+
+def attn_bwd_bf16kv(q, k, v, rptr, att, dagg, heads, slope, drop_p=0.0, seed=0, offset=0, n_dst_dev=None,
+                    offset_dev=None, dq=None):
+    """attn_bwd with dk | dv written as one bf16 [E, 2D] matrix (the operand of
+    the bf16 projection-gradient GEMMs); dq fp32."""
+    nd = rptr.numel() - 1
+    E, D = k.shape
+    ldq = 0 if (q.shape[0] == 1 and nd != 1) else q.stride(0)
+    if dq is None:
+        dq = torch.empty(nd, D, device=k.device, dtype=torch.float32)
+    dkv = torch.empty(E, 2 * D, device=k.device, dtype=torch.bfloat16)
+    qrows = nd if ldq else 1
+    nbytes = 4 * (qrows * D + nd * D + 2 * E * D + E * heads + (nd + 1) + nd * D) + 2 * 2 * E * D
+    _launch("attn_bwd", nbytes, 0, 1,
+            lambda: call("fb_attn_bwd_bf16kv", ptr(q), ldq, ptr(k), ptr(v), k.stride(0), ptr(rptr), nd,
+                         _p(n_dst_dev), heads, D, slope, drop_p, seed, offset, _p(offset_dev), ptr(att), ptr(dagg),
+                         dagg.stride(0), ptr(dq), ptr(dkv), dkv.data_ptr() + 2 * D, dkv.stride(0), stream_ptr()))
+    return dq, dkv
+
+
 def gru_fwd(gi, gh, h0, h1, n_dev=None):
     """GRUCell gates from the products gi = x W_ih^T + b_ih, gh = h0 W_hh^T + b_hh
     ([n, 3H]); writes h1 and keeps (r, z, n) in gi (memorys.py:272-304)."""

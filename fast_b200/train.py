@@ -47,21 +47,44 @@ def average_gradients(params, world, flat=None):
     return flat
 
 
+def _bf16_table(t, width):
+    """A feature table as bf16 rows padded with zeros to a multiple of 8
+    columns (kept as is when it already is one)."""
+    if t is None or t.dtype == torch.bfloat16:
+        return t
+    out = torch.zeros(t.shape[0], ops.pad8(width), device=t.device, dtype=torch.bfloat16)
+    out[:, :width] = t[:, :width]
+    return out
+
+
 class Trainer:
     """Eager trainer: host-sized blocks (the sampled sizes are read back each
     step).  fused=True runs forward + backward through FusedStep (no
     autograd); fused=False through the GeneralModel module under autograd."""
 
     def __init__(self, graph, node_feats, edge_feats, sample_param, memory_param, gnn_param, train_param,
-                 device, rank=0, world=1, seed=42, sampler_seed=1234, fused=False):
+                 device, rank=0, world=1, seed=42, sampler_seed=1234, fused=False, precision="fp32",
+                 feat_dims=None):
+        """precision 'bf16' (fused only) runs the projections on bf16 operands:
+        the feature tables are then bf16 with rows padded with zeros to a
+        multiple of 8 columns (fp32 tables are converted once here), and
+        feat_dims = (dn, de) gives their true widths when they arrive padded."""
         self.device = torch.device(device)
         self.rank, self.world = rank, world
         self.graph = graph
         self.sample_param = sample_param
-        self.node_feats, self.edge_feats = node_feats, edge_feats
         torch.manual_seed(seed)
-        dn = 0 if node_feats is None else node_feats.shape[1]
-        de = 0 if edge_feats is None else edge_feats.shape[1]
+        if feat_dims is not None:
+            dn, de = feat_dims
+        else:
+            dn = 0 if node_feats is None else node_feats.shape[1]
+            de = 0 if edge_feats is None else edge_feats.shape[1]
+        if precision == "bf16":
+            if not fused:
+                raise NotImplementedError("the bf16 projection mode runs through FusedStep")
+            node_feats = _bf16_table(node_feats, dn)
+            edge_feats = _bf16_table(edge_feats, de)
+        self.node_feats, self.edge_feats = node_feats, edge_feats
         self.mailbox = None
         if memory_param.get("type", "none") != "none":
             if not fused or world > 1:
@@ -76,19 +99,20 @@ class Trainer:
             for p in self.model.parameters():   # identical start on every rank
                 dist.broadcast(p.data, 0)
         # FusedStep re-seats the parameters in flat buffers: build it before an optimizer sees them
-        self.engine = FusedStep(self.model) if fused else None
+        self.engine = FusedStep(self.model, precision=precision) if fused else None
         self.loss_buf = torch.zeros((), device=self.device)
         self.opt = FlatAdam(self.engine, train_param["lr"]) if fused else \
             torch.optim.Adam(self.model.parameters(), lr=train_param["lr"])
         self.crit = torch.nn.BCEWithLogitsLoss()
         dv = self.device
-        self.indptr = torch.from_numpy(graph.indptr).to(dv)
-        self.indices = torch.from_numpy(graph.indices).to(dv)
-        self.eid = torch.from_numpy(graph.eid).to(dv)
-        self.ts_csr = torch.from_numpy(graph.ts_csr).to(dv)
-        self.src = torch.from_numpy(graph.src).to(dv)
-        self.dst = torch.from_numpy(graph.dst).to(dv)
-        self.ts = torch.from_numpy(graph.ts).to(dv)
+        # numpy arrays, or device tensors of a graph built on the device
+        self.indptr = torch.as_tensor(graph.indptr).to(dv)
+        self.indices = torch.as_tensor(graph.indices).to(dv)
+        self.eid = torch.as_tensor(graph.eid).to(dv)
+        self.ts_csr = torch.as_tensor(graph.ts_csr).to(dv)
+        self.src = torch.as_tensor(graph.src).to(dv)
+        self.dst = torch.as_tensor(graph.dst).to(dv)
+        self.ts = torch.as_tensor(graph.ts).to(dv)
         self.sampler = sampler_core.ParallelSampler(
             self.indptr, self.indices, self.eid, self.ts_csr, 1, 1, sample_param["layer"],
             list(sample_param["neighbor"]), sample_param["strategy"] == "recent", sample_param["prop_time"],
@@ -235,9 +259,11 @@ class GraphTrainer(Trainer):
     all-reduce of the flat gradient bucket."""
 
     def __init__(self, graph, node_feats, edge_feats, sample_param, memory_param, gnn_param, train_param,
-                 device, batch, rank=0, world=1, seed=42, sampler_seed=1234, optimizer="adam", fused=True):
+                 device, batch, rank=0, world=1, seed=42, sampler_seed=1234, optimizer="adam", fused=True,
+                 precision="fp32", feat_dims=None):
         super().__init__(graph, node_feats, edge_feats, sample_param, memory_param, gnn_param, train_param,
-                         device, rank=rank, world=world, seed=seed, sampler_seed=sampler_seed, fused=fused)
+                         device, rank=rank, world=world, seed=seed, sampler_seed=sampler_seed, fused=fused,
+                         precision=precision, feat_dims=feat_dims)
         self.B = batch
         self.R0 = 3 * batch
         dv = self.device

@@ -130,6 +130,13 @@ int fb_attn_bwd(const float *q, int64_t ldq, const float *k, const float *v, int
                 float slope, float drop_p, uint64_t seed, uint64_t offset, const uint64_t *offset_dev,
                 const float *att, const float *dagg, int64_t lddagg, float *dq, float *dk, float *dv,
                 int64_t lddkv, cudaStream_t stream);
+/* fb_attn_bwd with dk / dv written as bf16 bit patterns (round to nearest
+ * even) for the bf16 projection GEMMs; lddkv % 4 == 0. */
+int fb_attn_bwd_bf16kv(const float *q, int64_t ldq, const float *k, const float *v, int64_t ldkv,
+                       const int32_t *rptr, int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim,
+                       float slope, float drop_p, uint64_t seed, uint64_t offset, const uint64_t *offset_dev,
+                       const float *att, const float *dagg, int64_t lddagg, float *dq, uint16_t *dk, uint16_t *dv,
+                       int64_t lddkv, cudaStream_t stream);
 /* Sticky error bits of the attention kernels on the current device (2 = a
  * bounded wait for a shared-memory bulk copy timed out and the warp gave up);
  * synchronises; clear resets. */
@@ -217,6 +224,17 @@ int fb_gather_time_encode(const float *h, int64_t ldh, const int32_t *h_idx, int
                           const float *dt, const float *w, const float *b, int dtime,
                           float *A, int64_t lda, int64_t n_rows, const int32_t *n_rows_dev,
                           cudaStream_t stream);
+/* The bf16 projection rows of the bf16 precision mode: [h | f | cos(w dt + b)]
+ * as bf16 with h at column 0, f at column pad8(dn) and the time encoding at
+ * pad8(dn) + pad8(de) (pad8: up to a multiple of 8), so that each segment
+ * starts on a 16-byte boundary; the gaps are zeros.  h and f are bf16 tables
+ * (h_bf16 / f_bf16 = 1; rows 16-byte aligned and padded with zeros to a
+ * multiple of 8 columns) or fp32 (dims multiples of 4).  lda % 8 == 0. */
+int fb_gather_time_encode_bf16(const void *h, int h_bf16, int64_t ldh, const int32_t *h_idx, int64_t h_off,
+                               const int32_t *h_off_dev, int dn, const void *f, int f_bf16, int64_t ldf,
+                               const int32_t *f_idx, int de, const float *dt, const float *w, const float *b,
+                               int dtime, uint16_t *A, int64_t lda, int64_t n_rows, const int32_t *n_rows_dev,
+                               cudaStream_t stream);
 /* Gradient of the time encoding: with g = dL/dcos(w*dt+b) (rows at g + r*ldg),
  * dw[j] += sum_r -sin(w_j dt_r + b_j) dt_r g[r,j],  db[j] += sum_r -sin(..) g[r,j].
  * `ws` must hold fb_time_encode_bwd_ws_bytes(n_rows, dtime) bytes. */
@@ -286,6 +304,48 @@ typedef struct fb_gemm_problem {
 } fb_gemm_problem;
 size_t fb_gemm_group_ws_bytes(const fb_gemm_problem *probs, int n);
 int fb_gemm_group(const fb_gemm_problem *probs, int n, void *ws, size_t ws_bytes, cudaStream_t stream);
+/* The same groups with bf16 operands (bf16 bit patterns, round-to-nearest-
+ * even from fp32) and fp32 accumulation: the projections of the bf16
+ * precision mode, on the tcgen05 tensor cores (kind::f16).  Field meanings as
+ * in fb_gemm_problem (plus ka); C, bias and db stay fp32.  Every operand 16-byte
+ * aligned with a leading dimension (elements) that is a multiple of 8, k1 a
+ * multiple of 8, K >= 1 (TN: db via a virtual ones column at k = K).  ws:
+ * fb_gemm_bf16_group_ws_bytes(probs, n) bytes. */
+typedef struct fb_gemm_bf16_problem {
+  int kind;
+  const uint16_t *A; int64_t lda;
+  const uint16_t *A2; int64_t lda2; int k1;
+  const uint16_t *B; int64_t ldb;
+  const float *bias;
+  float *C; int64_t ldc;
+  int64_t M; const int32_t *M_dev;
+  int N, K;
+  int accumulate;
+  float *db; int db_accumulate;
+  int ka;        /* NT / NN with A2: data columns of A (<= k1; 0 means k1); A's
+                    columns [ka, k1) read as zeros, so k1 can round A's width up
+                    to the 8-column boundary where A2's block of B starts */
+} fb_gemm_bf16_problem;
+size_t fb_gemm_bf16_group_ws_bytes(const fb_gemm_bf16_problem *probs, int n);
+int fb_gemm_bf16_group(const fb_gemm_bf16_problem *probs, int n, void *ws, size_t ws_bytes, cudaStream_t stream);
+/* fp32 -> bf16 (round to nearest even) block copies, one launch for a list:
+ * job i copies src [rows, cols] (leading dimension lds) into dst (ldd); rows
+ * at or past *rows_dev are skipped when rows_dev is given.  At most
+ * FB_CAST_MAX_JOBS jobs per call.  Used for the bf16 copies of the
+ * projection weights (column segments placed at 8-element boundaries) and of
+ * fp32 activations that feed bf16 GEMMs. */
+enum { FB_CAST_MAX_JOBS = 32 };
+typedef struct fb_cast_job {
+  const float *src; int64_t lds;
+  uint16_t *dst; int64_t ldd;
+  int64_t rows; const int32_t *rows_dev;
+  int cols; int pad_;
+} fb_cast_job;
+int fb_cast_bf16(const fb_cast_job *jobs, int n, cudaStream_t stream);
+/* Synthetic feature tables on the device: dst[rows, ldd] (bf16) gets seeded
+ * N(0, 1) values in columns < cols (Box-Muller over a counter hash of
+ * (seed, element)) and zeros in the padding columns.  ldd even. */
+int fb_fill_normal_bf16(uint16_t *dst, int64_t rows, int cols, int64_t ldd, uint64_t seed, cudaStream_t stream);
 /* db[n] (+)= sum_m G[m, n]; deterministic.  ws: fb_colsum_ws_bytes(M, N). */
 size_t fb_colsum_ws_bytes(int64_t M, int N);
 int fb_colsum(const float *G, int64_t ldg, float *db, int64_t M, const int32_t *M_dev, int N,

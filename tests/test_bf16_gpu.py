@@ -1,0 +1,269 @@
+"""GPU: the bf16 precision mode's kernels.
+
+* fb_gemm_bf16_group (tcgen05 kind::f16) against an fp64 product of the same
+  bf16 operands: the products of bf16 values are exact in fp32, so the only
+  difference is the fp32 accumulation, bounded by K * 2^-23 * sum |a b|.
+  NT (with bias, accumulate, A | A2 concatenation), NN on a column block of a
+  bf16 weight copy, TN with the bias gradient; operand rows past the
+  device-side count hold NaN and must not reach the result.
+* fb_cast_bf16, fb_gather_time_encode_bf16 and fb_attn_bwd_bf16kv are
+  bit-exact against round-to-nearest-even of the fp32 kernels' outputs.
+* A whole FusedStep in the bf16 mode against the fp64 run of the oracle
+  (oracle/ref_math.py on the oracle sampler's blocks): every output within
+  bf16 accuracy -- relative L2 error <= 3e-2 per gradient tensor, 1e-2 for
+  the loss and predictions -- with node / edge widths (413 / 186) that
+  exercise every padded segment.
+"""
+import copy
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf(x):
+    return x.to(torch.bfloat16)
+
+
+def _check(got, a64, b64, K, name, base=None):
+    """|got - (base + a64 @ b64)| <= K 2^-23 (|a| @ |b|) + 2^-23 (|base| + |ref|),
+    elementwise: the accumulation bound plus the fp32 roundings of adding
+    bias / the accumulated output."""
+    ref = a64 @ b64
+    bound = K * 2.0 ** -23 * (a64.abs() @ b64.abs()) + 1e-30
+    if base is not None:
+        base = base.double()
+        ref = ref + base
+        bound = bound + 2.0 ** -23 * (base.abs() + ref.abs())
+    err = (got.double() - ref).abs()
+    bad = (err > bound) | ~torch.isfinite(got)
+    assert not bool(bad.any()), "%s: %d of %d outside the fp32-accumulation bound (max err %.3e)" % (
+        name, int(bad.sum()), bad.numel(), float(err.max()))
+
+
+def test_gemm_bf16_nt_bias_accumulate(cuda):
+    from fast_b200 import ops
+    g = torch.Generator(device="cpu").manual_seed(3)
+    M, N, K = 1000, 200, 708
+    A = _bf(torch.randn(M, 712, generator=g)).to(cuda)[:, :K]
+    W = _bf(torch.randn(N, 712, generator=g) * 0.05).to(cuda)[:, :K]
+    bias = torch.randn(N, generator=g).to(cuda)
+    C0 = torch.randn(M, N, generator=g).to(cuda)
+    C = C0.clone()
+    ops.gemm_bf16_group([dict(kind=ops.NT, A=A, B=W, bias=bias, out=C, accumulate=True)])
+    torch.cuda.synchronize()
+    _check(C, A.double(), W.double().T, K, "NT", base=C0.double() + bias.double())
+
+
+def test_gemm_bf16_nt_concat_and_device_rows(cuda):
+    from fast_b200 import ops
+    g = torch.Generator(device="cpu").manual_seed(4)
+    M, D, dn = 777, 100, 413
+    agg = _bf(torch.randn(M, 104, generator=g)).to(cuda)
+    agg[:, D:] = float("nan")                  # past A's width (ka): must read as zeros
+    qin = _bf(torch.randn(M, 520, generator=g)).to(cuda)
+    W = torch.zeros(D, 104 + 416, dtype=torch.bfloat16, device=cuda)
+    W[:, :D] = _bf(torch.randn(D, D, generator=g) * 0.05).to(cuda)
+    W[:, 104:104 + dn] = _bf(torch.randn(D, dn, generator=g) * 0.05).to(cuda)
+    n_dev = torch.tensor([700], dtype=torch.int32, device=cuda)
+    C = torch.full((M, D), 7.0, device=cuda)
+    ops.gemm_bf16_group([dict(kind=ops.NT, A=agg[:, :D], A2=qin[:, :dn], k1=104, B=W[:, :104 + dn], out=C,
+                              M_dev=n_dev)])
+    torch.cuda.synchronize()
+    a64 = torch.cat([agg[:700, :D].double(), torch.zeros(700, 4, dtype=torch.float64, device=cuda),
+                     qin[:700, :dn].double()], 1)
+    _check(C[:700], a64, W[:, :104 + dn].double().T, 104 + dn, "NT concat")
+    assert bool((C[700:] == 7.0).all())
+
+
+def test_gemm_bf16_nn_on_weight_columns(cuda):
+    from fast_b200 import ops
+    g = torch.Generator(device="cpu").manual_seed(5)
+    M, K = 2500, 200
+    G = _bf(torch.randn(M, K, generator=g)).to(cuda)
+    Wf = _bf(torch.randn(K, 712, generator=g) * 0.05).to(cuda)
+    for c0, n in ((608, 100), (0, 413), (416, 186)):
+        B = Wf[:, c0:c0 + n]
+        C = torch.empty(M, n, device=cuda)
+        ops.gemm_bf16_group([dict(kind=ops.NN, A=G, B=B, out=C)])
+        torch.cuda.synchronize()
+        _check(C, G.double(), B.double(), K, "NN cols %d" % c0)
+
+
+@pytest.mark.parametrize("M,m_dev", [(3000, 2777), (70000, 70000), (20000, 1)])
+def test_gemm_bf16_tn_bias_gradient_masks_stale_rows(cuda, M, m_dev):
+    from fast_b200 import ops
+    g = torch.Generator(device="cpu").manual_seed(6)
+    N, K = 200, 413
+    G = _bf(torch.randn(M, N, generator=g)).to(cuda)
+    X = _bf(torch.randn(M, 712, generator=g)).to(cuda)
+    G[m_dev:] = float("nan")
+    X[m_dev:] = float("nan")
+    dW0 = torch.randn(N, K, generator=g).to(cuda)
+    dW = dW0.clone()
+    db = torch.zeros(N, device=cuda)
+    n_dev = torch.tensor([m_dev], dtype=torch.int32, device=cuda)
+    ops.gemm_bf16_group([dict(kind=ops.TN, A=G, B=X[:, :K], out=dW, accumulate=True, db=db, db_accumulate=False,
+                              M_dev=n_dev)])
+    torch.cuda.synchronize()
+    g64, x64 = G[:m_dev].double(), X[:m_dev, :K].double()
+    _check(dW, g64.T, x64, m_dev, "TN dW", base=dW0)
+    ones = torch.ones(m_dev, 1, dtype=torch.float64, device=cuda)
+    _check(db.reshape(-1, 1), g64.T, ones, m_dev, "TN db")
+
+
+def test_gemm_bf16_group_mixed(cuda):
+    """One launch: NT, NN and two TN problems, as a layer's backward level issues them."""
+    from fast_b200 import ops
+    g = torch.Generator(device="cpu").manual_seed(7)
+    M, D = 5000, 100
+    dKV = _bf(torch.randn(M, 2 * D, generator=g)).to(cuda)
+    X = _bf(torch.randn(M, 400, generator=g)).to(cuda)
+    W = _bf(torch.randn(2 * D, 400, generator=g) * 0.05).to(cuda)
+    gW = torch.zeros(2 * D, 396, device=cuda)
+    gb = torch.zeros(2 * D, device=cuda)
+    dt_ = torch.empty(M, 100, device=cuda)
+    dh = torch.empty(M, 100, device=cuda)
+    KV = torch.empty(M, 2 * D, device=cuda)
+    ops.gemm_bf16_group([dict(kind=ops.TN, A=dKV, B=X[:, :290], out=gW[:, :290]),
+                         dict(kind=ops.TN, A=dKV, B=X[:, 296:396], out=gW[:, 290:390], db=gb),
+                         dict(kind=ops.NN, A=dKV, B=W[:, 296:396], out=dt_),
+                         dict(kind=ops.NN, A=dKV, B=W[:, 0:100], out=dh),
+                         dict(kind=ops.NT, A=X[:, :396], B=W[:, :396], out=KV)])
+    torch.cuda.synchronize()
+    d64, x64, w64 = dKV.double(), X.double(), W.double()
+    _check(gW[:, :290], d64.T, x64[:, :290], M, "TN seg 0")
+    _check(gW[:, 290:390], d64.T, x64[:, 296:396], M, "TN seg 1")
+    _check(gb.reshape(-1, 1), d64.T, torch.ones(M, 1, dtype=torch.float64, device=cuda), M, "TN db")
+    _check(dt_, d64, w64[:, 296:396], 2 * D, "NN te")
+    _check(dh, d64, w64[:, :100], 2 * D, "NN h")
+    _check(KV, x64[:, :396], w64[:, :396].T, 396, "NT")
+
+
+def test_cast_bf16_is_round_to_nearest_even(cuda):
+    from fast_b200 import ops
+    g = torch.Generator(device="cpu").manual_seed(8)
+    W = torch.randn(200, 699, generator=g).to(cuda)
+    H = torch.randn(500, 100, generator=g).to(cuda)
+    Wb = torch.zeros(200, 712, dtype=torch.bfloat16, device=cuda)
+    Hb = torch.full((500, 104), 3.0, dtype=torch.bfloat16, device=cuda)
+    rows = torch.tensor([321], dtype=torch.int32, device=cuda)
+    ops.cast_bf16([(W[:, :413], Wb[:, :413]), (W[:, 413:599], Wb[:, 416:602]), (W[:, 599:], Wb[:, 608:708]),
+                   (H, Hb[:, :100], rows)])
+    torch.cuda.synchronize()
+    assert torch.equal(Wb[:, :413], W[:, :413].to(torch.bfloat16))
+    assert torch.equal(Wb[:, 416:602], W[:, 413:599].to(torch.bfloat16))
+    assert torch.equal(Wb[:, 608:708], W[:, 599:].to(torch.bfloat16))
+    assert bool((Wb[:, 413:416] == 0).all()) and bool((Wb[:, 602:608] == 0).all())
+    assert torch.equal(Hb[:321, :100], H[:321].to(torch.bfloat16))
+    assert bool((Hb[321:] == 3.0).all()) and bool((Hb[:, 100:] == 3.0).all())
+
+
+def test_gather_bf16_matches_rounded_fp32_gather(cuda):
+    from fast_b200 import ops
+    g = torch.Generator(device="cpu").manual_seed(9)
+    n_nodes, n_edges, dn, de, dtime, E = 300, 5000, 413, 186, 100, 4099
+    nf = torch.randn(n_nodes, dn, generator=g)
+    ef = torch.randn(n_edges, de, generator=g)
+    nf_b = torch.zeros(n_nodes, ops.pad8(dn), dtype=torch.bfloat16)
+    nf_b[:, :dn] = nf.to(torch.bfloat16)
+    ef_b = torch.zeros(n_edges, ops.pad8(de), dtype=torch.bfloat16)
+    ef_b[:, :de] = ef.to(torch.bfloat16)
+    nf_b, ef_b = nf_b.to(cuda), ef_b.to(cuda)
+    nid = torch.randint(0, n_nodes, (E,), generator=g, dtype=torch.int32).to(cuda)
+    eid = torch.randint(0, n_edges, (E,), generator=g, dtype=torch.int32).to(cuda)
+    dt = (torch.rand(E, generator=g) * 1e5).to(cuda)
+    w = torch.randn(dtime, generator=g).to(cuda)
+    b = torch.randn(dtime, generator=g).to(cuda)
+    X, width = ops.gather_time_encode_bf16(E, h=nf_b, h_idx=nid, f=ef_b, f_idx=eid, dt=dt, w=w, b=b, dn=dn, de=de)
+    ref = ops.gather_time_encode(E, dt=dt, w=w, b=b)             # fp32 cos(w dt + b) from the fp32 kernel
+    torch.cuda.synchronize()
+    assert width == 416 + 192 + 100 and X.shape[1] == 712
+    assert torch.equal(X[:, :416], nf_b[nid.long()])
+    assert torch.equal(X[:, 416:608], ef_b[eid.long()])
+    assert torch.equal(X[:, 608:708], ref.to(torch.bfloat16))
+    # fp32 source (a layer's output) with a device row count
+    h = torch.randn(E, 100, generator=g).to(cuda)
+    n_dev = torch.tensor([4000], dtype=torch.int32, device=cuda)
+    out = torch.full((E, 400), 5.0, dtype=torch.bfloat16, device=cuda)
+    ops.gather_time_encode_bf16(E, h=h, f=ef_b, f_idx=eid, dt=dt, w=w, b=b, de=de, out=out, n_rows_dev=n_dev)
+    torch.cuda.synchronize()
+    assert torch.equal(out[:4000, :100], h[:4000].to(torch.bfloat16))
+    assert bool((out[:4000, 100:104] == 0).all())
+    assert torch.equal(out[:4000, 104:296], ef_b[eid[:4000].long()])
+    assert torch.equal(out[:4000, 296:396], ref[:4000].to(torch.bfloat16))
+    assert bool((out[4000:] == 5.0).all())
+
+
+def test_attn_bwd_bf16kv_is_the_rounded_fp32_gradient(cuda):
+    from fast_b200 import ops
+    g = torch.Generator(device="cpu").manual_seed(10)
+    nd, fan, D, H = 2000, 10, 100, 2
+    E = nd * fan
+    rptr = torch.arange(0, E + 1, fan, dtype=torch.int32).to(cuda)
+    q = torch.randn(nd, D, generator=g).to(cuda)
+    kv = torch.randn(E, 2 * D, generator=g).to(cuda)
+    dagg = torch.randn(nd, D, generator=g).to(cuda)
+    agg, att = ops.attn_fwd(q, kv[:, :D], kv[:, D:], rptr, H, 0.2, 0.1, 11, 0)
+    dq, dkv = ops.attn_bwd(q, kv[:, :D], kv[:, D:], rptr, att, dagg, H, 0.2, 0.1, 11, 0)
+    dq_b, dkv_b = ops.attn_bwd_bf16kv(q, kv[:, :D], kv[:, D:], rptr, att, dagg, H, 0.2, 0.1, 11, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(dq_b, dq)
+    assert torch.equal(dkv_b, dkv.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("dn,de", [(413, 186), (0, 172)])
+def test_bf16_step_matches_fp64_oracle_to_bf16_accuracy(cuda, dn, de):
+    from conftest import small_graph
+    from fast_b200.engine import FusedStep
+    from fast_b200.ext import sampler_core
+    from fast_b200.model import DeviceBlock, GeneralModel
+    from fast_b200.train import _bf16_table
+    from oracle import ref_math
+    from oracle.sampler import OracleSampler
+    layers, fanout, n_nodes, n_edges = 2, [10, 10], 300, 30000
+    g = small_graph(n_nodes=n_nodes, n_edges=n_edges, seed=21, int_ts=False, t_max=2e4, zipf=1.0)
+    torch.manual_seed(1)
+    # features exactly representable in bf16, so the tables carry no rounding of their own
+    nf = torch.randn(n_nodes, dn).to(torch.bfloat16).float() if dn else None
+    ef = torch.randn(n_edges, de).to(torch.bfloat16).float()
+    sp = dict(layer=layers, neighbor=fanout, strategy="recent", prop_time=False, history=1, duration=0)
+    gnn = dict(arch="transformer_attention", layer=layers, att_head=2, dim_time=100, dim_out=100)
+    tr = dict(lr=1e-4, dropout=0.0, att_dropout=0.0)
+    m64 = GeneralModel(dn, de, sp, dict(type="none", dim_out=0), gnn, tr).double()
+    m_gpu = copy.deepcopy(m64).float().to(cuda)
+    eng = FusedStep(m_gpu, precision="bf16")
+    dev = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
+    smp = sampler_core.ParallelSampler(dev(g["indptr"]), dev(g["indices"]), dev(g["eid"]), dev(g["ts"]), 1, 1,
+                                       layers, fanout, True, False, 1, 0.0)
+    ora = OracleSampler(g["indptr"], g["indices"], g["eid"], g["ts"], 1, 1, layers, fanout, True, False, 1, 0.0)
+    nf_d = _bf16_table(nf.to(cuda), dn) if dn else None
+    ef_d = _bf16_table(ef.to(cuda), de)
+    rng = np.random.default_rng(0)
+    B = 200
+    for b0 in range(5000, 5000 + 3 * B, B):
+        src, dst, t = g["src"][b0:b0 + B], g["dst"][b0:b0 + B], g["t"][b0:b0 + B]
+        roots = np.concatenate([src, dst, rng.integers(0, n_nodes, B).astype(np.int32)])
+        rts = np.concatenate([t, t, t]).astype(np.float32)
+        smp.sample_device(dev(roots), dev(rts))
+        blocks = [DeviceBlock(v, d) for v, d in zip(smp.block_views(), smp.dims())]
+        ora.sample(roots, rts)
+        loss_g = torch.zeros((), device=cuda)
+        scores = torch.empty(2 * B, device=cuda)
+        eng.step(blocks, nf_d, ef_d, loss_g, scores=scores)
+        m64.zero_grad()
+        rp, rn = ref_math.model_forward(m64, ora.get_ret(), nf.double() if dn else None, ef.double())
+        loss = ref_math.bce_loss(rp, rn)
+        loss.backward()
+        torch.cuda.synchronize()
+        rel = lambda a, b: float((a.double().cpu() - b).norm() / (b.norm() + 1e-12))  # noqa: E731
+        assert rel(scores[:B], rp.detach().view(-1)) < 1e-2
+        assert rel(scores[B:], rn.detach().view(-1)) < 1e-2
+        assert abs(float(loss_g) - float(loss)) < 1e-2 * abs(float(loss))
+        errs = {name: rel(pg.grad, p64.grad) for (name, p64), pg in zip(m64.named_parameters(), m_gpu.parameters())
+                if p64.grad is not None}
+        print("bf16 relative L2 errors:", {k: round(v, 5) for k, v in errs.items()})
+        bad = {k: v for k, v in errs.items() if not v < 3e-2}
+        assert not bad, bad

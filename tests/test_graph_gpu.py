@@ -30,14 +30,16 @@ def _setup(cuda, t_max, strategy="uniform", att_dropout=0.2):
     return cfg, g, ef, sp, mp, gp, tp
 
 
-@pytest.mark.parametrize("fused", [True, False])
-def test_graph_replay_is_the_static_eager_step(cuda, fused):
+@pytest.mark.parametrize("mode", ["fused", "module", "fused_bf16"])
+def test_graph_replay_is_the_static_eager_step(cuda, mode):
     from fast_b200.train import GraphTrainer
     cfg, g, ef, sp, mp, gp, tp = _setup(cuda, 1e5)
+    fused = mode != "module"
     if fused:
         tp["dropout"] = 0.1            # keyed by the model's device counter, replay-safe
-    mk = lambda: GraphTrainer(g, None, ef, dict(sp), mp, dict(gp), tp, cuda, batch=cfg.batch, seed=5,
-                              sampler_seed=77, optimizer="sgd", fused=fused)
+    prec = "bf16" if mode == "fused_bf16" else "fp32"
+    mk = lambda: GraphTrainer(g, None, ef, dict(sp), mp, dict(gp), tp, cuda, batch=cfg.batch, seed=5,  # noqa: E731
+                              sampler_seed=77, optimizer="sgd", fused=fused, precision=prec)
     graph, static = mk(), mk()
     B = cfg.batch
     starts = [10000 + i * B for i in range(7)]
