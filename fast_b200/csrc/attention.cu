@@ -1040,8 +1040,10 @@ int check_attn(const AttnArgs &a, bool bwd) {
     if (!a.att_out || !a.agg || a.ldagg % 4 || !aligned16(a.agg))
       return fb::set_error(FB_ERR_ARG, "attn_fwd: bad att/agg output");
   } else {
-    if (!a.att || !a.dagg || a.lddagg % 4 || !aligned16(a.dagg) || a.lddkv % 4 || !aligned16(a.dk) ||
-        !aligned16(a.dv) || !aligned16(a.dq))
+    // fp32 gradient rows are stored as 16-byte words, bf16 ones as 8-byte words
+    const uintptr_t kv_mask = a.kv_bf16 ? 7u : 15u;
+    const bool kv_ok = ((reinterpret_cast<uintptr_t>(a.dk) | reinterpret_cast<uintptr_t>(a.dv)) & kv_mask) == 0;
+    if (!a.att || !a.dagg || a.lddagg % 4 || !aligned16(a.dagg) || a.lddkv % 4 || !kv_ok || !aligned16(a.dq))
       return fb::set_error(FB_ERR_ARG, "attn_bwd: bad gradient buffers");
   }
   return FB_OK;

@@ -110,10 +110,12 @@ def layer_forward(layer, row, col, dt, n_dst, h=None, f=None, att_mask=None):
     return layer.layer_norm(rst)
 
 
-def model_forward(model, blocks, node_feats=None, edge_feats=None, neg_samples=1):
+def model_forward(model, blocks, node_feats=None, edge_feats=None, neg_samples=1, layer_fn=None):
     """GeneralModel.forward (modules.py:48-70) for memory-less TGAT models.
     blocks: sampler blocks in get_ret() order (objects with row()/col()/eid()/
-    dts()/nodes()/dim_out() accessors returning numpy arrays)."""
+    dts()/nodes()/dim_out() accessors returning numpy arrays).  layer_fn
+    replaces layer_forward (the bf16-rounding restatement uses it)."""
+    layer_fn = layer_fn or layer_forward
     mfgs = list(reversed(blocks))
     h = None
     for l in range(model.gnn_param["layer"]):
@@ -130,7 +132,7 @@ def model_forward(model, blocks, node_feats=None, edge_feats=None, neg_samples=1
             hin = node_feats[torch.from_numpy(b.nodes()).long()].to(_dtype(layer)) if node_feats is not None else None
         else:
             hin = h
-        h = layer_forward(layer, row, col, dt, n_dst, h=hin, f=f)
+        h = layer_fn(layer, row, col, dt, n_dst, h=hin, f=f)
     return model.edge_predictor(h, neg_samples=neg_samples)
 
 

@@ -8,11 +8,16 @@
   device-side count hold NaN and must not reach the result.
 * fb_cast_bf16, fb_gather_time_encode_bf16 and fb_attn_bwd_bf16kv are
   bit-exact against round-to-nearest-even of the fp32 kernels' outputs.
-* A whole FusedStep in the bf16 mode against the fp64 run of the oracle
-  (oracle/ref_math.py on the oracle sampler's blocks): every output within
-  bf16 accuracy -- relative L2 error <= 3e-2 per gradient tensor, 1e-2 for
-  the loss and predictions -- with node / edge widths (413 / 186) that
-  exercise every padded segment.
+* A whole FusedStep in the bf16 mode against oracle/bf16_math.py: the
+  reference layer in fp64 with bf16 rounding at exactly the device's
+  rounding points, on the oracle sampler's blocks.  Relative L2 error
+  <= 2e-3 per gradient tensor and <= 1e-3 for the loss and predictions
+  (what remains is fp32 arithmetic and the rare operand that fp32 and fp64
+  round to neighbouring bf16 values), with node / edge widths (413 / 186)
+  that exercise every padded segment, on a model whose ReLU inputs sit away
+  from the kink.  The plain bf16 error against the exact fp64 reference is
+  reported beside it: at initialisation the positive and negative loss
+  gradients nearly cancel, which lifts it to several percent.
 """
 import copy
 
@@ -221,7 +226,7 @@ def test_bf16_step_matches_fp64_oracle_to_bf16_accuracy(cuda, dn, de):
     from fast_b200.ext import sampler_core
     from fast_b200.model import DeviceBlock, GeneralModel
     from fast_b200.train import _bf16_table
-    from oracle import ref_math
+    from oracle import bf16_math, ref_math
     from oracle.sampler import OracleSampler
     layers, fanout, n_nodes, n_edges = 2, [10, 10], 300, 30000
     g = small_graph(n_nodes=n_nodes, n_edges=n_edges, seed=21, int_ts=False, t_max=2e4, zipf=1.0)
@@ -233,6 +238,15 @@ def test_bf16_step_matches_fp64_oracle_to_bf16_accuracy(cuda, dn, de):
     gnn = dict(arch="transformer_attention", layer=layers, att_head=2, dim_time=100, dim_out=100)
     tr = dict(lr=1e-4, dropout=0.0, att_dropout=0.0)
     m64 = GeneralModel(dn, de, sp, dict(type="none", dim_out=0), gnn, tr).double()
+    # ReLU pre-activations away from the kink (biases of w_out and of the
+    # predictor's two projections + 4): at the kink the gradient jumps, and a
+    # 1e-4 forward difference (an operand that fp32 and fp64 round to
+    # neighbouring bf16 values) would switch a whole gradient term
+    with torch.no_grad():
+        for l in range(layers):
+            m64.layers["l%dh0" % l].w_out.bias += 4.0
+        m64.edge_predictor.src_fc.bias += 4.0
+        m64.edge_predictor.dst_fc.bias += 4.0
     m_gpu = copy.deepcopy(m64).float().to(cuda)
     eng = FusedStep(m_gpu, precision="bf16")
     dev = lambda a: torch.from_numpy(a).to(cuda)  # noqa: E731
@@ -253,17 +267,22 @@ def test_bf16_step_matches_fp64_oracle_to_bf16_accuracy(cuda, dn, de):
         loss_g = torch.zeros((), device=cuda)
         scores = torch.empty(2 * B, device=cuda)
         eng.step(blocks, nf_d, ef_d, loss_g, scores=scores)
-        m64.zero_grad()
-        rp, rn = ref_math.model_forward(m64, ora.get_ret(), nf.double() if dn else None, ef.double())
-        loss = ref_math.bce_loss(rp, rn)
-        loss.backward()
         torch.cuda.synchronize()
         rel = lambda a, b: float((a.double().cpu() - b).norm() / (b.norm() + 1e-12))  # noqa: E731
-        assert rel(scores[:B], rp.detach().view(-1)) < 1e-2
-        assert rel(scores[B:], rn.detach().view(-1)) < 1e-2
-        assert abs(float(loss_g) - float(loss)) < 1e-2 * abs(float(loss))
-        errs = {name: rel(pg.grad, p64.grad) for (name, p64), pg in zip(m64.named_parameters(), m_gpu.parameters())
-                if p64.grad is not None}
-        print("bf16 relative L2 errors:", {k: round(v, 5) for k, v in errs.items()})
-        bad = {k: v for k, v in errs.items() if not v < 3e-2}
+        out = {}
+        for tag, fn in (("bf16", bf16_math.layer_forward_bf16), ("exact", None)):
+            m64.zero_grad()
+            rp, rn = ref_math.model_forward(m64, ora.get_ret(), nf.double() if dn else None, ef.double(),
+                                            layer_fn=fn)
+            loss = ref_math.bce_loss(rp, rn)
+            loss.backward()
+            out[tag] = dict(pos=rel(scores[:B], rp.detach().view(-1)), neg=rel(scores[B:], rn.detach().view(-1)),
+                            loss=abs(float(loss_g) - float(loss)) / abs(float(loss)),
+                            **{n: rel(pg.grad, p64.grad) for (n, p64), pg in zip(m64.named_parameters(),
+                                                                                 m_gpu.parameters())
+                               if p64.grad is not None})
+        print("relative L2 error vs the bf16-rounding oracle:", {k: "%.1e" % v for k, v in out["bf16"].items()})
+        print("relative L2 error vs the exact fp64 reference:", {k: "%.1e" % v for k, v in out["exact"].items()})
+        bad = {k: v for k, v in out["bf16"].items() if not v < (1e-3 if k in ("pos", "neg", "loss") else 2e-3)}
         assert not bad, bad
+        assert max(out["exact"].values()) < 0.25      # sanity: bf16 accuracy, not another function
