@@ -435,9 +435,10 @@ def run_fast(args):
         roof = {"kernel": name, "bound": "tensor", "achieved": round(ach, 3), "peak": pk["tf"], "unit": "TFLOP/s",
                 "frac": round(ach / pk["tf"], 5), "traffic": None,
                 "peak_source": "%s bf16 burst (MEASURED_PEAKS.json)" % pk["src"],
-                "note": ("fp32-accurate products as three TF32 tcgen05 MMAs each (achieved counts 2MNK, "
-                         "not the 3x tensor work)" if args.gemm == "tc" else "fp32 products on the CUDA cores")
-                        + "; the bf16 tensor peak is the only measured compute denominator"}
+                "note": ("bf16 operands, fp32 accumulation (tcgen05 kind::f16)" if bf16 else
+                         ("fp32-accurate products as three TF32 tcgen05 MMAs each (achieved counts 2MNK, "
+                          "not the 3x tensor work)" if args.gemm == "tc" else "fp32 products on the CUDA cores")
+                         + "; the bf16 tensor peak is the only measured compute denominator")}
     else:
         ach = r["bytes"] / (r["ms"] / 1000.0) / 1e9
         roof = {"kernel": name, "bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm"], "unit": "GB/s",

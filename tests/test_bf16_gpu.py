@@ -11,7 +11,9 @@
 * A whole FusedStep in the bf16 mode against oracle/bf16_math.py: the
   reference layer in fp64 with bf16 rounding at exactly the device's
   rounding points, on the oracle sampler's blocks.  Relative L2 error
-  <= 2e-3 per gradient tensor and <= 1e-3 for the loss and predictions
+  <= 2e-3 per gradient tensor (the key and value biases as one vector: the
+  key bias's exact gradient nearly vanishes) and <= 1e-3 for the loss and
+  predictions
   (what remains is fp32 arithmetic and the rare operand that fp32 and fp64
   round to neighbouring bf16 values), with node / edge widths (413 / 186)
   that exercise every padded segment, on a model whose ReLU inputs sit away
@@ -219,6 +221,26 @@ def test_attn_bwd_bf16kv_is_the_rounded_fp32_gradient(cuda):
     assert torch.equal(dkv_b, dkv.to(torch.bfloat16))
 
 
+def _bound(name):
+    """Relative L2 bound against the bf16-rounding oracle."""
+    return 1e-3 if name in ("pos", "neg", "loss") else 2e-3
+
+
+def _kv_bias_joined(grads):
+    """w_k.bias and w_v.bias of each layer as one vector (the device computes
+    them as one bias gradient).  Alone, the key bias's gradient is no test:
+    adding a constant to every logit of a destination leaves its softmax
+    unchanged, so that gradient is zero but for the LeakyReLU's negative
+    side, and what is left is rounding noise of large sums."""
+    out = {}
+    for n, g in grads.items():
+        if n.endswith("w_k.bias"):
+            out[n[:-len("w_k.bias")] + "kv.bias"] = torch.cat([g, grads[n[:-len("k.bias")] + "v.bias"]])
+        elif not n.endswith("w_v.bias"):
+            out[n] = g
+    return out
+
+
 @pytest.mark.parametrize("dn,de", [(413, 186), (0, 172)])
 def test_bf16_step_matches_fp64_oracle_to_bf16_accuracy(cuda, dn, de):
     from conftest import small_graph
@@ -276,13 +298,15 @@ def test_bf16_step_matches_fp64_oracle_to_bf16_accuracy(cuda, dn, de):
                                             layer_fn=fn)
             loss = ref_math.bce_loss(rp, rn)
             loss.backward()
+            gd = _kv_bias_joined({n: pg.grad.double().cpu() for (n, p64), pg in zip(m64.named_parameters(),
+                                                                                   m_gpu.parameters())
+                                  if p64.grad is not None})
+            gr = _kv_bias_joined({n: p64.grad for n, p64 in m64.named_parameters() if p64.grad is not None})
             out[tag] = dict(pos=rel(scores[:B], rp.detach().view(-1)), neg=rel(scores[B:], rn.detach().view(-1)),
                             loss=abs(float(loss_g) - float(loss)) / abs(float(loss)),
-                            **{n: rel(pg.grad, p64.grad) for (n, p64), pg in zip(m64.named_parameters(),
-                                                                                 m_gpu.parameters())
-                               if p64.grad is not None})
+                            **{n: rel(gd[n], gr[n]) for n in gr})
         print("relative L2 error vs the bf16-rounding oracle:", {k: "%.1e" % v for k, v in out["bf16"].items()})
         print("relative L2 error vs the exact fp64 reference:", {k: "%.1e" % v for k, v in out["exact"].items()})
-        bad = {k: v for k, v in out["bf16"].items() if not v < (1e-3 if k in ("pos", "neg", "loss") else 2e-3)}
+        bad = {k: v for k, v in out["bf16"].items() if not v < _bound(k)}
         assert not bad, bad
         assert max(out["exact"].values()) < 0.25      # sanity: bf16 accuracy, not another function
