@@ -670,10 +670,10 @@ def run_bf16_suite(args):
     dkv = (torch.randn(E, 2 * D, device=dev, generator=g)).to(torch.bfloat16)
     gW = torch.zeros(2 * D, dn + de + dt_, device=dev)
     gb = torch.zeros(2 * D, device=dev)
-    tn = [dict(kind=ops.TN, A=dkv, B=X[:, h_at:h_at + dn], out=gW[:, :dn], accumulate=True),
-          dict(kind=ops.TN, A=dkv, B=X[:, f_at:f_at + de], out=gW[:, dn:dn + de], accumulate=True),
-          dict(kind=ops.TN, A=dkv, B=X[:, t_at:t_at + dt_], out=gW[:, dn + de:], accumulate=True, db=gb)]
-    timed("k_bf_group (K|V weight + bias gradient, TN x3)", E * (2 * K + 2 * 2 * D), 2 * E * 2 * D * (K + 1),
+    tn = [dict(kind=ops.TN, A=dkv, B=X[:, :K], out=gW, accumulate=True, db=gb,
+               segs=[(h_at, dn, 0), (f_at, de, dn), (t_at, dt_, dn + de)])]
+    timed("k_bf_group (K|V weight + bias gradient, TN over the row's 3 segments)", E * (2 * K + 2 * 2 * D),
+          2 * E * 2 * D * (dn + de + dt_ + 1),
           lambda: ops.gemm_bf16_group(tn), "M=%d, N=%d, K=%d+%d+%d+1" % (E, 2 * D, dn, de, dt_))
     dAt = torch.empty(E, dt_, device=dev)
     timed("k_bf_group (time-encoding input gradient, NN)", E * (2 * 2 * D + 4 * dt_), 2 * E * dt_ * 2 * D,

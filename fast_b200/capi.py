@@ -123,8 +123,10 @@ _SIGS["fb_gemm_group"] = (_I, [ctypes.POINTER(GemmProblem), _I, _P, _SZ, _P])
 
 class GemmBf16Problem(ctypes.Structure):
     """fb_gemm_bf16_problem (include/fast_b200.h): fb_gemm_problem's fields
-    (operand pointers to bf16) plus ka."""
-    _fields_ = GemmProblem._fields_ + [("ka", ctypes.c_int)]
+    (operand pointers to bf16) plus ka and the TN column segments."""
+    _fields_ = GemmProblem._fields_ + [("ka", ctypes.c_int), ("nseg", ctypes.c_int),
+                                       ("seg_at", ctypes.c_int * 3), ("seg_len", ctypes.c_int * 3),
+                                       ("seg_to", ctypes.c_int * 3)]
 
 
 _SIGS["fb_gemm_bf16_group_ws_bytes"] = (_SZ, [ctypes.POINTER(GemmBf16Problem), _I])

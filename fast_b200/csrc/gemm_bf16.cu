@@ -7,7 +7,13 @@
 //   NN: C[m, n] (+)= sum_k A[m, k] B[k, n] + bias[n]     A K-major, B MN-major
 //   TN: P[s][n, k] = sum_{m in split s} G[m, n] X[m, k]  G, X MN-major; a
 //       ones column of X at k = K gives the bias gradient; k_bf_reduce sums
-//       the splits in a fixed order into C (+ C) and db (+ db)
+//       the splits in a fixed order into C (+ C) and db (+ db).  With column
+//       segments of X (a weight gradient over a bf16 projection row whose
+//       segments sit at 8-column boundaries) the tile roles swap: X's columns
+//       run along the MMA's M side and G's (few) columns along N, so X
+//       streams through once instead of once per 128 columns of G; the bias
+//       gradient comes from a ones column on the M side, and the reduce
+//       writes P transposed through the segment map, skipping the gaps.
 //   NT / NN may take A as [A | A2] concatenated along K (k1 % 8 == 0).
 //
 // Operands are bf16 in global memory and reach the tensor cores untouched:
@@ -91,7 +97,10 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, bool mn) {
 
 struct BfProb {
   CUtensorMap ta, ta2, tb;   // A (TN: G), A2, B (TN: X)
+  // TN: P is [N rows][Kp cols] in the tiling's own orientation; ones = 1:
+  // the ones column is B's column K, 2: it is A's column N - 1 (swapped form)
   int kind, a_mn, b_mn, k1, K, N, Kp, bn, rt, nt, ones, accumulate, db_accumulate, max_splits;
+  int swap, ktot, nseg, seg_at[3], seg_len[3], seg_to[3];
   uint32_t idesc;
   int64_t M;
   const int32_t *M_dev;
@@ -146,9 +155,17 @@ __device__ __forceinline__ Item decode(const BfArgs &a, const int *st, const lon
 // TN slice fix-up by the MMA warp: rows >= valid of every MN-major box (A's
 // two, B's nbox) are cleared -- they lie past the split or past the
 // device-side row count, where memory may hold anything -- and column
-// `onescol` of B is set to 1 for the rows that count.  In a 128-byte
-// swizzled row, 16-byte chunk c sits at position c ^ (row & 7).
-__device__ __forceinline__ void fix_tn_slice(uint8_t *a, uint8_t *b, int nbox, int valid, int onescol, int lane) {
+// `onescol` of B (or `onescol_a` of A) is set to 1 for the rows that count.
+// In a 128-byte swizzled row, 16-byte chunk c sits at position c ^ (row & 7).
+__device__ __forceinline__ void set_ones(uint8_t *box0, int col, int valid, int lane) {
+  uint8_t *base = box0 + (col >> 6) * kBox;
+  const int c = col & 63;
+  for (int r = lane; r < valid; r += 32)
+    *reinterpret_cast<uint16_t *>(base + r * 128 + (((c >> 3) ^ (r & 7)) << 4) + (c & 7) * 2) = 0x3F80u;
+}
+
+__device__ __forceinline__ void fix_tn_slice(uint8_t *a, uint8_t *b, int nbox, int valid, int onescol, int onescol_a,
+                                             int lane) {
   if (valid < BK) {
     const int per_box = (BK - valid) * 8;    // 16-byte words to clear per box
     for (int t = lane; t < (2 + nbox) * per_box; t += 32) {
@@ -157,12 +174,8 @@ __device__ __forceinline__ void fix_tn_slice(uint8_t *a, uint8_t *b, int nbox, i
       reinterpret_cast<uint4 *>(base + valid * 128)[e] = make_uint4(0u, 0u, 0u, 0u);
     }
   }
-  if (onescol >= 0) {
-    uint8_t *base = b + (onescol >> 6) * kBox;
-    const int c = onescol & 63;
-    for (int r = lane; r < valid; r += 32)
-      *reinterpret_cast<uint16_t *>(base + r * 128 + (((c >> 3) ^ (r & 7)) << 4) + (c & 7) * 2) = 0x3F80u;
-  }
+  if (onescol >= 0) set_ones(b, onescol, valid, lane);
+  if (onescol_a >= 0) set_ones(a, onescol_a, valid, lane);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant__ BfArgs a) {
@@ -281,7 +294,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
       const bool tn = q.kind == kTN, amn = q.a_mn != 0, bmn = q.b_mn != 0;
       const uint32_t idesc = q.idesc;
       const int nbox = q.bn / 64;
-      const int onescol = (tn && q.ones && q.K >= it.c0 && q.K < it.c0 + q.bn) ? q.K - it.c0 : -1;
+      const int onescol = (tn && q.ones == 1 && q.K >= it.c0 && q.K < it.c0 + q.bn) ? q.K - it.c0 : -1;
+      const int64_t ones_row = (int64_t)q.N - 1 - it.r0;     // swapped form: A's ones column in this tile
+      const int onescol_a = (tn && q.ones == 2 && ones_row >= 0 && ones_row < BM) ? (int)ones_row : -1;
       const uint64_t adv_a = amn ? (2048 >> 4) : 2, adv_b = bmn ? (2048 >> 4) : 2;   // one K step of 16
       const int b = tc & 1;
       if (tc >= 2 && !mbar_wait(acce + b, ((tc >> 1) - 1) & 1, abort_flag, err)) break;
@@ -295,8 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
         if (tn) {
           const int64_t left = it.s1 - (it.s0 + (int64_t)BK * j);
           const int valid = left <= 0 ? 0 : (left >= BK ? BK : (int)left);
-          if (valid < BK || onescol >= 0) {
-            fix_tn_slice(sA(s), sB(s), nbox, valid, onescol, lane);
+          if (valid < BK || onescol >= 0 || onescol_a >= 0) {
+            fix_tn_slice(sA(s), sB(s), nbox, valid, onescol, onescol_a, lane);
             fence_async_smem();
           }
           __syncwarp();
@@ -411,6 +426,24 @@ __global__ void k_bf_reduce(const __grid_constant__ BfArgs a) {
     for (int u = 0; u < 8; ++u) s += v[u];
   }
   for (; z < ns; ++z) s += part[(int64_t)z * stride];
+  if (q.swap) {
+    // P row n = column n of X, P column k = column k of G: C[k, map(n)], db[k]
+    float *c;
+    int acc;
+    if (q.ones == 2 && n == q.ktot) {
+      c = q.db + k;
+      acc = q.db_accumulate;
+    } else {
+      int col = -1;
+      for (int g = 0; g < q.nseg; ++g)
+        if (n >= q.seg_at[g] && n < q.seg_at[g] + q.seg_len[g]) col = q.seg_to[g] + (n - q.seg_at[g]);
+      if (col < 0) return;                   // a gap between segments
+      c = q.C + (int64_t)k * q.ldc + col;
+      acc = q.accumulate;
+    }
+    *c = acc ? (*c + s) : s;
+    return;
+  }
   float *c = (k < q.K) ? q.C + (int64_t)n * q.ldc + k : q.db + n;
   const int acc = (k < q.K) ? q.accumulate : q.db_accumulate;
   *c = acc ? (*c + s) : s;
@@ -457,9 +490,21 @@ uint32_t idesc_bf16(int bn, int a_mn, int b_mn) {
          ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
+// TN tiling: rows x cols of P (the swapped form when X comes in segments).
+void tn_dims(const fb_gemm_bf16_problem &p, int &rows, int &cols) {
+  if (p.nseg > 0) {
+    rows = p.K + (p.db ? 1 : 0);
+    cols = p.N;
+  } else {
+    rows = p.N;
+    cols = p.K + (p.db ? 1 : 0);
+  }
+}
+
 int tn_splits_max(const fb_gemm_bf16_problem &p) {
-  const int Kp = p.K + (p.db ? 1 : 0);
-  const int tiles = ((p.N + BM - 1) / BM) * ((Kp + bn_mnmajor(Kp) - 1) / bn_mnmajor(Kp));
+  int rows, cols;
+  tn_dims(p, rows, cols);
+  const int tiles = ((rows + BM - 1) / BM) * ((cols + bn_mnmajor(cols) - 1) / bn_mnmajor(cols));
   return std::max(1, num_sms() / std::max(tiles, 1));
 }
 
@@ -476,7 +521,16 @@ bool problem_ok(const fb_gemm_bf16_problem &p) {
   if (p.kind < FB_GEMM_NT || p.kind > FB_GEMM_TN) return false;
   if (p.M < 0 || p.M > (int64_t)1 << 30 || p.N < 1 || p.K < 1) return false;
   if (!p.A || !al16(p.A) || p.lda % 8 || !p.B || !al16(p.B) || p.ldb % 8) return false;
-  if (p.kind == FB_GEMM_TN) return p.lda >= p.N && p.ldb >= p.K && (p.C || p.K == 0) && p.ldc >= p.K;
+  if (p.kind == FB_GEMM_TN) {
+    if (p.nseg < 0 || p.nseg > 3 || p.lda < p.N || p.ldb < p.K || !p.C) return false;
+    if (p.nseg == 0) return p.ldc >= p.K;
+    int end = 0;
+    for (int g = 0; g < p.nseg; ++g) {
+      if (p.seg_len[g] < 1 || p.seg_at[g] < end || p.seg_to[g] < 0 || p.seg_to[g] + p.seg_len[g] > p.ldc) return false;
+      end = p.seg_at[g] + p.seg_len[g];
+    }
+    return end <= p.K;
+  }
   if (!p.C || p.ldc < p.N || p.ldb < (p.kind == FB_GEMM_NT ? p.K : p.N)) return false;
   if (p.A2 && p.k1 < p.K) {
     const int ka = p.ka > 0 ? p.ka : p.k1;
@@ -488,9 +542,10 @@ bool problem_ok(const fb_gemm_bf16_problem &p) {
 
 int64_t ws_floats(const fb_gemm_bf16_problem &p) {
   if (p.kind != FB_GEMM_TN || p.M < 1) return 0;
-  const int Kp = p.K + (p.db ? 1 : 0);
+  int rows, cols;
+  tn_dims(p, rows, cols);
   const int64_t ns = fb::tn_parts(p.M, kTnRowsMin, tn_splits_max(p));
-  return (ns * (int64_t)p.N * Kp + 63) / 64 * 64;
+  return (ns * (int64_t)rows * cols + 63) / 64 * 64;
 }
 
 int build_prob(BfProb &q, const fb_gemm_bf16_problem &p, float *ws) {
@@ -504,7 +559,32 @@ int build_prob(BfProb &q, const fb_gemm_bf16_problem &p, float *ws) {
   q.C = p.C;
   q.ldc = p.ldc;
   int rc;
-  if (p.kind == FB_GEMM_TN) {
+  if (p.kind == FB_GEMM_TN && p.nseg > 0) {
+    // swapped form: the tile's rows are X's columns (+ the ones row), its
+    // columns are G's; A of the tiling is X, B is G
+    q.swap = 1;
+    q.a_mn = q.b_mn = 1;
+    q.ktot = p.K;
+    q.ones = p.db ? 2 : 0;
+    q.N = p.K + (p.db ? 1 : 0);
+    q.K = p.N;
+    q.Kp = p.N;
+    q.bn = bn_mnmajor(q.Kp);
+    q.rt = (q.N + BM - 1) / BM;
+    q.nt = (q.Kp + q.bn - 1) / q.bn;
+    q.db = p.db;
+    q.db_accumulate = p.db_accumulate;
+    q.P = ws;
+    q.max_splits = tn_splits_max(p);
+    q.nseg = p.nseg;
+    for (int g = 0; g < p.nseg; ++g) {
+      q.seg_at[g] = p.seg_at[g];
+      q.seg_len[g] = p.seg_len[g];
+      q.seg_to[g] = p.seg_to[g];
+    }
+    if ((rc = make_map(&q.ta, p.B, p.M, p.K, p.ldb, BK))) return rc;
+    if ((rc = make_map(&q.tb, p.A, p.M, p.N, p.lda, BK))) return rc;
+  } else if (p.kind == FB_GEMM_TN) {
     q.a_mn = q.b_mn = 1;
     q.ones = p.db ? 1 : 0;
     q.Kp = p.K + q.ones;

@@ -262,11 +262,10 @@ class FusedStep:
                                       offset_dev=st["offset_dev"])
         X = st["A"]
         v = torch.empty(D, device=dev)            # sum over rows of dQ
-        probs = []
-        last = len(lp.kv_segs) - 1
-        for i, (at, lo, d) in enumerate(lp.kv_segs):
-            probs.append(dict(kind=ops.TN, A=dKV, B=X[:, at:at + d], out=lp.gW_kv[:, lo:lo + d], accumulate=True,
-                              M_dev=E_dev, db=lp.gb_kv if i == last else None))
+        # the K|V weight and bias gradient over the whole projection row: one
+        # TN problem, X's segments mapped to the weight's columns
+        probs = [dict(kind=ops.TN, A=dKV, B=X[:, :lp.kx], out=lp.gW_kv, accumulate=True, M_dev=E_dev,
+                      db=lp.gb_kv, segs=[(at, d, lo) for at, lo, d in lp.kv_segs])]
         if dh is not None:
             probs.append(dict(kind=ops.NN, A=dKV, B=lp.W_kv_bf[:, :dn], out=dh[nd:nd + E], M_dev=E_dev))
         dA_t = None
@@ -278,10 +277,8 @@ class FusedStep:
             dQ_bf = torch.empty(nd, lp.ka, device=dev, dtype=torch.bfloat16)
             ops.cast_bf16([(dQ, dQ_bf[:, :D], nd_dev)])
             dQb = dQ_bf[:, :D]
-            last = len(lp.q_segs) - 1
-            for i, (at, lo, d) in enumerate(lp.q_segs):
-                probs.append(dict(kind=ops.TN, A=dQb, B=Qin[:, at:at + d], out=g(L.w_q.weight)[:, lo:lo + d],
-                                  accumulate=True, M_dev=nd_dev, db=v if i == last else None, db_accumulate=False))
+            probs.append(dict(kind=ops.TN, A=dQb, B=Qin[:, :lp.kq], out=g(L.w_q.weight), accumulate=True,
+                              M_dev=nd_dev, db=v, db_accumulate=False, segs=[(at, d, lo) for at, lo, d in lp.q_segs]))
             if dh is not None:
                 probs.append(dict(kind=ops.NN, A=dQb, B=lp.W_q_bf[:, :dn], out=dh[:nd], accumulate=True,
                                   M_dev=nd_dev))

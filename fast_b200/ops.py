@@ -6,6 +6,7 @@ Every wrapper launches on torch's current CUDA stream through the C ABI
 allocator.  Inputs must be fp32 (int32 for ids) with unit column stride.
 """
 import contextlib
+import ctypes
 
 import torch
 
@@ -215,7 +216,9 @@ def gemm_bf16_group(problems, name="gemm_bf16_group"):
     fp32) on the tcgen05 kind::f16 kernel: products of bf16 values
     accumulated in fp32.  Same problem dicts as gemm_group (B required); with
     A2, k1 (a multiple of 8, >= A's width) is the column of B where A2's
-    block starts."""
+    block starts.  A TN problem may give segs = [(at, len, to), ...]: B's
+    columns [at, at + len) land in out's columns from `to`, the rest of B's
+    columns are skipped (a weight gradient over a bf16 projection row)."""
     from .capi import GemmBf16Problem
     arr = (GemmBf16Problem * len(problems))()
     nbytes, flops = 0, 0
@@ -240,10 +243,15 @@ def gemm_bf16_group(problems, name="gemm_bf16_group"):
         db = p.get("db")
         acc = int(bool(p.get("accumulate", False)))
         dba = p.get("db_accumulate")
+        segs = p.get("segs") or ()
+        if len(segs) > 3:
+            raise ValueError("gemm_bf16_group: at most 3 column segments")
+        pad3 = lambda v: (ctypes.c_int * 3)(*(list(v) + [0] * (3 - len(v))))  # noqa: E731
         arr[i] = GemmBf16Problem(kind, ptr(A), A.stride(0), ptr(A2), 0 if A2 is None else A2.stride(0), k1,
                                  ptr(B), B.stride(0), ptr(p.get("bias")), ptr(out), out.stride(0),
                                  M, _p(p.get("M_dev")), N, K, acc, ptr(db), int(acc if dba is None else bool(dba)),
-                                 A.shape[1] if A2 is not None else 0)
+                                 A.shape[1] if A2 is not None else 0, len(segs), pad3([g[0] for g in segs]),
+                                 pad3([g[1] for g in segs]), pad3([g[2] for g in segs]))
         keep.append((A, B, A2, out, db))
         nbytes += 2 * (M * K + N * K) + 4 * M * N
         flops += 2 * M * N * K

@@ -325,6 +325,13 @@ typedef struct fb_gemm_bf16_problem {
   int ka;        /* NT / NN with A2: data columns of A (<= k1; 0 means k1); A's
                     columns [ka, k1) read as zeros, so k1 can round A's width up
                     to the 8-column boundary where A2's block of B starts */
+  int nseg;      /* TN only, 0..3: X's columns come in segments -- columns
+                    [seg_at[i], seg_at[i] + seg_len[i]) land in C's columns from
+                    seg_to[i] (ascending, within [0, K)); columns of X outside
+                    them are skipped.  The weight gradient over a bf16
+                    projection row in one problem; the kernel then tiles X's
+                    columns along the MMA's M side, which reads X once */
+  int seg_at[3], seg_len[3], seg_to[3];
 } fb_gemm_bf16_problem;
 size_t fb_gemm_bf16_group_ws_bytes(const fb_gemm_bf16_problem *probs, int n);
 int fb_gemm_bf16_group(const fb_gemm_bf16_problem *probs, int n, void *ws, size_t ws_bytes, cudaStream_t stream);

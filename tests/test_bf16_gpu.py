@@ -121,6 +121,37 @@ def test_gemm_bf16_tn_bias_gradient_masks_stale_rows(cuda, M, m_dev):
     _check(db.reshape(-1, 1), g64.T, ones, m_dev, "TN db")
 
 
+@pytest.mark.parametrize("M,m_dev", [(5000, 4321), (200000, 200000)])
+def test_gemm_bf16_tn_column_segments(cuda, M, m_dev):
+    """The K|V weight gradient over a bf16 projection row in one TN problem:
+    X's columns in three segments at 8-column boundaries (the gaps hold NaN
+    and are skipped), the bias gradient, accumulate; rows past the device
+    count hold NaN."""
+    from fast_b200 import ops
+    g = torch.Generator(device="cpu").manual_seed(12)
+    N, segs = 200, [(0, 413, 0), (416, 186, 413), (608, 100, 599)]
+    G = _bf(torch.randn(M, N, generator=g)).to(cuda)
+    X = _bf(torch.randn(M, 712, generator=g)).to(cuda)
+    X[:, 413:416] = float("nan")
+    X[:, 602:608] = float("nan")
+    G[m_dev:] = float("nan")
+    X[m_dev:] = float("nan")
+    dW0 = torch.randn(N, 699, generator=g).to(cuda)
+    dW = dW0.clone()
+    db0 = torch.randn(N, generator=g).to(cuda)
+    db = db0.clone()
+    n_dev = torch.tensor([m_dev], dtype=torch.int32, device=cuda)
+    ops.gemm_bf16_group([dict(kind=ops.TN, A=G, B=X[:, :708], out=dW, accumulate=True, db=db, M_dev=n_dev,
+                              segs=segs)])
+    torch.cuda.synchronize()
+    g64 = G[:m_dev].double()
+    for at, ln, to in segs:
+        _check(dW[:, to:to + ln], g64.T, X[:m_dev, at:at + ln].double(), m_dev, "TN seg %d" % at,
+               base=dW0[:, to:to + ln])
+    _check(db.reshape(-1, 1), g64.T, torch.ones(m_dev, 1, dtype=torch.float64, device=cuda), m_dev, "TN db",
+           base=db0.reshape(-1, 1))
+
+
 def test_gemm_bf16_group_mixed(cuda):
     """One launch: NT, NN and two TN problems, as a layer's backward level issues them."""
     from fast_b200 import ops
