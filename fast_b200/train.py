@@ -9,7 +9,10 @@ sizes (and, in the end-to-end mode, the batch upload and the loss readback).
 Data parallelism: each rank takes a contiguous slice of every chronological
 batch, gradients are averaged with one NCCL all-reduce over a single flat
 bucket.  Equal slices make the averaged gradient the gradient of the global
-batch loss (mean_pos + mean_neg, train.py:373-374).
+batch loss (mean_pos + mean_neg, train.py:373-374).  A memory model (TGN)
+keeps the whole node memory on every rank; after each step one all_gather
+brings every rank's updated memory rows, and every rank writes them in the
+global batch's order, as one process would.
 """
 import numpy as np
 import torch
@@ -45,6 +48,30 @@ def average_gradients(params, world, flat=None):
         g.copy_(flat[off:off + g.numel()].view_as(g))
         off += g.numel()
     return flat
+
+
+def gather_global_order(local, world, out=None, perm=None):
+    """All ranks' rows of a per-rank list [src_r | dst_r | neg_r] (3 equal
+    sections of this rank's slice), returned in the global batch's order
+    [src | dst | neg] -- the order one process training on the whole batch
+    sees.  One all_gather (NCCL on GPUs, gloo on CPUs), then a permutation.
+    out / perm: buffers of a previous call with the same shape, reused."""
+    R = local.shape[0]
+    Br = R // 3
+    gathered = torch.empty((world * R,) + tuple(local.shape[1:]), device=local.device, dtype=local.dtype)
+    if dist.get_backend() == "nccl":
+        dist.all_gather_into_tensor(gathered, local.contiguous())
+    else:
+        parts = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(parts, local.contiguous())
+        torch.cat(parts, out=gathered)
+    if perm is None:
+        # global position s*(world*Br) + r*Br + i <- gathered position r*R + s*Br + i
+        perm = torch.arange(world * R, device=local.device).view(world, 3, Br).transpose(0, 1).reshape(-1)
+    if out is None:
+        out = torch.empty_like(gathered)
+    torch.index_select(gathered, 0, perm, out=out)
+    return out, perm
 
 
 def _bf16_table(t, width):
@@ -87,8 +114,11 @@ class Trainer:
         self.node_feats, self.edge_feats = node_feats, edge_feats
         self.mailbox = None
         if memory_param.get("type", "none") != "none":
-            if not fused or world > 1:
-                raise NotImplementedError("node memory trains through FusedStep on one GPU")
+            if not fused:
+                raise NotImplementedError("node memory trains through FusedStep")
+            if world > 1 and memory_param.get("deliver_to") != "self":
+                raise NotImplementedError("data-parallel node memory covers mails delivered to the roots "
+                                          "themselves (deliver_to: self, TGN)")
             self.model = MemoryModel(dn, de, sample_param, memory_param, gnn_param, train_param).to(self.device)
             self.mailbox = MailBox(memory_param, graph.n_nodes, de, self.device)
         else:
@@ -187,7 +217,25 @@ class Trainer:
         if self.mailbox is None:
             return
         R = roots.shape[0]
-        self.mailbox.update(roots, root_ts, self.engine.last_memory[:R], self.edge_feats, self.e0_buf, block=blocks[0])
+        h = self.engine.last_memory[:R]
+        if self.world > 1:
+            # every rank keeps the whole memory: all ranks' updates, applied
+            # in the global batch's order, keep the replicas equal to the
+            # tables of one process training on the global batch
+            roots, root_ts, h = self._memory_exchange(roots, root_ts, h)
+        self.mailbox.update(roots, root_ts, h, self.edge_feats, self.e0_buf, block=blocks[0])
+
+    def _memory_exchange(self, roots, root_ts, h):
+        """All ranks' (roots, times, updated memory) in the global order."""
+        bufs = getattr(self, "_xbufs", None)
+        if bufs is None or bufs[0][0].numel() != self.world * roots.shape[0]:
+            bufs = [(None, None)] * 3
+        res = []
+        for i, t in enumerate((roots, root_ts, h)):
+            out, perm = gather_global_order(t, self.world, out=bufs[i][0], perm=bufs[i][1])
+            res.append((out, perm))
+        self._xbufs = res
+        return res[0][0], res[1][0], res[2][0]
 
     def _sample_roots(self, roots, root_ts):
         """The roots the sampler sees: with no_neg (APAN, train.py:323-325) only
@@ -325,7 +373,13 @@ class GraphTrainer(Trainer):
         if self.world > 1:
             self._flat.div_(self.world)
         self.opt.step()
-        if self.mailbox is not None:
+        if self.mailbox is not None and self.world == 1:
+            self._update_memory(self._blocks, self.roots_buf, self.ts_buf)
+
+    def _memory_ranks(self):
+        """Several ranks: the memory exchange (NCCL) and writes, after the
+        optimizer graph and outside every captured graph."""
+        if self.mailbox is not None and self.world > 1:
             self._update_memory(self._blocks, self.roots_buf, self.ts_buf)
 
     def _eager_step(self):
@@ -333,6 +387,7 @@ class GraphTrainer(Trainer):
         if self.world > 1:
             dist.all_reduce(self._flat)
         self._apply()
+        self._memory_ranks()
 
     def capture(self, warmup=3):
         """Warm up on a side stream (allocator, lazy kernel loads, Adam state),
@@ -361,6 +416,7 @@ class GraphTrainer(Trainer):
         if self.world > 1:
             dist.all_reduce(self._flat)
             self.g_opt.replay()
+            self._memory_ranks()
 
     def load_device_roots(self, b0, b1):
         """Fills the input buffers with this rank's slice of the global batch

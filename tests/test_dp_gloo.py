@@ -7,6 +7,9 @@
 * Failure detection without a GPU: a rank that raises before the collective
   makes its peer's all-reduce end with an error under a short process-group
   timeout, instead of hanging.
+* The node-memory exchange of data-parallel TGN (gather_global_order): every
+  rank's [src_r | dst_r | neg_r] rows come back in the global batch's order
+  [src | dst | neg], on every rank, for id, time and memory-row tensors.
 """
 import os
 import socket
@@ -105,3 +108,36 @@ def test_dp_failed_rank_is_detected(tmp_path):
     assert (tmp_path / "status1.txt").read_text().startswith("error: injected failure")
     s0 = (tmp_path / "status0.txt").read_text()
     assert s0.startswith("error"), s0      # the peer's all-reduce ended with an error, it did not hang
+
+
+def _gather_worker(rank, world, port, outdir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    try:
+        sys.path.insert(0, ROOT)
+        from fast_b200.train import gather_global_order
+        gB = 12
+        roots = torch.arange(3 * gB, dtype=torch.int32) * 7 + 1        # a global [src | dst | neg] list
+        ts = roots.float() / 3
+        h = torch.stack([roots.float(), -roots.float()], 1)
+        per = gB // world
+        pick = lambda a: torch.cat([a[s * gB + rank * per:s * gB + (rank + 1) * per] for s in range(3)])  # noqa: E731
+        outs = [gather_global_order(pick(t), world)[0] for t in (roots, ts, h)]
+        ok = all(torch.equal(o, t) for o, t in zip(outs, (roots, ts, h)))
+        # a second call reusing the buffers
+        o2, _ = gather_global_order(pick(roots), world, out=torch.empty_like(roots), perm=None)
+        ok = ok and torch.equal(o2, roots)
+        status = "ok" if ok else "mismatch"
+    except Exception as e:
+        status = "error: " + str(e)[:200]
+    with open(os.path.join(outdir, "gather%d.txt" % rank), "w") as f:
+        f.write(status)
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_memory_exchange_restores_global_order(tmp_path, world):
+    mp.spawn(_gather_worker, args=(world, _port(), str(tmp_path)), nprocs=world, join=True)
+    for r in range(world):
+        assert (tmp_path / ("gather%d.txt" % r)).read_text() == "ok"

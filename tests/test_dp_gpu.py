@@ -10,6 +10,12 @@ all-reduce of the flat gradient buffer.  With recent sampling and one layer
 the sampled blocks are then exactly the single process's, so losses and
 parameters agree to fp32 rounding.  (With two or more recent layers the
 deeper layers' pointer updates see only the rank's own hop-1 nodes.)
+
+TGN-1 (GRU node memory, mails to the roots themselves) the same way: every
+rank keeps the whole memory and, after each step, writes all ranks' updated
+rows in the global batch's order (one NCCL all_gather), so the memory and
+mailbox tables, their timestamps, the losses and the parameters agree with
+one process training on the global batch.
 """
 import os
 import socket
@@ -97,3 +103,61 @@ def test_dp_two_ranks_equal_single_process(tmp_path):
     dp_params = np.load(tmp_path / "dp_params.npy")
     np.testing.assert_allclose(dp, single, rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(dp_params, params, rtol=1e-4, atol=1e-6)
+
+
+def _setup_tgn(dev):
+    cfg, g, ef, sp, mp_, gp, tp = _setup(dev)
+    mp_ = dict(type="node", dim_time=100, deliver_to="self", mail_combine="last", memory_update="gru",
+               mailbox_size=1, combine_node_feature=True, dim_out=100)
+    return cfg, g, ef, sp, mp_, gp, tp
+
+
+def _tgn_state(tr):
+    mb = tr.mailbox
+    return dict(params=torch.cat([p.detach().reshape(-1) for p in tr.model.parameters()]).cpu().numpy(),
+                **{k: getattr(mb, k).detach().cpu().numpy() for k in ("node_memory", "node_memory_ts", "mailbox",
+                                                                      "mailbox_ts")})
+
+
+def _tgn_worker(rank, world, port, outdir):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from fast_b200.train import GraphTrainer
+        cfg, g, ef, sp, mp_, gp, tp = _setup_tgn(dev)
+        gB = 128
+        tr = GraphTrainer(g, None, ef, sp, mp_, dict(gp), tp, dev, batch=gB // world, rank=rank, world=world,
+                          seed=5, sampler_seed=77, optimizer="sgd")
+        losses = _run(tr, gB)
+        t = torch.tensor(losses, device=dev)
+        dist.all_reduce(t)
+        st = _tgn_state(tr)
+        tr.g_main = tr.g_opt = None          # release graphs before tearing down NCCL
+        torch.cuda.synchronize()
+        np.savez(os.path.join(outdir, "tgn_rank%d.npz" % rank), loss=(t / world).cpu().numpy(), **st)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_dp_tgn_memory_two_ranks_equal_single_process(tmp_path):
+    import torch.multiprocessing as mp
+    mp.spawn(_tgn_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
+    from fast_b200.train import GraphTrainer
+    dev = torch.device("cuda", 0)
+    cfg, g, ef, sp, mp_, gp, tp = _setup_tgn(dev)
+    tr = GraphTrainer(g, None, ef, sp, mp_, dict(gp), tp, dev, batch=128, seed=5, sampler_seed=77, optimizer="sgd")
+    single = np.array(_run(tr, 128))
+    ref = _tgn_state(tr)
+    r0, r1 = (np.load(tmp_path / ("tgn_rank%d.npz" % r)) for r in range(2))
+    np.testing.assert_allclose(r0["loss"], single, rtol=1e-5, atol=1e-6)
+    for k in ("node_memory_ts", "mailbox_ts"):
+        assert np.array_equal(r0[k], ref[k]) and np.array_equal(r1[k], ref[k]), k
+    for k in ("node_memory", "mailbox", "params"):
+        assert np.array_equal(r0[k], r1[k]), k           # the replicas stay identical
+        np.testing.assert_allclose(r0[k], ref[k], rtol=1e-4, atol=1e-5, err_msg=k)
