@@ -45,41 +45,44 @@ struct GatherArgs {
   float *A; int64_t lda; int64_t n_rows; const int32_t *n_rows_dev;
 };
 
-// Batched form for 16-byte rows: a warp takes kBatch rows at a time, loads
+// Batched form for 16-byte rows: a warp takes NB rows at a time, loads
 // their ids (one lane each), then issues every 16-byte load of the batch's
-// source rows before any store, so kBatch rows are in flight per warp instead
-// of one.  Rows up to 512 floats per source table.
-constexpr int kBatch = 4;
+// source rows before any store, so NB rows are in flight per warp instead
+// of one.  NCH 16-byte chunks per lane cover a source row of up to
+// 128 NCH floats.  (Eight rows in flight measured slower than four.)
+constexpr int kBatch = 4;                     // rows per batch of the bf16 gather
 constexpr int kMaxChunks = 4;                 // 16-byte chunks per lane per source row
 
-__device__ __forceinline__ void gather_rows(const float *__restrict__ src, int64_t ld, const int64_t (&row)[kBatch],
+template <int NB, int NCH>
+__device__ __forceinline__ void gather_rows(const float *__restrict__ src, int64_t ld, const int64_t (&row)[NB],
                                             int nb, int nq, float *__restrict__ out0, int64_t lda, int lane) {
-  float4 v[kBatch][kMaxChunks];
+  float4 v[NB][NCH];
 #pragma unroll
-  for (int i = 0; i < kBatch; ++i)
+  for (int i = 0; i < NB; ++i)
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
+    for (int c = 0; c < NCH; ++c) {
       const int q = lane + 32 * c;
       v[i][c] = (i < nb && q < nq) ? __ldg(reinterpret_cast<const float4 *>(src + row[i] * ld) + q)
                                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
-  for (int i = 0; i < kBatch; ++i)
+  for (int i = 0; i < NB; ++i)
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
+    for (int c = 0; c < NCH; ++c) {
       const int q = lane + 32 * c;
       if (i < nb && q < nq) reinterpret_cast<float4 *>(out0 + i * lda)[q] = v[i][c];
     }
 }
 
+template <int NB, int NCH>
 __global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode_batched(GatherArgs a) {
   fb::pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t n = a.n_rows_dev ? min((int64_t)(*a.n_rows_dev), a.n_rows) : a.n_rows;
   const int64_t h_off = a.h_off + (a.h_off_dev ? (int64_t)(*a.h_off_dev) : 0);
-  const int64_t step = (int64_t)gridDim.x * kRowsPerCta * kBatch;
-  for (int64_t r0 = ((int64_t)blockIdx.x * kRowsPerCta + (threadIdx.x >> 5)) * kBatch; r0 < n; r0 += step) {
-    const int nb = (int)min((int64_t)kBatch, n - r0);
+  const int64_t step = (int64_t)gridDim.x * kRowsPerCta * NB;
+  for (int64_t r0 = ((int64_t)blockIdx.x * kRowsPerCta + (threadIdx.x >> 5)) * NB; r0 < n; r0 += step) {
+    const int nb = (int)min((int64_t)NB, n - r0);
     // ids and times of the batch: lane i loads row r0 + i's, then broadcast
     int64_t hid = 0, fid = 0;
     float tt = 0.f;
@@ -89,23 +92,38 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode_batched
       fid = a.f_idx ? (int64_t)a.f_idx[r] : r;
       tt = a.dt ? a.dt[r] : 0.f;
     }
-    int64_t hr[kBatch], fr[kBatch];
-    float t[kBatch];
+    int64_t hr[NB], fr[NB];
+    float t[NB];
 #pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
+    for (int i = 0; i < NB; ++i) {
       hr[i] = __shfl_sync(0xffffffffu, hid, i);
       fr[i] = __shfl_sync(0xffffffffu, fid, i);
       t[i] = __shfl_sync(0xffffffffu, tt, i);
     }
     float *out0 = a.A + r0 * a.lda;
-    if (a.dn > 0) gather_rows(a.h, a.ldh, hr, nb, a.dn / 4, out0, a.lda, lane);
-    if (a.de > 0) gather_rows(a.f, a.ldf, fr, nb, a.de / 4, out0 + a.dn, a.lda, lane);
+    if (a.dn > 0) gather_rows<NB, NCH>(a.h, a.ldh, hr, nb, a.dn / 4, out0, a.lda, lane);
+    if (a.de > 0) gather_rows<NB, NCH>(a.f, a.ldf, fr, nb, a.de / 4, out0 + a.dn, a.lda, lane);
     if (a.dtime > 0) {
-      for (int c = lane; c < a.dtime; c += 32) {
-        const float wc = __ldg(a.w + c), bc = __ldg(a.b + c);
+      // the time-encoding block in 16-byte stores when dtime % 4 == 0 and w, b
+      // are 16-byte aligned (the row offset dn + de is a multiple of 4 here)
+      if ((a.dtime & 3) == 0 && ((reinterpret_cast<uintptr_t>(a.w) | reinterpret_cast<uintptr_t>(a.b)) & 15) == 0) {
+        for (int c4 = lane; c4 < (a.dtime >> 2); c4 += 32) {
+          const float4 wc = __ldg(reinterpret_cast<const float4 *>(a.w) + c4);
+          const float4 bc = __ldg(reinterpret_cast<const float4 *>(a.b) + c4);
 #pragma unroll
-        for (int i = 0; i < kBatch; ++i)
-          if (i < nb) out0[i * a.lda + a.dn + a.de + c] = cosf(fmaf(t[i], wc, bc));
+          for (int i = 0; i < NB; ++i)
+            if (i < nb)
+              reinterpret_cast<float4 *>(out0 + i * a.lda + a.dn + a.de)[c4] =
+                  make_float4(cosf(fmaf(t[i], wc.x, bc.x)), cosf(fmaf(t[i], wc.y, bc.y)),
+                              cosf(fmaf(t[i], wc.z, bc.z)), cosf(fmaf(t[i], wc.w, bc.w)));
+        }
+      } else {
+        for (int c = lane; c < a.dtime; c += 32) {
+          const float wc = __ldg(a.w + c), bc = __ldg(a.b + c);
+#pragma unroll
+          for (int i = 0; i < NB; ++i)
+            if (i < nb) out0[i * a.lda + a.dn + a.de + c] = cosf(fmaf(t[i], wc, bc));
+        }
       }
     }
   }
@@ -346,6 +364,65 @@ __global__ void __launch_bounds__(256) k_te_bwd_part(const float *__restrict__ g
   }
 }
 
+// Stage 1 for dtime <= 512: one CTA per row chunk covers every column, thread
+// t on column t % dtime and row group t / dtime (kTeGroups groups striding
+// over the chunk's rows, eight rows' loads in flight), so no lane idles on a
+// partial 32-column block; the groups' sums are combined in a fixed order.
+constexpr int kTeGroups = 8;
+constexpr int kTeColsMax = 512;
+
+__global__ void __launch_bounds__(1024) k_te_bwd_rows(const float *__restrict__ g, int64_t ldg,
+                                                      const float *__restrict__ dt, const float *__restrict__ w,
+                                                      const float *__restrict__ b, int dtime, int groups,
+                                                      int64_t n_rows, const int32_t *n_rows_dev,
+                                                      float *__restrict__ part) {
+  fb::pdl_enter();
+  __shared__ float sw_s[kTeGroups * kTeColsMax / 2], sb_s[kTeGroups * kTeColsMax / 2];
+  const int64_t n = n_rows_dev ? min((int64_t)(*n_rows_dev), n_rows) : n_rows;
+  const int parts = fb::split_parts(n, kTeRowsPerCta, kTeMaxParts);
+  if ((int)blockIdx.y >= parts) return;
+  const int c = threadIdx.x % dtime, grp = threadIdx.x / dtime;
+  const bool live = grp < groups;
+  const int64_t per = (n + parts - 1) / parts;
+  const int64_t r0 = (int64_t)blockIdx.y * per;
+  const int64_t r1 = min(n, r0 + per);
+  float sw = 0.f, sb = 0.f;
+  if (live) {
+    const float wc = __ldg(w + c), bc = __ldg(b + c);
+    const int G = groups;
+    int64_t r = r0 + grp;
+    for (; r + 7 * G < r1; r += 8 * G) {
+      float tv[8], gv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        tv[u] = __ldg(dt + r + u * G);
+        gv[u] = __ldg(g + (r + u * G) * ldg + c);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float gs = -sin_big(fmaf(tv[u], wc, bc)) * gv[u];
+        sw = fmaf(gs, tv[u], sw);
+        sb += gs;
+      }
+    }
+    for (; r < r1; r += G) {
+      const float t = __ldg(dt + r);
+      const float gs = -sin_big(fmaf(t, wc, bc)) * __ldg(g + r * ldg + c);
+      sw = fmaf(gs, t, sw);
+      sb += gs;
+    }
+    sw_s[grp * dtime + c] = sw;
+    sb_s[grp * dtime + c] = sb;
+  }
+  __syncthreads();
+  if (grp == 0) {
+    float aw = 0.f, ab = 0.f;
+    for (int i = 0; i < groups; ++i) { aw += sw_s[i * dtime + c]; ab += sb_s[i * dtime + c]; }
+    part[((int64_t)blockIdx.y * 2 + 0) * dtime + c] = aw;
+    part[((int64_t)blockIdx.y * 2 + 1) * dtime + c] = ab;
+  }
+}
+
 // Stage 2: one warp per column sums the partials, lanes striding over them,
 // then a fixed shuffle tree (deterministic).
 __global__ void k_te_bwd_reduce(const float *__restrict__ part, int64_t n_rows, const int32_t *n_rows_dev, int dtime,
@@ -389,9 +466,17 @@ extern "C" int fb_gather_time_encode(const float *h, int64_t ldh, const int32_t 
   int64_t need = (n_rows + kRowsPerCta - 1) / kRowsPerCta;
   int grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, 148 * 16));
   if (vec && dn <= 4 * 32 * kMaxChunks && de <= 4 * 32 * kMaxChunks) {
-    const int64_t need_b = (n_rows + kRowsPerCta * kBatch - 1) / (kRowsPerCta * kBatch);
+    // four rows in flight per warp; source rows of <= 256 floats take two
+    // 16-byte chunks a lane, wider ones (<= 512) four
+    const bool narrow = dn <= 4 * 32 * 2 && de <= 4 * 32 * 2;
+    const int nb = 4;
+    const int64_t need_b = (n_rows + kRowsPerCta * nb - 1) / (kRowsPerCta * nb);
     const int grid_b = (int)std::max<int64_t>(1, std::min<int64_t>(need_b, 148 * 16));
-    FB_TRY_CUDA(fb::launch(k_gather_time_encode_batched, grid_b, 32 * kRowsPerCta, 0, stream, a));
+    if (narrow) {
+      FB_TRY_CUDA(fb::launch(k_gather_time_encode_batched<4, 2>, grid_b, 32 * kRowsPerCta, 0, stream, a));
+    } else {
+      FB_TRY_CUDA(fb::launch(k_gather_time_encode_batched<4, 4>, grid_b, 32 * kRowsPerCta, 0, stream, a));
+    }
   } else if (vec) {
     FB_TRY_CUDA(fb::launch(k_gather_time_encode<true>, grid, 32 * kRowsPerCta, 0, stream, a));
   } else {
@@ -439,9 +524,18 @@ extern "C" int fb_time_encode_bwd(const float *g, int64_t ldg, const float *dt, 
   // take the partition from the true count
   const int parts = te_parts(n_rows);
   float *part = static_cast<float *>(ws);
-  dim3 grid((dtime + 31) / 32, parts);
-  FB_TRY_CUDA(fb::launch(k_te_bwd_part, grid, 256, 0, stream, g, ldg, dt, w, b, dtime, n_rows, n_rows_dev, part));
-  FB_LAUNCHED("k_te_bwd_part");
+  if (dtime <= kTeColsMax) {
+    // groups of dtime threads: as many as fit 1024 threads, at most kTeGroups
+    const int groups = std::max(1, std::min(kTeGroups, 1024 / dtime));
+    const int threads = (groups * dtime + 31) / 32 * 32;
+    FB_TRY_CUDA(fb::launch(k_te_bwd_rows, dim3(1, parts), threads, 0, stream, g, ldg, dt, w, b, dtime, groups,
+                           n_rows, n_rows_dev, part));
+    FB_LAUNCHED("k_te_bwd_rows");
+  } else {
+    dim3 grid((dtime + 31) / 32, parts);
+    FB_TRY_CUDA(fb::launch(k_te_bwd_part, grid, 256, 0, stream, g, ldg, dt, w, b, dtime, n_rows, n_rows_dev, part));
+    FB_LAUNCHED("k_te_bwd_part");
+  }
   FB_TRY_CUDA(fb::launch(k_te_bwd_reduce, (dtime * 32 + 255) / 256, 256, 0, stream, part, n_rows, n_rows_dev, dtime, dw, db));
   FB_LAUNCHED("k_te_bwd_reduce");
   return FB_OK;
