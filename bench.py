@@ -306,13 +306,20 @@ def run_fast(args):
     sp, mp, gp, tp = model_params(cfg)
     fused = args.path == "fused"
     prec = dict(precision="bf16", feat_dims=(cfg.d_node, cfg.d_edge)) if bf16 else {}
+    if cfg.sharded:
+        # one global batch split across the ranks (config 5: 4,000 + 4,000 on 1/2/4/8 GPUs)
+        if cfg.batch % world:
+            raise SystemExit("config %d: its global batch of %d does not split over %d ranks" %
+                             (args.config, cfg.batch, world))
+        B, gB = cfg.batch // world, cfg.batch
+    else:
+        B = cfg.batch
+        gB = B * world
     if args.eager:
         tr = Trainer(graph, nf, ef, sp, mp, gp, tp, dev, rank=rank, world=world, fused=fused, **prec)
     else:
-        tr = GraphTrainer(graph, nf, ef, sp, mp, gp, tp, dev, batch=cfg.batch, rank=rank, world=world,
+        tr = GraphTrainer(graph, nf, ef, sp, mp, gp, tp, dev, batch=B, rank=rank, world=world,
                           fused=fused, **prec)
-    B = cfg.batch
-    gB = B * world
     n_batches = graph.train_end // gB
     warm, timed = epoch_schedule(n_batches, args.warmup, args.steps)
 
@@ -446,7 +453,8 @@ def run_fast(args):
                 "peak_source": "%s copy bandwidth (MEASURED_PEAKS.json)" % pk["src"]}
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "strong" if cfg.sharded else "weak",
         "vs_baseline": None, "dtype": "bf16" if bf16 else "f32", "data": data_label(args, cfg),
         "config": {"workload": cfg.name, "global_batch": gB, "local_batch": B, "fanout": list(cfg.fanout),
                    "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge,

@@ -33,6 +33,7 @@ class WorkloadConfig:
     fanout: tuple
     batch: int
     dtype: str = "fp32"
+    sharded: bool = False   # the global batch is `batch`, split across the ranks (else `batch` per rank)
 
 
 CONFIGS = {
@@ -45,7 +46,7 @@ CONFIGS = {
     4: WorkloadConfig("apan1_synthetic", 50_000, 3_000_000, ("zipf", 1.2), ("zipf", 1.2), 2e8, False, 0, 100,
                       "normal", "APAN-1", "recent", (10,), 600),
     5: WorkloadConfig("tgat2_gdelt_like", 16_700, 191_000_000, ("zipf", 1.05), ("zipf", 1.05), 2e8, False, 413, 186,
-                      "normal", "TGAT", "recent", (10, 10), 4000, "bf16"),
+                      "normal", "TGAT", "recent", (10, 10), 4000, "bf16", True),
 }
 
 
