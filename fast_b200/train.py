@@ -9,10 +9,11 @@ sizes (and, in the end-to-end mode, the batch upload and the loss readback).
 Data parallelism: each rank takes a contiguous slice of every chronological
 batch, gradients are averaged with one NCCL all-reduce over a single flat
 bucket.  Equal slices make the averaged gradient the gradient of the global
-batch loss (mean_pos + mean_neg, train.py:373-374).  A memory model (TGN)
-keeps the whole node memory on every rank; after each step one all_gather
-brings every rank's updated memory rows, and every rank writes them in the
-global batch's order, as one process would.
+batch loss (mean_pos + mean_neg, train.py:373-374).  A memory model keeps
+the whole node memory on every rank; after each step all_gathers bring every
+rank's updated memory rows (and, for APAN's delivery to sampled neighbours,
+every rank's sampled block), and every rank writes them in the global
+batch's order, as one process would.
 """
 import numpy as np
 import torch
@@ -74,6 +75,59 @@ def gather_global_order(local, world, out=None, perm=None):
     return out, perm
 
 
+def _all_gather(t, world):
+    out = torch.empty((world,) + tuple(t.shape), device=t.device, dtype=t.dtype)
+    if dist.get_backend() == "nccl":
+        dist.all_gather_into_tensor(out, t.contiguous())
+    else:
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t.contiguous())
+        torch.stack(parts, out=out)
+    return out
+
+
+def gather_neighbor_block_global(edge_nodes, row, rptr, Br, world):
+    """APAN's mail delivery to sampled neighbours on several ranks: every
+    rank's block for its positive roots [src_r | dst_r] (2 Br roots; its
+    edges' nodes and root rows padded to the same capacity on every rank,
+    rptr the CSR over those roots), listed as the block one process sampling
+    the global positive roots [src | dst] would list it -- the edges of the
+    src roots rank by rank, then those of the dst roots, each root's edges in
+    sampler order, and each row the root's index in the global list.
+    Returns (edge nodes, rows, edge count as a device int32 [1]); entries past
+    the count are left unset.  All counts stay on the device."""
+    cap = edge_nodes.shape[0]
+    dev = edge_nodes.device
+    gB = Br * world
+    cnt = torch.stack([rptr[Br] - rptr[0], rptr[2 * Br] - rptr[Br]]).to(torch.int64)
+    g_cnt = _all_gather(cnt, world)                       # [W, 2]: edges of the rank's src / dst roots
+    g_nodes = _all_gather(edge_nodes, world)              # [W, cap]
+    g_row = _all_gather(row, world).to(torch.int64)       # [W, cap] local root index
+    sec = g_cnt.sum(0)                                    # edges of all src roots, of all dst roots
+    pre = torch.cumsum(g_cnt, 0) - g_cnt                  # edges of the same section on lower ranks
+    e = torch.arange(cap, device=dev).view(1, cap)
+    c0, c1 = g_cnt[:, 0:1], g_cnt[:, 1:2]
+    in_dst = e >= c0
+    pos = torch.where(in_dst, sec[0] + pre[:, 1:2] + (e - c0), pre[:, 0:1] + e)
+    pos = torch.where(e < c0 + c1, pos, torch.full_like(pos, world * cap))     # padding -> a spare slot
+    r = torch.arange(world, device=dev).view(world, 1)
+    grow = (g_row // Br) * gB + r * Br + g_row % Br
+    nodes_out = torch.empty(world * cap + 1, device=dev, dtype=edge_nodes.dtype)
+    row_out = torch.empty(world * cap + 1, device=dev, dtype=row.dtype)
+    nodes_out.scatter_(0, pos.reshape(-1), g_nodes.reshape(-1))
+    row_out.scatter_(0, pos.reshape(-1), grow.to(row.dtype).reshape(-1))
+    return nodes_out[:-1], row_out[:-1], sec.sum().to(torch.int32).view(1)
+
+
+class _GlobalBlock:
+    """The neighbour-delivery view of the global batch's block (nodes, row,
+    edge count) that MailBox.update reads."""
+
+    def __init__(self, nodes, row, n_edges_dev):
+        self.nodes, self.row, self.n_edges_dev = nodes, row, n_edges_dev
+        self.n_edges = row.shape[0]
+
+
 def _bf16_table(t, width):
     """A feature table as bf16 rows padded with zeros to a multiple of 8
     columns (kept as is when it already is one)."""
@@ -116,9 +170,6 @@ class Trainer:
         if memory_param.get("type", "none") != "none":
             if not fused:
                 raise NotImplementedError("node memory trains through FusedStep")
-            if world > 1 and memory_param.get("deliver_to") != "self":
-                raise NotImplementedError("data-parallel node memory covers mails delivered to the roots "
-                                          "themselves (deliver_to: self, TGN)")
             self.model = MemoryModel(dn, de, sample_param, memory_param, gnn_param, train_param).to(self.device)
             self.mailbox = MailBox(memory_param, graph.n_nodes, de, self.device)
         else:
@@ -218,12 +269,32 @@ class Trainer:
             return
         R = roots.shape[0]
         h = self.engine.last_memory[:R]
+        block = blocks[0]
         if self.world > 1:
             # every rank keeps the whole memory: all ranks' updates, applied
             # in the global batch's order, keep the replicas equal to the
             # tables of one process training on the global batch
+            if self.mailbox.deliver_to == "neighbors":
+                block = self._neighbor_block(block, R // 3)
             roots, root_ts, h = self._memory_exchange(roots, root_ts, h)
-        self.mailbox.update(roots, root_ts, h, self.edge_feats, self.e0_buf, block=blocks[0])
+            if self.mailbox.deliver_to == "neighbors":
+                block = _GlobalBlock(torch.cat([roots[:2 * (R // 3) * self.world], block[0]]), block[1], block[2])
+        self.mailbox.update(roots, root_ts, h, self.edge_feats, self.e0_buf, block=block)
+
+    def _neighbor_block(self, blk, Br):
+        """This rank's block for its positive roots, padded to the capacity
+        every rank shares, gathered into the global order."""
+        cap = 2 * Br * int(self.sample_param["neighbor"][0])
+        n2 = 2 * Br
+        E = blk.row.shape[0]
+        if E >= cap:                               # capacity-sized block (no root has more than fanout edges)
+            nodes_e, row = blk.nodes[n2:n2 + cap], blk.row[:cap]
+        else:                                      # host-sized block: pad to the capacity
+            nodes_e = torch.zeros(cap, device=blk.row.device, dtype=blk.nodes.dtype)
+            row = torch.zeros(cap, device=blk.row.device, dtype=blk.row.dtype)
+            nodes_e[:E] = blk.nodes[n2:n2 + E]
+            row[:E] = blk.row
+        return gather_neighbor_block_global(nodes_e, row, blk.rptr, Br, self.world)
 
     def _memory_exchange(self, roots, root_ts, h):
         """All ranks' (roots, times, updated memory) in the global order."""

@@ -10,6 +10,10 @@
 * The node-memory exchange of data-parallel TGN (gather_global_order): every
   rank's [src_r | dst_r | neg_r] rows come back in the global batch's order
   [src | dst | neg], on every rank, for id, time and memory-row tensors.
+* APAN's neighbour delivery (gather_neighbor_block_global): the ranks' blocks
+  for their positive roots, padded to a shared capacity, become the block
+  one process sampling the global positive roots lists -- edge nodes and
+  each edge's global root row in the same order, and the edge count.
 """
 import os
 import socket
@@ -141,3 +145,50 @@ def test_memory_exchange_restores_global_order(tmp_path, world):
     mp.spawn(_gather_worker, args=(world, _port(), str(tmp_path)), nprocs=world, join=True)
     for r in range(world):
         assert (tmp_path / ("gather%d.txt" % r)).read_text() == "ok"
+
+
+def _neighbor_worker(rank, world, port, outdir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    try:
+        sys.path.insert(0, ROOT)
+        from fast_b200.train import gather_neighbor_block_global
+        gB, fan = 12, 4
+        Br = gB // world
+        g = torch.Generator().manual_seed(3)
+        deg = torch.randint(0, fan + 1, (2 * gB,), generator=g)       # edges of each global positive root
+        # the single-process block: edges in root order [src | dst]
+        g_rows = torch.repeat_interleave(torch.arange(2 * gB), deg).to(torch.int32)
+        g_nodes = torch.randint(0, 1000, (g_rows.numel(),), generator=g, dtype=torch.int32)
+        starts = torch.cumsum(deg, 0) - deg
+        # this rank's block: its src roots then its dst roots, local rows
+        mine = [s * gB + rank * Br + t for s in range(2) for t in range(Br)]
+        nodes, rows, rptr = [], [], [0]
+        for j, gr in enumerate(mine):
+            a, n = int(starts[gr]), int(deg[gr])
+            nodes.append(g_nodes[a:a + n])
+            rows.append(torch.full((n,), j, dtype=torch.int32))
+            rptr.append(rptr[-1] + n)
+        cap = 2 * Br * fan
+        E = rptr[-1]
+        ne = torch.full((cap,), -7, dtype=torch.int32)
+        ro = torch.full((cap,), -9, dtype=torch.int32)
+        ne[:E] = torch.cat(nodes)
+        ro[:E] = torch.cat(rows)
+        out_n, out_r, cnt = gather_neighbor_block_global(ne, ro, torch.tensor(rptr, dtype=torch.int32), Br, world)
+        Et = g_rows.numel()
+        ok = int(cnt[0]) == Et and torch.equal(out_n[:Et], g_nodes) and torch.equal(out_r[:Et], g_rows)
+        status = "ok" if ok else "mismatch"
+    except Exception as e:
+        status = "error: " + str(e)[:200]
+    with open(os.path.join(outdir, "nbr%d.txt" % rank), "w") as f:
+        f.write(status)
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_neighbor_block_exchange_restores_global_order(tmp_path, world):
+    mp.spawn(_neighbor_worker, args=(world, _port(), str(tmp_path)), nprocs=world, join=True)
+    for r in range(world):
+        assert (tmp_path / ("nbr%d.txt" % r)).read_text() == "ok"

@@ -11,11 +11,13 @@ the sampled blocks are then exactly the single process's, so losses and
 parameters agree to fp32 rounding.  (With two or more recent layers the
 deeper layers' pointer updates see only the rank's own hop-1 nodes.)
 
-TGN-1 (GRU node memory, mails to the roots themselves) the same way: every
+TGN-1 (GRU node memory, mails to the roots themselves) and APAN-1
+(transformer memory, mails to the sampled neighbours) the same way: every
 rank keeps the whole memory and, after each step, writes all ranks' updated
-rows in the global batch's order (one NCCL all_gather), so the memory and
-mailbox tables, their timestamps, the losses and the parameters agree with
-one process training on the global batch.
+rows (and, for APAN, all ranks' sampled blocks) in the global batch's order,
+so the memory and mailbox tables, their timestamps and slot pointers, the
+losses and the parameters agree with one process training on the global
+batch.
 """
 import os
 import socket
@@ -105,21 +107,30 @@ def test_dp_two_ranks_equal_single_process(tmp_path):
     np.testing.assert_allclose(dp_params, params, rtol=1e-4, atol=1e-6)
 
 
-def _setup_tgn(dev):
+def _setup_tgn(dev, model="tgn"):
     cfg, g, ef, sp, mp_, gp, tp = _setup(dev)
+    if model == "apan":
+        sp = dict(sp, no_neg=True)
+        mp_ = dict(type="node", dim_time=100, deliver_to="neighbors", mail_combine="last",
+                   memory_update="transformer", attention_head=2, mailbox_size=10, combine_node_feature=False,
+                   dim_out=100)
+        gp = dict(arch="identity")
+        return cfg, g, ef, sp, mp_, gp, tp
     mp_ = dict(type="node", dim_time=100, deliver_to="self", mail_combine="last", memory_update="gru",
                mailbox_size=1, combine_node_feature=True, dim_out=100)
     return cfg, g, ef, sp, mp_, gp, tp
 
 
+_TABLES = ("node_memory", "node_memory_ts", "mailbox", "mailbox_ts", "next_mail_pos")
+
+
 def _tgn_state(tr):
     mb = tr.mailbox
     return dict(params=torch.cat([p.detach().reshape(-1) for p in tr.model.parameters()]).cpu().numpy(),
-                **{k: getattr(mb, k).detach().cpu().numpy() for k in ("node_memory", "node_memory_ts", "mailbox",
-                                                                      "mailbox_ts")})
+                **{k: getattr(mb, k).detach().cpu().numpy() for k in _TABLES})
 
 
-def _tgn_worker(rank, world, port, outdir):
+def _tgn_worker(rank, world, port, outdir, model="tgn"):
     import datetime
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -129,7 +140,7 @@ def _tgn_worker(rank, world, port, outdir):
                             timeout=datetime.timedelta(seconds=60))
     try:
         from fast_b200.train import GraphTrainer
-        cfg, g, ef, sp, mp_, gp, tp = _setup_tgn(dev)
+        cfg, g, ef, sp, mp_, gp, tp = _setup_tgn(dev, model)
         gB = 128
         tr = GraphTrainer(g, None, ef, sp, mp_, dict(gp), tp, dev, batch=gB // world, rank=rank, world=world,
                           seed=5, sampler_seed=77, optimizer="sgd")
@@ -139,24 +150,26 @@ def _tgn_worker(rank, world, port, outdir):
         st = _tgn_state(tr)
         tr.g_main = tr.g_opt = None          # release graphs before tearing down NCCL
         torch.cuda.synchronize()
-        np.savez(os.path.join(outdir, "tgn_rank%d.npz" % rank), loss=(t / world).cpu().numpy(), **st)
+        np.savez(os.path.join(outdir, "%s_rank%d.npz" % (model, rank)), loss=(t / world).cpu().numpy(), **st)
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_dp_tgn_memory_two_ranks_equal_single_process(tmp_path):
+@pytest.mark.parametrize("model", ["tgn", "apan"])
+def test_dp_memory_two_ranks_equal_single_process(tmp_path, model):
+    """TGN (mails to the roots) and APAN (mails to the sampled neighbours)."""
     import torch.multiprocessing as mp
-    mp.spawn(_tgn_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_tgn_worker, args=(2, _port(), str(tmp_path), model), nprocs=2, join=True)
     from fast_b200.train import GraphTrainer
     dev = torch.device("cuda", 0)
-    cfg, g, ef, sp, mp_, gp, tp = _setup_tgn(dev)
+    cfg, g, ef, sp, mp_, gp, tp = _setup_tgn(dev, model)
     tr = GraphTrainer(g, None, ef, sp, mp_, dict(gp), tp, dev, batch=128, seed=5, sampler_seed=77, optimizer="sgd")
     single = np.array(_run(tr, 128))
     ref = _tgn_state(tr)
-    r0, r1 = (np.load(tmp_path / ("tgn_rank%d.npz" % r)) for r in range(2))
+    r0, r1 = (np.load(tmp_path / ("%s_rank%d.npz" % (model, r))) for r in range(2))
     np.testing.assert_allclose(r0["loss"], single, rtol=1e-5, atol=1e-6)
-    for k in ("node_memory_ts", "mailbox_ts"):
+    for k in ("node_memory_ts", "mailbox_ts", "next_mail_pos"):
         assert np.array_equal(r0[k], ref[k]) and np.array_equal(r1[k], ref[k]), k
     for k in ("node_memory", "mailbox", "params"):
         assert np.array_equal(r0[k], r1[k]), k           # the replicas stay identical
