@@ -306,8 +306,8 @@ __device__ __forceinline__ float sin_big(float x) {
   return x < 0.f ? -sv : sv;
 }
 
-constexpr int64_t kTeRowsPerCta = 128;
-constexpr int64_t kTeMaxParts = 296;   // two waves of 148 SMs at most
+constexpr int64_t kTeRowsPerCta = 64;
+constexpr int64_t kTeMaxParts = 592;   // two waves of two 800-thread CTAs per SM at most
 
 // Time-encoding backward, stage 1: CTA (x = 32-column tile, y = row chunk)
 // with 8 warps striding over the chunk's rows, lanes over columns; the warps'
