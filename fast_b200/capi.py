@@ -101,6 +101,9 @@ _SIGS = {
                                         _I64, _I64, _P, _P]),
     "fb_attn_bwd_bf16kv": (_I, [_P, _I64, _P, _P, _I64, _P, _I64, _P, _I, _I, _F, _F, _U64, _U64, _P, _P, _P, _I64,
                                 _P, _P, _P, _I64, _P]),
+    "fb_attn_fwd_kvbf16": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I, _I, _F, _F, _U64, _U64, _P, _P, _P, _I64, _P]),
+    "fb_attn_bwd_kvbf16": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I, _I, _F, _F, _U64, _U64, _P, _P, _P, _I64, _P,
+                                _P, _I64, _P]),
 }
 
 class GemmProblem(ctypes.Structure):
@@ -126,7 +129,7 @@ class GemmBf16Problem(ctypes.Structure):
     (operand pointers to bf16) plus ka and the TN column segments."""
     _fields_ = GemmProblem._fields_ + [("ka", ctypes.c_int), ("nseg", ctypes.c_int),
                                        ("seg_at", ctypes.c_int * 3), ("seg_len", ctypes.c_int * 3),
-                                       ("seg_to", ctypes.c_int * 3)]
+                                       ("seg_to", ctypes.c_int * 3), ("c_bf16", ctypes.c_int)]
 
 
 _SIGS["fb_gemm_bf16_group_ws_bytes"] = (_SZ, [ctypes.POINTER(GemmBf16Problem), _I])

@@ -164,6 +164,7 @@ struct AttnArgs {
   const float *dagg; int64_t lddagg;
   float *dq, *dk, *dv; int64_t lddkv;
   int kv_bf16;             // dk / dv are bf16 (bit patterns, round to nearest even)
+  int kv_in_bf16;          // k / v are bf16 rows (bulk-copy kernels only)
 };
 
 // Output (or incoming gradient) row of segment j: j itself, or the row named
@@ -768,15 +769,28 @@ __device__ __forceinline__ void slot_release() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Lane-per-edge dot products against the masked rows in shared memory.
-template <int HP>
-__device__ __forceinline__ void row_dots_sm(const float *row, const float4 (*sm)[32], int nq, float (&out)[HP]) {
+// Four consecutive features (float4 index q) of row `row` of a warp's slot:
+// fp32 rows, or bf16 rows (BF) widened to fp32.
+template <bool BF>
+__device__ __forceinline__ float4 slot4(const unsigned char *slot, int row, int rowf, int q) {
+  if (BF) {
+    const uint2 u = reinterpret_cast<const uint2 *>(slot + (size_t)row * rowf * 2)[q];
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                       __uint_as_float(u.y & 0xFFFF0000u));
+  }
+  return reinterpret_cast<const float4 *>(slot + (size_t)row * rowf * 4)[q];
+}
+
+// Lane-per-edge dot products of slot row `row` (features from float4 index
+// q0) against the masked rows in shared memory.
+template <int HP, bool BF>
+__device__ __forceinline__ void row_dots_sm(const unsigned char *slot, int row, int rowf, int q0,
+                                            const float4 (*sm)[32], int nq, float (&out)[HP]) {
 #pragma unroll
   for (int h = 0; h < HP; ++h) out[h] = 0.f;
-  const float4 *r4 = reinterpret_cast<const float4 *>(row);
 #pragma unroll 5
   for (int t = 0; t < nq; ++t) {
-    const float4 k = r4[t];
+    const float4 k = slot4<BF>(slot, row, rowf, q0 + t);
 #pragma unroll
     for (int h = 0; h < HP; ++h) {
       const float4 m = sm[h][t];
@@ -785,16 +799,18 @@ __device__ __forceinline__ void row_dots_sm(const float *row, const float4 (*sm)
   }
 }
 
-template <int HP>
+template <int HP, bool BF>
 __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_fwd_b(AttnArgs a) {
   fb::pdl_enter();
   extern __shared__ __align__(128) unsigned char smraw[];
   __shared__ uint64_t bar[kBulkWarps];
+  constexpr int kEsz = BF ? 2 : 4;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int rowf = (int)a.ldkv;
-  float *slot = reinterpret_cast<float *>(smraw) + (size_t)w * kBulkGroup * rowf;
+  unsigned char *slot = smraw + (size_t)w * kBulkGroup * rowf * kEsz;
+  const unsigned char *kbase = reinterpret_cast<const unsigned char *>(a.k);
   float4 (*qm)[32] =
-      reinterpret_cast<float4 (*)[32]>(smraw + (size_t)kBulkWarps * kBulkGroup * rowf * 4) + (size_t)w * HP;
+      reinterpret_cast<float4 (*)[32]>(smraw + (size_t)kBulkWarps * kBulkGroup * rowf * kEsz) + (size_t)w * HP;
   const int64_t n_dst = a.n_dst_dev ? min((int64_t)(*a.n_dst_dev), a.n_dst) : a.n_dst;
   const int nq = a.dim / 4, dh = a.dim / a.heads;
   const bool live = lane < nq;
@@ -823,14 +839,14 @@ __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_fwd_b(AttnArgs a) {
       for (int g0 = beg; g0 < end; g0 += kBulkGroup) {
         const int n = min(kBulkGroup, end - g0);
         slot_release();
-        if (lane == 0) bulk_copy(slot, a.k + (int64_t)g0 * a.ldkv, (uint32_t)(n * rowf * 4), &bar[w]);
+        if (lane == 0) bulk_copy(slot, kbase + (int64_t)g0 * a.ldkv * kEsz, (uint32_t)(n * rowf * kEsz), &bar[w]);
         const bool ok = bulk_wait(&bar[w], phase);
         phase ^= 1u;
         if (!ok) return;
         const bool valid = lane < n;
         const int64_t e = g0 + lane;
         float z[HP];
-        if (valid) row_dots_sm<HP>(slot + lane * rowf, qm, nq, z);
+        if (valid) row_dots_sm<HP, BF>(slot, lane, rowf, 0, qm, nq, z);
         float kp[HP];
         keep_heads<HP>(a, doff, e, valid, inv_keep, kp);
         float wt[HP], sc[HP];
@@ -854,7 +870,7 @@ __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_fwd_b(AttnArgs a) {
 #pragma unroll
           for (int h = 0; h < HP; ++h) wc[h] = __shfl_sync(0xffffffffu, wt[h], c);
           const float wa = hv<HP>(wc, hA), wb = hv<HP>(wc, hB);
-          const float4 v = live ? reinterpret_cast<const float4 *>(slot + c * rowf + a.dim)[lane] : zero4;
+          const float4 v = live ? slot4<BF>(slot, c, rowf, (a.dim >> 2) + lane) : zero4;
           acc.x = fmaf(wa, v.x, acc.x);
           acc.y = fmaf(wa, v.y, acc.y);
           acc.z = fmaf(wb, v.z, acc.z);
@@ -884,16 +900,18 @@ __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_fwd_b(AttnArgs a) {
   }
 }
 
-template <int HP>
+template <int HP, bool BF>
 __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_bwd_b(AttnArgs a) {
   fb::pdl_enter();
   extern __shared__ __align__(128) unsigned char smraw[];
   __shared__ uint64_t bar[kBulkWarps];
+  constexpr int kEsz = BF ? 2 : 4;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int rowf = (int)a.ldkv;
-  float *slot = reinterpret_cast<float *>(smraw) + (size_t)w * kBulkGroup * rowf;
+  unsigned char *slot = smraw + (size_t)w * kBulkGroup * rowf * kEsz;
+  const unsigned char *kbase = reinterpret_cast<const unsigned char *>(a.k);
   float4 (*qm)[32] =
-      reinterpret_cast<float4 (*)[32]>(smraw + (size_t)kBulkWarps * kBulkGroup * rowf * 4) + (size_t)w * 2 * HP;
+      reinterpret_cast<float4 (*)[32]>(smraw + (size_t)kBulkWarps * kBulkGroup * rowf * kEsz) + (size_t)w * 2 * HP;
   float4 (*dm)[32] = qm + HP;
   const int64_t n_dst = a.n_dst_dev ? min((int64_t)(*a.n_dst_dev), a.n_dst) : a.n_dst;
   const int nq = a.dim / 4, dh = a.dim / a.heads;
@@ -922,14 +940,14 @@ __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_bwd_b(AttnArgs a) {
       for (int g0 = beg; g0 < end; g0 += kBulkGroup) {
         const int n = min(kBulkGroup, end - g0);
         slot_release();
-        if (lane == 0) bulk_copy(slot, a.k + (int64_t)g0 * a.ldkv, (uint32_t)(n * rowf * 4), &bar[w]);
+        if (lane == 0) bulk_copy(slot, kbase + (int64_t)g0 * a.ldkv * kEsz, (uint32_t)(n * rowf * kEsz), &bar[w]);
         const bool ok = bulk_wait(&bar[w], phase);
         phase ^= 1u;
         if (!ok) return;
         const bool valid = lane < n;
         const int64_t e = g0 + lane;
         float d[HP], kp[HP], yk[HP];
-        if (valid) row_dots_sm<HP>(slot + lane * rowf + a.dim, dm, nq, d);
+        if (valid) row_dots_sm<HP, BF>(slot, lane, rowf, a.dim >> 2, dm, nq, d);
         keep_heads<HP>(a, doff, e, valid, inv_keep, kp);
 #pragma unroll
         for (int h = 0; h < HP; ++h) {
@@ -961,7 +979,7 @@ __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_bwd_b(AttnArgs a) {
         const int n = min(kBulkGroup, end - g0);
         if (!one) {
           slot_release();
-          if (lane == 0) bulk_copy(slot, a.k + (int64_t)g0 * a.ldkv, (uint32_t)(n * rowf * 4), &bar[w]);
+          if (lane == 0) bulk_copy(slot, kbase + (int64_t)g0 * a.ldkv * kEsz, (uint32_t)(n * rowf * kEsz), &bar[w]);
           const bool ok = bulk_wait(&bar[w], phase);
           phase ^= 1u;
           if (!ok) return;
@@ -969,13 +987,13 @@ __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_bwd_b(AttnArgs a) {
         const bool valid = lane < n;
         const int64_t e = g0 + lane;
         float z[HP], dl[HP], y[HP], dz[HP];
-        if (valid) row_dots_sm<HP>(slot + lane * rowf, qm, nq, z);
+        if (valid) row_dots_sm<HP, BF>(slot, lane, rowf, 0, qm, nq, z);
         if (one) {
 #pragma unroll
           for (int h = 0; h < HP; ++h) { dl[h] = dl1[h]; y[h] = y1[h]; }
         } else {
           float d[HP], kp[HP];
-          if (valid) row_dots_sm<HP>(slot + lane * rowf + a.dim, dm, nq, d);
+          if (valid) row_dots_sm<HP, BF>(slot, lane, rowf, a.dim >> 2, dm, nq, d);
           keep_heads<HP>(a, doff, e, valid, inv_keep, kp);
 #pragma unroll
           for (int h = 0; h < HP; ++h) {
@@ -997,7 +1015,7 @@ __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_bwd_b(AttnArgs a) {
           for (int h = 0; h < HP; ++h) zc[h] = __shfl_sync(0xffffffffu, dz[h], c);
           const float za = hv<HP>(zc, hA), zb = hv<HP>(zc, hB);
           if (live) {
-            const float4 k = reinterpret_cast<const float4 *>(slot + c * rowf)[lane];
+            const float4 k = slot4<BF>(slot, c, rowf, lane);
             if (a.dk)
               put4(a.dk, (int64_t)(g0 + c) * a.lddkv + 4 * lane,
                    make_float4(za * q4.x, za * q4.y, zb * q4.z, zb * q4.w), a.kv_bf16);
@@ -1033,7 +1051,8 @@ int check_attn(const AttnArgs &a, bool bwd) {
   if ((!a.x && (!a.q || !a.k)) || !a.v || !a.rptr || a.n_dst < 0 || a.ldkv % 4 || a.ldq % 4 || a.ldkv < 0 ||
       a.ldq < 0)
     return fb::set_error(FB_ERR_ARG, "attention: bad pointer or leading dimension (multiples of 4 floats)");
-  if (!aligned16(a.q) || !aligned16(a.k) || !aligned16(a.v))
+  // bf16 K|V rows are read whole from k (v = k + dim elements need not be 16-byte aligned)
+  if (!aligned16(a.q) || !aligned16(a.k) || (!a.kv_in_bf16 && !aligned16(a.v)) || (a.kv_in_bf16 && a.ldkv % 8))
     return fb::set_error(FB_ERR_ARG, "attention: q/k/v must be 16-byte aligned");
   if (!(a.drop_p >= 0.f && a.drop_p < 1.f)) return fb::set_error(FB_ERR_ARG, "attention: dropout p must be in [0, 1)");
   if (!bwd) {
@@ -1061,11 +1080,14 @@ bool short_path(const AttnArgs &a) {
 // Bulk-copy kernels: the edge-parallel shapes with the interleaved K|V rows.
 bool bulk_path(const AttnArgs &a) {
   static const bool off = getenv("FB_NO_BULK_ATTN") != nullptr;
-  return !off && short_path(a) && a.v == a.k + a.dim && a.ldkv == 2 * a.dim;
+  const size_t esz = a.kv_in_bf16 ? 2 : 4;
+  const bool interleaved = reinterpret_cast<const char *>(a.v) == reinterpret_cast<const char *>(a.k) + a.dim * esz;
+  return (!off || a.kv_in_bf16) && short_path(a) && interleaved && a.ldkv == 2 * a.dim;
 }
 
 size_t bulk_smem(const AttnArgs &a, int hp, bool bwd) {
-  return (size_t)kBulkWarps * ((size_t)kBulkGroup * a.ldkv * 4 + (bwd ? 2 : 1) * (size_t)hp * 32 * 16);
+  const size_t esz = a.kv_in_bf16 ? 2 : 4;
+  return (size_t)kBulkWarps * ((size_t)kBulkGroup * a.ldkv * esz + (bwd ? 2 : 1) * (size_t)hp * 32 * 16);
 }
 
 int bulk_grid(int64_t n_dst) {
@@ -1075,10 +1097,10 @@ int bulk_grid(int64_t n_dst) {
 // Opts a kernel into `bytes` of dynamic shared memory once per device.
 template <typename K>
 int allow_smem(K kernel, size_t bytes, int slot) {
-  static size_t done[8][64] = {};
+  static size_t done[12][64] = {};
   int dev = 0;
   FB_TRY_CUDA(cudaGetDevice(&dev));
-  size_t &d = done[slot & 7][dev & 63];
+  size_t &d = done[slot % 12][dev & 63];
   if (d < bytes) {
     FB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
     d = bytes;
@@ -1086,27 +1108,34 @@ int allow_smem(K kernel, size_t bytes, int slot) {
   return FB_OK;
 }
 
-template <int HP>
-int launch_bulk(const AttnArgs &a, bool bwd, cudaStream_t stream) {
+template <int HP, bool BF>
+int launch_bulk_t(const AttnArgs &a, bool bwd, cudaStream_t stream) {
   const size_t sm = bulk_smem(a, HP, bwd);
   const int grid = bulk_grid(a.n_dst);
-  const int slot = (HP == 1 ? 0 : (HP == 2 ? 1 : 2)) + (bwd ? 3 : 0);
+  const int slot = (HP == 1 ? 0 : (HP == 2 ? 1 : 2)) + (bwd ? 3 : 0) + (BF ? 6 : 0);
   int rc;
   if (bwd) {
-    if ((rc = allow_smem(k_attn_bwd_b<HP>, sm, slot))) return rc;
-    FB_TRY_CUDA(fb::launch(k_attn_bwd_b<HP>, grid, 32 * kBulkWarps, sm, stream, a));
+    if ((rc = allow_smem(k_attn_bwd_b<HP, BF>, sm, slot))) return rc;
+    FB_TRY_CUDA(fb::launch(k_attn_bwd_b<HP, BF>, grid, 32 * kBulkWarps, sm, stream, a));
     FB_LAUNCHED("k_attn_bwd_b");
   } else {
-    if ((rc = allow_smem(k_attn_fwd_b<HP>, sm, slot))) return rc;
-    FB_TRY_CUDA(fb::launch(k_attn_fwd_b<HP>, grid, 32 * kBulkWarps, sm, stream, a));
+    if ((rc = allow_smem(k_attn_fwd_b<HP, BF>, sm, slot))) return rc;
+    FB_TRY_CUDA(fb::launch(k_attn_fwd_b<HP, BF>, grid, 32 * kBulkWarps, sm, stream, a));
     FB_LAUNCHED("k_attn_fwd_b");
   }
   return FB_OK;
 }
 
+template <int HP>
+int launch_bulk(const AttnArgs &a, bool bwd, cudaStream_t stream) {
+  return a.kv_in_bf16 ? launch_bulk_t<HP, true>(a, bwd, stream) : launch_bulk_t<HP, false>(a, bwd, stream);
+}
+
 int launch_fwd(const AttnArgs &a, cudaStream_t stream) {
   int rc = check_attn(a, false);
   if (rc) return rc;
+  if (a.kv_in_bf16 && !bulk_path(a))
+    return fb::set_error(FB_ERR_UNSUPPORTED, "attention: bf16 K|V needs interleaved rows [E, 2 dim], dim <= 128");
   if (a.n_dst == 0) return FB_OK;
   const int grid = attn_grid(a.n_dst), nv = (a.dim / 4 + 31) / 32;
   if (bulk_path(a)) {
@@ -1134,6 +1163,8 @@ int launch_fwd(const AttnArgs &a, cudaStream_t stream) {
 int launch_bwd(const AttnArgs &a, cudaStream_t stream) {
   int rc = check_attn(a, true);
   if (rc) return rc;
+  if (a.kv_in_bf16 && !bulk_path(a))
+    return fb::set_error(FB_ERR_UNSUPPORTED, "attention: bf16 K|V needs interleaved rows [E, 2 dim], dim <= 128");
   if (a.n_dst == 0) return FB_OK;
   const int grid = attn_grid(a.n_dst), nv = (a.dim / 4 + 31) / 32;
   if (bulk_path(a)) {
@@ -1227,6 +1258,46 @@ extern "C" int fb_attn_bwd_bf16kv(const float *q, int64_t ldq, const float *k, c
   a.att = att; a.dagg = dagg; a.lddagg = lddagg; a.dq = dq; a.lddkv = lddkv;
   a.dk = reinterpret_cast<float *>(dk);
   a.dv = reinterpret_cast<float *>(dv);
+  a.kv_bf16 = 1;
+  return launch_bwd(a, stream);
+}
+
+// The attention forward on bf16 K|V rows kv[E, ldkv] (K in the first dim
+// columns, V in the next dim): the K|V projection's bf16 output in the bf16
+// projection mode.  Softmax, dropout and the weighted sum run in fp32.
+extern "C" int fb_attn_fwd_kvbf16(const float *q, int64_t ldq, const uint16_t *kv, int64_t ldkv,
+                                  const int32_t *rptr, int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim,
+                                  float slope, float drop_p, uint64_t seed, uint64_t offset,
+                                  const uint64_t *offset_dev, float *att, float *agg, int64_t ldagg,
+                                  cudaStream_t stream) {
+  AttnArgs a{};
+  a.offset_dev = offset_dev;
+  a.q = q; a.ldq = ldq; a.ldkv = ldkv; a.rptr = rptr; a.n_dst = n_dst; a.n_dst_dev = n_dst_dev;
+  a.k = reinterpret_cast<const float *>(kv);
+  a.v = reinterpret_cast<const float *>(kv + dim);
+  a.kv_in_bf16 = 1;
+  a.heads = heads; a.dim = dim; a.slope = slope; a.drop_p = drop_p; a.seed = seed; a.offset = offset;
+  a.att_out = att; a.agg = agg; a.ldagg = ldagg;
+  return launch_fwd(a, stream);
+}
+
+// Its backward: reads the bf16 K|V rows, writes dq fp32 and dK|dV as bf16
+// rows dkv[E, lddkv] in the same interleaved layout.
+extern "C" int fb_attn_bwd_kvbf16(const float *q, int64_t ldq, const uint16_t *kv, int64_t ldkv,
+                                  const int32_t *rptr, int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim,
+                                  float slope, float drop_p, uint64_t seed, uint64_t offset,
+                                  const uint64_t *offset_dev, const float *att, const float *dagg, int64_t lddagg,
+                                  float *dq, uint16_t *dkv, int64_t lddkv, cudaStream_t stream) {
+  AttnArgs a{};
+  a.offset_dev = offset_dev;
+  a.q = q; a.ldq = ldq; a.ldkv = ldkv; a.rptr = rptr; a.n_dst = n_dst; a.n_dst_dev = n_dst_dev;
+  a.k = reinterpret_cast<const float *>(kv);
+  a.v = reinterpret_cast<const float *>(kv + dim);
+  a.kv_in_bf16 = 1;
+  a.heads = heads; a.dim = dim; a.slope = slope; a.drop_p = drop_p; a.seed = seed; a.offset = offset;
+  a.att = att; a.dagg = dagg; a.lddagg = lddagg; a.dq = dq; a.lddkv = lddkv;
+  a.dk = reinterpret_cast<float *>(dkv);
+  a.dv = reinterpret_cast<float *>(dkv + dim);
   a.kv_bf16 = 1;
   return launch_bwd(a, stream);
 }

@@ -37,6 +37,7 @@
 // issuing work, drains what it already issued (again bounded), frees its
 // tensor memory and exits.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <algorithm>
 #include <cstring>
 #include <vector>
@@ -101,6 +102,7 @@ struct BfProb {
   // the ones column is B's column K, 2: it is A's column N - 1 (swapped form)
   int kind, a_mn, b_mn, k1, K, N, Kp, bn, rt, nt, ones, accumulate, db_accumulate, max_splits;
   int swap, ktot, nseg, seg_at[3], seg_len[3], seg_to[3];
+  int c_bf16;                // NT / NN: C holds bf16 (round to nearest even), written, not accumulated
   uint32_t idesc;
   int64_t M;
   const int32_t *M_dev;
@@ -359,6 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
       float *const out = tn ? q.P + (int64_t)it.z * q.N * q.Kp : q.C;
       const float *const bias = tn ? nullptr : q.bias;
       const bool accum = !tn && q.accumulate;
+      const bool c16 = q.c_bf16 != 0;
       const int64_t row0 = it.r0 + qd * 32;
       const int nrows = rows - row0 < 32 ? (int)max(rows - row0, (int64_t)0) : 32;
 #pragma unroll 1
@@ -370,7 +373,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
         for (int k = 0; k < 32; ++k) stg[lane * kStagePitch + k] = __uint_as_float(r[k]);
         __syncwarp();
         const int col = it.c0 + c0 + lane;
-        if (c0 + lane < bn && col < ncols) {
+        if (c16 && c0 + lane < bn && col < ncols) {
+          const float bv = bias ? bias[col] : 0.f;
+          uint16_t *o = reinterpret_cast<uint16_t *>(out) + row0 * ld + col;
+          const float *sv = stg + lane;
+#pragma unroll 8
+          for (int rr = 0; rr < nrows; ++rr) {
+            const __nv_bfloat16 hv = __float2bfloat16_rn(sv[rr * kStagePitch] + bv);
+            o[rr * ld] = *reinterpret_cast<const uint16_t *>(&hv);
+          }
+        } else if (c0 + lane < bn && col < ncols) {
           const float bv = bias ? bias[col] : 0.f;
           float *o = out + row0 * ld + col;
           const float *sv = stg + lane;
@@ -522,7 +534,7 @@ bool problem_ok(const fb_gemm_bf16_problem &p) {
   if (p.M < 0 || p.M > (int64_t)1 << 30 || p.N < 1 || p.K < 1) return false;
   if (!p.A || !al16(p.A) || p.lda % 8 || !p.B || !al16(p.B) || p.ldb % 8) return false;
   if (p.kind == FB_GEMM_TN) {
-    if (p.nseg < 0 || p.nseg > 3 || p.lda < p.N || p.ldb < p.K || !p.C) return false;
+    if (p.c_bf16 || p.nseg < 0 || p.nseg > 3 || p.lda < p.N || p.ldb < p.K || !p.C) return false;
     if (p.nseg == 0) return p.ldc >= p.K;
     int end = 0;
     for (int g = 0; g < p.nseg; ++g) {
@@ -532,6 +544,7 @@ bool problem_ok(const fb_gemm_bf16_problem &p) {
     return end <= p.K;
   }
   if (!p.C || p.ldc < p.N || p.ldb < (p.kind == FB_GEMM_NT ? p.K : p.N)) return false;
+  if (p.c_bf16 && p.accumulate) return false;
   if (p.A2 && p.k1 < p.K) {
     const int ka = p.ka > 0 ? p.ka : p.k1;
     return p.k1 >= 8 && p.k1 % 8 == 0 && ka <= p.k1 && p.lda >= ka && al16(p.A2) && p.lda2 % 8 == 0 &&
@@ -601,6 +614,7 @@ int build_prob(BfProb &q, const fb_gemm_bf16_problem &p, float *ws) {
     const bool two = p.A2 && p.k1 < p.K;
     q.k1 = two ? p.k1 : p.K;
     q.bias = p.bias;
+    q.c_bf16 = p.c_bf16;
     q.a_mn = 0;
     q.b_mn = p.kind == FB_GEMM_NN ? 1 : 0;
     q.bn = q.b_mn ? bn_mnmajor(p.N) : bn_kmajor(p.N);

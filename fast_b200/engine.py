@@ -170,8 +170,9 @@ class FusedStep:
 
     def _layer_fwd_bf16(self, l, blk, h, node_table, edge_table, offset_dev, training):
         """_layer_fwd with bf16 projections: bf16 projection rows from the
-        gather, K|V, Q and w_out products of bf16 operands accumulated in fp32;
-        attention, tail and everything after in fp32."""
+        gather, K|V, Q and w_out products of bf16 operands accumulated in fp32,
+        K|V stored as bf16; attention (fp32 arithmetic), tail and everything
+        after in fp32."""
         lp = self.layers[l]
         L, D, dn, de, dtime = lp.L, lp.D, lp.dn, lp.de, lp.dtime
         nd, E = blk.n_dst, blk.n_edges
@@ -191,7 +192,8 @@ class FusedStep:
             hsrc = hdst = {}
         X, kx = ops.gather_time_encode_bf16(E, f=edge_table if de > 0 else None, f_idx=blk.eid, dt=blk.dt_edges,
                                             w=wv, b=bt, device=dev, n_rows_dev=E_dev, dn=dn, de=de, **hsrc)
-        KV = torch.empty(E, 2 * D, device=dev)
+        # K|V stored as bf16 rows: the projection's bf16 output is the attention's input
+        KV = torch.empty(E, 2 * D, device=dev, dtype=torch.bfloat16)
         probs = [dict(kind=ops.NT, A=X[:, :kx], B=lp.W_kv_bf[:, :kx], bias=lp.b_kv, out=KV, M_dev=E_dev)]
         if dn > 0:
             Qin, kq = ops.gather_time_encode_bf16(nd, w=wv, b=bt, device=dev, n_rows_dev=nd_dev, dn=dn, **hdst)
@@ -205,8 +207,8 @@ class FusedStep:
             ops.gemm_bf16_group(probs, name="gemm_group:kv_q")
             ops.gemm_group([dict(kind=ops.NT, A=Qin, B=L.w_q.weight, bias=L.w_q.bias, out=Q)], name="gemm_group:q1")
         p_att = L.att_dropout_p if training else 0.0
-        agg, att = ops.attn_fwd(Q, KV[:, :D], KV[:, D:], blk.rptr, L.num_head, L.negative_slope, p_att,
-                                0x5EED + l, 0, n_dst_dev=nd_dev, offset_dev=offset_dev)
+        agg, att = ops.attn_fwd_kvbf16(Q, KV, blk.rptr, L.num_head, L.negative_slope, p_att, 0x5EED + l, 0,
+                                       n_dst_dev=nd_dev, offset_dev=offset_dev)
         agg_bf = torch.empty(nd, lp.ka, device=dev, dtype=torch.bfloat16)
         ops.cast_bf16([(agg, agg_bf[:, :D], nd_dev)])
         Z = torch.empty(nd, D, device=dev)
@@ -256,10 +258,8 @@ class FusedStep:
             dh = torch.empty(dh_rows, dn, device=dev)
             probs.append(dict(kind=ops.NN, A=dZb, B=lp.W_out_bf[:, lp.ka:lp.ka + dn], out=dh[:nd], M_dev=nd_dev))
         ops.gemm_bf16_group(probs, name="gemm_group:bwd_dz")
-        KV = st["KV"]
-        dQ, dKV = ops.attn_bwd_bf16kv(st["Q"], KV[:, :D], KV[:, D:], blk.rptr, st["att"], dagg, L.num_head,
-                                      L.negative_slope, st["p_att"], 0x5EED + l, 0, n_dst_dev=nd_dev,
-                                      offset_dev=st["offset_dev"])
+        dQ, dKV = ops.attn_bwd_kvbf16(st["Q"], st["KV"], blk.rptr, st["att"], dagg, L.num_head, L.negative_slope,
+                                      st["p_att"], 0x5EED + l, 0, n_dst_dev=nd_dev, offset_dev=st["offset_dev"])
         X = st["A"]
         v = torch.empty(D, device=dev)            # sum over rows of dQ
         # the K|V weight and bias gradient over the whole projection row: one

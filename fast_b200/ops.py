@@ -229,7 +229,11 @@ def gemm_bf16_group(problems, name="gemm_bf16_group"):
         for t in (A, B, A2):
             if t is not None:
                 _bf16_rows(t, "gemm_bf16_group operand")
-        _f32_rows(out, "gemm_bf16_group output")
+        c16 = out.dtype == torch.bfloat16
+        if c16:
+            _bf16_rows(out, "gemm_bf16_group output")
+        else:
+            _f32_rows(out, "gemm_bf16_group output")
         M = A.shape[0]
         if kind == TN:
             N, K = A.shape[1], B.shape[1]
@@ -251,7 +255,7 @@ def gemm_bf16_group(problems, name="gemm_bf16_group"):
                                  ptr(B), B.stride(0), ptr(p.get("bias")), ptr(out), out.stride(0),
                                  M, _p(p.get("M_dev")), N, K, acc, ptr(db), int(acc if dba is None else bool(dba)),
                                  A.shape[1] if A2 is not None else 0, len(segs), pad3([g[0] for g in segs]),
-                                 pad3([g[1] for g in segs]), pad3([g[2] for g in segs]))
+                                 pad3([g[1] for g in segs]), pad3([g[2] for g in segs]), int(c16))
         keep.append((A, B, A2, out, db))
         nbytes += 2 * (M * K + N * K) + 4 * M * N
         flops += 2 * M * N * K
@@ -320,6 +324,43 @@ def gather_time_encode_bf16(n_rows, h=None, h_idx=None, h_off=0, f=None, f_idx=N
                          ptr(dt), ptr(w), ptr(b), dtime, ptr(out), out.stride(0), n_rows, _p(n_rows_dev),
                          stream_ptr()))
     return out, width
+
+
+def attn_fwd_kvbf16(q, kv, rptr, heads, slope, drop_p=0.0, seed=0, offset=0, n_dst_dev=None, offset_dev=None):
+    """attn_fwd on bf16 K|V rows kv [E, 2D] (K then V): agg, att fp32."""
+    nd = rptr.numel() - 1
+    E, D2 = kv.shape
+    D = D2 // 2
+    _bf16_rows(kv, "attn_fwd_kvbf16 kv")
+    ldq = 0 if (q.shape[0] == 1 and nd != 1) else q.stride(0)
+    att = torch.empty(E, heads, device=kv.device, dtype=torch.float32)
+    agg = torch.empty(nd, D, device=kv.device, dtype=torch.float32)
+    qrows = nd if ldq else 1
+    nbytes = 4 * (qrows * D + (nd + 1) + nd * D + E * heads) + 2 * 2 * E * D
+    _launch("attn_fwd", nbytes, 0, 1,
+            lambda: call("fb_attn_fwd_kvbf16", ptr(q), ldq, ptr(kv), kv.stride(0), ptr(rptr), nd, _p(n_dst_dev),
+                         heads, D, slope, drop_p, seed, offset, _p(offset_dev), ptr(att), ptr(agg), agg.stride(0),
+                         stream_ptr()))
+    return agg, att
+
+
+def attn_bwd_kvbf16(q, kv, rptr, att, dagg, heads, slope, drop_p=0.0, seed=0, offset=0, n_dst_dev=None,
+                    offset_dev=None):
+    """attn_bwd on bf16 K|V rows: dq fp32 [Nd, D], dK|dV bf16 [E, 2D]."""
+    nd = rptr.numel() - 1
+    E, D2 = kv.shape
+    D = D2 // 2
+    _bf16_rows(kv, "attn_bwd_kvbf16 kv")
+    ldq = 0 if (q.shape[0] == 1 and nd != 1) else q.stride(0)
+    dq = torch.empty(nd, D, device=kv.device, dtype=torch.float32)
+    dkv = torch.empty(E, 2 * D, device=kv.device, dtype=torch.bfloat16)
+    qrows = nd if ldq else 1
+    nbytes = 4 * (qrows * D + nd * D + E * heads + (nd + 1) + nd * D) + 2 * 4 * E * D
+    _launch("attn_bwd", nbytes, 0, 1,
+            lambda: call("fb_attn_bwd_kvbf16", ptr(q), ldq, ptr(kv), kv.stride(0), ptr(rptr), nd, _p(n_dst_dev),
+                         heads, D, slope, drop_p, seed, offset, _p(offset_dev), ptr(att), ptr(dagg),
+                         dagg.stride(0), ptr(dq), ptr(dkv), dkv.stride(0), stream_ptr()))
+    return dq, dkv
 
 
 def attn_bwd_bf16kv(q, k, v, rptr, att, dagg, heads, slope, drop_p=0.0, seed=0, offset=0, n_dst_dev=None,

@@ -137,6 +137,20 @@ int fb_attn_bwd_bf16kv(const float *q, int64_t ldq, const float *k, const float 
                        float slope, float drop_p, uint64_t seed, uint64_t offset, const uint64_t *offset_dev,
                        const float *att, const float *dagg, int64_t lddagg, float *dq, uint16_t *dk, uint16_t *dv,
                        int64_t lddkv, cudaStream_t stream);
+/* fb_attn_fwd / fb_attn_bwd_bf16kv on bf16 K|V rows kv[E, ldkv] (K then V,
+ * dim columns each, ldkv == 2 dim, ldkv % 8 == 0, dim <= 128): the bf16
+ * projection mode, where the K|V projection stores bf16.  Softmax, dropout
+ * and the sums run in fp32; the backward writes dq fp32 and dK|dV as bf16
+ * rows in the same interleaved layout. */
+int fb_attn_fwd_kvbf16(const float *q, int64_t ldq, const uint16_t *kv, int64_t ldkv, const int32_t *rptr,
+                       int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim, float slope, float drop_p,
+                       uint64_t seed, uint64_t offset, const uint64_t *offset_dev, float *att, float *agg,
+                       int64_t ldagg, cudaStream_t stream);
+int fb_attn_bwd_kvbf16(const float *q, int64_t ldq, const uint16_t *kv, int64_t ldkv, const int32_t *rptr,
+                       int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim, float slope, float drop_p,
+                       uint64_t seed, uint64_t offset, const uint64_t *offset_dev, const float *att,
+                       const float *dagg, int64_t lddagg, float *dq, uint16_t *dkv, int64_t lddkv,
+                       cudaStream_t stream);
 /* Sticky error bits of the attention kernels on the current device (2 = a
  * bounded wait for a shared-memory bulk copy timed out and the warp gave up);
  * synchronises; clear resets. */
@@ -332,6 +346,9 @@ typedef struct fb_gemm_bf16_problem {
                     projection row in one problem; the kernel then tiles X's
                     columns along the MMA's M side, which reads X once */
   int seg_at[3], seg_len[3], seg_to[3];
+  int c_bf16;    /* NT / NN: C is bf16 (bit patterns, round to nearest even; no
+                    accumulate) -- the K|V projection feeding the attention's
+                    bf16 K|V path */
 } fb_gemm_bf16_problem;
 size_t fb_gemm_bf16_group_ws_bytes(const fb_gemm_bf16_problem *probs, int n);
 int fb_gemm_bf16_group(const fb_gemm_bf16_problem *probs, int n, void *ws, size_t ws_bytes, cudaStream_t stream);

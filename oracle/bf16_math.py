@@ -6,8 +6,9 @@ this is the reference layer (layers.py:98-240, restated in ref_math.py) with
 bf16 rounding (round to nearest even) inserted exactly where the device's
 bf16 mode rounds, and nowhere else:
   forward   the K|V projection rows [h_src | f | cos(w dt + b)], the query
-            rows [h_dst | cos(b)] (layers with node input), the attention
-            output entering w_out, and the weights w_k, w_v, w_q, w_out;
+            rows [h_dst | cos(b)] (layers with node input), the projected
+            K and V (stored as bf16), the attention output entering w_out,
+            and the weights w_k, w_v, w_q, w_out;
   backward  the gradients entering the projection-gradient products: dK|dV,
             dQ (layers with node input) and dZ (the w_out output).
 Products of rounded operands are exact; everything else (attention,
@@ -87,8 +88,10 @@ def layer_forward_bf16(layer, row, col, dt, n_dst, h=None, f=None):
     zero_time_feat = time_encode(layer.time_enc, torch.zeros(n_dst, dtype=torch.float32))
     parts = ([h[n_dst:]] if dn else []) + ([f] if de else []) + [time_feat]
     X = R(torch.cat(parts, dim=1))
-    K = G(X @ R(layer.w_k.weight).T + layer.w_k.bias)
-    V = G(X @ R(layer.w_v.weight).T + layer.w_v.bias)
+    # K and V are stored as bf16 by the projection (forward rounding), and
+    # their gradients are rounded where they enter the gradient products
+    K = R(G(X @ R(layer.w_k.weight).T + layer.w_k.bias))
+    V = R(G(X @ R(layer.w_v.weight).T + layer.w_v.bias))
     Wq = layer.w_q.weight
     if dn:
         Qh = R(h[:n_dst])
