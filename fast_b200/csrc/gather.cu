@@ -312,7 +312,13 @@ constexpr int64_t kTeMaxParts = 592;   // two waves of two 800-thread CTAs per S
 // Time-encoding backward, stage 1: CTA (x = 32-column tile, y = row chunk)
 // with 8 warps striding over the chunk's rows, lanes over columns; the warps'
 // sums are combined in shared memory in a fixed order.
-__global__ void __launch_bounds__(256) k_te_bwd_part(const float *__restrict__ g, int64_t ldg,
+// g as fp32, or as bf16 bits (the bf16 projection mode's time-encoding input
+// gradient); either is summed in fp32
+__device__ __forceinline__ float te_g(const float *p) { return __ldg(p); }
+__device__ __forceinline__ float te_g(const uint16_t *p) { return __uint_as_float((uint32_t)__ldg(p) << 16); }
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_te_bwd_part(const T *__restrict__ g, int64_t ldg,
                                                      const float *__restrict__ dt, const float *__restrict__ w,
                                                      const float *__restrict__ b, int dtime, int64_t n_rows,
                                                      const int32_t *n_rows_dev, float *__restrict__ part) {
@@ -336,7 +342,7 @@ __global__ void __launch_bounds__(256) k_te_bwd_part(const float *__restrict__ g
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         tv[u] = __ldg(dt + r + 8 * u);
-        gv[u] = __ldg(g + (r + 8 * u) * ldg + c);
+        gv[u] = te_g(g + (r + 8 * u) * ldg + c);
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
@@ -347,7 +353,7 @@ __global__ void __launch_bounds__(256) k_te_bwd_part(const float *__restrict__ g
     }
     for (; r < r1; r += 8) {
       const float t = __ldg(dt + r);
-      const float gs = -sin_big(fmaf(t, wc, bc)) * __ldg(g + r * ldg + c);
+      const float gs = -sin_big(fmaf(t, wc, bc)) * te_g(g + r * ldg + c);
       sw = fmaf(gs, t, sw);
       sb += gs;
     }
@@ -371,7 +377,8 @@ __global__ void __launch_bounds__(256) k_te_bwd_part(const float *__restrict__ g
 constexpr int kTeGroups = 8;
 constexpr int kTeColsMax = 512;
 
-__global__ void __launch_bounds__(1024) k_te_bwd_rows(const float *__restrict__ g, int64_t ldg,
+template <typename T>
+__global__ void __launch_bounds__(1024) k_te_bwd_rows(const T *__restrict__ g, int64_t ldg,
                                                       const float *__restrict__ dt, const float *__restrict__ w,
                                                       const float *__restrict__ b, int dtime, int groups,
                                                       int64_t n_rows, const int32_t *n_rows_dev,
@@ -396,7 +403,7 @@ __global__ void __launch_bounds__(1024) k_te_bwd_rows(const float *__restrict__ 
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         tv[u] = __ldg(dt + r + u * G);
-        gv[u] = __ldg(g + (r + u * G) * ldg + c);
+        gv[u] = te_g(g + (r + u * G) * ldg + c);
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
@@ -407,7 +414,7 @@ __global__ void __launch_bounds__(1024) k_te_bwd_rows(const float *__restrict__ 
     }
     for (; r < r1; r += G) {
       const float t = __ldg(dt + r);
-      const float gs = -sin_big(fmaf(t, wc, bc)) * __ldg(g + r * ldg + c);
+      const float gs = -sin_big(fmaf(t, wc, bc)) * te_g(g + r * ldg + c);
       sw = fmaf(gs, t, sw);
       sb += gs;
     }
@@ -515,9 +522,12 @@ extern "C" size_t fb_time_encode_bwd_ws_bytes(int64_t n_rows, int dtime) {
   return (size_t)(parts * 2 * std::max(dtime, 1)) * sizeof(float);
 }
 
-extern "C" int fb_time_encode_bwd(const float *g, int64_t ldg, const float *dt, const float *w, const float *b,
-                                  int dtime, int64_t n_rows, const int32_t *n_rows_dev, float *dw, float *db,
-                                  void *ws, cudaStream_t stream) {
+namespace {
+
+template <typename T>
+int te_bwd(const T *g, int64_t ldg, const float *dt, const float *w, const float *b,
+           int dtime, int64_t n_rows, const int32_t *n_rows_dev, float *dw, float *db, void *ws,
+           cudaStream_t stream) {
   if (!g || !dt || !w || !b || !dw || !db || !ws || dtime < 1 || n_rows < 0)
     return fb::set_error(FB_ERR_ARG, "time_encode_bwd: bad argument");
   // launched for n_rows (a capacity when n_rows_dev is given); the kernels
@@ -528,15 +538,29 @@ extern "C" int fb_time_encode_bwd(const float *g, int64_t ldg, const float *dt, 
     // groups of dtime threads: as many as fit 1024 threads, at most kTeGroups
     const int groups = std::max(1, std::min(kTeGroups, 1024 / dtime));
     const int threads = (groups * dtime + 31) / 32 * 32;
-    FB_TRY_CUDA(fb::launch(k_te_bwd_rows, dim3(1, parts), threads, 0, stream, g, ldg, dt, w, b, dtime, groups,
+    FB_TRY_CUDA(fb::launch(k_te_bwd_rows<T>, dim3(1, parts), threads, 0, stream, g, ldg, dt, w, b, dtime, groups,
                            n_rows, n_rows_dev, part));
     FB_LAUNCHED("k_te_bwd_rows");
   } else {
     dim3 grid((dtime + 31) / 32, parts);
-    FB_TRY_CUDA(fb::launch(k_te_bwd_part, grid, 256, 0, stream, g, ldg, dt, w, b, dtime, n_rows, n_rows_dev, part));
+    FB_TRY_CUDA(fb::launch(k_te_bwd_part<T>, grid, 256, 0, stream, g, ldg, dt, w, b, dtime, n_rows, n_rows_dev, part));
     FB_LAUNCHED("k_te_bwd_part");
   }
   FB_TRY_CUDA(fb::launch(k_te_bwd_reduce, (dtime * 32 + 255) / 256, 256, 0, stream, part, n_rows, n_rows_dev, dtime, dw, db));
   FB_LAUNCHED("k_te_bwd_reduce");
   return FB_OK;
+}
+
+}  // namespace
+
+extern "C" int fb_time_encode_bwd(const float *g, int64_t ldg, const float *dt, const float *w, const float *b,
+                                  int dtime, int64_t n_rows, const int32_t *n_rows_dev, float *dw, float *db,
+                                  void *ws, cudaStream_t stream) {
+  return te_bwd(g, ldg, dt, w, b, dtime, n_rows, n_rows_dev, dw, db, ws, stream);
+}
+
+extern "C" int fb_time_encode_bwd_bf16(const uint16_t *g, int64_t ldg, const float *dt, const float *w,
+                                       const float *b, int dtime, int64_t n_rows, const int32_t *n_rows_dev,
+                                       float *dw, float *db, void *ws, cudaStream_t stream) {
+  return te_bwd(g, ldg, dt, w, b, dtime, n_rows, n_rows_dev, dw, db, ws, stream);
 }

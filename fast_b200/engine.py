@@ -271,7 +271,8 @@ class FusedStep:
         dA_t = None
         if dtime > 0:
             t_at = lp.kv_segs[-1][0]
-            dA_t = torch.empty(E, dtime, device=dev)
+            # bf16, like the gradient of an autocast bf16 product; summed in fp32
+            dA_t = torch.empty(E, dtime, device=dev, dtype=torch.bfloat16)
             probs.append(dict(kind=ops.NN, A=dKV, B=lp.W_kv_bf[:, t_at:t_at + dtime], out=dA_t, M_dev=E_dev))
         if dn > 0:
             dQ_bf = torch.empty(nd, lp.ka, device=dev, dtype=torch.bfloat16)

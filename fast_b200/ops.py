@@ -257,7 +257,10 @@ def gemm_bf16_group(problems, name="gemm_bf16_group"):
                                  A.shape[1] if A2 is not None else 0, len(segs), pad3([g[0] for g in segs]),
                                  pad3([g[1] for g in segs]), pad3([g[2] for g in segs]), int(c16))
         keep.append((A, B, A2, out, db))
-        nbytes += 2 * (M * K + N * K) + 4 * M * N
+        if kind == TN:                     # reads A [M, N] and B [M, K]; writes the [N, K] gradient
+            nbytes += 2 * M * (N + K) + 4 * N * K
+        else:                              # reads A [M, K] and B; writes C [M, N] (bf16 or fp32)
+            nbytes += 2 * (M * K + N * K) + (2 if c16 else 4) * M * N
         flops += 2 * M * N * K
     n = len(problems)
     dev = problems[0]["A"].device
@@ -506,11 +509,15 @@ def gather_time_encode(n_rows, h=None, h_idx=None, h_off=0, f=None, f_idx=None, 
 
 
 def time_encode_bwd(g, dt, w, b, dw, db, n_dev=None):
-    """dw/db += gradient of cos(w*dt + b) given g = dL/dcos (rows at g.stride(0))."""
+    """dw/db += gradient of cos(w*dt + b) given g = dL/dcos (rows at g.stride(0));
+    g fp32 or bf16 (summed in fp32)."""
     n, dtime = g.shape
+    if g.dtype not in (torch.float32, torch.bfloat16) or g.stride(1) != 1:
+        raise ValueError("time_encode_bwd: g must be fp32 or bf16 with unit column stride")
+    fn, es = ("fb_time_encode_bwd_bf16", 2) if g.dtype == torch.bfloat16 else ("fb_time_encode_bwd", 4)
     ws = torch.empty(int(lib.fb_time_encode_bwd_ws_bytes(n, dtime)), device=g.device, dtype=torch.uint8)
-    _launch("time_encode_bwd", 4 * n * (dtime + 1), 0, 2,
-            lambda: call("fb_time_encode_bwd", ptr(g), g.stride(0), ptr(dt), ptr(w), ptr(b), dtime, n, _p(n_dev),
+    _launch("time_encode_bwd", es * n * dtime + 4 * n, 0, 2,
+            lambda: call(fn, ptr(g), g.stride(0), ptr(dt), ptr(w), ptr(b), dtime, n, _p(n_dev),
                          ptr(dw), ptr(db), ptr(ws), stream_ptr()))
 
 

@@ -256,6 +256,12 @@ size_t fb_time_encode_bwd_ws_bytes(int64_t n_rows, int dtime);
 int fb_time_encode_bwd(const float *g, int64_t ldg, const float *dt, const float *w, const float *b,
                        int dtime, int64_t n_rows, const int32_t *n_rows_dev, float *dw, float *db,
                        void *ws, cudaStream_t stream);
+/* The same with g as bf16 (raw bits), the bf16 projection mode's time-encoding
+ * input gradient; the sums are fp32, and equal fb_time_encode_bwd's on g
+ * widened to fp32.  Same workspace. */
+int fb_time_encode_bwd_bf16(const uint16_t *g, int64_t ldg, const float *dt, const float *w, const float *b,
+                            int dtime, int64_t n_rows, const int32_t *n_rows_dev, float *dw, float *db,
+                            void *ws, cudaStream_t stream);
 
 /* ------------------------------------------------------------------------- */
 /* fp32 projection GEMMs (torch.nn.Linear, layers.py:91-95).                  */

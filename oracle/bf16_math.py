@@ -10,7 +10,10 @@ bf16 mode rounds, and nowhere else:
             K and V (stored as bf16), the attention output entering w_out,
             and the weights w_k, w_v, w_q, w_out;
   backward  the gradients entering the projection-gradient products: dK|dV,
-            dQ (layers with node input) and dZ (the w_out output).
+            dQ (layers with node input) and dZ (the w_out output); and the
+            gradient of the K|V rows' time encoding cos(w dt + b), which the
+            device's product writes as bf16 (an autocast product's input
+            gradient is bf16 as well).
 Products of rounded operands are exact; everything else (attention,
 softmax, LayerNorm, predictor, loss) is fp64.  The Q-side time-encoding
 gradient takes the fp32 master w_q, as the device's fb_q_time_bwd does.
@@ -84,7 +87,7 @@ def layer_forward_bf16(layer, row, col, dt, n_dst, h=None, f=None):
         raise NotImplementedError("the bf16 restatement covers layers with time encoding")
     dn, de = layer.dim_node_feat, layer.dim_edge_feat
     rl = row.long()
-    time_feat = time_encode(layer.time_enc, dt)
+    time_feat = G(time_encode(layer.time_enc, dt))
     zero_time_feat = time_encode(layer.time_enc, torch.zeros(n_dst, dtype=torch.float32))
     parts = ([h[n_dst:]] if dn else []) + ([f] if de else []) + [time_feat]
     X = R(torch.cat(parts, dim=1))

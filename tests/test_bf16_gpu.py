@@ -299,6 +299,30 @@ def test_attn_bwd_bf16kv_is_the_rounded_fp32_gradient(cuda):
     assert torch.equal(dkv_b, dkv.to(torch.bfloat16))
 
 
+@pytest.mark.parametrize("E,e_dev", [(5000, 4444), (330000, 330000)])
+def test_time_encode_bwd_bf16_is_the_fp32_sum_of_the_widened_gradient(cuda, E, e_dev):
+    """fb_time_encode_bwd_bf16 on bf16 g gives fb_time_encode_bwd's result
+    on g widened to fp32, bit for bit (same partition, same summation order),
+    with the row count read on the device."""
+    from fast_b200 import ops
+    rng = np.random.default_rng(7)
+    d = 100
+    dt = torch.from_numpy((rng.random(E) * 2e8).astype(np.float32)).to(cuda)
+    w = torch.from_numpy(1 / 10 ** np.linspace(0, 9, d, dtype=np.float32)).to(cuda)
+    b = (torch.randn(d) * 0.1).to(cuda)
+    g16 = torch.randn(E, d).to(torch.bfloat16).to(cuda)
+    n_dev = torch.tensor([e_dev], dtype=torch.int32, device=cuda)
+    out = []
+    for g in (g16, g16.float()):
+        dw = torch.full((d,), 0.5, device=cuda)
+        db = torch.full((d,), -0.25, device=cuda)
+        ops.time_encode_bwd(g, dt, w, b, dw, db, n_dev=n_dev)
+        out.append((dw, db))
+    torch.cuda.synchronize()
+    assert torch.equal(out[0][0], out[1][0]) and torch.equal(out[0][1], out[1][1])
+    assert not torch.equal(out[0][0], torch.full_like(out[0][0], 0.5))
+
+
 def _bound(name):
     """Relative L2 bound against the bf16-rounding oracle (a tensor also
     passes when it is within 5x the error of the oracle's own fp32 run: each
