@@ -51,3 +51,19 @@ def test_dropin_modules_expose_reference_names():
         assert hasattr(sampler_core.ParallelSampler, meth), meth
     for acc in ["row", "col", "eid", "ts", "dts", "nodes", "dim_in", "dim_out", "uniE", "invE", "cntE"]:
         assert hasattr(sampler_core.TemporalGraphBlock, acc), acc
+
+
+def test_wrappers_reject_bad_operands_before_any_launch():
+    """Host-side checks of the ops wrappers: operands of the wrong type or
+    layout raise ValueError before the library is called (no GPU needed)."""
+    import pytest
+    import torch
+    from fast_b200 import ops
+    d = torch.zeros(4, dtype=torch.float32)
+    with pytest.raises(ValueError):                          # fp16 gradient
+        ops.time_encode_bwd(torch.zeros(4, 3, dtype=torch.float16), d, d[:3], d[:3], d[:3], d[:3])
+    with pytest.raises(ValueError):                          # column stride != 1
+        ops.time_encode_bwd(torch.zeros(3, 4).t(), d, d[:3], d[:3], d[:3], d[:3])
+    a = torch.zeros(16, 8, dtype=torch.float32)
+    with pytest.raises(ValueError):                          # fp32 operand to the bf16 GEMM
+        ops.gemm_bf16_group([dict(kind=ops.NT, A=a, B=a, out=torch.zeros(16, 16))])
