@@ -54,6 +54,9 @@ def parse():
                          "(one JSON line per kernel instead of the training-step line)")
     ap.add_argument("--suite-scale", type=float, default=1.0,
                     help="--suite kernels: fraction of the config-5 block sizes (small cases for ncu captures)")
+    ap.add_argument("--suite-table-rows", type=int, default=None,
+                    help="--suite bf16: rows of the edge-feature table the gather indexes at random "
+                         "(default 4 M x --suite-scale)")
     ap.add_argument("--cuda-profiler-range", action="store_true",
                     help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--path", default="fused", choices=["fused", "autograd"],
@@ -628,7 +631,7 @@ def run_bf16_suite(args):
     g.manual_seed(5)
     Nd, fan, D, dn, de, dt_ = int(132_000 * args.suite_scale), 10, 100, 413, 186, 100
     E = Nd * fan
-    rows_tab = int(4_000_000 * args.suite_scale)
+    rows_tab = args.suite_table_rows or int(4_000_000 * args.suite_scale)
     ntab = torch.zeros(16_700, ops.pad8(dn), device=dev, dtype=torch.bfloat16)
     ntab[:, :dn] = torch.randn(16_700, dn, device=dev, generator=g)
     etab = torch.zeros(rows_tab, ops.pad8(de), device=dev, dtype=torch.bfloat16)
@@ -671,8 +674,8 @@ def run_bf16_suite(args):
     Wb = torch.zeros(2 * D, ops.pad8(K), device=dev, dtype=torch.bfloat16)
     Wb[:, :K] = torch.randn(2 * D, K, device=dev, generator=g) * 0.05
     bkv = torch.zeros(2 * D, device=dev)
-    KV = torch.empty(E, 2 * D, device=dev)
-    timed("k_bf_group (K|V projection, NT)", E * (2 * K + 4 * 2 * D), 2 * E * 2 * D * K,
+    KV = torch.empty(E, 2 * D, device=dev, dtype=torch.bfloat16)      # K|V stored as bf16, as in the step
+    timed("k_bf_group (K|V projection, NT, bf16 output)", E * (2 * K + 2 * 2 * D), 2 * E * 2 * D * K,
           lambda: ops.gemm_bf16_group([dict(kind=ops.NT, A=X[:, :K], B=Wb[:, :K], bias=bkv, out=KV)]),
           "M=%d, N=%d, K=%d" % (E, 2 * D, K))
     dkv = (torch.randn(E, 2 * D, device=dev, generator=g)).to(torch.bfloat16)
@@ -683,8 +686,9 @@ def run_bf16_suite(args):
     timed("k_bf_group (K|V weight + bias gradient, TN over the row's 3 segments)", E * (2 * K + 2 * 2 * D),
           2 * E * 2 * D * (dn + de + dt_ + 1),
           lambda: ops.gemm_bf16_group(tn), "M=%d, N=%d, K=%d+%d+%d+1" % (E, 2 * D, dn, de, dt_))
-    dAt = torch.empty(E, dt_, device=dev)
-    timed("k_bf_group (time-encoding input gradient, NN)", E * (2 * 2 * D + 4 * dt_), 2 * E * dt_ * 2 * D,
+    dAt = torch.empty(E, dt_, device=dev, dtype=torch.bfloat16)       # bf16, as in the step
+    timed("k_bf_group (time-encoding input gradient, NN, bf16 output)", E * (2 * 2 * D + 2 * dt_),
+          2 * E * dt_ * 2 * D,
           lambda: ops.gemm_bf16_group([dict(kind=ops.NN, A=dkv, B=Wb[:, t_at:t_at + dt_], out=dAt)]),
           "M=%d, N=%d, K=%d" % (E, dt_, 2 * D))
     q = torch.randn(Nd, D, device=dev, generator=g) * 0.5
@@ -695,6 +699,15 @@ def run_bf16_suite(args):
     timed("k_attn_bwd (bulk-copy path, bf16 dK|dV)",
           4 * (2 * Nd * D + 2 * E * D + E * 2 + (Nd + 1) + Nd * D) + 2 * 2 * E * D, 0,
           lambda: ops.attn_bwd_bf16kv(q, kvf[:, :D], kvf[:, D:], rptr, att, dagg, 2, 0.2, 0.1, 1, 2),
+          "Nd=%d, E=%d, D=%d, H=2, dropout 0.1" % (Nd, E, D))
+    # the step's attention: bf16 K|V rows in, bf16 dK|dV out
+    kvb = kvf.to(torch.bfloat16)
+    timed("k_attn_fwd (bulk-copy path, bf16 K|V rows)", 4 * (Nd * D + (Nd + 1) + Nd * D + E * 2) + 2 * 2 * E * D,
+          0, lambda: ops.attn_fwd_kvbf16(q, kvb, rptr, 2, 0.2, 0.1, 1, 2),
+          "Nd=%d, E=%d, D=%d, H=2, dropout 0.1" % (Nd, E, D))
+    timed("k_attn_bwd (bulk-copy path, bf16 K|V rows and dK|dV)",
+          4 * (2 * Nd * D + E * 2 + (Nd + 1) + Nd * D) + 2 * 4 * E * D, 0,
+          lambda: ops.attn_bwd_kvbf16(q, kvb, rptr, att, dagg, 2, 0.2, 0.1, 1, 2),
           "Nd=%d, E=%d, D=%d, H=2, dropout 0.1" % (Nd, E, D))
     return 0
 
