@@ -254,7 +254,7 @@ def run_reference(args):
         _, cfg = workload_graph(args, cfg)
     threads = len(os.sched_getaffinity(0))
     graph, ef, nf = cpu_workload(cfg, args.data)
-    gB = cfg.batch * args.gpus          # the fast arm's global batch
+    gB = cfg.batch if cfg.sharded else cfg.batch * args.gpus     # the fast arm's global batch
     step, reset, kind = cpu_reference_step_fn(cfg, graph, ef, nf, threads, gB)
     warm, timed = epoch_schedule(graph.train_end // gB, args.warmup, args.steps)
     reset()
@@ -268,8 +268,8 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": data_label(args, cfg),
+        "higher_is_better": True, "scaling": "strong" if cfg.sharded else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": data_label(args, cfg),
         "config": {"workload": cfg.name, "global_batch": gB, "fanout": list(cfg.fanout),
                    "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge,
                    "batches": SCHEDULE_NOTE},
