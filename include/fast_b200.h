@@ -249,7 +249,8 @@ int fb_gather_time_encode_bf16(const void *h, int h_bf16, int64_t ldh, const int
                                const int32_t *f_idx, int de, const float *dt, const float *w, const float *b,
                                int dtime, uint16_t *A, int64_t lda, int64_t n_rows, const int32_t *n_rows_dev,
                                cudaStream_t stream);
-/* Gradient of the time encoding: with g = dL/dcos(w*dt+b) (rows at g + r*ldg),
+/* Gradient of the time encoding (TimeEncode, layers.py:17-29; autograd in the
+ * reference): with g = dL/dcos(w*dt+b) (rows at g + r*ldg),
  * dw[j] += sum_r -sin(w_j dt_r + b_j) dt_r g[r,j],  db[j] += sum_r -sin(..) g[r,j].
  * `ws` must hold fb_time_encode_bwd_ws_bytes(n_rows, dtime) bytes. */
 size_t fb_time_encode_bwd_ws_bytes(int64_t n_rows, int dtime);
