@@ -9,7 +9,8 @@
 * fb_cast_bf16, fb_gather_time_encode_bf16, fb_attn_bwd_bf16kv and the bf16
   output of the GEMM are bit-exact against round-to-nearest-even of the fp32
   kernels' outputs; the attention on bf16 K|V rows (fb_attn_fwd_kvbf16 /
-  fb_attn_bwd_kvbf16) equals the fp32 attention on the same, rounded, rows.
+  fb_attn_bwd_kvbf16) equals the fp32 attention on the same, rounded, rows;
+  fb_time_encode_bwd_bf16 equals fb_time_encode_bwd on the widened gradient.
 * A whole FusedStep in the bf16 mode against oracle/bf16_math.py: the
   reference layer in fp64 with bf16 rounding at exactly the device's
   rounding points, on the oracle sampler's blocks.  Relative L2 error
@@ -299,14 +300,14 @@ def test_attn_bwd_bf16kv_is_the_rounded_fp32_gradient(cuda):
     assert torch.equal(dkv_b, dkv.to(torch.bfloat16))
 
 
-@pytest.mark.parametrize("E,e_dev", [(5000, 4444), (330000, 330000)])
-def test_time_encode_bwd_bf16_is_the_fp32_sum_of_the_widened_gradient(cuda, E, e_dev):
+@pytest.mark.parametrize("E,e_dev,d", [(5000, 4444, 100), (330000, 330000, 100), (5000, 4999, 600)])
+def test_time_encode_bwd_bf16_is_the_fp32_sum_of_the_widened_gradient(cuda, E, e_dev, d):
     """fb_time_encode_bwd_bf16 on bf16 g gives fb_time_encode_bwd's result
     on g widened to fp32, bit for bit (same partition, same summation order),
-    with the row count read on the device."""
+    with the row count read on the device; 600 columns take the 32-column
+    tile kernel instead of the one for rows of up to 512."""
     from fast_b200 import ops
     rng = np.random.default_rng(7)
-    d = 100
     dt = torch.from_numpy((rng.random(E) * 2e8).astype(np.float32)).to(cuda)
     w = torch.from_numpy(1 / 10 ** np.linspace(0, 9, d, dtype=np.float32)).to(cuda)
     b = (torch.randn(d) * 0.1).to(cuda)
