@@ -67,3 +67,22 @@ def test_wrappers_reject_bad_operands_before_any_launch():
     a = torch.zeros(16, 8, dtype=torch.float32)
     with pytest.raises(ValueError):                          # fp32 operand to the bf16 GEMM
         ops.gemm_bf16_group([dict(kind=ops.NT, A=a, B=a, out=torch.zeros(16, 16))])
+
+
+def test_import_fails_loudly_without_the_library():
+    """No fallback: with libfast_b200.so absent, importing the binding (and
+    so every op) raises ImportError naming the build command."""
+    import subprocess
+    import sys
+    code = ("import os, sys\n"
+            "real = os.path.exists\n"
+            "os.path.exists = lambda p: False if str(p).endswith('libfast_b200.so') else real(p)\n"
+            "try:\n"
+            "    import fast_b200.ops\n"
+            "except ImportError as e:\n"
+            "    print('IMPORT-ERROR', e)\n"
+            "    sys.exit(0)\n"
+            "sys.exit(3)\n")
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr[-2000:]
+    assert "IMPORT-ERROR" in r.stdout and "fast_b200.build" in r.stdout
