@@ -1,21 +1,30 @@
-"""Benchmark of the temporal-attention training step (TGAT 2-layer, config 2).
+"""Benchmark of the temporal-attention training step (TGAT 2-layer).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl fast|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl fast|reference] [--config 5|2|...]
 
-One step = one chronological batch of 600 positive edges + 600 negatives per
-GPU (weak scaling: the global batch is 600*N, each rank a contiguous slice):
-2-hop uniform 10x10 temporal sampling, feature gather + time encoding,
-Q/K/V projections, edge softmax + aggregate, w_out/LayerNorm, edge
-predictor, BCE, backward, Adam (reference train.py:307-393).
+Default workload: config 5, the north star's scaling configuration (TGAT
+2-layer, recent 10x10, 16,700 nodes / 191 M edges, 413-d node and 186-d edge
+features, bf16 projections with fp32 softmax / LayerNorm / loss / Adam).  One
+step = one chronological global batch of 4,000 positive edges + 4,000
+negatives, split evenly over the N ranks (strong scaling): temporal sampling
+(the global batch advances every rank's time pointers), feature gather + time
+encoding, Q/K/V projections, edge softmax + aggregate, w_out/LayerNorm, edge
+predictor, BCE, backward, gradient all-reduce, Adam (reference
+train.py:307-393).  `--config 2` is the fp32 uniform 10x10 line (600 + 600
+per GPU, weak scaling).
 
 `value`   positive training edges/s with graph, features and batch lists
           resident in HBM (device-timed, max over ranks).
-`e2e`     the same through the reference-facing API with host buffers: numpy
-          roots/timestamps handed to ParallelSampler.sample() (H2D inside the
-          timed region) and the loss read back to the host every step.
+`e2e`     the same through the product's public training API with host
+          buffers: numpy roots/timestamps of every step go through pinned
+          staging into the captured step (GraphTrainer.step_host_pipelined),
+          H2D inside the timed region, and every step's loss is read back.
 `--impl reference` times the reference's CPU path of the same step: the
           reference sampler built from its own source (oracle/_ref, all host
-          threads) + the fp32 CPU restatement of layers.py/modules.py + Adam.
+          threads) + the fp32 CPU restatement of layers.py/modules.py
+          (oracle/ref_math.py over the parameter tree of oracle/ref_model.py)
+          + torch.optim.Adam.  It imports nothing from fast_b200 that loads
+          the product's library.
 """
 import argparse
 import json
@@ -39,11 +48,15 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="fast", choices=["fast", "reference"])
-    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--config", type=int, default=5)
     ap.add_argument("--data", default=None,
                     help="dataset directory in the reference's format (edges.csv + ext_full.npz) instead of the "
                          "config's synthetic graph; feature widths and the model still come from --config")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the cpu_baseline sample")
+    ap.add_argument("--cpu-edges", type=int, default=4_000_000,
+                    help="config 5 on the CPU: prefix subsample of the graph (its fp32 edge table is 142 GB)")
+    ap.add_argument("--cpu-batch-frac", type=float, default=0.25,
+                    help="config 5 on the CPU: each step trains on this fraction of the global batch")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=5)
     ap.add_argument("--eager", action="store_true", help="launch kernels step by step instead of a CUDA graph")
@@ -172,16 +185,32 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+class _RowsModulo:
+    """An edge-feature table of `rows` rows standing in for a larger one:
+    edge id e reads row e mod rows (rows drawn like the full table's, gathered
+    at the same random positions of a table far larger than the caches)."""
+
+    def __init__(self, table):
+        self.t = table
+        self.shape = (None, table.shape[1])
+
+    def __getitem__(self, idx):
+        return self.t[idx % self.t.shape[0]]
+
+
 def cpu_reference_step_fn(cfg, graph, edge_feats_cpu, node_feats_cpu, threads, B):
     """Closures running one reference-CPU training step on a batch index and
-    resetting the sampler (epoch start); returns (step, reset, kind)."""
+    resetting the sampler (epoch start); returns (step, reset, kind).  The
+    sampler is the reference's own (oracle/_ref, built from its source) when
+    present; the model is ref_math (layers.py/modules.py, DGL path) over the
+    parameter tree of oracle/ref_model.py, trained with torch.optim.Adam.
+    Nothing here loads the product's library."""
     import torch
-    from fast_b200.data import model_params
-    from fast_b200.model import GeneralModel
     from oracle import ref_math
+    from oracle.ref_model import GeneralModel
     from oracle.sampler import OracleSampler, load_reference
     torch.set_num_threads(threads)
-    sp, mp, gp, tp = model_params(cfg)
+    sp, mp, gp, tp = cpu_model_params(cfg)
     ref = load_reference()
     kind = "reference" if ref is not None else "port"
     S = ref.ParallelSampler if ref is not None else OracleSampler
@@ -192,23 +221,41 @@ def cpu_reference_step_fn(cfg, graph, edge_feats_cpu, node_feats_cpu, threads, B
                          sp, mp, gp, tp)
     opt = torch.optim.Adam(model.parameters(), lr=tp["lr"])
     rng = np.random.default_rng(1)
+    stats = dict(edges=0, steps=0)
 
-    def step(i):
-        """Training step on chronological batch i (positive edges [i*B, (i+1)*B))."""
-        b0 = i * B
+    def step(i, stride=None):
+        """Training step on chronological batch i: positive edges
+        [i * stride, i * stride + B) (stride defaults to B)."""
+        b0 = i * (stride or B)
         src, dst, t = graph.src[b0:b0 + B], graph.dst[b0:b0 + B], graph.ts[b0:b0 + B]
         roots = np.concatenate([src, dst, rng.integers(0, graph.n_nodes, B).astype(np.int32)])
         rts = np.concatenate([t, t, t]).astype(np.float32)
         sampler.sample(roots, rts, [])
         blocks = sampler.get_ret()
+        stats["edges"] += sum(len(b.row()) for b in blocks)
+        stats["steps"] += 1
         opt.zero_grad()
         pp, pn = ref_math.model_forward(model, blocks, node_feats_cpu, edge_feats_cpu)
         loss = ref_math.bce_loss(pp, pn)
         loss.backward()
         opt.step()
-        return float(loss)
+        return loss.item()
 
-    return step, sampler.reset, kind
+    return step, sampler.reset, kind, stats
+
+
+def cpu_model_params(cfg):
+    """sample/memory/gnn/train parameters of the config's reference model
+    (config/TGAT.yml with the CLI overrides of train.py:98), as
+    fast_b200.data.model_params gives them; restated here so that the CPU arm
+    imports nothing from the product."""
+    layers = len(cfg.fanout)
+    sample = dict(layer=layers, neighbor=list(cfg.fanout), strategy=cfg.strategy, prop_time=False, history=1,
+                  duration=0)
+    memory = dict(type="none", dim_out=0)
+    gnn = dict(arch="transformer_attention", layer=layers, att_head=2, dim_time=100, dim_out=100)
+    train = dict(lr=0.0001, dropout=0.1, att_dropout=0.1)
+    return sample, memory, gnn, train
 
 
 SCHEDULE_NOTE = ("warm-up = the epoch's first W batches; timed = K batches spread evenly over the rest of the "
@@ -228,19 +275,60 @@ def epoch_schedule(n_batches, warmup, steps):
     return warm, timed
 
 
-def cpu_workload(cfg, data=None):
+def cpu_plan(args, cfg):
+    """What the CPU arm runs for a config: (graph edges, table rows, fraction
+    of the global batch per step, note).  Configs 1-4 run at full size.
+    Config 5's fp32 tables (142 GB of edge features) exceed the host, so its
+    CPU arm samples a 20 M-edge graph drawn like config 5's (same 16,700 nodes,
+    endpoint and time distributions; every fan-out still fills), gathers edge
+    features from a 4 M-row table at the edge id modulo 4 M, and trains each
+    step on the first quarter of the chronological global batch."""
+    if not cfg.sharded or args.data:
+        return cfg.edges, cfg.edges, 1.0, "full graph"
+    n = min(cfg.edges, max(args.cpu_edges * 5, 1))
+    rows = min(n, args.cpu_edges)
+    return n, rows, args.cpu_batch_frac, (
+        "%d-edge graph drawn like %s (same nodes, endpoint and time distributions), edge features from a %d-row "
+        "fp32 table at edge id mod %d, each step %.0f%% of the global batch" %
+        (n, cfg.name, rows, rows, 100 * args.cpu_batch_frac))
+
+
+def cpu_workload(cfg, data=None, n_edges=None, table_rows=None):
     import torch
     from fast_b200.data import make_graph
     if data:
         from fast_b200.dataio import load_graph
         graph = load_graph(data)
     else:
-        graph = make_graph(cfg)
+        graph = make_graph(cfg, n_edges=n_edges)
     g = torch.Generator()
     g.manual_seed(7)
-    ef = torch.randn(cfg.edges, cfg.d_edge, generator=g) if cfg.d_edge else None
+    rows = table_rows or len(graph.src)
+    ef = torch.randn(rows, cfg.d_edge, generator=g) if cfg.d_edge else None
+    if ef is not None and rows < len(graph.src):
+        ef = _RowsModulo(ef)
     nf = torch.randn(cfg.nodes, cfg.d_node, generator=g) if cfg.d_node else None
     return graph, ef, nf
+
+
+def bench_config(args, cfg, world, B, gB):
+    """The `config` object of both arms' lines (the workload, not the arm)."""
+    bf16 = cfg.dtype == "bf16"
+    return {"workload": cfg.name, "global_batch": gB, "local_batch": B, "fanout": list(cfg.fanout),
+            "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_node": cfg.d_node,
+            "d_edge": cfg.d_edge, "parallelism": "dp%d" % world, "batches": SCHEDULE_NOTE,
+            "l2": "inputs larger than L2 (%.1f GB edge-feature table gathered at random rows)" %
+                  (cfg.edges * ((cfg.d_edge + 7) // 8 * 16 if bf16 else cfg.d_edge * 4) / 1e9)}
+
+
+def batch_sizes(cfg, world):
+    """(per-rank batch, global batch) of a step."""
+    if cfg.sharded:
+        # one global batch split across the ranks (config 5: 4,000 + 4,000 on 1/2/4/8 GPUs)
+        if cfg.batch % world:
+            raise SystemExit("%s: its global batch of %d does not split over %d ranks" % (cfg.name, cfg.batch, world))
+        return cfg.batch // world, cfg.batch
+    return cfg.batch, cfg.batch * world
 
 
 # ----------------------------------------------------------------------------- reference arm
@@ -248,34 +336,40 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    world = args.gpus
     from fast_b200.data import CONFIGS
     cfg = CONFIGS[args.config]
+    cfg_line = cfg
     if args.data:
-        _, cfg = workload_graph(args, cfg)
+        _, cfg_line = workload_graph(args, cfg, device=False)
+    elif args.edges:
+        import dataclasses
+        cfg_line = dataclasses.replace(cfg, edges=args.edges)
+    B, gB = batch_sizes(cfg_line, world)
     threads = len(os.sched_getaffinity(0))
-    graph, ef, nf = cpu_workload(cfg, args.data)
-    gB = cfg.batch if cfg.sharded else cfg.batch * args.gpus     # the fast arm's global batch
-    step, reset, kind = cpu_reference_step_fn(cfg, graph, ef, nf, threads, gB)
+    n_edges, rows, frac, note = cpu_plan(args, cfg_line)
+    graph, ef, nf = cpu_workload(cfg_line, args.data, n_edges=n_edges, table_rows=rows)
+    cB = max(1, int(round(gB * frac)))
+    step, reset, kind, stats = cpu_reference_step_fn(cfg_line, graph, ef, nf, threads, cB)
     warm, timed = epoch_schedule(graph.train_end // gB, args.warmup, args.steps)
     reset()
     for i in warm:
-        step(i)
+        step(i, gB)
+    stats.update(edges=0, steps=0)
     t0 = time.perf_counter()
     for i in timed:
-        step(i)
+        step(i, gB)
     dt = time.perf_counter() - t0
-    value = args.steps * gB / dt
+    value = args.steps * cB / dt
+    sample = ("%d batches of %d+%d roots (%s), spread over one epoch after %d warm-up batches; %.0f sampled edges "
+              "per step" % (args.steps, cB, 2 * cB, note, len(warm), stats["edges"] / max(stats["steps"], 1)))
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
-        "higher_is_better": True, "scaling": "strong" if cfg.sharded else "weak", "vs_baseline": None,
-        "dtype": "f32", "data": data_label(args, cfg),
-        "config": {"workload": cfg.name, "global_batch": gB, "fanout": list(cfg.fanout),
-                   "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge,
-                   "batches": SCHEDULE_NOTE},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
-                         "sample": "%d batches of %d+%d roots spread over one epoch of the full graph "
-                                   "(after %d warm-up batches)" % (args.steps, gB, 2 * gB, len(warm))},
+        "higher_is_better": True, "scaling": "strong" if cfg_line.sharded else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": data_label(args, cfg_line),
+        "config": bench_config(args, cfg_line, world, B, gB),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -299,7 +393,7 @@ def run_fast(args):
     ops.USE_TC = args.gemm == "tc"
     from fast_b200.train import GraphTrainer, Trainer
     cfg = CONFIGS[args.config]
-    graph, cfg = workload_graph(args, cfg)
+    graph, cfg = workload_graph(args, cfg, device=True)
     bf16 = cfg.dtype == "bf16"
     if bf16:
         # bf16 tables, rows padded to 8 columns, generated on the device
@@ -309,15 +403,7 @@ def run_fast(args):
     sp, mp, gp, tp = model_params(cfg)
     fused = args.path == "fused"
     prec = dict(precision="bf16", feat_dims=(cfg.d_node, cfg.d_edge)) if bf16 else {}
-    if cfg.sharded:
-        # one global batch split across the ranks (config 5: 4,000 + 4,000 on 1/2/4/8 GPUs)
-        if cfg.batch % world:
-            raise SystemExit("config %d: its global batch of %d does not split over %d ranks" %
-                             (args.config, cfg.batch, world))
-        B, gB = cfg.batch // world, cfg.batch
-    else:
-        B = cfg.batch
-        gB = B * world
+    B, gB = batch_sizes(cfg, world)
     if args.eager:
         tr = Trainer(graph, nf, ef, sp, mp, gp, tp, dev, rank=rank, world=world, fused=fused, **prec)
     else:
@@ -378,9 +464,14 @@ def run_fast(args):
     ms = float(t.item())
     value = args.steps * gB / (ms / 1000.0)
 
-    # end-to-end through the reference-facing API with host buffers, over the
-    # same batches from a fresh epoch
+    # end-to-end through the product's training API with host buffers, over
+    # the same batches from a fresh epoch.  The batches' edge lists come to
+    # the host before the timed region, as a user's data loader would hold
+    # them; each step's roots and times are built, staged and copied inside it.
     rng = np.random.default_rng(5)
+    host_edges = {i: tuple(_host(a[i * gB:(i + 1) * gB]) for a in (graph.src, graph.dst, graph.ts)) for i in timed}
+    lo = tr.rank * B
+    sel = np.concatenate([np.arange(lo, lo + B), gB + np.arange(lo, lo + B), 2 * gB + np.arange(lo, lo + B)])
     tr.reset_epoch()
     if world > 1:
         dist.barrier()
@@ -390,15 +481,11 @@ def run_fast(args):
     host_step = getattr(tr, "step_host_pipelined", tr.step_host)
     t0 = time.perf_counter()
     for i in timed:
-        b0, b1 = i * gB, (i + 1) * gB
+        src_np, dst_np, t_np = host_edges[i]
         # the global batch [src | dst | neg] (same rng seed on every rank), then this rank's slice
-        t_np = graph.ts[b0:b1]
-        groots = np.concatenate([graph.src[b0:b1], graph.dst[b0:b1],
-                                 rng.integers(0, graph.n_nodes, gB).astype(np.int32)])
+        groots = np.concatenate([src_np, dst_np, rng.integers(0, graph.n_nodes, gB).astype(np.int32)])
         gts = np.concatenate([t_np, t_np, t_np]).astype(np.float32)
-        lo = tr.rank * B
-        sel = np.concatenate([np.arange(lo, lo + B), gB + np.arange(lo, lo + B), 2 * gB + np.arange(lo, lo + B)])
-        host_step(groots[sel], gts[sel], groots, gts, **e0_kw(b0))
+        host_step(groots[sel], gts[sel], groots, gts, **e0_kw(i * gB))
     if hasattr(tr, "finish_pipelined"):
         tr.finish_pipelined()
     torch.cuda.synchronize()
@@ -415,12 +502,17 @@ def run_fast(args):
     tr.reset_epoch()
     args.profile_steps = max(1, min(args.profile_steps, len(timed)))
     prof = [timed[(2 * j + 1) * len(timed) // (2 * args.profile_steps)] for j in range(args.profile_steps)]
+    sampled = []
     for i in prof:
         groots, gts = tr.batch_roots(i * gB, (i + 1) * gB)
         roots, rts = tr.local_of(groots, gts)
         Trainer.step_device(tr, roots, rts, groots, gts, **e0_kw(i * gB))
+        sampled.append(sum(int(d[1]) for d in tr.sampler.dims()))
     kern = ops.TIMER.summary()
     ops.TIMER = None
+    t_samp = torch.tensor([float(np.mean(sampled))], device=dev)
+    if world > 1:
+        dist.all_reduce(t_samp)
 
     if rank != 0:
         if world > 1:
@@ -459,27 +551,27 @@ def run_fast(args):
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "strong" if cfg.sharded else "weak",
         "vs_baseline": None, "dtype": "bf16" if bf16 else "f32", "data": data_label(args, cfg),
-        "config": {"workload": cfg.name, "global_batch": gB, "local_batch": B, "fanout": list(cfg.fanout),
-                   "strategy": cfg.strategy, "nodes": cfg.nodes, "edges": cfg.edges, "d_edge": cfg.d_edge,
-                   "parallelism": "dp%d" % world, "launch": "eager" if args.eager else "cuda_graph",
-                   "batches": SCHEDULE_NOTE,
-                   "gemm": args.gemm, "step": args.path,
-                   "l2": "inputs larger than L2 (%.1f GB edge-feature table gathered at random rows)" %
-                         (cfg.edges * ((cfg.d_edge + 7) // 8 * 16 if bf16 else cfg.d_edge * 4) / 1e9),
-                   "precision": ("bf16 projections (w_q, w_k, w_v, w_out and their gradient products on bf16 "
-                                 "operands, fp32 accumulation); attention, softmax, LayerNorm, loss and Adam "
-                                 "in fp32" if bf16 else "fp32")},
+        "config": bench_config(args, cfg, world, B, gB),
+        "impl_config": {"launch": "eager" if args.eager else "cuda_graph", "gemm": args.gemm, "step": args.path,
+                        "precision": ("bf16 projections (w_q, w_k, w_v, w_out and their gradient products on "
+                                      "bf16 operands, fp32 accumulation); attention, softmax, LayerNorm, loss and "
+                                      "Adam in fp32" if bf16 else "fp32")},
+        # every rank copies its own roots and times (3B x 8 bytes) and, with several ranks, the global
+        # batch's (3gB x 8 bytes, for the time pointers), and reads back one fp32 loss
         "e2e": {"value": e2e_value, "unit": UNIT,
-                "h2d_bytes_per_step": world * 3 * B * 8 + (world * world * 3 * B * 8 if world > 1 else 0),
+                "h2d_bytes_per_step": world * 3 * B * 8 + (world * 3 * gB * 8 if world > 1 else 0),
                 "d2h_bytes_per_step": world * 4},
+        "workload_stats": {"sampled_edges_per_step": round(float(t_samp.item()), 1),
+                           "note": "edges of every layer's block summed over the ranks, mean of the profiled "
+                                   "steps (the same timed batches)"},
         "gpu_launches": int(launches),
         "roofline": roof,
         "kernels": kernels,
         "clocks": clocks,
         "last_loss": float(loss),
     }
-    if world == 1 and not args.no_cpu_baseline and getattr(tr, "mailbox", None) is None and not bf16:
-        line["cpu_baseline"] = cpu_baseline(cfg, warm, timed, args.cpu_seconds, args.data)
+    if world == 1 and not args.no_cpu_baseline and getattr(tr, "mailbox", None) is None:
+        line["cpu_baseline"] = cpu_baseline(args, cfg, args.cpu_seconds)
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -487,27 +579,32 @@ def run_fast(args):
     return 0
 
 
-def cpu_baseline(cfg, warm, timed, budget_s, data=None):
-    """Reference CPU path on the GPU run's batch schedule (1 GPU), stopped
-    after ~budget_s; a stop before the end keeps the earlier, smaller batches,
-    which favours the CPU."""
+def cpu_baseline(args, cfg, budget_s):
+    """The reference CPU path (as --impl reference) on the GPU run's batch
+    schedule (1 GPU), stopped after ~budget_s; a stop before the end keeps
+    the earlier, smaller batches, which favours the CPU."""
     threads = len(os.sched_getaffinity(0))
-    graph, ef, nf = cpu_workload(cfg, data)
-    step, reset, kind = cpu_reference_step_fn(cfg, graph, ef, nf, threads, cfg.batch)
+    n_edges, rows, frac, note = cpu_plan(args, cfg)
+    graph, ef, nf = cpu_workload(cfg, args.data, n_edges=n_edges, table_rows=rows)
+    _, gB = batch_sizes(cfg, 1)
+    cB = max(1, int(round(gB * frac)))
+    warm, timed = epoch_schedule(graph.train_end // gB, args.warmup, args.steps)
+    step, reset, kind, stats = cpu_reference_step_fn(cfg, graph, ef, nf, threads, cB)
     reset()
     for i in warm:
-        step(i)
+        step(i, gB)
+    stats.update(edges=0, steps=0)
     n, t0 = 0, time.perf_counter()
     for i in timed:
-        step(i)
+        step(i, gB)
         n += 1
-        el = time.perf_counter() - t0
-        if el > budget_s:
+        if time.perf_counter() - t0 > budget_s:
             break
     el = time.perf_counter() - t0
-    return {"value": n * cfg.batch / el, "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": "%d of the %d timed batches (%d+%d roots each, spread over one epoch of the full %s graph), "
-                      "%.1f s" % (n, len(timed), cfg.batch, 2 * cfg.batch, cfg.name, el)}
+    return {"value": n * cB / el, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": "%d of the %d timed batches (%d+%d roots each; %s; spread over one epoch), %.1f s, %.0f "
+                      "sampled edges per step" % (n, len(timed), cB, 2 * cB, note, el,
+                                                  stats["edges"] / max(stats["steps"], 1))}
 
 
 # ----------------------------------------------------------------------------- kernel roofline suite
@@ -720,16 +817,16 @@ def data_label(args, cfg):
     return "synthetic (seeded, %s shapes)" % cfg.name
 
 
-def workload_graph(args, cfg):
+def workload_graph(args, cfg, device=True):
     """The config's synthetic graph, or the dataset of --data (the config then
-    takes that graph's node and edge counts)."""
+    takes that graph's node and edge counts).  device: build the bf16 configs'
+    graphs on the current GPU (config 5: 191 M edges in seconds)."""
     import dataclasses
     from fast_b200.data import make_graph, make_graph_device
     if not args.data:
         n = args.edges or cfg.edges
         cfg = dataclasses.replace(cfg, edges=n)
-        if cfg.dtype == "bf16":
-            # built on the device (config 5: 191 M edges in seconds, not minutes)
+        if device and cfg.dtype == "bf16":
             import torch
             return make_graph_device(cfg, torch.device("cuda", torch.cuda.current_device())), cfg
         return make_graph(cfg, n_edges=n), cfg
@@ -737,6 +834,11 @@ def workload_graph(args, cfg):
     g = load_graph(args.data)
     return g, dataclasses.replace(cfg, name=os.path.basename(os.path.normpath(args.data)), nodes=g.n_nodes,
                                   edges=len(g.src))
+
+
+def _host(a):
+    """A numpy copy of an edge-list slice (numpy array or device tensor)."""
+    return a.cpu().numpy() if hasattr(a, "cpu") else np.asarray(a)
 
 
 def main():

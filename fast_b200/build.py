@@ -46,14 +46,18 @@ def build_lib(verbose=False):
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
     hdrs = sorted(glob.glob(os.path.join(CSRC, "*.cuh"))) + [os.path.join(INC, "fast_b200.h")]
     os.makedirs(BUILD, exist_ok=True)
-    objs = []
+    objs, todo = [], []
     for s in srcs:
         o = os.path.join(BUILD, os.path.basename(s) + ".o")
         if _newer(o, [s] + hdrs):
-            if verbose:
-                print("nvcc", os.path.basename(s), flush=True)
-            _run([NVCC] + NVCC_FLAGS + ["-c", s, "-o", o])
+            todo.append((s, o))
         objs.append(o)
+    if todo:
+        from concurrent.futures import ThreadPoolExecutor
+        if verbose:
+            print("nvcc", " ".join(os.path.basename(s) for s, _ in todo), flush=True)
+        with ThreadPoolExecutor(max_workers=max(1, min(len(todo), os.cpu_count() or 1))) as ex:
+            list(ex.map(lambda so: _run([NVCC] + NVCC_FLAGS + ["-c", so[0], "-o", so[1]]), todo))
     if _newer(LIB, objs):
         _run([NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda"])
     return LIB

@@ -42,6 +42,7 @@ _SIGS = {
     "fb_sampler_reset": (_I, [_P, _P]),
     "fb_sampler_sample": (_I, [_P, _P, _P, _I64, _I, _P]),
     "fb_sampler_update_pointers": (_I, [_P, _P, _P, _I64, _P]),
+    "fb_sampler_sample_shard": (_I, [_P, _P, _P, _I64, _P, _P, _I64, _P]),
     "fb_sampler_num_blocks": (_I, [_P]),
     "fb_sampler_block": (_I, [_P, _I, _P]),
     "fb_sampler_dims": (_I, [_P, _P, _P]),
@@ -217,6 +218,13 @@ class CSampler:
         r = np.ascontiguousarray(roots, dtype=np.int32)
         t = np.ascontiguousarray(root_ts, dtype=np.float32)
         check(lib.fb_sampler_sample(self.h, r.ctypes.data, t.ctypes.data, r.size, 0, stream_ptr()))
+
+    def sample_shard(self, roots, root_ts, global_roots, global_ts):
+        """One data-parallel rank's sample(): device (torch) tensors of this
+        rank's roots and of the global batch's (fb_sampler_sample_shard)."""
+        check(lib.fb_sampler_sample_shard(self.h, roots.data_ptr(), root_ts.data_ptr(), roots.numel(),
+                                          global_roots.data_ptr(), global_ts.data_ptr(), global_roots.numel(),
+                                          stream_ptr()))
 
     def dims(self):
         import numpy as np

@@ -419,6 +419,13 @@ struct fb_sampler {
   int32_t *dd_keys = nullptr, *dd_minpos = nullptr, *dd_slot = nullptr, *dd_uidx = nullptr;
   int2 *dd_part = nullptr;
   int64_t dd_cap_edges = 0, dd_table = 0;
+  // data-parallel shards: the global batch's blocks of every layer whose nodes
+  // advance a later layer's pointers, and their workspace
+  std::vector<BlockBuf> gblocks;
+  int32_t *gdims = nullptr;    // 8 per global block
+  int32_t *gws_cnt = nullptr, *gws_pick = nullptr;
+  int2 *gws_part = nullptr;
+  int64_t cap_g0 = 0;
   bool sampled = false;
 };
 
@@ -500,11 +507,17 @@ int ensure_capacity(fb_sampler *s, int64_t r0) {
   return FB_OK;
 }
 
-int run_layer_slot(fb_sampler *s, int bidx, const int32_t *roots, const float *rts, int64_t R_host,
-                   const int32_t *R_dev, int64_t R_cap, int use_ptr, int hist_i, int neighs, float offset,
-                   cudaStream_t st) {
+// Workspace of one block's count / scan / write passes.
+struct LayerWork {
+  int32_t *cnt;
+  int2 *part;
+  int32_t *pick;
+};
+
+int run_block(fb_sampler *s, BlockBuf &b, int32_t *dims, const LayerWork &w, int bidx, const int32_t *roots,
+              const float *rts, int64_t R_host, const int32_t *R_dev, int64_t R_cap, int use_ptr, int hist_i,
+              int neighs, float offset, cudaStream_t st) {
   const int nh = s->num_history;
-  BlockBuf &b = s->blocks[bidx];
   SampleArgs a;
   a.indptr = s->indptr; a.indices = s->indices; a.eid = s->eid; a.ts = s->ts;
   a.n_nodes = s->n_nodes;
@@ -517,16 +530,61 @@ int run_layer_slot(fb_sampler *s, int bidx, const int32_t *roots, const float *r
   a.key0 = (uint32_t)s->seed; a.key1 = (uint32_t)(s->seed >> 32);
   a.call_dev = s->call_dev; a.slot = (uint32_t)bidx;
   a.err = s->err;
-  a.pick = s->ws_pick;
-  int32_t *dims = s->dims + 8 * bidx;
+  a.pick = w.pick;
   const int nb = nblk(R_cap, kRootsPerCta);
-  FB_TRY_CUDA(fb::launch(k_sample_count, nb, kThreads, 0, st, a, s->ws_cnt, s->ws_part));
+  FB_TRY_CUDA(fb::launch(k_sample_count, nb, kThreads, 0, st, a, w.cnt, w.part));
   FB_LAUNCHED("k_sample_count");
-  FB_TRY_CUDA(fb::launch(k_scan_parts, 1, 1024, 0, st, s->ws_part, nb, R_host, R_dev, dims, b.rptr, b.cntE));
+  FB_TRY_CUDA(fb::launch(k_scan_parts, 1, 1024, 0, st, w.part, nb, R_host, R_dev, dims, b.rptr, b.cntE));
   FB_LAUNCHED("k_scan_parts");
-  FB_TRY_CUDA(fb::launch(k_sample_write, nb, kThreads, 0, st, a, s->ws_cnt, s->ws_part, b.row, b.col, b.eid, b.ts, b.dts,
+  FB_TRY_CUDA(fb::launch(k_sample_write, nb, kThreads, 0, st, a, w.cnt, w.part, b.row, b.col, b.eid, b.ts, b.dts,
                                           b.nodes, b.rptr, b.cntE, b.dte, b.nbr));
   FB_LAUNCHED("k_sample_write");
+  return FB_OK;
+}
+
+int run_layer_slot(fb_sampler *s, int bidx, const int32_t *roots, const float *rts, int64_t R_host,
+                   const int32_t *R_dev, int64_t R_cap, int use_ptr, int hist_i, int neighs, float offset,
+                   cudaStream_t st) {
+  const LayerWork w{s->ws_cnt, s->ws_part, s->ws_pick};
+  return run_block(s, s->blocks[bidx], s->dims + 8 * bidx, w, bidx, roots, rts, R_host, R_dev, R_cap, use_ptr,
+                   hist_i, neighs, offset, st);
+}
+
+// A layer after the first advances the pointers with the previous layer's
+// nodes when it samples with them (sampler_core.cpp:700-706).
+bool layer_uses_ptr(const fb_sampler *s, int l) {
+  return l == 0 || (s->prop_time && s->num_history == 1) || s->recent;
+}
+
+// Global blocks of the layers whose nodes advance a later layer's pointers:
+// layer l < L-1 when layer l+1 uses them.  g0 = global roots.
+int ensure_global_capacity(fb_sampler *s, int64_t g0) {
+  int nglob = 0;
+  for (int l = 0; l + 1 < s->num_layers; ++l)
+    if (layer_uses_ptr(s, l + 1)) nglob = l + 1;
+  if (nglob == 0) return FB_OK;
+  if (g0 <= s->cap_g0 && (int)s->gblocks.size() >= nglob) return FB_OK;
+  FB_TRY_CUDA(cudaDeviceSynchronize());
+  for (auto &b : s->gblocks) free_block(b);
+  void *ps[] = {s->gdims, s->gws_cnt, s->gws_pick, s->gws_part};
+  for (auto p : ps) if (p) cudaFree(p);
+  s->gblocks.assign(nglob, BlockBuf());
+  int64_t roots = g0, max_roots = 1, max_pick = 1;
+  for (int l = 0; l < nglob; ++l) {
+    const int64_t edges = roots * (int64_t)std::max(0, s->neigh[l]);
+    if (roots + edges > INT32_MAX) return fb::set_error(FB_ERR_UNSUPPORTED, "sampler: global blocks exceed int32");
+    int rc = alloc_block(s->gblocks[l], roots, edges);
+    if (rc) return rc;
+    max_roots = std::max(max_roots, roots);
+    max_pick = std::max(max_pick, edges);
+    roots += edges;
+  }
+  FB_TRY_CUDA(cudaMalloc(&s->gdims, 8 * 4 * nglob));
+  FB_TRY_CUDA(cudaMemset(s->gdims, 0, 8 * 4 * nglob));
+  FB_TRY_CUDA(cudaMalloc(&s->gws_cnt, max_roots * 4));
+  FB_TRY_CUDA(cudaMalloc(&s->gws_part, nblk(max_roots, kRootsPerCta) * sizeof(int2)));
+  FB_TRY_CUDA(cudaMalloc(&s->gws_pick, max_pick * 4));
+  s->cap_g0 = g0;
   return FB_OK;
 }
 
@@ -587,11 +645,13 @@ extern "C" int fb_sampler_destroy(fb_sampler *s) {
   cudaSetDevice(s->device);
   cudaDeviceSynchronize();
   for (auto &b : s->blocks) free_block(b);
+  for (auto &b : s->gblocks) free_block(b);
   if (s->owns_graph) {
     cudaFree(s->indptr); cudaFree(s->indices); cudaFree(s->eid); cudaFree(s->ts);
   }
   void *ps[] = {s->ts_ptr, s->dims, s->err, s->call_dev, s->roots_in, s->rts_in, s->ws_cnt, s->ws_part, s->ws_pick,
-                s->dd_keys, s->dd_minpos, s->dd_slot, s->dd_uidx, s->dd_part};
+                s->dd_keys, s->dd_minpos, s->dd_slot, s->dd_uidx, s->dd_part,
+                s->gdims, s->gws_cnt, s->gws_pick, s->gws_part};
   for (auto p : ps) if (p) cudaFree(p);
   cudaSetDevice(cur);
   delete s;
@@ -606,12 +666,25 @@ extern "C" int fb_sampler_reset(fb_sampler *s, cudaStream_t st) {
   return FB_OK;
 }
 
-extern "C" int fb_sampler_sample(fb_sampler *s, const int32_t *roots, const float *root_ts, int64_t n_roots,
-                                 int roots_on_device, cudaStream_t st) {
-  if (!s || n_roots < 0 || (n_roots > 0 && (!roots || !root_ts)))
-    return fb::set_error(FB_ERR_ARG, "fb_sampler_sample: bad argument");
+namespace {
+
+// sample() (sampler_core.cpp:597-712) over this process's roots.  With
+// g_roots (data-parallel shards), every pointer update that sample() over the
+// global batch would make is made instead of the local one: layer 0 advances
+// the pointers with the global roots, and a later layer with the nodes of the
+// global batch's previous-layer block, sampled here alongside the local one
+// (both read the same pointers).  The local roots are a subset of the global
+// ones and a max is idempotent, so the pointers, and every recent-k pick of
+// every layer, are those of one process sampling the global batch.
+int sample_impl(fb_sampler *s, const int32_t *roots, const float *root_ts, int64_t n_roots, int roots_on_device,
+                const int32_t *g_roots, const float *g_ts, int64_t n_global, cudaStream_t st) {
   int rc = ensure_capacity(s, n_roots);
   if (rc) return rc;
+  const bool global = g_roots != nullptr;
+  if (global) {
+    rc = ensure_global_capacity(s, n_global);
+    if (rc) return rc;
+  }
   const int32_t *r0 = roots;
   const float *t0 = root_ts;
   if (!roots_on_device && n_roots > 0) {
@@ -621,25 +694,31 @@ extern "C" int fb_sampler_sample(fb_sampler *s, const int32_t *roots, const floa
     t0 = s->rts_in;
   }
   const int nh = s->num_history;
-  std::vector<int64_t> cr, ce;
+  std::vector<int64_t> cr, ce, gcr, gce;
   block_caps(s, n_roots, cr, ce);
-  bool first = true;
+  if (global) block_caps(s, n_global, gcr, gce);
+  const int nglob = (int)s->gblocks.size();
   for (int l = 0; l < s->num_layers; ++l) {
-    int use_ptr = 0;
-    if (first || (s->prop_time && nh == 1) || s->recent) { first = false; use_ptr = 1; }
+    const int use_ptr = layer_uses_ptr(s, l) ? 1 : 0;
     const int neighs = s->neigh[l];
     // Roots of the pointer update before the history loop (sampler_core.cpp:464-476).
     const int32_t *ur = r0;
     const float *ut = t0;
     const int32_t *uR = nullptr;
-    if (l > 0) {
+    int64_t uR_host = n_roots, ucap = cr[l * nh];
+    if (global) {
+      ur = g_roots; ut = g_ts; uR_host = n_global; ucap = gcr[l * nh];
+      if (l > 0) {
+        ur = s->gblocks[l - 1].nodes; ut = s->gblocks[l - 1].ts; uR = s->gdims + 8 * (l - 1) + 3;
+      }
+    } else if (l > 0) {
       const int pb = (l - 1) * nh + nh - 1;
       ur = s->blocks[pb].nodes; ut = s->blocks[pb].ts; uR = s->dims + 8 * pb + 3;
     }
     const int64_t rcap = cr[l * nh];
-    if (use_ptr && rcap > 0) {
-      FB_TRY_CUDA(fb::launch(k_update_ptr, nblk(rcap * kGroup), kThreads, 0, st, s->indptr, s->ts, s->n_nodes, s->ts_ptr + (int64_t)nh * s->n_nodes,
-                                                    ur, ut, n_roots, uR, 0.f, s->err));
+    if (use_ptr && ucap > 0) {
+      FB_TRY_CUDA(fb::launch(k_update_ptr, nblk(ucap * kGroup), kThreads, 0, st, s->indptr, s->ts, s->n_nodes,
+                             s->ts_ptr + (int64_t)nh * s->n_nodes, ur, ut, uR_host, uR, 0.f, s->err));
       FB_LAUNCHED("k_update_ptr");
     }
     for (int i = 0; i < nh; ++i) {
@@ -660,12 +739,44 @@ extern "C" int fb_sampler_sample(fb_sampler *s, const int32_t *roots, const floa
       rc = run_layer_slot(s, l * nh + nh - 1 - i, hr, ht, n_roots, hR, rcap, use_ptr, i, neighs, offset, st);
       if (rc) return rc;
     }
+    if (global && l < nglob && gcr[l * nh] > 0) {
+      // the global batch's block of this layer, for the next layer's pointer update
+      const LayerWork w{s->gws_cnt, s->gws_part, s->gws_pick};
+      const int32_t *gr = l == 0 ? g_roots : s->gblocks[l - 1].nodes;
+      const float *gt = l == 0 ? g_ts : s->gblocks[l - 1].ts;
+      const int32_t *gR = l == 0 ? nullptr : s->gdims + 8 * (l - 1) + 3;
+      rc = run_block(s, s->gblocks[l], s->gdims + 8 * l, w, l * nh, gr, gt, n_global, gR, gcr[l * nh], use_ptr, 0,
+                     neighs, 0.f, st);
+      if (rc) return rc;
+    }
   }
   FB_TRY_CUDA(fb::launch(k_bump_call, 1, 1, 0, st, s->call_dev));
   FB_LAUNCHED("k_bump_call");
   s->call_index++;
   s->sampled = true;
   return FB_OK;
+}
+
+}  // namespace
+
+extern "C" int fb_sampler_sample(fb_sampler *s, const int32_t *roots, const float *root_ts, int64_t n_roots,
+                                 int roots_on_device, cudaStream_t st) {
+  if (!s || n_roots < 0 || (n_roots > 0 && (!roots || !root_ts)))
+    return fb::set_error(FB_ERR_ARG, "fb_sampler_sample: bad argument");
+  return sample_impl(s, roots, root_ts, n_roots, roots_on_device, nullptr, nullptr, 0, st);
+}
+
+extern "C" int fb_sampler_sample_shard(fb_sampler *s, const int32_t *roots, const float *root_ts, int64_t n_roots,
+                                       const int32_t *global_roots, const float *global_ts, int64_t n_global,
+                                       cudaStream_t st) {
+  if (!s || n_roots < 0 || n_global < n_roots || (n_roots > 0 && (!roots || !root_ts)) ||
+      (n_global > 0 && (!global_roots || !global_ts)))
+    return fb::set_error(FB_ERR_ARG, "fb_sampler_sample_shard: bad argument");
+  if (s->num_history != 1 || fabsf(s->wd) > 1e-7f)
+    return fb::set_error(FB_ERR_UNSUPPORTED,
+                         "fb_sampler_sample_shard: sharded sampling supports num_history 1 without a window");
+  if (n_global == 0) return sample_impl(s, roots, root_ts, n_roots, 1, nullptr, nullptr, 0, st);
+  return sample_impl(s, roots, root_ts, n_roots, 1, global_roots, global_ts, n_global, st);
 }
 
 extern "C" int fb_sampler_update_pointers(fb_sampler *s, const int32_t *roots, const float *root_ts, int64_t n_roots,

@@ -4,6 +4,7 @@
 // K7/K8, aggregate_shd_kernel.cu K9/K10, utils.cu).  One warp per segment,
 // fixed reduction order; only the scatter of arbitrary (unsorted) edge lists
 // uses float atomics, as the reference does.
+#include <atomic>
 #include <algorithm>
 #include <cfloat>
 #include "runtime.cuh"
@@ -234,20 +235,26 @@ extern "C" int fb_balanced_mask(const int32_t *ptr, int64_t n_ptr, int threshold
 }
 
 // ---- exclusive sum without any allocation ------------------------------------
-// Callers that cannot allocate device memory (code running while a CUDA graph
-// is being captured, hosts that hand the library a fixed memory budget, or
-// latency-critical loops where an allocator call would synchronise the device)
-// still need the scan's per-chunk partial sums somewhere.  They live in this
-// file-scope array: one int2 per 256-element chunk, 4096 chunks (32 KiB), so at
-// most 4096 * 256 = 1,048,576 elements per call.  Every GPU that loads the
-// library holds the array until the process exits.  All calls share it and it
-// keeps the last call's contents: the first kernel overwrites every chunk entry
-// a call uses before anything reads it, so nothing needs clearing, but two
-// calls whose kernels overlap on the GPU (different streams, no ordering)
-// corrupt each other's results.
+// Some callers cannot allocate device memory: a host that hands the library a
+// fixed memory budget and owns every allocation itself (an embedding runtime
+// with its own pool), or a latency-critical loop where a cudaMalloc would
+// synchronise the device.  They still need the scan's per-chunk partial sums
+// somewhere.  They live in this file-scope array: one int2 per 256-element
+// chunk, 4096 chunks (32 KiB), so at most 4096 * 256 = 1,048,576 elements per
+// call.  Every GPU that loads the library holds the array until the process
+// exits.  All calls share it and it keeps the last call's contents: the first
+// kernel overwrites every chunk entry a call uses before anything reads it, so
+// nothing needs clearing, but two calls whose kernels overlap on the GPU
+// (different streams, no ordering) corrupt each other's results.
 namespace {
 constexpr int64_t kStaticScanChunks = 4096;
-int2 *g_static_scan_scratch[64] = {nullptr};   // device address per device, from cudaGetSymbolAddress
+constexpr int kMaxDevices = 64;
+// The array's device address per device, from cudaGetSymbolAddress on the
+// first call there.  Atomic, so that host threads making their first calls at
+// the same time do not race on the cache (both store the same address).  The
+// address belongs to the device's primary context: after a cudaDeviceReset the
+// process must not call this entry point on that device again.
+std::atomic<int2 *> g_static_scan_scratch[kMaxDevices];
 }  // namespace
 
 static __device__ __align__(256) int2 g_scan_scratch[kStaticScanChunks];
@@ -259,15 +266,17 @@ extern "C" int fb_exclusive_sum_noalloc(const int32_t *in, int64_t n, int32_t *o
                          "exclusive_sum_noalloc: at most 1048576 elements (4096 chunks of 256) per call");
   int dev = 0;
   FB_TRY_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) return fb::set_error(FB_ERR_UNSUPPORTED, "exclusive_sum_noalloc: device index >= 64");
-  if (!g_static_scan_scratch[dev]) {
+  if (dev < 0 || dev >= kMaxDevices)
+    return fb::set_error(FB_ERR_UNSUPPORTED, "exclusive_sum_noalloc: device index >= 64");
+  int2 *part = g_static_scan_scratch[dev].load(std::memory_order_acquire);
+  if (!part) {
     // one-time set-up on this device: the host-side symbol is not a device
     // address, so ask the runtime for the array's address on the current device
     void *p = nullptr;
     FB_TRY_CUDA(cudaGetSymbolAddress(&p, g_scan_scratch));
-    g_static_scan_scratch[dev] = static_cast<int2 *>(p);
+    part = static_cast<int2 *>(p);
+    g_static_scan_scratch[dev].store(part, std::memory_order_release);
   }
-  int2 *part = g_static_scan_scratch[dev];
   const int nb = (int)std::max<int64_t>(1, (n + 255) / 256);
   k_xsum_part<<<nb, 256, 0, stream>>>(in, n, part);
   FB_LAUNCHED("k_xsum_part");

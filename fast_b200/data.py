@@ -75,6 +75,8 @@ def endpoints(rng, n_nodes, count, spec):
 
 @dataclasses.dataclass
 class TemporalGraph:
+    """The chronological edge list and its CSR, as numpy arrays or (a graph
+    built on the device) as device tensors."""
     src: np.ndarray
     dst: np.ndarray
     ts: np.ndarray          # float32, chronological
@@ -127,10 +129,11 @@ def make_graph_device(cfg, device, seed=42, n_edges=None):
     """make_graph's construction on the device, for graphs too large to build
     on the host in seconds (config 5: 191 M edges): Zipf endpoints, sorted
     float32 timestamps, the CSR by a stable sort of the chronological edge
-    list on the source id.  The CSR arrays stay device tensors; src, dst and
-    ts are also returned on the host (the end-to-end path feeds host roots).
-    Draws come from torch's device generator, so the graph differs from
-    make_graph's for the same seed."""
+    list on the source id.  Every array (the CSR and the chronological src,
+    dst and ts) stays a device tensor: at 191 M edges a host copy per rank
+    would cost 2.3 GB of host memory for each process.  Draws come from
+    torch's device generator, so the graph differs from make_graph's for the
+    same seed."""
     E = cfg.edges if n_edges is None else int(n_edges)
     N = cfg.nodes
     gen = torch.Generator(device=device)
@@ -159,7 +162,7 @@ def make_graph_device(cfg, device, seed=42, n_edges=None):
     ts_csr = ts[order]
     eid = order.to(torch.int32)
     del order
-    return TemporalGraph(src=src.cpu().numpy(), dst=dst.cpu().numpy(), ts=ts.cpu().numpy(),
+    return TemporalGraph(src=src, dst=dst, ts=ts,
                          indptr=indptr.to(torch.int32), indices=indices, eid=eid, ts_csr=ts_csr, n_nodes=N,
                          train_end=int(E * 0.70), val_end=int(E * 0.85))
 

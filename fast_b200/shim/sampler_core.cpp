@@ -6,6 +6,9 @@
 //
 // Additions for the device-resident training path:
 //   ParallelSampler.sample_device(roots, ts)   roots/ts already on the GPU
+//   ParallelSampler.sample_shard(roots, ts, global_roots, global_ts)
+//                                              one data-parallel rank's roots,
+//                                              pointers advanced by the global batch
 //   ParallelSampler.block_views()              zero-copy device views (valid
 //                                              until the next sample call)
 //   ParallelSampler.dims()                     per-block sizes (synchronises)
@@ -171,6 +174,23 @@ class Sampler {
                                      cur_stream()));
   }
 
+  // One data-parallel rank's sample(): its own device roots, with the time
+  // pointers advanced as one sample() over the global batch's roots would.
+  void sample_shard(torch::Tensor roots, torch::Tensor root_ts, torch::Tensor global_roots,
+                    torch::Tensor global_ts) {
+    for (const auto *t : {&roots, &root_ts, &global_roots, &global_ts})
+      TORCH_CHECK(t->is_cuda() && t->is_contiguous(), "sample_shard wants contiguous CUDA tensors");
+    TORCH_CHECK(roots.scalar_type() == torch::kInt32 && global_roots.scalar_type() == torch::kInt32 &&
+                    root_ts.scalar_type() == torch::kFloat32 && global_ts.scalar_type() == torch::kFloat32,
+                "roots int32, ts float32");
+    TORCH_CHECK(roots.numel() == root_ts.numel() && global_roots.numel() == global_ts.numel(),
+                "roots and ts differ in length");
+    const c10::cuda::CUDAGuard g(h->device);
+    check(fb_sampler_sample_shard(h->s, roots.data_ptr<int32_t>(), root_ts.data_ptr<float>(), roots.numel(),
+                                  global_roots.data_ptr<int32_t>(), global_ts.data_ptr<float>(),
+                                  global_roots.numel(), cur_stream()));
+  }
+
   std::vector<std::vector<int32_t>> dims() {
     const c10::cuda::CUDAGuard g(h->device);
     const int nb = fb_sampler_num_blocks(h->s);
@@ -296,6 +316,7 @@ PYBIND11_MODULE(sampler_core, m) {
            py::arg("csrFlag") = std::vector<int>())
       .def("sample_device", &Sampler::sample_device)
       .def("update_pointers", &Sampler::update_pointers)
+      .def("sample_shard", &Sampler::sample_shard)
       .def("reset", &Sampler::reset)
       .def("get_ret", &Sampler::get_ret)
       .def("dims", &Sampler::dims)

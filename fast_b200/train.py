@@ -212,7 +212,12 @@ class Trainer:
             use_ptr = first or sp["strategy"] == "recent" or (sp["prop_time"] and sp["history"] == 1)
             first = False
             n += (1 if use_ptr else 0) + 3 * sp["history"]
-        return n + 1 + (1 if self.world > 1 else 0)   # the call-counter bump (+ the global pointer update)
+        if self.world > 1:
+            # sharded sampling: the global batch's block of every layer whose nodes advance a later layer's
+            # pointers (count / scan / write each)
+            n += 3 * sum(1 for l in range(1, sp["layer"])
+                         if sp["strategy"] == "recent" or (sp["prop_time"] and sp["history"] == 1))
+        return n + 1   # the call-counter bump
 
     def reset_epoch(self):
         self.sampler.reset()
@@ -345,20 +350,27 @@ class Trainer:
         pointers, as one process training on the whole batch would.  Memory
         models also take e0, the id of the batch's first (positive) edge."""
         self._set_e0(e0)
-        if self.world > 1 and global_roots is not None:
-            self.sampler.update_pointers(global_roots, global_ts)
         sr, st = self._sample_roots(roots, root_ts)
-        ops.timed("sampler", lambda: self.sampler.sample_device(sr, st))
+        if self.world > 1 and global_roots is not None:
+            gr, gt = self._sample_roots(global_roots, global_ts)
+            ops.timed("sampler", lambda: self.sampler.sample_shard(sr, st, gr, gt))
+        else:
+            ops.timed("sampler", lambda: self.sampler.sample_device(sr, st))
         return self._train_on(self.blocks(), roots, root_ts)
 
     def step_host(self, roots_np, ts_np, global_roots_np=None, global_ts_np=None, e0=None):
         """End-to-end step through the reference-facing API: host roots in, host loss out."""
         self._set_e0(e0)
-        if self.world > 1 and global_roots_np is not None:
-            self.sampler.update_pointers(torch.from_numpy(global_roots_np).to(self.device),
-                                         torch.from_numpy(global_ts_np).to(self.device))
         sr, st = self._sample_roots(roots_np, ts_np)
-        self.sampler.sample(sr, st, [])
+        if self.world > 1 and global_roots_np is not None:
+            dv = self.device
+            gr, gt = self._sample_roots(global_roots_np, global_ts_np)
+            self.sampler.sample_shard(torch.from_numpy(np.ascontiguousarray(sr)).to(dv),
+                                      torch.from_numpy(np.ascontiguousarray(st)).to(dv),
+                                      torch.from_numpy(np.ascontiguousarray(gr)).to(dv),
+                                      torch.from_numpy(np.ascontiguousarray(gt)).to(dv))
+        else:
+            self.sampler.sample(sr, st, [])
         if self.mailbox is None:
             return float(self._train_on(self.blocks()))
         dev = self.device
@@ -423,10 +435,12 @@ class GraphTrainer(Trainer):
 
     # the body of one step on the static input buffers
     def _fwd_bwd(self):
-        if self.world > 1:
-            self.sampler.update_pointers(self.groots_buf, self.gts_buf)
         sr, st = self._sample_roots(self.roots_buf, self.ts_buf)
-        self.sampler.sample_device(sr, st)
+        if self.world > 1:
+            gr, gt = self._sample_roots(self.groots_buf, self.gts_buf)
+            self.sampler.sample_shard(sr, st, gr, gt)
+        else:
+            self.sampler.sample_device(sr, st)
         views = self.sampler.block_views()
         blocks = [StaticBlock(views[0], n_roots=sr.shape[0])] + [StaticBlock(v) for v in views[1:]]
         self._blocks = blocks

@@ -86,11 +86,27 @@ int fb_sampler_reset(fb_sampler *s, cudaStream_t stream);
 int fb_sampler_sample(fb_sampler *s, const int32_t *roots, const float *root_ts, int64_t n_roots,
                       int roots_on_device, cudaStream_t stream);
 /* Applies the first layer's pointer updates of sample() (update_ts_ptr,
- * :133-157) for device roots without sampling.  Data-parallel ranks call it
- * with the global batch's roots before sampling their own slice, so every
- * rank's time pointers equal the single-process ones (a max is idempotent). */
+ * :133-157) for device roots without sampling.  It advances the pointers the
+ * first layer samples with; data-parallel ranks sample with
+ * fb_sampler_sample_shard, which makes every layer's updates. */
 int fb_sampler_update_pointers(fb_sampler *s, const int32_t *roots, const float *root_ts, int64_t n_roots,
                                cudaStream_t stream);
+/* sample() of one data-parallel rank's shard (ParallelSampler::sample,
+ * :597-712, with update_ts_ptr :133-157 and the per-layer use_ptr rule
+ * :700-706).  roots/root_ts (device, n_roots) are this rank's roots, a subset
+ * of the global batch global_roots/global_ts (device, n_global).  Every
+ * pointer update that one sample() over the global batch makes is made here:
+ * layer 0 with the global roots, each later layer that samples with the
+ * pointers with the nodes of the global batch's previous-layer block, which
+ * this call samples alongside the rank's own.  Every block, of every layer,
+ * then holds exactly the picks that one process sampling the global batch
+ * makes for these roots (recent-k: bit for bit), and the pointers after the
+ * call are that process's.  num_history must be 1 with no window
+ * (FB_ERR_UNSUPPORTED otherwise).  Grows its buffers (synchronising the
+ * device) when n_global exceeds every earlier call. */
+int fb_sampler_sample_shard(fb_sampler *s, const int32_t *roots, const float *root_ts, int64_t n_roots,
+                            const int32_t *global_roots, const float *global_ts, int64_t n_global,
+                            cudaStream_t stream);
 /* Number of blocks from the last sample() (= num_layers * num_history), in
  * the reference's get_ret() order. */
 int fb_sampler_num_blocks(const fb_sampler *s);
@@ -211,14 +227,14 @@ int fb_segment_rows(const int32_t *indptr, int64_t n_seg, const int64_t *row, co
 size_t fb_exclusive_sum_ws_bytes(int64_t n);
 int fb_exclusive_sum(const int32_t *in, int64_t n, int32_t *out, void *ws, cudaStream_t stream);
 /* No counterpart in the reference.  fb_exclusive_sum for callers that cannot
- * allocate device memory -- code running while a CUDA graph is captured, hosts
- * that give the library a fixed memory budget, loops where an allocator call
- * would stall the device -- and so cannot provide `ws`.  The scratch is a
+ * allocate device memory and so cannot provide `ws`: a host that gives the
+ * library a fixed memory budget and owns every allocation itself, or a loop
+ * where an allocator call would synchronise the device.  The scratch is a
  * library-owned static device array (32 KiB, held by every GPU that loads the
  * library until exit); n is limited to 1,048,576 and larger n returns
  * FB_ERR_UNSUPPORTED.  It allocates nothing.  Its first call on a device looks
  * up the array's device address (cudaGetSymbolAddress), so make that first
- * call outside any stream capture.  All calls share the one array: calls whose
+ * call before any stream capture.  All calls share the one array: calls whose
  * kernels can overlap on the GPU (different streams without ordering) race. */
 int fb_exclusive_sum_noalloc(const int32_t *in, int64_t n, int32_t *out, cudaStream_t stream);
 

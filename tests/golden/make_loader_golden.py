@@ -20,7 +20,8 @@ import tempfile
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = "/root/reference"
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+from oracle.paths import REF_ROOT as REF  # noqa: E402
 
 
 def raw_edges(seed=5, n=3000):

@@ -29,9 +29,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = "/root/reference"
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.dirname(HERE))
+from oracle.paths import REF_ROOT as REF  # noqa: E402
 sys.path.insert(0, HERE)
 
 from conftest import small_graph  # noqa: E402

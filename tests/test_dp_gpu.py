@@ -3,13 +3,14 @@ training with the CUDA-graph trainer equals single-process training on the
 global batch.
 
 Each rank replays its captured step on a contiguous slice of every global
-batch, after advancing its time pointers with the global batch's roots
-(fb_sampler_update_pointers) and with the global negative list drawn from a
-generator seeded alike on every rank; gradients are averaged with one NCCL
-all-reduce of the flat gradient buffer.  With recent sampling and one layer
-the sampled blocks are then exactly the single process's, so losses and
-parameters agree to fp32 rounding.  (With two or more recent layers the
-deeper layers' pointer updates see only the rank's own hop-1 nodes.)
+batch, with the global negative list drawn from a generator seeded alike on
+every rank.  It samples its slice with fb_sampler_sample_shard: every layer's
+time-pointer update uses the global batch's roots of that layer (the roots
+for layer 0, the nodes of the global batch's previous-layer block after
+that), so with recent sampling every block of every layer holds exactly the
+single process's picks.  Gradients are averaged with one NCCL all-reduce of
+the flat gradient buffer, so losses and parameters agree to fp32 rounding,
+for one and for two recent layers.
 
 TGN-1 (GRU node memory, mails to the roots themselves) and APAN-1
 (transformer memory, mails to the sampled neighbours) the same way: every
@@ -39,16 +40,16 @@ def _port():
     return p
 
 
-def _setup(dev):
+def _setup(dev, layers=1):
     sys.path.insert(0, ROOT)
     from fast_b200.data import WorkloadConfig, make_graph
     cfg = WorkloadConfig("small", 400, 40000, ("zipf", 1.1), ("uniform",), 2e3, False, 0, 48, "normal", "TGAT",
-                         "recent", (8,), 64)
+                         "recent", (8,) * layers, 64)
     g = make_graph(cfg, seed=3)
     ef = torch.randn(cfg.edges, cfg.d_edge, generator=torch.Generator().manual_seed(1)).to(dev)
-    sp = dict(layer=1, neighbor=[8], strategy="recent", prop_time=False, history=1, duration=0)
+    sp = dict(layer=layers, neighbor=[8] * layers, strategy="recent", prop_time=False, history=1, duration=0)
     mp_ = dict(type="none", dim_out=0)
-    gp = dict(arch="transformer_attention", layer=1, att_head=2, dim_time=100, dim_out=100)
+    gp = dict(arch="transformer_attention", layer=layers, att_head=2, dim_time=100, dim_out=100)
     tp = dict(lr=1e-3, dropout=0.0, att_dropout=0.0)
     return cfg, g, ef, sp, mp_, gp, tp
 
@@ -64,7 +65,7 @@ def _run(tr, gB):
     return losses
 
 
-def _worker(rank, world, port, outdir):
+def _worker(rank, world, port, outdir, layers=1):
     import datetime
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -74,7 +75,7 @@ def _worker(rank, world, port, outdir):
                             timeout=datetime.timedelta(seconds=60))
     try:
         from fast_b200.train import GraphTrainer
-        cfg, g, ef, sp, mp_, gp, tp = _setup(dev)
+        cfg, g, ef, sp, mp_, gp, tp = _setup(dev, layers)
         gB = 128
         tr = GraphTrainer(g, None, ef, sp, mp_, dict(gp), tp, dev, batch=gB // world, rank=rank, world=world,
                           seed=5, sampler_seed=77, optimizer="sgd")
@@ -92,12 +93,13 @@ def _worker(rank, world, port, outdir):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_dp_two_ranks_equal_single_process(tmp_path):
+@pytest.mark.parametrize("layers", [1, 2])
+def test_dp_two_ranks_equal_single_process(tmp_path, layers):
     import torch.multiprocessing as mp
-    mp.spawn(_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _port(), str(tmp_path), layers), nprocs=2, join=True)
     from fast_b200.train import GraphTrainer
     dev = torch.device("cuda", 0)
-    cfg, g, ef, sp, mp_, gp, tp = _setup(dev)
+    cfg, g, ef, sp, mp_, gp, tp = _setup(dev, layers)
     tr = GraphTrainer(g, None, ef, sp, mp_, dict(gp), tp, dev, batch=128, seed=5, sampler_seed=77, optimizer="sgd")
     single = np.array(_run(tr, 128))
     params = torch.cat([p.detach().reshape(-1) for p in tr.model.parameters()]).cpu().numpy()

@@ -13,8 +13,15 @@ The second form covers gradients that are long sums with cancellation (the
 time-encoding frequencies sum E terms scaled by dt): there fp32 itself, the
 reference's included, is only as good as eps * sum|terms|, and the device
 result must be as accurate as the reference's fp32 result.
+
+The tensors allowed to pass by the norm form are listed, per case and path,
+in tests/golden/norm_form_allowed.json with the reason for each; a tensor
+that needs the norm form without being listed there fails the test.  With
+FB_RECORD_NORM_FORM=<file> the test also writes the tensors that needed it.
 """
 import copy
+import json
+import os
 
 import numpy as np
 import pytest
@@ -26,6 +33,26 @@ from oracle.sampler import OracleSampler
 
 pytestmark = pytest.mark.gpu
 RTOL, ATOL = 1e-5, 1e-6
+ALLOWED = os.path.join(os.path.dirname(__file__), "golden", "norm_form_allowed.json")
+
+
+def _allowed(case, path):
+    with open(ALLOWED) as f:
+        table = json.load(f)
+    return set(table["allowed"].get("%s/%s" % (case, path), []))
+
+
+def _record(case, path, names):
+    out = os.environ.get("FB_RECORD_NORM_FORM")
+    if not out:
+        return
+    table = {}
+    if os.path.exists(out):
+        with open(out) as f:
+            table = json.load(f)
+    table["%s/%s" % (case, path)] = sorted(names)
+    with open(out, "w") as f:
+        json.dump(table, f, indent=1, sort_keys=True)
 
 CASES = {
     # name: (layers, fanout, strategy-recent, d_node, d_edge)
@@ -83,6 +110,7 @@ def test_train_step_matches_oracle(cuda, case, path):
     rng = np.random.default_rng(0)
     B = 200
     failures = []
+    norm_form = set()
     for bt, b0 in enumerate(range(5000, 5000 + 3 * B, B)):
         src, dst, t = g["src"][b0:b0 + B], g["dst"][b0:b0 + B], g["t"][b0:b0 + B]
         roots = np.concatenate([src, dst, rng.integers(0, n_nodes, B).astype(np.int32)])
@@ -126,6 +154,10 @@ def test_train_step_matches_oracle(cuda, case, path):
             for p32, p64, pg in zip(m32.parameters(), m64.parameters(), m_gpu.parameters()):
                 p64.copy_(p32)
                 pg.copy_(p32)
+        norm_form |= {k for k, v in report.items() if v[2] == "norm"}
         print("batch", bt, "tensors passing only the norm form:",
               {k: v[:2] for k, v in report.items() if v[2] == "norm"})
+    _record(case, path, norm_form)
     assert not failures, failures
+    unlisted = norm_form - _allowed(case, path)
+    assert not unlisted, "passed only by the norm form, not listed in %s: %s" % (ALLOWED, sorted(unlisted))
