@@ -59,6 +59,9 @@ def parse():
                     help="config 5 on the CPU: each step trains on this fraction of the global batch")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-steps", type=int, default=5)
+    ap.add_argument("--breakdown-steps", type=int, default=10,
+                    help="steps of the per-phase device-time breakdown (sampling, forward+backward, all-reduce, "
+                         "Adam), each phase a graph of its own; 0 skips it")
     ap.add_argument("--eager", action="store_true", help="launch kernels step by step instead of a CUDA graph")
     ap.add_argument("--edges", type=int, default=None,
                     help="prefix subsample: the first N edges of the config's synthetic graph")
@@ -514,6 +517,28 @@ def run_fast(args):
     if world > 1:
         dist.all_reduce(t_samp)
 
+    # per-phase device time of the step (max over ranks), from graphs of each phase
+    breakdown = None
+    if args.breakdown_steps > 0 and not args.eager and hasattr(tr, "phase_times"):
+        tr.reset_epoch()
+
+        def load(j):
+            b = timed[j % len(timed)]
+            tr.load_device_roots(b * gB, (b + 1) * gB)
+
+        ph = tr.phase_times(min(args.breakdown_steps, len(timed)), load)
+        keys = sorted(ph)
+        t_ph = torch.tensor([ph[k] for k in keys], device=dev)
+        if world > 1:
+            dist.all_reduce(t_ph, op=dist.ReduceOp.MAX)
+        breakdown = {k: round(float(v), 4) for k, v in zip(keys, t_ph.tolist())}
+        breakdown["sum_of_phases"] = round(sum(v for k, v in breakdown.items() if k != "sample_local_only"), 4)
+        breakdown["step_in_one_graph"] = round(ms / args.steps, 4)
+        breakdown["note"] = ("ms per step, max over ranks; each phase replayed alone as its own graph (all-reduce "
+                             "launched eagerly), so the sum exceeds the one-graph step by the overlap and the "
+                             "launch gaps the single graph removes; sample_local_only = the sampler on this rank's "
+                             "roots without the global batch's pointer updates")
+
     if rank != 0:
         if world > 1:
             dist.barrier()
@@ -564,6 +589,7 @@ def run_fast(args):
         "workload_stats": {"sampled_edges_per_step": round(float(t_samp.item()), 1),
                            "note": "edges of every layer's block summed over the ranks, mean of the profiled "
                                    "steps (the same timed batches)"},
+        "step_breakdown_ms": breakdown,
         "gpu_launches": int(launches),
         "roofline": roof,
         "kernels": kernels,

@@ -126,12 +126,22 @@ _SIGS["fb_gemm_group_ws_bytes"] = (_SZ, [ctypes.POINTER(GemmProblem), _I])
 _SIGS["fb_gemm_group"] = (_I, [ctypes.POINTER(GemmProblem), _I, _P, _SZ, _P])
 
 
+class Bf16RowGather(ctypes.Structure):
+    """fb_bf16_row_gather (include/fast_b200.h): an operand's rows gathered
+    from up to three bf16 sources, in 64-column-aligned segments."""
+    _fields_ = [("nseg", ctypes.c_int), ("end", ctypes.c_int * 3), ("tab", ctypes.c_void_p * 3),
+                ("tab_rows", ctypes.c_int64 * 3), ("tab_ld", ctypes.c_int64 * 3), ("tab_cols", ctypes.c_int * 3),
+                ("idx", ctypes.c_void_p * 3)]
+
+
 class GemmBf16Problem(ctypes.Structure):
     """fb_gemm_bf16_problem (include/fast_b200.h): fb_gemm_problem's fields
-    (operand pointers to bf16) plus ka and the TN column segments."""
+    (operand pointers to bf16) plus ka, the TN column segments, the bf16
+    output flag and the optional gathered operand."""
     _fields_ = GemmProblem._fields_ + [("ka", ctypes.c_int), ("nseg", ctypes.c_int),
                                        ("seg_at", ctypes.c_int * 3), ("seg_len", ctypes.c_int * 3),
-                                       ("seg_to", ctypes.c_int * 3), ("c_bf16", ctypes.c_int)]
+                                       ("seg_to", ctypes.c_int * 3), ("c_bf16", ctypes.c_int),
+                                       ("gather", ctypes.POINTER(Bf16RowGather))]
 
 
 _SIGS["fb_gemm_bf16_group_ws_bytes"] = (_SZ, [ctypes.POINTER(GemmBf16Problem), _I])

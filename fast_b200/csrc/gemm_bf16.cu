@@ -15,6 +15,12 @@
 //       gradient comes from a ones column on the M side, and the reduce
 //       writes P transposed through the segment map, skipping the gaps.
 //   NT / NN may take A as [A | A2] concatenated along K (k1 % 8 == 0).
+//   Gathered operand (NT's A, or the segmented TN's X): the rows are not read
+//   from one matrix but gathered per 64-column segment from up to three bf16
+//   sources -- node-feature rows by node id, edge-feature rows by edge id
+//   (TMA tile::gather4, four rows per copy, spread over the producer warp's
+//   lanes), and a matrix read row by row (the time encoding) -- so the
+//   projection rows of a block are never written to memory.
 //
 // Operands are bf16 in global memory and reach the tensor cores untouched:
 // TMA moves 64-element (128-byte) rows with the 128-byte swizzle, K-major
@@ -26,7 +32,7 @@
 // drains the other.
 //
 // CTA = 12 warps:
-//   warp 0      TMA producer
+//   warp 0      TMA producer (lane 0; every lane issues row gathers)
 //   warp 1      TMEM allocator; the MMA issuer (one elected lane); for TN
 //               slices it clears the rows outside the split (rows past the
 //               device-side count hold stale data) and writes the ones column
@@ -39,6 +45,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <algorithm>
+#include <climits>
 #include <cstring>
 #include <vector>
 #include "runtime.cuh"
@@ -97,12 +104,15 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, bool mn) {
 }
 
 struct BfProb {
-  CUtensorMap ta, ta2, tb;   // A (TN: G), A2, B (TN: X)
+  CUtensorMap ta, ta2, tb;   // A (TN: G), A2, B (TN: X); gathered A: segments 0, 1 in ta, ta2
+  CUtensorMap tg;            // gathered A: segment 2
   // TN: P is [N rows][Kp cols] in the tiling's own orientation; ones = 1:
   // the ones column is B's column K, 2: it is A's column N - 1 (swapped form)
   int kind, a_mn, b_mn, k1, K, N, Kp, bn, rt, nt, ones, accumulate, db_accumulate, max_splits;
   int swap, ktot, nseg, seg_at[3], seg_len[3], seg_to[3];
   int c_bf16;                // NT / NN: C holds bf16 (round to nearest even), written, not accumulated
+  int gat, g_nseg, g_end[3], g_rows[3];   // A of the tiling gathered (see fb_bf16_row_gather)
+  const int32_t *g_idx[3];
   uint32_t idesc;
   int64_t M;
   const int32_t *M_dev;
@@ -118,7 +128,27 @@ struct BfArgs {
   int red_start[kMaxBf + 1];
   int32_t *err;
 };
-static_assert(sizeof(BfArgs) <= 4096, "kernel parameters of k_bf_group exceed 4 KB");
+// Large kernel parameters (CUDA 12.1+, up to 32,764 bytes on sm_70 and later).
+static_assert(sizeof(BfArgs) <= 32764, "kernel parameters of k_bf_group exceed 32 KB");
+
+// Segment of a gathered operand holding column c (g_nseg when past the last).
+__device__ __forceinline__ int gseg(const BfProb &q, int c) {
+  int s = 0;
+  while (s < q.g_nseg && c >= q.g_end[s]) ++s;
+  return s;
+}
+__device__ __forceinline__ int gstart(const BfProb &q, int s) { return s ? q.g_end[s - 1] : 0; }
+__device__ __forceinline__ const CUtensorMap *gmap(const BfProb &q, int s) {
+  return s == 0 ? &q.ta : (s == 1 ? &q.ta2 : &q.tg);
+}
+// Source row of operand row r in gathered segment s (rows past `valid`, and
+// indices outside the table, read row 0 / are clamped: those rows never
+// reach an output).
+__device__ __forceinline__ int grow(const BfProb &q, int s, int64_t r, int64_t valid) {
+  if (r >= valid) return 0;
+  const int v = __ldg(q.g_idx[s] + r);
+  return min(max(v, 0), q.g_rows[s] - 1);
+}
 
 struct Item {
   int p, z, nk, nk1, c0;
@@ -167,7 +197,11 @@ __device__ __forceinline__ void set_ones(uint8_t *box0, int col, int valid, int 
 }
 
 __device__ __forceinline__ void fix_tn_slice(uint8_t *a, uint8_t *b, int nbox, int valid, int onescol, int onescol_a,
-                                             int lane) {
+                                             int lane, int clear_a = 0) {
+  // A boxes that nothing loaded (past a gathered operand's last segment): zeros
+  for (int bx = 0; bx < 2; ++bx)
+    if (clear_a & (1 << bx))
+      for (int t = lane; t < kBox / 16; t += 32) reinterpret_cast<uint4 *>(a + bx * kBox)[t] = make_uint4(0u, 0u, 0u, 0u);
   if (valid < BK) {
     const int per_box = (BK - valid) * 8;    // 16-byte words to clear per box
     for (int t = lane; t < (2 + nbox) * per_box; t += 32) {
@@ -246,25 +280,73 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
   }
 
   if (warp == kWarpProducer) {
-    if (lane == 0) {
-      uint32_t g = 0;
-      bool stop = false;
-      for (int i = blockIdx.x; i < total && !stop; i += gridDim.x) {
-        const Item it = decode(a, s_start, s_m, s_per, i);
-        const BfProb &q = a.p[it.p];
-        const bool tn = q.kind == kTN, bmn = q.b_mn != 0;
-        const int bn = q.bn, k1 = q.k1, c0 = it.c0;
-        const uint32_t bytes = (uint32_t)(kAOp + bn * BK * 2);
-        const int r0 = (int)it.r0;
-        for (int j = 0; j < it.nk; ++j) {
-          const int s = g % kStages;
-          if (g >= kStages && !mbar_wait(empty + s, ((g / kStages) - 1) & 1, abort_flag, err)) {
-            stop = true;
-            break;
+    // lane 0 waits, arms the stage's barrier and issues the tiled copies; for
+    // a gathered operand every lane then issues row gathers (four rows each)
+    uint32_t g = 0;
+    bool stop = false;
+    for (int i = blockIdx.x; i < total && !stop; i += gridDim.x) {
+      const Item it = decode(a, s_start, s_m, s_per, i);
+      const BfProb &q = a.p[it.p];
+      const bool tn = q.kind == kTN, bmn = q.b_mn != 0, gat = q.gat != 0;
+      const int bn = q.bn, k1 = q.k1, c0 = it.c0;
+      const int r0 = (int)it.r0;
+      // NT gathered: this lane's rows r0 + 4 lane + u, their source rows per segment
+      int ix[3][4];
+      if (gat && !tn) {
+#pragma unroll
+        for (int sg = 0; sg < 3; ++sg)
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            ix[sg][u] = (sg < q.g_nseg && q.g_idx[sg]) ? grow(q, sg, (int64_t)r0 + 4 * lane + u, s_m[it.p]) : 0;
+      }
+      // TN gathered: lane = (box t = lane / 16, rows 4 (lane % 16) .. + 3 of the slice)
+      const int gt = lane >> 4, gq = lane & 15;
+      const int gsg = (gat && tn) ? gseg(q, r0 + 64 * gt) : 0;
+      const bool gidx = gat && tn && gsg < q.g_nseg && q.g_idx[gsg] != nullptr;
+      int nx[4] = {0, 0, 0, 0};
+      if (gidx) {
+        const int64_t m0 = it.s0 + 4 * gq;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) nx[u] = grow(q, gsg, m0 + u, it.s1);
+      }
+      uint32_t bytes = (uint32_t)(kAOp + bn * BK * 2);
+      if (gat && tn)
+        for (int t = 0; t < 2; ++t)
+          if (gseg(q, r0 + 64 * t) >= q.g_nseg) bytes -= kBox;    // past the last segment: cleared, not loaded
+      for (int j = 0; j < it.nk; ++j) {
+        const int s = g % kStages;
+        int ok = 1;
+        if (lane == 0) {
+          if (g >= kStages && !mbar_wait(empty + s, ((g / kStages) - 1) & 1, abort_flag, err)) ok = 0;
+          else mbar_expect_tx(full + s, bytes);
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) {
+          stop = true;
+          break;
+        }
+        const int kb = j < it.nk1 ? BK * j : k1 + BK * (j - it.nk1);
+        const int my = (int)it.s0 + BK * j;
+        if (gat && !tn) {
+          const int sg = gseg(q, kb);                         // kb < K: a segment
+          if (q.g_idx[sg]) {
+            tma_gather4(sA(s) + lane * 512, gmap(q, sg), full + s, kb - gstart(q, sg), ix[sg][0], ix[sg][1],
+                        ix[sg][2], ix[sg][3]);
+          } else if (lane == 0) {
+            tma_load_2d(sA(s), gmap(q, sg), full + s, kb - gstart(q, sg), r0);
           }
-          mbar_expect_tx(full + s, bytes);
-          const int kb = j < it.nk1 ? BK * j : k1 + BK * (j - it.nk1);
-          const int my = (int)it.s0 + BK * j;
+        } else if (gat) {
+          if (gidx) {
+            tma_gather4(sA(s) + gt * kBox + gq * 512, gmap(q, gsg), full + s, r0 + 64 * gt - gstart(q, gsg), nx[0],
+                        nx[1], nx[2], nx[3]);
+            if (j + 1 < it.nk) {
+              const int64_t m1 = it.s0 + BK * (j + 1) + 4 * gq;
+#pragma unroll
+              for (int u = 0; u < 4; ++u) nx[u] = grow(q, gsg, m1 + u, it.s1);
+            }
+          } else if (gq == 0 && gsg < q.g_nseg) {
+            tma_load_2d(sA(s) + gt * kBox, gmap(q, gsg), full + s, r0 + 64 * gt - gstart(q, gsg), my);
+          }
+        } else if (lane == 0) {
           if (tn) {
             tma_load_2d(sA(s), &q.ta, full + s, r0, my);
             tma_load_2d(sA(s) + kBox, &q.ta, full + s, r0 + 64, my);
@@ -273,19 +355,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
           } else {
             tma_load_2d(sA(s), &q.ta2, full + s, BK * (j - it.nk1), r0);
           }
+        }
+        if (lane == 0) {
           if (!bmn) {
             tma_load_2d(sB(s), &q.tb, full + s, kb, c0);
           } else {
             const int y = tn ? my : kb;
             for (int t = 0; t < bn / 64; ++t) tma_load_2d(sB(s) + t * kBox, &q.tb, full + s, c0 + 64 * t, y);
           }
-          ++g;
         }
+        __syncwarp();
+        ++g;
       }
-      if (*abort_flag) {
-        // let the copies already issued land before the CTA's memory goes away
-        for (uint32_t h = g > (uint32_t)kStages ? g - kStages : 0; h < g; ++h) mbar_drain(full + h % kStages, (h / kStages) & 1);
-      }
+    }
+    if (lane == 0 && *abort_flag) {
+      // let the copies already issued land before the CTA's memory goes away
+      for (uint32_t h = g > (uint32_t)kStages ? g - kStages : 0; h < g; ++h) mbar_drain(full + h % kStages, (h / kStages) & 1);
     }
   } else if (warp == kWarpMma) {
     uint32_t g = 0, tc = 0;
@@ -299,6 +384,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
       const int onescol = (tn && q.ones == 1 && q.K >= it.c0 && q.K < it.c0 + q.bn) ? q.K - it.c0 : -1;
       const int64_t ones_row = (int64_t)q.N - 1 - it.r0;     // swapped form: A's ones column in this tile
       const int onescol_a = (tn && q.ones == 2 && ones_row >= 0 && ones_row < BM) ? (int)ones_row : -1;
+      int clear_a = 0;                                        // gathered X: boxes past the last segment
+      if (tn && q.gat)
+        for (int t = 0; t < 2; ++t)
+          if (gseg(q, (int)it.r0 + 64 * t) >= q.g_nseg) clear_a |= 1 << t;
       const uint64_t adv_a = amn ? (2048 >> 4) : 2, adv_b = bmn ? (2048 >> 4) : 2;   // one K step of 16
       const int b = tc & 1;
       if (tc >= 2 && !mbar_wait(acce + b, ((tc >> 1) - 1) & 1, abort_flag, err)) break;
@@ -312,8 +401,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
         if (tn) {
           const int64_t left = it.s1 - (it.s0 + (int64_t)BK * j);
           const int valid = left <= 0 ? 0 : (left >= BK ? BK : (int)left);
-          if (valid < BK || onescol >= 0 || onescol_a >= 0) {
-            fix_tn_slice(sA(s), sB(s), nbox, valid, onescol, onescol_a, lane);
+          if (valid < BK || onescol >= 0 || onescol_a >= 0 || clear_a) {
+            fix_tn_slice(sA(s), sB(s), nbox, valid, onescol, onescol_a, lane, clear_a);
             fence_async_smem();
           }
           __syncwarp();
@@ -529,9 +618,40 @@ int64_t slices_per_item(const fb_gemm_bf16_problem &p) {
   return (k1 + BK - 1) / BK + (p.K - k1 + BK - 1) / BK;
 }
 
+// A gathered operand: 1..3 segments on 64-column boundaries, 16-byte aligned
+// sources with leading dimensions that are multiples of 8, K = the last end.
+bool gather_ok(const fb_bf16_row_gather &g, int K) {
+  if (g.nseg < 1 || g.nseg > 3) return false;
+  int prev = 0;
+  for (int s = 0; s < g.nseg; ++s) {
+    if (g.end[s] <= prev || g.end[s] % BK) return false;
+    if (!g.tab[s] || !al16(g.tab[s]) || g.tab_ld[s] % 8 || g.tab_cols[s] < 1 || g.tab_ld[s] < g.tab_cols[s] ||
+        g.tab_rows[s] < 1 || g.tab_rows[s] > INT32_MAX)
+      return false;
+    prev = g.end[s];
+  }
+  return prev == K;
+}
+
 bool problem_ok(const fb_gemm_bf16_problem &p) {
   if (p.kind < FB_GEMM_NT || p.kind > FB_GEMM_TN) return false;
   if (p.M < 0 || p.M > (int64_t)1 << 30 || p.N < 1 || p.K < 1) return false;
+  if (p.gather) {
+    if (!gather_ok(*p.gather, p.K)) return false;
+    if (p.kind == FB_GEMM_NT) {
+      if (p.A2 || !p.B || !al16(p.B) || p.ldb % 8 || p.ldb < p.K || !p.C || p.ldc < p.N) return false;
+      return !(p.c_bf16 && p.accumulate);
+    }
+    if (p.kind != FB_GEMM_TN || p.nseg < 1 || p.nseg > 3 || !p.A || !al16(p.A) || p.lda % 8 || p.lda < p.N ||
+        !p.C || p.c_bf16)
+      return false;
+    int end = 0;
+    for (int g = 0; g < p.nseg; ++g) {
+      if (p.seg_len[g] < 1 || p.seg_at[g] < end || p.seg_to[g] < 0 || p.seg_to[g] + p.seg_len[g] > p.ldc) return false;
+      end = p.seg_at[g] + p.seg_len[g];
+    }
+    return end <= p.K;
+  }
   if (!p.A || !al16(p.A) || p.lda % 8 || !p.B || !al16(p.B) || p.ldb % 8) return false;
   if (p.kind == FB_GEMM_TN) {
     if (p.c_bf16 || p.nseg < 0 || p.nseg > 3 || p.lda < p.N || p.ldb < p.K || !p.C) return false;
@@ -559,6 +679,23 @@ int64_t ws_floats(const fb_gemm_bf16_problem &p) {
   tn_dims(p, rows, cols);
   const int64_t ns = fb::tn_parts(p.M, kTnRowsMin, tn_splits_max(p));
   return (ns * (int64_t)rows * cols + 63) / 64 * 64;
+}
+
+// Tensor maps of a gathered operand: one-row boxes for the segments read by
+// row index (tile::gather4 copies), tiled boxes of `box_rows` rows for a
+// segment read row by row.
+int gather_maps(BfProb &q, const fb_bf16_row_gather &g, int box_rows) {
+  q.gat = 1;
+  q.g_nseg = g.nseg;
+  CUtensorMap *maps[3] = {&q.ta, &q.ta2, &q.tg};
+  for (int s = 0; s < g.nseg; ++s) {
+    q.g_end[s] = g.end[s];
+    q.g_rows[s] = (int)g.tab_rows[s];
+    q.g_idx[s] = g.idx[s];
+    const int rc = make_map(maps[s], g.tab[s], g.tab_rows[s], g.tab_cols[s], g.tab_ld[s], g.idx[s] ? 1 : box_rows);
+    if (rc) return rc;
+  }
+  return FB_OK;
 }
 
 int build_prob(BfProb &q, const fb_gemm_bf16_problem &p, float *ws) {
@@ -595,7 +732,11 @@ int build_prob(BfProb &q, const fb_gemm_bf16_problem &p, float *ws) {
       q.seg_len[g] = p.seg_len[g];
       q.seg_to[g] = p.seg_to[g];
     }
-    if ((rc = make_map(&q.ta, p.B, p.M, p.K, p.ldb, BK))) return rc;
+    if (p.gather) {
+      if ((rc = gather_maps(q, *p.gather, BK))) return rc;
+    } else if ((rc = make_map(&q.ta, p.B, p.M, p.K, p.ldb, BK))) {
+      return rc;
+    }
     if ((rc = make_map(&q.tb, p.A, p.M, p.N, p.lda, BK))) return rc;
   } else if (p.kind == FB_GEMM_TN) {
     q.a_mn = q.b_mn = 1;
@@ -620,8 +761,12 @@ int build_prob(BfProb &q, const fb_gemm_bf16_problem &p, float *ws) {
     q.bn = q.b_mn ? bn_mnmajor(p.N) : bn_kmajor(p.N);
     q.nt = (p.N + q.bn - 1) / q.bn;
     const int ka = two ? (p.ka > 0 ? p.ka : p.k1) : p.K;
-    if ((rc = make_map(&q.ta, p.A, p.M, ka, p.lda, BM))) return rc;
-    if (two && (rc = make_map(&q.ta2, p.A2, p.M, p.K - p.k1, p.lda2, BM))) return rc;
+    if (p.gather) {
+      if ((rc = gather_maps(q, *p.gather, BM))) return rc;
+    } else {
+      if ((rc = make_map(&q.ta, p.A, p.M, ka, p.lda, BM))) return rc;
+      if (two && (rc = make_map(&q.ta2, p.A2, p.M, p.K - p.k1, p.lda2, BM))) return rc;
+    }
     if (q.b_mn) rc = make_map(&q.tb, p.B, p.K, p.N, p.ldb, BK);
     else rc = make_map(&q.tb, p.B, p.N, p.K, p.ldb, q.bn);
     if (rc) return rc;

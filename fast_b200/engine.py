@@ -93,25 +93,42 @@ class FusedStep:
         one group, so K and V come from one GEMM."""
         m = self.model
         names = {id(p): n for n, p in m.named_parameters()}
-        groups = []                      # (layer or None, kind, shape, [parameter names])
+        # Gradient buckets in the order the backward finishes them: the edge
+        # predictor with the top layer, then each lower layer, then the
+        # memory updater; each bucket is one contiguous range of the buffer,
+        # so data-parallel training can all-reduce it while the layers below
+        # are still running their backward.
+        owners = ["edge_predictor."] + ["layers.l%dh0." % l for l in range(len(self.layers) - 1, -1, -1)]
+        groups = []                      # (layer or None, kind, shape, [parameter names], bucket)
         seated = set()
+
+        def bucket_of(name):
+            for i, o in enumerate(owners):
+                if name.startswith(o):
+                    return max(i - 1, 0)          # the predictor shares the top layer's bucket
+            return len(owners) - 1
+
         for lp in self.layers + ([self.mem_kv] if self.apan else []):
             L = lp.L
+            bk = bucket_of(names[id(L.w_k.weight)])
             groups.append((lp, "W", (2 * lp.D, L.w_k.weight.shape[1]), [names[id(L.w_k.weight)],
-                                                                         names[id(L.w_v.weight)]]))
-            groups.append((lp, "b", (2 * lp.D,), [names[id(L.w_k.bias)], names[id(L.w_v.bias)]]))
+                                                                         names[id(L.w_v.weight)]], bk))
+            groups.append((lp, "b", (2 * lp.D,), [names[id(L.w_k.bias)], names[id(L.w_v.bias)]], bk))
             seated.update(id(p) for p in (L.w_k.weight, L.w_v.weight, L.w_k.bias, L.w_v.bias))
         for n_, p in m.named_parameters():
             if id(p) not in seated:
-                groups.append((None, None, tuple(p.shape), [n_]))
+                groups.append((None, None, tuple(p.shape), [n_], bucket_of(n_)))
+        groups.sort(key=lambda g: g[4])           # stable: the order within a bucket is kept
         numel = lambda shape: int(torch.Size(shape).numel())
-        total = sum((numel(shape) + _ALIGN - 1) // _ALIGN * _ALIGN for _, _, shape, _ in groups)
+        total = sum((numel(shape) + _ALIGN - 1) // _ALIGN * _ALIGN for _, _, shape, _, _ in groups)
         dev = next(m.parameters()).device
         flat_p = torch.zeros(total, device=dev, dtype=torch.float32)
         flat_g = torch.zeros(total, device=dev, dtype=torch.float32)
         params = dict(m.named_parameters())
         off = 0
-        for lp, kind, shape, members in groups:
+        starts = {}
+        for lp, kind, shape, members, bk in groups:
+            starts.setdefault(bk, off)
             n = numel(shape)
             pv = flat_p[off:off + n].view(shape)
             gv = flat_g[off:off + n].view(shape)
@@ -133,6 +150,11 @@ class FusedStep:
                     lp.b_kv, lp.gb_kv = pv, gv
             off += (n + _ALIGN - 1) // _ALIGN * _ALIGN
         self.flat_params = flat_p
+        bks = sorted(starts)
+        # (lo, hi) of every bucket, in the order the backward completes them
+        self.grad_buckets = [(starts[b], starts[bks[i + 1]] if i + 1 < len(bks) else total)
+                             for i, b in enumerate(bks)]
+        self._bucket_ids = bks
         return flat_g
 
     def parameters(self):
@@ -537,8 +559,16 @@ class FusedStep:
         return dh
 
     # -- whole step -----------------------------------------------------------
+    def _buckets_done(self, hook, upto):
+        """Calls hook(i) for every gradient bucket i < upto not yet reported."""
+        if hook is None:
+            return
+        while self._reported < min(upto, len(self.grad_buckets)):
+            hook(self._reported)
+            self._reported += 1
+
     def step(self, blocks, node_table, edge_table, loss_out, zero_grad=True, scores=None, mailbox=None,
-             roots=None, root_ts=None):
+             roots=None, root_ts=None, grad_hook=None):
         """blocks in sampler order (hop 1 first), Device- or StaticBlocks.
         Writes the loss into loss_out (a 0-d device tensor) and the gradients
         into the parameters' .grad (zeroed first unless zero_grad=False);
@@ -546,7 +576,13 @@ class FusedStep:
         edge scores.  Memory models read their inputs from `mailbox` and
         leave the updated memory of the first layer's source rows in
         `last_memory`; APAN models take the batch's roots and times (its
-        updater runs on the roots, not on the sampled block)."""
+        updater runs on the roots, not on the sampled block).
+        grad_hook(i), when given, is called (on the host, in stream order) as
+        soon as the launches that write gradient bucket i
+        (self.grad_buckets[i], a range of self.flat) are enqueued: the
+        predictor's and the top layer's after that layer's backward, each
+        lower layer's after its own, every bucket by the end of the call."""
+        self._reported = 0
         m = self.model
         training = m.training
         mfgs = list(reversed(blocks))
@@ -560,7 +596,9 @@ class FusedStep:
         if self.apan:
             if mailbox is None or roots is None:
                 raise ValueError("an APAN step needs its MailBox and the batch's roots")
-            return self._apan_step(roots, root_ts, mailbox, loss_out, scores, training, m._drop_step)
+            out = self._apan_step(roots, root_ts, mailbox, loss_out, scores, training, m._drop_step)
+            self._buckets_done(grad_hook, len(self.grad_buckets))
+            return out
         saved, h = [], None
         mem_st = None
         if self.mem is not None:
@@ -578,13 +616,17 @@ class FusedStep:
                         m._drop_step, training)
             saved.append(st)
         dh = self._predictor(h, loss_out, scores)
-        for l in range(len(mfgs) - 1, -1, -1):
+        n_layers = len(mfgs)
+        for l in range(n_layers - 1, -1, -1):
             rows = mfgs[l - 1].n_dst if l > 0 else (mfgs[0].n_src if mem_st is not None else 0)
             dh = bwd(l, saved[l], dh, rows)
+            # bucket b holds layer n_layers - 1 - b (bucket 0 also the predictor)
+            self._buckets_done(grad_hook, n_layers - l)
         if mem_st is not None:
             if dh is None:                   # an empty block: no gradient reaches the memory updater
                 dh = torch.zeros(mem_st["n"], self.mem.dim_hid, device=dev)
             self._memory_bwd(mem_st, dh)
+        self._buckets_done(grad_hook, len(self.grad_buckets))
         return loss_out
 
 

@@ -51,6 +51,19 @@ def average_gradients(params, world, flat=None):
     return flat
 
 
+def average_flat(flat, world, async_op=False):
+    """Mean of a flat gradient buffer over the process group, in place: one
+    all-reduce with NCCL's average (no separate division launch), or sum and
+    divide where the backend has no average (gloo)."""
+    if dist.get_backend() == "nccl":
+        return dist.all_reduce(flat, op=dist.ReduceOp.AVG, async_op=async_op)
+    work = dist.all_reduce(flat, async_op=async_op)
+    if async_op:
+        work.wait()
+    flat.div_(world)
+    return None
+
+
 def gather_global_order(local, world, out=None, perm=None):
     """All ranks' rows of a per-rank list [src_r | dst_r | neg_r] (3 equal
     sections of this rank's slice), returned in the global batch's order
@@ -260,8 +273,7 @@ class Trainer:
 
     def _allreduce_grads(self):
         if self.engine is not None:          # the gradients already live in one flat buffer
-            dist.all_reduce(self.engine.flat)
-            self.engine.flat.div_(self.world)
+            average_flat(self.engine.flat, self.world)
         else:
             self._flat = average_gradients(list(self.model.parameters()), self.world, self._flat)
 
@@ -434,7 +446,7 @@ class GraphTrainer(Trainer):
         self.g_main = self.g_opt = None
 
     # the body of one step on the static input buffers
-    def _fwd_bwd(self):
+    def _sample(self):
         sr, st = self._sample_roots(self.roots_buf, self.ts_buf)
         if self.world > 1:
             gr, gt = self._sample_roots(self.groots_buf, self.gts_buf)
@@ -442,11 +454,23 @@ class GraphTrainer(Trainer):
         else:
             self.sampler.sample_device(sr, st)
         views = self.sampler.block_views()
-        blocks = [StaticBlock(views[0], n_roots=sr.shape[0])] + [StaticBlock(v) for v in views[1:]]
-        self._blocks = blocks
+        self._blocks = [StaticBlock(views[0], n_roots=sr.shape[0])] + [StaticBlock(v) for v in views[1:]]
+
+    def _compute(self, overlap=False):
+        """Forward + backward on the sampled blocks.  overlap (several ranks,
+        FusedStep): each gradient bucket is all-reduced (NCCL average,
+        asynchronously) as soon as the backward has written it, while the
+        layers below run their backward; _apply waits for them."""
+        blocks = self._blocks
         if self.engine is not None:
+            hook = None
+            self._works = []
+            if overlap:
+                def hook(i):
+                    lo, hi = self.engine.grad_buckets[i]
+                    self._works.append(average_flat(self._flat[lo:hi], self.world, async_op=True))
             self.engine.step(blocks, self.node_feats, self.edge_feats, self.loss_buf, mailbox=self.mailbox,
-                             roots=self.roots_buf, root_ts=self.ts_buf)
+                             roots=self.roots_buf, root_ts=self.ts_buf, grad_hook=hook)
             return
         self._flat.zero_()
         pred_pos, pred_neg = self.model(blocks, self.node_feats, self.edge_feats)
@@ -454,9 +478,23 @@ class GraphTrainer(Trainer):
         loss.backward()
         self.loss_buf.copy_(loss.detach())
 
+    def _fwd_bwd(self):
+        self._sample()
+        self._compute()
+
+    def _reduce(self):
+        """The data-parallel gradient average (after an overlapped backward:
+        waits for its bucket all-reduces)."""
+        works = getattr(self, "_works", None)
+        if works:
+            for w in works:
+                if w is not None:
+                    w.wait()
+            self._works = []
+        else:
+            average_flat(self._flat, self.world)
+
     def _apply(self):
-        if self.world > 1:
-            self._flat.div_(self.world)
         self.opt.step()
         if self.mailbox is not None and self.world == 1:
             self._update_memory(self._blocks, self.roots_buf, self.ts_buf)
@@ -467,17 +505,29 @@ class GraphTrainer(Trainer):
         if self.mailbox is not None and self.world > 1:
             self._update_memory(self._blocks, self.roots_buf, self.ts_buf)
 
+    def _overlap(self):
+        """Bucketed all-reduce inside the backward: several ranks on NCCL with
+        the fused engine (FB_NCCL_IN_GRAPH=0 keeps the all-reduce outside the
+        captured graph, between two graphs)."""
+        import os
+        return (self.world > 1 and self.engine is not None and dist.get_backend() == "nccl"
+                and os.environ.get("FB_NCCL_IN_GRAPH", "1") != "0")
+
     def _eager_step(self):
-        self._fwd_bwd()
+        self._sample()
+        self._compute(overlap=self._overlap())
         if self.world > 1:
-            dist.all_reduce(self._flat)
+            self._reduce()
         self._apply()
         self._memory_ranks()
 
     def capture(self, warmup=3):
-        """Warm up on a side stream (allocator, lazy kernel loads, Adam state),
-        then capture.  The warm-up steps are real training steps on whatever
-        is in the input buffers."""
+        """Warm up on a side stream (allocator, lazy kernel loads, Adam state,
+        NCCL communicators), then capture.  The warm-up steps are real
+        training steps on whatever is in the input buffers.  The whole step
+        -- sampling, forward, backward with its gradient all-reduces (NCCL
+        captured in the graph), Adam -- is one graph; with FB_NCCL_IN_GRAPH=0
+        several ranks use two graphs around one all-reduce."""
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
@@ -486,11 +536,15 @@ class GraphTrainer(Trainer):
         torch.cuda.current_stream(self.device).wait_stream(s)
         torch.cuda.synchronize(self.device)
         self.g_main = torch.cuda.CUDAGraph()
+        one_graph = self.world == 1 or self._overlap()
         with torch.cuda.graph(self.g_main):
-            self._fwd_bwd()
-            if self.world == 1:
+            self._sample()
+            self._compute(overlap=self._overlap())
+            if one_graph:
+                if self.world > 1:
+                    self._reduce()
                 self._apply()
-        if self.world > 1:
+        if not one_graph:
             self.g_opt = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.g_opt, pool=self.g_main.pool()):
                 self._apply()
@@ -498,10 +552,55 @@ class GraphTrainer(Trainer):
 
     def _replay(self):
         self.g_main.replay()
-        if self.world > 1:
-            dist.all_reduce(self._flat)
+        if self.g_opt is not None:
+            average_flat(self._flat, self.world)
             self.g_opt.replay()
+        if self.world > 1:
             self._memory_ranks()
+
+    def phase_times(self, steps, load):
+        """Device time of each phase of the step, for the data-parallel
+        breakdown: sampling (this rank's blocks plus, with several ranks, the
+        global batch's pointer updates), forward + backward, the gradient
+        all-reduce, Adam -- each captured in a graph of its own (the
+        all-reduce launched eagerly) and replayed `steps` times between CUDA
+        events, load(j) filling the input buffers before step j.  Also the
+        sampler with this rank's roots only (sample_device, the one-process
+        call).  Returns milliseconds per step; these steps train."""
+        dev = self.device
+        graphs = {}
+        for name, fn in (("sample", self._sample), ("forward_backward", lambda: self._compute(overlap=False)),
+                         ("adam", self.opt.step)):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            graphs[name] = g
+        if self.world > 1:
+            graphs["sample_local_only"] = torch.cuda.CUDAGraph()
+            sr, st = self._sample_roots(self.roots_buf, self.ts_buf)
+            with torch.cuda.graph(graphs["sample_local_only"]):
+                self.sampler.sample_device(sr, st)
+        torch.cuda.synchronize(dev)
+        acc = {k: 0.0 for k in list(graphs) + (["allreduce"] if self.world > 1 else [])}
+        for j in range(steps):
+            load(j)
+            order = ["sample", "forward_backward"] + (["allreduce"] if self.world > 1 else []) + ["adam"]
+            if self.world > 1:
+                order.append("sample_local_only")
+            for name in order:
+                if self.world > 1:
+                    dist.barrier()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                if name == "allreduce":
+                    average_flat(self._flat, self.world)
+                else:
+                    graphs[name].replay()
+                e1.record()
+                torch.cuda.synchronize(dev)
+                acc[name] += e0.elapsed_time(e1)
+        graphs.clear()
+        return {k: v / steps for k, v in acc.items()}
 
     def load_device_roots(self, b0, b1):
         """Fills the input buffers with this rank's slice of the global batch

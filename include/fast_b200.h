@@ -348,6 +348,26 @@ int fb_gemm_group(const fb_gemm_problem *probs, int n, void *ws, size_t ws_bytes
  * aligned with a leading dimension (elements) that is a multiple of 8, k1 a
  * multiple of 8, K >= 1 (TN: db via a virtual ones column at k = K).  ws:
  * fb_gemm_bf16_group_ws_bytes(probs, n) bytes. */
+/* Rows of a bf16 GEMM operand gathered from up to three sources instead of
+ * read from one matrix: the gathers of prepare_input (utils.py:126-196,
+ * node_feats[nodes], edge_feats[eid]) and the time encoding (layers.py:17-29)
+ * fused into the projection's operand load (TMA row gathers), so the
+ * projection rows are never written to memory.  The operand's columns come in
+ * nseg (1..3) segments, each starting and ending on a multiple of 64 columns:
+ * segment s covers [s ? end[s-1] : 0, end[s]), and its row r is row
+ * idx[s][r] (idx[s] NULL: row r) of the bf16 matrix tab[s] (tab_rows[s] rows,
+ * tab_cols[s] data columns, leading dimension tab_ld[s], a multiple of 8; tab
+ * 16-byte aligned).  Columns past tab_cols[s] read as zeros; row indices are
+ * clamped into [0, tab_rows[s]). */
+typedef struct fb_bf16_row_gather {
+  int nseg;
+  int end[3];
+  const uint16_t *tab[3];
+  int64_t tab_rows[3], tab_ld[3];
+  int tab_cols[3];
+  const int32_t *idx[3];
+} fb_bf16_row_gather;
+
 typedef struct fb_gemm_bf16_problem {
   int kind;
   const uint16_t *A; int64_t lda;
@@ -372,6 +392,9 @@ typedef struct fb_gemm_bf16_problem {
   int c_bf16;    /* NT / NN: C is bf16 (bit patterns, round to nearest even; no
                     accumulate) -- the K|V projection feeding the attention's
                     bf16 K|V path */
+  const fb_bf16_row_gather *gather;   /* NT (no A2): A's rows, A unused; TN with
+                    nseg > 0: X's rows, B unused; K = the last segment's end.
+                    NULL: the operand is the matrix */
 } fb_gemm_bf16_problem;
 size_t fb_gemm_bf16_group_ws_bytes(const fb_gemm_bf16_problem *probs, int n);
 int fb_gemm_bf16_group(const fb_gemm_bf16_problem *probs, int n, void *ws, size_t ws_bytes, cudaStream_t stream);

@@ -1,7 +1,8 @@
 """GPU: the device-built synthetic workload of config 5.
 
 * make_graph_device keeps the reference preprocessing contract that
-  make_graph keeps (fast_util/preprocess/gen_graph.py): chronological edge
+  make_graph keeps (fast_util/preprocess/gen_graph.py), with every array a
+  device tensor: chronological edge
   ids, non-decreasing float32 timestamps, a CSR keyed by the source whose
   every adjacency list is in chronological order (a stable sort on the
   source), indices / ts / eid consistent with the edge list.
@@ -21,7 +22,8 @@ def test_device_graph_keeps_the_csr_contract(cuda):
     cfg = dataclasses.replace(CONFIGS[5], edges=200_000)
     g = make_graph_device(cfg, cuda, seed=3)
     E, N = cfg.edges, cfg.nodes
-    src, dst, ts = g.src, g.dst, g.ts
+    assert g.src.is_cuda and g.dst.is_cuda and g.ts.is_cuda       # the edge list stays on the device
+    src, dst, ts = g.src.cpu().numpy(), g.dst.cpu().numpy(), g.ts.cpu().numpy()
     assert src.shape == (E,) and dst.shape == (E,) and ts.dtype == np.float32
     assert bool(np.all(np.diff(ts) >= 0))
     indptr = g.indptr.cpu().numpy().astype(np.int64)
