@@ -809,6 +809,26 @@ def run_bf16_suite(args):
     timed("k_bf_group (K|V weight + bias gradient, TN over the row's 3 segments)", E * (2 * K + 2 * 2 * D),
           2 * E * 2 * D * (dn + de + dt_ + 1),
           lambda: ops.gemm_bf16_group(tn), "M=%d, N=%d, K=%d+%d+%d+1" % (E, 2 * D, dn, de, dt_))
+    # layer 0 of the step: the projection rows gathered inside the GEMM from the tables (node rows by node
+    # id, edge rows by edge id) plus the time-encoding block, which alone is written
+    T, _ = ops.gather_time_encode_bf16(E, dt=dts, w=w, b=b, device=dev)
+    timed("k_gather_time_encode_bf16 (time encoding only)", E * (2 * 104 + 4), 0,
+          lambda: ops.gather_time_encode_bf16(E, dt=dts, w=w, b=b, out=T),
+          "E=%d rows of cos(%d) bf16" % (E, dt_))
+    gat = ops.RowGather([(ntab, dn, nid, 448), (etab, de, eid, 192), (T, dt_, None, 128)])
+    Wg = torch.zeros(2 * D, gat.K, device=dev, dtype=torch.bfloat16)
+    for at, src_at, d in ((0, h_at, dn), (448, f_at, de), (640, t_at, dt_)):
+        Wg[:, at:at + d] = Wb[:, src_at:src_at + d]
+    timed("k_bf_group (K|V projection, NT, rows gathered from the tables)",
+          gat.read_bytes(E) + 2 * 2 * D * gat.K + 2 * E * 2 * D, 2 * E * 2 * D * gat.K,
+          lambda: ops.gemm_bf16_group([dict(kind=ops.NT, gather=gat, M=E, B=Wg, bias=bkv, out=KV)]),
+          "M=%d, N=%d, K=%d (448 + 192 + 128)" % (E, 2 * D, gat.K))
+    tng = [dict(kind=ops.TN, A=dkv, gather=gat, out=gW, accumulate=True, db=gb,
+                segs=[(0, dn, 0), (448, de, dn), (640, dt_, dn + de)])]
+    timed("k_bf_group (K|V weight + bias gradient, TN, rows gathered from the tables)",
+          2 * E * 2 * D + gat.read_bytes(E) + 4 * 2 * D * (dn + de + dt_),
+          2 * E * 2 * D * (dn + de + dt_ + 1), lambda: ops.gemm_bf16_group(tng),
+          "M=%d, N=%d, K=%d+%d+%d+1" % (E, 2 * D, dn, de, dt_))
     dAt = torch.empty(E, dt_, device=dev, dtype=torch.bfloat16)       # bf16, as in the step
     timed("k_bf_group (time-encoding input gradient, NN, bf16 output)", E * (2 * 2 * D + 2 * dt_),
           2 * E * dt_ * 2 * D,

@@ -32,11 +32,20 @@ the backward runs layer 0's input gradient through the gates into the GRU's
 weights and the memory time encoder.  `last_memory` keeps the updated memory
 for the mailbox writes after the optimizer step (memorys.py:84-142).
 """
+import os
+
 import torch
 
 from . import ops
 
 _ALIGN = 64            # flat-buffer segments start on 256-byte boundaries
+# FB_FUSED_GATHER=0 materialises layer 0's bf16 projection rows as well (the
+# gathered-operand GEMM is the default)
+FUSED_GATHER_OFF = os.environ.get("FB_FUSED_GATHER", "1") == "0"
+
+
+def pad64(n):
+    return (n + 63) // 64 * 64 if n > 0 else 0
 
 
 class _LayerParams:
@@ -184,6 +193,15 @@ class FusedStep:
                 lp.W_q_bf = torch.zeros(D, ops.pad8(kq), **bf)
                 for at, lo, d in lp.q_segs:
                     self.cast_jobs.append((L.w_q.weight[:, lo:lo + d], lp.W_q_bf[:, at:at + d]))
+            # layer 0 reads the feature tables: its projection rows are gathered
+            # inside the GEMM (fused_layer0), in 64-column segments [h | f | t]
+            lp.g_w = (pad64(dn), pad64(de), pad64(dt))
+            if lp is self.layers[0]:
+                g_at = (0, lp.g_w[0], lp.g_w[0] + lp.g_w[1])
+                lp.g_segs = [(at, lo, d) for at, lo, d in zip(g_at, (0, dn, dn + de), (dn, de, dt)) if d > 0]
+                lp.W_kv_g = torch.zeros(2 * D, sum(lp.g_w), **bf)
+                for at, lo, d in lp.g_segs:
+                    self.cast_jobs.append((lp.W_kv[:, lo:lo + d], lp.W_kv_g[:, at:at + d]))
             lp.ka = ops.pad8(D)
             lp.W_out_bf = torch.zeros(D, ops.pad8(lp.ka + dn), **bf)
             self.cast_jobs.append((L.w_out.weight[:, :D], lp.W_out_bf[:, :D]))
@@ -212,11 +230,19 @@ class FusedStep:
             hsrc, hdst = dict(h=node_table, h_idx=blk.src_nodes), dict(h=node_table, h_idx=blk.dst_nodes)
         else:
             hsrc = hdst = {}
-        X, kx = ops.gather_time_encode_bf16(E, f=edge_table if de > 0 else None, f_idx=blk.eid, dt=blk.dt_edges,
-                                            w=wv, b=bt, device=dev, n_rows_dev=E_dev, dn=dn, de=de, **hsrc)
         # K|V stored as bf16 rows: the projection's bf16 output is the attention's input
         KV = torch.empty(E, 2 * D, device=dev, dtype=torch.bfloat16)
-        probs = [dict(kind=ops.NT, A=X[:, :kx], B=lp.W_kv_bf[:, :kx], bias=lp.b_kv, out=KV, M_dev=E_dev)]
+        gat = self._layer0_gather(l, blk, h, node_table, edge_table, wv, bt, dev)
+        if gat is not None:
+            # the projection rows [h | f | cos] are gathered inside the GEMM:
+            # only the time encoding is written, the tables are read in place
+            X = None
+            probs = [dict(kind=ops.NT, gather=gat, M=E, B=lp.W_kv_g, bias=lp.b_kv, out=KV, M_dev=E_dev)]
+        else:
+            X, kx = ops.gather_time_encode_bf16(E, f=edge_table if de > 0 else None, f_idx=blk.eid,
+                                                dt=blk.dt_edges, w=wv, b=bt, device=dev, n_rows_dev=E_dev, dn=dn,
+                                                de=de, **hsrc)
+            probs = [dict(kind=ops.NT, A=X[:, :kx], B=lp.W_kv_bf[:, :kx], bias=lp.b_kv, out=KV, M_dev=E_dev)]
         if dn > 0:
             Qin, kq = ops.gather_time_encode_bf16(nd, w=wv, b=bt, device=dev, n_rows_dev=nd_dev, dn=dn, **hdst)
             Q = torch.empty(nd, D, device=dev)
@@ -244,9 +270,33 @@ class FusedStep:
         y, out = ops.layer_tail_fwd(Z, L.layer_norm.weight, L.layer_norm.bias, eps=L.layer_norm.eps, drop_p=p_drop,
                                     seed=0x7A11 + l, offset_dev=offset_dev, y=Z, n_dev=nd_dev,
                                     gate_dev=E_dev if blk.static else None)
-        st = dict(blk=blk, A=X, KV=KV, Qin=Qin, Q=Q, agg=agg, agg_bf=agg_bf, att=att, y=y, p_att=p_att,
+        st = dict(blk=blk, A=X, gather=gat, KV=KV, Qin=Qin, Q=Q, agg=agg, agg_bf=agg_bf, att=att, y=y, p_att=p_att,
                   p_drop=p_drop, offset_dev=offset_dev)
         return st, out
+
+    def _layer0_gather(self, l, blk, h, node_table, edge_table, wv, bt, dev):
+        """The gathered projection rows of layer 0 (ops.RowGather), when the
+        layer reads bf16 feature tables: node rows by the edges' source node,
+        edge rows by edge id, and the time encoding cos(w dt + b), the one
+        block written (as [E, pad8(dtime)] bf16).  None: the layer takes the
+        previous layer's output, so its rows are materialised."""
+        lp = self.layers[l]
+        if l != 0 or h is not None or getattr(lp, "W_kv_g", None) is None or FUSED_GATHER_OFF:
+            return None
+        dn, de, dtime = lp.dn, lp.de, lp.dtime
+        if (dn > 0 and (node_table is None or node_table.dtype != torch.bfloat16)) or \
+                (de > 0 and (edge_table is None or edge_table.dtype != torch.bfloat16)):
+            return None
+        segs = []
+        if dn > 0:
+            segs.append((node_table, dn, blk.src_nodes, lp.g_w[0]))
+        if de > 0:
+            segs.append((edge_table, de, blk.eid, lp.g_w[1]))
+        if dtime > 0:
+            T, _ = ops.gather_time_encode_bf16(blk.n_edges, dt=blk.dt_edges, w=wv, b=bt, device=dev,
+                                               n_rows_dev=blk.n_edges_dev)
+            segs.append((T, dtime, None, lp.g_w[2]))
+        return ops.RowGather(segs)
 
     def _layer_bwd_bf16(self, l, st, dout, dh_rows):
         """_layer_bwd with bf16 operands for every projection-gradient product
@@ -282,20 +332,26 @@ class FusedStep:
         ops.gemm_bf16_group(probs, name="gemm_group:bwd_dz")
         dQ, dKV = ops.attn_bwd_kvbf16(st["Q"], st["KV"], blk.rptr, st["att"], dagg, L.num_head, L.negative_slope,
                                       st["p_att"], 0x5EED + l, 0, n_dst_dev=nd_dev, offset_dev=st["offset_dev"])
-        X = st["A"]
+        X, gat = st["A"], st["gather"]
         v = torch.empty(D, device=dev)            # sum over rows of dQ
         # the K|V weight and bias gradient over the whole projection row: one
-        # TN problem, X's segments mapped to the weight's columns
-        probs = [dict(kind=ops.TN, A=dKV, B=X[:, :lp.kx], out=lp.gW_kv, accumulate=True, M_dev=E_dev,
-                      db=lp.gb_kv, segs=[(at, d, lo) for at, lo, d in lp.kv_segs])]
+        # TN problem, X's segments mapped to the weight's columns (gathered
+        # rows: the same segments read from the tables again)
+        if gat is not None:
+            probs = [dict(kind=ops.TN, A=dKV, gather=gat, out=lp.gW_kv, accumulate=True, M_dev=E_dev,
+                          db=lp.gb_kv, segs=[(at, d, lo) for at, lo, d in lp.g_segs])]
+            W_t, t_at = lp.W_kv_g, lp.g_segs[-1][0]
+        else:
+            probs = [dict(kind=ops.TN, A=dKV, B=X[:, :lp.kx], out=lp.gW_kv, accumulate=True, M_dev=E_dev,
+                          db=lp.gb_kv, segs=[(at, d, lo) for at, lo, d in lp.kv_segs])]
+            W_t, t_at = lp.W_kv_bf, lp.kv_segs[-1][0]
         if dh is not None:
             probs.append(dict(kind=ops.NN, A=dKV, B=lp.W_kv_bf[:, :dn], out=dh[nd:nd + E], M_dev=E_dev))
         dA_t = None
         if dtime > 0:
-            t_at = lp.kv_segs[-1][0]
             # bf16, like the gradient of an autocast bf16 product; summed in fp32
             dA_t = torch.empty(E, dtime, device=dev, dtype=torch.bfloat16)
-            probs.append(dict(kind=ops.NN, A=dKV, B=lp.W_kv_bf[:, t_at:t_at + dtime], out=dA_t, M_dev=E_dev))
+            probs.append(dict(kind=ops.NN, A=dKV, B=W_t[:, t_at:t_at + dtime], out=dA_t, M_dev=E_dev))
         if dn > 0:
             dQ_bf = torch.empty(nd, lp.ka, device=dev, dtype=torch.bfloat16)
             ops.cast_bf16([(dQ, dQ_bf[:, :D], nd_dev)])

@@ -211,6 +211,47 @@ def _bf16_rows(t, name):
         raise ValueError("%s must be a CUDA bf16 matrix with unit column stride" % name)
 
 
+class RowGather:
+    """Rows of a bf16 GEMM operand gathered from up to three sources
+    (fb_bf16_row_gather): segments [(table, cols, idx, width)] in column
+    order -- a bf16 table [rows, ld] (ld a multiple of 8) whose first `cols`
+    columns are data, the int32 row index of every operand row (None: row r
+    of the table), and the segment's width in the operand, a multiple of 64.
+    Columns past `cols` read as zeros."""
+
+    def __init__(self, segments):
+        if not 1 <= len(segments) <= 3:
+            raise ValueError("RowGather: 1 to 3 segments")
+        self.segments = list(segments)
+        self.starts, end = [], 0
+        for tab, cols, idx, width in self.segments:
+            _bf16_rows(tab, "RowGather table")
+            if width % 64 or width < 1 or cols > tab.shape[1]:
+                raise ValueError("RowGather: segment widths are multiples of 64 columns")
+            if idx is not None and (idx.dtype != torch.int32 or not idx.is_contiguous()):
+                raise ValueError("RowGather: row indices must be contiguous int32")
+            self.starts.append(end)
+            end += width
+        self.K = end
+
+    def struct(self):
+        from .capi import Bf16RowGather
+        g = Bf16RowGather()
+        g.nseg = len(self.segments)
+        for s, (tab, cols, idx, width) in enumerate(self.segments):
+            g.end[s] = self.starts[s] + width
+            g.tab[s] = ptr(tab)
+            g.tab_rows[s] = tab.shape[0]
+            g.tab_ld[s] = tab.stride(0)
+            g.tab_cols[s] = cols
+            g.idx[s] = ptr(idx)
+        return g
+
+    def read_bytes(self, M):
+        """Algorithmic bytes of M gathered rows: each source row's data and its index."""
+        return sum(M * (2 * cols + (4 if idx is not None else 0)) for _, cols, idx, _ in self.segments)
+
+
 def gemm_bf16_group(problems, name="gemm_bf16_group"):
     """gemm_group with bf16 operands (torch.bfloat16 matrices; C, bias, db
     fp32) on the tcgen05 kind::f16 kernel: products of bf16 values
@@ -219,12 +260,14 @@ def gemm_bf16_group(problems, name="gemm_bf16_group"):
     block starts.  A TN problem may give segs = [(at, len, to), ...]: B's
     columns [at, at + len) land in out's columns from `to`, the rest of B's
     columns are skipped (a weight gradient over a bf16 projection row)."""
-    from .capi import GemmBf16Problem
+    from .capi import Bf16RowGather, GemmBf16Problem
     arr = (GemmBf16Problem * len(problems))()
+    gathers = (Bf16RowGather * len(problems))()
     nbytes, flops = 0, 0
     keep = []
     for i, p in enumerate(problems):
-        A, B, out, A2 = p["A"], p["B"], p.get("out"), p.get("A2")
+        A, B, out, A2 = p.get("A"), p.get("B"), p.get("out"), p.get("A2")
+        gat = p.get("gather")
         kind = p["kind"]
         for t in (A, B, A2):
             if t is not None:
@@ -234,8 +277,20 @@ def gemm_bf16_group(problems, name="gemm_bf16_group"):
             _bf16_rows(out, "gemm_bf16_group output")
         else:
             _f32_rows(out, "gemm_bf16_group output")
-        M = A.shape[0]
-        if kind == TN:
+        if gat is not None:
+            # NT: A's rows gathered (A absent, M from p["M"]); TN: X's rows gathered (B absent)
+            gathers[i] = gat.struct()
+            if kind == NT:
+                M, N, K = int(p["M"]), B.shape[0], gat.K
+            elif kind == TN:
+                M, N, K = A.shape[0], A.shape[1], gat.K
+            else:
+                raise ValueError("gemm_bf16_group: a gathered operand is NT's A or a segmented TN's X")
+        else:
+            M = A.shape[0]
+        if gat is not None:
+            pass
+        elif kind == TN:
             N, K = A.shape[1], B.shape[1]
         elif kind == NT:
             N, K = B.shape[0], A.shape[1] + (0 if A2 is None else A2.shape[1])
@@ -251,19 +306,25 @@ def gemm_bf16_group(problems, name="gemm_bf16_group"):
         if len(segs) > 3:
             raise ValueError("gemm_bf16_group: at most 3 column segments")
         pad3 = lambda v: (ctypes.c_int * 3)(*(list(v) + [0] * (3 - len(v))))  # noqa: E731
-        arr[i] = GemmBf16Problem(kind, ptr(A), A.stride(0), ptr(A2), 0 if A2 is None else A2.stride(0), k1,
-                                 ptr(B), B.stride(0), ptr(p.get("bias")), ptr(out), out.stride(0),
+        arr[i] = GemmBf16Problem(kind, ptr(A), 0 if A is None else A.stride(0), ptr(A2),
+                                 0 if A2 is None else A2.stride(0), k1,
+                                 ptr(B), 0 if B is None else B.stride(0), ptr(p.get("bias")), ptr(out), out.stride(0),
                                  M, _p(p.get("M_dev")), N, K, acc, ptr(db), int(acc if dba is None else bool(dba)),
                                  A.shape[1] if A2 is not None else 0, len(segs), pad3([g[0] for g in segs]),
-                                 pad3([g[1] for g in segs]), pad3([g[2] for g in segs]), int(c16))
-        keep.append((A, B, A2, out, db))
-        if kind == TN:                     # reads A [M, N] and B [M, K]; writes the [N, K] gradient
+                                 pad3([g[1] for g in segs]), pad3([g[2] for g in segs]), int(c16),
+                                 ctypes.pointer(gathers[i]) if gat is not None else None)
+        keep.append((A, B, A2, out, db, gat))
+        if gat is not None and kind == NT:  # gathered rows in once, weights, C out
+            nbytes += gat.read_bytes(M) + 2 * N * K + (2 if c16 else 4) * M * N
+        elif gat is not None:               # G [M, N] and the gathered rows in, the gradient out
+            nbytes += 2 * M * N + gat.read_bytes(M) + 4 * N * K
+        elif kind == TN:                   # reads A [M, N] and B [M, K]; writes the [N, K] gradient
             nbytes += 2 * M * (N + K) + 4 * N * K
         else:                              # reads A [M, K] and B; writes C [M, N] (bf16 or fp32)
             nbytes += 2 * (M * K + N * K) + (2 if c16 else 4) * M * N
         flops += 2 * M * N * K
     n = len(problems)
-    dev = problems[0]["A"].device
+    dev = out.device
     ws = torch.empty(int(lib.fb_gemm_bf16_group_ws_bytes(arr, n)), device=dev, dtype=torch.uint8)
     _launch(name, nbytes, flops, 2,
             lambda: call("fb_gemm_bf16_group", arr, n, ptr(ws), ws.numel(), stream_ptr()))

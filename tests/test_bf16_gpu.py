@@ -106,6 +106,76 @@ def test_gemm_bf16_nn_on_weight_columns(cuda):
         _check(C, G.double(), B.double(), K, "NN cols %d" % c0)
 
 
+@pytest.mark.parametrize("M,m_dev,dn", [(3000, 2777, 413), (70001, 70001, 413), (20000, 1, 413), (5000, 4321, 0)])
+def test_gemm_bf16_gathered_rows(cuda, M, m_dev, dn):
+    """The projection rows [h | f | t] gathered inside the GEMM (ops.RowGather:
+    node rows by node id, edge rows by edge id, the time block row by row,
+    64-column segments) give, for NT and for the segmented TN with the bias
+    gradient, the products of the materialised rows within the fp32
+    accumulation bound.  Rows past the device-side count carry indices far
+    outside the tables and NaN time rows: they must reach no output."""
+    from fast_b200 import ops
+    g = torch.Generator(device="cpu").manual_seed(11)
+    de, dt, D2 = 186, 100, 200
+    n_nodes, n_edge_rows = 1667, 9000
+    ntab = torch.zeros(n_nodes, 416, dtype=torch.bfloat16)
+    ntab[:, :dn] = _bf(torch.randn(n_nodes, dn, generator=g))
+    etab = torch.zeros(n_edge_rows, 192, dtype=torch.bfloat16)
+    etab[:, :de] = _bf(torch.randn(n_edge_rows, de, generator=g))
+    ntab, etab = ntab.to(cuda), etab.to(cuda)
+    nid = torch.randint(0, n_nodes, (M,), generator=g, dtype=torch.int32)
+    nid[::7] = 3                                             # repeated rows
+    eid = torch.randint(0, n_edge_rows, (M,), generator=g, dtype=torch.int32)
+    nid[m_dev:], eid[m_dev:] = 2 ** 30, -5                     # stale indices past the count
+    nid, eid = nid.to(cuda), eid.to(cuda)
+    T = torch.zeros(M, 104, dtype=torch.bfloat16)
+    T[:, :dt] = _bf(torch.rand(M, dt, generator=g) * 2 - 1)
+    T[m_dev:] = float("nan")
+    T = T.to(cuda)
+    segs, cols, wid = [], [], []
+    if dn:
+        segs.append((ntab, dn, nid, 448)); cols.append(dn); wid.append(448)
+    segs += [(etab, de, eid, 192), (T, dt, None, 128)]
+    cols += [de, dt]; wid += [192, 128]
+    gat = ops.RowGather(segs)
+    K = gat.K
+    # the materialised rows (past the count: zeros) and the weights in the same column layout
+    X = torch.zeros(m_dev, K, dtype=torch.float64, device=cuda)
+    at = 0
+    for (tab, c, idx, w) in segs:
+        X[:, at:at + c] = (tab[idx[:m_dev].long(), :c] if idx is not None else tab[:m_dev, :c]).double()
+        at += w
+    W = torch.zeros(D2, K, dtype=torch.bfloat16, device=cuda)
+    at = 0
+    for c, w in zip(cols, wid):
+        W[:, at:at + c] = _bf(torch.randn(D2, c, generator=g) * 0.05).to(cuda)
+        at += w
+    bias = torch.randn(D2, generator=g).to(cuda)
+    n_dev = torch.tensor([m_dev], dtype=torch.int32, device=cuda)
+    C = torch.full((M, D2), 7.0, device=cuda)
+    ops.gemm_bf16_group([dict(kind=ops.NT, gather=gat, M=M, B=W, bias=bias, out=C, M_dev=n_dev)])
+    torch.cuda.synchronize()
+    _check(C[:m_dev], X, W.double().T, K, "gathered NT", base=bias.double().expand(m_dev, D2))
+    assert bool((C[m_dev:] == 7.0).all())
+    # segmented TN with the bias gradient: dW[:, to + j] += sum_m G[m] X[m, at + j]
+    G = _bf(torch.randn(M, D2, generator=g)).to(cuda)
+    G[m_dev:] = float("nan")
+    dW0 = torch.randn(D2, sum(cols), generator=g).to(cuda)
+    dW = dW0.clone()
+    db = torch.zeros(D2, device=cuda)
+    tn_segs, at, to = [], 0, 0
+    for c, w in zip(cols, wid):
+        tn_segs.append((at, c, to))
+        at, to = at + w, to + c
+    ops.gemm_bf16_group([dict(kind=ops.TN, A=G, gather=gat, out=dW, accumulate=True, db=db, db_accumulate=False,
+                              M_dev=n_dev, segs=tn_segs)])
+    torch.cuda.synchronize()
+    Xc = torch.cat([X[:, a:a + c] for a, c, _ in tn_segs], 1)
+    g64 = G[:m_dev].double()
+    _check(dW, g64.T, Xc, m_dev, "gathered TN dW", base=dW0)
+    _check(db.reshape(-1, 1), g64.T, torch.ones(m_dev, 1, dtype=torch.float64, device=cuda), m_dev, "gathered TN db")
+
+
 @pytest.mark.parametrize("M,m_dev", [(3000, 2777), (70000, 70000), (20000, 1)])
 def test_gemm_bf16_tn_bias_gradient_masks_stale_rows(cuda, M, m_dev):
     from fast_b200 import ops
