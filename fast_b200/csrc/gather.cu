@@ -276,7 +276,8 @@ constexpr uint64_t kTwoOverPiQ64 = 0xa2f9836e4e44152aull;
 
 // sin(x) for a float x: |x| = (k + f) pi/2 with k an integer and |f| <= 1/2,
 // then +-sin(r) or +-cos(r), r = f pi/2, by the quadrant k mod 4 (the
-// library's double sin from 2^28 on).
+// library's double sin from 2^28 on).  Below 2^22 the reduction is two
+// double fmas; from there the fixed-point product below.
 __device__ __forceinline__ float sin_big(float x) {
   const float ax = fabsf(x);
   if (ax >= 268435456.f) return (float)sin((double)x);
@@ -284,6 +285,15 @@ __device__ __forceinline__ float sin_big(float x) {
   int q = 0;
   if (ax < 0.78539816f) {
     r = ax;
+  } else if (ax < 4194304.f) {
+    // |x| < 2^22: Cody & Waite's reduction with pi/2 split in two doubles, a
+    // 30-bit head (k * head is exact for k < 2^23) and a 53-bit tail;
+    // |pi/2 - head - tail| < 2e-26, so |r| is off by < 1e-19
+    const double xd = (double)ax;
+    const double kd = rint(xd * 0x1.45f306dc9c883p-1);               // nearest multiple of pi/2
+    const double rd = fma(-kd, -0x1.de973dcb3b39ap-31, fma(-kd, 0x1.921fb548p+0, xd));
+    r = (float)rd;
+    q = (int)((long long)kd & 3);
   } else {
     const uint32_t bits = __float_as_uint(ax);
     const int e = (int)(bits >> 23) - 127;             // -1 .. 27
