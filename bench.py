@@ -63,6 +63,9 @@ def parse():
                     help="steps of the per-phase device-time breakdown (sampling, forward+backward, all-reduce, "
                          "Adam), each phase a graph of its own; 0 skips it")
     ap.add_argument("--eager", action="store_true", help="launch kernels step by step instead of a CUDA graph")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="positive edges per step instead of the config's (one GPU at --batch 500 runs the per-rank "
+                         "workload of config 5 on 8 GPUs)")
     ap.add_argument("--edges", type=int, default=None,
                     help="prefix subsample: the first N edges of the config's synthetic graph")
     ap.add_argument("--suite", default=None, choices=["kernels", "bf16"],
@@ -345,9 +348,9 @@ def run_reference(args):
     cfg_line = cfg
     if args.data:
         _, cfg_line = workload_graph(args, cfg, device=False)
-    elif args.edges:
+    elif args.edges or args.batch:
         import dataclasses
-        cfg_line = dataclasses.replace(cfg, edges=args.edges)
+        cfg_line = dataclasses.replace(cfg, edges=args.edges or cfg.edges, batch=args.batch or cfg.batch)
     B, gB = batch_sizes(cfg_line, world)
     threads = len(os.sched_getaffinity(0))
     n_edges, rows, frac, note = cpu_plan(args, cfg_line)
@@ -869,6 +872,8 @@ def workload_graph(args, cfg, device=True):
     graphs on the current GPU (config 5: 191 M edges in seconds)."""
     import dataclasses
     from fast_b200.data import make_graph, make_graph_device
+    if args.batch:
+        cfg = dataclasses.replace(cfg, batch=args.batch)
     if not args.data:
         n = args.edges or cfg.edges
         cfg = dataclasses.replace(cfg, edges=n)

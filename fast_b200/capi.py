@@ -106,6 +106,10 @@ _SIGS = {
     "fb_attn_fwd_kvbf16": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I, _I, _F, _F, _U64, _U64, _P, _P, _P, _I64, _P]),
     "fb_attn_bwd_kvbf16": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I, _I, _F, _F, _U64, _U64, _P, _P, _P, _I64, _P,
                                 _P, _I64, _P]),
+    "fb_attn_fwd_kvbf16_bf16out": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I, _I, _F, _F, _U64, _U64, _P, _P, _P, _I64,
+                                        _P]),
+    "fb_attn_bwd_kvbf16_bf16dq": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I, _I, _F, _F, _U64, _U64, _P, _P, _P, _I64,
+                                       _P, _I64, _P, _I64, _P]),
 }
 
 class GemmProblem(ctypes.Structure):

@@ -165,6 +165,8 @@ struct AttnArgs {
   float *dq, *dk, *dv; int64_t lddkv;
   int kv_bf16;             // dk / dv are bf16 (bit patterns, round to nearest even)
   int kv_in_bf16;          // k / v are bf16 rows (bulk-copy kernels only)
+  int agg_bf16;            // agg is bf16 (bulk-copy kernels only): the next product's bf16 operand
+  int dq_bf16; int64_t lddq;  // dq is bf16 at lddq elements per row (bulk-copy kernels only)
 };
 
 // Output (or incoming gradient) row of segment j: j itself, or the row named
@@ -591,7 +593,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerCta, 4) k_attn_fwd_s(AttnArgs a)
         }
       }
     }
-    if (live) reinterpret_cast<float4 *>(a.agg + j * a.ldagg)[lane] = acc;
+    if (live) put4(a.agg, j * a.ldagg + 4 * lane, acc, a.agg_bf16);
   }
 }
 
@@ -824,7 +826,7 @@ __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_fwd_b(AttnArgs a) {
   if (a.n_dst_dev) {
     for (int64_t j = n_dst + (int64_t)blockIdx.x * kBulkWarps + w; j < a.n_dst;
          j += (int64_t)gridDim.x * kBulkWarps)
-      if (live) reinterpret_cast<float4 *>(a.agg + j * a.ldagg)[lane] = zero4;
+      if (live) put4(a.agg, j * a.ldagg + 4 * lane, zero4, a.agg_bf16);
   }
   for (int64_t j = (int64_t)blockIdx.x * kBulkWarps + w; j < n_dst; j += (int64_t)gridDim.x * kBulkWarps) {
     const int beg = a.rptr[j], end = a.rptr[j + 1];
@@ -896,7 +898,7 @@ __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_fwd_b(AttnArgs a) {
         }
       }
     }
-    if (live) reinterpret_cast<float4 *>(a.agg + j * a.ldagg)[lane] = acc;
+    if (live) put4(a.agg, j * a.ldagg + 4 * lane, acc, a.agg_bf16);
   }
 }
 
@@ -1027,7 +1029,7 @@ __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_bwd_b(AttnArgs a) {
         }
       }
     }
-    if (a.dq && live) reinterpret_cast<float4 *>(a.dq + j * (int64_t)a.dim)[lane] = dq;
+    if (a.dq && live) put4(a.dq, j * (a.dq_bf16 ? a.lddq : (int64_t)a.dim) + 4 * lane, dq, a.dq_bf16);
   }
 }
 
@@ -1056,13 +1058,14 @@ int check_attn(const AttnArgs &a, bool bwd) {
     return fb::set_error(FB_ERR_ARG, "attention: q/k/v must be 16-byte aligned");
   if (!(a.drop_p >= 0.f && a.drop_p < 1.f)) return fb::set_error(FB_ERR_ARG, "attention: dropout p must be in [0, 1)");
   if (!bwd) {
-    if (!a.att_out || !a.agg || a.ldagg % 4 || !aligned16(a.agg))
+    if (!a.att_out || !a.agg || a.ldagg % 4 || (!a.agg_bf16 && !aligned16(a.agg)))
       return fb::set_error(FB_ERR_ARG, "attn_fwd: bad att/agg output");
   } else {
     // fp32 gradient rows are stored as 16-byte words, bf16 ones as 8-byte words
     const uintptr_t kv_mask = a.kv_bf16 ? 7u : 15u;
     const bool kv_ok = ((reinterpret_cast<uintptr_t>(a.dk) | reinterpret_cast<uintptr_t>(a.dv)) & kv_mask) == 0;
-    if (!a.att || !a.dagg || a.lddagg % 4 || !aligned16(a.dagg) || a.lddkv % 4 || !kv_ok || !aligned16(a.dq))
+    if (!a.att || !a.dagg || a.lddagg % 4 || !aligned16(a.dagg) || a.lddkv % 4 || !kv_ok ||
+        (!a.dq_bf16 && !aligned16(a.dq)))
       return fb::set_error(FB_ERR_ARG, "attn_bwd: bad gradient buffers");
   }
   return FB_OK;
@@ -1134,8 +1137,12 @@ int launch_bulk(const AttnArgs &a, bool bwd, cudaStream_t stream) {
 int launch_fwd(const AttnArgs &a, cudaStream_t stream) {
   int rc = check_attn(a, false);
   if (rc) return rc;
-  if (a.kv_in_bf16 && !bulk_path(a))
-    return fb::set_error(FB_ERR_UNSUPPORTED, "attention: bf16 K|V needs interleaved rows [E, 2 dim], dim <= 128");
+  if ((a.kv_in_bf16 || a.agg_bf16 || a.dq_bf16) && !bulk_path(a))
+    return fb::set_error(FB_ERR_UNSUPPORTED,
+                         "attention: bf16 K|V rows and bf16 outputs need interleaved rows [E, 2 dim], dim <= 128");
+  if ((a.agg_bf16 && ((reinterpret_cast<uintptr_t>(a.agg) & 7u) || a.ldagg % 4)) ||
+      (a.dq_bf16 && a.dq && ((reinterpret_cast<uintptr_t>(a.dq) & 7u) || a.lddq % 4 || a.lddq < a.dim)))
+    return fb::set_error(FB_ERR_ARG, "attention: bf16 outputs need 8-byte aligned rows, pitch a multiple of 4");
   if (a.n_dst == 0) return FB_OK;
   const int grid = attn_grid(a.n_dst), nv = (a.dim / 4 + 31) / 32;
   if (bulk_path(a)) {
@@ -1163,8 +1170,12 @@ int launch_fwd(const AttnArgs &a, cudaStream_t stream) {
 int launch_bwd(const AttnArgs &a, cudaStream_t stream) {
   int rc = check_attn(a, true);
   if (rc) return rc;
-  if (a.kv_in_bf16 && !bulk_path(a))
-    return fb::set_error(FB_ERR_UNSUPPORTED, "attention: bf16 K|V needs interleaved rows [E, 2 dim], dim <= 128");
+  if ((a.kv_in_bf16 || a.agg_bf16 || a.dq_bf16) && !bulk_path(a))
+    return fb::set_error(FB_ERR_UNSUPPORTED,
+                         "attention: bf16 K|V rows and bf16 outputs need interleaved rows [E, 2 dim], dim <= 128");
+  if ((a.agg_bf16 && ((reinterpret_cast<uintptr_t>(a.agg) & 7u) || a.ldagg % 4)) ||
+      (a.dq_bf16 && a.dq && ((reinterpret_cast<uintptr_t>(a.dq) & 7u) || a.lddq % 4 || a.lddq < a.dim)))
+    return fb::set_error(FB_ERR_ARG, "attention: bf16 outputs need 8-byte aligned rows, pitch a multiple of 4");
   if (a.n_dst == 0) return FB_OK;
   const int grid = attn_grid(a.n_dst), nv = (a.dim / 4 + 31) / 32;
   if (bulk_path(a)) {
@@ -1296,6 +1307,48 @@ extern "C" int fb_attn_bwd_kvbf16(const float *q, int64_t ldq, const uint16_t *k
   a.kv_in_bf16 = 1;
   a.heads = heads; a.dim = dim; a.slope = slope; a.drop_p = drop_p; a.seed = seed; a.offset = offset;
   a.att = att; a.dagg = dagg; a.lddagg = lddagg; a.dq = dq; a.lddkv = lddkv;
+  a.dk = reinterpret_cast<float *>(dkv);
+  a.dv = reinterpret_cast<float *>(dkv + dim);
+  a.kv_bf16 = 1;
+  return launch_bwd(a, stream);
+}
+
+// fb_attn_fwd_kvbf16 with agg written as bf16 (round to nearest even) at
+// ldagg elements per row: the aggregate is only the w_out product's bf16
+// operand in the bf16 projection mode.
+extern "C" int fb_attn_fwd_kvbf16_bf16out(const float *q, int64_t ldq, const uint16_t *kv, int64_t ldkv,
+                                          const int32_t *rptr, int64_t n_dst, const int32_t *n_dst_dev, int heads,
+                                          int dim, float slope, float drop_p, uint64_t seed, uint64_t offset,
+                                          const uint64_t *offset_dev, float *att, uint16_t *agg, int64_t ldagg,
+                                          cudaStream_t stream) {
+  AttnArgs a{};
+  a.offset_dev = offset_dev;
+  a.q = q; a.ldq = ldq; a.ldkv = ldkv; a.rptr = rptr; a.n_dst = n_dst; a.n_dst_dev = n_dst_dev;
+  a.k = reinterpret_cast<const float *>(kv);
+  a.v = reinterpret_cast<const float *>(kv + dim);
+  a.kv_in_bf16 = 1;
+  a.heads = heads; a.dim = dim; a.slope = slope; a.drop_p = drop_p; a.seed = seed; a.offset = offset;
+  a.att_out = att; a.agg = reinterpret_cast<float *>(agg); a.ldagg = ldagg; a.agg_bf16 = 1;
+  return launch_fwd(a, stream);
+}
+
+// fb_attn_bwd_kvbf16 with dq written as bf16 at lddq elements per row: dq is
+// only the bf16 operand of the Q-side gradient products.
+extern "C" int fb_attn_bwd_kvbf16_bf16dq(const float *q, int64_t ldq, const uint16_t *kv, int64_t ldkv,
+                                         const int32_t *rptr, int64_t n_dst, const int32_t *n_dst_dev, int heads,
+                                         int dim, float slope, float drop_p, uint64_t seed, uint64_t offset,
+                                         const uint64_t *offset_dev, const float *att, const float *dagg,
+                                         int64_t lddagg, uint16_t *dq, int64_t lddq, uint16_t *dkv, int64_t lddkv,
+                                         cudaStream_t stream) {
+  AttnArgs a{};
+  a.offset_dev = offset_dev;
+  a.q = q; a.ldq = ldq; a.ldkv = ldkv; a.rptr = rptr; a.n_dst = n_dst; a.n_dst_dev = n_dst_dev;
+  a.k = reinterpret_cast<const float *>(kv);
+  a.v = reinterpret_cast<const float *>(kv + dim);
+  a.kv_in_bf16 = 1;
+  a.heads = heads; a.dim = dim; a.slope = slope; a.drop_p = drop_p; a.seed = seed; a.offset = offset;
+  a.att = att; a.dagg = dagg; a.lddagg = lddagg; a.lddkv = lddkv;
+  a.dq = reinterpret_cast<float *>(dq); a.dq_bf16 = 1; a.lddq = lddq;
   a.dk = reinterpret_cast<float *>(dkv);
   a.dv = reinterpret_cast<float *>(dkv + dim);
   a.kv_bf16 = 1;

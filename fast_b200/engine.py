@@ -258,10 +258,11 @@ class FusedStep:
             ops.gemm_bf16_group(probs, name="gemm_group:kv_q")
             ops.gemm_group([dict(kind=ops.NT, A=Qin, B=L.w_q.weight, bias=L.w_q.bias, out=Q)], name="gemm_group:q1")
         p_att = L.att_dropout_p if training else 0.0
-        agg, att = ops.attn_fwd_kvbf16(Q, KV, blk.rptr, L.num_head, L.negative_slope, p_att, 0x5EED + l, 0,
-                                       n_dst_dev=nd_dev, offset_dev=offset_dev)
+        # the aggregate is only the w_out product's bf16 operand: written as bf16
         agg_bf = torch.empty(nd, lp.ka, device=dev, dtype=torch.bfloat16)
-        ops.cast_bf16([(agg, agg_bf[:, :D], nd_dev)])
+        att = ops.attn_fwd_kvbf16_bf16out(Q, KV, blk.rptr, L.num_head, L.negative_slope, agg_bf[:, :D], p_att,
+                                          0x5EED + l, 0, n_dst_dev=nd_dev, offset_dev=offset_dev)
+        agg = None
         Z = torch.empty(nd, D, device=dev)
         if dn > 0:
             p_out = dict(kind=ops.NT, A=agg_bf[:, :D], A2=Qin[:, :dn], k1=lp.ka, B=lp.W_out_bf[:, :lp.ka + dn],
@@ -333,8 +334,16 @@ class FusedStep:
             dh = torch.empty(dh_rows, dn, device=dev)
             probs.append(dict(kind=ops.NN, A=dZb, B=lp.W_out_bf[:, lp.ka:lp.ka + dn], out=dh[:nd], M_dev=nd_dev))
         ops.gemm_bf16_group(probs, name="gemm_group:bwd_dz")
-        dQ, dKV = ops.attn_bwd_kvbf16(st["Q"], st["KV"], blk.rptr, st["att"], dagg, L.num_head, L.negative_slope,
-                                      st["p_att"], 0x5EED + l, 0, n_dst_dev=nd_dev, offset_dev=st["offset_dev"])
+        if dn > 0:
+            # dq is only the bf16 operand of the Q-side products: written as bf16
+            dQ_bf = torch.empty(nd, lp.ka, device=dev, dtype=torch.bfloat16)
+            dKV = ops.attn_bwd_kvbf16_bf16dq(st["Q"], st["KV"], blk.rptr, st["att"], dagg, L.num_head,
+                                             L.negative_slope, dQ_bf[:, :D], st["p_att"], 0x5EED + l, 0,
+                                             n_dst_dev=nd_dev, offset_dev=st["offset_dev"])
+        else:
+            dQ, dKV = ops.attn_bwd_kvbf16(st["Q"], st["KV"], blk.rptr, st["att"], dagg, L.num_head,
+                                          L.negative_slope, st["p_att"], 0x5EED + l, 0, n_dst_dev=nd_dev,
+                                          offset_dev=st["offset_dev"])
         X, gat = st["A"], st["gather"]
         v = torch.empty(D, device=dev)            # sum over rows of dQ
         # the K|V weight and bias gradient over the whole projection row: one
@@ -356,8 +365,6 @@ class FusedStep:
             dA_t = torch.empty(E, dtime, device=dev, dtype=torch.bfloat16)
             probs.append(dict(kind=ops.NN, A=dKV, B=W_t[:, t_at:t_at + dtime], out=dA_t, M_dev=E_dev))
         if dn > 0:
-            dQ_bf = torch.empty(nd, lp.ka, device=dev, dtype=torch.bfloat16)
-            ops.cast_bf16([(dQ, dQ_bf[:, :D], nd_dev)])
             dQb = dQ_bf[:, :D]
             probs.append(dict(kind=ops.TN, A=dQb, B=Qin[:, :lp.kq], out=g(L.w_q.weight), accumulate=True,
                               M_dev=nd_dev, db=v, db_accumulate=False, segs=[(at, d, lo) for at, lo, d in lp.q_segs]))

@@ -427,6 +427,47 @@ def attn_bwd_kvbf16(q, kv, rptr, att, dagg, heads, slope, drop_p=0.0, seed=0, of
     return dq, dkv
 
 
+def attn_fwd_kvbf16_bf16out(q, kv, rptr, heads, slope, agg_bf, drop_p=0.0, seed=0, offset=0, n_dst_dev=None,
+                            offset_dev=None):
+    """attn_fwd_kvbf16 writing the aggregate as bf16 into agg_bf ([Nd, D] view,
+    rows 8-byte aligned); returns att fp32."""
+    nd = rptr.numel() - 1
+    E, D2 = kv.shape
+    D = D2 // 2
+    _bf16_rows(kv, "attn_fwd_kvbf16_bf16out kv")
+    if agg_bf.dtype != torch.bfloat16 or tuple(agg_bf.shape) != (nd, D):
+        raise ValueError("attn_fwd_kvbf16_bf16out: agg_bf must be a bf16 [n_dst, D] view")
+    ldq = 0 if (q.shape[0] == 1 and nd != 1) else q.stride(0)
+    att = torch.empty(E, heads, device=kv.device, dtype=torch.float32)
+    qrows = nd if ldq else 1
+    nbytes = 4 * (qrows * D + (nd + 1) + E * heads) + 2 * nd * D + 2 * 2 * E * D
+    _launch("attn_fwd", nbytes, 0, 1,
+            lambda: call("fb_attn_fwd_kvbf16_bf16out", ptr(q), ldq, ptr(kv), kv.stride(0), ptr(rptr), nd,
+                         _p(n_dst_dev), heads, D, slope, drop_p, seed, offset, _p(offset_dev), ptr(att), ptr(agg_bf),
+                         agg_bf.stride(0), stream_ptr()))
+    return att
+
+
+def attn_bwd_kvbf16_bf16dq(q, kv, rptr, att, dagg, heads, slope, dq_bf, drop_p=0.0, seed=0, offset=0,
+                           n_dst_dev=None, offset_dev=None):
+    """attn_bwd_kvbf16 writing dq as bf16 into dq_bf ([Nd, D] view); returns dK|dV bf16 [E, 2D]."""
+    nd = rptr.numel() - 1
+    E, D2 = kv.shape
+    D = D2 // 2
+    _bf16_rows(kv, "attn_bwd_kvbf16_bf16dq kv")
+    if dq_bf.dtype != torch.bfloat16 or tuple(dq_bf.shape) != (nd, D):
+        raise ValueError("attn_bwd_kvbf16_bf16dq: dq_bf must be a bf16 [n_dst, D] view")
+    ldq = 0 if (q.shape[0] == 1 and nd != 1) else q.stride(0)
+    dkv = torch.empty(E, 2 * D, device=kv.device, dtype=torch.bfloat16)
+    qrows = nd if ldq else 1
+    nbytes = 4 * (qrows * D + nd * D + E * heads + (nd + 1)) + 2 * nd * D + 2 * 4 * E * D
+    _launch("attn_bwd", nbytes, 0, 1,
+            lambda: call("fb_attn_bwd_kvbf16_bf16dq", ptr(q), ldq, ptr(kv), kv.stride(0), ptr(rptr), nd,
+                         _p(n_dst_dev), heads, D, slope, drop_p, seed, offset, _p(offset_dev), ptr(att), ptr(dagg),
+                         dagg.stride(0), ptr(dq_bf), dq_bf.stride(0), ptr(dkv), dkv.stride(0), stream_ptr()))
+    return dkv
+
+
 def attn_bwd_bf16kv(q, k, v, rptr, att, dagg, heads, slope, drop_p=0.0, seed=0, offset=0, n_dst_dev=None,
                     offset_dev=None, dq=None):
     """attn_bwd with dk | dv written as one bf16 [E, 2D] matrix (the operand of

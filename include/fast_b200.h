@@ -167,6 +167,19 @@ int fb_attn_bwd_kvbf16(const float *q, int64_t ldq, const uint16_t *kv, int64_t 
                        uint64_t seed, uint64_t offset, const uint64_t *offset_dev, const float *att,
                        const float *dagg, int64_t lddagg, float *dq, uint16_t *dkv, int64_t lddkv,
                        cudaStream_t stream);
+/* The same two with the row outputs that only feed bf16 products written as
+ * bf16 (round to nearest even; rows 8-byte aligned, pitch a multiple of 4):
+ * agg [n_dst, ldagg] (the w_out operand, layers.py:213-217) and dq
+ * [n_dst, lddq] (the Q-side gradient operand) -- one cast launch less each. */
+int fb_attn_fwd_kvbf16_bf16out(const float *q, int64_t ldq, const uint16_t *kv, int64_t ldkv, const int32_t *rptr,
+                               int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim, float slope,
+                               float drop_p, uint64_t seed, uint64_t offset, const uint64_t *offset_dev, float *att,
+                               uint16_t *agg, int64_t ldagg, cudaStream_t stream);
+int fb_attn_bwd_kvbf16_bf16dq(const float *q, int64_t ldq, const uint16_t *kv, int64_t ldkv, const int32_t *rptr,
+                              int64_t n_dst, const int32_t *n_dst_dev, int heads, int dim, float slope,
+                              float drop_p, uint64_t seed, uint64_t offset, const uint64_t *offset_dev,
+                              const float *att, const float *dagg, int64_t lddagg, uint16_t *dq, int64_t lddq,
+                              uint16_t *dkv, int64_t lddkv, cudaStream_t stream);
 /* Sticky error bits of the attention kernels on the current device (2 = a
  * bounded wait for a shared-memory bulk copy timed out and the warp gave up);
  * synchronises; clear resets. */
