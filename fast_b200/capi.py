@@ -145,7 +145,9 @@ class GemmBf16Problem(ctypes.Structure):
     _fields_ = GemmProblem._fields_ + [("ka", ctypes.c_int), ("nseg", ctypes.c_int),
                                        ("seg_at", ctypes.c_int * 3), ("seg_len", ctypes.c_int * 3),
                                        ("seg_to", ctypes.c_int * 3), ("c_bf16", ctypes.c_int),
-                                       ("gather", ctypes.POINTER(Bf16RowGather))]
+                                       ("gather", ctypes.POINTER(Bf16RowGather)), ("add", ctypes.c_void_p),
+                                       ("add_idx", ctypes.c_void_p), ("ld_add", ctypes.c_int64),
+                                       ("add_rows", ctypes.c_int64)]
 
 
 _SIGS["fb_gemm_bf16_group_ws_bytes"] = (_SZ, [ctypes.POINTER(GemmBf16Problem), _I])

@@ -113,6 +113,10 @@ struct BfProb {
   int c_bf16;                // NT / NN: C holds bf16 (round to nearest even), written, not accumulated
   int gat, g_nseg, g_end[3], g_rows[3];   // A of the tiling gathered (see fb_bf16_row_gather)
   const int32_t *g_idx[3];
+  const float *add;                         // NT / NN: + add[add_idx[m] * ld_add + n] in the epilogue
+  const int32_t *add_idx;
+  int64_t ld_add;
+  int add_rows;
   uint32_t idesc;
   int64_t M;
   const int32_t *M_dev;
@@ -451,6 +455,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
       const float *const bias = tn ? nullptr : q.bias;
       const bool accum = !tn && q.accumulate;
       const bool c16 = q.c_bf16 != 0;
+      const float *const add = tn ? nullptr : q.add;
+      const int32_t *const add_idx = q.add_idx;
+      const int64_t ld_add = q.ld_add;
+      const int add_rows = q.add_rows;
       const int64_t row0 = it.r0 + qd * 32;
       const int nrows = rows - row0 < 32 ? (int)max(rows - row0, (int64_t)0) : 32;
 #pragma unroll 1
@@ -462,7 +470,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
         for (int k = 0; k < 32; ++k) stg[lane * kStagePitch + k] = __uint_as_float(r[k]);
         __syncwarp();
         const int col = it.c0 + c0 + lane;
-        if (c16 && c0 + lane < bn && col < ncols) {
+        if (add && c0 + lane < bn && col < ncols) {
+          // + a row of the add table per output row (NT / NN)
+          const float bv = bias ? bias[col] : 0.f;
+          const float *sv = stg + lane;
+          const float *pa = add + col;
+          for (int rr = 0; rr < nrows; ++rr) {
+            const int ix = min(max(__ldg(add_idx + row0 + rr), 0), add_rows - 1);
+            const float v = sv[rr * kStagePitch] + bv + __ldg(pa + (int64_t)ix * ld_add);
+            if (c16) {
+              const __nv_bfloat16 hv = __float2bfloat16_rn(v);
+              reinterpret_cast<uint16_t *>(out)[(row0 + rr) * ld + col] = *reinterpret_cast<const uint16_t *>(&hv);
+            } else {
+              float *o = out + (row0 + rr) * ld + col;
+              *o = accum ? *o + v : v;
+            }
+          }
+        } else if (c16 && c0 + lane < bn && col < ncols) {
           const float bv = bias ? bias[col] : 0.f;
           uint16_t *o = reinterpret_cast<uint16_t *>(out) + row0 * ld + col;
           const float *sv = stg + lane;
@@ -636,6 +660,8 @@ bool gather_ok(const fb_bf16_row_gather &g, int K) {
 bool problem_ok(const fb_gemm_bf16_problem &p) {
   if (p.kind < FB_GEMM_NT || p.kind > FB_GEMM_TN) return false;
   if (p.M < 0 || p.M > (int64_t)1 << 30 || p.N < 1 || p.K < 1) return false;
+  if (p.add && (p.kind == FB_GEMM_TN || !p.add_idx || p.ld_add < p.N || p.add_rows < 1 || p.add_rows > INT32_MAX))
+    return false;
   if (p.gather) {
     if (!gather_ok(*p.gather, p.K)) return false;
     if (p.kind == FB_GEMM_NT) {
@@ -701,6 +727,10 @@ int gather_maps(BfProb &q, const fb_bf16_row_gather &g, int box_rows) {
 int build_prob(BfProb &q, const fb_gemm_bf16_problem &p, float *ws) {
   std::memset(&q, 0, sizeof(q));
   q.kind = p.kind;
+  q.add = p.add;
+  q.add_idx = p.add_idx;
+  q.ld_add = p.ld_add;
+  q.add_rows = (int)p.add_rows;
   q.M = p.M;
   q.M_dev = p.M_dev;
   q.N = p.N;

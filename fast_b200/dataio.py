@@ -98,10 +98,53 @@ def build_ext_full(csv_path, npz_path=None, add_reverse=False):
     return res
 
 
-def load_graph(data_dir):
+def build_ext_full_device(csv_path, device, add_reverse=False):
+    """build_ext_full on the GPU: the same CSR (indptr, indices, ts, eid;
+    gen_graph.py's contract), as device tensors, byte for byte.  The lists are
+    grouped by node with a stable sort and ordered by time with a second
+    stable sort, both on the device; a list holding equal timestamps takes
+    the order of the reference's own np.argsort of its times (run on the host
+    for those lists only, as build_ext_full does), since an unstable sort's
+    order among ties is the one thing a device sort cannot reproduce."""
+    import pandas as pd
+    import torch
+    df = pd.read_csv(csv_path)
+    dev = torch.device(device)
+    src = torch.from_numpy(df["src"].values.astype(np.int32)).to(dev)
+    dst = torch.from_numpy(df["dst"].values.astype(np.int32)).to(dev)
+    t = torch.from_numpy(df["time"].values.astype(np.float32)).to(dev)
+    idx = torch.arange(len(df), dtype=torch.int32, device=dev)
+    num_nodes = max(int(df["src"].max()), int(df["dst"].max())) + 1
+    if add_reverse:
+        key, nbr = torch.stack([src, dst], 1).reshape(-1), torch.stack([dst, src], 1).reshape(-1)
+        tt, ii = t.repeat_interleave(2), idx.repeat_interleave(2)
+    else:
+        key, nbr, tt, ii = src, dst, t, idx
+    _, order = torch.sort(key, stable=True)                  # insertion order within each node
+    key, nbr, tt, ii = key[order], nbr[order], tt[order], ii[order]
+    indptr = torch.zeros(num_nodes + 1, dtype=torch.int64, device=dev)
+    indptr[1:] = torch.cumsum(torch.bincount(key.long(), minlength=num_nodes), 0)
+    _, by_t = torch.sort(tt, stable=True)                      # lexsort((tt, key)): time, then node
+    _, by_k = torch.sort(key[by_t], stable=True)
+    by_time = by_t[by_k]
+    out_nbr, out_t, out_i = nbr[by_time].clone(), tt[by_time].clone(), ii[by_time].clone()
+    same = (key[1:] == key[:-1]) & (out_t[1:] == out_t[:-1])
+    tie_nodes = torch.unique(key[:-1][same]).cpu().numpy()
+    if tie_nodes.size:
+        ip = indptr.cpu().numpy()
+        for n in tie_nodes:
+            b, e = int(ip[n]), int(ip[n + 1])
+            s = torch.from_numpy(np.argsort(tt[b:e].cpu().numpy())).to(dev)
+            out_nbr[b:e], out_t[b:e], out_i[b:e] = nbr[b:e][s], tt[b:e][s], ii[b:e][s]
+    return dict(indptr=indptr.to(torch.int32), indices=out_nbr, ts=out_t, eid=out_i)
+
+
+def load_graph(data_dir, device=None):
     """utils.py:54-57 + train.py:99-100: edges.csv and ext_full.npz of a
     dataset directory as a TemporalGraph (edge list in chronological order,
-    CSR, train / validation ends from ext_roll)."""
+    CSR, train / validation ends from ext_roll).  With `device`, every array
+    goes straight from the files into device memory (one copy each, nothing
+    rebuilt on the host), as make_graph_device's graphs are."""
     import pandas as pd
     df = pd.read_csv(os.path.join(data_dir, "edges.csv"))
     g = np.load(os.path.join(data_dir, "ext_full.npz"))
@@ -109,11 +152,14 @@ def load_graph(data_dir):
     n = len(df)
     train_end = int(np.argmax(roll > 0)) if (roll > 0).any() else n
     val_end = int(np.argmax(roll > 1)) if (roll > 1).any() else n
-    return TemporalGraph(src=df["src"].values.astype(np.int32), dst=df["dst"].values.astype(np.int32),
-                         ts=df["time"].values.astype(np.float32), indptr=g["indptr"].astype(np.int32),
-                         indices=g["indices"].astype(np.int32), eid=g["eid"].astype(np.int32),
-                         ts_csr=g["ts"].astype(np.float32), n_nodes=int(g["indptr"].shape[0] - 1),
-                         train_end=train_end, val_end=val_end)
+    arrays = dict(src=df["src"].values.astype(np.int32), dst=df["dst"].values.astype(np.int32),
+                  ts=df["time"].values.astype(np.float32), indptr=g["indptr"].astype(np.int32),
+                  indices=g["indices"].astype(np.int32), eid=g["eid"].astype(np.int32),
+                  ts_csr=g["ts"].astype(np.float32))
+    if device is not None:
+        import torch
+        arrays = {k: torch.from_numpy(v).to(torch.device(device)) for k, v in arrays.items()}
+    return TemporalGraph(n_nodes=int(g["indptr"].shape[0] - 1), train_end=train_end, val_end=val_end, **arrays)
 
 
 def write_dataset(graph, data_dir):

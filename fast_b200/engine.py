@@ -47,6 +47,12 @@ _ALIGN = 64            # flat-buffer segments start on 256-byte boundaries
 FUSED_GATHER_OFF = os.environ.get("FB_FUSED_GATHER", "0") != "1"
 
 
+# FB_SIDE_STREAMS=0 keeps every launch of the step on one stream
+SIDE_STREAMS = os.environ.get("FB_SIDE_STREAMS", "1") != "0"
+# FB_NODE_PRODUCT=0 computes layer 0's node-feature product per edge row
+NODE_PRODUCT = os.environ.get("FB_NODE_PRODUCT", "1") != "0"
+
+
 def pad64(n):
     return (n + 63) // 64 * 64 if n > 0 else 0
 
@@ -172,6 +178,42 @@ class FusedStep:
     def parameters(self):
         return list(self.model.parameters())
 
+    # -- a second stream for launches nothing downstream waits for ------------
+    def _side(self, fn, *uses):
+        """Enqueues fn's launches on a side stream, after everything enqueued
+        so far on the current stream, so that they overlap the launches that
+        follow (a layer's time-encoding and Q-bias gradients run beside the
+        next layer's backward).  `uses`: tensors allocated on the current
+        stream that fn reads.  The current stream joins the side stream at the
+        end of the step (_join); with FB_SIDE_STREAMS=0, fn runs inline."""
+        if not SIDE_STREAMS:
+            fn()
+            return
+        cur = torch.cuda.current_stream()
+        if getattr(self, "_side_stream", None) is None or self._side_stream.device != cur.device:
+            self._side_stream = torch.cuda.Stream(device=cur.device)
+        side = self._side_stream
+        side.wait_stream(cur)
+        for t in uses:
+            if t is not None:
+                t.record_stream(side)
+        with torch.cuda.stream(side):
+            fn()
+        self._side_pending = True
+
+    def _in_side(self):
+        """Context for launches that must follow the side stream's work (a
+        gradient bucket's all-reduce, issued from the stream that last wrote it)."""
+        import contextlib
+        if SIDE_STREAMS and getattr(self, "_side_pending", False):
+            return torch.cuda.stream(self._side_stream)
+        return contextlib.nullcontext()
+
+    def _join(self):
+        if getattr(self, "_side_pending", False):
+            torch.cuda.current_stream().wait_stream(self._side_stream)
+            self._side_pending = False
+
     # -- bf16 projection mode -------------------------------------------------
     def _build_bf16(self):
         """bf16 copies of the projection weights in the column layout of the
@@ -246,11 +288,23 @@ class FusedStep:
                                                 dt=blk.dt_edges, w=wv, b=bt, device=dev, n_rows_dev=E_dev, dn=dn,
                                                 de=de, **hsrc)
             probs = [dict(kind=ops.NT, A=X[:, :kx], B=lp.W_kv_bf[:, :kx], bias=lp.b_kv, out=KV, M_dev=E_dev)]
+            if self._node_product(l, h, node_table, E):
+                # the node-feature block of every K|V row is the product of one of
+                # the table's few rows: P = table . W_h^T once per table row, then
+                # the rows' product runs over their [f | time] columns only and adds
+                # P[source node] in its epilogue
+                f_at = lp.kv_segs[1][0]
+                P = torch.empty(node_table.shape[0], 2 * D, device=dev)
+                probs = [dict(kind=ops.NT, A=node_table[:, :dn], B=lp.W_kv_bf[:, :dn], out=P)]
+                kv_prob = dict(kind=ops.NT, A=X[:, f_at:kx], B=lp.W_kv_bf[:, f_at:kx], bias=lp.b_kv, out=KV,
+                               M_dev=E_dev, add=P, add_idx=blk.src_nodes)
         if dn > 0:
             Qin, kq = ops.gather_time_encode_bf16(nd, w=wv, b=bt, device=dev, n_rows_dev=nd_dev, dn=dn, **hdst)
             Q = torch.empty(nd, D, device=dev)
             probs.append(dict(kind=ops.NT, A=Qin[:, :kq], B=lp.W_q_bf[:, :kq], bias=L.w_q.bias, out=Q, M_dev=nd_dev))
             ops.gemm_bf16_group(probs, name="gemm_group:kv_q")
+            if gat is None and X is not None and probs[0]["out"] is not KV:
+                ops.gemm_bf16_group([kv_prob], name="gemm_group:kv_rows")
         else:
             # one shared Q input row cos(b_t): its product stays fp32
             Qin = ops.gather_time_encode(1, w=wv, b=bt, device=dev)
@@ -277,6 +331,15 @@ class FusedStep:
         st = dict(blk=blk, A=X, gather=gat, KV=KV, Qin=Qin, Q=Q, agg=agg, agg_bf=agg_bf, att=att, y=y, p_att=p_att,
                   p_drop=p_drop, offset_dev=offset_dev)
         return st, out
+
+    def _node_product(self, l, h, node_table, E):
+        """Layer 0's node-feature product runs per node-table row (then gathered
+        by the epilogue) when the table has fewer rows than a quarter of the
+        block's edges: bf16 tables read by index, no previous-layer input.
+        FB_NODE_PRODUCT=0 keeps the per-edge product."""
+        lp = self.layers[l]
+        return (NODE_PRODUCT and l == 0 and h is None and lp.dn > 0 and lp.de + lp.dtime > 0 and
+                node_table is not None and node_table.dtype == torch.bfloat16 and 4 * node_table.shape[0] < E)
 
     def _layer0_gather(self, l, blk, h, node_table, edge_table, wv, bt, dev):
         """The gathered projection rows of layer 0 (ops.RowGather), when the
@@ -376,17 +439,28 @@ class FusedStep:
             ops.gemm_bf16_group(probs, name="gemm_group:bwd_dkv_dq")
             ops.gemm_group([dict(kind=ops.TN, A=dQ, B=None, out=None, M_dev=nd_dev, db=v, db_accumulate=False)],
                            name="gemm_group:dq_sum")
+        self._side(lambda: self._time_grads(l, st, dA_t, v), dA_t, v, st["Qin"])
+        return dh
+
+    def _time_grads(self, l, st, dA_t, v):
+        """The time encoder's and the Q bias's gradients of layer l, from the
+        time-encoding input gradient dA_t and v = sum over rows of dQ: nothing
+        else in the step reads them."""
+        lp = self.layers[l]
+        L, dn, dtime = lp.L, lp.dn, lp.dtime
+        blk = st["blk"]
+        g = lambda p: p.grad
         if dtime > 0:
             ops.time_encode_bwd(dA_t, blk.dt_edges, L.time_enc.w.weight.view(-1), L.time_enc.w.bias,
-                                g(L.time_enc.w.weight).view(-1), g(L.time_enc.w.bias), n_dev=E_dev)
+                                g(L.time_enc.w.weight).view(-1), g(L.time_enc.w.bias), n_dev=blk.n_edges_dev)
         bt = L.time_enc.w.bias if dtime > 0 else None
         gbt = g(L.time_enc.w.bias) if dtime > 0 else None
         if dn == 0:
+            # one shared Q input row cos(b_t): every Q-side gradient needs only sum_rows dQ
             ops.q_time_bwd(v, L.w_q.weight, dn, dtime, bt, g(L.w_q.bias), gbt, qin0=st["Qin"][0],
                            dW_q=g(L.w_q.weight))
         else:
             ops.q_time_bwd(v, L.w_q.weight, dn, dtime, bt, g(L.w_q.bias), gbt)
-        return dh
 
     # -- one layer ------------------------------------------------------------
     def _layer_fwd(self, l, blk, h, node_table, edge_table, offset_dev, training):
@@ -486,16 +560,7 @@ class FusedStep:
                 probs.append(dict(kind=ops.NN, A=dQ, B=L.w_q.weight[:, :dn], out=dh[:nd], accumulate=True,
                                   M_dev=nd_dev))
         ops.gemm_group(probs, name="gemm_group:bwd_dkv_dq")
-        if dtime > 0:
-            ops.time_encode_bwd(dA_t, blk.dt_edges, L.time_enc.w.weight.view(-1), L.time_enc.w.bias,
-                                g(L.time_enc.w.weight).view(-1), g(L.time_enc.w.bias), n_dev=E_dev)
-        bt = L.time_enc.w.bias if dtime > 0 else None
-        gbt = g(L.time_enc.w.bias) if dtime > 0 else None
-        if dn == 0:
-            # one shared Q input row cos(b_t): every Q-side gradient needs only sum_rows dQ
-            ops.q_time_bwd(v, L.w_q.weight, dn, dtime, bt, g(L.w_q.bias), gbt, qin0=Qin[0], dW_q=g(L.w_q.weight))
-        else:
-            ops.q_time_bwd(v, L.w_q.weight, dn, dtime, bt, g(L.w_q.bias), gbt)
+        self._side(lambda: self._time_grads(l, st, dA_t, v), dA_t, v, Qin)
         return dh
 
     # -- node memory (GRU updater) ---------------------------------------------
@@ -626,12 +691,14 @@ class FusedStep:
 
     # -- whole step -----------------------------------------------------------
     def _buckets_done(self, hook, upto):
-        """Calls hook(i) for every gradient bucket i < upto not yet reported."""
+        """Calls hook(i) for every gradient bucket i < upto not yet reported
+        (on the side stream when side launches wrote into it)."""
         if hook is None:
             return
-        while self._reported < min(upto, len(self.grad_buckets)):
-            hook(self._reported)
-            self._reported += 1
+        with self._in_side():
+            while self._reported < min(upto, len(self.grad_buckets)):
+                hook(self._reported)
+                self._reported += 1
 
     def step(self, blocks, node_table, edge_table, loss_out, zero_grad=True, scores=None, mailbox=None,
              roots=None, root_ts=None, grad_hook=None):
@@ -693,6 +760,7 @@ class FusedStep:
                 dh = torch.zeros(mem_st["n"], self.mem.dim_hid, device=dev)
             self._memory_bwd(mem_st, dh)
         self._buckets_done(grad_hook, len(self.grad_buckets))
+        self._join()
         return loss_out
 
 

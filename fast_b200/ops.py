@@ -313,7 +313,16 @@ def gemm_bf16_group(problems, name="gemm_bf16_group"):
                                  A.shape[1] if A2 is not None else 0, len(segs), pad3([g[0] for g in segs]),
                                  pad3([g[1] for g in segs]), pad3([g[2] for g in segs]), int(c16),
                                  ctypes.pointer(gathers[i]) if gat is not None else None)
-        keep.append((A, B, A2, out, db, gat))
+        add, add_idx = p.get("add"), p.get("add_idx")
+        if add is not None:
+            # C[m] += add[add_idx[m]] in the epilogue: an fp32 table [rows, >= N] and int32 indices
+            _f32_rows(add, "gemm_bf16_group add table")
+            if add_idx is None or add_idx.dtype != torch.int32 or add.shape[1] < N:
+                raise ValueError("gemm_bf16_group: add needs an fp32 [rows, >= N] table and int32 add_idx")
+            arr[i].add, arr[i].add_idx = ptr(add), ptr(add_idx)
+            arr[i].ld_add, arr[i].add_rows = add.stride(0), add.shape[0]
+            nbytes += 4 * M * (N + 1)
+        keep.append((A, B, A2, out, db, gat, add, add_idx))
         if gat is not None and kind == NT:  # gathered rows in once, weights, C out
             nbytes += gat.read_bytes(M) + 2 * N * K + (2 if c16 else 4) * M * N
         elif gat is not None:               # G [M, N] and the gathered rows in, the gradient out

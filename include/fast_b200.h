@@ -408,6 +408,13 @@ typedef struct fb_gemm_bf16_problem {
   const fb_bf16_row_gather *gather;   /* NT (no A2): A's rows, A unused; TN with
                     nseg > 0: X's rows, B unused; K = the last segment's end.
                     NULL: the operand is the matrix */
+  const float *add;                   /* NT / NN, or NULL: C[m, n] (+)= ... +
+                    add[add_idx[m] * ld_add + n] (an fp32 table of add_rows rows,
+                    ld_add >= N; indices clamped into it), added before the bf16
+                    rounding -- a product whose input rows repeat a few distinct
+                    rows, computed once per row in the table */
+  const int32_t *add_idx;
+  int64_t ld_add, add_rows;
 } fb_gemm_bf16_problem;
 size_t fb_gemm_bf16_group_ws_bytes(const fb_gemm_bf16_problem *probs, int n);
 int fb_gemm_bf16_group(const fb_gemm_bf16_problem *probs, int n, void *ws, size_t ws_bytes, cudaStream_t stream);

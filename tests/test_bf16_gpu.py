@@ -106,6 +106,38 @@ def test_gemm_bf16_nn_on_weight_columns(cuda):
         _check(C, G.double(), B.double(), K, "NN cols %d" % c0)
 
 
+@pytest.mark.parametrize("c16", [True, False])
+def test_gemm_bf16_nt_epilogue_adds_table_rows(cuda, c16):
+    """NT with an fp32 table added per output row (C[m] += add[add_idx[m]]):
+    the node-feature block of layer 0's K|V product, computed once per table
+    row.  Equal to the product plus the gathered rows within the fp32
+    accumulation bound (then one bf16 rounding for a bf16 C); rows past the
+    device-side count carry out-of-range indices and stay untouched."""
+    from fast_b200 import ops
+    g = torch.Generator(device="cpu").manual_seed(12)
+    M, m_dev, N, K, rows = 5000, 4700, 200, 292, 777
+    X = _bf(torch.randn(M, 296, generator=g)).to(cuda)[:, :K]
+    W = _bf(torch.randn(N, 296, generator=g) * 0.05).to(cuda)[:, :K]
+    P = torch.randn(rows, N, generator=g).to(cuda)
+    idx = torch.randint(0, rows, (M,), generator=g, dtype=torch.int32)
+    idx[m_dev:] = 10 ** 7
+    idx = idx.to(cuda)
+    bias = torch.randn(N, generator=g).to(cuda)
+    n_dev = torch.tensor([m_dev], dtype=torch.int32, device=cuda)
+    C = torch.full((M, N), 7.0, device=cuda, dtype=torch.bfloat16 if c16 else torch.float32)
+    ops.gemm_bf16_group([dict(kind=ops.NT, A=X, B=W, bias=bias, out=C, M_dev=n_dev, add=P, add_idx=idx)])
+    torch.cuda.synchronize()
+    base = bias.double() + P[idx[:m_dev].long()].double()
+    if c16:
+        ref = (X[:m_dev].double() @ W.double().T + base).float().to(torch.bfloat16).float()
+        err = (C[:m_dev].float() - ref).abs()
+        # one bf16 step at most (the fp32 sum may round to the neighbouring bf16 value)
+        assert bool((err <= 2.0 ** -7 * ref.abs() + 1e-30).all())
+    else:
+        _check(C[:m_dev], X[:m_dev].double(), W.double().T, K, "NT + rows", base=base)
+    assert bool((C[m_dev:].float() == 7.0).all())
+
+
 @pytest.mark.parametrize("M,m_dev,dn", [(3000, 2777, 413), (70001, 70001, 413), (20000, 1, 413), (5000, 4321, 0)])
 def test_gemm_bf16_gathered_rows(cuda, M, m_dev, dn):
     """The projection rows [h | f | t] gathered inside the GEMM (ops.RowGather:
