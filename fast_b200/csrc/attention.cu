@@ -1033,6 +1033,275 @@ __global__ void __launch_bounds__(32 * kBulkWarps) k_attn_bwd_b(AttnArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Bulk-copy kernels with lane-per-(edge, head) dot products, for 1 or 2
+// heads: lane l holds edge l / HP of the group and head l % HP, and takes the
+// dot product over that head's dh features only (the other kernels give every
+// lane all heads over all features, with queries masked per head), so a group
+// of up to 12 edges keeps 12 * HP lanes busy instead of 12.  Softmax
+// statistics are reductions over the lanes of one head; the row outputs stay
+// lane-per-feature, each taking its edge's weight from lane c * HP + head.
+
+// sum over t < dh/2 of q[2t] row[2t] + q[2t+1] row[2t+1]: the row is slot row i
+// from element f0 (fp32, or bf16 widened), q a float array in shared memory.
+template <bool BF>
+__device__ __forceinline__ float head_dot(const unsigned char *slot, int i, int rowf, int f0, const float *q, int dh) {
+  float acc = 0.f;
+  if (BF) {
+    const uint32_t *r = reinterpret_cast<const uint32_t *>(slot + ((size_t)i * rowf + f0) * 2);
+    const float2 *q2 = reinterpret_cast<const float2 *>(q);
+#pragma unroll 5
+    for (int t = 0; t < dh / 2; ++t) {
+      const uint32_t u = r[t];
+      const float2 qq = q2[t];
+      acc = fmaf(qq.x, __uint_as_float(u << 16), fmaf(qq.y, __uint_as_float(u & 0xFFFF0000u), acc));
+    }
+  } else {
+    const float2 *r = reinterpret_cast<const float2 *>(slot + ((size_t)i * rowf + f0) * 4);
+    const float2 *q2 = reinterpret_cast<const float2 *>(q);
+#pragma unroll 5
+    for (int t = 0; t < dh / 2; ++t) {
+      const float2 k = r[t];
+      const float2 qq = q2[t];
+      acc = fmaf(qq.x, k.x, fmaf(qq.y, k.y, acc));
+    }
+  }
+  return acc;
+}
+
+// Reductions over the lanes of one head (lanes l, l + HP, l + 2 HP, ...).
+template <int HP>
+__device__ __forceinline__ float head_max(float v) {
+#pragma unroll
+  for (int o = HP; o < 32; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+template <int HP>
+__device__ __forceinline__ float head_sum(float v) {
+#pragma unroll
+  for (int o = HP; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Dropout keep scale of (edge e, head h): drop_scale()'s decision.
+__device__ __forceinline__ float keep1(const AttnArgs &a, uint64_t doff, int64_t e, int h, float inv_keep) {
+  if (a.drop_p <= 0.f) return 1.f;
+  if (a.mask_u) return a.mask_u[e * a.heads + h] > a.drop_p ? inv_keep : 0.f;
+  const fb::Philox4 r = fb::philox4x32_10((uint32_t)e, (uint32_t)(e >> 32), (uint32_t)doff, (uint32_t)(doff >> 32),
+                                          (uint32_t)a.seed, (uint32_t)(a.seed >> 32));
+  const uint32_t w = h == 0 ? r.v[0] : (h == 1 ? r.v[1] : (h == 2 ? r.v[2] : r.v[3]));
+  return ((float)(w >> 8) * (1.0f / 16777216.0f) >= a.drop_p) ? inv_keep : 0.f;
+}
+
+// Stages one row of dim floats into a warp's shared-memory array.
+__device__ __forceinline__ void stage_row(float *dst, const float *x, int nq, int lane) {
+  if (lane < nq) reinterpret_cast<float4 *>(dst)[lane] = __ldg(reinterpret_cast<const float4 *>(x) + lane);
+}
+
+template <int HP, bool BF>
+__global__ void __launch_bounds__(32 * kBulkWarps) k_attn_fwd_h(AttnArgs a) {
+  static_assert(HP == 1 || HP == 2, "lane-per-(edge, head) kernels take 1 or 2 heads");
+  fb::pdl_enter();
+  extern __shared__ __align__(128) unsigned char smraw[];
+  __shared__ uint64_t bar[kBulkWarps];
+  constexpr int kEsz = BF ? 2 : 4;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int rowf = (int)a.ldkv;
+  unsigned char *slot = smraw + (size_t)w * kBulkGroup * rowf * kEsz;
+  const unsigned char *kbase = reinterpret_cast<const unsigned char *>(a.k);
+  float *qs = reinterpret_cast<float *>(smraw + (size_t)kBulkWarps * kBulkGroup * rowf * kEsz) + (size_t)w * 128;
+  const int64_t n_dst = a.n_dst_dev ? min((int64_t)(*a.n_dst_dev), a.n_dst) : a.n_dst;
+  const int nq = a.dim / 4, dh = a.dim / a.heads;
+  const bool live = lane < nq;
+  const int hA = live ? (4 * lane) / dh : 0, hB = live ? (4 * lane + 2) / dh : 0;
+  const int li = lane / HP, lh = lane % HP;
+  const uint64_t doff = a.offset_dev ? *a.offset_dev : a.offset;
+  const float inv_keep = a.drop_p > 0.f ? 1.f / (1.f - a.drop_p) : 1.f;
+  const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (lane == 0) bar_init(&bar[w]);
+  __syncwarp();
+  uint32_t phase = 0;
+  if (a.n_dst_dev) {
+    for (int64_t j = n_dst + (int64_t)blockIdx.x * kBulkWarps + w; j < a.n_dst;
+         j += (int64_t)gridDim.x * kBulkWarps)
+      if (live) put4(a.agg, j * a.ldagg + 4 * lane, zero4, a.agg_bf16);
+  }
+  for (int64_t j = (int64_t)blockIdx.x * kBulkWarps + w; j < n_dst; j += (int64_t)gridDim.x * kBulkWarps) {
+    const int beg = a.rptr[j], end = a.rptr[j + 1];
+    float4 acc = zero4;
+    if (end > beg) {
+      slot_release();
+      stage_row(qs, a.q + j * a.ldq, nq, lane);
+      const bool one = end - beg <= kBulkGroup;
+      float m = -FLT_MAX, ssum = 0.f, ex = 0.f;       // this lane's head
+      for (int g0 = beg; g0 < end; g0 += kBulkGroup) {
+        const int n = min(kBulkGroup, end - g0);
+        slot_release();
+        if (lane == 0) bulk_copy(slot, kbase + (int64_t)g0 * a.ldkv * kEsz, (uint32_t)(n * rowf * kEsz), &bar[w]);
+        const bool ok = bulk_wait(&bar[w], phase);
+        phase ^= 1u;
+        if (!ok) return;
+        __syncwarp();
+        const bool vl = li < n && lh < a.heads;
+        const int64_t e = g0 + li;
+        const float z = vl ? head_dot<BF>(slot, li, rowf, lh * dh, qs + lh * dh, dh) : 0.f;
+        const float kp = vl ? keep1(a, doff, e, lh, inv_keep) : 0.f;
+        const float zz = vl ? leaky(z, a.slope) : -FLT_MAX;
+        if (!one && vl) a.att_out[e * a.heads + lh] = zz;          // raw; normalised below
+        const float mn = fmaxf(m, head_max<HP>(zz));
+        const float sc = (m == -FLT_MAX) ? 0.f : expf(m - mn);
+        m = mn;
+        ex = vl ? expf(zz - mn) : 0.f;
+        ssum = ssum * sc + head_sum<HP>(ex);
+        const float wt = ex * kp;
+        const float sa = __shfl_sync(0xffffffffu, sc, hA), sb = __shfl_sync(0xffffffffu, sc, hB);
+        acc.x *= sa; acc.y *= sa; acc.z *= sb; acc.w *= sb;
+#pragma unroll 4
+        for (int c = 0; c < n; ++c) {
+          const float wa = __shfl_sync(0xffffffffu, wt, c * HP + hA);
+          const float wb = __shfl_sync(0xffffffffu, wt, c * HP + hB);
+          const float4 v = live ? slot4<BF>(slot, c, rowf, (a.dim >> 2) + lane) : zero4;
+          acc.x = fmaf(wa, v.x, acc.x);
+          acc.y = fmaf(wa, v.y, acc.y);
+          acc.z = fmaf(wb, v.z, acc.z);
+          acc.w = fmaf(wb, v.w, acc.w);
+        }
+      }
+      const float inv = 1.f / ssum;                   // lanes of a live head
+      const float ia = __shfl_sync(0xffffffffu, inv, hA), ib = __shfl_sync(0xffffffffu, inv, hB);
+      acc.x *= ia; acc.y *= ia; acc.z *= ib; acc.w *= ib;
+      if (one) {
+        if (li < end - beg && lh < a.heads) a.att_out[(int64_t)(beg + li) * a.heads + lh] = ex * inv;
+      } else {
+        float mh[HP], ih[HP];
+#pragma unroll
+        for (int h = 0; h < HP; ++h) {
+          mh[h] = __shfl_sync(0xffffffffu, m, h);
+          ih[h] = __shfl_sync(0xffffffffu, inv, h);
+        }
+        __syncwarp();
+        for (int t = lane; t < (end - beg) * a.heads; t += 32) {
+          const int h = t % a.heads;
+          float *pz = a.att_out + (int64_t)beg * a.heads + t;
+          *pz = expf(*pz - hv<HP>(mh, h)) * hv<HP>(ih, h);
+        }
+      }
+    }
+    if (live) put4(a.agg, j * a.ldagg + 4 * lane, acc, a.agg_bf16);
+  }
+}
+
+template <int HP, bool BF>
+__global__ void __launch_bounds__(32 * kBulkWarps) k_attn_bwd_h(AttnArgs a) {
+  static_assert(HP == 1 || HP == 2, "lane-per-(edge, head) kernels take 1 or 2 heads");
+  fb::pdl_enter();
+  extern __shared__ __align__(128) unsigned char smraw[];
+  __shared__ uint64_t bar[kBulkWarps];
+  constexpr int kEsz = BF ? 2 : 4;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int rowf = (int)a.ldkv;
+  unsigned char *slot = smraw + (size_t)w * kBulkGroup * rowf * kEsz;
+  const unsigned char *kbase = reinterpret_cast<const unsigned char *>(a.k);
+  float *qs = reinterpret_cast<float *>(smraw + (size_t)kBulkWarps * kBulkGroup * rowf * kEsz) + (size_t)w * 256;
+  float *ds = qs + 128;
+  const int64_t n_dst = a.n_dst_dev ? min((int64_t)(*a.n_dst_dev), a.n_dst) : a.n_dst;
+  const int nq = a.dim / 4, dh = a.dim / a.heads;
+  const bool live = lane < nq;
+  const int hA = live ? (4 * lane) / dh : 0, hB = live ? (4 * lane + 2) / dh : 0;
+  const int li = lane / HP, lh = lane % HP;
+  const uint64_t doff = a.offset_dev ? *a.offset_dev : a.offset;
+  const float inv_keep = a.drop_p > 0.f ? 1.f / (1.f - a.drop_p) : 1.f;
+  const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (lane == 0) bar_init(&bar[w]);
+  __syncwarp();
+  uint32_t phase = 0;
+  for (int64_t j = (int64_t)blockIdx.x * kBulkWarps + w; j < n_dst; j += (int64_t)gridDim.x * kBulkWarps) {
+    const int beg = a.rptr[j], end = a.rptr[j + 1];
+    float4 dq = zero4;
+    if (end > beg) {
+      slot_release();
+      stage_row(qs, a.q + j * a.ldq, nq, lane);
+      stage_row(ds, a.dagg + j * a.lddagg, nq, lane);
+      const float4 q4 = live ? __ldg(reinterpret_cast<const float4 *>(a.q + j * a.ldq) + lane) : zero4;
+      const float4 da4 = live ? __ldg(reinterpret_cast<const float4 *>(a.dagg + j * a.lddagg) + lane) : zero4;
+      const bool one = end - beg <= kBulkGroup;
+      // pass 1 (lane per edge and head): dL/dy through dropout from the V rows,
+      // sum_e y dL/dy of the lane's head; dV rows lane-per-feature
+      float sd = 0.f, dl1 = 0.f, y1 = 0.f;
+      for (int g0 = beg; g0 < end; g0 += kBulkGroup) {
+        const int n = min(kBulkGroup, end - g0);
+        slot_release();
+        if (lane == 0) bulk_copy(slot, kbase + (int64_t)g0 * a.ldkv * kEsz, (uint32_t)(n * rowf * kEsz), &bar[w]);
+        const bool ok = bulk_wait(&bar[w], phase);
+        phase ^= 1u;
+        if (!ok) return;
+        __syncwarp();
+        const bool vl = li < n && lh < a.heads;
+        const int64_t e = g0 + li;
+        const float d = vl ? head_dot<BF>(slot, li, rowf, a.dim + lh * dh, ds + lh * dh, dh) : 0.f;
+        const float kp = vl ? keep1(a, doff, e, lh, inv_keep) : 0.f;
+        const float y = vl ? __ldg(a.att + e * a.heads + lh) : 0.f;
+        const float dl = d * kp;
+        sd += head_sum<HP>(y * dl);
+        dl1 = dl;
+        y1 = y;
+        const float yk = y * kp;
+        if (a.dv) {
+#pragma unroll 4
+          for (int c = 0; c < n; ++c) {
+            const float ya = __shfl_sync(0xffffffffu, yk, c * HP + hA);
+            const float yb = __shfl_sync(0xffffffffu, yk, c * HP + hB);
+            if (live)
+              put4(a.dv, (int64_t)(g0 + c) * a.lddkv + 4 * lane,
+                   make_float4(ya * da4.x, ya * da4.y, yb * da4.z, yb * da4.w), a.kv_bf16);
+          }
+        }
+      }
+      // pass 2: the logits again from the K rows, LeakyReLU and softmax
+      // backward per (edge, head), dK rows and dq lane-per-feature; a single
+      // group is still in the slot
+      for (int g0 = beg; g0 < end; g0 += kBulkGroup) {
+        const int n = min(kBulkGroup, end - g0);
+        if (!one) {
+          slot_release();
+          if (lane == 0) bulk_copy(slot, kbase + (int64_t)g0 * a.ldkv * kEsz, (uint32_t)(n * rowf * kEsz), &bar[w]);
+          const bool ok = bulk_wait(&bar[w], phase);
+          phase ^= 1u;
+          if (!ok) return;
+          __syncwarp();
+        }
+        const bool vl = li < n && lh < a.heads;
+        const int64_t e = g0 + li;
+        const float z = vl ? head_dot<BF>(slot, li, rowf, lh * dh, qs + lh * dh, dh) : 0.f;
+        float dl = dl1, y = y1;
+        if (!one) {
+          const float d = vl ? head_dot<BF>(slot, li, rowf, a.dim + lh * dh, ds + lh * dh, dh) : 0.f;
+          dl = d * (vl ? keep1(a, doff, e, lh, inv_keep) : 0.f);
+          y = vl ? __ldg(a.att + e * a.heads + lh) : 0.f;
+        }
+        const float g = y * (dl - sd);
+        const float dz = vl ? (z > 0.f ? g : g * a.slope) : 0.f;
+#pragma unroll 4
+        for (int c = 0; c < n; ++c) {
+          const float za = __shfl_sync(0xffffffffu, dz, c * HP + hA);
+          const float zb = __shfl_sync(0xffffffffu, dz, c * HP + hB);
+          if (live) {
+            const float4 k = slot4<BF>(slot, c, rowf, lane);
+            if (a.dk)
+              put4(a.dk, (int64_t)(g0 + c) * a.lddkv + 4 * lane,
+                   make_float4(za * q4.x, za * q4.y, zb * q4.z, zb * q4.w), a.kv_bf16);
+            dq.x = fmaf(za, k.x, dq.x);
+            dq.y = fmaf(za, k.y, dq.y);
+            dq.z = fmaf(zb, k.z, dq.z);
+            dq.w = fmaf(zb, k.w, dq.w);
+          }
+        }
+      }
+    }
+    if (a.dq && live) put4(a.dq, j * (a.dq_bf16 ? a.lddq : (int64_t)a.dim) + 4 * lane, dq, a.dq_bf16);
+  }
+}
+
 int attn_grid(int64_t n_dst) {
   static int sms_of[64] = {0};
   int dev = 0;
@@ -1090,7 +1359,10 @@ bool bulk_path(const AttnArgs &a) {
 
 size_t bulk_smem(const AttnArgs &a, int hp, bool bwd) {
   const size_t esz = a.kv_in_bf16 ? 2 : 4;
-  return (size_t)kBulkWarps * ((size_t)kBulkGroup * a.ldkv * esz + (bwd ? 2 : 1) * (size_t)hp * 32 * 16);
+  // the masked-query kernels stage hp rows of 32 float4 per staged vector;
+  // the lane-per-(edge, head) kernels (hp <= 2) one row of 128 floats
+  const size_t per = hp <= 2 ? 128 * 4 : (size_t)hp * 32 * 16;
+  return (size_t)kBulkWarps * ((size_t)kBulkGroup * a.ldkv * esz + (bwd ? 2 : 1) * per);
 }
 
 int bulk_grid(int64_t n_dst) {
@@ -1100,10 +1372,10 @@ int bulk_grid(int64_t n_dst) {
 // Opts a kernel into `bytes` of dynamic shared memory once per device.
 template <typename K>
 int allow_smem(K kernel, size_t bytes, int slot) {
-  static size_t done[12][64] = {};
+  static size_t done[24][64] = {};
   int dev = 0;
   FB_TRY_CUDA(cudaGetDevice(&dev));
-  size_t &d = done[slot % 12][dev & 63];
+  size_t &d = done[slot % 24][dev & 63];
   if (d < bytes) {
     FB_TRY_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
     d = bytes;
@@ -1117,13 +1389,31 @@ int launch_bulk_t(const AttnArgs &a, bool bwd, cudaStream_t stream) {
   const int grid = bulk_grid(a.n_dst);
   const int slot = (HP == 1 ? 0 : (HP == 2 ? 1 : 2)) + (bwd ? 3 : 0) + (BF ? 6 : 0);
   int rc;
+  if constexpr (HP <= 2) {
+    // lane-per-(edge, head) dot products (FB_MASKED_ATTN selects the masked-query kernels)
+    static const bool masked = getenv("FB_MASKED_ATTN") != nullptr;
+    if (!masked) {
+      if (bwd) {
+        if ((rc = allow_smem(k_attn_bwd_h<HP, BF>, sm, slot))) return rc;
+        FB_TRY_CUDA(fb::launch(k_attn_bwd_h<HP, BF>, grid, 32 * kBulkWarps, sm, stream, a));
+        FB_LAUNCHED("k_attn_bwd_h");
+      } else {
+        if ((rc = allow_smem(k_attn_fwd_h<HP, BF>, sm, slot))) return rc;
+        FB_TRY_CUDA(fb::launch(k_attn_fwd_h<HP, BF>, grid, 32 * kBulkWarps, sm, stream, a));
+        FB_LAUNCHED("k_attn_fwd_h");
+      }
+      return FB_OK;
+    }
+  }
+  const size_t smm = (size_t)kBulkWarps * ((size_t)kBulkGroup * a.ldkv * (BF ? 2 : 4) + (bwd ? 2 : 1) *
+                                           (size_t)HP * 32 * 16);
   if (bwd) {
-    if ((rc = allow_smem(k_attn_bwd_b<HP, BF>, sm, slot))) return rc;
-    FB_TRY_CUDA(fb::launch(k_attn_bwd_b<HP, BF>, grid, 32 * kBulkWarps, sm, stream, a));
+    if ((rc = allow_smem(k_attn_bwd_b<HP, BF>, smm, slot + 12))) return rc;
+    FB_TRY_CUDA(fb::launch(k_attn_bwd_b<HP, BF>, grid, 32 * kBulkWarps, smm, stream, a));
     FB_LAUNCHED("k_attn_bwd_b");
   } else {
-    if ((rc = allow_smem(k_attn_fwd_b<HP, BF>, sm, slot))) return rc;
-    FB_TRY_CUDA(fb::launch(k_attn_fwd_b<HP, BF>, grid, 32 * kBulkWarps, sm, stream, a));
+    if ((rc = allow_smem(k_attn_fwd_b<HP, BF>, smm, slot + 12))) return rc;
+    FB_TRY_CUDA(fb::launch(k_attn_fwd_b<HP, BF>, grid, 32 * kBulkWarps, smm, stream, a));
     FB_LAUNCHED("k_attn_fwd_b");
   }
   return FB_OK;

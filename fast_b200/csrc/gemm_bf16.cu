@@ -461,6 +461,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
       const int add_rows = q.add_rows;
       const int64_t row0 = it.r0 + qd * 32;
       const int nrows = rows - row0 < 32 ? (int)max(rows - row0, (int64_t)0) : 32;
+      // add table: lane r holds the (clamped) table row of output row row0 + r
+      const int add_row = (add && lane < nrows) ? min(max(__ldg(add_idx + row0 + lane), 0), add_rows - 1) : 0;
 #pragma unroll 1
       for (int c0 = 32 * half; c0 < bn; c0 += 64) {
         uint32_t r[32];
@@ -470,20 +472,33 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
         for (int k = 0; k < 32; ++k) stg[lane * kStagePitch + k] = __uint_as_float(r[k]);
         __syncwarp();
         const int col = it.c0 + c0 + lane;
-        if (add && c0 + lane < bn && col < ncols) {
-          // + a row of the add table per output row (NT / NN)
-          const float bv = bias ? bias[col] : 0.f;
+        if (add) {
+          // + a row of the add table per output row (NT / NN): the 32 rows'
+          // indices were loaded once per block (lane r holds row r's), and eight
+          // rows' table loads are in flight at a time
+          const bool on = c0 + lane < bn && col < ncols;
+          const float bv = (bias && on) ? bias[col] : 0.f;
           const float *sv = stg + lane;
-          const float *pa = add + col;
-          for (int rr = 0; rr < nrows; ++rr) {
-            const int ix = min(max(__ldg(add_idx + row0 + rr), 0), add_rows - 1);
-            const float v = sv[rr * kStagePitch] + bv + __ldg(pa + (int64_t)ix * ld_add);
-            if (c16) {
-              const __nv_bfloat16 hv = __float2bfloat16_rn(v);
-              reinterpret_cast<uint16_t *>(out)[(row0 + rr) * ld + col] = *reinterpret_cast<const uint16_t *>(&hv);
-            } else {
-              float *o = out + (row0 + rr) * ld + col;
-              *o = accum ? *o + v : v;
+          const float *pa = add + (on ? col : 0);
+          for (int r8 = 0; r8 < nrows; r8 += 8) {
+            float pv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int ix = __shfl_sync(0xffffffffu, add_row, (r8 + u) & 31);
+              pv[u] = (on && r8 + u < nrows) ? __ldg(pa + (int64_t)ix * ld_add) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int rr = r8 + u;
+              if (!on || rr >= nrows) continue;
+              const float v = sv[rr * kStagePitch] + bv + pv[u];
+              if (c16) {
+                const __nv_bfloat16 hv = __float2bfloat16_rn(v);
+                reinterpret_cast<uint16_t *>(out)[(row0 + rr) * ld + col] = *reinterpret_cast<const uint16_t *>(&hv);
+              } else {
+                float *o = out + (row0 + rr) * ld + col;
+                *o = accum ? *o + v : v;
+              }
             }
           }
         } else if (c16 && c0 + lane < bn && col < ncols) {

@@ -186,7 +186,7 @@ class FusedStep:
         next layer's backward).  `uses`: tensors allocated on the current
         stream that fn reads.  The current stream joins the side stream at the
         end of the step (_join); with FB_SIDE_STREAMS=0, fn runs inline."""
-        if not SIDE_STREAMS:
+        if not SIDE_STREAMS or ops.TIMER is not None:     # the per-kernel timer measures kernels alone
             fn()
             return
         cur = torch.cuda.current_stream()

@@ -129,10 +129,15 @@ def test_gemm_bf16_nt_epilogue_adds_table_rows(cuda, c16):
     torch.cuda.synchronize()
     base = bias.double() + P[idx[:m_dev].long()].double()
     if c16:
-        ref = (X[:m_dev].double() @ W.double().T + base).float().to(torch.bfloat16).float()
-        err = (C[:m_dev].float() - ref).abs()
-        # one bf16 step at most (the fp32 sum may round to the neighbouring bf16 value)
-        assert bool((err <= 2.0 ** -7 * ref.abs() + 1e-30).all())
+        a64, w64 = X[:m_dev].double(), W.double().T
+        exact = a64 @ w64 + base
+        # the fp32 accumulation bound, then one bf16 rounding of a value that fp32
+        # may have moved across a rounding boundary
+        acc = K * 2.0 ** -23 * (a64.abs() @ w64.abs()) + 2.0 ** -22 * (bias.double().abs() +
+                                                                      P[idx[:m_dev].long()].double().abs() +
+                                                                      exact.abs())
+        err = (C[:m_dev].double() - exact).abs()
+        assert bool((err <= acc + 2.0 ** -7 * (exact.abs() + acc)).all())
     else:
         _check(C[:m_dev], X[:m_dev].double(), W.double().T, K, "NT + rows", base=base)
     assert bool((C[m_dev:].float() == 7.0).all())
