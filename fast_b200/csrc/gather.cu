@@ -440,6 +440,85 @@ __global__ void __launch_bounds__(1024) k_te_bwd_rows(const T *__restrict__ g, i
   }
 }
 
+// Stage 1 for even dtime <= 512 with pair-aligned rows: as k_te_bwd_rows, but
+// thread t owns the column pair (2 (t % (dtime/2)), +1) -- one 4- or 8-byte
+// load of g and one load of dt per two elements -- and the row groups' sums
+// are combined in the same fixed order.
+__device__ __forceinline__ float2 te_g2(const float *p) { return __ldg(reinterpret_cast<const float2 *>(p)); }
+__device__ __forceinline__ float2 te_g2(const uint16_t *p) {
+  const uint32_t u = __ldg(reinterpret_cast<const uint32_t *>(p));
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(512) k_te_bwd_pairs(const T *__restrict__ g, int64_t ldg,
+                                                      const float *__restrict__ dt, const float *__restrict__ w,
+                                                      const float *__restrict__ b, int dtime, int groups,
+                                                      int64_t n_rows, const int32_t *n_rows_dev,
+                                                      float *__restrict__ part) {
+  fb::pdl_enter();
+  __shared__ float sw_s[kTeGroups * kTeColsMax], sb_s[kTeGroups * kTeColsMax];
+  const int64_t n = n_rows_dev ? min((int64_t)(*n_rows_dev), n_rows) : n_rows;
+  const int parts = fb::split_parts(n, kTeRowsPerCta, kTeMaxParts);
+  if ((int)blockIdx.y >= parts) return;
+  const int half = dtime >> 1;
+  const int c = 2 * (threadIdx.x % half), grp = threadIdx.x / half;
+  const bool live = grp < groups;
+  const int64_t per = (n + parts - 1) / parts;
+  const int64_t r0 = (int64_t)blockIdx.y * per;
+  const int64_t r1 = min(n, r0 + per);
+  float sw0 = 0.f, sb0 = 0.f, sw1 = 0.f, sb1 = 0.f;
+  if (live) {
+    const float w0 = __ldg(w + c), b0 = __ldg(b + c), w1 = __ldg(w + c + 1), b1 = __ldg(b + c + 1);
+    const int G = groups;
+    const T *gp = g + (r0 + grp) * ldg + c;
+    const int64_t gstep = (int64_t)G * ldg;
+    int64_t r = r0 + grp;
+    for (; r + 7 * G < r1; r += 8 * G, gp += 8 * gstep) {
+      float tv[8];
+      float2 gv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        tv[u] = __ldg(dt + r + u * G);
+        gv[u] = te_g2(gp + u * gstep);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float g0 = -sin_big(fmaf(tv[u], w0, b0)) * gv[u].x;
+        const float g1 = -sin_big(fmaf(tv[u], w1, b1)) * gv[u].y;
+        sw0 = fmaf(g0, tv[u], sw0);
+        sb0 += g0;
+        sw1 = fmaf(g1, tv[u], sw1);
+        sb1 += g1;
+      }
+    }
+    for (; r < r1; r += G, gp += gstep) {
+      const float t = __ldg(dt + r);
+      const float2 gg = te_g2(gp);
+      const float g0 = -sin_big(fmaf(t, w0, b0)) * gg.x;
+      const float g1 = -sin_big(fmaf(t, w1, b1)) * gg.y;
+      sw0 = fmaf(g0, t, sw0);
+      sb0 += g0;
+      sw1 = fmaf(g1, t, sw1);
+      sb1 += g1;
+    }
+    sw_s[grp * dtime + c] = sw0;
+    sb_s[grp * dtime + c] = sb0;
+    sw_s[grp * dtime + c + 1] = sw1;
+    sb_s[grp * dtime + c + 1] = sb1;
+  }
+  __syncthreads();
+  if (grp == 0) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      float aw = 0.f, ab = 0.f;
+      for (int i = 0; i < groups; ++i) { aw += sw_s[i * dtime + c + k]; ab += sb_s[i * dtime + c + k]; }
+      part[((int64_t)blockIdx.y * 2 + 0) * dtime + c + k] = aw;
+      part[((int64_t)blockIdx.y * 2 + 1) * dtime + c + k] = ab;
+    }
+  }
+}
+
 // Stage 2: one warp per column sums the partials, lanes striding over them,
 // then a fixed shuffle tree (deterministic).
 __global__ void k_te_bwd_reduce(const float *__restrict__ part, int64_t n_rows, const int32_t *n_rows_dev, int dtime,
@@ -544,7 +623,18 @@ int te_bwd(const T *g, int64_t ldg, const float *dt, const float *w, const float
   // take the partition from the true count
   const int parts = te_parts(n_rows);
   float *part = static_cast<float *>(ws);
-  if (dtime <= kTeColsMax) {
+  static const bool no_pairs = getenv("FB_TE_BWD_SINGLE") != nullptr;
+  const size_t pair_bytes = sizeof(T) * 2;
+  if (!no_pairs && dtime % 2 == 0 && dtime <= kTeColsMax && ldg % 2 == 0 &&
+      (reinterpret_cast<uintptr_t>(g) % pair_bytes) == 0) {
+    // groups of dtime / 2 threads (a column pair each): as many as fit 512 threads, at most kTeGroups
+    const int half = dtime / 2;
+    const int groups = std::max(1, std::min(kTeGroups, 512 / half));
+    const int threads = (groups * half + 31) / 32 * 32;
+    FB_TRY_CUDA(fb::launch(k_te_bwd_pairs<T>, dim3(1, parts), threads, 0, stream, g, ldg, dt, w, b, dtime, groups,
+                           n_rows, n_rows_dev, part));
+    FB_LAUNCHED("k_te_bwd_pairs");
+  } else if (dtime <= kTeColsMax) {
     // groups of dtime threads: as many as fit 1024 threads, at most kTeGroups
     const int groups = std::max(1, std::min(kTeGroups, 1024 / dtime));
     const int threads = (groups * dtime + 31) / 32 * 32;
