@@ -672,14 +672,17 @@ def run_kernel_suite(args):
             fn()
         torch.cuda.synchronize()
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clock = clock_sampler(0)
+        clock.start()
         s0.record()
         for _ in range(10):
             fn()
         s1.record()
         torch.cuda.synchronize()
+        clocks = clock.stop()
         us = s0.elapsed_time(s1) * 100.0          # per launch, microseconds
         line = {"suite": "kernels", "kernel": name, "shape": shape, "us_per_launch": round(us, 2),
-                "bytes_per_launch": int(nbytes)}
+                "bytes_per_launch": int(nbytes), "clocks": clocks}
         if flops:
             tfs = flops / us / 1e6
             if args.gemm == "tc":
@@ -776,14 +779,17 @@ def run_bf16_suite(args):
             fn()
         torch.cuda.synchronize()
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clock = clock_sampler(0)
+        clock.start()
         s0.record()
         for _ in range(10):
             fn()
         s1.record()
         torch.cuda.synchronize()
+        clocks = clock.stop()
         us = s0.elapsed_time(s1) * 100.0
         line = {"suite": "bf16", "kernel": name, "shape": shape, "us_per_launch": round(us, 2),
-                "bytes_per_launch": int(nbytes)}
+                "bytes_per_launch": int(nbytes), "clocks": clocks}
         gbs = nbytes / us / 1e3
         line.update({"achieved_GB_s": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm"], 3)})
         if flops:

@@ -461,47 +461,38 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
       const int add_rows = q.add_rows;
       const int64_t row0 = it.r0 + qd * 32;
       const int nrows = rows - row0 < 32 ? (int)max(rows - row0, (int64_t)0) : 32;
-      // add table: lane r holds the (clamped) table row of output row row0 + r
+      // add table: lane r adds the (clamped) table row of output row row0 + r
       const int add_row = (add && lane < nrows) ? min(max(__ldg(add_idx + row0 + lane), 0), add_rows - 1) : 0;
 #pragma unroll 1
       for (int c0 = 32 * half; c0 < bn; c0 += 64) {
         uint32_t r[32];
         tmem_ld32(t + c0, r);
+        if (add && lane < nrows) {
+          // + this lane's row of the add table (the lane holds one output row's
+          // 32 columns here), read as 16-byte words
+          const int cb = it.c0 + c0;
+          const float *src = add + (int64_t)add_row * ld_add + cb;
+          if (cb + 32 <= ncols) {
+#pragma unroll
+            for (int k4 = 0; k4 < 8; ++k4) {
+              const float4 v = __ldg(reinterpret_cast<const float4 *>(src) + k4);
+              r[4 * k4 + 0] = __float_as_uint(__uint_as_float(r[4 * k4 + 0]) + v.x);
+              r[4 * k4 + 1] = __float_as_uint(__uint_as_float(r[4 * k4 + 1]) + v.y);
+              r[4 * k4 + 2] = __float_as_uint(__uint_as_float(r[4 * k4 + 2]) + v.z);
+              r[4 * k4 + 3] = __float_as_uint(__uint_as_float(r[4 * k4 + 3]) + v.w);
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < 32; ++k)
+              if (cb + k < ncols) r[k] = __float_as_uint(__uint_as_float(r[k]) + __ldg(src + k));
+          }
+        }
         __syncwarp();
 #pragma unroll
         for (int k = 0; k < 32; ++k) stg[lane * kStagePitch + k] = __uint_as_float(r[k]);
         __syncwarp();
         const int col = it.c0 + c0 + lane;
-        if (add) {
-          // + a row of the add table per output row (NT / NN): the 32 rows'
-          // indices were loaded once per block (lane r holds row r's), and eight
-          // rows' table loads are in flight at a time
-          const bool on = c0 + lane < bn && col < ncols;
-          const float bv = (bias && on) ? bias[col] : 0.f;
-          const float *sv = stg + lane;
-          const float *pa = add + (on ? col : 0);
-          for (int r8 = 0; r8 < nrows; r8 += 8) {
-            float pv[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int ix = __shfl_sync(0xffffffffu, add_row, (r8 + u) & 31);
-              pv[u] = (on && r8 + u < nrows) ? __ldg(pa + (int64_t)ix * ld_add) : 0.f;
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int rr = r8 + u;
-              if (!on || rr >= nrows) continue;
-              const float v = sv[rr * kStagePitch] + bv + pv[u];
-              if (c16) {
-                const __nv_bfloat16 hv = __float2bfloat16_rn(v);
-                reinterpret_cast<uint16_t *>(out)[(row0 + rr) * ld + col] = *reinterpret_cast<const uint16_t *>(&hv);
-              } else {
-                float *o = out + (row0 + rr) * ld + col;
-                *o = accum ? *o + v : v;
-              }
-            }
-          }
-        } else if (c16 && c0 + lane < bn && col < ncols) {
+        if (c16 && c0 + lane < bn && col < ncols) {
           const float bv = bias ? bias[col] : 0.f;
           uint16_t *o = reinterpret_cast<uint16_t *>(out) + row0 * ld + col;
           const float *sv = stg + lane;
@@ -675,7 +666,8 @@ bool gather_ok(const fb_bf16_row_gather &g, int K) {
 bool problem_ok(const fb_gemm_bf16_problem &p) {
   if (p.kind < FB_GEMM_NT || p.kind > FB_GEMM_TN) return false;
   if (p.M < 0 || p.M > (int64_t)1 << 30 || p.N < 1 || p.K < 1) return false;
-  if (p.add && (p.kind == FB_GEMM_TN || !p.add_idx || p.ld_add < p.N || p.add_rows < 1 || p.add_rows > INT32_MAX))
+  if (p.add && (p.kind == FB_GEMM_TN || !p.add_idx || p.ld_add < p.N || p.ld_add % 4 || !al16(p.add) ||
+                p.add_rows < 1 || p.add_rows > INT32_MAX))
     return false;
   if (p.gather) {
     if (!gather_ok(*p.gather, p.K)) return false;
