@@ -57,19 +57,28 @@ using namespace fbtc;
 
 constexpr int BM = 128;                      // MMA M = TMEM lanes
 constexpr int BK = 64;                       // reduction slice: 64 bf16 = one 128-byte swizzle row
-constexpr int kStages = 4;
+constexpr int kStagesN = 4;                  // stages of the standard variant (48 KB each)
+constexpr int kStagesW = 3;                  // of the wide variant (64 KB each)
 constexpr int kMaxBn = 256;
 constexpr int kMaxBf = 7;                    // problems per launch (parameters under 4 KB)
 constexpr int kAOp = BM * BK * 2;            // 16 KB
 constexpr int kBOp = kMaxBn * BK * 2;        // 32 KB
-constexpr int kStage = kAOp + kBOp;
+// Wide variant (launches holding a segmented TN): such a TN item covers 2 BM
+// columns of X with two MMAs per K step sharing the staged G slice, so the A
+// area of a stage holds four MN-major boxes.
+template <bool W> __host__ __device__ constexpr int a_bytes() { return W ? 2 * kAOp : kAOp; }
+template <bool W> __host__ __device__ constexpr int stages() { return W ? kStagesW : kStagesN; }
+template <bool W> __host__ __device__ constexpr int stage_bytes() { return a_bytes<W>() + kBOp; }
 constexpr int kBox = BK * 128;               // one MN-major box: BK rows of 64 elements
 constexpr int kEpiWarps = 8;
 constexpr int kStagePitch = 33;              // epilogue staging rows (floats; odd: no bank conflicts)
 constexpr int kStageWarp = 32 * kStagePitch * 4;
 constexpr int kBarBytes = 256;
-constexpr int kSmem = 1024 + kStages * kStage + kBarBytes + kEpiWarps * kStageWarp;
-static_assert(kSmem <= 232448, "shared memory of k_bf_group exceeds 227 KB");
+template <bool W> __host__ __device__ constexpr int smem_bytes() {
+  return 1024 + stages<W>() * stage_bytes<W>() + kBarBytes + kEpiWarps * kStageWarp;
+}
+static_assert(smem_bytes<false>() <= 232448 && smem_bytes<true>() <= 232448,
+              "shared memory of k_bf_group exceeds 227 KB");
 constexpr int kTmemCols = 512;               // two accumulators of up to 256 columns
 constexpr int kAccStride = 256;
 constexpr int64_t kTnRowsMin = 512;          // TN: rows per split, at least
@@ -111,6 +120,7 @@ struct BfProb {
   int kind, a_mn, b_mn, k1, K, N, Kp, bn, rt, nt, ones, accumulate, db_accumulate, max_splits;
   int swap, ktot, nseg, seg_at[3], seg_len[3], seg_to[3];
   int c_bf16;                // NT / NN: C holds bf16 (round to nearest even), written, not accumulated
+  int wide;                  // segmented TN in a wide launch: items of 2 BM rows (X columns)
   int gat, g_nseg, g_end[3], g_rows[3];   // A of the tiling gathered (see fb_bf16_row_gather)
   const int32_t *g_idx[3];
   const float *add;                         // NT / NN: + add[add_idx[m] * ld_add + n] in the epilogue
@@ -171,7 +181,7 @@ __device__ __forceinline__ Item decode(const BfArgs &a, const int *st, const lon
     const int per_z = q.rt * q.nt;
     it.z = l / per_z;
     l -= it.z * per_z;
-    it.r0 = (int64_t)(l / q.nt) * BM;
+    it.r0 = (int64_t)(l / q.nt) * (q.wide ? 2 * BM : BM);
     it.c0 = (l % q.nt) * q.bn;
     it.s0 = (int64_t)it.z * sper[p];
     it.s1 = min((int64_t)sm[p], it.s0 + (int64_t)sper[p]);
@@ -201,16 +211,16 @@ __device__ __forceinline__ void set_ones(uint8_t *box0, int col, int valid, int 
 }
 
 __device__ __forceinline__ void fix_tn_slice(uint8_t *a, uint8_t *b, int nbox, int valid, int onescol, int onescol_a,
-                                             int lane, int clear_a = 0) {
+                                             int lane, int clear_a = 0, int na = 2) {
   // A boxes that nothing loaded (past a gathered operand's last segment): zeros
   for (int bx = 0; bx < 2; ++bx)
     if (clear_a & (1 << bx))
       for (int t = lane; t < kBox / 16; t += 32) reinterpret_cast<uint4 *>(a + bx * kBox)[t] = make_uint4(0u, 0u, 0u, 0u);
   if (valid < BK) {
     const int per_box = (BK - valid) * 8;    // 16-byte words to clear per box
-    for (int t = lane; t < (2 + nbox) * per_box; t += 32) {
+    for (int t = lane; t < (na + nbox) * per_box; t += 32) {
       const int bx = t / per_box, e = t - bx * per_box;
-      uint8_t *base = bx < 2 ? a + bx * kBox : b + (bx - 2) * kBox;
+      uint8_t *base = bx < na ? a + bx * kBox : b + (bx - na) * kBox;
       reinterpret_cast<uint4 *>(base + valid * 128)[e] = make_uint4(0u, 0u, 0u, 0u);
     }
   }
@@ -218,11 +228,13 @@ __device__ __forceinline__ void fix_tn_slice(uint8_t *a, uint8_t *b, int nbox, i
   if (onescol_a >= 0) set_ones(a, onescol_a, valid, lane);
 }
 
+template <bool W>
 __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant__ BfArgs a) {
+  constexpr int kStages = stages<W>(), kStage = stage_bytes<W>(), kAOpS = a_bytes<W>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align1024(smem_raw);
   auto sA = [&](int s) { return smem + s * kStage; };
-  auto sB = [&](int s) { return smem + s * kStage + kAOp; };
+  auto sB = [&](int s) { return smem + s * kStage + kAOpS; };
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStage);
   uint64_t *full = bars, *empty = bars + kStages;
   uint64_t *accf = bars + 2 * kStages, *acce = bars + 2 * kStages + 2, *drain = bars + 2 * kStages + 4;
@@ -313,7 +325,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
 #pragma unroll
         for (int u = 0; u < 4; ++u) nx[u] = grow(q, gsg, m0 + u, it.s1);
       }
-      uint32_t bytes = (uint32_t)(kAOp + bn * BK * 2);
+      const bool wide = q.wide != 0;
+      uint32_t bytes = (uint32_t)((wide ? 2 * kAOp : kAOp) + bn * BK * 2);
       if (gat && tn)
         for (int t = 0; t < 2; ++t)
           if (gseg(q, r0 + 64 * t) >= q.g_nseg) bytes -= kBox;    // past the last segment: cleared, not loaded
@@ -352,8 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
           }
         } else if (lane == 0) {
           if (tn) {
-            tma_load_2d(sA(s), &q.ta, full + s, r0, my);
-            tma_load_2d(sA(s) + kBox, &q.ta, full + s, r0 + 64, my);
+            for (int t = 0; t < (wide ? 4 : 2); ++t) tma_load_2d(sA(s) + t * kBox, &q.ta, full + s, r0 + 64 * t, my);
           } else if (j < it.nk1) {
             tma_load_2d(sA(s), &q.ta, full + s, BK * j, r0);
           } else {
@@ -377,24 +389,32 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
       for (uint32_t h = g > (uint32_t)kStages ? g - kStages : 0; h < g; ++h) mbar_drain(full + h % kStages, (h / kStages) & 1);
     }
   } else if (warp == kWarpMma) {
-    uint32_t g = 0, tc = 0;
+    uint32_t g = 0, used[2] = {0u, 0u};
+    int nxt = 0;
     bool stop = false;
-    for (int i = blockIdx.x; i < total && !stop; i += gridDim.x, ++tc) {
+    for (int i = blockIdx.x; i < total && !stop; i += gridDim.x) {
       const Item it = decode(a, s_start, s_m, s_per, i);
       const BfProb &q = a.p[it.p];
       const bool tn = q.kind == kTN, amn = q.a_mn != 0, bmn = q.b_mn != 0;
+      const bool wide = q.wide != 0;
       const uint32_t idesc = q.idesc;
       const int nbox = q.bn / 64;
       const int onescol = (tn && q.ones == 1 && q.K >= it.c0 && q.K < it.c0 + q.bn) ? q.K - it.c0 : -1;
       const int64_t ones_row = (int64_t)q.N - 1 - it.r0;     // swapped form: A's ones column in this tile
-      const int onescol_a = (tn && q.ones == 2 && ones_row >= 0 && ones_row < BM) ? (int)ones_row : -1;
+      const int onescol_a = (tn && q.ones == 2 && ones_row >= 0 && ones_row < (wide ? 2 * BM : BM)) ? (int)ones_row
+                                                                                                   : -1;
       int clear_a = 0;                                        // gathered X: boxes past the last segment
       if (tn && q.gat)
         for (int t = 0; t < 2; ++t)
           if (gseg(q, (int)it.r0 + 64 * t) >= q.g_nseg) clear_a |= 1 << t;
       const uint64_t adv_a = amn ? (2048 >> 4) : 2, adv_b = bmn ? (2048 >> 4) : 2;   // one K step of 16
-      const int b = tc & 1;
-      if (tc >= 2 && !mbar_wait(acce + b, ((tc >> 1) - 1) & 1, abort_flag, err)) break;
+      // accumulators of this item: the next one in turn, or both (wide)
+      const int b = wide ? 0 : nxt;
+      if (!wide) nxt ^= 1;
+      bool free_ok = true;
+      for (int bb = b; bb <= (wide ? 1 : b); ++bb)
+        if (used[bb] >= 1 && !mbar_wait(acce + bb, (used[bb] - 1) & 1, abort_flag, err)) free_ok = false;
+      if (!free_ok) break;
       const uint32_t d = tmem + (uint32_t)(b * kAccStride);
       for (int j = 0; j < it.nk; ++j) {
         const int s = g % kStages;
@@ -406,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
           const int64_t left = it.s1 - (it.s0 + (int64_t)BK * j);
           const int valid = left <= 0 ? 0 : (left >= BK ? BK : (int)left);
           if (valid < BK || onescol >= 0 || onescol_a >= 0 || clear_a) {
-            fix_tn_slice(sA(s), sB(s), nbox, valid, onescol, onescol_a, lane, clear_a);
+            fix_tn_slice(sA(s), sB(s), nbox, valid, onescol, onescol_a, lane, clear_a, wide ? 4 : 2);
             fence_async_smem();
           }
           __syncwarp();
@@ -417,11 +437,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
             umma_bf16(d, ad + kk * adv_a, bd + kk * adv_b, idesc, (j | kk) != 0 ? 1u : 0u);
+          if (wide) {
+            // X columns BM .. 2 BM of the item: the other accumulator, the same G slice
+            const uint64_t ad1 = sdesc(smem_u32(sA(s) + 2 * kBox), amn);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              umma_bf16(d + kAccStride, ad1 + kk * adv_a, bd + kk * adv_b, idesc, (j | kk) != 0 ? 1u : 0u);
+          }
           umma_commit(empty + s);
-          if (j == it.nk - 1) umma_commit(accf + b);
+          if (j == it.nk - 1) {
+            umma_commit(accf + b);
+            if (wide) umma_commit(accf + 1);
+          }
         }
         __syncwarp();
         ++g;
+      }
+      if (!stop) {
+        ++used[b];
+        if (wide) ++used[1];
       }
     }
     if (lane == 0) {
@@ -436,12 +470,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
     const int half = e >> 2;
     const uint32_t tlane = (uint32_t)(qd * 32) << 16;
     float *stg = reinterpret_cast<float *>(smem + kStages * kStage + kBarBytes + e * kStageWarp);
-    uint32_t tc = 0;
-    for (int i = blockIdx.x; i < total; i += gridDim.x, ++tc) {
+    uint32_t used[2] = {0u, 0u};
+    int nxt = 0;
+    bool quit = false;
+    for (int i = blockIdx.x; i < total && !quit; i += gridDim.x) {
       const Item it = decode(a, s_start, s_m, s_per, i);
       const BfProb &q = a.p[it.p];
-      const int b = tc & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(accf + b, (tc >> 1) & 1, abort_flag, err) ? 1 : 0)) break;
+      const bool wide = q.wide != 0;
+      const int b0 = wide ? 0 : nxt;
+      if (!wide) nxt ^= 1;
+     for (int b = b0; b <= (wide ? 1 : b0); ++b) {
+      if (!__all_sync(0xffffffffu, mbar_wait(accf + b, used[b] & 1, abort_flag, err) ? 1 : 0)) {
+        quit = true;
+        break;
+      }
       tc_fence_after();
       const uint32_t t = tmem + tlane + (uint32_t)(b * kAccStride);
       // the problem's fields in registers (read through the parameter
@@ -459,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
       const int32_t *const add_idx = q.add_idx;
       const int64_t ld_add = q.ld_add;
       const int add_rows = q.add_rows;
-      const int64_t row0 = it.r0 + qd * 32;
+      const int64_t row0 = it.r0 + (wide ? (int64_t)b * BM : 0) + qd * 32;
       const int nrows = rows - row0 < 32 ? (int)max(rows - row0, (int64_t)0) : 32;
       // add table: lane r adds the (clamped) table row of output row row0 + r
       const int add_row = (add && lane < nrows) ? min(max(__ldg(add_idx + row0 + lane), 0), add_rows - 1) : 0;
@@ -523,6 +565,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
       }
       tc_fence_before();
       mbar_arrive(acce + b);
+      ++used[b];
+     }
     }
   }
   tc_fence_before();
@@ -632,10 +676,17 @@ void tn_dims(const fb_gemm_bf16_problem &p, int &rows, int &cols) {
   }
 }
 
+// Segmented TN problems on materialised rows run wide (items of 2 BM rows).
+bool tn_wide(const fb_gemm_bf16_problem &p) {
+  static const bool off = getenv("FB_TN_NARROW") != nullptr;
+  return !off && p.kind == FB_GEMM_TN && p.nseg > 0 && !p.gather;
+}
+
 int tn_splits_max(const fb_gemm_bf16_problem &p) {
   int rows, cols;
   tn_dims(p, rows, cols);
-  const int tiles = ((rows + BM - 1) / BM) * ((cols + bn_mnmajor(cols) - 1) / bn_mnmajor(cols));
+  const int tr = tn_wide(p) ? 2 * BM : BM;
+  const int tiles = ((rows + tr - 1) / tr) * ((cols + bn_mnmajor(cols) - 1) / bn_mnmajor(cols));
   return std::max(1, num_sms() / std::max(tiles, 1));
 }
 
@@ -757,7 +808,8 @@ int build_prob(BfProb &q, const fb_gemm_bf16_problem &p, float *ws) {
     q.K = p.N;
     q.Kp = p.N;
     q.bn = bn_mnmajor(q.Kp);
-    q.rt = (q.N + BM - 1) / BM;
+    q.wide = tn_wide(p) ? 1 : 0;
+    q.rt = (q.N + (q.wide ? 2 * BM : BM) - 1) / (q.wide ? 2 * BM : BM);
     q.nt = (q.Kp + q.bn - 1) / q.bn;
     q.db = p.db;
     q.db_accumulate = p.db_accumulate;
@@ -817,9 +869,12 @@ int launch_group(const std::vector<const fb_gemm_bf16_problem *> &probs, const s
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr_set[dev]) {
-    FB_TRY_CUDA(cudaFuncSetAttribute(k_bf_group, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
-    attr_set[dev] = true;
+  if (!attr_set[dev & 63]) {
+    FB_TRY_CUDA(cudaFuncSetAttribute(k_bf_group<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     smem_bytes<false>()));
+    FB_TRY_CUDA(cudaFuncSetAttribute(k_bf_group<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     smem_bytes<true>()));
+    attr_set[dev & 63] = true;
   }
   BfArgs a;
   std::memset(&a, 0, sizeof(a));
@@ -842,7 +897,13 @@ int launch_group(const std::vector<const fb_gemm_bf16_problem *> &probs, const s
   a.red_start[a.n] = red;
   if (items == 0) return FB_OK;
   const int grid = (int)std::min<int64_t>(items, num_sms());
-  FB_TRY_CUDA(fb::launch(k_bf_group, grid, kThreads, kSmem, stream, a));
+  bool wide = false;
+  for (int i = 0; i < a.n; ++i) wide = wide || a.p[i].wide;
+  if (wide) {
+    FB_TRY_CUDA(fb::launch(k_bf_group<true>, grid, kThreads, smem_bytes<true>(), stream, a));
+  } else {
+    FB_TRY_CUDA(fb::launch(k_bf_group<false>, grid, kThreads, smem_bytes<false>(), stream, a));
+  }
   FB_LAUNCHED("k_bf_group");
   if (red > 0) {
     FB_TRY_CUDA(fb::launch(k_bf_reduce, red, 256, 0, stream, a));
