@@ -623,9 +623,11 @@ int te_bwd(const T *g, int64_t ldg, const float *dt, const float *w, const float
   // take the partition from the true count
   const int parts = te_parts(n_rows);
   float *part = static_cast<float *>(ws);
-  static const bool no_pairs = getenv("FB_TE_BWD_SINGLE") != nullptr;
+  // column pairs (FB_TE_BWD_PAIRS=1): measured slower than one column per
+  // thread on a B200 (298 against 214 us per config-5 step), so opt-in
+  static const bool pairs = getenv("FB_TE_BWD_PAIRS") != nullptr;
   const size_t pair_bytes = sizeof(T) * 2;
-  if (!no_pairs && dtime % 2 == 0 && dtime <= kTeColsMax && ldg % 2 == 0 &&
+  if (pairs && dtime % 2 == 0 && dtime <= kTeColsMax && ldg % 2 == 0 &&
       (reinterpret_cast<uintptr_t>(g) % pair_bytes) == 0) {
     // groups of dtime / 2 threads (a column pair each): as many as fit 512 threads, at most kTeGroups
     const int half = dtime / 2;

@@ -123,6 +123,9 @@ struct BfProb {
   int wide;                  // segmented TN in a wide launch: items of 2 BM rows (X columns)
   int gat, g_nseg, g_end[3], g_rows[3];   // A of the tiling gathered (see fb_bf16_row_gather)
   const int32_t *g_idx[3];
+  const uint16_t *g_tab[3];                 // gathered segments' sources (16-byte cp.async copies)
+  int64_t g_ld[3];
+  int g_cols[3];
   const float *add;                         // NT / NN: + add[add_idx[m] * ld_add + n] in the epilogue
   const int32_t *add_idx;
   int64_t ld_add;
@@ -306,65 +309,115 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
       const bool tn = q.kind == kTN, bmn = q.b_mn != 0, gat = q.gat != 0;
       const int bn = q.bn, k1 = q.k1, c0 = it.c0;
       const int r0 = (int)it.r0;
-      // NT gathered: this lane's rows r0 + 4 lane + u, their source rows per segment
+      // Gathered rows are copied by every lane with cp.async, 16 bytes at a time,
+      // straight into the 128-byte-swizzled layout (16-byte chunk c of tile row
+      // r at r * 128 + ((c ^ (r & 7)) << 4)); columns past the source's data
+      // are zero-filled.  NT: lane l copies tile rows l + 32 u (u < 4); TN: rows
+      // l + 32 u (u < 2) of each of the slice's two X boxes.
       int ix[3][4];
       if (gat && !tn) {
 #pragma unroll
         for (int sg = 0; sg < 3; ++sg)
 #pragma unroll
           for (int u = 0; u < 4; ++u)
-            ix[sg][u] = (sg < q.g_nseg && q.g_idx[sg]) ? grow(q, sg, (int64_t)r0 + 4 * lane + u, s_m[it.p]) : 0;
+            ix[sg][u] = (sg < q.g_nseg && q.g_idx[sg]) ? grow(q, sg, (int64_t)r0 + lane + 32 * u, s_m[it.p]) : 0;
       }
-      // TN gathered: lane = (box t = lane / 16, rows 4 (lane % 16) .. + 3 of the slice)
-      const int gt = lane >> 4, gq = lane & 15;
-      const int gsg = (gat && tn) ? gseg(q, r0 + 64 * gt) : 0;
-      const bool gidx = gat && tn && gsg < q.g_nseg && q.g_idx[gsg] != nullptr;
-      int nx[4] = {0, 0, 0, 0};
-      if (gidx) {
-        const int64_t m0 = it.s0 + 4 * gq;
+      int gsg[2] = {0, 0}, nx[2][2] = {{0, 0}, {0, 0}};
+      bool gidx[2] = {false, false};
+      if (gat && tn) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) nx[u] = grow(q, gsg, m0 + u, it.s1);
+        for (int t = 0; t < 2; ++t) {
+          gsg[t] = gseg(q, r0 + 64 * t);
+          gidx[t] = gsg[t] < q.g_nseg && q.g_idx[gsg[t]] != nullptr;
+          if (gidx[t])
+#pragma unroll
+            for (int u = 0; u < 2; ++u) nx[t][u] = grow(q, gsg[t], it.s0 + lane + 32 * u, it.s1);
+        }
       }
       const bool wide = q.wide != 0;
+      // bytes the TMA copies of a stage bring (gathered boxes arrive through cp.async)
       uint32_t bytes = (uint32_t)((wide ? 2 * kAOp : kAOp) + bn * BK * 2);
-      if (gat && tn)
+      if (gat && tn) {
         for (int t = 0; t < 2; ++t)
-          if (gseg(q, r0 + 64 * t) >= q.g_nseg) bytes -= kBox;    // past the last segment: cleared, not loaded
+          if (gsg[t] >= q.g_nseg || gidx[t]) bytes -= kBox;  // cleared (past the last segment) or gathered
+      }
       for (int j = 0; j < it.nk; ++j) {
         const int s = g % kStages;
         int ok = 1;
-        if (lane == 0) {
-          if (g >= kStages && !mbar_wait(empty + s, ((g / kStages) - 1) & 1, abort_flag, err)) ok = 0;
-          else mbar_expect_tx(full + s, bytes);
-        }
+        if (lane == 0 && g >= kStages && !mbar_wait(empty + s, ((g / kStages) - 1) & 1, abort_flag, err)) ok = 0;
         if (!__shfl_sync(0xffffffffu, ok, 0)) {
           stop = true;
           break;
         }
         const int kb = j < it.nk1 ? BK * j : k1 + BK * (j - it.nk1);
         const int my = (int)it.s0 + BK * j;
+        bool tiled_a = true;                                 // lane 0 issues A by TMA
         if (gat && !tn) {
-          const int sg = gseg(q, kb);                         // kb < K: a segment
+          const int sg = gseg(q, kb);                        // kb < K: a segment
           if (q.g_idx[sg]) {
-            tma_gather4(sA(s) + lane * 512, gmap(q, sg), full + s, kb - gstart(q, sg), ix[sg][0], ix[sg][1],
-                        ix[sg][2], ix[sg][3]);
-          } else if (lane == 0) {
-            tma_load_2d(sA(s), gmap(q, sg), full + s, kb - gstart(q, sg), r0);
+            tiled_a = false;
+            const int col = kb - gstart(q, sg);
+            const uint16_t *tab = q.g_tab[sg];
+            const int64_t ld = q.g_ld[sg];
+            const int cols = q.g_cols[sg];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int r = lane + 32 * u;
+              const uint16_t *src = tab + (int64_t)ix[sg][u] * ld + col;
+              uint8_t *dst = sA(s) + r * 128;
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                const int nb = min(max(2 * (cols - col - 8 * c), 0), 16);
+                cp_async16(dst + ((c ^ (r & 7)) << 4), nb ? src + 8 * c : tab, (uint32_t)nb);
+              }
+            }
+            cp_async_arrive(full + s);
           }
         } else if (gat) {
-          if (gidx) {
-            tma_gather4(sA(s) + gt * kBox + gq * 512, gmap(q, gsg), full + s, r0 + 64 * gt - gstart(q, gsg), nx[0],
-                        nx[1], nx[2], nx[3]);
-            if (j + 1 < it.nk) {
-              const int64_t m1 = it.s0 + BK * (j + 1) + 4 * gq;
+          bool any = false;
 #pragma unroll
-              for (int u = 0; u < 4; ++u) nx[u] = grow(q, gsg, m1 + u, it.s1);
+          for (int t = 0; t < 2; ++t) {
+            if (!gidx[t]) continue;
+            any = true;
+            const int col = r0 + 64 * t - gstart(q, gsg[t]);
+            const uint16_t *tab = q.g_tab[gsg[t]];
+            const int64_t ld = q.g_ld[gsg[t]];
+            const int cols = q.g_cols[gsg[t]];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int r = lane + 32 * u;
+              const uint16_t *src = tab + (int64_t)nx[t][u] * ld + col;
+              uint8_t *dst = sA(s) + t * kBox + r * 128;
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                const int nb = min(max(2 * (cols - col - 8 * c), 0), 16);
+                cp_async16(dst + ((c ^ (r & 7)) << 4), nb ? src + 8 * c : tab, (uint32_t)nb);
+              }
             }
-          } else if (gq == 0 && gsg < q.g_nseg) {
-            tma_load_2d(sA(s) + gt * kBox, gmap(q, gsg), full + s, r0 + 64 * gt - gstart(q, gsg), my);
           }
-        } else if (lane == 0) {
-          if (tn) {
+          if (any) cp_async_arrive(full + s);
+          // the next slice's source rows
+          if (j + 1 < it.nk) {
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+              if (gidx[t])
+#pragma unroll
+                for (int u = 0; u < 2; ++u) nx[t][u] = grow(q, gsg[t], it.s0 + BK * (j + 1) + lane + 32 * u, it.s1);
+          }
+        }
+        __syncwarp();                                        // every lane's pending arrival before lane 0's
+        if (lane == 0) {
+          mbar_expect_tx(full + s, bytes);
+          if (gat && tn) {
+            for (int t = 0; t < 2; ++t)
+              if (gsg[t] < q.g_nseg && !gidx[t])
+                tma_load_2d(sA(s) + t * kBox, gmap(q, gsg[t]), full + s, r0 + 64 * t - gstart(q, gsg[t]), my);
+          } else if (gat) {
+            if (tiled_a) {
+              const int sg = gseg(q, kb);
+              tma_load_2d(sA(s), gmap(q, sg), full + s, kb - gstart(q, sg), r0);
+            }
+          } else if (tn) {
             for (int t = 0; t < (wide ? 4 : 2); ++t) tma_load_2d(sA(s) + t * kBox, &q.ta, full + s, r0 + 64 * t, my);
           } else if (j < it.nk1) {
             tma_load_2d(sA(s), &q.ta, full + s, BK * j, r0);

@@ -89,6 +89,19 @@ __device__ __forceinline__ void tma_gather4(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
+// 16 bytes global -> shared (cp.async, L2-cached); only the first src_bytes
+// are read, the rest of the 16 are zero-filled.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+
+// One more pending arrival on bar, made once every cp.async this thread has
+// issued so far has landed.
+__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
