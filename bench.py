@@ -560,7 +560,11 @@ def run_fast(args):
     # the sampler entry times a whole sample() call (several kernels), not one kernel
     top = max(((k, v) for k, v in kern.items() if k != "sampler"), key=lambda kv: kv[1]["ms"])
     name, r = top
-    if r["flops"] > 0 and name.startswith("gemm"):
+    # the binding roof: a contraction whose algorithmic bytes take longer at the copy bandwidth than its
+    # flops at the tensor peak (flops per byte below the machine balance) is bounded by HBM
+    tensor_bound = (r["flops"] > 0 and name.startswith("gemm") and
+                    r["flops"] / (pk["tf"] * 1e12) >= r["bytes"] / (pk["hbm"] * 1e9))
+    if tensor_bound:
         ach = r["flops"] / (r["ms"] / 1000.0) / 1e12
         roof = {"kernel": name, "bound": "tensor", "achieved": round(ach, 3), "peak": pk["tf"], "unit": "TFLOP/s",
                 "frac": round(ach / pk["tf"], 5), "traffic": None,
@@ -574,6 +578,12 @@ def run_fast(args):
         roof = {"kernel": name, "bound": "hbm", "achieved": round(ach, 1), "peak": pk["hbm"], "unit": "GB/s",
                 "frac": round(ach / pk["hbm"], 4), "traffic": None,
                 "peak_source": "%s copy bandwidth (MEASURED_PEAKS.json)" % pk["src"]}
+        if r["flops"] > 0:
+            tfs = r["flops"] / (r["ms"] / 1000.0) / 1e12
+            roof["note"] = ("a contraction below the machine balance (%.0f flop/B against %.0f): its algorithmic "
+                            "bytes at the copy bandwidth take longer than its flops at the bf16 peak; tensor: "
+                            "%.1f TFLOP/s, %.3f of %s" % (r["flops"] / r["bytes"], pk["tf"] * 1e3 / pk["hbm"], tfs,
+                                                          tfs / pk["tf"], pk["tf"]))
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
@@ -838,6 +848,29 @@ def run_bf16_suite(args):
           2 * E * 2 * D + gat.read_bytes(E) + 4 * 2 * D * (dn + de + dt_),
           2 * E * 2 * D * (dn + de + dt_ + 1), lambda: ops.gemm_bf16_group(tng),
           "M=%d, N=%d, K=%d+%d+%d+1" % (E, 2 * D, dn, de, dt_))
+    # layer 0 of the step with the node product: the gather writes [f | cos] rows only, and the weight
+    # gradient reads the node block from the table by source node (cp.async row copies)
+    XF = torch.empty(E, ops.pad8(ops.pad8(de) + dt_), device=dev, dtype=torch.bfloat16)
+    timed("k_gather_time_encode_bf16 ([f | cos] rows, node block left out)", E * (2 * XF.shape[1] + 2 * 192 + 12), 0,
+          lambda: ops.gather_time_encode_bf16(E, f=etab, f_idx=eid, dt=dts, w=w, b=b, out=XF, de=de),
+          "E=%d rows of [f(%d) | cos(%d)] bf16" % (E, de, dt_))
+    gnr = ops.RowGather([(ntab, dn, nid, 448), (XF, ops.pad8(de) + dt_, None, 320)])
+    tnr = [dict(kind=ops.TN, A=dkv, gather=gnr, out=gW, accumulate=True, db=gb,
+                segs=[(0, dn, 0), (448, de, dn), (448 + ops.pad8(de), dt_, dn + de)])]
+    timed("k_bf_group (K|V weight + bias gradient, TN, node rows by index + [f | cos] rows)",
+          2 * E * 2 * D + gnr.read_bytes(E) + 4 * 2 * D * (dn + de + dt_),
+          2 * E * 2 * D * (dn + de + dt_ + 1), lambda: ops.gemm_bf16_group(tnr),
+          "M=%d, N=%d, K=%d+%d+%d+1" % (E, 2 * D, dn, de, dt_))
+    # the same TN operand with the node block materialised: both segments read row by row by TMA
+    XH = torch.empty(E, 448, device=dev, dtype=torch.bfloat16)
+    XH[:, :416] = ntab[nid.long()]
+    gtm = ops.RowGather([(XH, dn, None, 448), (XF, ops.pad8(de) + dt_, None, 320)])
+    tnm = [dict(tnr[0], gather=gtm)]
+    timed("k_bf_group (K|V weight + bias gradient, TN, [node rows | [f | cos] rows] both read row by row)",
+          2 * E * 2 * D + gtm.read_bytes(E) + 4 * 2 * D * (dn + de + dt_),
+          2 * E * 2 * D * (dn + de + dt_ + 1), lambda: ops.gemm_bf16_group(tnm),
+          "M=%d, N=%d, K=%d+%d+%d+1" % (E, 2 * D, dn, de, dt_))
+    del XH
     dAt = torch.empty(E, dt_, device=dev, dtype=torch.bfloat16)       # bf16, as in the step
     timed("k_bf_group (time-encoding input gradient, NN, bf16 output)", E * (2 * 2 * D + 2 * dt_),
           2 * E * dt_ * 2 * D,

@@ -18,8 +18,10 @@
 //   Gathered operand (NT's A, or the segmented TN's X): the rows are not read
 //   from one matrix but gathered per 64-column segment from up to three bf16
 //   sources -- node-feature rows by node id, edge-feature rows by edge id
-//   (TMA tile::gather4, four rows per copy, spread over the producer warp's
-//   lanes), and a matrix read row by row (the time encoding) -- so the
+//   (16-byte cp.async copies from every producer lane, written in the
+//   swizzled layout and counted on the stage's barrier through
+//   cp.async.mbarrier.arrive), and a matrix read row by row by TMA (the time
+//   encoding) -- so the
 //   projection rows of a block are never written to memory.
 //
 // Operands are bf16 in global memory and reach the tensor cores untouched:
@@ -83,6 +85,7 @@ constexpr int kTmemCols = 512;               // two accumulators of up to 256 co
 constexpr int kAccStride = 256;
 constexpr int64_t kTnRowsMin = 512;          // TN: rows per split, at least
 constexpr int kWarpProducer = 0, kWarpMma = 1, kWarpEpi0 = 4;
+
 constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;
 
 enum : int { kNT = 0, kNN = 1, kTN = 2 };
@@ -231,6 +234,26 @@ __device__ __forceinline__ void fix_tn_slice(uint8_t *a, uint8_t *b, int nbox, i
   if (onescol_a >= 0) set_ones(a, onescol_a, valid, lane);
 }
 
+// 64 columns (128 bytes) from column `col` of 32 U gathered rows into a
+// 128-byte-swizzled box (16-byte chunk c of box row r at r * 128 + ((c ^ (r &
+// 7)) << 4)), by cp.async: lane l copies box rows l + 32 u, source row
+// idx[u]; columns at or past `cols` are zero-filled.
+template <int U>
+__device__ __forceinline__ void gather_box(uint8_t *box, const uint16_t *tab, int64_t ld, int col, int cols,
+                                           const int (&idx)[U], int lane) {
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int r = lane + 32 * u;
+    const uint16_t *src = tab + (int64_t)idx[u] * ld + col;
+    uint8_t *dst = box + r * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int nb = min(max(2 * (cols - col - 8 * c), 0), 16);
+      cp_async16(dst + ((c ^ (r & 7)) << 4), nb ? src + 8 * c : tab, (uint32_t)nb);
+    }
+  }
+}
+
 template <bool W>
 __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant__ BfArgs a) {
   constexpr int kStages = stages<W>(), kStage = stage_bytes<W>(), kAOpS = a_bytes<W>();
@@ -250,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(full + s, 1);
+      mbar_init(full + s, 32);                     // the producer warp's lanes
       mbar_init(empty + s, 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -299,8 +322,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
   }
 
   if (warp == kWarpProducer) {
-    // lane 0 waits, arms the stage's barrier and issues the tiled copies; for
-    // a gathered operand every lane then issues row gathers (four rows each)
+    // every lane waits for a stage to be free, issues its gathered-row copies
+    // (if any) and arrives; lane 0 arms the barrier with the byte count of the
+    // tiled (TMA) copies and issues them
     uint32_t g = 0;
     bool stop = false;
     for (int i = blockIdx.x; i < total && !stop; i += gridDim.x) {
@@ -309,11 +333,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
       const bool tn = q.kind == kTN, bmn = q.b_mn != 0, gat = q.gat != 0;
       const int bn = q.bn, k1 = q.k1, c0 = it.c0;
       const int r0 = (int)it.r0;
-      // Gathered rows are copied by every lane with cp.async, 16 bytes at a time,
-      // straight into the 128-byte-swizzled layout (16-byte chunk c of tile row
-      // r at r * 128 + ((c ^ (r & 7)) << 4)); columns past the source's data
-      // are zero-filled.  NT: lane l copies tile rows l + 32 u (u < 4); TN: rows
-      // l + 32 u (u < 2) of each of the slice's two X boxes.
+      // Gathered rows are copied by every lane with cp.async (gather_box): the
+      // source row of tile row lane + 32 u sits in this lane's register u.  NT:
+      // ix[segment][u] for the item's 128 rows.  TN: the two X boxes' 64 rows
+      // of a slice, in two register sets used by alternate slices, so a set's
+      // index loads are issued two slices ahead of the copies that use them.
       int ix[3][4];
       if (gat && !tn) {
 #pragma unroll
@@ -322,17 +346,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
           for (int u = 0; u < 4; ++u)
             ix[sg][u] = (sg < q.g_nseg && q.g_idx[sg]) ? grow(q, sg, (int64_t)r0 + lane + 32 * u, s_m[it.p]) : 0;
       }
-      int gsg[2] = {0, 0}, nx[2][2] = {{0, 0}, {0, 0}};
+      int gsg[2] = {0, 0};
       bool gidx[2] = {false, false};
+      int nxa[2][2] = {{0, 0}, {0, 0}}, nxb[2][2] = {{0, 0}, {0, 0}};
+      auto load_nx = [&](int jj, int (&o)[2][2]) {
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int u = 0; u < 2; ++u)
+            o[t][u] = (gidx[t] && jj < it.nk) ? grow(q, gsg[t], it.s0 + (int64_t)BK * jj + lane + 32 * u, it.s1) : 0;
+      };
       if (gat && tn) {
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           gsg[t] = gseg(q, r0 + 64 * t);
           gidx[t] = gsg[t] < q.g_nseg && q.g_idx[gsg[t]] != nullptr;
-          if (gidx[t])
-#pragma unroll
-            for (int u = 0; u < 2; ++u) nx[t][u] = grow(q, gsg[t], it.s0 + lane + 32 * u, it.s1);
         }
+        load_nx(0, nxa);
+        load_nx(1, nxb);
       }
       const bool wide = q.wide != 0;
       // bytes the TMA copies of a stage bring (gathered boxes arrive through cp.async)
@@ -341,14 +372,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
         for (int t = 0; t < 2; ++t)
           if (gsg[t] >= q.g_nseg || gidx[t]) bytes -= kBox;  // cleared (past the last segment) or gathered
       }
-      for (int j = 0; j < it.nk; ++j) {
+      // slice j of the item into the next stage; false: the pipeline stopped
+      auto slice = [&](int j, const int (&nx)[2][2]) -> bool {
         const int s = g % kStages;
         int ok = 1;
         if (lane == 0 && g >= kStages && !mbar_wait(empty + s, ((g / kStages) - 1) & 1, abort_flag, err)) ok = 0;
-        if (!__shfl_sync(0xffffffffu, ok, 0)) {
-          stop = true;
-          break;
-        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
+        __syncwarp();                                        // the stage is free for every lane's copies
         const int kb = j < it.nk1 ? BK * j : k1 + BK * (j - it.nk1);
         const int my = (int)it.s0 + BK * j;
         bool tiled_a = true;                                 // lane 0 issues A by TMA
@@ -356,58 +386,29 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
           const int sg = gseg(q, kb);                        // kb < K: a segment
           if (q.g_idx[sg]) {
             tiled_a = false;
-            const int col = kb - gstart(q, sg);
-            const uint16_t *tab = q.g_tab[sg];
-            const int64_t ld = q.g_ld[sg];
-            const int cols = q.g_cols[sg];
+            int cur[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const int r = lane + 32 * u;
-              const uint16_t *src = tab + (int64_t)ix[sg][u] * ld + col;
-              uint8_t *dst = sA(s) + r * 128;
-#pragma unroll
-              for (int c = 0; c < 8; ++c) {
-                const int nb = min(max(2 * (cols - col - 8 * c), 0), 16);
-                cp_async16(dst + ((c ^ (r & 7)) << 4), nb ? src + 8 * c : tab, (uint32_t)nb);
-              }
-            }
+            for (int u = 0; u < 4; ++u) cur[u] = sg == 0 ? ix[0][u] : (sg == 1 ? ix[1][u] : ix[2][u]);
+            gather_box<4>(sA(s), q.g_tab[sg], q.g_ld[sg], kb - gstart(q, sg), q.g_cols[sg], cur, lane);
             cp_async_arrive(full + s);
           }
         } else if (gat) {
           bool any = false;
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            if (!gidx[t]) continue;
-            any = true;
-            const int col = r0 + 64 * t - gstart(q, gsg[t]);
-            const uint16_t *tab = q.g_tab[gsg[t]];
-            const int64_t ld = q.g_ld[gsg[t]];
-            const int cols = q.g_cols[gsg[t]];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int r = lane + 32 * u;
-              const uint16_t *src = tab + (int64_t)nx[t][u] * ld + col;
-              uint8_t *dst = sA(s) + t * kBox + r * 128;
-#pragma unroll
-              for (int c = 0; c < 8; ++c) {
-                const int nb = min(max(2 * (cols - col - 8 * c), 0), 16);
-                cp_async16(dst + ((c ^ (r & 7)) << 4), nb ? src + 8 * c : tab, (uint32_t)nb);
-              }
+          for (int t = 0; t < 2; ++t)
+            if (gidx[t]) {
+              any = true;
+              gather_box<2>(sA(s) + t * kBox, q.g_tab[gsg[t]], q.g_ld[gsg[t]], r0 + 64 * t - gstart(q, gsg[t]),
+                            q.g_cols[gsg[t]], nx[t], lane);
             }
-          }
           if (any) cp_async_arrive(full + s);
-          // the next slice's source rows
-          if (j + 1 < it.nk) {
-#pragma unroll
-            for (int t = 0; t < 2; ++t)
-              if (gidx[t])
-#pragma unroll
-                for (int u = 0; u < 2; ++u) nx[t][u] = grow(q, gsg[t], it.s0 + BK * (j + 1) + lane + 32 * u, it.s1);
-          }
         }
-        __syncwarp();                                        // every lane's pending arrival before lane 0's
+        // every lane arrives on the stage's barrier (lane 0 with the TMA byte
+        // count), each after its cp.async arrival: the phase completes when the
+        // tiled copies and every lane's gathered copies have landed
+        if (lane != 0) mbar_arrive(full + s);
         if (lane == 0) {
-          mbar_expect_tx(full + s, bytes);
+          mbar_expect_tx(full + s, tiled_a ? bytes : bytes - kAOp);
           if (gat && tn) {
             for (int t = 0; t < 2; ++t)
               if (gsg[t] < q.g_nseg && !gidx[t])
@@ -424,8 +425,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
           } else {
             tma_load_2d(sA(s), &q.ta2, full + s, BK * (j - it.nk1), r0);
           }
-        }
-        if (lane == 0) {
           if (!bmn) {
             tma_load_2d(sB(s), &q.tb, full + s, kb, c0);
           } else {
@@ -435,6 +434,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
         }
         __syncwarp();
         ++g;
+        return true;
+      };
+      const bool ring = gat && tn;
+      for (int j = 0; j < it.nk; j += 2) {
+        if (!slice(j, nxa)) {
+          stop = true;
+          break;
+        }
+        if (ring) load_nx(j + 2, nxa);
+        if (j + 1 < it.nk) {
+          if (!slice(j + 1, nxb)) {
+            stop = true;
+            break;
+          }
+          if (ring) load_nx(j + 3, nxb);
+        }
       }
     }
     if (lane == 0 && *abort_flag) {
@@ -453,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
       const uint32_t idesc = q.idesc;
       const int nbox = q.bn / 64;
       const int onescol = (tn && q.ones == 1 && q.K >= it.c0 && q.K < it.c0 + q.bn) ? q.K - it.c0 : -1;
-      const int64_t ones_row = (int64_t)q.N - 1 - it.r0;     // swapped form: A's ones column in this tile
+      const int64_t ones_row = (int64_t)q.ktot - it.r0;      // swapped form: A's ones column in this tile
       const int onescol_a = (tn && q.ones == 2 && ones_row >= 0 && ones_row < (wide ? 2 * BM : BM)) ? (int)ones_row
                                                                                                    : -1;
       int clear_a = 0;                                        // gathered X: boxes past the last segment
@@ -719,9 +734,22 @@ uint32_t idesc_bf16(int bn, int a_mn, int b_mn) {
 }
 
 // TN tiling: rows x cols of P (the swapped form when X comes in segments).
+// Segmented TN with a bias gradient: the X column that carries the ones (its
+// row of P is the bias gradient) -- the first column outside every segment
+// (a gap between or after the segments, overwritten in shared memory), or K,
+// one row past the operand, when the segments leave no gap.
+int tn_ones_row(const fb_gemm_bf16_problem &p) {
+  for (int c = 0; c < p.K; ++c) {
+    bool in = false;
+    for (int g = 0; g < p.nseg && !in; ++g) in = c >= p.seg_at[g] && c < p.seg_at[g] + p.seg_len[g];
+    if (!in) return c;
+  }
+  return p.K;
+}
+
 void tn_dims(const fb_gemm_bf16_problem &p, int &rows, int &cols) {
   if (p.nseg > 0) {
-    rows = p.K + (p.db ? 1 : 0);
+    rows = p.db ? std::max(p.K, tn_ones_row(p) + 1) : p.K;
     cols = p.N;
   } else {
     rows = p.N;
@@ -818,9 +846,9 @@ int64_t ws_floats(const fb_gemm_bf16_problem &p) {
   return (ns * (int64_t)rows * cols + 63) / 64 * 64;
 }
 
-// Tensor maps of a gathered operand: one-row boxes for the segments read by
-// row index (tile::gather4 copies), tiled boxes of `box_rows` rows for a
-// segment read row by row.
+// A gathered operand: tensor maps with `box_rows`-row boxes for the segments
+// read row by row; the segments read by row index are copied with cp.async
+// from their source pointers.
 int gather_maps(BfProb &q, const fb_bf16_row_gather &g, int box_rows) {
   q.gat = 1;
   q.g_nseg = g.nseg;
@@ -829,7 +857,11 @@ int gather_maps(BfProb &q, const fb_bf16_row_gather &g, int box_rows) {
     q.g_end[s] = g.end[s];
     q.g_rows[s] = (int)g.tab_rows[s];
     q.g_idx[s] = g.idx[s];
-    const int rc = make_map(maps[s], g.tab[s], g.tab_rows[s], g.tab_cols[s], g.tab_ld[s], g.idx[s] ? 1 : box_rows);
+    q.g_tab[s] = static_cast<const uint16_t *>(g.tab[s]);
+    q.g_ld[s] = g.tab_ld[s];
+    q.g_cols[s] = (int)g.tab_cols[s];
+    if (g.idx[s]) continue;
+    const int rc = make_map(maps[s], g.tab[s], g.tab_rows[s], g.tab_cols[s], g.tab_ld[s], box_rows);
     if (rc) return rc;
   }
   return FB_OK;
@@ -855,9 +887,9 @@ int build_prob(BfProb &q, const fb_gemm_bf16_problem &p, float *ws) {
     // columns are G's; A of the tiling is X, B is G
     q.swap = 1;
     q.a_mn = q.b_mn = 1;
-    q.ktot = p.K;
+    q.ktot = p.db ? tn_ones_row(p) : p.K;
     q.ones = p.db ? 2 : 0;
-    q.N = p.K + (p.db ? 1 : 0);
+    q.N = std::max(p.K, q.ktot + (p.db ? 1 : 0));
     q.K = p.N;
     q.Kp = p.N;
     q.bn = bn_mnmajor(q.Kp);

@@ -1,5 +1,5 @@
 // PTX wrappers shared by the tcgen05 GEMMs (gemm_tc.cu, gemm_bf16.cu):
-// mbarriers with bounded waits, 2-D TMA tile loads and row gathers, tensor-memory
+// mbarriers with bounded waits, 2-D TMA tile loads, cp.async row copies, tensor-memory
 // allocation / loads / stores, MMA completion commits, and the tensor-map
 // encoder looked up from the driver.  Every TMA load here is issued by one
 // CTA for its own shared memory.
@@ -76,19 +76,6 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
-// Four rows (y0..y3) of 64-element (128-byte) boxes at column x of a 2-D
-// tensor whose map has a one-row box (tile::gather4, sm_100a): the rows land
-// at dst, dst + 128, dst + 256, dst + 384 with the map's swizzle applied by
-// shared-memory address, as a 4-row tiled box would.
-__device__ __forceinline__ void tma_gather4(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y0, int y1,
-                                            int y2, int y3) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3)
-      : "memory");
-}
-
 // 16 bytes global -> shared (cp.async, L2-cached); only the first src_bytes
 // are read, the rest of the 16 are zero-filled.
 __device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
@@ -97,7 +84,8 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t 
 }
 
 // One more pending arrival on bar, made once every cp.async this thread has
-// issued so far has landed.
+// issued so far has landed (the pending count rises now and falls then, so
+// the thread still makes its own arrival on the barrier afterwards).
 __device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
   asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }

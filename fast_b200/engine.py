@@ -40,10 +40,11 @@ from . import ops
 
 _ALIGN = 64            # flat-buffer segments start on 256-byte boundaries
 # FB_FUSED_GATHER=1 gathers layer 0's bf16 projection rows inside the GEMM
-# (TMA tile::gather4 from the feature tables) instead of materialising them.
-# Off by default: on a B200 the row gathers deliver ~4 bytes per clock per SM,
-# so the gathered K|V projection takes 1.46 ms at config 5's hop 2 against
-# 0.61 ms for the GEMM plus 0.63 ms for the gather that writes the rows.
+# (cp.async row copies from the feature tables by the producer warp) instead
+# of materialising them.  Off by default: inside the GEMM's pipeline the row
+# copies deliver ~4 bytes per clock per SM, so the gathered K|V projection
+# takes ~1.5 ms at config 5's hop 2 against 0.61 ms for the GEMM plus 0.63 ms
+# for the gather that writes the rows.
 FUSED_GATHER_OFF = os.environ.get("FB_FUSED_GATHER", "0") != "1"
 
 

@@ -7,6 +7,7 @@ allocator.  Inputs must be fp32 (int32 for ids) with unit column stride.
 """
 import contextlib
 import ctypes
+import os
 
 import torch
 
@@ -48,14 +49,21 @@ class KernelTimer:
 TIMER = None            # set to a KernelTimer to time every kernel wrapper
 USE_TC = False          # route eligible gemm_nt calls to the tcgen05 kernel
 LAUNCHES = [0]          # kernels launched through these wrappers
+# FB_NVTX=1: each wrapper's launches inside an NVTX range named like its timer
+# entry (eager steps), so a profiler can select one group by name
+NVTX = os.environ.get("FB_NVTX", "0") == "1"
 
 
 def _launch(name, nbytes, flops, kernels, fn):
     LAUNCHES[0] += kernels
+    if NVTX:
+        torch.cuda.nvtx.range_push(name)
     if TIMER is None:
         fn()
     else:
         TIMER.run(name, nbytes, flops, fn)
+    if NVTX:
+        torch.cuda.nvtx.range_pop()
 
 
 def timed(name, fn):

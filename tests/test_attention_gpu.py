@@ -209,3 +209,52 @@ def test_fastagg_legacy_ops(cuda):
     big = torch.from_numpy(rng.integers(0, 5, 300_000).astype(np.int32)).to(cuda)
     np.testing.assert_array_equal(fastAgg.exclusive_sum(big).cpu().numpy()[1:],
                                   np.cumsum(big.cpu().numpy()))
+
+
+@pytest.mark.parametrize("bcast", [False, True])
+@pytest.mark.parametrize("kv_bf16", [False, True])
+def test_attention_device_count_launch_is_the_exact_launch(cuda, bcast, kv_bf16):
+    """Graph mode launches the attention over capacity-sized blocks with the
+    destination count and the dropout offset on the device.  Over the live
+    rows that launch must give the exact-size launch's results bit for bit
+    (agg rows past the count are zeros); the capacity rows past the count
+    hold NaN K|V rows and segments that must be ignored."""
+    from fast_b200 import ops
+    rng = np.random.default_rng(17)
+    n_dst, cap, dim, heads, drop = 500, 640, 100, 2, 0.2
+    rptr, row = _segments(rng, n_dst, 8, big=((7, 40),))
+    E = int(rptr[-1])
+    extra = np.cumsum(rng.integers(0, 9, cap - n_dst)) + E
+    rptr_cap = np.concatenate([rptr, extra]).astype(np.int32)
+    E_cap = int(rptr_cap[-1])
+    torch.manual_seed(3)
+    q = torch.randn(1 if bcast else cap, dim) * 0.5
+    kv = torch.full((E_cap, 2 * dim), float("nan"))
+    kv[:E] = torch.randn(E, 2 * dim) * 0.5
+    dagg = torch.randn(cap, dim)
+    qd, dg = q.to(cuda), dagg.to(cuda)
+    kvd = kv.to(cuda).to(torch.bfloat16).float() if kv_bf16 else kv.to(cuda)
+    nd_dev = torch.tensor([n_dst], dtype=torch.int32, device=cuda)
+    off_dev = torch.tensor([7], dtype=torch.int64, device=cuda)
+    qe = qd if bcast else qd[:n_dst]
+    rp, rpc = torch.from_numpy(rptr).to(cuda), torch.from_numpy(rptr_cap).to(cuda)
+    if kv_bf16:
+        kvb = kvd.to(torch.bfloat16)
+        agg0, att0 = ops.attn_fwd_kvbf16(qe, kvb[:E], rp, heads, 0.2, drop, 123, 7)
+        agg1, att1 = ops.attn_fwd_kvbf16(qd, kvb, rpc, heads, 0.2, drop, 123, 0, n_dst_dev=nd_dev, offset_dev=off_dev)
+        dq0, dkv0 = ops.attn_bwd_kvbf16(qe, kvb[:E], rp, att0, dg[:n_dst], heads, 0.2, drop, 123, 7)
+        dq1, dkv1 = ops.attn_bwd_kvbf16(qd, kvb, rpc, att1, dg, heads, 0.2, drop, 123, 0, n_dst_dev=nd_dev,
+                                        offset_dev=off_dev)
+    else:
+        agg0, att0 = ops.attn_fwd(qe, kvd[:E, :dim], kvd[:E, dim:], rp, heads, 0.2, drop, 123, 7)
+        agg1, att1 = ops.attn_fwd(qd, kvd[:, :dim], kvd[:, dim:], rpc, heads, 0.2, drop, 123, 0, n_dst_dev=nd_dev,
+                                  offset_dev=off_dev)
+        dq0, dkv0 = ops.attn_bwd(qe, kvd[:E, :dim], kvd[:E, dim:], rp, att0, dg[:n_dst], heads, 0.2, drop, 123, 7)
+        dq1, dkv1 = ops.attn_bwd(qd, kvd[:, :dim], kvd[:, dim:], rpc, att1, dg, heads, 0.2, drop, 123, 0,
+                                 n_dst_dev=nd_dev, offset_dev=off_dev)
+    torch.cuda.synchronize()
+    assert torch.equal(agg1[:n_dst], agg0)
+    assert int(torch.count_nonzero(agg1[n_dst:])) == 0
+    assert torch.equal(att1[:E], att0)
+    assert torch.equal(dq1[:n_dst], dq0)
+    assert torch.equal(dkv1[:E].float(), dkv0.float())

@@ -143,14 +143,18 @@ def test_gemm_bf16_nt_epilogue_adds_table_rows(cuda, c16):
     assert bool((C[m_dev:].float() == 7.0).all())
 
 
-@pytest.mark.parametrize("M,m_dev,dn", [(3000, 2777, 413), (70001, 70001, 413), (20000, 1, 413), (5000, 4321, 0)])
-def test_gemm_bf16_gathered_rows(cuda, M, m_dev, dn):
+@pytest.mark.parametrize("M,m_dev,dn,layout", [(3000, 2777, 413, "tables"), (70001, 70001, 413, "tables"),
+                                                (20000, 1, 413, "tables"), (5000, 4321, 0, "tables"),
+                                                (3000, 2777, 413, "node_rows"), (70001, 70001, 413, "node_rows")])
+def test_gemm_bf16_gathered_rows(cuda, M, m_dev, dn, layout):
     """The projection rows [h | f | t] gathered inside the GEMM (ops.RowGather:
     node rows by node id, edge rows by edge id, the time block row by row,
-    64-column segments) give, for NT and for the segmented TN with the bias
-    gradient, the products of the materialised rows within the fp32
-    accumulation bound.  Rows past the device-side count carry indices far
-    outside the tables and NaN time rows: they must reach no output."""
+    64-column segments; "node_rows": node rows by node id, then one matrix
+    [f | t] read row by row, the layer-0 weight gradient's operand) give, for
+    NT and for the segmented TN with the bias gradient, the products of the
+    materialised rows within the fp32 accumulation bound.  Rows past the
+    device-side count carry indices far outside the tables and NaN rows: they
+    must reach no output."""
     from fast_b200 import ops
     g = torch.Generator(device="cpu").manual_seed(11)
     de, dt, D2 = 186, 100, 200
@@ -172,8 +176,15 @@ def test_gemm_bf16_gathered_rows(cuda, M, m_dev, dn):
     segs, cols, wid = [], [], []
     if dn:
         segs.append((ntab, dn, nid, 448)); cols.append(dn); wid.append(448)
-    segs += [(etab, de, eid, 192), (T, dt, None, 128)]
-    cols += [de, dt]; wid += [192, 128]
+    if layout == "tables":
+        segs += [(etab, de, eid, 192), (T, dt, None, 128)]
+        cols += [de, dt]; wid += [192, 128]
+    else:
+        # [f | t] rows written by the gather: f at 0, t at 192, 296 columns
+        XF = torch.zeros(M, 296, dtype=torch.bfloat16, device=cuda)
+        XF[:m_dev, :de] = etab[eid[:m_dev].long(), :de]
+        XF[:, 192:192 + dt] = T[:, :dt]
+        segs.append((XF, 192 + dt, None, 320)); cols.append(192 + dt); wid.append(320)
     gat = ops.RowGather(segs)
     K = gat.K
     # the materialised rows (past the count: zeros) and the weights in the same column layout
