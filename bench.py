@@ -86,6 +86,13 @@ def parse():
 
 
 # ----------------------------------------------------------------------------- helpers
+# DRAM bytes over algorithmic bytes of the wrappers that can be the dominant kernel, from one ncu capture of
+# the same step on a 4 M-edge prefix (profiles/ncu_dram_traffic_bwd_dkv_dq_gather_edges4m.md); the traffic of
+# a full-size launch is the ratio times its algorithmic bytes
+NCU_TRAFFIC = {"gemm_group:bwd_dkv_dq": 1834.6 / 1873.3, "gather_time_encode": 1081.9 / 1966.7}
+NCU_TRAFFIC_SRC = "profiles/ncu_dram_traffic_bwd_dkv_dq_gather_edges4m.md"
+
+
 def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -542,6 +549,8 @@ def run_fast(args):
                              "launch gaps the single graph removes; sample_local_only = the sampler on this rank's "
                              "roots without the global batch's pointer updates")
 
+    if world > 1 and hasattr(tr, "release"):
+        tr.release()                       # graphs holding NCCL calls go before the process group
     if rank != 0:
         if world > 1:
             dist.barrier()
@@ -584,6 +593,11 @@ def run_fast(args):
                             "bytes at the copy bandwidth take longer than its flops at the bf16 peak; tensor: "
                             "%.1f TFLOP/s, %.3f of %s" % (r["flops"] / r["bytes"], pk["tf"] * 1e3 / pk["hbm"], tfs,
                                                           tfs / pk["tf"], pk["tf"]))
+    if bf16 and name in NCU_TRAFFIC:
+        roof["traffic"] = int(NCU_TRAFFIC[name] * r["bytes"] / r["launches"])
+        roof["traffic_unit"] = "bytes per launch"
+        roof["traffic_source"] = ("dram__bytes_read.sum + dram__bytes_write.sum over the algorithmic bytes of the "
+                                  "same launches (%s), times this launch's algorithmic bytes" % NCU_TRAFFIC_SRC)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,

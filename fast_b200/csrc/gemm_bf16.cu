@@ -145,6 +145,7 @@ struct BfProb {
 struct BfArgs {
   BfProb p[kMaxBf];
   int n;
+  int gat_any;                              // a problem has a gathered operand (cp.async row copies)
   int red_start[kMaxBf + 1];
   int32_t *err;
 };
@@ -273,7 +274,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(full + s, 32);                     // the producer warp's lanes
+      // with gathered rows every producer lane arrives (after its copies), else lane 0
+      mbar_init(full + s, a.gat_any ? 32 : 1);
       mbar_init(empty + s, 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -403,10 +405,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
             }
           if (any) cp_async_arrive(full + s);
         }
-        // every lane arrives on the stage's barrier (lane 0 with the TMA byte
-        // count), each after its cp.async arrival: the phase completes when the
-        // tiled copies and every lane's gathered copies have landed
-        if (lane != 0) mbar_arrive(full + s);
+        // with gathered rows in the launch every lane arrives on the stage's
+        // barrier (lane 0 with the TMA byte count), each after its cp.async
+        // arrival: the phase completes when the tiled copies and every lane's
+        // gathered copies have landed
+        if (a.gat_any && lane != 0) mbar_arrive(full + s);
         if (lane == 0) {
           mbar_expect_tx(full + s, tiled_a ? bytes : bytes - kAOp);
           if (gat && tn) {
@@ -971,6 +974,7 @@ int launch_group(const std::vector<const fb_gemm_bf16_problem *> &probs, const s
     const int rc = build_prob(q, *probs[i], ws[i]);
     if (rc) return rc;
     a.red_start[a.n] = red;
+    a.gat_any |= q.gat;
     if (q.kind == kTN) {
       items += (int64_t)q.rt * q.nt * fb::tn_parts(q.M, kTnRowsMin, q.max_splits);
       red += (int)(((int64_t)q.N * q.Kp + 255) / 256);

@@ -706,7 +706,10 @@ int sample_impl(fb_sampler *s, const int32_t *roots, const float *root_ts, int64
     const float *ut = t0;
     const int32_t *uR = nullptr;
     int64_t uR_host = n_roots, ucap = cr[l * nh];
-    if (global) {
+    if (!use_ptr) {
+      // no pointer update in this layer (and, sharded, no global block of the layer above)
+    } else if (global) {
+      // a layer l > 0 that uses the pointers has the global block of layer l - 1
       ur = g_roots; ut = g_ts; uR_host = n_global; ucap = gcr[l * nh];
       if (l > 0) {
         ur = s->gblocks[l - 1].nodes; ut = s->gblocks[l - 1].ts; uR = s->gdims + 8 * (l - 1) + 3;

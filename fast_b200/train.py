@@ -631,6 +631,16 @@ class GraphTrainer(Trainer):
         self._replay()
         return self.loss_buf
 
+    def release(self):
+        """Drops the captured graphs after the device has finished with them.
+        A graph that holds NCCL calls must be released before the process
+        group is destroyed, or the process waits on exit for good."""
+        torch.cuda.synchronize()
+        self.g_main = self.g_opt = None
+        import gc
+        gc.collect()
+        torch.cuda.synchronize()
+
     def step_host_pipelined(self, roots_np, ts_np, global_roots_np=None, global_ts_np=None, e0=None):
         """step_host without waiting for this step: the inputs go through pinned
         slot i % 2, the loss comes back into that slot's pinned word, and the

@@ -64,6 +64,12 @@ def test_graph_replay_is_the_static_eager_step(cuda, mode):
 @pytest.mark.parametrize("fused", [True, False])
 @pytest.mark.parametrize("strategy", ["recent", "uniform"])
 def test_graph_trainer_matches_eager_trainer(cuda, strategy, fused):
+    """The graph trainer (capacity-sized blocks, counts on the device) trains
+    like the eager one (exact-sized blocks), loss for loss.  The two round
+    differently -- the products of capacity- and exact-sized blocks split their
+    sums differently -- so the ReLU inputs are moved off the kink (biases of
+    w_out and of the predictor's two projections + 4): a pre-activation within
+    rounding of 0 would otherwise switch a whole gradient term between them."""
     from fast_b200.train import GraphTrainer, Trainer
     cfg, g, ef, sp, mp, gp, tp = _setup(cuda, 2e3, strategy)
     if fused:
@@ -72,6 +78,11 @@ def test_graph_trainer_matches_eager_trainer(cuda, strategy, fused):
     eager.opt = torch.optim.SGD(eager.model.parameters(), lr=tp["lr"])
     graph = GraphTrainer(g, None, ef, dict(sp), mp, dict(gp), tp, cuda, batch=cfg.batch, seed=5, sampler_seed=77,
                          optimizer="sgd", fused=fused)
+    with torch.no_grad():
+        for tr in (eager, graph):
+            for name, p in tr.model.named_parameters():
+                if name.endswith(("w_out.bias", "src_fc.bias", "dst_fc.bias")):
+                    p += 4.0
     B = cfg.batch
     starts = [10000 + i * B for i in range(7)]
     graph.load_device_roots(starts[0], starts[0] + B)
