@@ -203,10 +203,13 @@ class FusedStep:
         self._side_pending = True
 
     def _in_side(self):
-        """Context for launches that must follow the side stream's work (a
-        gradient bucket's all-reduce, issued from the stream that last wrote it)."""
+        """Context for launches that must follow everything enqueued so far on
+        both streams (a gradient bucket's all-reduce, whose gradients the
+        current stream and the side stream wrote): the side stream first
+        waits for the current one."""
         import contextlib
         if SIDE_STREAMS and getattr(self, "_side_pending", False):
+            self._side_stream.wait_stream(torch.cuda.current_stream())
             return torch.cuda.stream(self._side_stream)
         return contextlib.nullcontext()
 
