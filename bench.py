@@ -875,6 +875,13 @@ def run_bf16_suite(args):
           2 * E * 2 * D + gnr.read_bytes(E) + 4 * 2 * D * (dn + de + dt_),
           2 * E * 2 * D * (dn + de + dt_ + 1), lambda: ops.gemm_bf16_group(tnr),
           "M=%d, N=%d, K=%d+%d+%d+1" % (E, 2 * D, dn, de, dt_))
+    # the weight gradient over the [f | cos] rows alone (the node block's gradient taken another way)
+    tnf = [dict(kind=ops.TN, A=dkv, B=XF[:, :ops.pad8(de) + dt_], out=gW[:, dn:], accumulate=True, db=gb,
+                segs=[(0, de, 0), (ops.pad8(de), dt_, de)])]
+    timed("k_bf_group (K|V weight + bias gradient, TN over [f | cos] rows only)",
+          2 * E * 2 * D + 2 * E * (ops.pad8(de) + dt_) + 4 * 2 * D * (de + dt_),
+          2 * E * 2 * D * (de + dt_ + 1), lambda: ops.gemm_bf16_group(tnf),
+          "M=%d, N=%d, K=%d+%d+1" % (E, 2 * D, de, dt_))
     # the same TN operand with the node block materialised: both segments read row by row by TMA
     XH = torch.empty(E, 448, device=dev, dtype=torch.bfloat16)
     XH[:, :416] = ntab[nid.long()]

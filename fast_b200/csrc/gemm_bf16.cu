@@ -83,7 +83,7 @@ static_assert(smem_bytes<false>() <= 232448 && smem_bytes<true>() <= 232448,
               "shared memory of k_bf_group exceeds 227 KB");
 constexpr int kTmemCols = 512;               // two accumulators of up to 256 columns
 constexpr int kAccStride = 256;
-constexpr int64_t kTnRowsMin = 512;          // TN: rows per split, at least
+constexpr int64_t kTnRowsMin = 512;          // TN: rows per split, at least (FB_TN_ROWS_MIN overrides)
 constexpr int kWarpProducer = 0, kWarpMma = 1, kWarpEpi0 = 4;
 
 constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;
@@ -124,6 +124,7 @@ struct BfProb {
   int swap, ktot, nseg, seg_at[3], seg_len[3], seg_to[3];
   int c_bf16;                // NT / NN: C holds bf16 (round to nearest even), written, not accumulated
   int wide;                  // segmented TN in a wide launch: items of 2 BM rows (X columns)
+  int rows_min;                            // TN: rows per split, at least
   int gat, g_nseg, g_end[3], g_rows[3];   // A of the tiling gathered (see fb_bf16_row_gather)
   const int32_t *g_idx[3];
   const uint16_t *g_tab[3];                 // gathered segments' sources (16-byte cp.async copies)
@@ -304,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
       s_m[p] = M;
       s_start[p] = acc;
       if (q.kind == kTN) {
-        const int ns = fb::tn_parts(M, kTnRowsMin, q.max_splits);
+        const int ns = fb::tn_parts(M, q.rows_min, q.max_splits);
         s_per[p] = ((M + ns - 1) / ns + BK - 1) / BK * BK;
         acc += q.rt * q.nt * ns;
       } else {
@@ -439,19 +440,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_bf_group(const __grid_constant_
         ++g;
         return true;
       };
-      const bool ring = gat && tn;
-      for (int j = 0; j < it.nk; j += 2) {
-        if (!slice(j, nxa)) {
-          stop = true;
-          break;
-        }
-        if (ring) load_nx(j + 2, nxa);
-        if (j + 1 < it.nk) {
-          if (!slice(j + 1, nxb)) {
+      if (!(gat && tn)) {
+        for (int j = 0; j < it.nk; ++j)
+          if (!slice(j, nxa)) {
             stop = true;
             break;
           }
-          if (ring) load_nx(j + 3, nxb);
+      } else {
+        for (int j = 0; j < it.nk; j += 2) {
+          if (!slice(j, nxa)) {
+            stop = true;
+            break;
+          }
+          load_nx(j + 2, nxa);
+          if (j + 1 < it.nk) {
+            if (!slice(j + 1, nxb)) {
+              stop = true;
+              break;
+            }
+            load_nx(j + 3, nxb);
+          }
         }
       }
     }
@@ -658,7 +666,7 @@ __global__ void k_bf_reduce(const __grid_constant__ BfArgs a) {
   if (i >= (int64_t)q.N * q.Kp) return;
   int64_t M = q.M_dev ? min((int64_t)(*q.M_dev), q.M) : q.M;
   M = max(M, (int64_t)0);
-  const int ns = fb::tn_parts(M, kTnRowsMin, q.max_splits);
+  const int ns = fb::tn_parts(M, q.rows_min, q.max_splits);
   const int n = (int)(i / q.Kp), k = (int)(i % q.Kp);
   const int64_t stride = (int64_t)q.N * q.Kp;
   const float *part = q.P + i;
@@ -766,17 +774,35 @@ bool tn_wide(const fb_gemm_bf16_problem &p) {
   return !off && p.kind == FB_GEMM_TN && p.nseg > 0 && !p.gather;
 }
 
+int tn_rows_min() {
+  static const int v = [] {
+    const char *e = getenv("FB_TN_ROWS_MIN");
+    const int x = e ? atoi(e) : 0;
+    return x >= 64 ? x : (int)kTnRowsMin;
+  }();
+  return v;
+}
+
+int tn_split_waves() {
+  static const int v = [] {
+    const char *e = getenv("FB_TN_SPLIT_WAVES");
+    const int x = e ? atoi(e) : 0;
+    return x >= 1 && x <= 8 ? x : 1;
+  }();
+  return v;
+}
+
 int tn_splits_max(const fb_gemm_bf16_problem &p) {
   int rows, cols;
   tn_dims(p, rows, cols);
   const int tr = tn_wide(p) ? 2 * BM : BM;
   const int tiles = ((rows + tr - 1) / tr) * ((cols + bn_mnmajor(cols) - 1) / bn_mnmajor(cols));
-  return std::max(1, num_sms() / std::max(tiles, 1));
+  return std::max(1, tn_split_waves() * num_sms() / std::max(tiles, 1));
 }
 
 int64_t slices_per_item(const fb_gemm_bf16_problem &p) {
   if (p.kind == FB_GEMM_TN) {
-    const int ns = fb::tn_parts(p.M, kTnRowsMin, tn_splits_max(p));
+    const int ns = fb::tn_parts(p.M, tn_rows_min(), tn_splits_max(p));
     return ((p.M + ns - 1) / ns + BK - 1) / BK;
   }
   const int k1 = (p.A2 && p.k1 < p.K) ? p.k1 : p.K;
@@ -845,7 +871,7 @@ int64_t ws_floats(const fb_gemm_bf16_problem &p) {
   if (p.kind != FB_GEMM_TN || p.M < 1) return 0;
   int rows, cols;
   tn_dims(p, rows, cols);
-  const int64_t ns = fb::tn_parts(p.M, kTnRowsMin, tn_splits_max(p));
+  const int64_t ns = fb::tn_parts(p.M, tn_rows_min(), tn_splits_max(p));
   return (ns * (int64_t)rows * cols + 63) / 64 * 64;
 }
 
@@ -873,6 +899,7 @@ int gather_maps(BfProb &q, const fb_bf16_row_gather &g, int box_rows) {
 int build_prob(BfProb &q, const fb_gemm_bf16_problem &p, float *ws) {
   std::memset(&q, 0, sizeof(q));
   q.kind = p.kind;
+  q.rows_min = tn_rows_min();
   q.add = p.add;
   q.add_idx = p.add_idx;
   q.ld_add = p.ld_add;
@@ -976,7 +1003,7 @@ int launch_group(const std::vector<const fb_gemm_bf16_problem *> &probs, const s
     a.red_start[a.n] = red;
     a.gat_any |= q.gat;
     if (q.kind == kTN) {
-      items += (int64_t)q.rt * q.nt * fb::tn_parts(q.M, kTnRowsMin, q.max_splits);
+      items += (int64_t)q.rt * q.nt * fb::tn_parts(q.M, q.rows_min, q.max_splits);
       red += (int)(((int64_t)q.N * q.Kp + 255) / 256);
     } else {
       items += (q.M + BM - 1) / BM * q.nt;
