@@ -202,6 +202,28 @@ class FusedStep:
             fn()
         self._side_pending = True
 
+    def _side_record(self, fn, *uses):
+        """_side, returning an event recorded on the side stream after fn's
+        launches (None when fn ran inline): a later launch on the current
+        stream that needs fn's results waits on it (_await) instead of on
+        the whole side stream."""
+        self._side(fn, *uses)
+        if not getattr(self, "_side_pending", False) or not SIDE_STREAMS or ops.TIMER is not None:
+            return None
+        ev = torch.cuda.Event()
+        ev.record(self._side_stream)
+        return ev
+
+    @staticmethod
+    def _await(ev):
+        if ev is not None:
+            torch.cuda.current_stream().wait_event(ev)
+
+    def _await_weights(self):
+        """The current stream waits once per step for the bf16 weight copies."""
+        self._await(getattr(self, "_weights_ev", None))
+        self._weights_ev = None
+
     def _in_side(self):
         """Context for launches that must follow everything enqueued so far on
         both streams (a gradient bucket's all-reduce, whose gradients the
@@ -282,6 +304,14 @@ class FusedStep:
         # K|V stored as bf16 rows: the projection's bf16 output is the attention's input
         KV = torch.empty(E, 2 * D, device=dev, dtype=torch.bfloat16)
         gat = self._layer0_gather(l, blk, h, node_table, edge_table, wv, bt, dev)
+        P = p_ev = None
+        if gat is None and self._node_product(l, h, node_table, E):
+            # the node product P = table . W_h^T on the side stream (after the
+            # weight cast), beside this layer's gathers
+            P = torch.empty(node_table.shape[0], 2 * D, device=dev)
+            p_ev = self._side_record(
+                lambda: ops.gemm_bf16_group([dict(kind=ops.NT, A=node_table[:, :dn], B=lp.W_kv_bf[:, :dn], out=P)],
+                                            name="gemm_group:node_product"), P, node_table)
         if gat is not None:
             # the projection rows [h | f | cos] are gathered inside the GEMM:
             # only the time encoding is written, the tables are read in place
@@ -292,27 +322,28 @@ class FusedStep:
                                                 dt=blk.dt_edges, w=wv, b=bt, device=dev, n_rows_dev=E_dev, dn=dn,
                                                 de=de, **hsrc)
             probs = [dict(kind=ops.NT, A=X[:, :kx], B=lp.W_kv_bf[:, :kx], bias=lp.b_kv, out=KV, M_dev=E_dev)]
-            if self._node_product(l, h, node_table, E):
+            if P is not None:
                 # the node-feature block of every K|V row is the product of one of
-                # the table's few rows: P = table . W_h^T once per table row, then
-                # the rows' product runs over their [f | time] columns only and adds
-                # P[source node] in its epilogue
+                # the table's few rows (P, above); the rows' product runs over their
+                # [f | time] columns only and adds P[source node] in its epilogue
                 f_at = lp.kv_segs[1][0]
-                P = torch.empty(node_table.shape[0], 2 * D, device=dev)
-                probs = [dict(kind=ops.NT, A=node_table[:, :dn], B=lp.W_kv_bf[:, :dn], out=P)]
+                probs = []
                 kv_prob = dict(kind=ops.NT, A=X[:, f_at:kx], B=lp.W_kv_bf[:, f_at:kx], bias=lp.b_kv, out=KV,
                                M_dev=E_dev, add=P, add_idx=blk.src_nodes)
         if dn > 0:
             Qin, kq = ops.gather_time_encode_bf16(nd, w=wv, b=bt, device=dev, n_rows_dev=nd_dev, dn=dn, **hdst)
             Q = torch.empty(nd, D, device=dev)
             probs.append(dict(kind=ops.NT, A=Qin[:, :kq], B=lp.W_q_bf[:, :kq], bias=L.w_q.bias, out=Q, M_dev=nd_dev))
+            self._await_weights()
             ops.gemm_bf16_group(probs, name="gemm_group:kv_q")
-            if gat is None and X is not None and probs[0]["out"] is not KV:
+            if P is not None:
+                self._await(p_ev)
                 ops.gemm_bf16_group([kv_prob], name="gemm_group:kv_rows")
         else:
             # one shared Q input row cos(b_t): its product stays fp32
             Qin = ops.gather_time_encode(1, w=wv, b=bt, device=dev)
             Q = torch.empty(1, D, device=dev)
+            self._await_weights()
             ops.gemm_bf16_group(probs, name="gemm_group:kv_q")
             ops.gemm_group([dict(kind=ops.NT, A=Qin, B=L.w_q.weight, bias=L.w_q.bias, out=Q)], name="gemm_group:q1")
         p_att = L.att_dropout_p if training else 0.0
@@ -744,8 +775,11 @@ class FusedStep:
             h, mem_st = self._memory_fwd(mfgs[0], mailbox)
             self.last_memory = h
         bf16 = self.precision == "bf16"
+        self._weights_ev = None
         if bf16:
-            ops.cast_bf16(self.cast_jobs, name="cast_bf16:weights")
+            # the bf16 weight copies on the side stream, beside layer 0's gathers;
+            # the first product that reads them waits for them
+            self._weights_ev = self._side_record(lambda: ops.cast_bf16(self.cast_jobs, name="cast_bf16:weights"))
         fwd = self._layer_fwd_bf16 if bf16 else self._layer_fwd
         bwd = self._layer_bwd_bf16 if bf16 else self._layer_bwd
         for l, blk in enumerate(mfgs):
