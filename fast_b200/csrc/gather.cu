@@ -10,16 +10,17 @@
 // Rounding: torch's CPU Linear(1, d) produces w*dt + b with one rounding
 // (a fused multiply-add); with dt up to ~1e8 the argument of cos is large and
 // a second rounding changes the feature by O(1), so the kernel uses fmaf.
-// The backward needs sin of fp32 arguments of 1e5..1e8 radians (real
+// The backward needs sin of fp32 arguments up to 1e8 radians and beyond (real
 // timestamps).  The library's double sin handles them exactly but is bound by
 // the fp64 rate (~100 operations per call).  sin_big() reduces the argument
-// by pi/2 in integer arithmetic instead -- the float's 24-bit mantissa times
-// a 64-bit fixed-point 2/pi gives the quadrant and 32 fraction bits exactly,
-// the idea of Payne & Hanek ("Radian reduction for trigonometric functions",
-// SIGNUM Newsletter 18, 1983) with one word of 2/pi, enough below 2^28 -- and
-// evaluates the Taylor series of sin and cos on |r| <= pi/4 in fp32 (degrees
-// 9 and 10: truncation below 2e-9).  The forward keeps cosf, which measured
-// faster in its wide gather.
+// by pi/2 in fp32 with a three-float split of pi/2 below 2^22 (Cody & Waite),
+// in integer arithmetic above (the float's 24-bit mantissa times a 64-bit
+// fixed-point 2/pi gives the quadrant and 32 fraction bits exactly, the idea
+// of Payne & Hanek, "Radian reduction for trigonometric functions", SIGNUM
+// Newsletter 18, 1983, with one word of 2/pi, enough below 2^28), and
+// evaluates the Taylor series of sin and cos on |r| <= 0.96 in fp32 (degrees
+// 11 and 10: truncation below 1.3e-9).  The forward keeps cosf, which
+// measured faster in its wide gather.
 #include <cuda_bf16.h>
 #include "runtime.cuh"
 
@@ -274,46 +275,61 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode_bf16(Ga
 // round(2/pi * 2^64)
 constexpr uint64_t kTwoOverPiQ64 = 0xa2f9836e4e44152aull;
 
-// sin(x) for a float x: |x| = (k + f) pi/2 with k an integer and |f| <= 1/2,
-// then +-sin(r) or +-cos(r), r = f pi/2, by the quadrant k mod 4 (the
-// library's double sin from 2^28 on).  Below 2^22 the reduction is two
-// double fmas; from there the fixed-point product below.
-__device__ __forceinline__ float sin_big(float x) {
-  const float ax = fabsf(x);
-  if (ax >= 268435456.f) return (float)sin((double)x);
-  float r;
-  int q = 0;
-  if (ax < 0.78539816f) {
-    r = ax;
-  } else if (ax < 4194304.f) {
-    // |x| < 2^22: Cody & Waite's reduction with pi/2 split in two doubles, a
-    // 30-bit head (k * head is exact for k < 2^23) and a 53-bit tail;
-    // |pi/2 - head - tail| < 2e-26, so |r| is off by < 1e-19
-    const double xd = (double)ax;
-    const double kd = rint(xd * 0x1.45f306dc9c883p-1);               // nearest multiple of pi/2
-    const double rd = fma(-kd, -0x1.de973dcb3b39ap-31, fma(-kd, 0x1.921fb548p+0, xd));
-    r = (float)rd;
-    q = (int)((long long)kd & 3);
-  } else {
-    const uint32_t bits = __float_as_uint(ax);
-    const int e = (int)(bits >> 23) - 127;             // -1 .. 27
-    const uint64_t m = (bits & 0x7FFFFFu) | 0x800000u;  // |x| = m 2^(e-23)
-    const uint64_t lo = m * kTwoOverPiQ64, hi = __umul64hi(m, kTwoOverPiQ64);
-    const int s = 87 - e;                               // |x| 2/pi = (hi:lo) 2^-s, s in 60 .. 88
-    q = (int)((s >= 64 ? hi >> (s - 64) : (lo >> s) | (hi << (64 - s))) & 3u);
-    const int sh = s - 32;                              // 28 .. 56
-    const int32_t fb = (int32_t)(uint32_t)((lo >> sh) | (hi << (64 - sh)));   // fraction, 32 bits
-    if (fb < 0) q = (q + 1) & 3;                        // fraction >= 1/2: the next quadrant
-    r = (float)fb * 0x1.921fb6p-32f;                     // pi/2 * 2^-32
-  }
+// +-sin(r) or +-cos(r) for the quadrant q (mod 4) of an argument reduced to
+// r, |r| <= 0.96: sin(r + q pi/2).  Taylor series of sin and cos (degrees 11
+// and 10, coefficients 1/n!; truncation below 1.3e-9 on that interval).
+__device__ __forceinline__ float sin_quadrant(float r, int q) {
   const float r2 = r * r;
-  // Taylor coefficients 1/n!, alternating
-  const float sr = fmaf(r2 * r, fmaf(r2, fmaf(r2, fmaf(r2, 1.f / 362880.f, -1.f / 5040.f), 1.f / 120.f), -1.f / 6.f), r);
+  const float sr = fmaf(r2 * r, fmaf(r2, fmaf(r2, fmaf(r2, fmaf(r2, -1.f / 39916800.f, 1.f / 362880.f), -1.f / 5040.f),
+                                                1.f / 120.f), -1.f / 6.f), r);
   const float cr = fmaf(r2, fmaf(r2, fmaf(r2, fmaf(r2, fmaf(r2, -1.f / 3628800.f, 1.f / 40320.f), -1.f / 720.f),
                                                 1.f / 24.f), -0.5f), 1.f);
   const float v = (q & 1) ? cr : sr;
-  const float sv = (q & 2) ? -v : v;
+  return (q & 2) ? -v : v;
+}
+
+// sin(x) for |x| >= 2^22: |x| = (k + f) pi/2 with k an integer and |f| <= 1/2,
+// r = f pi/2, from the fixed-point product below; from 2^28 on the library's
+// double sin.  Kept out of line: arguments this large are rare (w dt beyond
+// 4e6 rad).
+__device__ __noinline__ float sin_far(float x) {
+  const float ax = fabsf(x);
+  if (ax >= 268435456.f) return (float)sin((double)x);
+  const uint32_t bits = __float_as_uint(ax);
+  const int e = (int)(bits >> 23) - 127;             // 22 .. 27
+  const uint64_t m = (bits & 0x7FFFFFu) | 0x800000u;  // |x| = m 2^(e-23)
+  const uint64_t lo = m * kTwoOverPiQ64, hi = __umul64hi(m, kTwoOverPiQ64);
+  const int s = 87 - e;                               // |x| 2/pi = (hi:lo) 2^-s, s in 60 .. 65
+  int q = (int)((s >= 64 ? hi >> (s - 64) : (lo >> s) | (hi << (64 - s))) & 3u);
+  const int sh = s - 32;                              // 28 .. 33
+  const int32_t fb = (int32_t)(uint32_t)((lo >> sh) | (hi << (64 - sh)));   // fraction, 32 bits
+  if (fb < 0) q = (q + 1) & 3;                        // fraction >= 1/2: the next quadrant
+  const float r = (float)((double)fb * 0x1.921fb54442d18p-32);   // pi/2 * 2^-32, one rounding to float
+  const float sv = sin_quadrant(r, q);
   return x < 0.f ? -sv : sv;
+}
+
+// sin(x) for a float x, to about 2 ulp of the double result.  |x| < 2^22 (every
+// argument of a time encoding but the rare far ones): Cody & Waite's reduction
+// in fp32 ("Software Manual for the Elementary Functions", 1980), with pi/2
+// split into three floats C1 = fl(pi/2), C2 = fl(pi/2 - C1), C3 = fl(pi/2 -
+// C1 - C2) (computed from Machin's series; |pi/2 - C1 - C2 - C3| < 1.1e-23).
+// k = rint(x fl(2/pi)) comes from adding 1.5 2^23 (the float's last mantissa
+// bits are then k, so k mod 4 is read from them); fl(2/pi) is 2.6e-8 below
+// 2/pi, so |x 2/pi - k| <= 0.61 and |r| <= 0.96.  The first fma x - k C1 is
+// exact (for |x| >= 1, x and k C1 are multiples of 2^-23 and the result is
+// below 2 in magnitude; for |x| < 1, k is 0 or +-1 and Sterbenz's lemma
+// applies), the next two round once each, so r carries about one ulp of its
+// own plus 2^-45.  No double arithmetic, no conversion, and no divergence
+// between lanes of a warp whose arguments differ in size.
+__device__ __forceinline__ float sin_big(float x) {
+  if (!(fabsf(x) < 4194304.f)) return isnan(x) ? x : sin_far(x);
+  const float s = fmaf(x, 0x1.45f306p-1f, 12582912.f);   // 1.5 2^23 + k
+  const float k = __fsub_rn(s, 12582912.f);
+  float r = fmaf(-k, 0x1.921fb6p+0f, x);
+  r = fmaf(-k, -0x1.777a5cp-25f, r);
+  r = fmaf(-k, -0x1.ee59dap-50f, r);
+  return sin_quadrant(r, __float_as_int(s));
 }
 
 constexpr int64_t kTeRowsPerCta = 64;
@@ -440,81 +456,103 @@ __global__ void __launch_bounds__(1024) k_te_bwd_rows(const T *__restrict__ g, i
   }
 }
 
-// Stage 1 for even dtime <= 512 with pair-aligned rows: as k_te_bwd_rows, but
-// thread t owns the column pair (2 (t % (dtime/2)), +1) -- one 4- or 8-byte
-// load of g and one load of dt per two elements -- and the row groups' sums
-// are combined in the same fixed order.
-__device__ __forceinline__ float2 te_g2(const float *p) { return __ldg(reinterpret_cast<const float2 *>(p)); }
-__device__ __forceinline__ float2 te_g2(const uint16_t *p) {
+// Stage 1 for dtime <= 512 with V-column-aligned rows (V = 2 or 4): as
+// k_te_bwd_rows, but thread t owns the V adjacent columns V (t % (dtime/V)) ..
+// +V-1 -- one 4- to 16-byte load of g and one load of dt per V elements -- in
+// CTAs of at most 512 threads (two per SM), and the row groups' sums are
+// combined in a fixed order.
+__device__ __forceinline__ void te_gv(const float *p, float (&o)[2]) {
+  const float2 v = __ldg(reinterpret_cast<const float2 *>(p));
+  o[0] = v.x, o[1] = v.y;
+}
+__device__ __forceinline__ void te_gv(const float *p, float (&o)[4]) {
+  const float4 v = __ldg(reinterpret_cast<const float4 *>(p));
+  o[0] = v.x, o[1] = v.y, o[2] = v.z, o[3] = v.w;
+}
+__device__ __forceinline__ void te_gv(const uint16_t *p, float (&o)[2]) {
   const uint32_t u = __ldg(reinterpret_cast<const uint32_t *>(p));
-  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+  o[0] = __uint_as_float(u << 16), o[1] = __uint_as_float(u & 0xFFFF0000u);
+}
+__device__ __forceinline__ void te_gv(const uint16_t *p, float (&o)[4]) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2 *>(p));
+  o[0] = __uint_as_float(u.x << 16), o[1] = __uint_as_float(u.x & 0xFFFF0000u);
+  o[2] = __uint_as_float(u.y << 16), o[3] = __uint_as_float(u.y & 0xFFFF0000u);
 }
 
-template <typename T>
-__global__ void __launch_bounds__(512) k_te_bwd_pairs(const T *__restrict__ g, int64_t ldg,
-                                                      const float *__restrict__ dt, const float *__restrict__ w,
-                                                      const float *__restrict__ b, int dtime, int groups,
-                                                      int64_t n_rows, const int32_t *n_rows_dev,
-                                                      float *__restrict__ part) {
+constexpr int kTeVecThreads = 512;
+
+template <typename T, int V>
+__global__ void __launch_bounds__(kTeVecThreads, 2) k_te_bwd_vec(const T *__restrict__ g, int64_t ldg,
+                                                                 const float *__restrict__ dt,
+                                                                 const float *__restrict__ w,
+                                                                 const float *__restrict__ b, int dtime, int groups,
+                                                                 int64_t n_rows, const int32_t *n_rows_dev,
+                                                                 float *__restrict__ part) {
   fb::pdl_enter();
-  __shared__ float sw_s[kTeGroups * kTeColsMax], sb_s[kTeGroups * kTeColsMax];
+  // groups * dtime / V <= kTeVecThreads
+  __shared__ float sw_s[kTeVecThreads * V], sb_s[kTeVecThreads * V];
   const int64_t n = n_rows_dev ? min((int64_t)(*n_rows_dev), n_rows) : n_rows;
   const int parts = fb::split_parts(n, kTeRowsPerCta, kTeMaxParts);
   if ((int)blockIdx.y >= parts) return;
-  const int half = dtime >> 1;
-  const int c = 2 * (threadIdx.x % half), grp = threadIdx.x / half;
+  const int nt = dtime / V;
+  const int c = V * (threadIdx.x % nt), grp = threadIdx.x / nt;
   const bool live = grp < groups;
   const int64_t per = (n + parts - 1) / parts;
   const int64_t r0 = (int64_t)blockIdx.y * per;
   const int64_t r1 = min(n, r0 + per);
-  float sw0 = 0.f, sb0 = 0.f, sw1 = 0.f, sb1 = 0.f;
+  float sw[V], sb[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) sw[v] = sb[v] = 0.f;
   if (live) {
-    const float w0 = __ldg(w + c), b0 = __ldg(b + c), w1 = __ldg(w + c + 1), b1 = __ldg(b + c + 1);
+    float wv[V], bv[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) wv[v] = __ldg(w + c + v), bv[v] = __ldg(b + c + v);
     const int G = groups;
     const T *gp = g + (r0 + grp) * ldg + c;
     const int64_t gstep = (int64_t)G * ldg;
     int64_t r = r0 + grp;
-    for (; r + 7 * G < r1; r += 8 * G, gp += 8 * gstep) {
-      float tv[8];
-      float2 gv[8];
+    for (; r + 3 * G < r1; r += 4 * G, gp += 4 * gstep) {
+      float tv[4], gv[4][V];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < 4; ++u) {
         tv[u] = __ldg(dt + r + u * G);
-        gv[u] = te_g2(gp + u * gstep);
+        te_gv(gp + u * gstep, gv[u]);
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float g0 = -sin_big(fmaf(tv[u], w0, b0)) * gv[u].x;
-        const float g1 = -sin_big(fmaf(tv[u], w1, b1)) * gv[u].y;
-        sw0 = fmaf(g0, tv[u], sw0);
-        sb0 += g0;
-        sw1 = fmaf(g1, tv[u], sw1);
-        sb1 += g1;
+      for (int u = 0; u < 4; ++u) {
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          const float gs = -sin_big(fmaf(tv[u], wv[v], bv[v])) * gv[u][v];
+          sw[v] = fmaf(gs, tv[u], sw[v]);
+          sb[v] += gs;
+        }
       }
     }
     for (; r < r1; r += G, gp += gstep) {
       const float t = __ldg(dt + r);
-      const float2 gg = te_g2(gp);
-      const float g0 = -sin_big(fmaf(t, w0, b0)) * gg.x;
-      const float g1 = -sin_big(fmaf(t, w1, b1)) * gg.y;
-      sw0 = fmaf(g0, t, sw0);
-      sb0 += g0;
-      sw1 = fmaf(g1, t, sw1);
-      sb1 += g1;
+      float gg[V];
+      te_gv(gp, gg);
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        const float gs = -sin_big(fmaf(t, wv[v], bv[v])) * gg[v];
+        sw[v] = fmaf(gs, t, sw[v]);
+        sb[v] += gs;
+      }
     }
-    sw_s[grp * dtime + c] = sw0;
-    sb_s[grp * dtime + c] = sb0;
-    sw_s[grp * dtime + c + 1] = sw1;
-    sb_s[grp * dtime + c + 1] = sb1;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      sw_s[grp * dtime + c + v] = sw[v];
+      sb_s[grp * dtime + c + v] = sb[v];
+    }
   }
   __syncthreads();
   if (grp == 0) {
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
+    for (int v = 0; v < V; ++v) {
       float aw = 0.f, ab = 0.f;
-      for (int i = 0; i < groups; ++i) { aw += sw_s[i * dtime + c + k]; ab += sb_s[i * dtime + c + k]; }
-      part[((int64_t)blockIdx.y * 2 + 0) * dtime + c + k] = aw;
-      part[((int64_t)blockIdx.y * 2 + 1) * dtime + c + k] = ab;
+      for (int i = 0; i < groups; ++i) { aw += sw_s[i * dtime + c + v]; ab += sb_s[i * dtime + c + v]; }
+      part[((int64_t)blockIdx.y * 2 + 0) * dtime + c + v] = aw;
+      part[((int64_t)blockIdx.y * 2 + 1) * dtime + c + v] = ab;
     }
   }
 }
@@ -623,19 +661,29 @@ int te_bwd(const T *g, int64_t ldg, const float *dt, const float *w, const float
   // take the partition from the true count
   const int parts = te_parts(n_rows);
   float *part = static_cast<float *>(ws);
-  // column pairs (FB_TE_BWD_PAIRS=1): measured slower than one column per
-  // thread on a B200 (298 against 214 us per config-5 step), so opt-in
-  static const bool pairs = getenv("FB_TE_BWD_PAIRS") != nullptr;
-  const size_t pair_bytes = sizeof(T) * 2;
-  if (pairs && dtime % 2 == 0 && dtime <= kTeColsMax && ldg % 2 == 0 &&
-      (reinterpret_cast<uintptr_t>(g) % pair_bytes) == 0) {
-    // groups of dtime / 2 threads (a column pair each): as many as fit 512 threads, at most kTeGroups
-    const int half = dtime / 2;
-    const int groups = std::max(1, std::min(kTeGroups, 512 / half));
-    const int threads = (groups * half + 31) / 32 * 32;
-    FB_TRY_CUDA(fb::launch(k_te_bwd_pairs<T>, dim3(1, parts), threads, 0, stream, g, ldg, dt, w, b, dtime, groups,
-                           n_rows, n_rows_dev, part));
-    FB_LAUNCHED("k_te_bwd_pairs");
+  // V adjacent columns per thread, the widest of 4 and 2 that dtime, the
+  // pitch and the alignment of g allow (FB_TE_BWD_VEC=1/2/4 forces one
+  // column per thread / at most V; FB_TE_BWD_GROUPS caps the row groups)
+  static const int vec_env = getenv("FB_TE_BWD_VEC") ? atoi(getenv("FB_TE_BWD_VEC")) : 4;
+  static const int gcap = getenv("FB_TE_BWD_GROUPS") ? std::max(1, atoi(getenv("FB_TE_BWD_GROUPS"))) : 1 << 20;
+  const auto fits = [&](int V) {
+    return vec_env >= V && dtime % V == 0 && dtime <= kTeColsMax && ldg % V == 0 &&
+           reinterpret_cast<uintptr_t>(g) % (sizeof(T) * V) == 0;
+  };
+  const int V = fits(4) ? 4 : fits(2) ? 2 : 1;
+  if (V > 1) {
+    // groups of dtime / V threads: as many as fit kTeVecThreads threads
+    const int nt = dtime / V;
+    const int groups = std::max(1, std::min(gcap, kTeVecThreads / nt));
+    const int threads = (groups * nt + 31) / 32 * 32;
+    if (V == 4) {
+      FB_TRY_CUDA(fb::launch(k_te_bwd_vec<T, 4>, dim3(1, parts), threads, 0, stream, g, ldg, dt, w, b, dtime, groups,
+                             n_rows, n_rows_dev, part));
+    } else {
+      FB_TRY_CUDA(fb::launch(k_te_bwd_vec<T, 2>, dim3(1, parts), threads, 0, stream, g, ldg, dt, w, b, dtime, groups,
+                             n_rows, n_rows_dev, part));
+    }
+    FB_LAUNCHED("k_te_bwd_vec");
   } else if (dtime <= kTeColsMax) {
     // groups of dtime threads: as many as fit 1024 threads, at most kTeGroups
     const int groups = std::max(1, std::min(kTeGroups, 1024 / dtime));

@@ -80,16 +80,62 @@ def test_gather_time_encode(cuda):
     torch.testing.assert_close(out3.cpu(), torch.cos(lin.bias.data).expand(3, -1), rtol=1e-6, atol=1e-7)
 
 
+def test_time_encode_bwd_sine_accuracy(cuda):
+    """The sine inside the time-encoding backward, one argument per column:
+    one row with dt = 1, w = 0 and b = the arguments gives db[c] = -sin(b[c])
+    exactly (x = fma(1, 0, b) = b, one term per sum).  Arguments: log-uniform
+    magnitudes from 1e-6 to 1e9, the floats nearest to k pi/2 (the hardest
+    reductions) for k up to 1e8, the floats nearest to (k + 1/2) pi/2 just
+    below 2^22 (the largest reduced arguments of the fp32 reduction) and the
+    edges of each reduction range (2^22, 2^28).  Below 2^22 (the fp32
+    reduction) every value is within 2 ulp of the double sine of the same
+    float; above, within 2 ulp plus 5e-10 (the fixed-point reduction keeps 32
+    fraction bits)."""
+    from fast_b200 import ops
+    rng = np.random.default_rng(7)
+    mags = 10.0 ** rng.uniform(-6, 9, 6000)
+    args = [(mags * rng.choice([-1.0, 1.0], mags.size)).astype(np.float32)]
+    ks = np.concatenate([np.arange(1, 4000), rng.integers(4000, 340000, 3000), rng.integers(340000, 10 ** 8, 2000)])
+    near = (ks.astype(np.float64) * (np.pi / 2)).astype(np.float32)
+    args += [near, -near, np.nextafter(near, np.float32(np.inf)), np.nextafter(near, np.float32(0))]
+    edges = np.array([2.0 ** 19, 2.0 ** 22, 2.0 ** 28, 0.7853981633974483, 1.5707963267948966], dtype=np.float32)
+    args += [edges, np.nextafter(edges, np.float32(0)), np.nextafter(edges, np.float32(np.inf)), -edges,
+             np.array([0.0, -0.0, 1e-30, -1e-30, 1e-38], dtype=np.float32),
+             ((np.arange(2600000, 2670000, 7) + 0.5) * (np.pi / 2)).astype(np.float32)]
+    x = np.concatenate(args)
+    d = 512
+    x = np.concatenate([x, np.zeros((-x.size) % d, dtype=np.float32)])
+    got = np.empty_like(x)
+    one = torch.ones(1, device=cuda)
+    g = torch.ones(1, d, device=cuda)
+    w = torch.zeros(d, device=cuda)
+    for i in range(0, x.size, d):
+        b = torch.from_numpy(x[i:i + d]).to(cuda)
+        dw = torch.zeros(d, device=cuda)
+        db = torch.zeros(d, device=cuda)
+        ops.time_encode_bwd(g, one, w, b, dw, db)
+        got[i:i + d] = -db.cpu().numpy()
+        assert torch.equal(dw, db)
+    ref = np.sin(x.astype(np.float64))
+    err = np.abs(got.astype(np.float64) - ref)
+    ulp = np.spacing(np.abs(ref).astype(np.float32)).astype(np.float64)
+    fast = np.abs(x) < 2.0 ** 22
+    assert np.all(err[fast] <= 2 * ulp[fast]), float(np.max(err[fast] / ulp[fast]))
+    assert np.all(err[~fast] <= 2 * ulp[~fast] + 5e-10)
+
+
+@pytest.mark.parametrize("d", [100, 50, 37])
 @pytest.mark.parametrize("dt_max", [1e4, 2e8, 3e8])
-def test_time_encode_bwd(cuda, dt_max):
+def test_time_encode_bwd(cuda, dt_max, d):
     """dw, db of cos(w dt + b) against an fp64 sum over the same single-rounded
     arguments; E-term sums are compared within the fp32 summation bound
     sum|terms| * E * 2^-24.  dt up to 2e8 (the timestamps of the synthetic
     graphs) exercises the kernel's own argument reduction, 3e8 the fallback
-    beyond it."""
+    beyond it.  Widths 100 and 50 take the kernel with four and two columns
+    per thread, 37 the one-column kernel."""
     from fast_b200 import ops
     rng = np.random.default_rng(1)
-    E, d = 5000, 100
+    E = 5000
     dt = torch.from_numpy((rng.random(E) * dt_max).astype(np.float32))
     w = torch.from_numpy(1 / 10 ** np.linspace(0, 9, d, dtype=np.float32))
     b = torch.randn(d) * 0.1
