@@ -13,14 +13,10 @@
 // The backward needs sin of fp32 arguments up to 1e8 radians and beyond (real
 // timestamps).  The library's double sin handles them exactly but is bound by
 // the fp64 rate (~100 operations per call).  sin_big() reduces the argument
-// by pi/2 in fp32 with a three-float split of pi/2 below 2^22 (Cody & Waite),
-// in integer arithmetic above (the float's 24-bit mantissa times a 64-bit
-// fixed-point 2/pi gives the quadrant and 32 fraction bits exactly, the idea
-// of Payne & Hanek, "Radian reduction for trigonometric functions", SIGNUM
-// Newsletter 18, 1983, with one word of 2/pi, enough below 2^28), and
-// evaluates the Taylor series of sin and cos on |r| <= 0.96 in fp32 (degrees
-// 11 and 10: truncation below 1.3e-9).  The forward keeps cosf, which
-// measured faster in its wide gather.
+// by pi/2 itself (Cody & Waite: a three-float split of pi/2 in fp32 below
+// 2^22, a two-double split up to 2^28) and evaluates the Taylor series of sin
+// and cos on |r| <= 0.96 in fp32 (degrees 11 and 10: truncation below
+// 1.3e-9).  The forward keeps cosf, which measured faster in its wide gather.
 #include <cuda_bf16.h>
 #include "runtime.cuh"
 
@@ -272,9 +268,6 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) k_gather_time_encode_bf16(Ga
   }
 }
 
-// round(2/pi * 2^64)
-constexpr uint64_t kTwoOverPiQ64 = 0xa2f9836e4e44152aull;
-
 // +-sin(r) or +-cos(r) for the quadrant q (mod 4) of an argument reduced to
 // r, |r| <= 0.96: sin(r + q pi/2).  Taylor series of sin and cos (degrees 11
 // and 10, coefficients 1/n!; truncation below 1.3e-9 on that interval).
@@ -288,25 +281,18 @@ __device__ __forceinline__ float sin_quadrant(float r, int q) {
   return (q & 2) ? -v : v;
 }
 
-// sin(x) for |x| >= 2^22: |x| = (k + f) pi/2 with k an integer and |f| <= 1/2,
-// r = f pi/2, from the fixed-point product below; from 2^28 on the library's
-// double sin.  Kept out of line: arguments this large are rare (w dt beyond
-// 4e6 rad).
+// sin(x) for |x| >= 2^22: below 2^28, Cody & Waite's reduction in double with
+// pi/2 split into a 30-bit head and a 53-bit tail (|pi/2 - head - tail| <
+// 2e-26): x - k head is exact (a multiple of 2^-29 below 1 in magnitude, for
+// k < 2^28), the tail's fma rounds once, so r is off by < 1e-17; from 2^28 on
+// the library's double sin.  Kept out of line: arguments this large are rare
+// (w dt beyond 4.2e6 rad).
 __device__ __noinline__ float sin_far(float x) {
-  const float ax = fabsf(x);
-  if (ax >= 268435456.f) return (float)sin((double)x);
-  const uint32_t bits = __float_as_uint(ax);
-  const int e = (int)(bits >> 23) - 127;             // 22 .. 27
-  const uint64_t m = (bits & 0x7FFFFFu) | 0x800000u;  // |x| = m 2^(e-23)
-  const uint64_t lo = m * kTwoOverPiQ64, hi = __umul64hi(m, kTwoOverPiQ64);
-  const int s = 87 - e;                               // |x| 2/pi = (hi:lo) 2^-s, s in 60 .. 65
-  int q = (int)((s >= 64 ? hi >> (s - 64) : (lo >> s) | (hi << (64 - s))) & 3u);
-  const int sh = s - 32;                              // 28 .. 33
-  const int32_t fb = (int32_t)(uint32_t)((lo >> sh) | (hi << (64 - sh)));   // fraction, 32 bits
-  if (fb < 0) q = (q + 1) & 3;                        // fraction >= 1/2: the next quadrant
-  const float r = (float)((double)fb * 0x1.921fb54442d18p-32);   // pi/2 * 2^-32, one rounding to float
-  const float sv = sin_quadrant(r, q);
-  return x < 0.f ? -sv : sv;
+  if (fabsf(x) >= 268435456.f) return (float)sin((double)x);
+  const double xd = (double)x;
+  const double kd = rint(xd * 0x1.45f306dc9c883p-1);               // nearest multiple of pi/2
+  const float r = (float)fma(-kd, -0x1.de973dcb3b39ap-31, fma(-kd, 0x1.921fb548p+0, xd));
+  return sin_quadrant(r, (int)((long long)kd & 3));
 }
 
 // sin(x) for a float x, to about 2 ulp of the double result.  |x| < 2^22 (every
