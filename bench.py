@@ -54,7 +54,7 @@ def parse():
                          "config's synthetic graph; feature widths and the model still come from --config")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the cpu_baseline sample")
     ap.add_argument("--cpu-edges", type=int, default=4_000_000,
-                    help="config 5 on the CPU: prefix subsample of the graph (its fp32 edge table is 142 GB)")
+                    help="config 5 on the CPU: edges of a smaller graph drawn like config 5's (its fp32 edge table is 142 GB)")
     ap.add_argument("--cpu-batch-frac", type=float, default=0.25,
                     help="config 5 on the CPU: each step trains on this fraction of the global batch")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -67,7 +67,7 @@ def parse():
                     help="positive edges per step instead of the config's (one GPU at --batch 500 runs the per-rank "
                          "workload of config 5 on 8 GPUs)")
     ap.add_argument("--edges", type=int, default=None,
-                    help="prefix subsample: the first N edges of the config's synthetic graph")
+                    help="a smaller graph of N edges drawn like the config's (same nodes, endpoint and time distributions, so each node's edges lie further apart in time)")
     ap.add_argument("--suite", default=None, choices=["kernels", "bf16"],
                     help="kernels: time each hot kernel alone at config-5 block sizes against the HBM roofline "
                          "(one JSON line per kernel instead of the training-step line)")
@@ -87,7 +87,7 @@ def parse():
 
 # ----------------------------------------------------------------------------- helpers
 # DRAM bytes over algorithmic bytes of the wrappers that can be the dominant kernel, from one ncu capture of
-# the same step on a 4 M-edge prefix (profiles/ncu_dram_traffic_bwd_dkv_dq_gather_edges4m.md); the traffic of
+# the same step on a 4 M-edge graph drawn like config 5's (profiles/ncu_dram_traffic_bwd_dkv_dq_gather_edges4m.md); the traffic of
 # a full-size launch is the ratio times its algorithmic bytes
 NCU_TRAFFIC = {"gemm_group:bwd_dkv_dq": 1834.6 / 1873.3, "gather_time_encode": 1081.9 / 1966.7}
 NCU_TRAFFIC_SRC = "profiles/ncu_dram_traffic_bwd_dkv_dq_gather_edges4m.md"
@@ -897,6 +897,15 @@ def run_bf16_suite(args):
           2 * E * dt_ * 2 * D,
           lambda: ops.gemm_bf16_group([dict(kind=ops.NN, A=dkv, B=Wb[:, t_at:t_at + dt_], out=dAt)]),
           "M=%d, N=%d, K=%d" % (E, dt_, 2 * D))
+    # the time-encoding backward on that gradient: its cost depends on how
+    # many arguments w dt + b pass 2^22 (the double-precision reduction)
+    dw_, db_ = torch.zeros(dt_, device=dev), torch.zeros(dt_, device=dev)
+    for hi in (1e5, 4e6, 2e8):
+        dth = torch.rand(E, device=dev, generator=g) * hi
+        far = float(((dth[:, None] * w[None, :]).abs() >= 2.0 ** 22).float().mean())
+        timed("k_te_bwd_vec (bf16 gradient, dt uniform below %.0e)" % hi, E * (2 * dt_ + 4), 0,
+              lambda: ops.time_encode_bwd(dAt, dth, w, b, dw_, db_),
+              "rows=%d, dtime=%d, %.1f%% of arguments past 2^22" % (E, dt_, 100 * far))
     q = torch.randn(Nd, D, device=dev, generator=g) * 0.5
     kvf = torch.randn(E, 2 * D, device=dev, generator=g) * 0.5
     rptr = torch.arange(0, E + 1, fan, device=dev, dtype=torch.int32)
@@ -922,7 +931,7 @@ def data_label(args, cfg):
     if args.data:
         return "dataset %s read from edges.csv + ext_full.npz; seeded random features" % cfg.name
     if args.edges:
-        return "synthetic (seeded, %s shapes; prefix subsample: first %d edges)" % (cfg.name, cfg.edges)
+        return "synthetic (seeded, %s shapes; a %d-edge graph drawn like the config's)" % (cfg.name, cfg.edges)
     return "synthetic (seeded, %s shapes)" % cfg.name
 
 
