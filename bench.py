@@ -54,7 +54,8 @@ def parse():
                          "config's synthetic graph; feature widths and the model still come from --config")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the cpu_baseline sample")
     ap.add_argument("--cpu-edges", type=int, default=4_000_000,
-                    help="config 5 on the CPU: edges of a smaller graph drawn like config 5's (its fp32 edge table is 142 GB)")
+                    help="config 5 on the CPU: edges of a smaller graph drawn like config 5's (its fp32 edge "
+                         "table is 142 GB)")
     ap.add_argument("--cpu-batch-frac", type=float, default=0.25,
                     help="config 5 on the CPU: each step trains on this fraction of the global batch")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -67,7 +68,8 @@ def parse():
                     help="positive edges per step instead of the config's (one GPU at --batch 500 runs the per-rank "
                          "workload of config 5 on 8 GPUs)")
     ap.add_argument("--edges", type=int, default=None,
-                    help="a smaller graph of N edges drawn like the config's (same nodes, endpoint and time distributions, so each node's edges lie further apart in time)")
+                    help="a smaller graph of N edges drawn like the config's (same nodes, endpoint and time "
+                         "distributions, so each node's edges lie further apart in time)")
     ap.add_argument("--suite", default=None, choices=["kernels", "bf16"],
                     help="kernels: time each hot kernel alone at config-5 block sizes against the HBM roofline "
                          "(one JSON line per kernel instead of the training-step line)")
@@ -892,7 +894,7 @@ def run_bf16_suite(args):
           2 * E * 2 * D * (dn + de + dt_ + 1), lambda: ops.gemm_bf16_group(tnm),
           "M=%d, N=%d, K=%d+%d+%d+1" % (E, 2 * D, dn, de, dt_))
     del XH
-    dAt = torch.empty(E, dt_, device=dev, dtype=torch.bfloat16)       # bf16, as in the step
+    dAt = torch.empty(E, ops.pad8(dt_), device=dev, dtype=torch.bfloat16)[:, :dt_]   # bf16, as in the step
     timed("k_bf_group (time-encoding input gradient, NN, bf16 output)", E * (2 * 2 * D + 2 * dt_),
           2 * E * dt_ * 2 * D,
           lambda: ops.gemm_bf16_group([dict(kind=ops.NN, A=dkv, B=Wb[:, t_at:t_at + dt_], out=dAt)]),
