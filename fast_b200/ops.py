@@ -205,7 +205,8 @@ def gemm_group(problems, name="gemm_group"):
     n = len(problems)
     dev = problems[0]["A"].device
     ws = torch.empty(int(lib.fb_gemm_group_ws_bytes(arr, n)), device=dev, dtype=torch.uint8)
-    _launch(name, nbytes, flops, 2,
+    # the grouped GEMM, plus the split reduction when the group holds a TN problem
+    _launch(name, nbytes, flops, 1 + int(any(p["kind"] == TN for p in problems)),
             lambda: call("fb_gemm_group", arr, n, ptr(ws), ws.numel(), stream_ptr()))
 
 
@@ -343,7 +344,8 @@ def gemm_bf16_group(problems, name="gemm_bf16_group"):
     n = len(problems)
     dev = out.device
     ws = torch.empty(int(lib.fb_gemm_bf16_group_ws_bytes(arr, n)), device=dev, dtype=torch.uint8)
-    _launch(name, nbytes, flops, 2,
+    # the grouped GEMM, plus the split reduction when the group holds a TN problem
+    _launch(name, nbytes, flops, 1 + int(any(p["kind"] == TN for p in problems)),
             lambda: call("fb_gemm_bf16_group", arr, n, ptr(ws), ws.numel(), stream_ptr()))
 
 
