@@ -68,6 +68,8 @@ _SIGS = {
     "fb_time_encode_bwd_ws_bytes": (_SZ, [_I64, _I]),
     "fb_time_encode_bwd": (_I, [_P, _I64, _P, _P, _P, _I, _I64, _P, _P, _P, _P, _P]),
     "fb_time_encode_bwd_bf16": (_I, [_P, _I64, _P, _P, _P, _I, _I64, _P, _P, _P, _P, _P]),
+    "fb_gather_rows_tiered": (_I, [_P, _I64, _P, _P, _I64, _P, _I64, _I64, _P, _I64, _I, _I, _P, _I64, _P, _P, _P]),
+    "fb_host_rows_device_pointer": (_I, [_P, _P]),
     "fb_gemm_nt": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _I, _I, _I, _P]),
     "fb_gemm_nt_tc_supported": (_I, [_P, _I64, _P, _I64, _I, _I]),
     "fb_gemm_nt_tc": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _I, _I, _I, _P]),

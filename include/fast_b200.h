@@ -294,6 +294,27 @@ int fb_time_encode_bwd_bf16(const uint16_t *g, int64_t ldg, const float *dt, con
                             void *ws, cudaStream_t stream);
 
 /* ------------------------------------------------------------------------- */
+/* Feature rows split between HBM and page-locked host memory: the slim      */
+/* feature cache (slimCache.py:184-403: init_cache, fresh_cache,             */
+/* trans2Device :261-403).                                                   */
+/* ------------------------------------------------------------------------- */
+/* out[r, 0:d) = table row ids[r] for r < n (n_dev overrides when not NULL):
+ * from dev_rows[slot_of[ids[r]]] when that slot is in [0, n_dev_rows), else
+ * from host_rows[ids[r]] (the full table, read by the GPU from page-locked
+ * host memory: pass the address fb_host_rows_device_pointer returns).  Rows
+ * are elem_bytes = 4 (fp32) or 2 (bf16) wide elements with leading dimensions
+ * in elements.  An id outside [0, n_rows_total) gives a zero row and sets bit
+ * 1 of *err (may be NULL); *misses (may be NULL) is increased by the rows read
+ * from host memory. */
+int fb_gather_rows_tiered(const int32_t *ids, int64_t n, const int32_t *n_dev, const int32_t *slot_of,
+                          int64_t n_rows_total, const void *dev_rows, int64_t ld_dev, int64_t n_dev_rows,
+                          const void *host_rows, int64_t ld_host, int d, int elem_bytes, void *out, int64_t ld_out,
+                          unsigned long long *misses, int32_t *err, cudaStream_t stream);
+/* The device address of page-locked, mapped host memory (cudaHostGetDevicePointer);
+ * fails for pageable memory. */
+int fb_host_rows_device_pointer(const void *host, void **dev);
+
+/* ------------------------------------------------------------------------- */
 /* fp32 projection GEMMs (torch.nn.Linear, layers.py:91-95).                  */
 /* ------------------------------------------------------------------------- */
 /* C[m, n] = sum_k A[m,k] B[n,k] (+ bias[n]) (+ C when accumulate)   "NT"
