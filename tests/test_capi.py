@@ -69,6 +69,22 @@ def test_wrappers_reject_bad_operands_before_any_launch():
         ops.gemm_bf16_group([dict(kind=ops.NT, A=a, B=a, out=torch.zeros(16, 16))])
 
 
+def test_tiered_gather_rejects_bad_arguments_before_any_launch():
+    """fb_gather_rows_tiered checks its arguments on the host: element width,
+    row width, leading dimensions and missing tables return FB_ERR_ARG (1)
+    without touching a GPU."""
+    from fast_b200.capi import lib
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.addressof(buf)
+    args = dict(ids=p, n=4, n_dev=None, slot_of=p, n_rows_total=8, dev_rows=p, ld_dev=4, n_dev_rows=2,
+                host_rows=p, ld_host=4, d=4, elem_bytes=4, out=p, ld_out=4, misses=None, err=None, stream=None)
+    for bad in (dict(elem_bytes=3), dict(d=0), dict(ld_out=3), dict(ld_host=2), dict(host_rows=None),
+                dict(dev_rows=None), dict(ids=None), dict(n=-1)):
+        a = dict(args, **bad)
+        assert lib.fb_gather_rows_tiered(*a.values()) == 1, bad
+    assert lib.fb_host_rows_device_pointer(None, None) == 1
+
+
 def test_import_fails_loudly_without_the_library():
     """No fallback: with libfast_b200.so absent, importing the binding (and
     so every op) raises ImportError naming the build command."""
