@@ -59,8 +59,10 @@ class TieredFeatureTable:
     memory, the hot ones also in HBM.
 
     table: CPU tensor (fp32 or bf16; copied into page-locked memory unless it
-    is pinned already).  hot_ids: row ids to place in HBM (e.g.
-    hot_ids_by_count(count_ids(sampled_ids, rows), capacity)).
+    is pinned already, so a table near the size of host memory should be
+    allocated pinned from the start: torch.empty(rows, d, pin_memory=True)).
+    hot_ids: row ids to place in HBM (e.g. hot_ids_by_count(count_ids(
+    sampled_ids, rows), capacity)).
     """
 
     def __init__(self, table, hot_ids, device="cuda"):
